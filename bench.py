@@ -1,0 +1,266 @@
+"""Benchmark: audio-seconds separated per second by the B200 HTDemucs v4 backend.
+
+Workload (BASELINE configuration "full-track htdemucs"): one 240 s stereo
+44.1 kHz seeded pink-noise track (RMS 0.1), 7.8 s segments, overlap 0.25,
+shifts 1 (ShiftRng seed 0x5eed1234), all chunks of the track batched into one
+forward; random-init weights (seeded, LayerScale 1e-4). A step is one
+whole-track separation. With N GPUs the track's chunks are sharded
+contiguously over the ranks (strong scaling: the total work is fixed); the
+only exchange is the overlap-add boundary between neighbouring shards plus
+the final gather of the stems to rank 0.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Prints one JSON line (rank 0). ``--impl reference`` times the reference's CPU
+path — here the C++ restatement under oracle/, since the Rust reference cannot
+be built in this environment — on the host cores, one segment per step.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "demucs-wgpu_b200"))
+
+import synth  # noqa: E402
+
+TRACK_SECONDS = 240.0
+SR = 44100
+SEGMENT = synth.SEGMENT_SAMPLES
+SEGMENT_GFLOP = 334.9  # algorithmic FLOPs of one segment forward (2*MAC over the layer table)
+METRIC = "audio-sec separated/sec (htdemucs)"
+UNIT = "audio-s/s"
+WORKLOAD = "full-track htdemucs: 240 s stereo 44.1 kHz pink noise (RMS 0.1), segment 7.8 s, overlap 0.25, shifts 1, all chunks batched"
+
+
+def _peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            d = json.load(f)
+        return d["hbm_gbs"], d["bf16_tflops"], "measured"
+    except Exception:
+        return 6650.0, 1590.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.samples = []
+        self._stop = threading.Event()
+        self._t = None
+
+    def _run(self):
+        while not self._stop.is_set():
+            try:
+                out = subprocess.run(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}",
+                                      "--format=csv,noheader,nounits"], capture_output=True,
+                                     text=True, timeout=5).stdout.strip()
+                if out:
+                    self.samples.append([x.strip() for x in out.split(",")])
+            except Exception:
+                pass
+            self._stop.wait(0.2)
+
+    def __enter__(self):
+        self._t = threading.Thread(target=self._run, daemon=True)
+        self._t.start()
+        return self
+
+    def __exit__(self, *a):
+        self._stop.set()
+        self._t.join(timeout=10)
+
+    def summary(self):
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm = [float(s[1]) for s in self.samples if s[1].replace(".", "").isdigit()]
+        mx = [float(s[2]) for s in self.samples if s[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for s in self.samples for i in range(4)
+                          if len(s) > 5 + i and s[5 + i].lower() == "active"})
+        return {"sm_mhz": float(np.median(sm)) if sm else None,
+                "sm_max_mhz": max(mx) if mx else None, "reasons": reasons,
+                "samples": len(self.samples)}
+
+
+def cpu_baseline(seconds_budget=30.0):
+    """The oracle (C++ restatement of the reference CPU forward) on all host
+    threads: one 7.8 s segment per repetition, 1 warm-up + up to 2 timed."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle
+
+    threads = oracle.threads(0)
+    w = synth.random_weights(0)
+    m = oracle.OracleModel(w)
+    seg = synth.gaussian_audio(1, 1)
+    m.forward(seg)
+    times = []
+    t_all = time.perf_counter()
+    while len(times) < 2 and time.perf_counter() - t_all < seconds_budget:
+        t0 = time.perf_counter()
+        m.forward(seg)
+        times.append(time.perf_counter() - t0)
+    t = float(np.median(times))
+    return {"value": round(SEGMENT / SR / t, 3), "unit": UNIT, "cores": threads, "kind": "port",
+            "sample": f"one 343980-sample segment forward (config 1 shapes), median of {len(times)} after 1 warm-up, {t:.2f} s each"}
+
+
+def run_reference(args, rank, world):
+    if rank != 0:
+        return
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle
+
+    threads = oracle.threads(0)
+    w = synth.random_weights(0)
+    m = oracle.OracleModel(w)
+    track = synth.pink_noise(2024, int(TRACK_SECONDS * SR))
+    # one padded chunk of the workload per step (the first chunk of the shift view)
+    seg = np.zeros((1, 2, SEGMENT), dtype=np.float32)
+    mean = track.mean()
+    std = track.mean(axis=0).std(ddof=1) + 1e-8
+    seg[0] = (track[:, :SEGMENT] - mean) / std
+    for _ in range(args.warmup):
+        m.forward(seg)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        m.forward(seg)
+    dt = (time.perf_counter() - t0) / args.steps
+    value = SEGMENT / SR / dt
+    line = {"metric": METRIC, "value": round(value, 3), "unit": UNIT, "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(dt * 1e3, 3),
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic", "impl": "reference",
+            "config": {"workload": WORKLOAD, "step": "one segment forward of the workload on the host CPU"},
+            "cpu_baseline": {"value": round(value, 3), "unit": UNIT, "cores": threads, "kind": "port",
+                             "sample": "one 343980-sample chunk of the workload per step (oracle/ C++ restatement of the reference CPU forward; the Rust reference is not buildable here)"},
+            "e2e": {"value": round(value, 3), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def run_ours(args, rank, world, local_rank):
+    import torch
+    import dmx
+
+    dev = local_rank
+    torch.cuda.set_device(dev)
+    n = int(TRACK_SECONDS * SR)
+    track = synth.pink_noise(2024, n)
+    shifts, overlap = 1, 0.25
+    max_shift = int(0.5 * SR)
+    # chunk plan of the single shift pass (ShiftRng first draw)
+    rng = (0x5EED1234 * 6364136223846793005 + 1) & (2**64 - 1)
+    rng = (rng * 6364136223846793005 + 1442695040888963407) & (2**64 - 1)
+    offset = (rng >> 33) % (max_shift + 1)
+    vlen = n + max_shift - offset
+    chunks = dmx.num_chunks(vlen)
+    weights = synth.random_weights(0)
+    blob = synth.write_safetensors(weights)
+
+    if world > 1:
+        raise SystemExit("multi-GPU sharding is not wired into bench.py yet")
+
+    h = dmx.Handle(blob, device=dev, max_batch=chunks)
+    lr = torch.from_numpy(track).to(f"cuda:{dev}").contiguous()
+    stems = torch.empty((4, 2, n), dtype=torch.float32, device=f"cuda:{dev}")
+    stream = torch.cuda.ExternalStream(h.stream, device=f"cuda:{dev}")
+
+    def step():
+        h.separate_track_device(lr.data_ptr(), n, stems.data_ptr(), shifts=shifts, overlap=overlap,
+                                batch=chunks)
+
+    for _ in range(args.warmup):
+        step()
+    h.synchronize()
+    launches = h.kernel_launches()
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(dev) as clocks:
+        start.record(stream)
+        for _ in range(args.steps):
+            step()
+        end.record(stream)
+        h.synchronize()
+        torch.cuda.synchronize()
+    ms = start.elapsed_time(end) / args.steps
+    value = TRACK_SECONDS / (ms / 1e3)
+
+    # e2e through the public host API: pinned host input -> stems in host memory
+    pin = torch.from_numpy(track).pin_memory()
+    out_pin = torch.empty((4, 2, n), dtype=torch.float32).pin_memory()
+    left, right, out_np = pin[0].numpy(), pin[1].numpy(), out_pin.numpy()
+    h.separate_track(left, right, shifts=shifts, overlap=overlap, batch=chunks)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        res = h.separate_track(left, right, shifts=shifts, overlap=overlap, batch=chunks)
+    e2e_s = (time.perf_counter() - t0) / args.steps
+    out_np[...] = res
+
+    # per-kernel device timing of one more step (untimed pass) for the roofline
+    h.set_stage_timing(True)
+    step()
+    h.synchronize()
+    stages = h.stage_times()
+    h.set_stage_timing(False)
+    hbm, bf16, peak_kind = _peaks()
+    top = max(stages.items(), key=lambda kv: kv[1][0])
+    total_ms = sum(v[0] for v in stages.values())
+    flops_per_segment = SEGMENT_GFLOP * 1e9
+    achieved = flops_per_segment * chunks / (ms / 1e3) / 1e12  # whole forward, TFLOP/s
+    line = {"metric": METRIC, "value": round(value, 3), "unit": UNIT, "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 3),
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic",
+            "config": {"workload": WORKLOAD, "chunks_per_step": chunks, "segment_samples": SEGMENT,
+                       "precision": "fp32 SIMT", "l2": "inputs and workspace larger than L2 (126 MB)"},
+            "e2e": {"value": round(TRACK_SECONDS / e2e_s, 3), "unit": UNIT,
+                    "h2d_bytes_per_step": int(2 * n * 4), "d2h_bytes_per_step": int(8 * n * 4)},
+            "gpu_launches": int(launches) * args.steps,
+            "clocks": clocks.summary(),
+            "roofline": {"bound": "tensor", "achieved": round(achieved, 3), "peak": bf16,
+                         "unit": "TFLOP/s", "frac": round(achieved / bf16, 5), "traffic": None,
+                         "kernel": "whole forward (all contractions, SIMT fp32)",
+                         "peak_kind": f"{peak_kind} bf16 dense"},
+            "kernels": {k: {"ms": round(v[0], 3), "launches": v[1], "share": round(v[0] / total_ms, 4)}
+                        for k, v in sorted(stages.items(), key=lambda kv: -kv[1][0])},
+            "top_kernel": top[0]}
+    if rank == 0 and world == 1:
+        line["cpu_baseline"] = cpu_baseline()
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    h.close()
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    args = ap.parse_args()
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", str(args.gpus)))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        run_reference(args, rank, world)
+    else:
+        run_ours(args, rank, world, local_rank)
+
+
+if __name__ == "__main__":
+    main()

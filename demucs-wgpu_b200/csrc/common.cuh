@@ -1,0 +1,54 @@
+// Shared device helpers for the HTDemucs v4 sm_100a kernels.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#define DMX_DEVICE __device__ __forceinline__
+
+namespace dmx {
+
+constexpr int kSegment = 343980;  // int(39/5 * 44100)
+constexpr int kHop = 1024;
+constexpr int kNfft = 4096;
+constexpr int kBins = 2048;       // Nyquist dropped (spec.rs:101-111)
+constexpr int kFrames = 336;      // ceil(343980 / 1024)
+constexpr int kPad = 1536;        // hop/2*3 (spec.rs:66)
+constexpr int kStftLen = 347136;  // 343980 + 1536 + 1620
+
+// Exact GELU: 0.5 x (1 + erf(x / sqrt 2)) with CUDA's erff.
+DMX_DEVICE float gelu(float x) { return 0.5f * x * (1.0f + erff(x * 0.70710678118654752f)); }
+DMX_DEVICE float sigmoid(float g) { return 1.0f / (1.0f + expf(-g)); }
+
+DMX_DEVICE double warp_sum(double v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+DMX_DEVICE float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+DMX_DEVICE float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+// Row statistics held as (sum, sum of squares) in f64, the way the reference
+// accumulates GroupNorm / normalisation moments (demucs/ops.rs:564-578).
+struct RowNorm {
+  float mean, inv;
+};
+DMX_DEVICE RowNorm row_norm(const double* stats, int row, double count) {
+  const double sum = stats[2 * row], sq = stats[2 * row + 1];
+  const double mean = sum / count;
+  const double var = fmax(sq / count - mean * mean, 0.0);
+  RowNorm r;
+  r.inv = 1.0f / (float)sqrt(var + 1e-5);
+  r.mean = (float)mean;
+  return r;
+}
+
+}  // namespace dmx

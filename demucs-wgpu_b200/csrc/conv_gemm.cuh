@@ -1,0 +1,78 @@
+// Implicit-GEMM convolution: one kernel family for every convolution and
+// linear of the HTDemucs v4 forward, over channels-last activations.
+//
+//   out[p, n] = epilogue( sum_{tap, ci} W[tap*Cin + ci, n] * A(p, tap, ci) )
+//
+// p runs over an output grid (b, y, x); the input position of a tap is
+// (y*sy + dy[tap], x*sx + dx[tap]) and reads zero outside the input (this is
+// the padding of every Conv1d/Conv2d, the right-pad of the waveform encoder
+// and the zero rows of the transposed convolutions). No im2col matrix is ever
+// materialised: the gather happens while the tile is staged in shared memory.
+#pragma once
+
+#include "common.cuh"
+
+namespace dmx {
+
+constexpr int kMaxTaps = 16;
+
+enum ProMode : int {
+  PRO_NONE = 0,
+  PRO_BATCH_AFFINE = 1,  // (v - shift[b]) * scale[b]   (input normalisation)
+  PRO_ADD = 2,           // v + x2                      (decoder skip connection)
+  PRO_GN_GELU = 3        // gelu(v*inv*g[c] + (b[c] - mean*inv*g[c]))  (DConv norm1)
+};
+
+enum EpiMode : int {
+  EPI_STORE = 0,          // acc + bias
+  EPI_GELU = 1,           // gelu(acc + bias)
+  EPI_GLU = 2,            // value * sigmoid(gate), columns interleaved (2c, 2c+1)
+  EPI_GLU_EMB = 3,        // GLU + emb[y, c]
+  EPI_STATS = 4,          // row moments of acc + bias, nothing stored
+  EPI_STORE_STATS = 5,    // store acc + bias and accumulate row moments
+  EPI_DCONV_TAIL = 6,     // out[c] = res[c] + gamma[c] * GLU(GN(acc + bias))
+  EPI_RESIDUAL = 7        // out = res + gamma[n] * (acc + bias) [+ row moments]
+};
+
+struct ConvParams {
+  // input gather, element strides: b*i_bs + iy*i_ys + ix*i_xs + ci*i_cs
+  const float* x;
+  const float* x2;
+  int64_t i_bs, i_ys, i_xs, i_cs;
+  int Hin, Win, Cin;
+  int sy, sx;
+  int ntaps;
+  int dy[kMaxTaps], dx[kMaxTaps];
+  // output grid, M = B * Hq * Wq positions
+  int B, Hq, Wq;
+  // packed weights [Kpad][Npad] (zero padded), bias [Npad]
+  const float* w;
+  int K, Npad;
+  const float* bias;
+  int N;  // live GEMM columns (2C for the GLU modes)
+  // output element = b*o_bs + y*o_ys + x*o_xs + o_off + column (GLU modes:
+  // column/2); channels are contiguous
+  float* out;
+  int64_t o_bs, o_ys, o_xs, o_off;
+  // prologue
+  const float* pro_scale;  // PRO_BATCH_AFFINE: float4 {mean, scale, ..} per segment; GN: gain
+  const float* pro_shift;  // GN: bias
+  const double* pro_stats;
+  int pro_rowlen;
+  double pro_count;
+  // epilogue
+  double* epi_stats;
+  int epi_rowlen;
+  const double* epi_nstats;
+  double epi_count;
+  const float* epi_gw;
+  const float* epi_gb;
+  int epi_half;  // C for the GLU-with-norm tail (gate channel = c + C)
+  const float* epi_gamma;
+  const float* epi_res;
+  const float* epi_emb;
+};
+
+void launch_conv_gemm(const ConvParams& p, int pro, int epi, cudaStream_t stream);
+
+}  // namespace dmx

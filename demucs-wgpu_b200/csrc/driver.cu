@@ -1,0 +1,211 @@
+// Separation driver on the device (streaming.rs:52-400, pipeline.rs:105-151,
+// 380-515, mix.rs:552-633): global normalisation of the track, centred chunk
+// extraction from the (shifted) view, triangular overlap-add and the final
+// divide / trim / denormalise. The sums are formed in the reference's order
+// (chunks in increasing index), so the result does not depend on how the
+// chunks were grouped into forwards or spread over GPUs.
+#include "common.cuh"
+#include "kernels.h"
+
+namespace dmx {
+
+namespace {
+
+__global__ void track_moments_kernel(const float* __restrict__ left,
+                                     const float* __restrict__ right, int64_t n,
+                                     double* __restrict__ stats) {
+  __shared__ double red[2][32];
+  double s = 0.0, q = 0.0;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const double r = ((double)left[i] + (double)right[i]) / 2.0;
+    s += r;
+    q += r * r;
+  }
+  s = warp_sum(s);
+  q = warp_sum(q);
+  if ((threadIdx.x & 31) == 0) {
+    red[0][threadIdx.x / 32] = s;
+    red[1][threadIdx.x / 32] = q;
+  }
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    const int nw = blockDim.x / 32;
+    s = threadIdx.x < nw ? red[0][threadIdx.x] : 0.0;
+    q = threadIdx.x < nw ? red[1][threadIdx.x] : 0.0;
+    s = warp_sum(s);
+    q = warp_sum(q);
+    if (threadIdx.x == 0) {
+      atomicAdd(&stats[0], s);
+      atomicAdd(&stats[1], q);
+    }
+  }
+}
+
+// mean, std (+1e-8) of the channel-mean signal (streaming.rs:52-78), then
+// (x - mean) / std into mix_norm (2, n).
+__global__ void track_normalize_kernel(const float* __restrict__ left,
+                                       const float* __restrict__ right, int64_t n,
+                                       const double* __restrict__ stats,
+                                       float* __restrict__ mix_norm, float2* __restrict__ norm) {
+  const double count = (double)n;
+  const double sum = stats[0], sq = stats[1];
+  const double mean = sum / count;
+  const double var = count > 1.0 ? (sq - sum * sum / count) / (count - 1.0) : 0.0;
+  const float meanf = (float)mean;
+  const float sd = (float)sqrt(fmax(var, 0.0)) + 1e-8f;
+  if (blockIdx.x == 0 && threadIdx.x == 0) *norm = make_float2(meanf, sd);
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    mix_norm[i] = (left[i] - meanf) / sd;
+    mix_norm[n + i] = (right[i] - meanf) / sd;
+  }
+}
+
+struct ChunkGeom {
+  int64_t length, view_length, shift_offset, max_shift, stride;
+  int segment;
+};
+
+DMX_DEVICE int64_t chunk_len(const ChunkGeom& g, int64_t c) {
+  const int64_t start = c * g.stride;
+  const int64_t rest = g.view_length - start;
+  return rest < g.segment ? rest : g.segment;
+}
+
+__global__ void gather_chunks_kernel(const float* __restrict__ mix_norm, ChunkGeom g,
+                                     int64_t chunk0, float* __restrict__ out) {
+  const int slot = blockIdx.y, c = blockIdx.z;
+  const int64_t chunk = chunk0 + slot;
+  const int64_t vstart = chunk * g.stride;
+  const int64_t len = chunk_len(g, chunk);
+  const int64_t start = vstart - (g.segment - len) / 2;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < g.segment;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t v = start + i;
+    float sample = 0.f;
+    if (v >= 0 && v < g.view_length) {
+      const int64_t mi = g.max_shift ? g.shift_offset + v - g.max_shift : v;
+      if (mi >= 0 && mi < g.length) sample = mix_norm[(int64_t)c * g.length + mi];
+    }
+    out[((int64_t)slot * 2 + c) * g.segment + i] = sample;
+  }
+}
+
+// acc (8, view_hi - view_lo) += weight * trimmed chunk output, chunks
+// [chunk0, chunk0 + count) in increasing order per sample.
+__global__ void ola_accumulate_kernel(const float* __restrict__ chunks, ChunkGeom g,
+                                      int64_t chunk0, int count, const float* __restrict__ weight,
+                                      float* __restrict__ acc, int64_t view_lo, int64_t view_hi) {
+  const int64_t first = chunk0 * g.stride;
+  const int64_t last_c = chunk0 + count - 1;
+  const int64_t end = last_c * g.stride + chunk_len(g, last_c);
+  const int64_t v = first + (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (v >= end || v < view_lo || v >= view_hi) return;
+  int64_t chi = v / g.stride;
+  if (chi > last_c) chi = last_c;
+  int64_t clo = chi - (g.segment + g.stride - 1) / g.stride;
+  if (clo < chunk0) clo = chunk0;
+  float vals[8];
+#pragma unroll
+  for (int r = 0; r < 8; ++r) vals[r] = acc[(int64_t)r * (view_hi - view_lo) + (v - view_lo)];
+  for (int64_t c = clo; c <= chi; ++c) {
+    const int64_t u = v - c * g.stride;
+    const int64_t len = chunk_len(g, c);
+    if (u < 0 || u >= len) continue;
+    const int64_t trim = (g.segment - len) / 2;
+    const float w = weight[u];
+    const float* src = chunks + (c - chunk0) * 8 * (int64_t)g.segment + trim + u;
+#pragma unroll
+    for (int r = 0; r < 8; ++r) vals[r] += w * src[(int64_t)r * g.segment];
+  }
+#pragma unroll
+  for (int r = 0; r < 8; ++r) acc[(int64_t)r * (view_hi - view_lo) + (v - view_lo)] = vals[r];
+}
+
+// mode 0: stems = (acc/sw) * std + mean            (shifts == 0)
+// mode 1: stems = ((acc/sw) * scale) * std + mean  (shifts == 1)
+// mode 2: pass  += acc/sw                          (one of several shifts)
+// mode 3: stems = (pass * scale) * std + mean      (after the last shift)
+__global__ void ola_finish_kernel(const float* __restrict__ acc, ChunkGeom g, int64_t trim,
+                                  const float* __restrict__ weight, const float2* __restrict__ norm,
+                                  float scale, int mode, float* __restrict__ pass,
+                                  float* __restrict__ stems) {
+  const int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (t >= g.length) return;
+  const float2 nz = *norm;
+  if (mode == 3) {
+#pragma unroll
+    for (int r = 0; r < 8; ++r)
+      stems[(int64_t)r * g.length + t] = (pass[(int64_t)r * g.length + t] * scale) * nz.y + nz.x;
+    return;
+  }
+  const int64_t v = t + trim;
+  if (v >= g.view_length) return;
+  const int64_t nchunks = (g.view_length + g.stride - 1) / g.stride;
+  int64_t chi = v / g.stride;
+  if (chi > nchunks - 1) chi = nchunks - 1;
+  int64_t clo = chi - (g.segment + g.stride - 1) / g.stride;
+  if (clo < 0) clo = 0;
+  float sw = 0.f;
+  for (int64_t c = clo; c <= chi; ++c) {
+    const int64_t u = v - c * g.stride;
+    if (u >= 0 && u < chunk_len(g, c)) sw += weight[u];
+  }
+#pragma unroll
+  for (int r = 0; r < 8; ++r) {
+    const float y = acc[(int64_t)r * g.view_length + v] / sw;
+    if (mode == 0) stems[(int64_t)r * g.length + t] = y * nz.y + nz.x;
+    else if (mode == 1) stems[(int64_t)r * g.length + t] = (y * scale) * nz.y + nz.x;
+    else pass[(int64_t)r * g.length + t] += y;
+  }
+}
+
+}  // namespace
+
+void launch_track_normalize(const float* left, const float* right, int64_t n, double* stats,
+                            float* mix_norm, float2* norm, cudaStream_t s) {
+  cudaMemsetAsync(stats, 0, 2 * sizeof(double), s);
+  track_moments_kernel<<<296, 512, 0, s>>>(left, right, n, stats);
+  track_normalize_kernel<<<296, 512, 0, s>>>(left, right, n, stats, mix_norm, norm);
+}
+
+static ChunkGeom geom(int64_t length, int64_t shift_offset, int64_t max_shift, int segment,
+                      int64_t stride) {
+  ChunkGeom g;
+  g.length = length;
+  g.shift_offset = shift_offset;
+  g.max_shift = max_shift;
+  g.view_length = max_shift ? length + max_shift - shift_offset : length;
+  g.stride = stride;
+  g.segment = segment;
+  return g;
+}
+
+void launch_gather_chunks(const float* mix_norm, int64_t length, int64_t shift_offset,
+                          int64_t max_shift, int segment, int64_t stride, int64_t chunk0,
+                          int count, float* out, cudaStream_t s) {
+  const ChunkGeom g = geom(length, shift_offset, max_shift, segment, stride);
+  gather_chunks_kernel<<<dim3(84, count, 2), 1024, 0, s>>>(mix_norm, g, chunk0, out);
+}
+
+void launch_ola_accumulate(const float* chunks, int64_t length, int64_t shift_offset,
+                           int64_t max_shift, int segment, int64_t stride, int64_t chunk0,
+                           int count, const float* weight, float* acc, int64_t view_lo,
+                           int64_t view_hi, cudaStream_t s) {
+  const ChunkGeom g = geom(length, shift_offset, max_shift, segment, stride);
+  const int64_t span = (count - 1) * stride + segment;
+  ola_accumulate_kernel<<<(unsigned)((span + 255) / 256), 256, 0, s>>>(
+      chunks, g, chunk0, count, weight, acc, view_lo, view_hi);
+}
+
+void launch_ola_finish(const float* acc, int64_t length, int64_t shift_offset, int64_t max_shift,
+                       int segment, int64_t stride, const float* weight, const float2* norm,
+                       float scale, int mode, float* pass, float* stems, cudaStream_t s) {
+  const ChunkGeom g = geom(length, shift_offset, max_shift, segment, stride);
+  const int64_t trim = max_shift ? max_shift - shift_offset : 0;
+  ola_finish_kernel<<<(unsigned)((length + 255) / 256), 256, 0, s>>>(acc, g, trim, weight, norm,
+                                                                     scale, mode, pass, stems);
+}
+
+}  // namespace dmx

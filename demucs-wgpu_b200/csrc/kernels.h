@@ -1,0 +1,42 @@
+// Launchers of the sm_100a kernels (host side). All take the stream to
+// enqueue on; none synchronises.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace dmx {
+
+// spectral.cu
+void launch_stft_cac(const float* mix, int B, const float* window, const float2* tw, float* out,
+                     double* stats, cudaStream_t s);
+void launch_wave_moments(const float* mix, int B, int64_t n, double* stats, cudaStream_t s);
+void launch_norm_finalize(const double* stats, double count, int B, float4* norm, cudaStream_t s);
+void launch_istft(const float* spec, const float4* norm, const float* window, const float2* tw,
+                  float* frames, const float* envelope, const float* time_branch,
+                  const float4* norm_t, float* out, int B, cudaStream_t s);
+
+// transformer.cu
+void launch_layer_norm(const float* x, int64_t rows, int ntok, const float* w, const float* b,
+                       const float* pos, float* out, cudaStream_t s);
+void launch_group_norm_apply(float* x, int B, int64_t ntok, const double* stats, const float* w,
+                             const float* b, cudaStream_t s);
+void launch_flash_attention(const float* q, int ldq, const float* k, const float* v, int ldkv,
+                            float* o, int ldo, int B, int heads, int nq, int nk, float scale,
+                            cudaStream_t s);
+
+// driver.cu
+void launch_track_normalize(const float* left, const float* right, int64_t n, double* stats,
+                            float* mix_norm, float2* norm, cudaStream_t s);
+void launch_gather_chunks(const float* mix_norm, int64_t length, int64_t shift_offset,
+                          int64_t max_shift, int segment, int64_t stride, int64_t chunk0,
+                          int count, float* out, cudaStream_t s);
+void launch_ola_accumulate(const float* chunks, int64_t length, int64_t shift_offset,
+                           int64_t max_shift, int segment, int64_t stride, int64_t chunk0,
+                           int count, const float* weight, float* acc, int64_t view_lo,
+                           int64_t view_hi, cudaStream_t s);
+void launch_ola_finish(const float* acc, int64_t length, int64_t shift_offset, int64_t max_shift,
+                       int segment, int64_t stride, const float* weight, const float2* norm,
+                       float scale, int mode, float* pass, float* stems, cudaStream_t s);
+
+}  // namespace dmx

@@ -1,0 +1,1532 @@
+// Host runtime of the B200 HTDemucs v4 backend: weight ingestion and packing,
+// the per-handle workspace, the forward's launch sequence and the C ABI of
+// include/dmx.h.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <chrono>
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <map>
+#include <memory>
+#include <stdexcept>
+#include <string>
+#include <thread>
+#include <vector>
+
+#include "conv_gemm.cuh"
+#include "dmx.h"
+#include "kernels.h"
+
+using namespace dmx;
+
+namespace {
+
+thread_local std::string g_error;
+
+struct Error : std::runtime_error {
+  int code;
+  Error(int c, const std::string& m) : std::runtime_error(m), code(c) {}
+};
+
+#define CK(call)                                                                       \
+  do {                                                                                 \
+    cudaError_t e_ = (call);                                                           \
+    if (e_ != cudaSuccess)                                                             \
+      throw Error(e_ == cudaErrorMemoryAllocation ? DMX_ERR_NOMEM : DMX_ERR_CUDA,      \
+                  std::string(#call) + ": " + cudaGetErrorString(e_));                 \
+  } while (0)
+
+// ---------------------------------------------------------------------------
+// safetensors: 8-byte little-endian header size, JSON header, raw data.
+// ---------------------------------------------------------------------------
+struct HostTensor {
+  std::vector<int64_t> shape;
+  const float* data = nullptr;
+  size_t count() const {
+    size_t n = 1;
+    for (int64_t s : shape) n *= (size_t)s;
+    return n;
+  }
+};
+
+struct Json {
+  const char* p;
+  const char* end;
+  void ws() {
+    while (p < end && (*p == ' ' || *p == '\n' || *p == '\r' || *p == '\t')) ++p;
+  }
+  void expect(char c) {
+    ws();
+    if (p >= end || *p != c) throw Error(DMX_ERR_WEIGHTS, std::string("safetensors header: expected ") + c);
+    ++p;
+  }
+  bool peek(char c) {
+    ws();
+    return p < end && *p == c;
+  }
+  std::string str() {
+    expect('"');
+    std::string s;
+    while (p < end && *p != '"') {
+      if (*p == '\\' && p + 1 < end) ++p;
+      s += *p++;
+    }
+    expect('"');
+    return s;
+  }
+  double num() {
+    ws();
+    char* e = nullptr;
+    const double v = strtod(p, &e);
+    if (e == p) throw Error(DMX_ERR_WEIGHTS, "safetensors header: expected a number");
+    p = e;
+    return v;
+  }
+  void skip() {
+    ws();
+    if (peek('{')) {
+      expect('{');
+      if (peek('}')) { expect('}'); return; }
+      do { str(); expect(':'); skip(); } while (peek(',') && (expect(','), true));
+      expect('}');
+    } else if (peek('[')) {
+      expect('[');
+      if (peek(']')) { expect(']'); return; }
+      do { skip(); } while (peek(',') && (expect(','), true));
+      expect(']');
+    } else if (peek('"')) {
+      str();
+    } else {
+      while (p < end && *p != ',' && *p != '}' && *p != ']') ++p;
+    }
+  }
+};
+
+std::map<std::string, HostTensor> parse_safetensors(const void* blob, size_t len) {
+  if (len < 8) throw Error(DMX_ERR_WEIGHTS, "safetensors blob shorter than its header size");
+  uint64_t n;
+  std::memcpy(&n, blob, 8);
+  if (8 + n > len) throw Error(DMX_ERR_WEIGHTS, "safetensors header runs past the blob");
+  const char* base = static_cast<const char*>(blob) + 8 + n;
+  const size_t data_len = len - 8 - n;
+  Json j{static_cast<const char*>(blob) + 8, static_cast<const char*>(blob) + 8 + n};
+  std::map<std::string, HostTensor> out;
+  j.expect('{');
+  if (j.peek('}')) return out;
+  while (true) {
+    const std::string name = j.str();
+    j.expect(':');
+    if (name == "__metadata__") {
+      j.skip();
+    } else {
+      HostTensor t;
+      std::string dtype;
+      size_t a = 0, b = 0;
+      j.expect('{');
+      while (true) {
+        const std::string key = j.str();
+        j.expect(':');
+        if (key == "dtype") {
+          dtype = j.str();
+        } else if (key == "shape") {
+          j.expect('[');
+          if (!j.peek(']')) {
+            do { t.shape.push_back((int64_t)j.num()); } while (j.peek(',') && (j.expect(','), true));
+          }
+          j.expect(']');
+        } else if (key == "data_offsets") {
+          j.expect('[');
+          a = (size_t)j.num();
+          j.expect(',');
+          b = (size_t)j.num();
+          j.expect(']');
+        } else {
+          j.skip();
+        }
+        if (j.peek(',')) { j.expect(','); continue; }
+        j.expect('}');
+        break;
+      }
+      if (dtype != "F32") throw Error(DMX_ERR_WEIGHTS, name + ": dtype " + dtype + " is not F32");
+      if (b < a || b > data_len || b - a != t.count() * 4)
+        throw Error(DMX_ERR_WEIGHTS, name + ": data_offsets do not match the shape");
+      if ((reinterpret_cast<uintptr_t>(base + a) & 3) != 0)
+        throw Error(DMX_ERR_WEIGHTS, name + ": tensor data is not 4-byte aligned");
+      t.data = reinterpret_cast<const float*>(base + a);
+      out[name] = t;
+    }
+    if (j.peek(',')) { j.expect(','); continue; }
+    j.expect('}');
+    break;
+  }
+  return out;
+}
+
+// ---------------------------------------------------------------------------
+// Packed weights.
+// ---------------------------------------------------------------------------
+constexpr int kBK = 16, kBN = 64;
+
+struct Tap {
+  int dy, dx;  // input offset of the tap
+};
+
+struct Packed {
+  size_t w_off = 0, b_off = 0;  // float offsets into the weight arena
+  int K = 0, Kpad = 0, N = 0, Npad = 0;
+  std::vector<Tap> taps;
+  const float* w = nullptr;
+  const float* bias = nullptr;
+};
+
+struct Vec {  // a plain per-channel vector on the device
+  size_t off = 0;
+  int n = 0;
+  const float* p = nullptr;
+};
+
+struct WeightBuilder {
+  std::vector<float> host;
+  size_t alloc(size_t n) {
+    const size_t off = host.size();
+    host.resize(off + ((n + 63) / 64) * 64, 0.f);
+    return off;
+  }
+};
+
+struct DConvW {
+  Packed conv1, conv2;  // conv1: 3 taps C -> C/8; conv2: 1x1 C/8 -> 2C (GLU interleaved)
+  Vec n1w, n1b, n2w, n2b, gamma;
+  int C = 0, hidden = 0;
+};
+
+struct EncW {
+  Packed conv, rewrite;
+  DConvW dconv;
+  int cin = 0, cout = 0;
+};
+
+struct DecW {
+  Packed rewrite;
+  Packed convt[4];  // per output phase
+  DConvW dconv;
+  int cin = 0, cout = 0;
+};
+
+struct LayerW {
+  bool cross = false;
+  Packed qkv, q, kv, out, lin1, lin2;
+  Vec n1w, n1b, n2w, n2b, n3w, n3b, now, nob, g1, g2;
+};
+
+struct Model {
+  EncW enc[4], tenc[4];
+  DecW dec[4], tdec[4];  // execution order
+  Packed up, up_t, down, down_t;
+  Vec norm_in_w, norm_in_b, norm_in_t_w, norm_in_t_b;
+  LayerW layers[5], layers_t[5];
+  Vec emb;     // 0.2 * (10 * W)[f, c], (512, 48)
+  Vec pos2d;   // (2688, 512)
+  Vec pos1d;   // (1344, 512)
+  Vec window;  // periodic Hann (4096)
+  Vec env;     // window-squared envelope of the interior, (1024)
+  Vec ola_w;   // triangular transition weight (segment)
+  size_t tw_off = 0;  // float2 twiddles (2048)
+};
+
+struct Loader {
+  const std::map<std::string, HostTensor>& t;
+  WeightBuilder& wb;
+
+  const HostTensor& get(const std::string& name, std::vector<int64_t> shape) {
+    auto it = t.find(name);
+    if (it == t.end()) throw Error(DMX_ERR_WEIGHTS, "missing tensor " + name);
+    if (it->second.shape != shape) {
+      std::string s = name + ": shape [";
+      for (int64_t d : it->second.shape) s += std::to_string(d) + ",";
+      s += "] expected [";
+      for (int64_t d : shape) s += std::to_string(d) + ",";
+      throw Error(DMX_ERR_WEIGHTS, s + "]");
+    }
+    return it->second;
+  }
+
+  Vec vec(const std::string& name, int n) {
+    const HostTensor& h = get(name, {n});
+    Vec v;
+    v.n = n;
+    v.off = wb.alloc(n);
+    std::memcpy(&wb.host[v.off], h.data, n * sizeof(float));
+    return v;
+  }
+
+  // Generic packer: element (tap, ci, column) = value(tap, ci, co(column)).
+  template <class F>
+  Packed pack(int ntaps, int cin, int cols, bool glu, const float* bias, F value,
+              std::vector<Tap> taps) {
+    Packed p;
+    p.K = ntaps * cin;
+    p.Kpad = (p.K + kBK - 1) / kBK * kBK;
+    p.N = cols;
+    p.Npad = (cols + kBN - 1) / kBN * kBN;
+    p.taps = std::move(taps);
+    p.w_off = wb.alloc((size_t)p.Kpad * p.Npad);
+    p.b_off = wb.alloc(p.Npad);
+    const int half = cols / 2;
+    for (int n = 0; n < cols; ++n) {
+      const int co = glu ? ((n % 2 == 0) ? n / 2 : n / 2 + half) : n;
+      for (int tap = 0; tap < ntaps; ++tap)
+        for (int ci = 0; ci < cin; ++ci)
+          wb.host[p.w_off + (size_t)(tap * cin + ci) * p.Npad + n] = value(tap, ci, co);
+      wb.host[p.b_off + n] = bias[co];
+    }
+    return p;
+  }
+
+  // Conv (Cout, Cin, kh, kw) with an explicit tap list of (ky, kx) kernel
+  // indices and their input offsets.
+  Packed conv(const std::string& prefix, std::vector<int64_t> shape,
+              const std::vector<std::pair<int, int>>& kidx, std::vector<Tap> taps, bool glu) {
+    const HostTensor& w = get(prefix + ".weight", shape);
+    const HostTensor& b = get(prefix + ".bias", {shape[0]});
+    const int cout = (int)shape[0], cin = (int)shape[1];
+    const int kh = shape.size() == 4 ? (int)shape[2] : 1;
+    const int kw = shape.size() == 4 ? (int)shape[3] : (int)shape[2];
+    return pack((int)kidx.size(), cin, cout, glu, b.data,
+                [&](int tap, int ci, int co) {
+                  const int ky = kidx[tap].first, kx = kidx[tap].second;
+                  return w.data[(((size_t)co * cin + ci) * kh + ky) * kw + kx];
+                },
+                std::move(taps));
+  }
+
+  // ConvTranspose (Cin, Cout, k[, 1]) restricted to the two kernel rows that
+  // feed output phase `phase` (see the header of convt_taps).
+  Packed convt(const std::string& prefix, std::vector<int64_t> shape, int phase) {
+    const HostTensor& w = get(prefix + ".weight", shape);
+    const int cin = (int)shape[0], cout = (int)shape[1];
+    const HostTensor& b = get(prefix + ".bias", {cout});
+    const int k = (int)shape[2];
+    static const int kf[4][2] = {{2, 6}, {3, 7}, {0, 4}, {1, 5}};
+    static const int dq[4][2] = {{0, -1}, {0, -1}, {1, 0}, {1, 0}};
+    std::vector<Tap> taps = {{dq[phase][0], 0}, {dq[phase][1], 0}};
+    return pack(2, cin, cout, false, b.data,
+                [&](int tap, int ci, int co) {
+                  return w.data[((size_t)ci * cout + co) * k + kf[phase][tap]];
+                },
+                taps);
+  }
+
+  Packed linear(const std::string& wname, const std::string& bname, int out, int in, int row0,
+                int rows) {
+    const HostTensor& w = get(wname, {out, in});
+    const HostTensor& b = get(bname, {out});
+    return pack(1, in, rows, false, b.data + row0,
+                [&](int, int ci, int co) { return w.data[(size_t)(row0 + co) * in + ci]; },
+                {{0, 0}});
+  }
+
+  DConvW dconv(const std::string& prefix, int C, bool freq) {
+    DConvW d;
+    d.C = C;
+    d.hidden = C / 8;
+    (void)freq;
+    return d;
+  }
+};
+
+std::vector<std::pair<int, int>> kidx_line(int k, bool along_h) {
+  std::vector<std::pair<int, int>> v;
+  for (int i = 0; i < k; ++i) v.push_back(along_h ? std::make_pair(i, 0) : std::make_pair(0, i));
+  return v;
+}
+
+void load_dconv(Loader& L, const std::string& prefix, int C, DConvW* out, int d_unused = 0) {
+  (void)d_unused;
+  out->C = C;
+  out->hidden = C / 8;
+}
+
+struct DConvLayerW {
+  Packed conv1, conv2;
+  Vec n1w, n1b, n2w, n2b, gamma;
+};
+
+}  // namespace
+
+// ---------------------------------------------------------------------------
+// The handle.
+// ---------------------------------------------------------------------------
+struct DConvFull {
+  DConvLayerW layer[2];
+  int C = 0, hidden = 0;
+};
+
+struct dmx_pending {
+  dmx_handle* h;
+  int64_t n;
+  cudaEvent_t done;
+  float* out_dev;
+  float* host_pinned;
+};
+
+struct dmx_handle {
+  dmx_config cfg{};
+  int device = 0;
+  cudaStream_t stream = nullptr;
+  float* wdev = nullptr;
+  Model m;
+  DConvFull enc_dc[4], tenc_dc[4], dec_dc[4], tdec_dc[4];
+  // workspace
+  char* ws = nullptr;
+  size_t ws_cap = 0, ws_off = 0;
+  bool measuring = false;
+  size_t ws_peak = 0;
+  int64_t launches = 0;
+  // io staging
+  float* io_in = nullptr;
+  float* io_out = nullptr;
+  int64_t io_cap = 0;
+  float* pinned_in = nullptr;
+  float* pinned_out = nullptr;
+  dmx_trace_fn trace = nullptr;
+  void* trace_user = nullptr;
+  bool stage_timing = false;
+  std::vector<std::pair<std::string, cudaEvent_t>> marks;
+  std::vector<std::string> stage_names;
+  std::vector<float> stage_ms;
+  std::vector<int> stage_counts;
+  dmx_pending pending{};
+  char* track_ws = nullptr;
+  size_t track_cap = 0;
+
+  float* W(size_t off) const { return wdev + off; }
+
+  void* alloc(size_t bytes) {
+    bytes = (bytes + 255) / 256 * 256;
+    if (measuring) {
+      ws_off += bytes;
+      ws_peak = std::max(ws_peak, ws_off);
+      return reinterpret_cast<void*>(0x100);
+    }
+    if (ws_off + bytes > ws_cap) throw Error(DMX_ERR_NOMEM, "workspace exhausted");
+    void* p = ws + ws_off;
+    ws_off += bytes;
+    return p;
+  }
+  float* falloc(size_t n) { return static_cast<float*>(alloc(n * sizeof(float))); }
+  double* dalloc(size_t n) { return static_cast<double*>(alloc(n * sizeof(double))); }
+
+  bool live() const { return !measuring; }
+
+  void mark(const std::string& name) {
+    if (!stage_timing || measuring) return;
+    cudaEvent_t e;
+    CK(cudaEventCreate(&e));
+    CK(cudaEventRecord(e, stream));
+    marks.emplace_back(name, e);
+  }
+
+  void zero(void* p, size_t bytes) {
+    if (!live()) return;
+    CK(cudaMemsetAsync(p, 0, bytes, stream));
+  }
+
+  void gemm(const ConvParams& p, int pro, int epi, const char* tag = "gemm") {
+    ++launches;
+    if (!live()) return;
+    mark(tag);
+    if ((epi == EPI_STATS || epi == EPI_STORE_STATS || epi == EPI_RESIDUAL) && p.epi_stats &&
+        p.epi_rowlen < 128)
+      throw Error(DMX_ERR_INVALID, "row statistics need rows of at least 128 positions");
+    launch_conv_gemm(p, pro, epi, stream);
+  }
+
+  void after(const char* what) {
+    if (!live()) return;
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) throw Error(DMX_ERR_CUDA, std::string(what) + ": " + cudaGetErrorString(e));
+  }
+};
+
+namespace {
+
+ConvParams base_params(const Packed& pk, const float* W0) {
+  ConvParams p;
+  std::memset(&p, 0, sizeof(p));
+  p.w = W0 + pk.w_off;
+  p.bias = W0 + pk.b_off;
+  p.K = pk.K;
+  p.Npad = pk.Npad;
+  p.N = pk.N;
+  p.ntaps = (int)pk.taps.size();
+  for (int i = 0; i < p.ntaps; ++i) {
+    p.dy[i] = pk.taps[i].dy;
+    p.dx[i] = pk.taps[i].dx;
+  }
+  p.sy = p.sx = 1;
+  return p;
+}
+
+// Channels-last activation geometry: (B, H, W, C).
+void set_input(ConvParams& p, const float* x, int B, int H, int W, int C) {
+  (void)B;
+  p.x = x;
+  p.Hin = H;
+  p.Win = W;
+  p.Cin = C;
+  p.i_cs = 1;
+  p.i_xs = C;
+  p.i_ys = (int64_t)W * C;
+  p.i_bs = (int64_t)H * W * C;
+}
+void set_output(ConvParams& p, float* out, int B, int Hq, int Wq, int Cout) {
+  p.B = B;
+  p.Hq = Hq;
+  p.Wq = Wq;
+  p.out = out;
+  p.o_xs = Cout;
+  p.o_ys = (int64_t)Wq * Cout;
+  p.o_bs = (int64_t)Hq * Wq * Cout;
+  p.o_off = 0;
+}
+
+// DConv residual branch in place on x (rows, T, C) channels-last
+// (host.rs:985-1059): conv1 (k3, dilation 2^d) with its row moments, then the
+// 1x1 GEMM twice — once for the moments of its output, once for
+// GroupNorm + GLU + LayerScale + residual.
+void run_dconv(dmx_handle* h, const DConvFull& dc, float* x, int rows, int T) {
+  const int C = dc.C, hid = dc.hidden;
+  float* y = h->falloc((size_t)rows * T * hid);
+  double* st = h->dalloc((size_t)rows * 4);
+  for (int d = 0; d < 2; ++d) {
+    const DConvLayerW& L = dc.layer[d];
+    h->zero(st, (size_t)rows * 4 * sizeof(double));
+    double* st1 = st;
+    double* st2 = st + 2 * rows;
+    {
+      ConvParams p = base_params(L.conv1, h->wdev);
+      set_input(p, x, rows, 1, T, C);
+      set_output(p, y, rows, 1, T, hid);
+      p.epi_stats = st1;
+      p.epi_rowlen = T;
+      h->gemm(p, PRO_NONE, EPI_STORE_STATS, "dconv.conv1");
+    }
+    ConvParams p = base_params(L.conv2, h->wdev);
+    set_input(p, y, rows, 1, T, hid);
+    set_output(p, x, rows, 1, T, C);
+    p.pro_stats = st1;
+    p.pro_rowlen = T;
+    p.pro_count = (double)hid * T;
+    p.pro_scale = h->W(L.n1w.off);
+    p.pro_shift = h->W(L.n1b.off);
+    p.epi_stats = st2;
+    p.epi_rowlen = T;
+    h->gemm(p, PRO_GN_GELU, EPI_STATS, "dconv.stats");
+    p.epi_stats = nullptr;
+    p.epi_nstats = st2;
+    p.epi_count = 2.0 * C * T;
+    p.epi_gw = h->W(L.n2w.off);
+    p.epi_gb = h->W(L.n2b.off);
+    p.epi_half = C;
+    p.epi_gamma = h->W(L.gamma.off);
+    p.epi_res = x;
+    h->gemm(p, PRO_GN_GELU, EPI_DCONV_TAIL, "dconv.tail");
+  }
+}
+
+// Host-side tracing: copy a device tensor and hand it over in the reference's
+// layout. kind 0: freq (B, F, T, C) -> (B, C, F, T); kind 1: time (B, T, C)
+// -> (B, C, T); kind 2: as is with the given shape.
+void trace_tensor(dmx_handle* h, const std::string& name, const float* dev, int kind,
+                  std::vector<int64_t> dims) {
+  if (!h->trace || h->measuring) return;
+  size_t n = 1;
+  for (int64_t d : dims) n *= (size_t)d;
+  std::vector<float> host(n), out(n);
+  CK(cudaStreamSynchronize(h->stream));
+  CK(cudaMemcpy(host.data(), dev, n * sizeof(float), cudaMemcpyDeviceToHost));
+  std::vector<int64_t> shape;
+  if (kind == 0) {
+    const int64_t B = dims[0], F = dims[1], T = dims[2], C = dims[3];
+    for (int64_t b = 0; b < B; ++b)
+      for (int64_t f = 0; f < F; ++f)
+        for (int64_t t = 0; t < T; ++t)
+          for (int64_t c = 0; c < C; ++c)
+            out[((b * C + c) * F + f) * T + t] = host[((b * F + f) * T + t) * C + c];
+    shape = {B, C, F, T};
+  } else if (kind == 1) {
+    const int64_t B = dims[0], T = dims[1], C = dims[2];
+    for (int64_t b = 0; b < B; ++b)
+      for (int64_t t = 0; t < T; ++t)
+        for (int64_t c = 0; c < C; ++c) out[(b * C + c) * T + t] = host[(b * T + t) * C + c];
+    shape = {B, C, T};
+  } else {
+    out = host;
+    shape = dims;
+  }
+  h->trace(name.c_str(), out.data(), shape.data(), (int)shape.size(), h->trace_user);
+}
+
+// One transformer layer on stream X (B, n, 512), in place (host.rs:1315-1429).
+struct XfBufs {
+  float *xn, *kvn, *qkv, *kv2, *att, *hid;
+  double* stats;
+};
+
+void xf_gemm(dmx_handle* h, const char* tag, const Packed& pk, const float* in, int B, int n,
+             float* out, int epi, const float* res = nullptr, const float* gamma = nullptr,
+             double* stats = nullptr) {
+  ConvParams p = base_params(pk, h->wdev);
+  const int cin = pk.K;
+  set_input(p, in, B, 1, n, cin);
+  set_output(p, out, B, 1, n, pk.N);
+  p.epi_res = res;
+  p.epi_gamma = gamma;
+  p.epi_stats = stats;
+  p.epi_rowlen = n;
+  h->gemm(p, PRO_NONE, epi, tag);
+}
+
+void xf_tail(dmx_handle* h, const LayerW& L, float* X, int B, int n, const XfBufs& bb,
+             const Vec& nw, const Vec& nb) {
+  // out-projection + LayerScale residual
+  xf_gemm(h, "xf.outproj", L.out, bb.att, B, n, X, EPI_RESIDUAL, X, h->W(L.g1.off));
+  h->mark("xf.layernorm");
+  if (h->live()) launch_layer_norm(X, (int64_t)B * n, n, h->W(nw.off), h->W(nb.off), nullptr, bb.xn, h->stream);
+  ++h->launches;
+  xf_gemm(h, "xf.ffn1", L.lin1, bb.xn, B, n, bb.hid, EPI_GELU);
+  h->zero(bb.stats, (size_t)B * 2 * sizeof(double));
+  xf_gemm(h, "xf.ffn2", L.lin2, bb.hid, B, n, X, EPI_RESIDUAL, X, h->W(L.g2.off), bb.stats);
+  h->mark("xf.groupnorm");
+  if (h->live()) launch_group_norm_apply(X, B, n, bb.stats, h->W(L.now.off), h->W(L.nob.off), h->stream);
+  ++h->launches;
+}
+
+void xf_self(dmx_handle* h, const LayerW& L, float* X, int B, int n, const XfBufs& bb) {
+  h->mark("xf.layernorm");
+  if (h->live()) launch_layer_norm(X, (int64_t)B * n, n, h->W(L.n1w.off), h->W(L.n1b.off), nullptr, bb.xn, h->stream);
+  ++h->launches;
+  xf_gemm(h, "xf.qkv", L.qkv, bb.xn, B, n, bb.qkv, EPI_STORE);
+  h->mark("xf.attention");
+  if (h->live())
+    launch_flash_attention(bb.qkv, 1536, bb.qkv + 512, bb.qkv + 1024, 1536, bb.att, 512, B, 8, n, n,
+                           0.125f, h->stream);
+  ++h->launches;
+  xf_tail(h, L, X, B, n, bb, L.n2w, L.n2b);
+}
+
+// kv projection of the other stream for a cross layer (LN2 of this layer).
+void xf_cross_kv(dmx_handle* h, const LayerW& L, const float* other, int B, int n_other,
+                 float* kv_out, float* scratch) {
+  h->mark("xf.layernorm");
+  if (h->live())
+    launch_layer_norm(other, (int64_t)B * n_other, n_other, h->W(L.n2w.off), h->W(L.n2b.off), nullptr,
+                      scratch, h->stream);
+  ++h->launches;
+  xf_gemm(h, "xf.kv", L.kv, scratch, B, n_other, kv_out, EPI_STORE);
+}
+
+void xf_cross(dmx_handle* h, const LayerW& L, float* X, int B, int n, const float* kv, int n_other,
+              const XfBufs& bb) {
+  h->mark("xf.layernorm");
+  if (h->live()) launch_layer_norm(X, (int64_t)B * n, n, h->W(L.n1w.off), h->W(L.n1b.off), nullptr, bb.xn, h->stream);
+  ++h->launches;
+  xf_gemm(h, "xf.q", L.q, bb.xn, B, n, bb.qkv, EPI_STORE);
+  h->mark("xf.attention");
+  if (h->live())
+    launch_flash_attention(bb.qkv, 512, kv, kv + 512, 1024, bb.att, 512, B, 8, n, n_other, 0.125f,
+                           h->stream);
+  ++h->launches;
+  xf_tail(h, L, X, B, n, bb, L.n3w, L.n3b);
+}
+
+// The whole forward of G segments: mix (G, 2, L) device, normalised chunks ->
+// out (G, 4, 2, L) device (Htdemucs::forward, host.rs:202-520).
+void forward(dmx_handle* h, const float* mix, int G, float* out) {
+  const int L = kSegment;
+  const Model& m = h->m;
+  h->ws_off = 0;
+  cudaStream_t s = h->stream;
+  const float2* tw = reinterpret_cast<const float2*>(h->W(m.tw_off));
+
+  // (a) spectrogram + moments
+  double* mom = h->dalloc((size_t)G * 4);
+  float4* norm = static_cast<float4*>(h->alloc((size_t)G * 2 * sizeof(float4)));
+  float4* norm_f = norm;
+  float4* norm_t = norm + G;
+  float* X = h->falloc((size_t)G * kBins * kFrames * 4);
+  h->zero(mom, (size_t)G * 4 * sizeof(double));
+  h->mark("spec.stft");
+  if (h->live()) {
+    launch_stft_cac(mix, G, h->W(m.window.off), tw, X, mom, s);
+    launch_wave_moments(mix, G, 2LL * L, mom + 2 * G, s);
+    launch_norm_finalize(mom, (double)kBins * kFrames * 4, G, norm_f, s);
+    launch_norm_finalize(mom + 2 * G, 2.0 * L, G, norm_t, s);
+    h->after("spectrogram");
+  }
+  h->launches += 4;
+
+  // (b) encoders
+  float* skip[4];
+  float* tskip[4];
+  int Fs[5], Cs[5], Ts[5], TCs[5], lengths_t[4];
+  Fs[0] = kBins;
+  Cs[0] = 4;
+  Ts[0] = L;
+  TCs[0] = 2;
+  const float* xin = X;
+  const float* tin = mix;
+  for (int i = 0; i < 4; ++i) {
+    // time encoder (host.rs:625-678)
+    {
+      const EncW& E = m.tenc[i];
+      const int Tin = Ts[i];
+      lengths_t[i] = Tin;
+      const int Tpad = (Tin + 3) / 4 * 4;
+      const int To = (Tpad + 4 - 8) / 4 + 1;
+      const int Co = E.cout;
+      float* y = h->falloc((size_t)G * To * Co);
+      ConvParams p = base_params(E.conv, h->wdev);
+      if (i == 0) {  // raw (G, 2, L) waveform, normalised on load
+        p.x = tin;
+        p.Hin = 1;
+        p.Win = L;
+        p.Cin = 2;
+        p.i_cs = L;
+        p.i_xs = 1;
+        p.i_ys = 0;
+        p.i_bs = 2LL * L;
+        p.pro_scale = reinterpret_cast<const float*>(norm_t);
+      } else {
+        set_input(p, tin, G, 1, Tin, TCs[i]);
+      }
+      p.sx = 4;
+      set_output(p, y, G, 1, To, Co);
+      h->gemm(p, i == 0 ? PRO_BATCH_AFFINE : PRO_NONE, EPI_GELU, "tenc.conv");
+      run_dconv(h, h->tenc_dc[i], y, G, To);
+      float* z = h->falloc((size_t)G * To * Co);
+      ConvParams r = base_params(E.rewrite, h->wdev);
+      set_input(r, y, G, 1, To, Co);
+      set_output(r, z, G, 1, To, Co);
+      h->gemm(r, PRO_NONE, EPI_GLU, "tenc.rewrite");
+      tskip[i] = z;
+      tin = z;
+      Ts[i + 1] = To;
+      TCs[i + 1] = Co;
+      trace_tensor(h, "tencoder." + std::to_string(i), z, 1, {G, To, Co});
+    }
+    // freq encoder (host.rs:577-622)
+    {
+      const EncW& E = m.enc[i];
+      const int F = Fs[i], Fo = (F + 4 - 8) / 4 + 1, Co = E.cout;
+      float* y = h->falloc((size_t)G * Fo * kFrames * Co);
+      ConvParams p = base_params(E.conv, h->wdev);
+      set_input(p, xin, G, F, kFrames, Cs[i]);
+      p.sy = 4;
+      if (i == 0) p.pro_scale = reinterpret_cast<const float*>(norm_f);
+      set_output(p, y, G, Fo, kFrames, Co);
+      h->gemm(p, i == 0 ? PRO_BATCH_AFFINE : PRO_NONE, EPI_GELU, "enc.conv");
+      run_dconv(h, h->enc_dc[i], y, G * Fo, kFrames);
+      float* z = h->falloc((size_t)G * Fo * kFrames * Co);
+      ConvParams r = base_params(E.rewrite, h->wdev);
+      set_input(r, y, G, Fo, kFrames, Co);
+      set_output(r, z, G, Fo, kFrames, Co);
+      if (i == 0) r.epi_emb = h->W(m.emb.off);
+      h->gemm(r, PRO_NONE, i == 0 ? EPI_GLU_EMB : EPI_GLU, "enc.rewrite");
+      skip[i] = z;
+      xin = z;
+      Fs[i + 1] = Fo;
+      Cs[i + 1] = Co;
+      trace_tensor(h, i == 0 ? "encoder.0.post_emb" : "encoder." + std::to_string(i), z, 0,
+                   {G, Fo, kFrames, Co});
+    }
+  }
+
+  // (c) channel up-samplers into token layouts (host.rs:320-338, 845-890)
+  const int Fb = Fs[4], Tb = kFrames, ntok = Fb * Tb, Tt = Ts[4];
+  const int D = 512;
+  float* S = h->falloc((size_t)G * ntok * D);
+  float* Tk = h->falloc((size_t)G * Tt * D);
+  XfBufs bb;
+  bb.xn = h->falloc((size_t)G * ntok * D);
+  bb.kvn = h->falloc((size_t)G * ntok * D);
+  bb.qkv = h->falloc((size_t)G * ntok * 3 * D);
+  bb.kv2 = h->falloc((size_t)G * ntok * 2 * D);
+  bb.att = h->falloc((size_t)G * ntok * D);
+  bb.hid = h->falloc((size_t)G * ntok * 4 * D);
+  bb.stats = h->dalloc((size_t)G * 2);
+  {
+    ConvParams p = base_params(m.up, h->wdev);
+    set_input(p, skip[3], G, Fb, Tb, Cs[4]);
+    p.B = G;
+    p.Hq = Fb;
+    p.Wq = Tb;
+    p.out = bb.kvn;  // tokens t*Fb + f
+    p.o_bs = (int64_t)ntok * D;
+    p.o_ys = D;
+    p.o_xs = (int64_t)Fb * D;
+    h->gemm(p, PRO_NONE, EPI_STORE, "xf.upsample");
+    ConvParams q = base_params(m.up_t, h->wdev);
+    set_input(q, tskip[3], G, 1, Tt, TCs[4]);
+    set_output(q, bb.kv2, G, 1, Tt, D);
+    h->gemm(q, PRO_NONE, EPI_STORE, "xf.upsample");
+    h->mark("xf.layernorm");
+    if (h->live()) {
+      launch_layer_norm(bb.kvn, (int64_t)G * ntok, ntok, h->W(m.norm_in_w.off), h->W(m.norm_in_b.off),
+                        h->W(m.pos2d.off), S, s);
+      launch_layer_norm(bb.kv2, (int64_t)G * Tt, Tt, h->W(m.norm_in_t_w.off), h->W(m.norm_in_t_b.off),
+                        h->W(m.pos1d.off), Tk, s);
+    }
+    h->launches += 2;
+    trace_tensor(h, "crosstransformer.in#0", S, 2, {G, ntok, D});
+    trace_tensor(h, "crosstransformer.in#1", Tk, 2, {G, Tt, D});
+  }
+  // (d) five layers, alternating self / cross (host.rs:899-936)
+  for (int l = 0; l < 5; ++l) {
+    const LayerW& A = m.layers[l];
+    const LayerW& At = m.layers_t[l];
+    if (!A.cross) {
+      xf_self(h, A, S, G, ntok, bb);
+      xf_self(h, At, Tk, G, Tt, bb);
+    } else {
+      // kv for the time stream from the OLD spectral stream, first
+      xf_cross_kv(h, At, S, G, ntok, bb.kv2, bb.kvn);
+      float* kv_s = bb.hid;  // spectral layer's kv from the time stream (hid is free here)
+      xf_cross_kv(h, A, Tk, G, Tt, kv_s, bb.xn);
+      // the spectral layer needs its kv before xf_tail reuses hid: copy-free
+      // ordering — attention consumes kv_s before the FFN writes hid.
+      xf_cross(h, A, S, G, ntok, kv_s, Tt, bb);
+      xf_cross(h, At, Tk, G, Tt, bb.kv2, ntok, bb);
+    }
+    trace_tensor(h, "crosstransformer.layers." + std::to_string(l), S, 2, {G, ntok, D});
+    trace_tensor(h, "crosstransformer.layers_t." + std::to_string(l), Tk, 2, {G, Tt, D});
+  }
+  // (e) channel down-samplers back to (G, F, T, 384) and (G, T, 384)
+  float* x = h->falloc((size_t)G * ntok * Cs[4]);
+  float* xt = h->falloc((size_t)G * Tt * TCs[4]);
+  {
+    ConvParams p = base_params(m.down, h->wdev);
+    p.x = S;
+    p.Hin = Fb;
+    p.Win = Tb;
+    p.Cin = D;
+    p.i_cs = 1;
+    p.i_ys = D;
+    p.i_xs = (int64_t)Fb * D;
+    p.i_bs = (int64_t)ntok * D;
+    set_output(p, x, G, Fb, Tb, Cs[4]);
+    h->gemm(p, PRO_NONE, EPI_STORE, "xf.downsample");
+    ConvParams q = base_params(m.down_t, h->wdev);
+    set_input(q, Tk, G, 1, Tt, D);
+    set_output(q, xt, G, 1, Tt, TCs[4]);
+    h->gemm(q, PRO_NONE, EPI_STORE, "xf.downsample");
+  }
+
+  // (f) decoders, innermost first (host.rs:408-450)
+  int F = Fb, C = Cs[4], Tc = Tt, Ct = TCs[4];
+  for (int e = 0; e < 4; ++e) {
+    const bool last = e == 3;
+    const int j = 3 - e;
+    {  // freq decoder (host.rs:682-759)
+      const DecW& Dw = m.dec[e];
+      float* g = h->falloc((size_t)G * F * kFrames * C);
+      ConvParams r = base_params(Dw.rewrite, h->wdev);
+      set_input(r, x, G, F, kFrames, C);
+      r.x2 = skip[j];
+      set_output(r, g, G, F, kFrames, C);
+      h->gemm(r, PRO_ADD, EPI_GLU, "dec.rewrite");
+      run_dconv(h, h->dec_dc[e], g, G * F, kFrames);
+      const int Co = Dw.cout, Fo = 4 * F;
+      float* o = h->falloc((size_t)G * Fo * kFrames * Co);
+      for (int ph = 0; ph < 4; ++ph) {
+        ConvParams p = base_params(Dw.convt[ph], h->wdev);
+        set_input(p, g, G, F, kFrames, C);
+        p.B = G;
+        p.Hq = F;
+        p.Wq = kFrames;
+        p.out = o;
+        p.o_xs = Co;
+        p.o_ys = 4LL * kFrames * Co;
+        p.o_off = (int64_t)ph * kFrames * Co;
+        p.o_bs = (int64_t)Fo * kFrames * Co;
+        h->gemm(p, PRO_NONE, last ? EPI_STORE : EPI_GELU, "dec.convtr");
+      }
+      x = o;
+      F = Fo;
+      C = Co;
+      trace_tensor(h, "decoder." + std::to_string(j), x, 0, {G, F, kFrames, C});
+    }
+    {  // time decoder (host.rs:763-827)
+      const DecW& Dw = m.tdec[e];
+      float* g = h->falloc((size_t)G * Tc * Ct);
+      ConvParams r = base_params(Dw.rewrite, h->wdev);
+      set_input(r, xt, G, 1, Tc, Ct);
+      r.x2 = tskip[j];
+      set_output(r, g, G, 1, Tc, Ct);
+      h->gemm(r, PRO_ADD, EPI_GLU, "tdec.rewrite");
+      run_dconv(h, h->tdec_dc[e], g, G, Tc);
+      const int Co = Dw.cout, len = lengths_t[j];
+      float* o = h->falloc((size_t)G * len * Co);
+      for (int ph = 0; ph < 4; ++ph) {
+        const int nq = (len - ph + 3) / 4;
+        if (nq <= 0) continue;
+        ConvParams p = base_params(Dw.convt[ph], h->wdev);
+        set_input(p, g, G, 1, Tc, Ct);
+        // taps move along time for the waveform branch
+        for (int t = 0; t < p.ntaps; ++t) {
+          p.dx[t] = p.dy[t];
+          p.dy[t] = 0;
+        }
+        p.B = G;
+        p.Hq = 1;
+        p.Wq = nq;
+        p.out = o;
+        p.o_xs = 4LL * Co;
+        p.o_ys = 0;
+        p.o_off = (int64_t)ph * Co;
+        p.o_bs = (int64_t)len * Co;
+        h->gemm(p, PRO_NONE, last ? EPI_STORE : EPI_GELU, "tdec.convtr");
+      }
+      xt = o;
+      Tc = len;
+      Ct = Co;
+      trace_tensor(h, "tdecoder." + std::to_string(j), xt, 1, {G, Tc, Ct});
+    }
+  }
+
+  // (g) iSTFT + branch sum (host.rs:466-519)
+  float* frames = h->falloc((size_t)G * 8 * kFrames * kNfft);
+  h->mark("spec.istft");
+  if (h->live()) {
+    launch_istft(x, norm_f, h->W(m.window.off), tw, frames, h->W(m.env.off), xt, norm_t, out, G, s);
+    h->after("istft");
+  }
+  h->launches += 2;
+}
+
+void finish_stage_times(dmx_handle* h) {
+  if (h->marks.empty()) return;
+  CK(cudaEventSynchronize(h->marks.back().second));
+  h->stage_names.clear();
+  h->stage_ms.clear();
+  h->stage_counts.clear();
+  std::map<std::string, size_t> index;
+  for (size_t i = 0; i + 1 < h->marks.size(); ++i) {
+    float ms = 0.f;
+    CK(cudaEventElapsedTime(&ms, h->marks[i].second, h->marks[i + 1].second));
+    auto it = index.find(h->marks[i].first);
+    if (it == index.end()) {
+      index[h->marks[i].first] = h->stage_names.size();
+      h->stage_names.push_back(h->marks[i].first);
+      h->stage_ms.push_back(ms);
+      h->stage_counts.push_back(1);
+    } else {
+      h->stage_ms[it->second] += ms;
+      h->stage_counts[it->second] += 1;
+    }
+  }
+  for (auto& mk : h->marks) cudaEventDestroy(mk.second);
+  h->marks.clear();
+}
+
+// Sizes the workspace for `G` segments by a dry run of the launch sequence.
+void ensure_workspace(dmx_handle* h, int G) {
+  h->measuring = true;
+  h->ws_off = 0;
+  h->ws_peak = 0;
+  forward(h, nullptr, G, nullptr);
+  h->measuring = false;
+  const size_t need = h->ws_peak + (1 << 20);
+  if (need > h->ws_cap) {
+    if (h->ws) CK(cudaFree(h->ws));
+    h->ws = nullptr;
+    h->ws_cap = 0;
+    CK(cudaMalloc(&h->ws, need));
+    h->ws_cap = need;
+  }
+}
+
+void run_forward(dmx_handle* h, const float* mix_dev, int64_t n, float* out_dev) {
+  if (n <= 0) throw Error(DMX_ERR_INVALID, "n_segments must be positive");
+  const int cap = std::max(1, h->cfg.max_batch);
+  for (int64_t s0 = 0; s0 < n; s0 += cap) {
+    const int G = (int)std::min<int64_t>(cap, n - s0);
+    ensure_workspace(h, G);
+    forward(h, mix_dev + s0 * 2 * kSegment, G, out_dev + s0 * 8 * kSegment);
+  }
+}
+
+void load_model(dmx_handle* h, const std::map<std::string, HostTensor>& t) {
+  WeightBuilder wb;
+  Loader L{t, wb};
+  Model& m = h->m;
+  auto line8 = [](bool along_h) {
+    std::vector<std::pair<int, int>> k;
+    std::vector<Tap> taps;
+    for (int i = 0; i < 8; ++i) {
+      k.emplace_back(along_h ? i : 0, along_h ? 0 : i);
+      taps.push_back(along_h ? Tap{i - 2, 0} : Tap{0, i - 2});
+    }
+    return std::make_pair(k, taps);
+  };
+  auto load_dc = [&](const std::string& prefix, int C, DConvFull* dc) {
+    dc->C = C;
+    dc->hidden = C / 8;
+    for (int d = 0; d < 2; ++d) {
+      const std::string at = prefix + ".dconv.layers." + std::to_string(d);
+      const int dil = 1 << d;
+      DConvLayerW& Lw = dc->layer[d];
+      Lw.conv1 = L.conv(at + ".0", {C / 8, C, 3}, {{0, 0}, {0, 1}, {0, 2}},
+                        {{0, -dil}, {0, 0}, {0, dil}}, false);
+      Lw.n1w = L.vec(at + ".1.weight", C / 8);
+      Lw.n1b = L.vec(at + ".1.bias", C / 8);
+      Lw.conv2 = L.conv(at + ".3", {2 * C, C / 8, 1}, {{0, 0}}, {{0, 0}}, true);
+      Lw.n2w = L.vec(at + ".4.weight", 2 * C);
+      Lw.n2b = L.vec(at + ".4.bias", 2 * C);
+      Lw.gamma = L.vec(at + ".6.scale", C);
+    }
+  };
+  int chin_z = 4, chin = 2, chout = 48;
+  for (int i = 0; i < 4; ++i) {
+    const std::string e = "encoder." + std::to_string(i), te = "tencoder." + std::to_string(i);
+    auto fl = line8(true);
+    m.enc[i].conv = L.conv(e + ".conv", {chout, chin_z, 8, 1}, fl.first, fl.second, false);
+    m.enc[i].rewrite = L.conv(e + ".rewrite", {2 * chout, chout, 1, 1}, {{0, 0}}, {{0, 0}}, true);
+    m.enc[i].cin = chin_z;
+    m.enc[i].cout = chout;
+    load_dc(e, chout, &h->enc_dc[i]);
+    auto tl = line8(false);
+    m.tenc[i].conv = L.conv(te + ".conv", {chout, chin, 8}, tl.first, tl.second, false);
+    m.tenc[i].rewrite = L.conv(te + ".rewrite", {2 * chout, chout, 1}, {{0, 0}}, {{0, 0}}, true);
+    m.tenc[i].cin = chin;
+    m.tenc[i].cout = chout;
+    load_dc(te, chout, &h->tenc_dc[i]);
+    chin_z = chin = chout;
+    chout *= 2;
+  }
+  for (int e = 0; e < 4; ++e) {
+    const int j = 3 - e;
+    const int cin = 48 << j;
+    const int cout_f = j == 0 ? 16 : 48 << (j - 1);
+    const int cout_t = j == 0 ? 8 : 48 << (j - 1);
+    const std::string d = "decoder." + std::to_string(j), td = "tdecoder." + std::to_string(j);
+    std::vector<std::pair<int, int>> k9;
+    std::vector<Tap> t9;
+    for (int ky = 0; ky < 3; ++ky)
+      for (int kx = 0; kx < 3; ++kx) {
+        k9.emplace_back(ky, kx);
+        t9.push_back({ky - 1, kx - 1});
+      }
+    m.dec[e].rewrite = L.conv(d + ".rewrite", {2 * cin, cin, 3, 3}, k9, t9, true);
+    for (int ph = 0; ph < 4; ++ph) m.dec[e].convt[ph] = L.convt(d + ".conv_tr", {cin, cout_f, 8, 1}, ph);
+    m.dec[e].cin = cin;
+    m.dec[e].cout = cout_f;
+    load_dc(d, cin, &h->dec_dc[e]);
+    m.tdec[e].rewrite = L.conv(td + ".rewrite", {2 * cin, cin, 3}, {{0, 0}, {0, 1}, {0, 2}},
+                               {{0, -1}, {0, 0}, {0, 1}}, true);
+    for (int ph = 0; ph < 4; ++ph) m.tdec[e].convt[ph] = L.convt(td + ".conv_tr", {cin, cout_t, 8}, ph);
+    m.tdec[e].cin = cin;
+    m.tdec[e].cout = cout_t;
+    load_dc(td, cin, &h->tdec_dc[e]);
+  }
+  m.up = L.conv("channel_upsampler", {512, 384, 1}, {{0, 0}}, {{0, 0}}, false);
+  m.up_t = L.conv("channel_upsampler_t", {512, 384, 1}, {{0, 0}}, {{0, 0}}, false);
+  m.down = L.conv("channel_downsampler", {384, 512, 1}, {{0, 0}}, {{0, 0}}, false);
+  m.down_t = L.conv("channel_downsampler_t", {384, 512, 1}, {{0, 0}}, {{0, 0}}, false);
+  m.norm_in_w = L.vec("crosstransformer.norm_in.weight", 512);
+  m.norm_in_b = L.vec("crosstransformer.norm_in.bias", 512);
+  m.norm_in_t_w = L.vec("crosstransformer.norm_in_t.weight", 512);
+  m.norm_in_t_b = L.vec("crosstransformer.norm_in_t.bias", 512);
+  for (int s = 0; s < 2; ++s)
+    for (int l = 0; l < 5; ++l) {
+      LayerW& Lw = s == 0 ? m.layers[l] : m.layers_t[l];
+      const std::string at = std::string("crosstransformer.") + (s == 0 ? "layers." : "layers_t.") + std::to_string(l);
+      Lw.cross = l % 2 == 1;
+      const std::string attn = at + (Lw.cross ? ".cross_attn" : ".self_attn");
+      if (Lw.cross) {
+        Lw.q = L.linear(attn + ".in_proj_weight", attn + ".in_proj_bias", 1536, 512, 0, 512);
+        Lw.kv = L.linear(attn + ".in_proj_weight", attn + ".in_proj_bias", 1536, 512, 512, 1024);
+        Lw.n3w = L.vec(at + ".norm3.weight", 512);
+        Lw.n3b = L.vec(at + ".norm3.bias", 512);
+      } else {
+        Lw.qkv = L.linear(attn + ".in_proj_weight", attn + ".in_proj_bias", 1536, 512, 0, 1536);
+      }
+      Lw.out = L.linear(attn + ".out_proj.weight", attn + ".out_proj.bias", 512, 512, 0, 512);
+      Lw.lin1 = L.linear(at + ".linear1.weight", at + ".linear1.bias", 2048, 512, 0, 2048);
+      Lw.lin2 = L.linear(at + ".linear2.weight", at + ".linear2.bias", 512, 2048, 0, 512);
+      Lw.n1w = L.vec(at + ".norm1.weight", 512);
+      Lw.n1b = L.vec(at + ".norm1.bias", 512);
+      Lw.n2w = L.vec(at + ".norm2.weight", 512);
+      Lw.n2b = L.vec(at + ".norm2.bias", 512);
+      Lw.now = L.vec(at + ".norm_out.weight", 512);
+      Lw.nob = L.vec(at + ".norm_out.bias", 512);
+      Lw.g1 = L.vec(at + ".gamma_1.scale", 512);
+      Lw.g2 = L.vec(at + ".gamma_2.scale", 512);
+    }
+  // Tables computed on the host in f32 exactly as the reference does.
+  {
+    const HostTensor& e = L.get("freq_emb.embedding.weight", {512, 48});
+    m.emb.n = 512 * 48;
+    m.emb.off = wb.alloc(m.emb.n);
+    for (int i = 0; i < m.emb.n; ++i) wb.host[m.emb.off + i] = 0.2f * (e.data[i] * 10.0f);
+  }
+  {  // create_2d_sin_embedding (host.rs:1078-1106): token t*8 + f
+    const int dim = 512, half = 256, pairs = 128, height = 8, width = 336;
+    const float log_period = std::log(10000.0f) / (float)half;
+    std::vector<float> div(pairs);
+    for (int jj = 0; jj < pairs; ++jj) div[jj] = std::exp(-((float)(2 * jj)) * log_period);
+    m.pos2d.n = width * height * dim;
+    m.pos2d.off = wb.alloc(m.pos2d.n);
+    for (int t = 0; t < width; ++t)
+      for (int f = 0; f < height; ++f) {
+        float* o = &wb.host[m.pos2d.off + ((size_t)t * height + f) * dim];
+        for (int jj = 0; jj < pairs; ++jj) {
+          const float w = (float)t * div[jj], hh = (float)f * div[jj];
+          o[2 * jj] = std::sin(w);
+          o[2 * jj + 1] = std::cos(w);
+          o[half + 2 * jj] = std::sin(hh);
+          o[half + 2 * jj + 1] = std::cos(hh);
+        }
+      }
+  }
+  {  // create_sin_embedding (host.rs:1110-1122)
+    const int length = 1344, dim = 512, half = 256;
+    m.pos1d.n = length * dim;
+    m.pos1d.off = wb.alloc(m.pos1d.n);
+    for (int t = 0; t < length; ++t)
+      for (int i = 0; i < half; ++i) {
+        const float exponent = (float)i / ((float)half - 1.0f);
+        const float phase = (float)t / std::pow(10000.0f, exponent);
+        wb.host[m.pos1d.off + (size_t)t * dim + i] = std::cos(phase);
+        wb.host[m.pos1d.off + (size_t)t * dim + half + i] = std::sin(phase);
+      }
+  }
+  {  // periodic Hann (stft.rs:54-61), envelope, twiddles, OLA weight
+    m.window.n = kNfft;
+    m.window.off = wb.alloc(kNfft);
+    for (int i = 0; i < kNfft; ++i)
+      wb.host[m.window.off + i] = (float)(0.5 - 0.5 * std::cos(2.0 * M_PI * (double)i / (double)kNfft));
+    m.env.n = kHop;
+    m.env.off = wb.alloc(kHop);
+    for (int r = 0; r < kHop; ++r) {
+      float env = 0.f;  // frames in increasing order: offsets r+3072 .. r
+      for (int k = 3; k >= 0; --k) {
+        const float w = wb.host[m.window.off + r + k * kHop];
+        env += w * w;
+      }
+      wb.host[m.env.off + r] = env;
+    }
+    m.tw_off = wb.alloc(2 * 2048);
+    for (int k = 0; k < 2048; ++k) {
+      const double a = 2.0 * M_PI * (double)k / (double)kNfft;
+      wb.host[m.tw_off + 2 * k] = (float)std::cos(a);
+      wb.host[m.tw_off + 2 * k + 1] = (float)-std::sin(a);
+    }
+    // transition_weight(segment, 1.0) (pipeline.rs:117-131)
+    const int seg = h->cfg.segment_samples, half = seg / 2;
+    m.ola_w.n = seg;
+    m.ola_w.off = wb.alloc(seg);
+    for (int i = 0; i < seg; ++i)
+      wb.host[m.ola_w.off + i] = (float)(i < half ? i + 1 : seg - i);
+    const float mx = std::max((float)std::max(half, seg - half), 1.0f);
+    for (int i = 0; i < seg; ++i) wb.host[m.ola_w.off + i] = wb.host[m.ola_w.off + i] / mx;
+  }
+  CK(cudaMalloc(&h->wdev, wb.host.size() * sizeof(float)));
+  CK(cudaMemcpy(h->wdev, wb.host.data(), wb.host.size() * sizeof(float), cudaMemcpyHostToDevice));
+}
+
+int fail(const Error& e) {
+  g_error = e.what();
+  return e.code;
+}
+int fail_std(const std::exception& e) {
+  g_error = e.what();
+  return DMX_ERR_INVALID;
+}
+
+}  // namespace
+
+// ---------------------------------------------------------------------------
+// C ABI
+// ---------------------------------------------------------------------------
+extern "C" {
+
+void dmx_default_config(dmx_config* c) {
+  c->sources = 4;
+  c->audio_channels = 2;
+  c->samplerate = 44100;
+  c->segment_samples = kSegment;
+  c->precision = DMX_FP32;
+  c->max_batch = 8;
+}
+
+const char* dmx_last_error(void) { return g_error.c_str(); }
+
+dmx_status dmx_create(const dmx_config* cfg, const void* blob, size_t len, int device,
+                      dmx_handle** out) {
+  if (!cfg || !blob || !out) {
+    g_error = "dmx_create: null argument";
+    return DMX_ERR_INVALID;
+  }
+  std::unique_ptr<dmx_handle> h(new dmx_handle());
+  try {
+    if (cfg->sources != 4 || cfg->audio_channels != 2 || cfg->samplerate != 44100 ||
+        cfg->segment_samples != kSegment)
+      throw Error(DMX_ERR_INVALID,
+                  "only the default htdemucs configuration is supported (4 sources, stereo, "
+                  "44100 Hz, 343980-sample segments)");
+    if (cfg->precision != DMX_FP32)
+      throw Error(DMX_ERR_INVALID, "this build implements precision DMX_FP32 only");
+    if (cfg->max_batch < 1 || cfg->max_batch > 256)
+      throw Error(DMX_ERR_INVALID, "max_batch must be in [1, 256]");
+    h->cfg = *cfg;
+    h->device = device;
+    CK(cudaSetDevice(device));
+    CK(cudaStreamCreateWithFlags(&h->stream, cudaStreamNonBlocking));
+    const auto tensors = parse_safetensors(blob, len);
+    load_model(h.get(), tensors);
+    const char* st = getenv("DMX_STAGE_TIMING");
+    h->stage_timing = st && st[0] == '1';
+    *out = h.release();
+    return DMX_OK;
+  } catch (const Error& e) {
+    return fail(e);
+  } catch (const std::exception& e) {
+    return fail_std(e);
+  }
+}
+
+void dmx_destroy(dmx_handle* h) {
+  if (!h) return;
+  cudaSetDevice(h->device);
+  if (h->stream) cudaStreamSynchronize(h->stream);
+  if (h->pending.done) cudaEventDestroy(h->pending.done);
+  cudaFree(h->wdev);
+  cudaFree(h->ws);
+  cudaFree(h->io_in);
+  cudaFree(h->io_out);
+  cudaFree(h->track_ws);
+  cudaFreeHost(h->pinned_in);
+  cudaFreeHost(h->pinned_out);
+  if (h->stream) cudaStreamDestroy(h->stream);
+  delete h;
+}
+
+dmx_status dmx_set_trace(dmx_handle* h, dmx_trace_fn fn, void* user) {
+  if (!h) return DMX_ERR_INVALID;
+  h->trace = fn;
+  h->trace_user = user;
+  return DMX_OK;
+}
+
+dmx_status dmx_forward_device(dmx_handle* h, const float* mix_dev, int64_t n, float* out_dev,
+                              void* stream) {
+  try {
+    CK(cudaSetDevice(h->device));
+    h->launches = 0;
+    cudaStream_t user = static_cast<cudaStream_t>(stream);
+    if (user && user != h->stream) {
+      cudaEvent_t e;
+      CK(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
+      CK(cudaEventRecord(e, user));
+      CK(cudaStreamWaitEvent(h->stream, e, 0));
+      run_forward(h, mix_dev, n, out_dev);
+      CK(cudaEventRecord(e, h->stream));
+      CK(cudaStreamWaitEvent(user, e, 0));
+      CK(cudaEventDestroy(e));
+    } else {
+      run_forward(h, mix_dev, n, out_dev);
+    }
+    h->mark("end");
+    finish_stage_times(h);
+    return DMX_OK;
+  } catch (const Error& e) {
+    return fail(e);
+  } catch (const std::exception& e) {
+    return fail_std(e);
+  }
+}
+
+static void ensure_io(dmx_handle* h, int64_t n) {
+  if (n <= h->io_cap) return;
+  cudaFree(h->io_in);
+  cudaFree(h->io_out);
+  cudaFreeHost(h->pinned_in);
+  cudaFreeHost(h->pinned_out);
+  h->io_in = h->io_out = h->pinned_in = h->pinned_out = nullptr;
+  CK(cudaMalloc(&h->io_in, (size_t)n * 2 * kSegment * sizeof(float)));
+  CK(cudaMalloc(&h->io_out, (size_t)n * 8 * kSegment * sizeof(float)));
+  CK(cudaMallocHost(&h->pinned_in, (size_t)n * 2 * kSegment * sizeof(float)));
+  CK(cudaMallocHost(&h->pinned_out, (size_t)n * 8 * kSegment * sizeof(float)));
+  h->io_cap = n;
+}
+
+dmx_status dmx_forward_start(dmx_handle* h, const float* mix, int64_t n, dmx_pending** out) {
+  try {
+    if (!h || !mix || !out || n <= 0) throw Error(DMX_ERR_INVALID, "dmx_forward_start: bad argument");
+    if (h->pending.h) throw Error(DMX_ERR_INVALID, "a forward is already queued on this handle");
+    CK(cudaSetDevice(h->device));
+    h->launches = 0;
+    ensure_io(h, n);
+    std::memcpy(h->pinned_in, mix, (size_t)n * 2 * kSegment * sizeof(float));
+    CK(cudaMemcpyAsync(h->io_in, h->pinned_in, (size_t)n * 2 * kSegment * sizeof(float),
+                       cudaMemcpyHostToDevice, h->stream));
+    run_forward(h, h->io_in, n, h->io_out);
+    h->mark("end");
+    CK(cudaMemcpyAsync(h->pinned_out, h->io_out, (size_t)n * 8 * kSegment * sizeof(float),
+                       cudaMemcpyDeviceToHost, h->stream));
+    if (!h->pending.done) CK(cudaEventCreateWithFlags(&h->pending.done, cudaEventDisableTiming));
+    CK(cudaEventRecord(h->pending.done, h->stream));
+    h->pending.h = h;
+    h->pending.n = n;
+    *out = &h->pending;
+    return DMX_OK;
+  } catch (const Error& e) {
+    return fail(e);
+  } catch (const std::exception& e) {
+    return fail_std(e);
+  }
+}
+
+dmx_status dmx_forward_collect(dmx_pending* p, float* out) {
+  try {
+    if (!p || !p->h || !out) throw Error(DMX_ERR_INVALID, "dmx_forward_collect: bad argument");
+    dmx_handle* h = p->h;
+    // bounded wait: poll the event with a deadline instead of blocking forever
+    const auto deadline = std::chrono::steady_clock::now() + std::chrono::seconds(600);
+    while (true) {
+      const cudaError_t e = cudaEventQuery(p->done);
+      if (e == cudaSuccess) break;
+      if (e != cudaErrorNotReady) CK(e);
+      if (std::chrono::steady_clock::now() > deadline) {
+        h->pending.h = nullptr;
+        throw Error(DMX_ERR_TIMEOUT, "forward did not complete within the deadline");
+      }
+      std::this_thread::sleep_for(std::chrono::microseconds(50));
+    }
+    std::memcpy(out, h->pinned_out, (size_t)p->n * 8 * kSegment * sizeof(float));
+    h->pending.h = nullptr;
+    finish_stage_times(h);
+    return DMX_OK;
+  } catch (const Error& e) {
+    return fail(e);
+  } catch (const std::exception& e) {
+    return fail_std(e);
+  }
+}
+
+int64_t dmx_num_chunks(int64_t view_length, int segment, double overlap) {
+  const int64_t stride = (int64_t)((1.0 - overlap) * (double)segment);
+  if (view_length <= 0 || stride <= 0) return 0;
+  return (view_length + stride - 1) / stride;
+}
+
+dmx_status dmx_track_shard(dmx_handle* h, const float* mix_norm_dev, int64_t length,
+                           int64_t shift_offset, int64_t max_shift, int segment, double overlap,
+                           double transition_power, int64_t chunk_lo, int64_t chunk_hi, int batch,
+                           float* acc_dev, int64_t view_lo, int64_t view_hi) {
+  try {
+    if (segment != kSegment) throw Error(DMX_ERR_INVALID, "segment must be 343980");
+    if (transition_power != 1.0) throw Error(DMX_ERR_INVALID, "transition_power must be 1");
+    CK(cudaSetDevice(h->device));
+    const int64_t stride = (int64_t)((1.0 - overlap) * (double)segment);
+    if (stride <= 0) throw Error(DMX_ERR_INVALID, "overlap leaves a zero stride");
+    const int cap = std::max(1, batch > 0 ? std::min(batch, h->cfg.max_batch) : h->cfg.max_batch);
+    ensure_io(h, cap);
+    for (int64_t c0 = chunk_lo; c0 < chunk_hi; c0 += cap) {
+      const int G = (int)std::min<int64_t>(cap, chunk_hi - c0);
+      h->mark("track.gather");
+      launch_gather_chunks(mix_norm_dev, length, shift_offset, max_shift, segment, stride, c0, G,
+                           h->io_in, h->stream);
+      ++h->launches;
+      run_forward(h, h->io_in, G, h->io_out);
+      h->mark("track.ola");
+      launch_ola_accumulate(h->io_out, length, shift_offset, max_shift, segment, stride, c0, G,
+                            h->W(h->m.ola_w.off), acc_dev, view_lo, view_hi, h->stream);
+      ++h->launches;
+      CK(cudaGetLastError());
+    }
+    return DMX_OK;
+  } catch (const Error& e) {
+    return fail(e);
+  } catch (const std::exception& e) {
+    return fail_std(e);
+  }
+}
+
+dmx_status dmx_separate_track_device(dmx_handle* h, const float* lr_dev, int64_t n,
+                                     const dmx_separate_opts* opts, float* d_stems,
+                                     dmx_progress_fn progress, void* user) {
+  try {
+    if (!h || !lr_dev || !d_stems || n <= 0)
+      throw Error(DMX_ERR_INVALID, "dmx_separate_track_device: bad argument");
+    dmx_separate_opts o{1, 0.25, 1.0, 0};
+    if (opts) o = *opts;
+    if (o.transition_power != 1.0) throw Error(DMX_ERR_INVALID, "transition_power must be 1");
+    if (o.shifts < 0) throw Error(DMX_ERR_INVALID, "shifts must be >= 0");
+    CK(cudaSetDevice(h->device));
+    const int seg = kSegment;
+    const int64_t stride = (int64_t)((1.0 - o.overlap) * (double)seg);
+    if (stride <= 0) throw Error(DMX_ERR_INVALID, "overlap leaves a zero stride");
+    const int64_t max_shift = o.shifts > 0 ? (int64_t)(0.5 * 44100.0) : 0;
+    const int64_t view_cap = n + max_shift;
+    // track-sized scratch, kept on the handle between calls
+    const size_t need = (size_t)(2 * n + 8 * view_cap + (o.shifts > 1 ? 8 * n : 0)) * sizeof(float) +
+                        4 * sizeof(double) + 256;
+    if (need > h->track_cap) {
+      cudaFree(h->track_ws);
+      h->track_ws = nullptr;
+      h->track_cap = 0;
+      CK(cudaMalloc(&h->track_ws, need));
+      h->track_cap = need;
+    }
+    double* d_stats = reinterpret_cast<double*>(h->track_ws);
+    float2* d_norm = reinterpret_cast<float2*>(h->track_ws + 4 * sizeof(double));
+    float* d_mix = reinterpret_cast<float*>(h->track_ws + 256);
+    float* d_acc = d_mix + 2 * n;
+    float* d_pass = o.shifts > 1 ? d_acc + 8 * view_cap : nullptr;
+    h->launches = 0;
+    if (d_pass) CK(cudaMemsetAsync(d_pass, 0, 8 * n * sizeof(float), h->stream));
+    h->mark("track.normalize");
+    launch_track_normalize(lr_dev, lr_dev + n, n, d_stats, d_mix, d_norm, h->stream);
+    h->launches += 2;
+    // ShiftRng (pipeline.rs:136-151), seed 0x5eed1234
+    uint64_t rng = 0x5eed1234ULL * 6364136223846793005ULL + 1ULL;
+    const int passes = std::max(1, o.shifts);
+    const float scale = o.shifts > 0 ? 1.0f / (float)o.shifts : 1.0f;
+    size_t done = 0, total = 0;
+    std::vector<int64_t> offsets;
+    for (int pass = 0; pass < passes; ++pass) {
+      int64_t offset = 0;
+      if (o.shifts > 0) {
+        rng = rng * 6364136223846793005ULL + 1442695040888963407ULL;
+        offset = (int64_t)((rng >> 33) % (uint64_t)(max_shift + 1));
+      }
+      offsets.push_back(offset);
+      const int64_t vlen = o.shifts > 0 ? n + max_shift - offset : n;
+      total += (size_t)dmx_num_chunks(vlen, seg, o.overlap);
+    }
+    const int batch = o.batch > 0 ? std::min(o.batch, h->cfg.max_batch) : h->cfg.max_batch;
+    for (int pass = 0; pass < passes; ++pass) {
+      const int64_t offset = offsets[pass];
+      const int64_t vlen = o.shifts > 0 ? n + max_shift - offset : n;
+      const int64_t chunks = dmx_num_chunks(vlen, seg, o.overlap);
+      CK(cudaMemsetAsync(d_acc, 0, 8 * vlen * sizeof(float), h->stream));
+      for (int64_t c0 = 0; c0 < chunks; c0 += batch) {
+        const int64_t c1 = std::min<int64_t>(chunks, c0 + batch);
+        const dmx_status st = dmx_track_shard(h, d_mix, n, offset, max_shift, seg, o.overlap, 1.0, c0,
+                                              c1, batch, d_acc, 0, vlen);
+        if (st != DMX_OK) return st;
+        done += (size_t)(c1 - c0);
+        if (progress) {
+          CK(cudaStreamSynchronize(h->stream));
+          progress(done, total, user);
+        }
+      }
+      const int mode = o.shifts == 0 ? 0 : (o.shifts == 1 ? 1 : 2);
+      h->mark("track.finish");
+      ++h->launches;
+      launch_ola_finish(d_acc, n, offset, max_shift, seg, stride, h->W(h->m.ola_w.off), d_norm, scale,
+                        mode, d_pass, d_stems, h->stream);
+    }
+    if (o.shifts > 1) ++h->launches;
+    if (o.shifts > 1)
+      launch_ola_finish(d_acc, n, 0, max_shift, seg, stride, h->W(h->m.ola_w.off), d_norm, scale, 3,
+                        d_pass, d_stems, h->stream);
+    h->mark("end");
+    CK(cudaGetLastError());
+    return DMX_OK;
+  } catch (const Error& e) {
+    return fail(e);
+  } catch (const std::exception& e) {
+    return fail_std(e);
+  }
+}
+
+dmx_status dmx_separate_track(dmx_handle* h, const float* left, const float* right, int64_t n,
+                              const dmx_separate_opts* opts, float* stems_out,
+                              dmx_progress_fn progress, void* user) {
+  try {
+    if (!h || !left || !right || !stems_out || n <= 0)
+      throw Error(DMX_ERR_INVALID, "dmx_separate_track: bad argument");
+    CK(cudaSetDevice(h->device));
+    float *d_lr = nullptr, *d_stems = nullptr;
+    struct Free {
+      std::vector<void*> p;
+      ~Free() { for (void* q : p) cudaFree(q); }
+    } fr;
+    CK(cudaMalloc(&d_lr, 2 * n * sizeof(float)));
+    fr.p.push_back(d_lr);
+    CK(cudaMalloc(&d_stems, 8 * n * sizeof(float)));
+    fr.p.push_back(d_stems);
+    CK(cudaMemcpyAsync(d_lr, left, n * sizeof(float), cudaMemcpyHostToDevice, h->stream));
+    CK(cudaMemcpyAsync(d_lr + n, right, n * sizeof(float), cudaMemcpyHostToDevice, h->stream));
+    const dmx_status st = dmx_separate_track_device(h, d_lr, n, opts, d_stems, progress, user);
+    if (st != DMX_OK) return st;
+    CK(cudaMemcpyAsync(stems_out, d_stems, 8 * n * sizeof(float), cudaMemcpyDeviceToHost, h->stream));
+    CK(cudaStreamSynchronize(h->stream));
+    finish_stage_times(h);
+    return DMX_OK;
+  } catch (const Error& e) {
+    return fail(e);
+  } catch (const std::exception& e) {
+    return fail_std(e);
+  }
+}
+
+int dmx_stage_times(dmx_handle* h, const char** names, float* ms, int* counts, int cap) {
+  if (!h) return 0;
+  const int n = std::min<int>(cap, (int)h->stage_names.size());
+  for (int i = 0; i < n; ++i) {
+    names[i] = h->stage_names[i].c_str();
+    ms[i] = h->stage_ms[i];
+    if (counts) counts[i] = h->stage_counts[i];
+  }
+  return n;
+}
+
+dmx_status dmx_set_stage_timing(dmx_handle* h, int on) {
+  if (!h) return DMX_ERR_INVALID;
+  h->stage_timing = on != 0;
+  return DMX_OK;
+}
+
+int64_t dmx_kernel_launches(dmx_handle* h) { return h ? h->launches : 0; }
+
+void* dmx_stream(dmx_handle* h) { return h ? static_cast<void*>(h->stream) : nullptr; }
+
+dmx_status dmx_synchronize(dmx_handle* h) {
+  try {
+    if (!h) throw Error(DMX_ERR_INVALID, "dmx_synchronize: null handle");
+    CK(cudaSetDevice(h->device));
+    // bounded wait on the handle's stream
+    cudaEvent_t e;
+    CK(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
+    CK(cudaEventRecord(e, h->stream));
+    const auto deadline = std::chrono::steady_clock::now() + std::chrono::seconds(600);
+    while (true) {
+      const cudaError_t q = cudaEventQuery(e);
+      if (q == cudaSuccess) break;
+      if (q != cudaErrorNotReady) {
+        cudaEventDestroy(e);
+        CK(q);
+      }
+      if (std::chrono::steady_clock::now() > deadline) {
+        cudaEventDestroy(e);
+        throw Error(DMX_ERR_TIMEOUT, "the handle's stream did not drain within the deadline");
+      }
+      std::this_thread::sleep_for(std::chrono::microseconds(20));
+    }
+    CK(cudaEventDestroy(e));
+    finish_stage_times(h);
+    return DMX_OK;
+  } catch (const Error& e) {
+    return fail(e);
+  }
+}
+
+}  // extern "C"

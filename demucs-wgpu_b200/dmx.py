@@ -1,0 +1,220 @@
+"""ctypes binding of libdmx_cuda.so (include/dmx.h).
+
+The binding is a thin mirror of the C ABI; it never falls back to anything:
+if the library is missing or fails to load, every call raises.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "libdmx_cuda.so")
+SEGMENT = 343980
+
+FP32, TF32, BF16, TF32X3 = 0, 1, 2, 3
+
+# The symbols include/dmx.h declares, in order.
+EXPORTS = (
+    "dmx_default_config", "dmx_create", "dmx_destroy", "dmx_last_error", "dmx_forward_start",
+    "dmx_forward_collect", "dmx_forward_device", "dmx_separate_track",
+    "dmx_separate_track_device", "dmx_num_chunks", "dmx_track_shard", "dmx_set_trace",
+    "dmx_set_stage_timing", "dmx_stage_times", "dmx_kernel_launches", "dmx_stream",
+    "dmx_synchronize",
+)
+
+_f32p = ctypes.POINTER(ctypes.c_float)
+_i64p = ctypes.POINTER(ctypes.c_int64)
+TRACE_FN = ctypes.CFUNCTYPE(None, ctypes.c_char_p, _f32p, _i64p, ctypes.c_int, ctypes.c_void_p)
+PROGRESS_FN = ctypes.CFUNCTYPE(None, ctypes.c_size_t, ctypes.c_size_t, ctypes.c_void_p)
+
+
+class Config(ctypes.Structure):
+    _fields_ = [("sources", ctypes.c_int), ("audio_channels", ctypes.c_int),
+                ("samplerate", ctypes.c_int), ("segment_samples", ctypes.c_int),
+                ("precision", ctypes.c_int), ("max_batch", ctypes.c_int)]
+
+
+class SeparateOpts(ctypes.Structure):
+    _fields_ = [("shifts", ctypes.c_int), ("overlap", ctypes.c_double),
+                ("transition_power", ctypes.c_double), ("batch", ctypes.c_int)]
+
+
+class DmxError(RuntimeError):
+    def __init__(self, code, message):
+        super().__init__(f"dmx error {code}: {message}")
+        self.code = code
+
+
+_lib = None
+
+
+def lib():
+    """Load libdmx_cuda.so (raises if it is absent: there is no fallback)."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise ImportError(f"{LIB_PATH} is not built; run demucs-wgpu_b200/build.py")
+        L = ctypes.CDLL(LIB_PATH)
+        L.dmx_default_config.argtypes = [ctypes.POINTER(Config)]
+        L.dmx_create.argtypes = [ctypes.POINTER(Config), ctypes.c_void_p, ctypes.c_size_t,
+                                 ctypes.c_int, ctypes.POINTER(ctypes.c_void_p)]
+        L.dmx_destroy.argtypes = [ctypes.c_void_p]
+        L.dmx_last_error.restype = ctypes.c_char_p
+        L.dmx_forward_start.argtypes = [ctypes.c_void_p, _f32p, ctypes.c_int64,
+                                        ctypes.POINTER(ctypes.c_void_p)]
+        L.dmx_forward_collect.argtypes = [ctypes.c_void_p, _f32p]
+        L.dmx_forward_device.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64,
+                                         ctypes.c_void_p, ctypes.c_void_p]
+        L.dmx_separate_track.argtypes = [ctypes.c_void_p, _f32p, _f32p, ctypes.c_int64,
+                                         ctypes.POINTER(SeparateOpts), _f32p, PROGRESS_FN,
+                                         ctypes.c_void_p]
+        L.dmx_separate_track_device.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64,
+                                                ctypes.POINTER(SeparateOpts), ctypes.c_void_p,
+                                                PROGRESS_FN, ctypes.c_void_p]
+        L.dmx_set_stage_timing.argtypes = [ctypes.c_void_p, ctypes.c_int]
+        L.dmx_stream.restype = ctypes.c_void_p
+        L.dmx_stream.argtypes = [ctypes.c_void_p]
+        L.dmx_synchronize.argtypes = [ctypes.c_void_p]
+        L.dmx_num_chunks.restype = ctypes.c_int64
+        L.dmx_num_chunks.argtypes = [ctypes.c_int64, ctypes.c_int, ctypes.c_double]
+        L.dmx_track_shard.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64,
+                                      ctypes.c_int64, ctypes.c_int64, ctypes.c_int,
+                                      ctypes.c_double, ctypes.c_double, ctypes.c_int64,
+                                      ctypes.c_int64, ctypes.c_int, ctypes.c_void_p,
+                                      ctypes.c_int64, ctypes.c_int64]
+        L.dmx_set_trace.argtypes = [ctypes.c_void_p, TRACE_FN, ctypes.c_void_p]
+        L.dmx_stage_times.argtypes = [ctypes.c_void_p, ctypes.POINTER(ctypes.c_char_p), _f32p,
+                                      ctypes.POINTER(ctypes.c_int), ctypes.c_int]
+        L.dmx_kernel_launches.restype = ctypes.c_int64
+        L.dmx_kernel_launches.argtypes = [ctypes.c_void_p]
+        _lib = L
+    return _lib
+
+
+def _check(rc):
+    if rc != 0:
+        raise DmxError(rc, lib().dmx_last_error().decode())
+
+
+def _ptr(a):
+    assert a.dtype == np.float32 and a.flags.c_contiguous
+    return a.ctypes.data_as(_f32p)
+
+
+def default_config():
+    c = Config()
+    lib().dmx_default_config(ctypes.byref(c))
+    return c
+
+
+class Handle:
+    """One loaded network on one GPU (dmx_create / dmx_destroy)."""
+
+    def __init__(self, blob: bytes, device: int = 0, precision: int = FP32, max_batch: int = 8):
+        L = lib()
+        cfg = default_config()
+        cfg.precision = precision
+        cfg.max_batch = max_batch
+        self._blob = blob
+        buf = ctypes.create_string_buffer(blob, len(blob))
+        self._buf = buf
+        h = ctypes.c_void_p()
+        _check(L.dmx_create(ctypes.byref(cfg), ctypes.cast(buf, ctypes.c_void_p), len(blob),
+                            device, ctypes.byref(h)))
+        self._h = h
+        self.device = device
+        self.max_batch = max_batch
+        self._trace_cb = None
+
+    def close(self):
+        if getattr(self, "_h", None):
+            lib().dmx_destroy(self._h)
+            self._h = None
+
+    __del__ = close
+
+    # SegmentForward.start / collect
+    def forward_start(self, mix):
+        mix = np.ascontiguousarray(mix, dtype=np.float32)
+        assert mix.ndim == 3 and mix.shape[1:] == (2, SEGMENT), mix.shape
+        pending = ctypes.c_void_p()
+        _check(lib().dmx_forward_start(self._h, _ptr(mix), mix.shape[0], ctypes.byref(pending)))
+        return pending, mix.shape[0]
+
+    def forward_collect(self, pending):
+        p, n = pending
+        out = np.empty((n, 4, 2, SEGMENT), dtype=np.float32)
+        _check(lib().dmx_forward_collect(p, _ptr(out)))
+        return out
+
+    def forward(self, mix):
+        return self.forward_collect(self.forward_start(mix))
+
+    def forward_device(self, mix_ptr: int, n: int, out_ptr: int, stream: int = 0):
+        _check(lib().dmx_forward_device(self._h, ctypes.c_void_p(mix_ptr), n,
+                                        ctypes.c_void_p(out_ptr), ctypes.c_void_p(stream)))
+
+    def separate_track(self, left, right, shifts=1, overlap=0.25, transition_power=1.0,
+                       batch=0, progress=None):
+        left = np.ascontiguousarray(left, dtype=np.float32)
+        right = np.ascontiguousarray(right, dtype=np.float32)
+        n = left.shape[0]
+        stems = np.empty((4, 2, n), dtype=np.float32)
+        opts = SeparateOpts(shifts, overlap, transition_power, batch)
+        cb = PROGRESS_FN(0) if progress is None else PROGRESS_FN(lambda d, t, _u: progress(d, t))
+        _check(lib().dmx_separate_track(self._h, _ptr(left), _ptr(right), n, ctypes.byref(opts),
+                                        _ptr(stems), cb, None))
+        return stems
+
+    def track_shard(self, mix_norm_ptr, length, shift_offset, max_shift, overlap, chunk_lo,
+                    chunk_hi, batch, acc_ptr, view_lo, view_hi):
+        _check(lib().dmx_track_shard(self._h, ctypes.c_void_p(mix_norm_ptr), length, shift_offset,
+                                     max_shift, SEGMENT, overlap, 1.0, chunk_lo, chunk_hi, batch,
+                                     ctypes.c_void_p(acc_ptr), view_lo, view_hi))
+
+    def set_trace(self, store: dict | None):
+        if store is None:
+            self._trace_cb = TRACE_FN(0)
+        else:
+            def _record(name, data, shape, ndim, _user):
+                dims = tuple(shape[i] for i in range(ndim))
+                store[name.decode()] = np.ctypeslib.as_array(data, shape=dims).copy()
+            self._trace_cb = TRACE_FN(_record)
+        _check(lib().dmx_set_trace(self._h, self._trace_cb, None))
+
+    def separate_track_device(self, lr_ptr: int, n: int, stems_ptr: int, shifts=1,
+                              overlap=0.25, batch=0):
+        """Enqueue a whole-track separation on device buffers (returns at once)."""
+        opts = SeparateOpts(shifts, overlap, 1.0, batch)
+        _check(lib().dmx_separate_track_device(self._h, ctypes.c_void_p(lr_ptr), n,
+                                               ctypes.byref(opts), ctypes.c_void_p(stems_ptr),
+                                               PROGRESS_FN(0), None))
+
+    def set_stage_timing(self, on: bool):
+        _check(lib().dmx_set_stage_timing(self._h, int(bool(on))))
+
+    def stage_times(self):
+        """{kernel tag: (total ms, launches)} of the last forward with timing on."""
+        names = (ctypes.c_char_p * 64)()
+        ms = (ctypes.c_float * 64)()
+        counts = (ctypes.c_int * 64)()
+        n = lib().dmx_stage_times(self._h, names, ms, counts, 64)
+        return {names[i].decode(): (ms[i], counts[i]) for i in range(n)}
+
+    @property
+    def stream(self) -> int:
+        return lib().dmx_stream(self._h) or 0
+
+    def synchronize(self):
+        _check(lib().dmx_synchronize(self._h))
+
+    def kernel_launches(self) -> int:
+        return lib().dmx_kernel_launches(self._h)
+
+
+def num_chunks(view_length: int, segment: int = SEGMENT, overlap: float = 0.25) -> int:
+    return lib().dmx_num_chunks(view_length, segment, overlap)

@@ -1,0 +1,147 @@
+/*
+ * dmx.h — C ABI of the B200 (sm_100a) HTDemucs v4 inference backend.
+ *
+ * This is the drop-in boundary a `Backend::Cuda` in the reference's library
+ * binds to. Each entry point names the reference interface it replaces
+ * (paths relative to the reference project, crates/demucs-core/src/...).
+ *
+ * Conventions: every function returns a dmx_status (0 = OK). On failure
+ * dmx_last_error() returns a thread-local message. Host pointers are plain
+ * float arrays, row-major; no CUDA or framework types cross the boundary.
+ * A handle is used by one host thread at a time (the reference runner is
+ * !Sync: gpu/htdemucs.rs:2344-2351).
+ */
+#ifndef DMX_H
+#define DMX_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef int dmx_status;
+enum {
+  DMX_OK = 0,
+  DMX_ERR_INVALID = 1,   /* bad argument, shape or configuration */
+  DMX_ERR_WEIGHTS = 2,   /* weight blob missing a tensor or with a wrong shape */
+  DMX_ERR_CUDA = 3,      /* a CUDA call failed */
+  DMX_ERR_TIMEOUT = 4,   /* a bounded wait gave up */
+  DMX_ERR_NOMEM = 5      /* device memory exhausted */
+};
+
+/* Arithmetic of the contractions (convolutions, linears, attention).
+ * FP32: SIMT fp32 FMA (the max-abs 1e-4 parity build).
+ * TF32 / BF16: tensor-core kinds (the SNR >= 60 dB builds). */
+typedef enum { DMX_FP32 = 0, DMX_TF32 = 1, DMX_BF16 = 2, DMX_TF32X3 = 3 } dmx_precision;
+
+typedef struct {
+  int sources;         /* 4 (config.rs:46-49) */
+  int audio_channels;  /* 2 */
+  int samplerate;      /* 44100 */
+  int segment_samples; /* 343980 = int(39/5 * 44100) (config.rs:222-224) */
+  int precision;       /* dmx_precision */
+  int max_batch;       /* segments per forward the workspace is sized for */
+} dmx_config;
+
+typedef struct dmx_handle dmx_handle;
+typedef struct dmx_pending dmx_pending;
+
+/* Fills the reference defaults (HtdemucsConfig::default, config.rs:43-71). */
+void dmx_default_config(dmx_config* cfg);
+
+/* Demucs::load / GpuHtdemucsRunner::with_selector + GpuWeights::load
+ * (api.rs:394-420, gpu/htdemucs.rs:536-660, 2377-2388): parse a safetensors
+ * blob holding the PyTorch-named F32 tensors (weights.rs:211-578), repack and
+ * upload them once to `device`. */
+dmx_status dmx_create(const dmx_config* cfg, const void* safetensors_blob, size_t blob_len,
+                      int device, dmx_handle** out);
+void dmx_destroy(dmx_handle* h);
+const char* dmx_last_error(void);
+
+/* SegmentForward::start (demucs/pipeline.rs:178-190; DeviceForward::start,
+ * gpu/htdemucs.rs:2824-2847): queue one forward of `mix`, a host
+ * (n_segments, 2, segment_samples) array of already-normalised padded chunks,
+ * and return with the work in flight. The caller keeps `mix` alive until
+ * collect. */
+dmx_status dmx_forward_start(dmx_handle* h, const float* mix, int64_t n_segments,
+                             dmx_pending** out);
+/* SegmentForward::collect: wait (bounded) and write (n_segments, 4, 2,
+ * segment_samples) stems in normalised units to host `out`. */
+dmx_status dmx_forward_collect(dmx_pending* p, float* out);
+
+/* The same forward on device buffers of the handle's GPU (no host copies):
+ * mix_dev (n, 2, segment_samples) -> out_dev (n, 4, 2, segment_samples),
+ * enqueued on `stream` (a cudaStream_t, NULL = the handle's stream). */
+dmx_status dmx_forward_device(dmx_handle* h, const float* mix_dev, int64_t n_segments,
+                              float* out_dev, void* stream);
+
+typedef struct {
+  int shifts;              /* SeparateOptions::shifts (pipeline.rs:17-38) */
+  double overlap;          /* 0.25 */
+  double transition_power; /* 1.0 */
+  int batch;               /* chunks per forward (DEMUCS_BATCH); 0 = all */
+} dmx_separate_opts;
+
+typedef void (*dmx_progress_fn)(size_t done, size_t total, void* user);
+
+/* Demucs::separate_with_options for one stereo track (api.rs:438-545 with the
+ * driver of pipeline.rs:380-515 and streaming.rs:52-400): global
+ * normalisation, shift passes (ShiftRng seed 0x5eed1234), chunking, batched
+ * forwards, triangular overlap-add and denormalisation, all on the device.
+ * `stems_out` is (4, 2, n) host memory. */
+dmx_status dmx_separate_track(dmx_handle* h, const float* left, const float* right, int64_t n,
+                              const dmx_separate_opts* opts, float* stems_out,
+                              dmx_progress_fn progress, void* user);
+
+/* dmx_separate_track on device buffers of the handle's GPU: lr_dev holds the
+ * raw (2, n) stereo track, stems_dev receives (4, 2, n). Enqueued on the
+ * handle's stream; returns without waiting unless `progress` is set. */
+dmx_status dmx_separate_track_device(dmx_handle* h, const float* lr_dev, int64_t n,
+                                     const dmx_separate_opts* opts, float* stems_dev,
+                                     dmx_progress_fn progress, void* user);
+
+/* Chunk plan of a split pass (streaming.rs:88-94, 296-330): number of chunks
+ * of a view of `view_length` samples. */
+int64_t dmx_num_chunks(int64_t view_length, int segment, double overlap);
+
+/* One shard of a track for multi-GPU chunk sharding: forward chunks
+ * [chunk_lo, chunk_hi) of the shift view of the (device, normalised) mix and
+ * overlap-add them, unnormalised by the window sum, into `acc_dev` over view
+ * samples [view_lo, view_hi) — (8, view_hi - view_lo) floats — adding to what
+ * is there. The window sums are analytic (dmx_ola_finish divides by them). */
+dmx_status dmx_track_shard(dmx_handle* h, const float* mix_norm_dev, int64_t length,
+                           int64_t shift_offset, int64_t max_shift, int segment, double overlap,
+                           double transition_power, int64_t chunk_lo, int64_t chunk_hi,
+                           int batch, float* acc_dev, int64_t view_lo, int64_t view_hi);
+
+/* Optional activation tracing (mirrors TraceSink, demucs/host.rs:117-125):
+ * named intermediates copied to host in the reference's own layouts. */
+typedef void (*dmx_trace_fn)(const char* name, const float* data, const int64_t* shape, int ndim,
+                             void* user);
+dmx_status dmx_set_trace(dmx_handle* h, dmx_trace_fn fn, void* user);
+
+/* Per-launch device timing (cudaEvents between consecutive launches on the
+ * handle's stream), off by default; it serialises nothing but adds one event
+ * per launch. dmx_stage_times then reports, for the last forward, each kernel
+ * tag with its summed milliseconds and launch count; returns the count of
+ * tags written (at most `cap`). */
+dmx_status dmx_set_stage_timing(dmx_handle* h, int on);
+int dmx_stage_times(dmx_handle* h, const char** names, float* ms, int* counts, int cap);
+
+/* Number of kernels the last forward launched. */
+int64_t dmx_kernel_launches(dmx_handle* h);
+
+/* The handle's CUDA stream (a cudaStream_t), for callers that order their
+ * own work or events around the device entry points. */
+void* dmx_stream(dmx_handle* h);
+
+/* Waits (bounded) until the handle's stream has drained. */
+dmx_status dmx_synchronize(dmx_handle* h);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* DMX_H */

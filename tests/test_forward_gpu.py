@@ -1,0 +1,69 @@
+"""CUDA forward vs the CPU oracle on seeded weights and audio (GPU).
+
+The gate for the FP32 build is the north-star tolerance: max-abs <= 1e-4 per
+stem against the reference CPU path (restated by the oracle), at the
+benchmark's configuration 1 (one 343980-sample stereo segment, N(0, 0.1^2)
+audio, random-init weights with LayerScale 1e-4) and with LayerScale 1 so the
+residual branches carry weight.
+"""
+
+import numpy as np
+import pytest
+
+import oracle
+import synth
+
+pytestmark = pytest.mark.gpu
+
+
+def _handle(weights, max_batch=4):
+    import dmx
+    return dmx.Handle(synth.write_safetensors(weights), device=0, max_batch=max_batch)
+
+
+def _per_stem_maxabs(a, b):
+    return np.abs(a.astype(np.float64) - b).reshape(a.shape[0], 4, -1).max(axis=-1)
+
+
+@pytest.mark.parametrize("layer_scale", [1e-4, 1.0])
+def test_forward_matches_oracle_fp32(layer_scale):
+    w = synth.random_weights(3, layer_scale=layer_scale, norm_jitter=0.1)
+    mix = synth.gaussian_audio(7, 1)
+    ref = oracle.OracleModel(w).forward(mix)
+    got = _handle(w).forward(mix)
+    assert got.shape == ref.shape
+    worst = _per_stem_maxabs(got, ref)
+    assert np.isfinite(got).all()
+    assert worst.max() <= 1e-4, worst
+
+
+def test_stage_traces_match_oracle():
+    w = synth.random_weights(4, layer_scale=1.0, norm_jitter=0.1)
+    mix = synth.gaussian_audio(8, 1)
+    tr_o, tr_g = {}, {}
+    oracle.OracleModel(w).forward(mix, trace=tr_o)
+    h = _handle(w)
+    h.set_trace(tr_g)
+    h.forward(mix)
+    assert tr_g, "no traces recorded"
+    for name, got in tr_g.items():
+        ref = tr_o[name]
+        assert got.shape == ref.shape, (name, got.shape, ref.shape)
+        rms = np.sqrt(np.mean(ref.astype(np.float64) ** 2))
+        rel = np.mean(np.abs(got.astype(np.float64) - ref)) / rms
+        assert rel < 1e-4, f"{name}: mean-abs/rms {rel:.3e}"
+
+
+def test_batch_independence():
+    # demucs_alignment.rs:232-261: element 0 of a batch-2 run matches the single run.
+    w = synth.random_weights(5)
+    single = synth.lcg_audio(12345, (1, 2, synth.SEGMENT_SAMPLES), 0.1)
+    pair = np.concatenate([single, synth.gaussian_audio(9, 1, std=0.05)])
+    h = _handle(w)
+    one = h.forward(single)
+    two = h.forward(pair)
+    # f64 moments are reduced with atomics, so compare at the reference's
+    # own > 100 dB bar (mean-abs SNR, fixtures.rs:133-149) rather than bitwise.
+    err = np.mean(np.abs(one[0].astype(np.float64) - two[0]))
+    rms = np.sqrt(np.mean(one[0].astype(np.float64) ** 2))
+    assert err == 0 or -20 * np.log10(err / rms) > 100
