@@ -1,0 +1,61 @@
+// Tensor-core (tcgen05 / TMEM / TMA) implicit-GEMM convolution for sm_100a.
+//
+// One CTA computes a 128 x BN output tile with cta_group::1 UMMA (kind::tf32,
+// fp32 accumulate in TMEM). Warp 0 issues TMA tile loads into a STAGES-deep
+// shared-memory ring, warp 1 issues the MMAs (one elected thread), warps 2-5
+// drain the accumulator with tcgen05.ld and apply the same fused epilogues as
+// the SIMT path (conv_gemm.cuh). The A operand is an activation tile read
+// straight from the channels-last tensor by TMA — the convolution taps are
+// coordinate offsets and the padding is TMA's out-of-bounds zero fill, so no
+// patch matrix exists anywhere. No load uses cluster multicast.
+#pragma once
+
+#include <cuda.h>
+
+#include "conv_gemm.cuh"
+
+namespace dmx {
+
+enum TcAMode : int {
+  TC_ROWS = 0,  // A is a [rows][K] matrix; tile = 128 consecutive rows
+  TC_2D = 1     // A is a (B, H, W, C) tensor; tile = 8 x 16 positions; taps (dy, dx)
+};
+
+struct TcParams {
+  int mode;
+  int B, Hq, Wq;     // output-position grid (TC_2D) ; rows = B*Hq*Wq (TC_ROWS: B=1,Hq=1)
+  int Cin;           // channels per tap (K tile never straddles taps)
+  int ntaps;
+  int dy[kMaxTaps], dx[kMaxTaps];
+  int K, Kpad, N, Npad;
+  const float* bias;
+  // output addressing and epilogue, as in ConvParams
+  float* out;
+  int64_t o_bs, o_ys, o_xs, o_off;
+  double* epi_stats;
+  int epi_rowlen;
+  const double* epi_nstats;
+  double epi_count;
+  const float* epi_gw;
+  const float* epi_gb;
+  int epi_half;
+  const float* epi_gamma;
+  const float* epi_res;
+  const float* epi_emb;
+  int* err;  // set non-zero when a bounded wait gives up
+};
+
+// Host: build the two tensor maps and launch. `a` describes the A operand
+// tensor (channels-last, element strides), `w` the K-major packed weights
+// [Npad][Kpad]. Returns false when the shape is not supported by the
+// tensor-core path (the caller then uses the SIMT kernel).
+struct TcOperandA {
+  const float* ptr;
+  int B, H, W, C;           // TC_2D: (B, H, W, C); TC_ROWS: rows = W (B = H = 1), K = C
+  int64_t sb, sh, sw;       // element strides of b, h, w (channels contiguous)
+};
+bool tc_gemm_supported(const TcOperandA& a, const TcParams& p);
+void launch_tc_gemm(const TcOperandA& a, const float* wk, const TcParams& p, int epi,
+                    cudaStream_t s);
+
+}  // namespace dmx
