@@ -161,6 +161,12 @@ __global__ void __launch_bounds__(256) conv_gemm_kernel(const ConvParams p) {
 #pragma unroll
         for (int j = 0; j < TN; ++j) v[j] = gelu(v[j]);
       }
+      if (p.epi_add) {
+        const float* ad = p.epi_add + orow + nb;
+#pragma unroll
+        for (int j = 0; j < TN; ++j)
+          if (nb + j < p.N) v[j] += ad[j];
+      }
       float* o = p.out + orow + nb;
       if (nb + TN <= p.N && ((orow & 3) == 0)) {
         *reinterpret_cast<float4*>(o) = make_float4(v[0], v[1], v[2], v[3]);

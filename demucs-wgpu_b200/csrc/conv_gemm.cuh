@@ -71,6 +71,7 @@ struct ConvParams {
   const float* epi_gamma;
   const float* epi_res;
   const float* epi_emb;
+  const float* epi_add;  // EPI_STORE / EPI_GELU: + add[element] after the activation
 };
 
 void launch_conv_gemm(const ConvParams& p, int pro, int epi, cudaStream_t stream);

@@ -18,6 +18,7 @@
 
 #include "conv_gemm.cuh"
 #include "dmx.h"
+#include "tc_gemm.cuh"
 #include "kernels.h"
 
 using namespace dmx;
@@ -176,6 +177,9 @@ struct Tap {
 
 struct Packed {
   size_t w_off = 0, b_off = 0;  // float offsets into the weight arena
+  size_t tc_off = 0;            // K-major copy [Npad][K] for the tensor-core path
+  bool has_tc = false;
+  int cin = 0;
   int K = 0, Kpad = 0, N = 0, Npad = 0;
   std::vector<Tap> taps;
   const float* w = nullptr;
@@ -273,14 +277,20 @@ struct Loader {
     p.N = cols;
     p.Npad = (cols + kBN - 1) / kBN * kBN;
     p.taps = std::move(taps);
+    p.cin = cin;
     p.w_off = wb.alloc((size_t)p.Kpad * p.Npad);
     p.b_off = wb.alloc(p.Npad);
+    p.has_tc = cin % 16 == 0;
+    if (p.has_tc) p.tc_off = wb.alloc((size_t)p.Npad * p.K);
     const int half = cols / 2;
     for (int n = 0; n < cols; ++n) {
       const int co = glu ? ((n % 2 == 0) ? n / 2 : n / 2 + half) : n;
       for (int tap = 0; tap < ntaps; ++tap)
-        for (int ci = 0; ci < cin; ++ci)
-          wb.host[p.w_off + (size_t)(tap * cin + ci) * p.Npad + n] = value(tap, ci, co);
+        for (int ci = 0; ci < cin; ++ci) {
+          const float v = value(tap, ci, co);
+          wb.host[p.w_off + (size_t)(tap * cin + ci) * p.Npad + n] = v;
+          if (p.has_tc) wb.host[p.tc_off + (size_t)n * p.K + tap * cin + ci] = v;
+        }
       wb.host[p.b_off + n] = bias[co];
     }
     return p;
@@ -402,6 +412,8 @@ struct dmx_handle {
   dmx_pending pending{};
   char* track_ws = nullptr;
   size_t track_cap = 0;
+  int* err = nullptr;  // device flag raised by bounded waits in the tensor-core kernels
+  int64_t tc_launches = 0;
 
   float* W(size_t off) const { return wdev + off; }
 
@@ -435,14 +447,90 @@ struct dmx_handle {
     CK(cudaMemsetAsync(p, 0, bytes, stream));
   }
 
-  void gemm(const ConvParams& p, int pro, int epi, const char* tag = "gemm") {
+  void gemm(const ConvParams& p, int pro, int epi, const char* tag = "gemm",
+            const Packed* pk = nullptr) {
     ++launches;
     if (!live()) return;
-    mark(tag);
     if ((epi == EPI_STATS || epi == EPI_STORE_STATS || epi == EPI_RESIDUAL) && p.epi_stats &&
         p.epi_rowlen < 128)
       throw Error(DMX_ERR_INVALID, "row statistics need rows of at least 128 positions");
+    mark(tag);
+    if (pk && cfg.precision == DMX_TF32 && try_tc(p, pro, epi, *pk)) return;
     launch_conv_gemm(p, pro, epi, stream);
+  }
+
+  // The tensor-core path takes a launch when its A operand is a plain
+  // channels-last tile read (no prologue transform) with stride-1 taps.
+  bool try_tc(const ConvParams& p, int pro, int epi, const Packed& pk) {
+    if (pro != PRO_NONE || !pk.has_tc || p.i_cs != 1 || p.sy != 1 || p.sx != 1) return false;
+    TcParams t;
+    std::memset(&t, 0, sizeof(t));
+    TcOperandA a;
+    a.ptr = p.x;
+    a.C = p.Cin;
+    bool taps_zero = true;
+    for (int i = 0; i < p.ntaps; ++i) taps_zero = taps_zero && p.dy[i] == 0 && p.dx[i] == 0;
+    const bool rows = taps_zero && p.Hq == p.Hin && p.Wq == p.Win && p.i_xs == p.Cin &&
+                      p.i_ys == (int64_t)p.Win * p.Cin && p.i_bs == (int64_t)p.Hin * p.Win * p.Cin;
+    if (rows) {
+      t.mode = TC_ROWS;
+      a.B = 1;
+      a.H = 1;
+      a.W = p.B * p.Hin * p.Win;
+      a.sw = p.Cin;
+      a.sh = a.sb = 0;
+    } else if (p.Hin == 1 && p.Hq == 1) {
+      t.mode = TC_1D;
+      a.B = p.B;
+      a.H = 1;
+      a.W = p.Win;
+      a.sw = p.i_xs;
+      a.sh = 0;
+      a.sb = p.i_bs;
+    } else {
+      t.mode = TC_2D;
+      a.B = p.B;
+      a.H = p.Hin;
+      a.W = p.Win;
+      a.sw = p.i_xs;
+      a.sh = p.i_ys;
+      a.sb = p.i_bs;
+    }
+    t.B = p.B;
+    t.Hq = p.Hq;
+    t.Wq = p.Wq;
+    t.Cin = p.Cin;
+    t.ntaps = p.ntaps;
+    for (int i = 0; i < p.ntaps; ++i) {
+      t.dy[i] = p.dy[i];
+      t.dx[i] = p.dx[i];
+    }
+    t.K = p.K;
+    t.Kpad = pk.K;
+    t.N = p.N;
+    t.Npad = p.Npad;
+    t.bias = p.bias;
+    t.out = p.out;
+    t.o_bs = p.o_bs;
+    t.o_ys = p.o_ys;
+    t.o_xs = p.o_xs;
+    t.o_off = p.o_off;
+    t.epi_stats = p.epi_stats;
+    t.epi_rowlen = p.epi_rowlen;
+    t.epi_nstats = p.epi_nstats;
+    t.epi_count = p.epi_count;
+    t.epi_gw = p.epi_gw;
+    t.epi_gb = p.epi_gb;
+    t.epi_half = p.epi_half;
+    t.epi_gamma = p.epi_gamma;
+    t.epi_res = p.epi_res;
+    t.epi_emb = p.epi_emb;
+    t.epi_add = p.epi_add;
+    t.err = err;
+    if (!tc_gemm_supported(a, t)) return false;
+    launch_tc_gemm(a, wdev + pk.tc_off, t, epi, stream);
+    ++tc_launches;
+    return true;
   }
 
   void after(const char* what) {
@@ -513,7 +601,7 @@ void run_dconv(dmx_handle* h, const DConvFull& dc, float* x, int rows, int T) {
       set_output(p, y, rows, 1, T, hid);
       p.epi_stats = st1;
       p.epi_rowlen = T;
-      h->gemm(p, PRO_NONE, EPI_STORE_STATS, "dconv.conv1");
+      h->gemm(p, PRO_NONE, EPI_STORE_STATS, "dconv.conv1", &L.conv1);
     }
     ConvParams p = base_params(L.conv2, h->wdev);
     set_input(p, y, rows, 1, T, hid);
@@ -525,7 +613,7 @@ void run_dconv(dmx_handle* h, const DConvFull& dc, float* x, int rows, int T) {
     p.pro_shift = h->W(L.n1b.off);
     p.epi_stats = st2;
     p.epi_rowlen = T;
-    h->gemm(p, PRO_GN_GELU, EPI_STATS, "dconv.stats");
+    h->gemm(p, PRO_GN_GELU, EPI_STATS, "dconv.stats", &L.conv2);
     p.epi_stats = nullptr;
     p.epi_nstats = st2;
     p.epi_count = 2.0 * C * T;
@@ -534,7 +622,7 @@ void run_dconv(dmx_handle* h, const DConvFull& dc, float* x, int rows, int T) {
     p.epi_half = C;
     p.epi_gamma = h->W(L.gamma.off);
     p.epi_res = x;
-    h->gemm(p, PRO_GN_GELU, EPI_DCONV_TAIL, "dconv.tail");
+    h->gemm(p, PRO_GN_GELU, EPI_DCONV_TAIL, "dconv.tail", &L.conv2);
   }
 }
 
@@ -542,13 +630,18 @@ void run_dconv(dmx_handle* h, const DConvFull& dc, float* x, int rows, int T) {
 // layout. kind 0: freq (B, F, T, C) -> (B, C, F, T); kind 1: time (B, T, C)
 // -> (B, C, T); kind 2: as is with the given shape.
 void trace_tensor(dmx_handle* h, const std::string& name, const float* dev, int kind,
-                  std::vector<int64_t> dims) {
+                  std::vector<int64_t> dims, const float* minus = nullptr) {
   if (!h->trace || h->measuring) return;
   size_t n = 1;
   for (int64_t d : dims) n *= (size_t)d;
   std::vector<float> host(n), out(n);
   CK(cudaStreamSynchronize(h->stream));
   CK(cudaMemcpy(host.data(), dev, n * sizeof(float), cudaMemcpyDeviceToHost));
+  if (minus) {  // the stored tensor already carries the next layer's skip connection
+    std::vector<float> sub(n);
+    CK(cudaMemcpy(sub.data(), minus, n * sizeof(float), cudaMemcpyDeviceToHost));
+    for (size_t i = 0; i < n; ++i) host[i] -= sub[i];
+  }
   std::vector<int64_t> shape;
   if (kind == 0) {
     const int64_t B = dims[0], F = dims[1], T = dims[2], C = dims[3];
@@ -588,7 +681,7 @@ void xf_gemm(dmx_handle* h, const char* tag, const Packed& pk, const float* in, 
   p.epi_gamma = gamma;
   p.epi_stats = stats;
   p.epi_rowlen = n;
-  h->gemm(p, PRO_NONE, epi, tag);
+  h->gemm(p, PRO_NONE, epi, tag, &pk);
 }
 
 void xf_tail(dmx_handle* h, const LayerW& L, float* X, int B, int n, const XfBufs& bb,
@@ -706,13 +799,13 @@ void forward(dmx_handle* h, const float* mix, int G, float* out) {
       }
       p.sx = 4;
       set_output(p, y, G, 1, To, Co);
-      h->gemm(p, i == 0 ? PRO_BATCH_AFFINE : PRO_NONE, EPI_GELU, "tenc.conv");
+      h->gemm(p, i == 0 ? PRO_BATCH_AFFINE : PRO_NONE, EPI_GELU, "tenc.conv", &E.conv);
       run_dconv(h, h->tenc_dc[i], y, G, To);
       float* z = h->falloc((size_t)G * To * Co);
       ConvParams r = base_params(E.rewrite, h->wdev);
       set_input(r, y, G, 1, To, Co);
       set_output(r, z, G, 1, To, Co);
-      h->gemm(r, PRO_NONE, EPI_GLU, "tenc.rewrite");
+      h->gemm(r, PRO_NONE, EPI_GLU, "tenc.rewrite", &E.rewrite);
       tskip[i] = z;
       tin = z;
       Ts[i + 1] = To;
@@ -729,14 +822,14 @@ void forward(dmx_handle* h, const float* mix, int G, float* out) {
       p.sy = 4;
       if (i == 0) p.pro_scale = reinterpret_cast<const float*>(norm_f);
       set_output(p, y, G, Fo, kFrames, Co);
-      h->gemm(p, i == 0 ? PRO_BATCH_AFFINE : PRO_NONE, EPI_GELU, "enc.conv");
+      h->gemm(p, i == 0 ? PRO_BATCH_AFFINE : PRO_NONE, EPI_GELU, "enc.conv", &E.conv);
       run_dconv(h, h->enc_dc[i], y, G * Fo, kFrames);
       float* z = h->falloc((size_t)G * Fo * kFrames * Co);
       ConvParams r = base_params(E.rewrite, h->wdev);
       set_input(r, y, G, Fo, kFrames, Co);
       set_output(r, z, G, Fo, kFrames, Co);
       if (i == 0) r.epi_emb = h->W(m.emb.off);
-      h->gemm(r, PRO_NONE, i == 0 ? EPI_GLU_EMB : EPI_GLU, "enc.rewrite");
+      h->gemm(r, PRO_NONE, i == 0 ? EPI_GLU_EMB : EPI_GLU, "enc.rewrite", &E.rewrite);
       skip[i] = z;
       xin = z;
       Fs[i + 1] = Fo;
@@ -769,11 +862,11 @@ void forward(dmx_handle* h, const float* mix, int G, float* out) {
     p.o_bs = (int64_t)ntok * D;
     p.o_ys = D;
     p.o_xs = (int64_t)Fb * D;
-    h->gemm(p, PRO_NONE, EPI_STORE, "xf.upsample");
+    h->gemm(p, PRO_NONE, EPI_STORE, "xf.upsample", &m.up);
     ConvParams q = base_params(m.up_t, h->wdev);
     set_input(q, tskip[3], G, 1, Tt, TCs[4]);
     set_output(q, bb.kv2, G, 1, Tt, D);
-    h->gemm(q, PRO_NONE, EPI_STORE, "xf.upsample");
+    h->gemm(q, PRO_NONE, EPI_STORE, "xf.upsample", &m.up_t);
     h->mark("xf.layernorm");
     if (h->live()) {
       launch_layer_norm(bb.kvn, (int64_t)G * ntok, ntok, h->W(m.norm_in_w.off), h->W(m.norm_in_b.off),
@@ -819,11 +912,13 @@ void forward(dmx_handle* h, const float* mix, int G, float* out) {
     p.i_xs = (int64_t)Fb * D;
     p.i_bs = (int64_t)ntok * D;
     set_output(p, x, G, Fb, Tb, Cs[4]);
-    h->gemm(p, PRO_NONE, EPI_STORE, "xf.downsample");
+    p.epi_add = skip[3];
+    h->gemm(p, PRO_NONE, EPI_STORE, "xf.downsample", &m.down);
     ConvParams q = base_params(m.down_t, h->wdev);
     set_input(q, Tk, G, 1, Tt, D);
     set_output(q, xt, G, 1, Tt, TCs[4]);
-    h->gemm(q, PRO_NONE, EPI_STORE, "xf.downsample");
+    q.epi_add = tskip[3];
+    h->gemm(q, PRO_NONE, EPI_STORE, "xf.downsample", &m.down_t);
   }
 
   // (f) decoders, innermost first (host.rs:408-450)
@@ -836,9 +931,8 @@ void forward(dmx_handle* h, const float* mix, int G, float* out) {
       float* g = h->falloc((size_t)G * F * kFrames * C);
       ConvParams r = base_params(Dw.rewrite, h->wdev);
       set_input(r, x, G, F, kFrames, C);
-      r.x2 = skip[j];
       set_output(r, g, G, F, kFrames, C);
-      h->gemm(r, PRO_ADD, EPI_GLU, "dec.rewrite");
+      h->gemm(r, PRO_NONE, EPI_GLU, "dec.rewrite", &Dw.rewrite);
       run_dconv(h, h->dec_dc[e], g, G * F, kFrames);
       const int Co = Dw.cout, Fo = 4 * F;
       float* o = h->falloc((size_t)G * Fo * kFrames * Co);
@@ -853,21 +947,22 @@ void forward(dmx_handle* h, const float* mix, int G, float* out) {
         p.o_ys = 4LL * kFrames * Co;
         p.o_off = (int64_t)ph * kFrames * Co;
         p.o_bs = (int64_t)Fo * kFrames * Co;
-        h->gemm(p, PRO_NONE, last ? EPI_STORE : EPI_GELU, "dec.convtr");
+        if (!last) p.epi_add = skip[j - 1];
+        h->gemm(p, PRO_NONE, last ? EPI_STORE : EPI_GELU, "dec.convtr", &Dw.convt[ph]);
       }
       x = o;
       F = Fo;
       C = Co;
-      trace_tensor(h, "decoder." + std::to_string(j), x, 0, {G, F, kFrames, C});
+      trace_tensor(h, "decoder." + std::to_string(j), x, 0, {G, F, kFrames, C},
+                   last ? nullptr : skip[j - 1]);
     }
     {  // time decoder (host.rs:763-827)
       const DecW& Dw = m.tdec[e];
       float* g = h->falloc((size_t)G * Tc * Ct);
       ConvParams r = base_params(Dw.rewrite, h->wdev);
       set_input(r, xt, G, 1, Tc, Ct);
-      r.x2 = tskip[j];
       set_output(r, g, G, 1, Tc, Ct);
-      h->gemm(r, PRO_ADD, EPI_GLU, "tdec.rewrite");
+      h->gemm(r, PRO_NONE, EPI_GLU, "tdec.rewrite", &Dw.rewrite);
       run_dconv(h, h->tdec_dc[e], g, G, Tc);
       const int Co = Dw.cout, len = lengths_t[j];
       float* o = h->falloc((size_t)G * len * Co);
@@ -889,12 +984,14 @@ void forward(dmx_handle* h, const float* mix, int G, float* out) {
         p.o_ys = 0;
         p.o_off = (int64_t)ph * Co;
         p.o_bs = (int64_t)len * Co;
-        h->gemm(p, PRO_NONE, last ? EPI_STORE : EPI_GELU, "tdec.convtr");
+        if (!last) p.epi_add = tskip[j - 1];
+        h->gemm(p, PRO_NONE, last ? EPI_STORE : EPI_GELU, "tdec.convtr", &Dw.convt[ph]);
       }
       xt = o;
       Tc = len;
       Ct = Co;
-      trace_tensor(h, "tdecoder." + std::to_string(j), xt, 1, {G, Tc, Ct});
+      trace_tensor(h, "tdecoder." + std::to_string(j), xt, 1, {G, Tc, Ct},
+                   last ? nullptr : tskip[j - 1]);
     }
   }
 
@@ -906,6 +1003,17 @@ void forward(dmx_handle* h, const float* mix, int G, float* out) {
     h->after("istft");
   }
   h->launches += 2;
+}
+
+// Raises DMX_ERR_TIMEOUT when a tensor-core kernel gave up a bounded wait.
+void check_device_flag(dmx_handle* h) {
+  int flag = 0;
+  CK(cudaMemcpy(&flag, h->err, sizeof(int), cudaMemcpyDeviceToHost));
+  if (flag) {
+    CK(cudaMemset(h->err, 0, sizeof(int)));
+    throw Error(DMX_ERR_TIMEOUT, "a tensor-core kernel gave up a bounded wait (code " +
+                                     std::to_string(flag) + ")");
+  }
 }
 
 void finish_stage_times(dmx_handle* h) {
@@ -1179,14 +1287,16 @@ dmx_status dmx_create(const dmx_config* cfg, const void* blob, size_t len, int d
       throw Error(DMX_ERR_INVALID,
                   "only the default htdemucs configuration is supported (4 sources, stereo, "
                   "44100 Hz, 343980-sample segments)");
-    if (cfg->precision != DMX_FP32)
-      throw Error(DMX_ERR_INVALID, "this build implements precision DMX_FP32 only");
+    if (cfg->precision != DMX_FP32 && cfg->precision != DMX_TF32)
+      throw Error(DMX_ERR_INVALID, "precision must be DMX_FP32 or DMX_TF32");
     if (cfg->max_batch < 1 || cfg->max_batch > 256)
       throw Error(DMX_ERR_INVALID, "max_batch must be in [1, 256]");
     h->cfg = *cfg;
     h->device = device;
     CK(cudaSetDevice(device));
     CK(cudaStreamCreateWithFlags(&h->stream, cudaStreamNonBlocking));
+    CK(cudaMalloc(&h->err, sizeof(int)));
+    CK(cudaMemset(h->err, 0, sizeof(int)));
     const auto tensors = parse_safetensors(blob, len);
     load_model(h.get(), tensors);
     const char* st = getenv("DMX_STAGE_TIMING");
@@ -1206,6 +1316,7 @@ void dmx_destroy(dmx_handle* h) {
   if (h->stream) cudaStreamSynchronize(h->stream);
   if (h->pending.done) cudaEventDestroy(h->pending.done);
   cudaFree(h->wdev);
+  cudaFree(h->err);
   cudaFree(h->ws);
   cudaFree(h->io_in);
   cudaFree(h->io_out);
@@ -1308,8 +1419,9 @@ dmx_status dmx_forward_collect(dmx_pending* p, float* out) {
       }
       std::this_thread::sleep_for(std::chrono::microseconds(50));
     }
-    std::memcpy(out, h->pinned_out, (size_t)p->n * 8 * kSegment * sizeof(float));
     h->pending.h = nullptr;
+    check_device_flag(h);
+    std::memcpy(out, h->pinned_out, (size_t)p->n * 8 * kSegment * sizeof(float));
     finish_stage_times(h);
     return DMX_OK;
   } catch (const Error& e) {
@@ -1469,6 +1581,7 @@ dmx_status dmx_separate_track(dmx_handle* h, const float* left, const float* rig
     if (st != DMX_OK) return st;
     CK(cudaMemcpyAsync(stems_out, d_stems, 8 * n * sizeof(float), cudaMemcpyDeviceToHost, h->stream));
     CK(cudaStreamSynchronize(h->stream));
+    check_device_flag(h);
     finish_stage_times(h);
     return DMX_OK;
   } catch (const Error& e) {
@@ -1522,6 +1635,7 @@ dmx_status dmx_synchronize(dmx_handle* h) {
       std::this_thread::sleep_for(std::chrono::microseconds(20));
     }
     CK(cudaEventDestroy(e));
+    check_device_flag(h);
     finish_stage_times(h);
     return DMX_OK;
   } catch (const Error& e) {

@@ -1,0 +1,508 @@
+// tcgen05 implicit-GEMM kernel (see tc_gemm.cuh for the design).
+#include <cudaTypedefs.h>
+
+#include <mutex>
+
+#include "tc_gemm.cuh"
+
+namespace dmx {
+
+namespace {
+
+constexpr int BM = 128;
+constexpr long long kWaitNs = 2000000000LL;  // bounded waits give up after 2 s
+
+DMX_DEVICE uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+DMX_DEVICE uint64_t now_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+DMX_DEVICE void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
+}
+DMX_DEVICE void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
+               "r"(bytes)
+               : "memory");
+}
+DMX_DEVICE bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Bounded wait: returns false (and raises the error flag) after kWaitNs.
+DMX_DEVICE bool mbar_wait(uint64_t* bar, uint32_t parity, int* err, int code) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = now_ns();
+  while (true) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if (now_ns() - t0 > (uint64_t)kWaitNs) {
+      if (err) atomicExch(err, code);
+      return false;
+    }
+  }
+}
+
+DMX_DEVICE void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar, int c0, int c1) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];" ::
+          "r"(smem_u32(dst)),
+      "l"(map), "r"(smem_u32(bar)), "r"(c0), "r"(c1)
+      : "memory");
+}
+DMX_DEVICE void tma_load_3d(void* dst, const CUtensorMap* map, uint64_t* bar, int c0, int c1,
+                            int c2) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5}], [%2];" ::
+          "r"(smem_u32(dst)),
+      "l"(map), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2)
+      : "memory");
+}
+DMX_DEVICE void tma_load_4d(void* dst, const CUtensorMap* map, uint64_t* bar, int c0, int c1,
+                            int c2, int c3) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5, %6}], [%2];" ::
+          "r"(smem_u32(dst)),
+      "l"(map), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
+      : "memory");
+}
+
+// UMMA shared-memory descriptor, K-major, 128B or 64B swizzle
+// (start >> 4 | LBO=1 | SBO = 8 rows * row bytes | version 1 | layout).
+DMX_DEVICE uint64_t umma_desc(uint32_t saddr, int row_bytes) {
+  const uint64_t layout = row_bytes == 128 ? 2ull : 4ull;
+  const uint64_t sbo = (uint64_t)(8 * row_bytes) >> 4;
+  return (uint64_t)((saddr >> 4) & 0x3FFF) | (1ull << 16) | (sbo << 32) | (1ull << 46) |
+         (layout << 61);
+}
+
+DMX_DEVICE void umma_tf32(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                          uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate));
+}
+DMX_DEVICE void umma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                   smem_u32(bar))
+               : "memory");
+}
+DMX_DEVICE void tmem_ld32(uint32_t taddr, float* v) {
+  uint32_t r[32];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, "
+      "%12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, "
+      "%30, %31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]),
+        "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]),
+        "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+template <int BN, int BK, int STAGES>
+struct Smem {
+  static constexpr int A_BYTES = BM * BK * 4;
+  static constexpr int B_BYTES = BN * BK * 4;
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int TOTAL = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
+};
+
+template <int BN, int BK, int STAGES, int EPI>
+__global__ void __launch_bounds__(192, 1)
+    tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                   const TcParams p) {
+  using S = Smem<BN, BK, STAGES>;
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  unsigned char* smem = reinterpret_cast<unsigned char*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * S::STAGE_BYTES);
+  uint64_t* empty = full + STAGES;
+  uint64_t* acc_full = empty + STAGES;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_full + 1);
+  __shared__ double s_stats[4];
+  __shared__ int s_fail;
+
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int n0 = blockIdx.y * BN;
+
+  // tile origin
+  int tb = 0, ty0 = 0, tx0 = 0;
+  int64_t m0 = 0;
+  if (p.mode == TC_2D) {
+    const int nxb = (p.Wq + 15) / 16, nyb = (p.Hq + 7) / 8;
+    const int idx = blockIdx.x;
+    tx0 = (idx % nxb) * 16;
+    ty0 = ((idx / nxb) % nyb) * 8;
+    tb = idx / (nxb * nyb);
+  } else if (p.mode == TC_1D) {
+    const int nxb = (p.Wq + BM - 1) / BM;
+    tx0 = (blockIdx.x % nxb) * BM;
+    tb = blockIdx.x / nxb;
+  } else {
+    m0 = (int64_t)blockIdx.x * BM;
+  }
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(acc_full, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    s_fail = 0;
+  }
+  if (threadIdx.x < 4) s_stats[threadIdx.x] = 0.0;
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_u32(tmem_slot)),
+                 "r"(BN));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+  const uint32_t tmem = *tmem_slot;
+  const int ktiles = p.Kpad / BK;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---------------- TMA producer ----------------
+      for (int kt = 0; kt < ktiles; ++kt) {
+        const int s = kt % STAGES;
+        const uint32_t ph = (kt / STAGES) & 1;
+        if (!mbar_wait(&empty[s], ph ^ 1, p.err, 1)) {
+          s_fail = 1;
+          break;
+        }
+        unsigned char* a_dst = smem + s * S::STAGE_BYTES;
+        unsigned char* b_dst = a_dst + S::A_BYTES;
+        mbar_expect_tx(&full[s], S::STAGE_BYTES);
+        const int k0 = kt * BK;
+        if (p.mode == TC_2D) {
+          const int tap = k0 / p.Cin, c0 = k0 - tap * p.Cin;
+          tma_load_4d(a_dst, &tmA, &full[s], c0, tx0 + p.dx[tap], ty0 + p.dy[tap], tb);
+        } else if (p.mode == TC_1D) {
+          const int tap = k0 / p.Cin, c0 = k0 - tap * p.Cin;
+          tma_load_3d(a_dst, &tmA, &full[s], c0, tx0 + p.dx[tap], tb);
+        } else {
+          tma_load_2d(a_dst, &tmA, &full[s], k0, (int)m0);
+        }
+        tma_load_2d(b_dst, &tmB, &full[s], k0, n0);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ---------------- MMA issuer ----------------
+      constexpr uint32_t idesc = (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)(BN >> 3) << 17) |
+                                 ((uint32_t)(BM >> 4) << 24);
+      bool ok = true;
+      for (int kt = 0; kt < ktiles && ok; ++kt) {
+        const int s = kt % STAGES;
+        const uint32_t ph = (kt / STAGES) & 1;
+        if (!mbar_wait(&full[s], ph, p.err, 2)) {
+          ok = false;
+          break;
+        }
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        const uint32_t a_addr = smem_u32(smem + s * S::STAGE_BYTES);
+        const uint32_t b_addr = a_addr + S::A_BYTES;
+#pragma unroll
+        for (int j = 0; j < BK / 8; ++j) {
+          const uint64_t ad = umma_desc(a_addr + j * 32, BK * 4);
+          const uint64_t bd = umma_desc(b_addr + j * 32, BK * 4);
+          umma_tf32(tmem, ad, bd, idesc, (kt | j) != 0);
+        }
+        umma_commit(&empty[s]);
+      }
+      umma_commit(acc_full);
+    }
+  } else {
+    // ---------------- epilogue: warps 2..5, one TMEM lane (row) per thread ----------------
+    const int quarter = warp % 4;  // TMEM lane group this warp may access
+    const int r = quarter * 32 + lane;
+    const bool ok = mbar_wait(acc_full, 0, p.err, 3);
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    int b, y, x;
+    int64_t pos;
+    bool valid;
+    if (p.mode == TC_2D) {
+      y = ty0 + r / 16;
+      x = tx0 + r % 16;
+      b = tb;
+      valid = y < p.Hq && x < p.Wq;
+      pos = ((int64_t)b * p.Hq + y) * p.Wq + x;
+    } else if (p.mode == TC_1D) {
+      y = 0;
+      x = tx0 + r;
+      b = tb;
+      valid = x < p.Wq;
+      pos = (int64_t)b * p.Wq + x;
+    } else {
+      pos = m0 + r;
+      const int64_t plane = (int64_t)p.Hq * p.Wq;
+      valid = pos < (int64_t)p.B * plane;
+      b = (int)(pos / plane);
+      const int64_t rem = pos - (int64_t)b * plane;
+      y = (int)(rem / p.Wq);
+      x = (int)(rem % p.Wq);
+    }
+    const int64_t orow = (int64_t)b * p.o_bs + (int64_t)y * p.o_ys + (int64_t)x * p.o_xs + p.o_off;
+    constexpr bool kStats = EPI == EPI_STATS || EPI == EPI_STORE_STATS || EPI == EPI_RESIDUAL;
+    double ls = 0.0, lq = 0.0;
+    RowNorm nr{0.f, 0.f};
+    if (EPI == EPI_DCONV_TAIL && valid) nr = row_norm(p.epi_nstats, (int)(pos / p.epi_rowlen), p.epi_count);
+    const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
+    for (int c0 = 0; c0 < BN; c0 += 32) {
+      float v[32];
+      __syncwarp();
+      tmem_ld32(tmem + lane_base + (uint32_t)c0, v);
+      const int nb = n0 + c0;
+      if (ok && valid && nb < p.N) {
+#pragma unroll
+      for (int j = 0; j < 32; ++j) v[j] += p.bias[nb + j];
+      if (EPI == EPI_STORE || EPI == EPI_GELU || EPI == EPI_STORE_STATS) {
+        if (EPI == EPI_GELU) {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) v[j] = gelu(v[j]);
+        }
+        if (p.epi_add) {
+          const float* ad = p.epi_add + orow + nb;
+          for (int j = 0; j < 32; ++j)
+            if (nb + j < p.N) v[j] += ad[j];
+        }
+        float* o = p.out + orow + nb;
+        if (nb + 32 <= p.N && ((orow + nb) & 3) == 0) {
+#pragma unroll
+          for (int j = 0; j < 32; j += 4)
+            *reinterpret_cast<float4*>(o + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+        } else {
+          for (int j = 0; j < 32; ++j)
+            if (nb + j < p.N) o[j] = v[j];
+        }
+      }
+      if (EPI == EPI_GLU || EPI == EPI_GLU_EMB) {
+#pragma unroll
+        for (int j = 0; j < 32; j += 2) {
+          if (nb + j >= p.N) break;
+          const int c = (nb + j) / 2;
+          float g = v[j] * sigmoid(v[j + 1]);
+          if (EPI == EPI_GLU_EMB) g += p.epi_emb[(int64_t)y * (p.N / 2) + c];
+          p.out[orow + c] = g;
+        }
+      }
+      if (EPI == EPI_DCONV_TAIL) {
+#pragma unroll
+        for (int j = 0; j < 32; j += 2) {
+          if (nb + j >= p.N) break;
+          const int c = (nb + j) / 2;
+          const float vs = nr.inv * p.epi_gw[c];
+          const float vsh = p.epi_gb[c] - nr.mean * vs;
+          const float gs = nr.inv * p.epi_gw[c + p.epi_half];
+          const float gsh = p.epi_gb[c + p.epi_half] - nr.mean * gs;
+          const float value = v[j] * vs + vsh;
+          const float gate = v[j + 1] * gs + gsh;
+          const int64_t o = orow + c;
+          p.out[o] = p.epi_res[o] + p.epi_gamma[c] * (value * sigmoid(gate));
+        }
+      }
+      if (EPI == EPI_RESIDUAL) {
+        float* o = p.out + orow + nb;
+        const float* rr = p.epi_res + orow + nb;
+        for (int j = 0; j < 32; ++j)
+          if (nb + j < p.N) {
+            v[j] = rr[j] + p.epi_gamma[nb + j] * v[j];
+            o[j] = v[j];
+          }
+      }
+      if (kStats) {
+        for (int j = 0; j < 32; ++j)
+          if (nb + j < p.N) {
+            ls += (double)v[j];
+            lq += (double)v[j] * v[j];
+          }
+      }
+      }  // ok && valid
+    }
+    __syncwarp();
+    if (kStats && p.epi_stats) {
+      // rows of one tile span at most two statistic rows (rowlen >= 128)
+      int64_t first;
+      if (p.mode == TC_2D) {
+        const int64_t p0 = ((int64_t)tb * p.Hq + ty0) * p.Wq + tx0;
+        first = p0 / p.epi_rowlen;
+      } else if (p.mode == TC_1D) {
+        first = ((int64_t)tb * p.Wq + tx0) / p.epi_rowlen;
+      } else {
+        first = m0 / p.epi_rowlen;
+      }
+      const int slot = valid ? (int)(pos / p.epi_rowlen - first) : 0;
+      double s0 = slot == 0 ? ls : 0.0, q0 = slot == 0 ? lq : 0.0;
+      double s1 = slot == 1 ? ls : 0.0, q1 = slot == 1 ? lq : 0.0;
+      s0 = warp_sum(s0);
+      q0 = warp_sum(q0);
+      s1 = warp_sum(s1);
+      q1 = warp_sum(q1);
+      if (lane == 0) {
+        atomicAdd(&s_stats[0], s0);
+        atomicAdd(&s_stats[1], q0);
+        atomicAdd(&s_stats[2], s1);
+        atomicAdd(&s_stats[3], q1);
+      }
+      asm volatile("bar.sync 1, 128;" ::: "memory");
+      if (warp == 2 && lane == 0) {
+        atomicAdd(&p.epi_stats[2 * first], s_stats[0]);
+        atomicAdd(&p.epi_stats[2 * first + 1], s_stats[1]);
+        if (s_stats[2] != 0.0 || s_stats[3] != 0.0) {
+          atomicAdd(&p.epi_stats[2 * (first + 1)], s_stats[2]);
+          atomicAdd(&p.epi_stats[2 * (first + 1) + 1], s_stats[3]);
+        }
+      }
+    }
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(BN));
+  }
+}
+
+// ---------------------------------------------------------------------------
+// host side
+// ---------------------------------------------------------------------------
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+  });
+  return fn;
+}
+
+bool make_map(CUtensorMap* map, const float* base, int rank, const cuuint64_t* dims,
+              const cuuint64_t* strides_bytes, const cuuint32_t* box, CUtensorMapSwizzle swz) {
+  auto fn = encode_fn();
+  if (!fn) return false;
+  cuuint32_t estr[5] = {1, 1, 1, 1, 1};
+  const CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, (cuuint32_t)rank,
+                        const_cast<float*>(base), dims, strides_bytes, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+template <int BN, int BK, int STAGES>
+void launch_cfg(const CUtensorMap& ma, const CUtensorMap& mb, const TcParams& p, int epi,
+                dim3 grid, cudaStream_t s) {
+  const int smem = Smem<BN, BK, STAGES>::TOTAL;
+#define DMX_TC_CASE(E)                                                                        \
+  case E: {                                                                                   \
+    static bool attr = false;                                                                 \
+    if (!attr) {                                                                              \
+      cudaFuncSetAttribute(tc_gemm_kernel<BN, BK, STAGES, E>,                                 \
+                           cudaFuncAttributeMaxDynamicSharedMemorySize, smem);                \
+      attr = true;                                                                            \
+    }                                                                                         \
+    tc_gemm_kernel<BN, BK, STAGES, E><<<grid, 192, smem, s>>>(ma, mb, p);                     \
+    break;                                                                                    \
+  }
+  switch (epi) {
+    DMX_TC_CASE(EPI_STORE)
+    DMX_TC_CASE(EPI_GELU)
+    DMX_TC_CASE(EPI_GLU)
+    DMX_TC_CASE(EPI_GLU_EMB)
+    DMX_TC_CASE(EPI_STATS)
+    DMX_TC_CASE(EPI_STORE_STATS)
+    DMX_TC_CASE(EPI_DCONV_TAIL)
+    DMX_TC_CASE(EPI_RESIDUAL)
+  }
+#undef DMX_TC_CASE
+}
+
+int pick_bn(int N) { return N <= 128 ? 128 : 256; }
+
+}  // namespace
+
+bool tc_gemm_supported(const TcOperandA& a, const TcParams& p) {
+  if (!encode_fn()) return false;
+  const int bk = (p.Cin % 32 == 0) ? 32 : (p.Cin % 16 == 0 ? 16 : 0);
+  if (bk == 0) return false;
+  if (p.mode == TC_2D || p.mode == TC_1D) {
+    if (a.C != p.Cin) return false;
+    if ((a.sw * 4) % 16 || (a.sh * 4) % 16 || (a.sb * 4) % 16) return false;
+  } else {
+    if (p.ntaps != 1) return false;
+    if ((a.sw * 4) % 16) return false;
+  }
+  if ((reinterpret_cast<uintptr_t>(a.ptr) & 15) != 0) return false;
+  return true;
+}
+
+void launch_tc_gemm(const TcOperandA& a, const float* wk, const TcParams& p, int epi,
+                    cudaStream_t s) {
+  const int bk = (p.Cin % 32 == 0) ? 32 : 16;
+  const CUtensorMapSwizzle swz = bk == 32 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
+  const int bn = pick_bn(p.N);
+  CUtensorMap ma, mb;
+  bool ok;
+  dim3 grid;
+  if (p.mode == TC_2D) {
+    const cuuint64_t dims[4] = {(cuuint64_t)a.C, (cuuint64_t)a.W, (cuuint64_t)a.H, (cuuint64_t)a.B};
+    const cuuint64_t str[3] = {(cuuint64_t)a.sw * 4, (cuuint64_t)a.sh * 4, (cuuint64_t)a.sb * 4};
+    const cuuint32_t box[4] = {(cuuint32_t)bk, 16, 8, 1};
+    ok = make_map(&ma, a.ptr, 4, dims, str, box, swz);
+    grid.x = (unsigned)(((p.Wq + 15) / 16) * ((p.Hq + 7) / 8) * p.B);
+  } else if (p.mode == TC_1D) {
+    const cuuint64_t dims[3] = {(cuuint64_t)a.C, (cuuint64_t)a.W, (cuuint64_t)a.B};
+    const cuuint64_t str[2] = {(cuuint64_t)a.sw * 4, (cuuint64_t)a.sb * 4};
+    const cuuint32_t box[3] = {(cuuint32_t)bk, (cuuint32_t)BM, 1};
+    ok = make_map(&ma, a.ptr, 3, dims, str, box, swz);
+    grid.x = (unsigned)(((p.Wq + BM - 1) / BM) * p.B);
+  } else {
+    const cuuint64_t dims[2] = {(cuuint64_t)a.C, (cuuint64_t)a.W};
+    const cuuint64_t str[1] = {(cuuint64_t)a.sw * 4};
+    const cuuint32_t box[2] = {(cuuint32_t)bk, (cuuint32_t)BM};
+    ok = make_map(&ma, a.ptr, 2, dims, str, box, swz);
+    grid.x = (unsigned)((a.W + BM - 1) / BM);
+  }
+  {
+    const cuuint64_t dims[2] = {(cuuint64_t)p.Kpad, (cuuint64_t)p.Npad};
+    const cuuint64_t str[1] = {(cuuint64_t)p.Kpad * 4};
+    const cuuint32_t box[2] = {(cuuint32_t)bk, (cuuint32_t)bn};
+    ok = ok && make_map(&mb, wk, 2, dims, str, box, swz);
+  }
+  if (!ok) return;  // caller checked tc_gemm_supported; a failed encode leaves the output untouched
+  grid.y = (unsigned)((p.N + bn - 1) / bn);
+  grid.z = 1;
+  if (bn == 128) {
+    if (bk == 32) launch_cfg<128, 32, 6>(ma, mb, p, epi, grid, s);
+    else launch_cfg<128, 16, 8>(ma, mb, p, epi, grid, s);
+  } else {
+    if (bk == 32) launch_cfg<256, 32, 4>(ma, mb, p, epi, grid, s);
+    else launch_cfg<256, 16, 6>(ma, mb, p, epi, grid, s);
+  }
+}
+
+}  // namespace dmx

@@ -18,7 +18,8 @@ namespace dmx {
 
 enum TcAMode : int {
   TC_ROWS = 0,  // A is a [rows][K] matrix; tile = 128 consecutive rows
-  TC_2D = 1     // A is a (B, H, W, C) tensor; tile = 8 x 16 positions; taps (dy, dx)
+  TC_2D = 1,    // A is a (B, H, W, C) tensor; tile = 8 x 16 positions; taps (dy, dx)
+  TC_1D = 2     // A is a (B, W, C) tensor; tile = 128 positions along W; taps dx
 };
 
 struct TcParams {
@@ -42,6 +43,7 @@ struct TcParams {
   const float* epi_gamma;
   const float* epi_res;
   const float* epi_emb;
+  const float* epi_add;
   int* err;  // set non-zero when a bounded wait gives up
 };
 
@@ -51,7 +53,7 @@ struct TcParams {
 // tensor-core path (the caller then uses the SIMT kernel).
 struct TcOperandA {
   const float* ptr;
-  int B, H, W, C;           // TC_2D: (B, H, W, C); TC_ROWS: rows = W (B = H = 1), K = C
+  int B, H, W, C;           // TC_2D: (B, H, W, C); TC_1D: (B, W, C); TC_ROWS: rows = W, K = C
   int64_t sb, sh, sw;       // element strides of b, h, w (channels contiguous)
 };
 bool tc_gemm_supported(const TcOperandA& a, const TcParams& p);

@@ -1,0 +1,43 @@
+"""Tensor-core (tcgen05 kind::tf32) build vs the CPU oracle (GPU).
+
+Gate from the north star: per-stem SNR >= 60 dB for the TF32/BF16 builds.
+SNR here is energy based, 10*log10(sum ref^2 / sum (ref - x)^2); the
+reference's own mean-abs form (fixtures.rs:133-149) is reported beside it.
+"""
+
+import numpy as np
+import pytest
+
+import oracle
+import synth
+
+pytestmark = pytest.mark.gpu
+
+
+def snr_db(ref, x):
+    ref = ref.astype(np.float64)
+    err = ref - x
+    return 10 * np.log10(np.sum(ref ** 2) / max(np.sum(err ** 2), 1e-300))
+
+
+def snr_meanabs_db(ref, x):
+    ref = ref.astype(np.float64)
+    return -20 * np.log10(np.mean(np.abs(ref - x)) / np.sqrt(np.mean(ref ** 2)))
+
+
+@pytest.mark.parametrize("layer_scale", [1e-4, 1.0])
+def test_tf32_forward_snr(layer_scale):
+    import dmx
+    w = synth.random_weights(3, layer_scale=layer_scale, norm_jitter=0.1)
+    mix = synth.gaussian_audio(7, 1)
+    tr_o, tr_g = {}, {}
+    ref = oracle.OracleModel(w).forward(mix, trace=tr_o)
+    h = dmx.Handle(synth.write_safetensors(w), device=0, precision=dmx.TF32, max_batch=2)
+    h.set_trace(tr_g)
+    got = h.forward(mix)
+    for name, g in tr_g.items():
+        print(f"{name:36s} snr {snr_db(tr_o[name], g):7.2f} dB")
+    per_stem = [snr_db(ref[0, s], got[0, s]) for s in range(4)]
+    print("per-stem SNR", per_stem, "mean-abs SNR", [snr_meanabs_db(ref[0, s], got[0, s]) for s in range(4)])
+    assert np.isfinite(got).all()
+    assert min(per_stem) >= 60.0, per_stem
