@@ -40,11 +40,14 @@ DMX_DEVICE bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 // Bounded wait: returns false (and raises the error flag) after kWaitNs.
+// Also gives up early once any CTA has raised the flag, so a failed launch
+// drains in milliseconds instead of waiting out every CTA's own deadline.
 DMX_DEVICE bool mbar_wait(uint64_t* bar, uint32_t parity, int* err, int code) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = now_ns();
-  while (true) {
+  for (uint32_t i = 0;; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
+    if ((i & 255) == 0 && err && *reinterpret_cast<volatile int*>(err) != 0) return false;
     if (now_ns() - t0 > (uint64_t)kWaitNs) {
       if (err) atomicExch(err, code);
       return false;
@@ -140,6 +143,8 @@ __global__ void __launch_bounds__(192, 1)
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const int n0 = blockIdx.y * BN;
+  // a previous CTA of this stream gave up: do nothing (uniform across the CTA)
+  if (p.err && *reinterpret_cast<volatile int*>(p.err) != 0) return;
 
   // tile origin
   int tb = 0, ty0 = 0, tx0 = 0;
