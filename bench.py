@@ -175,7 +175,7 @@ def run_ours(args, rank, world, local_rank):
     if world > 1:
         raise SystemExit("multi-GPU sharding is not wired into bench.py yet")
 
-    h = dmx.Handle(blob, device=dev, max_batch=chunks)
+    h = dmx.Handle(blob, device=dev, max_batch=chunks, precision=getattr(dmx, args.precision))
     lr = torch.from_numpy(track).to(f"cuda:{dev}").contiguous()
     stems = torch.empty((4, 2, n), dtype=torch.float32, device=f"cuda:{dev}")
     stream = torch.cuda.ExternalStream(h.stream, device=f"cuda:{dev}")
@@ -224,22 +224,23 @@ def run_ours(args, rank, world, local_rank):
     achieved = flops_per_segment * chunks / (ms / 1e3) / 1e12  # whole forward, TFLOP/s
     line = {"metric": METRIC, "value": round(value, 3), "unit": UNIT, "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 3),
-            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": {"FP32": "f32", "TF32": "tf32", "TF32X3": "tf32x3"}[args.precision],
             "data": "synthetic",
             "config": {"workload": WORKLOAD, "chunks_per_step": chunks, "segment_samples": SEGMENT,
-                       "precision": "fp32 SIMT", "l2": "inputs and workspace larger than L2 (126 MB)"},
+                       "precision": args.precision, "l2": "inputs and workspace larger than L2 (126 MB)"},
             "e2e": {"value": round(TRACK_SECONDS / e2e_s, 3), "unit": UNIT,
                     "h2d_bytes_per_step": int(2 * n * 4), "d2h_bytes_per_step": int(8 * n * 4)},
             "gpu_launches": int(launches) * args.steps,
             "clocks": clocks.summary(),
             "roofline": {"bound": "tensor", "achieved": round(achieved, 3), "peak": bf16,
                          "unit": "TFLOP/s", "frac": round(achieved / bf16, 5), "traffic": None,
-                         "kernel": "whole forward (all contractions, SIMT fp32)",
+                         "kernel": "whole forward (all contractions)",
                          "peak_kind": f"{peak_kind} bf16 dense"},
             "kernels": {k: {"ms": round(v[0], 3), "launches": v[1], "share": round(v[0] / total_ms, 4)}
                         for k, v in sorted(stages.items(), key=lambda kv: -kv[1][0])},
             "top_kernel": top[0]}
-    if rank == 0 and world == 1:
+    if rank == 0 and world == 1 and not args.no_cpu:
         line["cpu_baseline"] = cpu_baseline()
     if rank == 0:
         print(json.dumps(line), flush=True)
@@ -252,6 +253,8 @@ def main():
     ap.add_argument("--steps", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--precision", default="TF32", choices=["FP32", "TF32", "TF32X3"])
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU-baseline leg")
     args = ap.parse_args()
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", str(args.gpus)))

@@ -177,7 +177,8 @@ struct Tap {
 
 struct Packed {
   size_t w_off = 0, b_off = 0;  // float offsets into the weight arena
-  size_t tc_off = 0;            // K-major copy [Npad][K] for the tensor-core path
+  size_t tc_off = 0;            // K-major copy [Npad][K], rounded to nearest tf32
+  size_t tc_lo_off = 0;         // its residual w - tf32(w) (3xTF32 split)
   bool has_tc = false;
   int cin = 0;
   int K = 0, Kpad = 0, N = 0, Npad = 0;
@@ -191,6 +192,17 @@ struct Vec {  // a plain per-channel vector on the device
   int n = 0;
   const float* p = nullptr;
 };
+
+// fp32 -> nearest tf32 (ties to even), in an fp32 container.
+float round_tf32_host(float x) {
+  uint32_t b;
+  std::memcpy(&b, &x, 4);
+  b += 0x0FFFu + ((b >> 13) & 1u);
+  b &= 0xFFFFE000u;
+  float r;
+  std::memcpy(&r, &b, 4);
+  return r;
+}
 
 struct WeightBuilder {
   std::vector<float> host;
@@ -281,7 +293,10 @@ struct Loader {
     p.w_off = wb.alloc((size_t)p.Kpad * p.Npad);
     p.b_off = wb.alloc(p.Npad);
     p.has_tc = cin % 16 == 0;
-    if (p.has_tc) p.tc_off = wb.alloc((size_t)p.Npad * p.K);
+    if (p.has_tc) {
+      p.tc_off = wb.alloc((size_t)p.Npad * p.K);
+      p.tc_lo_off = wb.alloc((size_t)p.Npad * p.K);
+    }
     const int half = cols / 2;
     for (int n = 0; n < cols; ++n) {
       const int co = glu ? ((n % 2 == 0) ? n / 2 : n / 2 + half) : n;
@@ -289,7 +304,11 @@ struct Loader {
         for (int ci = 0; ci < cin; ++ci) {
           const float v = value(tap, ci, co);
           wb.host[p.w_off + (size_t)(tap * cin + ci) * p.Npad + n] = v;
-          if (p.has_tc) wb.host[p.tc_off + (size_t)n * p.K + tap * cin + ci] = v;
+          if (p.has_tc) {
+            const float hi = round_tf32_host(v);
+            wb.host[p.tc_off + (size_t)n * p.K + tap * cin + ci] = hi;
+            wb.host[p.tc_lo_off + (size_t)n * p.K + tap * cin + ci] = v - hi;
+          }
         }
       wb.host[p.b_off + n] = bias[co];
     }
@@ -455,7 +474,9 @@ struct dmx_handle {
         p.epi_rowlen < 128)
       throw Error(DMX_ERR_INVALID, "row statistics need rows of at least 128 positions");
     mark(tag);
-    if (pk && cfg.precision == DMX_TF32 && try_tc(p, pro, epi, *pk)) return;
+    if (pk && (cfg.precision == DMX_TF32 || cfg.precision == DMX_TF32X3) &&
+        try_tc(p, pro, epi, *pk))
+      return;
     launch_conv_gemm(p, pro, epi, stream);
   }
 
@@ -528,7 +549,8 @@ struct dmx_handle {
     t.epi_add = p.epi_add;
     t.err = err;
     if (!tc_gemm_supported(a, t)) return false;
-    launch_tc_gemm(a, wdev + pk.tc_off, t, epi, stream);
+    launch_tc_gemm(a, wdev + pk.tc_off,
+                   cfg.precision == DMX_TF32X3 ? wdev + pk.tc_lo_off : nullptr, t, epi, stream);
     ++tc_launches;
     return true;
   }
@@ -1287,8 +1309,9 @@ dmx_status dmx_create(const dmx_config* cfg, const void* blob, size_t len, int d
       throw Error(DMX_ERR_INVALID,
                   "only the default htdemucs configuration is supported (4 sources, stereo, "
                   "44100 Hz, 343980-sample segments)");
-    if (cfg->precision != DMX_FP32 && cfg->precision != DMX_TF32)
-      throw Error(DMX_ERR_INVALID, "precision must be DMX_FP32 or DMX_TF32");
+    if (cfg->precision != DMX_FP32 && cfg->precision != DMX_TF32 &&
+        cfg->precision != DMX_TF32X3)
+      throw Error(DMX_ERR_INVALID, "precision must be DMX_FP32, DMX_TF32 or DMX_TF32X3");
     if (cfg->max_batch < 1 || cfg->max_batch > 256)
       throw Error(DMX_ERR_INVALID, "max_batch must be in [1, 256]");
     h->cfg = *cfg;

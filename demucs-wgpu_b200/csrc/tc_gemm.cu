@@ -118,25 +118,36 @@ DMX_DEVICE void tmem_ld32(uint32_t taddr, float* v) {
   for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
 }
 
-template <int BN, int BK, int STAGES>
+template <int BN, int BK, int STAGES, bool SPLIT>
 struct Smem {
   static constexpr int A_BYTES = BM * BK * 4;
   static constexpr int B_BYTES = BN * BK * 4;
-  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-  static constexpr int TOTAL = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
+  // stage: A | B [| A_lo | B_lo]; TMA fills A, B (and B_lo), the converter
+  // warps round A in place (and write A_lo)
+  static constexpr int STAGE_BYTES = SPLIT ? 2 * (A_BYTES + B_BYTES) : A_BYTES + B_BYTES;
+  static constexpr int TMA_BYTES = SPLIT ? A_BYTES + 2 * B_BYTES : A_BYTES + B_BYTES;
+  static constexpr int TOTAL = STAGES * STAGE_BYTES + 1024 /*align*/ + 512 /*barriers*/;
 };
 
-template <int BN, int BK, int STAGES, int EPI>
+// fp32 -> nearest tf32 (ties to even), kept in an fp32 container.
+DMX_DEVICE float round_tf32(float x) {
+  uint32_t b = __float_as_uint(x);
+  b += 0x0FFFu + ((b >> 13) & 1u);
+  return __uint_as_float(b & 0xFFFFE000u);
+}
+
+template <int BN, int BK, int STAGES, int EPI, bool SPLIT>
 __global__ void __launch_bounds__(192, 1)
     tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                   const TcParams p) {
-  using S = Smem<BN, BK, STAGES>;
+                   const __grid_constant__ CUtensorMap tmBlo, const TcParams p) {
+  using S = Smem<BN, BK, STAGES, SPLIT>;
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   unsigned char* smem = reinterpret_cast<unsigned char*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * S::STAGE_BYTES);
   uint64_t* empty = full + STAGES;
-  uint64_t* acc_full = empty + STAGES;
+  uint64_t* conv = empty + STAGES;
+  uint64_t* acc_full = conv + STAGES;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_full + 1);
   __shared__ double s_stats[4];
   __shared__ int s_fail;
@@ -167,6 +178,7 @@ __global__ void __launch_bounds__(192, 1)
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
+      mbar_init(&conv[s], 128);
     }
     mbar_init(acc_full, 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -197,7 +209,7 @@ __global__ void __launch_bounds__(192, 1)
         }
         unsigned char* a_dst = smem + s * S::STAGE_BYTES;
         unsigned char* b_dst = a_dst + S::A_BYTES;
-        mbar_expect_tx(&full[s], S::STAGE_BYTES);
+        mbar_expect_tx(&full[s], S::TMA_BYTES);
         const int k0 = kt * BK;
         if (p.mode == TC_2D) {
           const int tap = k0 / p.Cin, c0 = k0 - tap * p.Cin;
@@ -209,6 +221,7 @@ __global__ void __launch_bounds__(192, 1)
           tma_load_2d(a_dst, &tmA, &full[s], k0, (int)m0);
         }
         tma_load_2d(b_dst, &tmB, &full[s], k0, n0);
+        if (SPLIT) tma_load_2d(b_dst + S::B_BYTES + S::A_BYTES, &tmBlo, &full[s], k0, n0);
       }
     }
   } else if (warp == 1) {
@@ -220,18 +233,27 @@ __global__ void __launch_bounds__(192, 1)
       for (int kt = 0; kt < ktiles && ok; ++kt) {
         const int s = kt % STAGES;
         const uint32_t ph = (kt / STAGES) & 1;
-        if (!mbar_wait(&full[s], ph, p.err, 2)) {
+        if (!mbar_wait(&conv[s], ph, p.err, 2)) {
           ok = false;
           break;
         }
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
         const uint32_t a_addr = smem_u32(smem + s * S::STAGE_BYTES);
         const uint32_t b_addr = a_addr + S::A_BYTES;
+        const uint32_t alo_addr = b_addr + S::B_BYTES;
+        const uint32_t blo_addr = alo_addr + S::A_BYTES;
 #pragma unroll
         for (int j = 0; j < BK / 8; ++j) {
           const uint64_t ad = umma_desc(a_addr + j * 32, BK * 4);
           const uint64_t bd = umma_desc(b_addr + j * 32, BK * 4);
-          umma_tf32(tmem, ad, bd, idesc, (kt | j) != 0);
+          if (SPLIT) {
+            // small terms first: lo*hi + hi*lo, then hi*hi
+            umma_tf32(tmem, umma_desc(alo_addr + j * 32, BK * 4), bd, idesc, (kt | j) != 0);
+            umma_tf32(tmem, ad, umma_desc(blo_addr + j * 32, BK * 4), idesc, 1);
+            umma_tf32(tmem, ad, bd, idesc, 1);
+          } else {
+            umma_tf32(tmem, ad, bd, idesc, (kt | j) != 0);
+          }
         }
         umma_commit(&empty[s]);
       }
@@ -241,6 +263,37 @@ __global__ void __launch_bounds__(192, 1)
     // ---------------- epilogue: warps 2..5, one TMEM lane (row) per thread ----------------
     const int quarter = warp % 4;  // TMEM lane group this warp may access
     const int r = quarter * 32 + lane;
+    {
+      // converter: round each landed A row to nearest tf32 in place (the
+      // tensor core would otherwise truncate), and for SPLIT write the
+      // residual x - tf32(x) into the A_lo buffer at the same offset.
+      const int row = threadIdx.x - 64;
+      bool live = true;
+      for (int kt = 0; kt < ktiles; ++kt) {
+        const int s = kt % STAGES;
+        const uint32_t ph = (kt / STAGES) & 1;
+        if (live && !mbar_wait(&full[s], ph, p.err, 4)) live = false;
+        if (live) {
+          float4* a = reinterpret_cast<float4*>(smem + s * S::STAGE_BYTES + row * BK * 4);
+          float4* alo = reinterpret_cast<float4*>(smem + s * S::STAGE_BYTES + S::A_BYTES +
+                                                  S::B_BYTES + row * BK * 4);
+#pragma unroll
+          for (int q = 0; q < BK / 4; ++q) {
+            const float4 x = a[q];
+            float4 hi;
+            hi.x = round_tf32(x.x);
+            hi.y = round_tf32(x.y);
+            hi.z = round_tf32(x.z);
+            hi.w = round_tf32(x.w);
+            a[q] = hi;
+            if (SPLIT) alo[q] = make_float4(x.x - hi.x, x.y - hi.y, x.z - hi.z, x.w - hi.w);
+          }
+        }
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(&conv[s]))
+                     : "memory");
+      }
+    }
     const bool ok = mbar_wait(acc_full, 0, p.err, 3);
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     int b, y, x;
@@ -418,19 +471,19 @@ bool make_map(CUtensorMap* map, const float* base, int rank, const cuuint64_t* d
   return r == CUDA_SUCCESS;
 }
 
-template <int BN, int BK, int STAGES>
-void launch_cfg(const CUtensorMap& ma, const CUtensorMap& mb, const TcParams& p, int epi,
-                dim3 grid, cudaStream_t s) {
-  const int smem = Smem<BN, BK, STAGES>::TOTAL;
+template <int BN, int BK, int STAGES, bool SPLIT>
+void launch_cfg(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mblo,
+                const TcParams& p, int epi, dim3 grid, cudaStream_t s) {
+  const int smem = Smem<BN, BK, STAGES, SPLIT>::TOTAL;
 #define DMX_TC_CASE(E)                                                                        \
   case E: {                                                                                   \
     static bool attr = false;                                                                 \
     if (!attr) {                                                                              \
-      cudaFuncSetAttribute(tc_gemm_kernel<BN, BK, STAGES, E>,                                 \
+      cudaFuncSetAttribute(tc_gemm_kernel<BN, BK, STAGES, E, SPLIT>,                          \
                            cudaFuncAttributeMaxDynamicSharedMemorySize, smem);                \
       attr = true;                                                                            \
     }                                                                                         \
-    tc_gemm_kernel<BN, BK, STAGES, E><<<grid, 192, smem, s>>>(ma, mb, p);                     \
+    tc_gemm_kernel<BN, BK, STAGES, E, SPLIT><<<grid, 192, smem, s>>>(ma, mb, mblo, p);        \
     break;                                                                                    \
   }
   switch (epi) {
@@ -465,12 +518,12 @@ bool tc_gemm_supported(const TcOperandA& a, const TcParams& p) {
   return true;
 }
 
-void launch_tc_gemm(const TcOperandA& a, const float* wk, const TcParams& p, int epi,
-                    cudaStream_t s) {
+void launch_tc_gemm(const TcOperandA& a, const float* wk, const float* wk_lo, const TcParams& p,
+                    int epi, cudaStream_t s) {
   const int bk = (p.Cin % 32 == 0) ? 32 : 16;
   const CUtensorMapSwizzle swz = bk == 32 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
   const int bn = pick_bn(p.N);
-  CUtensorMap ma, mb;
+  CUtensorMap ma, mb, mblo;
   bool ok;
   dim3 grid;
   if (p.mode == TC_2D) {
@@ -497,16 +550,25 @@ void launch_tc_gemm(const TcOperandA& a, const float* wk, const TcParams& p, int
     const cuuint64_t str[1] = {(cuuint64_t)p.Kpad * 4};
     const cuuint32_t box[2] = {(cuuint32_t)bk, (cuuint32_t)bn};
     ok = ok && make_map(&mb, wk, 2, dims, str, box, swz);
+    ok = ok && make_map(&mblo, wk_lo ? wk_lo : wk, 2, dims, str, box, swz);
   }
   if (!ok) return;  // caller checked tc_gemm_supported; a failed encode leaves the output untouched
   grid.y = (unsigned)((p.N + bn - 1) / bn);
   grid.z = 1;
-  if (bn == 128) {
-    if (bk == 32) launch_cfg<128, 32, 6>(ma, mb, p, epi, grid, s);
-    else launch_cfg<128, 16, 8>(ma, mb, p, epi, grid, s);
+  if (wk_lo) {  // 3xTF32: split stages are twice the size
+    if (bn == 128) {
+      if (bk == 32) launch_cfg<128, 32, 3, true>(ma, mb, mblo, p, epi, grid, s);
+      else launch_cfg<128, 16, 6, true>(ma, mb, mblo, p, epi, grid, s);
+    } else {
+      if (bk == 32) launch_cfg<256, 32, 2, true>(ma, mb, mblo, p, epi, grid, s);
+      else launch_cfg<256, 16, 4, true>(ma, mb, mblo, p, epi, grid, s);
+    }
+  } else if (bn == 128) {
+    if (bk == 32) launch_cfg<128, 32, 6, false>(ma, mb, mblo, p, epi, grid, s);
+    else launch_cfg<128, 16, 8, false>(ma, mb, mblo, p, epi, grid, s);
   } else {
-    if (bk == 32) launch_cfg<256, 32, 4>(ma, mb, p, epi, grid, s);
-    else launch_cfg<256, 16, 6>(ma, mb, p, epi, grid, s);
+    if (bk == 32) launch_cfg<256, 32, 4, false>(ma, mb, mblo, p, epi, grid, s);
+    else launch_cfg<256, 16, 6, false>(ma, mb, mblo, p, epi, grid, s);
   }
 }
 

@@ -57,7 +57,9 @@ struct TcOperandA {
   int64_t sb, sh, sw;       // element strides of b, h, w (channels contiguous)
 };
 bool tc_gemm_supported(const TcOperandA& a, const TcParams& p);
-void launch_tc_gemm(const TcOperandA& a, const float* wk, const TcParams& p, int epi,
-                    cudaStream_t s);
+// wk: K-major weights rounded to nearest tf32; wk_lo: their residuals
+// (w - tf32(w)) for the 3xTF32 split, or null for single-pass TF32.
+void launch_tc_gemm(const TcOperandA& a, const float* wk, const float* wk_lo, const TcParams& p,
+                    int epi, cudaStream_t s);
 
 }  // namespace dmx

@@ -31,9 +31,13 @@ enum {
   DMX_ERR_NOMEM = 5      /* device memory exhausted */
 };
 
-/* Arithmetic of the contractions (convolutions, linears, attention).
- * FP32: SIMT fp32 FMA (the max-abs 1e-4 parity build).
- * TF32 / BF16: tensor-core kinds (the SNR >= 60 dB builds). */
+/* Arithmetic of the contractions (convolutions, linears).
+ * FP32: SIMT fp32 FMA everywhere (the max-abs 1e-4 parity build).
+ * TF32: tcgen05 kind::tf32 with both operands rounded to nearest tf32, fp32
+ *       accumulate (the SNR >= 60 dB build).
+ * TF32X3: tcgen05 kind::tf32 on split operands, hi*hi + hi*lo + lo*hi
+ *       (fp32-class accuracy on the tensor cores).
+ * BF16: reserved. */
 typedef enum { DMX_FP32 = 0, DMX_TF32 = 1, DMX_BF16 = 2, DMX_TF32X3 = 3 } dmx_precision;
 
 typedef struct {

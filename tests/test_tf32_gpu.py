@@ -26,13 +26,15 @@ def snr_meanabs_db(ref, x):
 
 
 @pytest.mark.parametrize("layer_scale", [1e-4, 1.0])
-def test_tf32_forward_snr(layer_scale):
+@pytest.mark.parametrize("precision", ["TF32", "TF32X3"])
+def test_tensor_core_forward(layer_scale, precision):
     import dmx
     w = synth.random_weights(3, layer_scale=layer_scale, norm_jitter=0.1)
     mix = synth.gaussian_audio(7, 1)
     tr_o, tr_g = {}, {}
     ref = oracle.OracleModel(w).forward(mix, trace=tr_o)
-    h = dmx.Handle(synth.write_safetensors(w), device=0, precision=dmx.TF32, max_batch=2)
+    h = dmx.Handle(synth.write_safetensors(w), device=0, precision=getattr(dmx, precision),
+                   max_batch=2)
     h.set_trace(tr_g)
     got = h.forward(mix)
     for name, g in tr_g.items():
@@ -41,3 +43,8 @@ def test_tf32_forward_snr(layer_scale):
     print("per-stem SNR", per_stem, "mean-abs SNR", [snr_meanabs_db(ref[0, s], got[0, s]) for s in range(4)])
     assert np.isfinite(got).all()
     assert min(per_stem) >= 60.0, per_stem
+    if precision == "TF32X3":
+        # the split keeps fp32-class accuracy: the FP32 build's max-abs gate
+        worst = np.abs(got.astype(np.float64) - ref).reshape(4, -1).max(axis=1)
+        print("TF32X3 per-stem max-abs", worst)
+        assert worst.max() <= 1e-4, worst
