@@ -20,6 +20,14 @@ constexpr int kStftLen = 347136;  // 343980 + 1536 + 1620
 DMX_DEVICE float gelu(float x) { return 0.5f * x * (1.0f + erff(x * 0.70710678118654752f)); }
 DMX_DEVICE float sigmoid(float g) { return 1.0f / (1.0f + expf(-g)); }
 
+// fp32 -> nearest tf32 (ties to even), kept in an fp32 container.
+DMX_DEVICE float round_tf32(float x) {
+  uint32_t b = __float_as_uint(x);
+  b += 0x0FFFu + ((b >> 13) & 1u);
+  return __uint_as_float(b & 0xFFFFE000u);
+}
+
+
 DMX_DEVICE double warp_sum(double v) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);

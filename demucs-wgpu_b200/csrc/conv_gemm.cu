@@ -161,6 +161,21 @@ __global__ void __launch_bounds__(256) conv_gemm_kernel(const ConvParams p) {
 #pragma unroll
         for (int j = 0; j < TN; ++j) v[j] = gelu(v[j]);
       }
+      if (EPI == EPI_STORE && p.round_out) {
+#pragma unroll
+        for (int j = 0; j < TN; ++j) v[j] = round_tf32(v[j]);
+      }
+      if (EPI == EPI_STORE && p.vt_out) {
+        const int64_t bb = pos / p.vt_ntok, tok = pos % p.vt_ntok;
+#pragma unroll
+        for (int j = 0; j < TN; ++j) {
+          const int n = nb + j;
+          if (n >= p.vt_col0 && n < p.N) {
+            const int c = n - p.vt_col0;
+            p.vt_out[((bb * 8 + c / 64) * 64 + c % 64) * (int64_t)p.vt_ntok + tok] = v[j];
+          }
+        }
+      }
       if (p.epi_add) {
         const float* ad = p.epi_add + orow + nb;
 #pragma unroll

@@ -72,6 +72,11 @@ struct ConvParams {
   const float* epi_res;
   const float* epi_emb;
   const float* epi_add;  // EPI_STORE / EPI_GELU: + add[element] after the activation
+  int round_out;         // EPI_STORE: round stored values to nearest tf32
+  // EPI_STORE: columns >= vt_col0 are also written transposed per segment and
+  // 64-wide head, vt[((b*heads + h)*64 + d)*vt_ntok + token] (attention's V^T)
+  float* vt_out;
+  int vt_col0, vt_ntok;
 };
 
 void launch_conv_gemm(const ConvParams& p, int pro, int epi, cudaStream_t stream);

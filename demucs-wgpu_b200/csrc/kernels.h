@@ -17,6 +17,9 @@ void launch_istft(const float* spec, const float4* norm, const float* window, co
                   const float4* norm_t, float* out, int B, cudaStream_t s);
 
 // transformer.cu
+void launch_gn_gelu_pad(const float* y, int64_t positions, int T, int hid, int hp,
+                        const double* stats, const float* w, const float* b, float* out,
+                        cudaStream_t s);
 void launch_layer_norm(const float* x, int64_t rows, int ntok, const float* w, const float* b,
                        const float* pos, float* out, cudaStream_t s);
 void launch_group_norm_apply(float* x, int B, int64_t ntok, const double* stats, const float* w,

@@ -318,14 +318,16 @@ struct Loader {
   // Conv (Cout, Cin, kh, kw) with an explicit tap list of (ky, kx) kernel
   // indices and their input offsets.
   Packed conv(const std::string& prefix, std::vector<int64_t> shape,
-              const std::vector<std::pair<int, int>>& kidx, std::vector<Tap> taps, bool glu) {
+              const std::vector<std::pair<int, int>>& kidx, std::vector<Tap> taps, bool glu,
+              int cin_pad = 0) {
     const HostTensor& w = get(prefix + ".weight", shape);
     const HostTensor& b = get(prefix + ".bias", {shape[0]});
     const int cout = (int)shape[0], cin = (int)shape[1];
     const int kh = shape.size() == 4 ? (int)shape[2] : 1;
     const int kw = shape.size() == 4 ? (int)shape[3] : (int)shape[2];
-    return pack((int)kidx.size(), cin, cout, glu, b.data,
+    return pack((int)kidx.size(), std::max(cin, cin_pad), cout, glu, b.data,
                 [&](int tap, int ci, int co) {
+                  if (ci >= cin) return 0.0f;  // zero rows for padded input channels
                   const int ky = kidx[tap].first, kx = kidx[tap].second;
                   return w.data[(((size_t)co * cin + ci) * kh + ky) * kw + kx];
                 },
@@ -547,6 +549,10 @@ struct dmx_handle {
     t.epi_res = p.epi_res;
     t.epi_emb = p.epi_emb;
     t.epi_add = p.epi_add;
+    t.round_out = p.round_out;
+    t.vt_out = p.vt_out;
+    t.vt_col0 = p.vt_col0;
+    t.vt_ntok = p.vt_ntok;
     t.err = err;
     if (!tc_gemm_supported(a, t)) return false;
     launch_tc_gemm(a, wdev + pk.tc_off,
@@ -605,12 +611,15 @@ void set_output(ConvParams& p, float* out, int B, int Hq, int Wq, int Cout) {
 }
 
 // DConv residual branch in place on x (rows, T, C) channels-last
-// (host.rs:985-1059): conv1 (k3, dilation 2^d) with its row moments, then the
-// 1x1 GEMM twice — once for the moments of its output, once for
-// GroupNorm + GLU + LayerScale + residual.
+// (host.rs:985-1059). Per layer: conv1 (k3, dilation 2^d) with its row
+// moments; GroupNorm + GELU materialised once into a zero-padded hidden
+// tensor; then the 1x1 GEMM twice — once for the moments of its output, once
+// for GroupNorm + GLU + LayerScale + residual straight into x.
 void run_dconv(dmx_handle* h, const DConvFull& dc, float* x, int rows, int T) {
-  const int C = dc.C, hid = dc.hidden;
-  float* y = h->falloc((size_t)rows * T * hid);
+  const int C = dc.C, hid = dc.hidden, hp = (hid + 15) / 16 * 16;
+  const int64_t positions = (int64_t)rows * T;
+  float* y = h->falloc((size_t)positions * hid);
+  float* yp = h->falloc((size_t)positions * hp);
   double* st = h->dalloc((size_t)rows * 4);
   for (int d = 0; d < 2; ++d) {
     const DConvLayerW& L = dc.layer[d];
@@ -625,26 +634,27 @@ void run_dconv(dmx_handle* h, const DConvFull& dc, float* x, int rows, int T) {
       p.epi_rowlen = T;
       h->gemm(p, PRO_NONE, EPI_STORE_STATS, "dconv.conv1", &L.conv1);
     }
+    h->mark("dconv.gngelu");
+    if (h->live())
+      launch_gn_gelu_pad(y, positions, T, hid, hp, st1, h->W(L.n1w.off), h->W(L.n1b.off), yp,
+                         h->stream);
+    ++h->launches;
     ConvParams p = base_params(L.conv2, h->wdev);
-    set_input(p, y, rows, 1, T, hid);
+    set_input(p, yp, rows, 1, T, hp);
     set_output(p, x, rows, 1, T, C);
-    p.pro_stats = st1;
-    p.pro_rowlen = T;
-    p.pro_count = (double)hid * T;
-    p.pro_scale = h->W(L.n1w.off);
-    p.pro_shift = h->W(L.n1b.off);
     p.epi_stats = st2;
     p.epi_rowlen = T;
-    h->gemm(p, PRO_GN_GELU, EPI_STATS, "dconv.stats", &L.conv2);
+    h->gemm(p, PRO_NONE, EPI_STATS, "dconv.stats", &L.conv2);
     p.epi_stats = nullptr;
     p.epi_nstats = st2;
     p.epi_count = 2.0 * C * T;
+    p.epi_rowlen = T;
     p.epi_gw = h->W(L.n2w.off);
     p.epi_gb = h->W(L.n2b.off);
     p.epi_half = C;
     p.epi_gamma = h->W(L.gamma.off);
     p.epi_res = x;
-    h->gemm(p, PRO_GN_GELU, EPI_DCONV_TAIL, "dconv.tail", &L.conv2);
+    h->gemm(p, PRO_NONE, EPI_DCONV_TAIL, "dconv.tail", &L.conv2);
   }
 }
 
@@ -689,13 +699,19 @@ void trace_tensor(dmx_handle* h, const std::string& name, const float* dev, int 
 // One transformer layer on stream X (B, n, 512), in place (host.rs:1315-1429).
 struct XfBufs {
   float *xn, *kvn, *qkv, *kv2, *att, *hid;
+  float *vt1, *vt2;  // V^T copies for the tensor-core attention
   double* stats;
 };
 
 void xf_gemm(dmx_handle* h, const char* tag, const Packed& pk, const float* in, int B, int n,
              float* out, int epi, const float* res = nullptr, const float* gamma = nullptr,
-             double* stats = nullptr) {
+             double* stats = nullptr, bool round_out = false, float* vt = nullptr,
+             int vt_col0 = 0) {
   ConvParams p = base_params(pk, h->wdev);
+  p.round_out = round_out;
+  p.vt_out = vt;
+  p.vt_col0 = vt_col0;
+  p.vt_ntok = n;
   const int cin = pk.K;
   set_input(p, in, B, 1, n, cin);
   set_output(p, out, B, 1, n, pk.N);
@@ -725,9 +741,13 @@ void xf_self(dmx_handle* h, const LayerW& L, float* X, int B, int n, const XfBuf
   h->mark("xf.layernorm");
   if (h->live()) launch_layer_norm(X, (int64_t)B * n, n, h->W(L.n1w.off), h->W(L.n1b.off), nullptr, bb.xn, h->stream);
   ++h->launches;
-  xf_gemm(h, "xf.qkv", L.qkv, bb.xn, B, n, bb.qkv, EPI_STORE);
+  const bool tc_attn = h->cfg.precision == DMX_TF32;
+  xf_gemm(h, "xf.qkv", L.qkv, bb.xn, B, n, bb.qkv, EPI_STORE, nullptr, nullptr, nullptr, tc_attn,
+          tc_attn ? bb.vt1 : nullptr, 1024);
   h->mark("xf.attention");
-  if (h->live())
+  if (h->live() && !(tc_attn && launch_attention_tc(bb.qkv, 1536, 0, bb.qkv, 1536, 512, 1024, bb.vt1,
+                                                     bb.att, 512, B, 8, n, n, 0.125f, h->err,
+                                                     h->stream)))
     launch_flash_attention(bb.qkv, 1536, bb.qkv + 512, bb.qkv + 1024, 1536, bb.att, 512, B, 8, n, n,
                            0.125f, h->stream);
   ++h->launches;
@@ -736,23 +756,28 @@ void xf_self(dmx_handle* h, const LayerW& L, float* X, int B, int n, const XfBuf
 
 // kv projection of the other stream for a cross layer (LN2 of this layer).
 void xf_cross_kv(dmx_handle* h, const LayerW& L, const float* other, int B, int n_other,
-                 float* kv_out, float* scratch) {
+                 float* kv_out, float* scratch, float* vt) {
   h->mark("xf.layernorm");
   if (h->live())
     launch_layer_norm(other, (int64_t)B * n_other, n_other, h->W(L.n2w.off), h->W(L.n2b.off), nullptr,
                       scratch, h->stream);
   ++h->launches;
-  xf_gemm(h, "xf.kv", L.kv, scratch, B, n_other, kv_out, EPI_STORE);
+  const bool tc_attn = h->cfg.precision == DMX_TF32;
+  xf_gemm(h, "xf.kv", L.kv, scratch, B, n_other, kv_out, EPI_STORE, nullptr, nullptr, nullptr,
+          tc_attn, tc_attn ? vt : nullptr, 512);
 }
 
-void xf_cross(dmx_handle* h, const LayerW& L, float* X, int B, int n, const float* kv, int n_other,
-              const XfBufs& bb) {
+void xf_cross(dmx_handle* h, const LayerW& L, float* X, int B, int n, const float* kv,
+              const float* vt, int n_other, const XfBufs& bb) {
   h->mark("xf.layernorm");
   if (h->live()) launch_layer_norm(X, (int64_t)B * n, n, h->W(L.n1w.off), h->W(L.n1b.off), nullptr, bb.xn, h->stream);
   ++h->launches;
-  xf_gemm(h, "xf.q", L.q, bb.xn, B, n, bb.qkv, EPI_STORE);
+  const bool tc_attn = h->cfg.precision == DMX_TF32;
+  xf_gemm(h, "xf.q", L.q, bb.xn, B, n, bb.qkv, EPI_STORE, nullptr, nullptr, nullptr, tc_attn);
   h->mark("xf.attention");
-  if (h->live())
+  if (h->live() && !(tc_attn && launch_attention_tc(bb.qkv, 512, 0, kv, 1024, 0, 512, vt, bb.att,
+                                                     512, B, 8, n, n_other, 0.125f, h->err,
+                                                     h->stream)))
     launch_flash_attention(bb.qkv, 512, kv, kv + 512, 1024, bb.att, 512, B, 8, n, n_other, 0.125f,
                            h->stream);
   ++h->launches;
@@ -874,6 +899,8 @@ void forward(dmx_handle* h, const float* mix, int G, float* out) {
   bb.att = h->falloc((size_t)G * ntok * D);
   bb.hid = h->falloc((size_t)G * ntok * 4 * D);
   bb.stats = h->dalloc((size_t)G * 2);
+  bb.vt1 = h->falloc((size_t)G * ntok * D);
+  bb.vt2 = h->falloc((size_t)G * ntok * D);
   {
     ConvParams p = base_params(m.up, h->wdev);
     set_input(p, skip[3], G, Fb, Tb, Cs[4]);
@@ -909,13 +936,13 @@ void forward(dmx_handle* h, const float* mix, int G, float* out) {
       xf_self(h, At, Tk, G, Tt, bb);
     } else {
       // kv for the time stream from the OLD spectral stream, first
-      xf_cross_kv(h, At, S, G, ntok, bb.kv2, bb.kvn);
+      xf_cross_kv(h, At, S, G, ntok, bb.kv2, bb.kvn, bb.vt2);
       float* kv_s = bb.hid;  // spectral layer's kv from the time stream (hid is free here)
-      xf_cross_kv(h, A, Tk, G, Tt, kv_s, bb.xn);
+      xf_cross_kv(h, A, Tk, G, Tt, kv_s, bb.xn, bb.vt1);
       // the spectral layer needs its kv before xf_tail reuses hid: copy-free
       // ordering — attention consumes kv_s before the FFN writes hid.
-      xf_cross(h, A, S, G, ntok, kv_s, Tt, bb);
-      xf_cross(h, At, Tk, G, Tt, bb.kv2, ntok, bb);
+      xf_cross(h, A, S, G, ntok, kv_s, bb.vt1, Tt, bb);
+      xf_cross(h, At, Tk, G, Tt, bb.kv2, bb.vt2, ntok, bb);
     }
     trace_tensor(h, "crosstransformer.layers." + std::to_string(l), S, 2, {G, ntok, D});
     trace_tensor(h, "crosstransformer.layers_t." + std::to_string(l), Tk, 2, {G, Tt, D});
@@ -1114,7 +1141,8 @@ void load_model(dmx_handle* h, const std::map<std::string, HostTensor>& t) {
                         {{0, -dil}, {0, 0}, {0, dil}}, false);
       Lw.n1w = L.vec(at + ".1.weight", C / 8);
       Lw.n1b = L.vec(at + ".1.bias", C / 8);
-      Lw.conv2 = L.conv(at + ".3", {2 * C, C / 8, 1}, {{0, 0}}, {{0, 0}}, true);
+      Lw.conv2 = L.conv(at + ".3", {2 * C, C / 8, 1}, {{0, 0}}, {{0, 0}}, true,
+                        (C / 8 + 15) / 16 * 16);
       Lw.n2w = L.vec(at + ".4.weight", 2 * C);
       Lw.n2b = L.vec(at + ".4.bias", 2 * C);
       Lw.gamma = L.vec(at + ".6.scale", C);

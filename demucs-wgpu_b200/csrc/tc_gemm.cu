@@ -3,6 +3,7 @@
 
 #include <mutex>
 
+#include "tc_common.cuh"
 #include "tc_gemm.cuh"
 
 namespace dmx {
@@ -10,114 +11,6 @@ namespace dmx {
 namespace {
 
 constexpr int BM = 128;
-constexpr long long kWaitNs = 2000000000LL;  // bounded waits give up after 2 s
-
-DMX_DEVICE uint32_t smem_u32(const void* p) {
-  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
-}
-DMX_DEVICE uint64_t now_ns() {
-  uint64_t t;
-  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-  return t;
-}
-DMX_DEVICE void mbar_init(uint64_t* bar, uint32_t count) {
-  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
-}
-DMX_DEVICE void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
-  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
-               "r"(bytes)
-               : "memory");
-}
-DMX_DEVICE bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
-  uint32_t ok;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-      "selp.u32 %0, 1, 0, p;\n\t}"
-      : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(parity)
-      : "memory");
-  return ok != 0;
-}
-// Bounded wait: returns false (and raises the error flag) after kWaitNs.
-// Also gives up early once any CTA has raised the flag, so a failed launch
-// drains in milliseconds instead of waiting out every CTA's own deadline.
-DMX_DEVICE bool mbar_wait(uint64_t* bar, uint32_t parity, int* err, int code) {
-  if (mbar_try_wait(bar, parity)) return true;
-  const uint64_t t0 = now_ns();
-  for (uint32_t i = 0;; ++i) {
-    if (mbar_try_wait(bar, parity)) return true;
-    if ((i & 255) == 0 && err && *reinterpret_cast<volatile int*>(err) != 0) return false;
-    if (now_ns() - t0 > (uint64_t)kWaitNs) {
-      if (err) atomicExch(err, code);
-      return false;
-    }
-  }
-}
-
-DMX_DEVICE void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar, int c0, int c1) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];" ::
-          "r"(smem_u32(dst)),
-      "l"(map), "r"(smem_u32(bar)), "r"(c0), "r"(c1)
-      : "memory");
-}
-DMX_DEVICE void tma_load_3d(void* dst, const CUtensorMap* map, uint64_t* bar, int c0, int c1,
-                            int c2) {
-  asm volatile(
-      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5}], [%2];" ::
-          "r"(smem_u32(dst)),
-      "l"(map), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2)
-      : "memory");
-}
-DMX_DEVICE void tma_load_4d(void* dst, const CUtensorMap* map, uint64_t* bar, int c0, int c1,
-                            int c2, int c3) {
-  asm volatile(
-      "cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5, %6}], [%2];" ::
-          "r"(smem_u32(dst)),
-      "l"(map), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
-      : "memory");
-}
-
-// UMMA shared-memory descriptor, K-major, 128B or 64B swizzle
-// (start >> 4 | LBO=1 | SBO = 8 rows * row bytes | version 1 | layout).
-DMX_DEVICE uint64_t umma_desc(uint32_t saddr, int row_bytes) {
-  const uint64_t layout = row_bytes == 128 ? 2ull : 4ull;
-  const uint64_t sbo = (uint64_t)(8 * row_bytes) >> 4;
-  return (uint64_t)((saddr >> 4) & 0x3FFF) | (1ull << 16) | (sbo << 32) | (1ull << 46) |
-         (layout << 61);
-}
-
-DMX_DEVICE void umma_tf32(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
-                          uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
-      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate));
-}
-DMX_DEVICE void umma_commit(uint64_t* bar) {
-  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
-                   smem_u32(bar))
-               : "memory");
-}
-DMX_DEVICE void tmem_ld32(uint32_t taddr, float* v) {
-  uint32_t r[32];
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, "
-      "%12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, "
-      "%30, %31}, [%32];"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
-        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
-        "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]),
-        "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]),
-        "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
-      : "r"(taddr));
-  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-#pragma unroll
-  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
-}
-
 template <int BN, int BK, int STAGES, bool SPLIT>
 struct Smem {
   static constexpr int A_BYTES = BM * BK * 4;
@@ -129,12 +22,6 @@ struct Smem {
   static constexpr int TOTAL = STAGES * STAGE_BYTES + 1024 /*align*/ + 512 /*barriers*/;
 };
 
-// fp32 -> nearest tf32 (ties to even), kept in an fp32 container.
-DMX_DEVICE float round_tf32(float x) {
-  uint32_t b = __float_as_uint(x);
-  b += 0x0FFFu + ((b >> 13) & 1u);
-  return __uint_as_float(b & 0xFFFFE000u);
-}
 
 template <int BN, int BK, int STAGES, int EPI, bool SPLIT>
 __global__ void __launch_bounds__(192, 1)
@@ -244,12 +131,12 @@ __global__ void __launch_bounds__(192, 1)
         const uint32_t blo_addr = alo_addr + S::A_BYTES;
 #pragma unroll
         for (int j = 0; j < BK / 8; ++j) {
-          const uint64_t ad = umma_desc(a_addr + j * 32, BK * 4);
-          const uint64_t bd = umma_desc(b_addr + j * 32, BK * 4);
+          const uint64_t ad = umma_desc_k(a_addr + j * 32, BK * 4);
+          const uint64_t bd = umma_desc_k(b_addr + j * 32, BK * 4);
           if (SPLIT) {
             // small terms first: lo*hi + hi*lo, then hi*hi
-            umma_tf32(tmem, umma_desc(alo_addr + j * 32, BK * 4), bd, idesc, (kt | j) != 0);
-            umma_tf32(tmem, ad, umma_desc(blo_addr + j * 32, BK * 4), idesc, 1);
+            umma_tf32(tmem, umma_desc_k(alo_addr + j * 32, BK * 4), bd, idesc, (kt | j) != 0);
+            umma_tf32(tmem, ad, umma_desc_k(blo_addr + j * 32, BK * 4), idesc, 1);
             umma_tf32(tmem, ad, bd, idesc, 1);
           } else {
             umma_tf32(tmem, ad, bd, idesc, (kt | j) != 0);
@@ -338,6 +225,19 @@ __global__ void __launch_bounds__(192, 1)
         if (EPI == EPI_GELU) {
 #pragma unroll
           for (int j = 0; j < 32; ++j) v[j] = gelu(v[j]);
+        }
+        if (EPI == EPI_STORE && p.round_out) {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) v[j] = round_tf32(v[j]);
+        }
+        if (EPI == EPI_STORE && p.vt_out && nb >= p.vt_col0) {
+          // whole 32-column chunks belong to one head (vt_col0 and 64 are multiples of 32)
+          const int c = nb - p.vt_col0, hh = c / 64, d0 = c % 64;
+          const int64_t row = pos;
+          const int64_t bb = row / p.vt_ntok, tok = row % p.vt_ntok;
+          float* vt = p.vt_out + ((bb * 8 + hh) * 64 + d0) * (int64_t)p.vt_ntok + tok;
+          for (int j = 0; j < 32; ++j)
+            if (nb + j < p.N) vt[(int64_t)j * p.vt_ntok] = v[j];
         }
         if (p.epi_add) {
           const float* ad = p.epi_add + orow + nb;
@@ -445,32 +345,6 @@ __global__ void __launch_bounds__(192, 1)
 // ---------------------------------------------------------------------------
 // host side
 // ---------------------------------------------------------------------------
-PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
-  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-  static std::once_flag once;
-  std::call_once(once, [] {
-    void* ptr = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) ==
-            cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
-  });
-  return fn;
-}
-
-bool make_map(CUtensorMap* map, const float* base, int rank, const cuuint64_t* dims,
-              const cuuint64_t* strides_bytes, const cuuint32_t* box, CUtensorMapSwizzle swz) {
-  auto fn = encode_fn();
-  if (!fn) return false;
-  cuuint32_t estr[5] = {1, 1, 1, 1, 1};
-  const CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, (cuuint32_t)rank,
-                        const_cast<float*>(base), dims, strides_bytes, box, estr,
-                        CU_TENSOR_MAP_INTERLEAVE_NONE, swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  return r == CUDA_SUCCESS;
-}
-
 template <int BN, int BK, int STAGES, bool SPLIT>
 void launch_cfg(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mblo,
                 const TcParams& p, int epi, dim3 grid, cudaStream_t s) {
@@ -504,7 +378,7 @@ int pick_bn(int N) { return N <= 128 ? 128 : 256; }
 }  // namespace
 
 bool tc_gemm_supported(const TcOperandA& a, const TcParams& p) {
-  if (!encode_fn()) return false;
+  if (!tensor_map_encoder()) return false;
   const int bk = (p.Cin % 32 == 0) ? 32 : (p.Cin % 16 == 0 ? 16 : 0);
   if (bk == 0) return false;
   if (p.mode == TC_2D || p.mode == TC_1D) {
@@ -530,27 +404,27 @@ void launch_tc_gemm(const TcOperandA& a, const float* wk, const float* wk_lo, co
     const cuuint64_t dims[4] = {(cuuint64_t)a.C, (cuuint64_t)a.W, (cuuint64_t)a.H, (cuuint64_t)a.B};
     const cuuint64_t str[3] = {(cuuint64_t)a.sw * 4, (cuuint64_t)a.sh * 4, (cuuint64_t)a.sb * 4};
     const cuuint32_t box[4] = {(cuuint32_t)bk, 16, 8, 1};
-    ok = make_map(&ma, a.ptr, 4, dims, str, box, swz);
+    ok = make_tensor_map(&ma, a.ptr, 4, dims, str, box, swz);
     grid.x = (unsigned)(((p.Wq + 15) / 16) * ((p.Hq + 7) / 8) * p.B);
   } else if (p.mode == TC_1D) {
     const cuuint64_t dims[3] = {(cuuint64_t)a.C, (cuuint64_t)a.W, (cuuint64_t)a.B};
     const cuuint64_t str[2] = {(cuuint64_t)a.sw * 4, (cuuint64_t)a.sb * 4};
     const cuuint32_t box[3] = {(cuuint32_t)bk, (cuuint32_t)BM, 1};
-    ok = make_map(&ma, a.ptr, 3, dims, str, box, swz);
+    ok = make_tensor_map(&ma, a.ptr, 3, dims, str, box, swz);
     grid.x = (unsigned)(((p.Wq + BM - 1) / BM) * p.B);
   } else {
     const cuuint64_t dims[2] = {(cuuint64_t)a.C, (cuuint64_t)a.W};
     const cuuint64_t str[1] = {(cuuint64_t)a.sw * 4};
     const cuuint32_t box[2] = {(cuuint32_t)bk, (cuuint32_t)BM};
-    ok = make_map(&ma, a.ptr, 2, dims, str, box, swz);
+    ok = make_tensor_map(&ma, a.ptr, 2, dims, str, box, swz);
     grid.x = (unsigned)((a.W + BM - 1) / BM);
   }
   {
     const cuuint64_t dims[2] = {(cuuint64_t)p.Kpad, (cuuint64_t)p.Npad};
     const cuuint64_t str[1] = {(cuuint64_t)p.Kpad * 4};
     const cuuint32_t box[2] = {(cuuint32_t)bk, (cuuint32_t)bn};
-    ok = ok && make_map(&mb, wk, 2, dims, str, box, swz);
-    ok = ok && make_map(&mblo, wk_lo ? wk_lo : wk, 2, dims, str, box, swz);
+    ok = ok && make_tensor_map(&mb, wk, 2, dims, str, box, swz);
+    ok = ok && make_tensor_map(&mblo, wk_lo ? wk_lo : wk, 2, dims, str, box, swz);
   }
   if (!ok) return;  // caller checked tc_gemm_supported; a failed encode leaves the output untouched
   grid.y = (unsigned)((p.N + bn - 1) / bn);

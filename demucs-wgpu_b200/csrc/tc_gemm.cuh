@@ -44,6 +44,9 @@ struct TcParams {
   const float* epi_res;
   const float* epi_emb;
   const float* epi_add;
+  int round_out;  // EPI_STORE: round stored values to nearest tf32 (attention operands)
+  float* vt_out;  // EPI_STORE: V^T copy of columns >= vt_col0 (see ConvParams)
+  int vt_col0, vt_ntok;
   int* err;  // set non-zero when a bounded wait gives up
 };
 
@@ -61,5 +64,12 @@ bool tc_gemm_supported(const TcOperandA& a, const TcParams& p);
 // (w - tf32(w)) for the 3xTF32 split, or null for single-pass TF32.
 void launch_tc_gemm(const TcOperandA& a, const float* wk, const float* wk_lo, const TcParams& p,
                     int epi, cudaStream_t s);
+
+// Tensor-core flash attention (attention_tc.cu). Returns false when the shape
+// is not supported (the caller then uses the SIMT kernel).
+// vt: V^T as (segment, head, dim, key), written by the projection epilogue.
+bool launch_attention_tc(const float* q, int ldq, int q_col, const float* kv, int ldkv, int k_col,
+                         int v_col, const float* vt, float* out, int ldo, int B, int heads, int nq,
+                         int nk, float scale, int* err, cudaStream_t s);
 
 }  // namespace dmx
