@@ -11,9 +11,13 @@ namespace dmx {
 
 namespace {
 
-__global__ void track_moments_kernel(const float* __restrict__ left,
-                                     const float* __restrict__ right, int64_t n,
-                                     double* __restrict__ stats) {
+constexpr int kNormBlocks = 296;  // fixed grid: the f64 partials are summed in block order
+
+// Per-block moments of the channel-mean signal, written to partials[2*block]
+// (no atomics, so the result does not depend on scheduling).
+__global__ void track_partials_kernel(const float* __restrict__ left,
+                                      const float* __restrict__ right, int64_t n,
+                                      double* __restrict__ partials) {
   __shared__ double red[2][32];
   double s = 0.0, q = 0.0;
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
@@ -36,25 +40,33 @@ __global__ void track_moments_kernel(const float* __restrict__ left,
     s = warp_sum(s);
     q = warp_sum(q);
     if (threadIdx.x == 0) {
-      atomicAdd(&stats[0], s);
-      atomicAdd(&stats[1], q);
+      partials[2 * blockIdx.x] = s;
+      partials[2 * blockIdx.x + 1] = q;
     }
   }
 }
 
 // mean, std (+1e-8) of the channel-mean signal (streaming.rs:52-78), then
-// (x - mean) / std into mix_norm (2, n).
+// (x - mean) / std into mix_norm (2, n) (streaming.rs:81-85).
 __global__ void track_normalize_kernel(const float* __restrict__ left,
                                        const float* __restrict__ right, int64_t n,
-                                       const double* __restrict__ stats,
+                                       const double* __restrict__ partials, int nparts,
                                        float* __restrict__ mix_norm, float2* __restrict__ norm) {
-  const double count = (double)n;
-  const double sum = stats[0], sq = stats[1];
-  const double mean = sum / count;
-  const double var = count > 1.0 ? (sq - sum * sum / count) / (count - 1.0) : 0.0;
-  const float meanf = (float)mean;
-  const float sd = (float)sqrt(fmax(var, 0.0)) + 1e-8f;
-  if (blockIdx.x == 0 && threadIdx.x == 0) *norm = make_float2(meanf, sd);
+  __shared__ float2 s_norm;
+  if (threadIdx.x == 0) {
+    double sum = 0.0, sq = 0.0;
+    for (int i = 0; i < nparts; ++i) {
+      sum += partials[2 * i];
+      sq += partials[2 * i + 1];
+    }
+    const double count = (double)n;
+    const double mean = sum / count;
+    const double var = count > 1.0 ? (sq - sum * sum / count) / (count - 1.0) : 0.0;
+    s_norm = make_float2((float)mean, (float)sqrt(fmax(var, 0.0)) + 1e-8f);
+    if (blockIdx.x == 0) *norm = s_norm;
+  }
+  __syncthreads();
+  const float meanf = s_norm.x, sd = s_norm.y;
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
        i += (int64_t)gridDim.x * blockDim.x) {
     mix_norm[i] = (left[i] - meanf) / sd;
@@ -163,12 +175,14 @@ __global__ void ola_finish_kernel(const float* __restrict__ acc, ChunkGeom g, in
 
 }  // namespace
 
-void launch_track_normalize(const float* left, const float* right, int64_t n, double* stats,
+void launch_track_normalize(const float* left, const float* right, int64_t n, double* scratch,
                             float* mix_norm, float2* norm, cudaStream_t s) {
-  cudaMemsetAsync(stats, 0, 2 * sizeof(double), s);
-  track_moments_kernel<<<296, 512, 0, s>>>(left, right, n, stats);
-  track_normalize_kernel<<<296, 512, 0, s>>>(left, right, n, stats, mix_norm, norm);
+  track_partials_kernel<<<kNormBlocks, 512, 0, s>>>(left, right, n, scratch);
+  track_normalize_kernel<<<kNormBlocks, 512, 0, s>>>(left, right, n, scratch, kNormBlocks, mix_norm,
+                                                     norm);
 }
+
+int track_normalize_scratch_doubles() { return 2 * kNormBlocks; }
 
 static ChunkGeom geom(int64_t length, int64_t shift_offset, int64_t max_shift, int segment,
                       int64_t stride) {

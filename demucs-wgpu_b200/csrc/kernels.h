@@ -29,8 +29,10 @@ void launch_flash_attention(const float* q, int ldq, const float* k, const float
                             cudaStream_t s);
 
 // driver.cu
-void launch_track_normalize(const float* left, const float* right, int64_t n, double* stats,
+// scratch: track_normalize_scratch_doubles() doubles of per-block partials
+void launch_track_normalize(const float* left, const float* right, int64_t n, double* scratch,
                             float* mix_norm, float2* norm, cudaStream_t s);
+int track_normalize_scratch_doubles();
 void launch_gather_chunks(const float* mix_norm, int64_t length, int64_t shift_offset,
                           int64_t max_shift, int segment, int64_t stride, int64_t chunk0,
                           int count, float* out, cudaStream_t s);

@@ -433,6 +433,10 @@ struct dmx_handle {
   dmx_pending pending{};
   char* track_ws = nullptr;
   size_t track_cap = 0;
+  float* host_io = nullptr;  // device staging of dmx_separate_track's host arrays
+  size_t host_io_cap = 0;
+  double* norm_scratch = nullptr;  // per-block moment partials of dmx_normalize_track_device
+  size_t norm_cap = 0;
   int* err = nullptr;  // device flag raised by bounded waits in the tensor-core kernels
   int64_t tc_launches = 0;
 
@@ -1372,6 +1376,8 @@ void dmx_destroy(dmx_handle* h) {
   cudaFree(h->io_in);
   cudaFree(h->io_out);
   cudaFree(h->track_ws);
+  cudaFree(h->host_io);
+  cudaFree(h->norm_scratch);
   cudaFreeHost(h->pinned_in);
   cudaFreeHost(h->pinned_out);
   if (h->stream) cudaStreamDestroy(h->stream);
@@ -1482,6 +1488,33 @@ dmx_status dmx_forward_collect(dmx_pending* p, float* out) {
   }
 }
 
+dmx_status dmx_normalize_track_device(dmx_handle* h, const float* lr_dev, int64_t n,
+                                      float* mix_norm_dev, float* mean_std_dev) {
+  try {
+    if (!h || !lr_dev || !mix_norm_dev || !mean_std_dev || n <= 0)
+      throw Error(DMX_ERR_INVALID, "dmx_normalize_track_device: bad argument");
+    if ((reinterpret_cast<uintptr_t>(mean_std_dev) & 7) != 0)
+      throw Error(DMX_ERR_INVALID, "mean_std_dev must be 8-byte aligned");
+    CK(cudaSetDevice(h->device));
+    const size_t need = (size_t)track_normalize_scratch_doubles() * sizeof(double);
+    if (need > h->norm_cap) {
+      cudaFree(h->norm_scratch);
+      h->norm_scratch = nullptr;
+      h->norm_cap = 0;
+      CK(cudaMalloc(&h->norm_scratch, need));
+      h->norm_cap = need;
+    }
+    launch_track_normalize(lr_dev, lr_dev + n, n, h->norm_scratch, mix_norm_dev,
+                           reinterpret_cast<float2*>(mean_std_dev), h->stream);
+    CK(cudaGetLastError());
+    return DMX_OK;
+  } catch (const Error& e) {
+    return fail(e);
+  } catch (const std::exception& e) {
+    return fail_std(e);
+  }
+}
+
 int64_t dmx_num_chunks(int64_t view_length, int segment, double overlap) {
   const int64_t stride = (int64_t)((1.0 - overlap) * (double)segment);
   if (view_length <= 0 || stride <= 0) return 0;
@@ -1538,18 +1571,21 @@ dmx_status dmx_separate_track_device(dmx_handle* h, const float* lr_dev, int64_t
     const int64_t max_shift = o.shifts > 0 ? (int64_t)(0.5 * 44100.0) : 0;
     const int64_t view_cap = n + max_shift;
     // track-sized scratch, kept on the handle between calls
+    const size_t scratch_bytes = (size_t)track_normalize_scratch_doubles() * sizeof(double);
     const size_t need = (size_t)(2 * n + 8 * view_cap + (o.shifts > 1 ? 8 * n : 0)) * sizeof(float) +
-                        4 * sizeof(double) + 256;
+                        scratch_bytes + 512;
     if (need > h->track_cap) {
       cudaFree(h->track_ws);
+  cudaFree(h->host_io);
+  cudaFree(h->norm_scratch);
       h->track_ws = nullptr;
       h->track_cap = 0;
       CK(cudaMalloc(&h->track_ws, need));
       h->track_cap = need;
     }
     double* d_stats = reinterpret_cast<double*>(h->track_ws);
-    float2* d_norm = reinterpret_cast<float2*>(h->track_ws + 4 * sizeof(double));
-    float* d_mix = reinterpret_cast<float*>(h->track_ws + 256);
+    float2* d_norm = reinterpret_cast<float2*>(h->track_ws + scratch_bytes);
+    float* d_mix = reinterpret_cast<float*>(h->track_ws + scratch_bytes + 512);
     float* d_acc = d_mix + 2 * n;
     float* d_pass = o.shifts > 1 ? d_acc + 8 * view_cap : nullptr;
     h->launches = 0;
@@ -1617,15 +1653,18 @@ dmx_status dmx_separate_track(dmx_handle* h, const float* left, const float* rig
     if (!h || !left || !right || !stems_out || n <= 0)
       throw Error(DMX_ERR_INVALID, "dmx_separate_track: bad argument");
     CK(cudaSetDevice(h->device));
-    float *d_lr = nullptr, *d_stems = nullptr;
-    struct Free {
-      std::vector<void*> p;
-      ~Free() { for (void* q : p) cudaFree(q); }
-    } fr;
-    CK(cudaMalloc(&d_lr, 2 * n * sizeof(float)));
-    fr.p.push_back(d_lr);
-    CK(cudaMalloc(&d_stems, 8 * n * sizeof(float)));
-    fr.p.push_back(d_stems);
+    // host-track staging kept on the handle between calls (grown on demand)
+    const size_t need = (size_t)10 * n * sizeof(float);
+    if (need > h->host_io_cap) {
+      cudaFree(h->host_io);
+  cudaFree(h->norm_scratch);
+      h->host_io = nullptr;
+      h->host_io_cap = 0;
+      CK(cudaMalloc(&h->host_io, need));
+      h->host_io_cap = need;
+    }
+    float* d_lr = h->host_io;
+    float* d_stems = h->host_io + 2 * n;
     CK(cudaMemcpyAsync(d_lr, left, n * sizeof(float), cudaMemcpyHostToDevice, h->stream));
     CK(cudaMemcpyAsync(d_lr + n, right, n * sizeof(float), cudaMemcpyHostToDevice, h->stream));
     const dmx_status st = dmx_separate_track_device(h, d_lr, n, opts, d_stems, progress, user);

@@ -21,7 +21,7 @@ FP32, TF32, BF16, TF32X3 = 0, 1, 2, 3
 EXPORTS = (
     "dmx_default_config", "dmx_create", "dmx_destroy", "dmx_last_error", "dmx_forward_start",
     "dmx_forward_collect", "dmx_forward_device", "dmx_separate_track",
-    "dmx_separate_track_device", "dmx_num_chunks", "dmx_track_shard", "dmx_set_trace",
+    "dmx_separate_track_device", "dmx_normalize_track_device", "dmx_num_chunks", "dmx_track_shard", "dmx_set_trace",
     "dmx_set_stage_timing", "dmx_stage_times", "dmx_kernel_launches", "dmx_stream",
     "dmx_synchronize",
 )
@@ -75,6 +75,8 @@ def lib():
         L.dmx_separate_track_device.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64,
                                                 ctypes.POINTER(SeparateOpts), ctypes.c_void_p,
                                                 PROGRESS_FN, ctypes.c_void_p]
+        L.dmx_normalize_track_device.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64,
+                                                 ctypes.c_void_p, ctypes.c_void_p]
         L.dmx_set_stage_timing.argtypes = [ctypes.c_void_p, ctypes.c_int]
         L.dmx_stream.restype = ctypes.c_void_p
         L.dmx_stream.argtypes = [ctypes.c_void_p]
@@ -159,11 +161,14 @@ class Handle:
                                         ctypes.c_void_p(out_ptr), ctypes.c_void_p(stream)))
 
     def separate_track(self, left, right, shifts=1, overlap=0.25, transition_power=1.0,
-                       batch=0, progress=None):
+                       batch=0, progress=None, out=None):
+        """Whole-track separation of host arrays; ``out`` (4, 2, n) float32 may
+        be supplied (e.g. pinned memory) to avoid a fresh allocation."""
         left = np.ascontiguousarray(left, dtype=np.float32)
         right = np.ascontiguousarray(right, dtype=np.float32)
         n = left.shape[0]
-        stems = np.empty((4, 2, n), dtype=np.float32)
+        stems = np.empty((4, 2, n), dtype=np.float32) if out is None else out
+        assert stems.shape == (4, 2, n) and stems.dtype == np.float32 and stems.flags.c_contiguous
         opts = SeparateOpts(shifts, overlap, transition_power, batch)
         cb = PROGRESS_FN(0) if progress is None else PROGRESS_FN(lambda d, t, _u: progress(d, t))
         _check(lib().dmx_separate_track(self._h, _ptr(left), _ptr(right), n, ctypes.byref(opts),
@@ -193,6 +198,12 @@ class Handle:
         _check(lib().dmx_separate_track_device(self._h, ctypes.c_void_p(lr_ptr), n,
                                                ctypes.byref(opts), ctypes.c_void_p(stems_ptr),
                                                PROGRESS_FN(0), None))
+
+    def normalize_track_device(self, lr_ptr: int, n: int, mix_norm_ptr: int, mean_std_ptr: int):
+        """Enqueue the global normalisation of a (2, n) device track."""
+        _check(lib().dmx_normalize_track_device(self._h, ctypes.c_void_p(lr_ptr), n,
+                                                ctypes.c_void_p(mix_norm_ptr),
+                                                ctypes.c_void_p(mean_std_ptr)))
 
     def set_stage_timing(self, on: bool):
         _check(lib().dmx_set_stage_timing(self._h, int(bool(on))))

@@ -106,6 +106,16 @@ dmx_status dmx_separate_track_device(dmx_handle* h, const float* lr_dev, int64_t
                                      const dmx_separate_opts* opts, float* stems_dev,
                                      dmx_progress_fn progress, void* user);
 
+/* Global normalisation of a raw stereo track on the device (Separator's
+ * normalisation: streaming.rs:52-85 scan_norm + apply_norm_inplace): from
+ * lr_dev (2, n) writes (x - mean) / std into mix_norm_dev (2, n) and
+ * {mean, std} into mean_std_dev (2 floats, 8-byte aligned); mean and the
+ * unbiased std of the channel-mean signal are reduced in f64 in a fixed
+ * order, so every rank of a sharded run derives the same constants.
+ * Enqueued on the handle's stream. */
+dmx_status dmx_normalize_track_device(dmx_handle* h, const float* lr_dev, int64_t n,
+                                      float* mix_norm_dev, float* mean_std_dev);
+
 /* Chunk plan of a split pass (streaming.rs:88-94, 296-330): number of chunks
  * of a view of `view_length` samples. */
 int64_t dmx_num_chunks(int64_t view_length, int segment, double overlap);

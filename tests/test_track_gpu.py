@@ -52,3 +52,24 @@ def test_progress_reports_every_chunk():
     import dmx
     total = dmx.num_chunks(track.shape[1])
     assert seen == [(i + 1, total) for i in range(total)]
+
+
+def test_normalize_track_matches_oracle_scan_norm():
+    # streaming.rs:52-85: mean / unbiased std (+1e-8) of the channel-mean signal
+    import ctypes
+    import torch
+    import dmx
+    h = _handle(synth.random_weights(24), max_batch=1)
+    track = synth.pink_noise(34, 1_000_003)
+    lr = torch.from_numpy(track).cuda()
+    norm = torch.empty_like(lr)
+    ms = torch.empty(2, dtype=torch.float32, device="cuda")
+    h.normalize_track_device(lr.data_ptr(), track.shape[1], norm.data_ptr(), ms.data_ptr())
+    h.synchronize()
+    mean, std = ctypes.c_float(), ctypes.c_float()
+    oracle.lib().orc_scan_norm(oracle.ptr(track), 2, ctypes.c_int64(track.shape[1]),
+                               ctypes.byref(mean), ctypes.byref(std))
+    got = ms.cpu().numpy()
+    assert got[0] == mean.value and got[1] == std.value, (got, mean.value, std.value)
+    ref = (track - mean.value) / std.value
+    assert np.array_equal(norm.cpu().numpy(), ref.astype(np.float32))
