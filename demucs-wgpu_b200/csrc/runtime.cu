@@ -1576,8 +1576,6 @@ dmx_status dmx_separate_track_device(dmx_handle* h, const float* lr_dev, int64_t
                         scratch_bytes + 512;
     if (need > h->track_cap) {
       cudaFree(h->track_ws);
-  cudaFree(h->host_io);
-  cudaFree(h->norm_scratch);
       h->track_ws = nullptr;
       h->track_cap = 0;
       CK(cudaMalloc(&h->track_ws, need));
@@ -1657,7 +1655,6 @@ dmx_status dmx_separate_track(dmx_handle* h, const float* left, const float* rig
     const size_t need = (size_t)10 * n * sizeof(float);
     if (need > h->host_io_cap) {
       cudaFree(h->host_io);
-  cudaFree(h->norm_scratch);
       h->host_io = nullptr;
       h->host_io_cap = 0;
       CK(cudaMalloc(&h->host_io, need));
