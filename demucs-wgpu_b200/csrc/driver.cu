@@ -184,6 +184,12 @@ void launch_track_normalize(const float* left, const float* right, int64_t n, do
 
 int track_normalize_scratch_doubles() { return 2 * kNormBlocks; }
 
+void launch_track_normalize_blocks(const float* left, const float* right, int64_t n, int blocks,
+                                   double* scratch, float* mix_norm, float2* norm, cudaStream_t s) {
+  track_partials_kernel<<<blocks, 512, 0, s>>>(left, right, n, scratch);
+  track_normalize_kernel<<<blocks, 512, 0, s>>>(left, right, n, scratch, blocks, mix_norm, norm);
+}
+
 static ChunkGeom geom(int64_t length, int64_t shift_offset, int64_t max_shift, int segment,
                       int64_t stride) {
   ChunkGeom g;

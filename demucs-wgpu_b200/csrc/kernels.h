@@ -7,6 +7,9 @@
 
 namespace dmx {
 
+// Sets the thread-local message dmx_last_error() returns (runtime.cu).
+void set_last_error(const char* msg);
+
 // spectral.cu
 void launch_stft_cac(const float* mix, int B, const float* window, const float2* tw, float* out,
                      double* stats, cudaStream_t s);
@@ -33,6 +36,9 @@ void launch_flash_attention(const float* q, int ldq, const float* k, const float
 void launch_track_normalize(const float* left, const float* right, int64_t n, double* scratch,
                             float* mix_norm, float2* norm, cudaStream_t s);
 int track_normalize_scratch_doubles();
+// The same two kernels on `blocks` blocks; scratch holds 2*blocks doubles.
+void launch_track_normalize_blocks(const float* left, const float* right, int64_t n, int blocks,
+                                   double* scratch, float* mix_norm, float2* norm, cudaStream_t s);
 void launch_gather_chunks(const float* mix_norm, int64_t length, int64_t shift_offset,
                           int64_t max_shift, int segment, int64_t stride, int64_t chunk0,
                           int count, float* out, cudaStream_t s);

@@ -1312,6 +1312,9 @@ int fail_std(const std::exception& e) {
 
 }  // namespace
 
+// Lets other translation units (noalloc.cu) report through dmx_last_error.
+void dmx::set_last_error(const char* msg) { g_error = msg; }
+
 // ---------------------------------------------------------------------------
 // C ABI
 // ---------------------------------------------------------------------------

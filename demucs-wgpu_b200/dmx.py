@@ -21,7 +21,8 @@ FP32, TF32, BF16, TF32X3 = 0, 1, 2, 3
 EXPORTS = (
     "dmx_default_config", "dmx_create", "dmx_destroy", "dmx_last_error", "dmx_forward_start",
     "dmx_forward_collect", "dmx_forward_device", "dmx_separate_track",
-    "dmx_separate_track_device", "dmx_normalize_track_device", "dmx_num_chunks", "dmx_track_shard", "dmx_set_trace",
+    "dmx_separate_track_device", "dmx_normalize_track_device", "dmx_normalize_track_noalloc",
+    "dmx_num_chunks", "dmx_track_shard", "dmx_set_trace",
     "dmx_set_stage_timing", "dmx_stage_times", "dmx_kernel_launches", "dmx_stream",
     "dmx_synchronize",
 )
@@ -77,6 +78,8 @@ def lib():
                                                 PROGRESS_FN, ctypes.c_void_p]
         L.dmx_normalize_track_device.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64,
                                                  ctypes.c_void_p, ctypes.c_void_p]
+        L.dmx_normalize_track_noalloc.argtypes = [ctypes.c_void_p, ctypes.c_int64, ctypes.c_void_p,
+                                                  ctypes.c_void_p, ctypes.c_void_p]
         L.dmx_set_stage_timing.argtypes = [ctypes.c_void_p, ctypes.c_int]
         L.dmx_stream.restype = ctypes.c_void_p
         L.dmx_stream.argtypes = [ctypes.c_void_p]
@@ -225,6 +228,17 @@ class Handle:
 
     def kernel_launches(self) -> int:
         return lib().dmx_kernel_launches(self._h)
+
+
+def normalize_track_noalloc(lr_ptr: int, n: int, mix_norm_ptr: int, mean_std_ptr: int,
+                            stream: int = 0):
+    """dmx_normalize_track_noalloc: the track normalisation without a handle
+    and without allocating device memory (for callers that may not allocate,
+    such as real-time audio callbacks), on the current device's buffers."""
+    _check(lib().dmx_normalize_track_noalloc(ctypes.c_void_p(lr_ptr), n,
+                                             ctypes.c_void_p(mix_norm_ptr),
+                                             ctypes.c_void_p(mean_std_ptr),
+                                             ctypes.c_void_p(stream)))
 
 
 def num_chunks(view_length: int, segment: int = SEGMENT, overlap: float = 0.25) -> int:

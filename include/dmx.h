@@ -116,6 +116,24 @@ dmx_status dmx_separate_track_device(dmx_handle* h, const float* lr_dev, int64_t
 dmx_status dmx_normalize_track_device(dmx_handle* h, const float* lr_dev, int64_t n,
                                       float* mix_norm_dev, float* mean_std_dev);
 
+/* Allocation-free track normalisation. No counterpart in the reference: it
+ * exists for callers that cannot allocate device memory when they need it —
+ * real-time audio hosts whose processing callback must not block on the
+ * driver's allocator, and applications that reserve their whole device budget
+ * up front — and so cannot create a dmx_handle either. Same result as
+ * dmx_normalize_track_device on the current device's buffers (lr_dev (2, n)
+ * -> mix_norm_dev (2, n), mean_std_dev {mean, std}), enqueued on `stream`
+ * (a cudaStream_t, NULL = legacy default stream), with no cudaMalloc/cudaFree:
+ * its scratch is a 128 KiB file-scope device array (partials of one block per
+ * 65,536 samples), so n is limited to 536,870,912 samples per channel and
+ * larger tracks are rejected with DMX_ERR_INVALID. The first call on a device
+ * resolves that array's device address (cudaGetSymbolAddress) with the device
+ * current, and should come before any stream capture. All calls on a device
+ * share the array: calls that overlap on the GPU (different streams, no
+ * ordering between them) race and must be serialised by the caller. */
+dmx_status dmx_normalize_track_noalloc(const float* lr_dev, int64_t n, float* mix_norm_dev,
+                                       float* mean_std_dev, void* stream);
+
 /* Chunk plan of a split pass (streaming.rs:88-94, 296-330): number of chunks
  * of a view of `view_length` samples. */
 int64_t dmx_num_chunks(int64_t view_length, int segment, double overlap);
