@@ -154,41 +154,72 @@ def run_reference(args, rank, world):
 
 
 def run_ours(args, rank, world, local_rank):
+    import datetime
+
     import torch
     import dmx
+    import shard
 
     dev = local_rank
     torch.cuda.set_device(dev)
+    dist = None
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180),
+                                device_id=torch.device(f"cuda:{dev}"))
     n = int(TRACK_SECONDS * SR)
     track = synth.pink_noise(2024, n)
     shifts, overlap = 1, 0.25
-    max_shift = int(0.5 * SR)
-    # chunk plan of the single shift pass (ShiftRng first draw)
-    rng = (0x5EED1234 * 6364136223846793005 + 1) & (2**64 - 1)
-    rng = (rng * 6364136223846793005 + 1442695040888963407) & (2**64 - 1)
-    offset = (rng >> 33) % (max_shift + 1)
-    vlen = n + max_shift - offset
-    chunks = dmx.num_chunks(vlen)
+    p = shard.plan(n, world, shifts=shifts, overlap=overlap)
+    me = p.rank(rank)
+    mine = me.chunk_hi - me.chunk_lo
     weights = synth.random_weights(0)
     blob = synth.write_safetensors(weights)
-
-    if world > 1:
-        raise SystemExit("multi-GPU sharding is not wired into bench.py yet")
-
-    h = dmx.Handle(blob, device=dev, max_batch=chunks, precision=getattr(dmx, args.precision))
-    lr = torch.from_numpy(track).to(f"cuda:{dev}").contiguous()
-    stems = torch.empty((4, 2, n), dtype=torch.float32, device=f"cuda:{dev}")
+    h = dmx.Handle(blob, device=dev, max_batch=max(1, mine if world > 1 else p.chunks),
+                   precision=getattr(dmx, args.precision))
     stream = torch.cuda.ExternalStream(h.stream, device=f"cuda:{dev}")
+    cuda = f"cuda:{dev}"
+    with torch.cuda.stream(stream):
+        lr = torch.from_numpy(track).to(cuda).contiguous()
+        stems = torch.zeros((4, 2, n), dtype=torch.float32, device=cuda)
+        if world > 1:
+            mix_norm = torch.empty_like(lr)
+            mean_std = torch.empty(2, dtype=torch.float32, device=cuda)
+            acc = torch.empty((8, p.view_length), dtype=torch.float32, device=cuda)
 
     def step():
-        h.separate_track_device(lr.data_ptr(), n, stems.data_ptr(), shifts=shifts, overlap=overlap,
-                                batch=chunks)
+        if world == 1:
+            h.separate_track_device(lr.data_ptr(), n, stems.data_ptr(), shifts=shifts,
+                                    overlap=overlap, batch=p.chunks)
+            return
+        with torch.cuda.stream(stream):
+            h.normalize_track_device(lr.data_ptr(), n, mix_norm.data_ptr(), mean_std.data_ptr())
+            acc.zero_()
+            if mine:
+                h.track_shard(mix_norm.data_ptr(), n, p.offset, p.max_shift, overlap, me.chunk_lo,
+                              me.chunk_hi, mine, acc.data_ptr(), 0, p.view_length)
+            shard.exchange_tails(dist, p, rank, acc)
+            if me.t_hi > me.t_lo:
+                h.track_finish(acc.data_ptr(), n, p.offset, p.max_shift, overlap, shifts,
+                               mean_std.data_ptr(), stems.data_ptr(), me.t_lo, me.t_hi)
+            shard.gather_stems(dist, p, rank, stems.view(8, n))
 
+    def barrier():
+        if dist is not None:
+            dist.barrier()
+
+    barrier()
     for _ in range(args.warmup):
         step()
     h.synchronize()
-    launches = h.kernel_launches()
     torch.cuda.synchronize()
+    before = h.kernel_launches()
+    step()
+    h.synchronize()
+    launches = h.kernel_launches() if world == 1 else h.kernel_launches() - before
+    torch.cuda.synchronize()
+    barrier()
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(dev) as clocks:
         start.record(stream)
@@ -198,43 +229,67 @@ def run_ours(args, rank, world, local_rank):
         h.synchronize()
         torch.cuda.synchronize()
     ms = start.elapsed_time(end) / args.steps
+    if dist is not None:
+        t = torch.tensor([ms], device=cuda)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
     value = TRACK_SECONDS / (ms / 1e3)
 
-    # e2e through the public host API: pinned host input -> stems in host memory
+    # e2e through the public host API: pinned host track in, stems back in pinned host memory
     pin = torch.from_numpy(track).pin_memory()
     out_pin = torch.empty((4, 2, n), dtype=torch.float32).pin_memory()
-    left, right, out_np = pin[0].numpy(), pin[1].numpy(), out_pin.numpy()
-    h.separate_track(left, right, shifts=shifts, overlap=overlap, batch=chunks, out=out_np)
-    t0 = time.perf_counter()
-    for _ in range(args.steps):
-        h.separate_track(left, right, shifts=shifts, overlap=overlap, batch=chunks, out=out_np)
-    e2e_s = (time.perf_counter() - t0) / args.steps
+    if world == 1:
+        left, right, out_np = pin[0].numpy(), pin[1].numpy(), out_pin.numpy()
+        h.separate_track(left, right, shifts=shifts, overlap=overlap, batch=p.chunks, out=out_np)
+        t0 = time.perf_counter()
+        for _ in range(args.steps):
+            h.separate_track(left, right, shifts=shifts, overlap=overlap, batch=p.chunks, out=out_np)
+        e2e_s = (time.perf_counter() - t0) / args.steps
+    else:
+        def e2e_step():
+            with torch.cuda.stream(stream):
+                lr.copy_(pin, non_blocking=True)
+            step()
+            if rank == 0:
+                with torch.cuda.stream(stream):
+                    out_pin.copy_(stems, non_blocking=True)
+            h.synchronize()
+        e2e_step()
+        barrier()
+        t0 = time.perf_counter()
+        for _ in range(args.steps):
+            e2e_step()
+        barrier()
+        t = torch.tensor([(time.perf_counter() - t0) / args.steps], device=cuda)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_s = float(t.item())
 
-    # per-kernel device timing of one more step (untimed pass) for the roofline
+    # per-kernel device timing of one more (untimed) step for the roofline
     h.set_stage_timing(True)
     step()
     h.synchronize()
     stages = h.stage_times()
     h.set_stage_timing(False)
     hbm, bf16, peak_kind = _peaks()
-    top = max(stages.items(), key=lambda kv: kv[1][0])
-    total_ms = sum(v[0] for v in stages.values())
-    flops_per_segment = SEGMENT_GFLOP * 1e9
-    achieved = flops_per_segment * chunks / (ms / 1e3) / 1e12  # whole forward, TFLOP/s
+    top = max(stages.items(), key=lambda kv: kv[1][0]) if stages else ("none", (0.0, 0))
+    total_ms = sum(v[0] for v in stages.values()) or 1.0
+    achieved = SEGMENT_GFLOP * 1e9 * p.chunks / (ms / 1e3) / 1e12 / world  # per GPU, TFLOP/s
     line = {"metric": METRIC, "value": round(value, 3), "unit": UNIT, "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 3),
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
             "dtype": {"FP32": "f32", "TF32": "tf32", "TF32X3": "tf32x3"}[args.precision],
             "data": "synthetic",
-            "config": {"workload": WORKLOAD, "chunks_per_step": chunks, "segment_samples": SEGMENT,
-                       "precision": args.precision, "l2": "inputs and workspace larger than L2 (126 MB)"},
+            "config": {"workload": WORKLOAD, "chunks_per_step": p.chunks, "segment_samples": SEGMENT,
+                       "chunks_per_gpu": [r.chunk_hi - r.chunk_lo for r in p.ranks],
+                       "precision": args.precision, "parallelism": f"chunk-sharded x{world}",
+                       "l2": "inputs and workspace larger than L2 (126 MB)"},
             "e2e": {"value": round(TRACK_SECONDS / e2e_s, 3), "unit": UNIT,
-                    "h2d_bytes_per_step": int(2 * n * 4), "d2h_bytes_per_step": int(8 * n * 4)},
+                    "h2d_bytes_per_step": int(2 * n * 4) * world, "d2h_bytes_per_step": int(8 * n * 4)},
             "gpu_launches": int(launches) * args.steps,
             "clocks": clocks.summary(),
             "roofline": {"bound": "tensor", "achieved": round(achieved, 3), "peak": bf16,
                          "unit": "TFLOP/s", "frac": round(achieved / bf16, 5), "traffic": None,
-                         "kernel": "whole forward (all contractions)",
+                         "kernel": "whole forward per GPU (all contractions, 334.9 GFLOP per segment)",
                          "peak_kind": f"{peak_kind} bf16 dense"},
             "kernels": {k: {"ms": round(v[0], 3), "launches": v[1], "share": round(v[0] / total_ms, 4)}
                         for k, v in sorted(stages.items(), key=lambda kv: -kv[1][0])},
@@ -244,6 +299,9 @@ def run_ours(args, rank, world, local_rank):
     if rank == 0:
         print(json.dumps(line), flush=True)
     h.close()
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
 
 
 def main():

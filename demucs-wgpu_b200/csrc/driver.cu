@@ -142,9 +142,9 @@ __global__ void ola_accumulate_kernel(const float* __restrict__ chunks, ChunkGeo
 __global__ void ola_finish_kernel(const float* __restrict__ acc, ChunkGeom g, int64_t trim,
                                   const float* __restrict__ weight, const float2* __restrict__ norm,
                                   float scale, int mode, float* __restrict__ pass,
-                                  float* __restrict__ stems) {
-  const int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (t >= g.length) return;
+                                  float* __restrict__ stems, int64_t t_lo, int64_t t_hi) {
+  const int64_t t = t_lo + (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (t >= t_hi || t >= g.length) return;
   const float2 nz = *norm;
   if (mode == 3) {
 #pragma unroll
@@ -221,11 +221,15 @@ void launch_ola_accumulate(const float* chunks, int64_t length, int64_t shift_of
 
 void launch_ola_finish(const float* acc, int64_t length, int64_t shift_offset, int64_t max_shift,
                        int segment, int64_t stride, const float* weight, const float2* norm,
-                       float scale, int mode, float* pass, float* stems, cudaStream_t s) {
+                       float scale, int mode, float* pass, float* stems, cudaStream_t s,
+                       int64_t t_lo, int64_t t_hi) {
   const ChunkGeom g = geom(length, shift_offset, max_shift, segment, stride);
   const int64_t trim = max_shift ? max_shift - shift_offset : 0;
-  ola_finish_kernel<<<(unsigned)((length + 255) / 256), 256, 0, s>>>(acc, g, trim, weight, norm,
-                                                                     scale, mode, pass, stems);
+  if (t_hi < 0 || t_hi > length) t_hi = length;
+  if (t_lo < 0) t_lo = 0;
+  if (t_hi <= t_lo) return;
+  ola_finish_kernel<<<(unsigned)((t_hi - t_lo + 255) / 256), 256, 0, s>>>(
+      acc, g, trim, weight, norm, scale, mode, pass, stems, t_lo, t_hi);
 }
 
 }  // namespace dmx

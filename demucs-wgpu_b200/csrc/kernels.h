@@ -46,8 +46,10 @@ void launch_ola_accumulate(const float* chunks, int64_t length, int64_t shift_of
                            int64_t max_shift, int segment, int64_t stride, int64_t chunk0,
                            int count, const float* weight, float* acc, int64_t view_lo,
                            int64_t view_hi, cudaStream_t s);
+// output samples [t_lo, t_hi) only (t_hi < 0: to the end)
 void launch_ola_finish(const float* acc, int64_t length, int64_t shift_offset, int64_t max_shift,
                        int segment, int64_t stride, const float* weight, const float2* norm,
-                       float scale, int mode, float* pass, float* stems, cudaStream_t s);
+                       float scale, int mode, float* pass, float* stems, cudaStream_t s,
+                       int64_t t_lo = 0, int64_t t_hi = -1);
 
 }  // namespace dmx

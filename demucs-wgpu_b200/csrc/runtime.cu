@@ -1518,6 +1518,32 @@ dmx_status dmx_normalize_track_device(dmx_handle* h, const float* lr_dev, int64_
   }
 }
 
+dmx_status dmx_track_finish(dmx_handle* h, const float* acc_dev, int64_t length,
+                            int64_t shift_offset, int64_t max_shift, int segment, double overlap,
+                            int shifts, const float* mean_std_dev, float* stems_dev, int64_t t_lo,
+                            int64_t t_hi) {
+  try {
+    if (!h || !acc_dev || !mean_std_dev || !stems_dev || length <= 0)
+      throw Error(DMX_ERR_INVALID, "dmx_track_finish: bad argument");
+    if (segment != kSegment) throw Error(DMX_ERR_INVALID, "segment must be 343980");
+    if (shifts < 0 || shifts > 1)
+      throw Error(DMX_ERR_INVALID, "dmx_track_finish handles a single pass (shifts 0 or 1)");
+    CK(cudaSetDevice(h->device));
+    const int64_t stride = (int64_t)((1.0 - overlap) * (double)segment);
+    if (stride <= 0) throw Error(DMX_ERR_INVALID, "overlap leaves a zero stride");
+    h->mark("track.finish");
+    launch_ola_finish(acc_dev, length, shift_offset, max_shift, segment, stride,
+                      h->W(h->m.ola_w.off), reinterpret_cast<const float2*>(mean_std_dev), 1.0f,
+                      shifts, nullptr, stems_dev, h->stream, t_lo, t_hi);
+    CK(cudaGetLastError());
+    return DMX_OK;
+  } catch (const Error& e) {
+    return fail(e);
+  } catch (const std::exception& e) {
+    return fail_std(e);
+  }
+}
+
 int64_t dmx_num_chunks(int64_t view_length, int segment, double overlap) {
   const int64_t stride = (int64_t)((1.0 - overlap) * (double)segment);
   if (view_length <= 0 || stride <= 0) return 0;

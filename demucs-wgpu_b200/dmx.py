@@ -22,7 +22,7 @@ EXPORTS = (
     "dmx_default_config", "dmx_create", "dmx_destroy", "dmx_last_error", "dmx_forward_start",
     "dmx_forward_collect", "dmx_forward_device", "dmx_separate_track",
     "dmx_separate_track_device", "dmx_normalize_track_device", "dmx_normalize_track_noalloc",
-    "dmx_num_chunks", "dmx_track_shard", "dmx_set_trace",
+    "dmx_num_chunks", "dmx_track_finish", "dmx_track_shard", "dmx_set_trace",
     "dmx_set_stage_timing", "dmx_stage_times", "dmx_kernel_launches", "dmx_stream",
     "dmx_synchronize",
 )
@@ -80,6 +80,10 @@ def lib():
                                                  ctypes.c_void_p, ctypes.c_void_p]
         L.dmx_normalize_track_noalloc.argtypes = [ctypes.c_void_p, ctypes.c_int64, ctypes.c_void_p,
                                                   ctypes.c_void_p, ctypes.c_void_p]
+        L.dmx_track_finish.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64,
+                                       ctypes.c_int64, ctypes.c_int64, ctypes.c_int, ctypes.c_double,
+                                       ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p,
+                                       ctypes.c_int64, ctypes.c_int64]
         L.dmx_set_stage_timing.argtypes = [ctypes.c_void_p, ctypes.c_int]
         L.dmx_stream.restype = ctypes.c_void_p
         L.dmx_stream.argtypes = [ctypes.c_void_p]
@@ -207,6 +211,13 @@ class Handle:
         _check(lib().dmx_normalize_track_device(self._h, ctypes.c_void_p(lr_ptr), n,
                                                 ctypes.c_void_p(mix_norm_ptr),
                                                 ctypes.c_void_p(mean_std_ptr)))
+
+    def track_finish(self, acc_ptr, length, shift_offset, max_shift, overlap, shifts,
+                     mean_std_ptr, stems_ptr, t_lo=0, t_hi=-1):
+        _check(lib().dmx_track_finish(self._h, ctypes.c_void_p(acc_ptr), length, shift_offset,
+                                      max_shift, SEGMENT, overlap, shifts,
+                                      ctypes.c_void_p(mean_std_ptr), ctypes.c_void_p(stems_ptr),
+                                      t_lo, t_hi))
 
     def set_stage_timing(self, on: bool):
         _check(lib().dmx_set_stage_timing(self._h, int(bool(on))))

@@ -1,0 +1,153 @@
+"""Chunk sharding of one track over ranks (one process per GPU).
+
+The unit of work is a chunk of the split pass (streaming.rs:296-400): its
+forward depends on nothing but its own padded samples, so a track's chunks are
+split into contiguous ranges, one per rank. Each rank overlap-adds its chunks
+into its own span of the view; spans of neighbouring ranks overlap by at most
+``segment - stride`` samples (one chunk's tail), which is the only data that
+crosses between GPUs before the final gather of the stems to rank 0.
+
+Every sample receives at most two weighted contributions (stride >
+segment / 2), and ``(0 + a) + b == (0 + b) + a`` in IEEE arithmetic, so the
+sharded result is identical to the single-GPU one whatever the rank count.
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+SEGMENT = 343980
+SR = 44100
+SHIFT_SEED = 0x5EED1234
+
+
+def shift_offsets(shifts: int, max_shift: int, seed: int = SHIFT_SEED):
+    """The offsets ShiftRng draws for each pass (pipeline.rs:136-151, 416-418)."""
+    mask = (1 << 64) - 1
+    state = (seed * 6364136223846793005 + 1) & mask
+    out = []
+    for _ in range(shifts):
+        state = (state * 6364136223846793005 + 1442695040888963407) & mask
+        out.append((state >> 33) % (max_shift + 1))
+    return out
+
+
+@dataclass
+class RankPlan:
+    rank: int
+    chunk_lo: int
+    chunk_hi: int
+    span_lo: int   # view samples this rank's chunks write
+    span_hi: int
+    own_lo: int    # view samples this rank finalises
+    own_hi: int
+    send_lo: int   # tail sent to rank + 1 (empty when send_lo >= send_hi)
+    send_hi: int
+    t_lo: int      # output samples this rank finalises
+    t_hi: int
+
+
+@dataclass
+class TrackPlan:
+    length: int
+    shifts: int
+    overlap: float
+    segment: int
+    stride: int
+    max_shift: int
+    offset: int
+    view_length: int
+    trim: int
+    chunks: int
+    ranks: list
+
+    def rank(self, r: int) -> RankPlan:
+        return self.ranks[r]
+
+
+def plan(length: int, world: int, shifts: int = 1, overlap: float = 0.25,
+         segment: int = SEGMENT, samplerate: int = SR) -> TrackPlan:
+    """Single-pass plan (shifts 0 or 1) of a ``length``-sample track over ``world`` ranks."""
+    if shifts not in (0, 1):
+        raise ValueError("sharding covers one pass: shifts must be 0 or 1")
+    stride = int((1.0 - overlap) * segment)
+    if stride <= 0:
+        raise ValueError("overlap leaves a zero stride")
+    max_shift = int(0.5 * samplerate) if shifts else 0
+    offset = shift_offsets(1, max_shift)[0] if shifts else 0
+    view_length = length + max_shift - offset if shifts else length
+    trim = max_shift - offset if shifts else 0
+    chunks = -(-view_length // stride)
+    base, extra = divmod(chunks, world)
+    ranks, c = [], 0
+    for r in range(world):
+        k = base + (1 if r < extra else 0)
+        lo, hi = c, c + k
+        c = hi
+        if k == 0:
+            ranks.append(RankPlan(r, lo, hi, 0, 0, 0, 0, 0, 0, 0, 0))
+            continue
+        span_lo = lo * stride
+        span_hi = min(view_length, (hi - 1) * stride + segment)
+        own_lo = lo * stride
+        own_hi = view_length if hi == chunks else hi * stride
+        send_lo, send_hi = own_hi, span_hi if hi < chunks else own_hi
+        t_lo = max(0, own_lo - trim)
+        t_hi = max(t_lo, min(length, own_hi - trim))
+        ranks.append(RankPlan(r, lo, hi, span_lo, span_hi, own_lo, own_hi, send_lo, send_hi,
+                              t_lo, t_hi))
+    return TrackPlan(length, shifts, overlap, segment, stride, max_shift, offset, view_length,
+                     trim, chunks, ranks)
+
+
+def exchange_tails(dist, p: TrackPlan, rank: int, acc):
+    """Rank r adds rank r-1's tail into its own head: ``acc`` is this rank's
+    (8, view_length) accumulator (torch tensor on the backend's device)."""
+    import torch
+
+    world = len(p.ranks)
+    me = p.rank(rank)
+    ops = []
+    recv = None
+    if rank + 1 < world and me.send_hi > me.send_lo and p.rank(rank + 1).chunk_hi > p.rank(rank + 1).chunk_lo:
+        send = acc[:, me.send_lo:me.send_hi].contiguous()
+        ops.append(dist.P2POp(dist.isend, send, rank + 1))
+    if rank > 0:
+        prev = p.rank(rank - 1)
+        if prev.send_hi > prev.send_lo and me.chunk_hi > me.chunk_lo:
+            recv = torch.empty((acc.shape[0], prev.send_hi - prev.send_lo), dtype=acc.dtype,
+                               device=acc.device)
+            ops.append(dist.P2POp(dist.irecv, recv, rank - 1))
+    if ops:
+        for req in dist.batch_isend_irecv(ops):
+            req.wait()
+    if recv is not None:
+        prev = p.rank(rank - 1)
+        acc[:, prev.send_lo:prev.send_hi] += recv
+
+
+def gather_stems(dist, p: TrackPlan, rank: int, stems):
+    """Rank 0 receives every rank's owned output samples into ``stems`` (8, length)."""
+    import torch
+
+    world = len(p.ranks)
+    me = p.rank(rank)
+    if rank == 0:
+        bufs = []
+        ops = []
+        for r in range(1, world):
+            q = p.rank(r)
+            if q.t_hi > q.t_lo:
+                buf = torch.empty((stems.shape[0], q.t_hi - q.t_lo), dtype=stems.dtype,
+                                  device=stems.device)
+                bufs.append((q, buf))
+                ops.append(dist.P2POp(dist.irecv, buf, r))
+        if ops:
+            for req in dist.batch_isend_irecv(ops):
+                req.wait()
+        for q, buf in bufs:
+            stems[:, q.t_lo:q.t_hi] = buf
+    elif me.t_hi > me.t_lo:
+        send = stems[:, me.t_lo:me.t_hi].contiguous()
+        for req in dist.batch_isend_irecv([dist.P2POp(dist.isend, send, 0)]):
+            req.wait()

@@ -148,6 +148,19 @@ dmx_status dmx_track_shard(dmx_handle* h, const float* mix_norm_dev, int64_t len
                            double transition_power, int64_t chunk_lo, int64_t chunk_hi,
                            int batch, float* acc_dev, int64_t view_lo, int64_t view_hi);
 
+/* The end of one split pass over the samples a rank owns (the flush and
+ * denormalisation of streaming.rs:219-260 and api.rs:713-724): for output
+ * samples t in [t_lo, t_hi) (t_hi < 0: to the end), stems = acc / (sum of the
+ * triangular weights covering view sample t + trim) * std + mean, read from
+ * acc_dev (8, view_length) as dmx_track_shard filled it (over the whole view)
+ * and mean_std_dev from dmx_normalize_track_device. stems_dev is (4, 2,
+ * length). Single pass only: shifts 0 (no trim) or 1 (trim max_shift -
+ * shift_offset); scale 1/shifts = 1. */
+dmx_status dmx_track_finish(dmx_handle* h, const float* acc_dev, int64_t length,
+                            int64_t shift_offset, int64_t max_shift, int segment, double overlap,
+                            int shifts, const float* mean_std_dev, float* stems_dev, int64_t t_lo,
+                            int64_t t_hi);
+
 /* Optional activation tracing (mirrors TraceSink, demucs/host.rs:117-125):
  * named intermediates copied to host in the reference's own layouts. */
 typedef void (*dmx_trace_fn)(const char* name, const float* data, const int64_t* shape, int ndim,

@@ -1,0 +1,123 @@
+"""Multi-rank chunk sharding of one track, on CPU with gloo (no GPU).
+
+Two (and three) ranks each overlap-add their contiguous chunk range with a
+deterministic stand-in forward, exchange the boundary tails, finalise the
+samples they own and gather them to rank 0 — the host logic of the multi-GPU
+path in bench.py (shard.py) — and rank 0's stems must equal the oracle's
+single-process driver (streaming.rs:296-400, pipeline.rs:380-515) on the same
+track.
+"""
+
+import ctypes
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+SEG = int(44100 * 0.25)
+
+
+def _forward(padded):
+    # a deterministic, position-dependent stand-in for the network
+    g = padded.shape[0]
+    out = np.repeat(padded[:, None], 4, axis=1) * np.float32(0.75)
+    out += np.float32(0.01) * np.roll(out, 5, axis=-1)
+    return out.reshape(g, 4, 2, -1).astype(np.float32)
+
+
+def _track():
+    i = np.arange(2 * (SEG * 7 + 123))
+    return (np.sin(i * 0.0137) * 0.3 + ((i % 97) - 48) / 480.0).astype(np.float32).reshape(2, -1)
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _worker(rank, world, port, out_path):
+    import datetime
+    import sys
+
+    import torch.distributed as dist
+
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    sys.path[:0] = [os.path.join(root, "demucs-wgpu_b200"), os.path.join(root, "oracle")]
+    import oracle
+    import shard
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=60))
+    track = _track()
+    n = track.shape[1]
+    p = shard.plan(n, world, shifts=1, overlap=0.25, segment=SEG)
+    mean, std = ctypes.c_float(), ctypes.c_float()
+    oracle.lib().orc_scan_norm(oracle.ptr(track), 2, ctypes.c_int64(n), ctypes.byref(mean),
+                               ctypes.byref(std))
+    mix = ((track - np.float32(mean.value)) / np.float32(std.value)).astype(np.float32)
+    weight = np.empty(SEG, np.float32)
+    oracle.lib().orc_transition_weight(SEG, 1.0, oracle.ptr(weight))
+    me = p.rank(rank)
+    acc = torch.zeros((8, p.view_length), dtype=torch.float32)
+    a = acc.numpy()
+    for c in range(me.chunk_lo, me.chunk_hi):
+        vstart = c * p.stride
+        length = min(p.view_length - vstart, SEG)
+        padded = np.empty((2, SEG), np.float32)
+        oracle.lib().orc_padded_chunk(oracle.ptr(mix), 2, ctypes.c_int64(n),
+                                      ctypes.c_int64(p.offset), ctypes.c_int64(p.max_shift),
+                                      ctypes.c_int64(vstart), ctypes.c_int64(length), SEG,
+                                      oracle.ptr(padded))
+        y = _forward(padded[None])[0].reshape(8, SEG)
+        trim = (SEG - length) // 2
+        a[:, vstart:vstart + length] += weight[None, :length] * y[:, trim:trim + length]
+    shard.exchange_tails(dist, p, rank, acc)
+    stems = torch.zeros((8, n), dtype=torch.float32)
+    s = stems.numpy()
+    for t in range(me.t_lo, me.t_hi):
+        v = t + p.trim
+        sw = np.float32(0.0)
+        for c in range(max(0, v // p.stride - 2), min(p.chunks, v // p.stride + 1)):
+            u = v - c * p.stride
+            if 0 <= u < min(p.view_length - c * p.stride, SEG):
+                sw = np.float32(sw + weight[u])
+        s[:, t] = (a[:, v] / sw) * np.float32(std.value) + np.float32(mean.value)
+    shard.gather_stems(dist, p, rank, stems)
+    if rank == 0:
+        np.save(out_path, stems.numpy())
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2, 3])
+def test_sharded_track_matches_single_process_driver(world, tmp_path):
+    import oracle
+
+    out_path = str(tmp_path / "stems.npy")
+    port = _free_port()
+    mp.start_processes(_worker, args=(world, port, out_path), nprocs=world, join=True,
+                       start_method="spawn")
+    got = np.load(out_path).reshape(4, 2, -1)
+    ref = oracle.separate_with(_forward, _track(), SEG, shifts=1)
+    assert got.shape == ref.shape
+    np.testing.assert_allclose(got, ref, rtol=0, atol=2e-6)
+
+
+def test_plan_partitions_every_chunk_once():
+    import shard
+
+    for world in (1, 2, 3, 8):
+        p = shard.plan(10_584_000, world, shifts=1)
+        assert p.chunks == 42
+        covered = [c for r in p.ranks for c in range(r.chunk_lo, r.chunk_hi)]
+        assert covered == list(range(42))
+        assert p.ranks[0].t_lo == 0 and p.ranks[-1].t_hi == 10_584_000
+        for a, b in zip(p.ranks, p.ranks[1:]):
+            assert a.t_hi == b.t_lo and a.own_hi == b.own_lo
+            assert a.send_hi - a.send_lo <= p.segment - p.stride
