@@ -180,13 +180,17 @@ def run_ours(args, rank, world, local_rank):
                    precision=getattr(dmx, args.precision))
     stream = torch.cuda.ExternalStream(h.stream, device=f"cuda:{dev}")
     cuda = f"cuda:{dev}"
-    with torch.cuda.stream(stream):
-        lr = torch.from_numpy(track).to(cuda).contiguous()
-        stems = torch.zeros((4, 2, n), dtype=torch.float32, device=cuda)
-        if world > 1:
-            mix_norm = torch.empty_like(lr)
-            mean_std = torch.empty(2, dtype=torch.float32, device=cuda)
-            acc = torch.empty((8, p.view_length), dtype=torch.float32, device=cuda)
+    # buffers come from torch's allocator on its default stream and are only
+    # used on the handle's stream after a synchronize; they are released before
+    # the handle (and its stream) is destroyed
+    lr = torch.from_numpy(track).to(cuda).contiguous()
+    stems = torch.zeros((4, 2, n), dtype=torch.float32, device=cuda)
+    mix_norm = mean_std = acc = None
+    if world > 1:
+        mix_norm = torch.empty_like(lr)
+        mean_std = torch.empty(2, dtype=torch.float32, device=cuda)
+        acc = torch.empty((8, p.view_length), dtype=torch.float32, device=cuda)
+    torch.cuda.synchronize()
 
     def step():
         if world == 1:
@@ -298,6 +302,10 @@ def run_ours(args, rank, world, local_rank):
         line["cpu_baseline"] = cpu_baseline()
     if rank == 0:
         print(json.dumps(line), flush=True)
+    h.synchronize()
+    torch.cuda.synchronize()
+    del lr, stems, mix_norm, mean_std, acc, pin, out_pin
+    torch.cuda.empty_cache()
     h.close()
     if dist is not None:
         dist.barrier()

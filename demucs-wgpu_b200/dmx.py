@@ -135,13 +135,14 @@ class Handle:
         _check(L.dmx_create(ctypes.byref(cfg), ctypes.cast(buf, ctypes.c_void_p), len(blob),
                             device, ctypes.byref(h)))
         self._h = h
+        self._destroy = L.dmx_destroy  # kept: module globals may be gone at interpreter exit
         self.device = device
         self.max_batch = max_batch
         self._trace_cb = None
 
     def close(self):
         if getattr(self, "_h", None):
-            lib().dmx_destroy(self._h)
+            self._destroy(self._h)
             self._h = None
 
     __del__ = close

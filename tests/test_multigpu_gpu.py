@@ -1,11 +1,14 @@
-"""Chunk-sharded separation over 2 GPUs (NCCL) equals the 1-GPU result.
+"""Chunk-sharded separation over 2 GPUs (NCCL) reproduces the 1-GPU result.
 
 Each rank forwards its contiguous chunk range (dmx_track_shard), the boundary
 tail crosses to the neighbour, each rank finalises the samples it owns
-(dmx_track_finish) and rank 0 gathers the stems. With at most two
-contributions per sample the sums are order-independent, so the result must
-be bit-identical to dmx_separate_track on one GPU. Skipped with fewer than two
-visible GPUs.
+(dmx_track_finish) and rank 0 gathers the stems, which are compared with
+dmx_separate_track on one GPU. Skipped with fewer than two visible GPUs.
+
+The OLA sums are order-independent, but the forward reduces its per-segment
+moments with f64 atomics whose order varies from run to run, so the two runs
+agree to that rounding (the same > 100 dB bar as the batch-independence
+test), not bit for bit.
 """
 
 import os
@@ -76,7 +79,7 @@ def _worker(rank, world, port, out_path):
     dist.destroy_process_group()
 
 
-def test_two_gpu_sharding_is_bit_identical_to_one_gpu(tmp_path):
+def test_two_gpu_sharding_matches_one_gpu(tmp_path):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs two GPUs")
     out_path = str(tmp_path / "stems.npy")
@@ -84,4 +87,7 @@ def test_two_gpu_sharding_is_bit_identical_to_one_gpu(tmp_path):
                        start_method="spawn")
     sharded, single = np.load(out_path)
     assert np.isfinite(sharded).all()
-    assert np.array_equal(sharded, single)
+    err = np.abs(sharded.astype(np.float64) - single)
+    rms = np.sqrt(np.mean(single.astype(np.float64) ** 2))
+    print(f"2-GPU vs 1-GPU: max-abs {err.max():.3e}, mean-abs SNR {-20 * np.log10(max(err.mean(), 1e-30) / rms):.1f} dB")
+    assert err.max() == 0 or -20 * np.log10(err.mean() / rms) > 100
