@@ -39,16 +39,48 @@ SEGMENT = synth.SEGMENT_SAMPLES
 SEGMENT_GFLOP = 334.9  # algorithmic FLOPs of one segment forward (2*MAC over the layer table)
 METRIC = "audio-sec separated/sec (htdemucs)"
 UNIT = "audio-s/s"
-WORKLOAD = "full-track htdemucs: 240 s stereo 44.1 kHz pink noise (RMS 0.1), segment 7.8 s, overlap 0.25, shifts 1, all chunks batched"
+# DRAM bytes (read + write) per launch of the dominant kernel tag, from one ncu
+# capture of the same workload (None until captured): tag -> bytes per launch.
+TRAFFIC = {}
+
+
+def workload(seconds):
+    return (f"full-track htdemucs: {seconds:g} s stereo 44.1 kHz pink noise (RMS 0.1), segment 7.8 s, "
+            "overlap 0.25, shifts 1, all chunks batched")
 
 
 def _peaks():
+    """(HBM GB/s, bf16 TFLOP/s burst, bf16 TFLOP/s sustained, "measured"|"fallback")."""
     try:
         with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
             d = json.load(f)
-        return d["hbm_gbs"], d["bf16_tflops"], "measured"
+        return (d["hbm_gbs"], d["bf16_tflops"], d.get("bf16_tflops_sustained", d["bf16_tflops"]),
+                "measured")
     except Exception:
-        return 6650.0, 1590.0, "fallback"
+        return 6650.0, 1590.0, 1400.0, "fallback"
+
+
+def roofline(stages, traffic=None):
+    """Roofline of the dominant kernel tag (most device time in the step).
+
+    ``stages``: {tag: (ms, launches, flops, bytes)} from the runtime's
+    per-launch accounting (algorithmic FLOPs, minimum HBM bytes). The kernels
+    run inside a long step, so the tensor peak is the sustained one."""
+    hbm, _, bf16_sustained, kind = _peaks()
+    tag, (ms, launches, flops, nbytes) = max(stages.items(), key=lambda kv: kv[1][0])
+    s = ms / 1e3
+    intensity = flops / nbytes if nbytes else float("inf")
+    ridge = bf16_sustained * 1e12 / (hbm * 1e9)
+    if flops > 0 and intensity >= ridge:
+        bound, achieved, peak, unit = "tensor", flops / s / 1e12, bf16_sustained, "TFLOP/s"
+    else:
+        bound, achieved, peak, unit = "hbm", nbytes / s / 1e9, hbm, "GB/s"
+    return {"bound": bound, "achieved": round(achieved, 3), "peak": peak, "unit": unit,
+            "frac": round(achieved / peak, 5), "traffic": traffic,
+            "kernel": tag, "launches": launches,
+            "flops_per_launch": flops / max(launches, 1), "bytes_per_launch": nbytes / max(launches, 1),
+            "arith_intensity": round(intensity, 2) if nbytes else None,
+            "peak_kind": f"{kind} ({'bf16 dense sustained' if unit == 'TFLOP/s' else 'HBM copy'})"}
 
 
 class ClockSampler:
@@ -129,7 +161,7 @@ def run_reference(args, rank, world):
     threads = oracle.threads(0)
     w = synth.random_weights(0)
     m = oracle.OracleModel(w)
-    track = synth.pink_noise(2024, int(TRACK_SECONDS * SR))
+    track = synth.pink_noise(2024, int(args.seconds * SR))
     # one padded chunk of the workload per step (the first chunk of the shift view)
     seg = np.zeros((1, 2, SEGMENT), dtype=np.float32)
     mean = track.mean()
@@ -146,7 +178,7 @@ def run_reference(args, rank, world):
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(dt * 1e3, 3),
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
             "data": "synthetic", "impl": "reference",
-            "config": {"workload": WORKLOAD, "step": "one segment forward of the workload on the host CPU"},
+            "config": {"workload": workload(args.seconds), "step": "one segment forward of the workload on the host CPU"},
             "cpu_baseline": {"value": round(value, 3), "unit": UNIT, "cores": threads, "kind": "port",
                              "sample": "one 343980-sample chunk of the workload per step (oracle/ C++ restatement of the reference CPU forward; the Rust reference is not buildable here)"},
             "e2e": {"value": round(value, 3), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
@@ -168,7 +200,8 @@ def run_ours(args, rank, world, local_rank):
 
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180),
                                 device_id=torch.device(f"cuda:{dev}"))
-    n = int(TRACK_SECONDS * SR)
+    seconds = args.seconds
+    n = int(seconds * SR)
     track = synth.pink_noise(2024, n)
     shifts, overlap = 1, 0.25
     p = shard.plan(n, world, shifts=shifts, overlap=overlap)
@@ -237,7 +270,7 @@ def run_ours(args, rank, world, local_rank):
         t = torch.tensor([ms], device=cuda)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms = float(t.item())
-    value = TRACK_SECONDS / (ms / 1e3)
+    value = seconds / (ms / 1e3)
 
     # e2e through the public host API: pinned host track in, stems back in pinned host memory
     pin = torch.from_numpy(track).pin_memory()
@@ -272,32 +305,32 @@ def run_ours(args, rank, world, local_rank):
     h.set_stage_timing(True)
     step()
     h.synchronize()
-    stages = h.stage_times()
+    stages = h.stage_times(work=True)
     h.set_stage_timing(False)
-    hbm, bf16, peak_kind = _peaks()
-    top = max(stages.items(), key=lambda kv: kv[1][0]) if stages else ("none", (0.0, 0))
+    _, _, bf16_sustained, _ = _peaks()
     total_ms = sum(v[0] for v in stages.values()) or 1.0
-    achieved = SEGMENT_GFLOP * 1e9 * p.chunks / (ms / 1e3) / 1e12 / world  # per GPU, TFLOP/s
+    whole = SEGMENT_GFLOP * 1e9 * (me.chunk_hi - me.chunk_lo) / (ms / 1e3) / 1e12  # this GPU
     line = {"metric": METRIC, "value": round(value, 3), "unit": UNIT, "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 3),
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
             "dtype": {"FP32": "f32", "TF32": "tf32", "TF32X3": "tf32x3"}[args.precision],
             "data": "synthetic",
-            "config": {"workload": WORKLOAD, "chunks_per_step": p.chunks, "segment_samples": SEGMENT,
+            "config": {"workload": workload(seconds), "chunks_per_step": p.chunks, "segment_samples": SEGMENT,
                        "chunks_per_gpu": [r.chunk_hi - r.chunk_lo for r in p.ranks],
                        "precision": args.precision, "parallelism": f"chunk-sharded x{world}",
                        "l2": "inputs and workspace larger than L2 (126 MB)"},
-            "e2e": {"value": round(TRACK_SECONDS / e2e_s, 3), "unit": UNIT,
+            "e2e": {"value": round(seconds / e2e_s, 3), "unit": UNIT,
                     "h2d_bytes_per_step": int(2 * n * 4) * world, "d2h_bytes_per_step": int(8 * n * 4)},
             "gpu_launches": int(launches) * args.steps,
             "clocks": clocks.summary(),
-            "roofline": {"bound": "tensor", "achieved": round(achieved, 3), "peak": bf16,
-                         "unit": "TFLOP/s", "frac": round(achieved / bf16, 5), "traffic": None,
-                         "kernel": "whole forward per GPU (all contractions, 334.9 GFLOP per segment)",
-                         "peak_kind": f"{peak_kind} bf16 dense"},
-            "kernels": {k: {"ms": round(v[0], 3), "launches": v[1], "share": round(v[0] / total_ms, 4)}
-                        for k, v in sorted(stages.items(), key=lambda kv: -kv[1][0])},
-            "top_kernel": top[0]}
+            "roofline": roofline(stages, TRAFFIC.get(max(stages, key=lambda k: stages[k][0]))),
+            "whole_forward": {"achieved": round(whole, 3), "unit": "TFLOP/s",
+                              "frac": round(whole / bf16_sustained, 5),
+                              "note": "334.9 GFLOP per segment over the whole step, rank 0's chunks"},
+            "kernels": {k: {"ms": round(v[0], 3), "launches": v[1], "share": round(v[0] / total_ms, 4),
+                            "tflops": round(v[2] / (v[0] / 1e3) / 1e12, 2) if v[0] else None,
+                            "gbs": round(v[3] / (v[0] / 1e3) / 1e9, 1) if v[0] else None}
+                        for k, v in sorted(stages.items(), key=lambda kv: -kv[1][0])}}
     if rank == 0 and world == 1 and not args.no_cpu:
         line["cpu_baseline"] = cpu_baseline()
     if rank == 0:
@@ -320,6 +353,8 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--precision", default="TF32", choices=["FP32", "TF32", "TF32X3"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU-baseline leg")
+    ap.add_argument("--seconds", type=float, default=TRACK_SECONDS,
+                    help="track length (the benchmark is 240 s; shorter tracks are for profiling)")
     args = ap.parse_args()
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", str(args.gpus)))

@@ -180,7 +180,8 @@ struct Packed {
   size_t tc_off = 0;            // K-major copy [Npad][K], rounded to nearest tf32
   size_t tc_lo_off = 0;         // its residual w - tf32(w) (3xTF32 split)
   bool has_tc = false;
-  int cin = 0;
+  int cin = 0;       // input channels as packed (zero rows pad it to a multiple of 16)
+  int cin_real = 0;  // the layer's own input channels (for the work count)
   int K = 0, Kpad = 0, N = 0, Npad = 0;
   std::vector<Tap> taps;
   const float* w = nullptr;
@@ -290,6 +291,7 @@ struct Loader {
     p.Npad = (cols + kBN - 1) / kBN * kBN;
     p.taps = std::move(taps);
     p.cin = cin;
+    p.cin_real = cin;
     p.w_off = wb.alloc((size_t)p.Kpad * p.Npad);
     p.b_off = wb.alloc(p.Npad);
     p.has_tc = cin % 16 == 0;
@@ -325,13 +327,15 @@ struct Loader {
     const int cout = (int)shape[0], cin = (int)shape[1];
     const int kh = shape.size() == 4 ? (int)shape[2] : 1;
     const int kw = shape.size() == 4 ? (int)shape[3] : (int)shape[2];
-    return pack((int)kidx.size(), std::max(cin, cin_pad), cout, glu, b.data,
-                [&](int tap, int ci, int co) {
-                  if (ci >= cin) return 0.0f;  // zero rows for padded input channels
-                  const int ky = kidx[tap].first, kx = kidx[tap].second;
-                  return w.data[(((size_t)co * cin + ci) * kh + ky) * kw + kx];
-                },
-                std::move(taps));
+    Packed p = pack((int)kidx.size(), std::max(cin, cin_pad), cout, glu, b.data,
+                    [&](int tap, int ci, int co) {
+                      if (ci >= cin) return 0.0f;  // zero rows for padded input channels
+                      const int ky = kidx[tap].first, kx = kidx[tap].second;
+                      return w.data[(((size_t)co * cin + ci) * kh + ky) * kw + kx];
+                    },
+                    std::move(taps));
+    p.cin_real = cin;
+    return p;
   }
 
   // ConvTranspose (Cin, Cout, k[, 1]) restricted to the two kernel rows that
@@ -426,10 +430,16 @@ struct dmx_handle {
   dmx_trace_fn trace = nullptr;
   void* trace_user = nullptr;
   bool stage_timing = false;
-  std::vector<std::pair<std::string, cudaEvent_t>> marks;
+  struct Mark {
+    std::string name;
+    cudaEvent_t ev;
+    double flops, bytes;  // algorithmic work of the launch that starts here
+  };
+  std::vector<Mark> marks;
   std::vector<std::string> stage_names;
   std::vector<float> stage_ms;
   std::vector<int> stage_counts;
+  std::vector<double> stage_flops, stage_bytes;
   dmx_pending pending{};
   char* track_ws = nullptr;
   size_t track_cap = 0;
@@ -459,12 +469,15 @@ struct dmx_handle {
 
   bool live() const { return !measuring; }
 
-  void mark(const std::string& name) {
+  // Stage timing: an event before each launch, tagged with the launch's
+  // algorithmic FLOPs (2 per MAC) and its minimum HBM bytes (each operand read
+  // once, each result written once).
+  void mark(const std::string& name, double flops = 0.0, double bytes = 0.0) {
     if (!stage_timing || measuring) return;
     cudaEvent_t e;
     CK(cudaEventCreate(&e));
     CK(cudaEventRecord(e, stream));
-    marks.emplace_back(name, e);
+    marks.push_back({name, e, flops, bytes});
   }
 
   void zero(void* p, size_t bytes) {
@@ -479,7 +492,18 @@ struct dmx_handle {
     if ((epi == EPI_STATS || epi == EPI_STORE_STATS || epi == EPI_RESIDUAL) && p.epi_stats &&
         p.epi_rowlen < 128)
       throw Error(DMX_ERR_INVALID, "row statistics need rows of at least 128 positions");
-    mark(tag);
+    if (stage_timing) {
+      const double M = (double)p.B * p.Hq * p.Wq;
+      const int cin = pk ? pk->cin_real : p.Cin;
+      const double K = (double)p.ntaps * cin;
+      const bool glu = epi == EPI_GLU || epi == EPI_GLU_EMB || epi == EPI_DCONV_TAIL;
+      const double nout = glu ? p.N / 2 : p.N;
+      double bytes = 4.0 * ((double)p.B * p.Hin * p.Win * cin + K * p.N);
+      if (pro == PRO_ADD) bytes += 4.0 * p.B * p.Hin * p.Win * cin;
+      if (epi != EPI_STATS) bytes += 4.0 * M * nout;
+      if (epi == EPI_RESIDUAL || epi == EPI_DCONV_TAIL) bytes += 4.0 * M * nout;
+      mark(tag, 2.0 * M * K * p.N, bytes);
+    }
     if (pk && (cfg.precision == DMX_TF32 || cfg.precision == DMX_TF32X3) &&
         try_tc(p, pro, epi, *pk))
       return;
@@ -638,7 +662,7 @@ void run_dconv(dmx_handle* h, const DConvFull& dc, float* x, int rows, int T) {
       p.epi_rowlen = T;
       h->gemm(p, PRO_NONE, EPI_STORE_STATS, "dconv.conv1", &L.conv1);
     }
-    h->mark("dconv.gngelu");
+    h->mark("dconv.gngelu", 0.0, 4.0 * positions * (hid + hp));
     if (h->live())
       launch_gn_gelu_pad(y, positions, T, hid, hp, st1, h->W(L.n1w.off), h->W(L.n1b.off), yp,
                          h->stream);
@@ -730,25 +754,25 @@ void xf_tail(dmx_handle* h, const LayerW& L, float* X, int B, int n, const XfBuf
              const Vec& nw, const Vec& nb) {
   // out-projection + LayerScale residual
   xf_gemm(h, "xf.outproj", L.out, bb.att, B, n, X, EPI_RESIDUAL, X, h->W(L.g1.off));
-  h->mark("xf.layernorm");
+  h->mark("xf.layernorm", 0.0, 8.0 * B * n * 512);
   if (h->live()) launch_layer_norm(X, (int64_t)B * n, n, h->W(nw.off), h->W(nb.off), nullptr, bb.xn, h->stream);
   ++h->launches;
   xf_gemm(h, "xf.ffn1", L.lin1, bb.xn, B, n, bb.hid, EPI_GELU);
   h->zero(bb.stats, (size_t)B * 2 * sizeof(double));
   xf_gemm(h, "xf.ffn2", L.lin2, bb.hid, B, n, X, EPI_RESIDUAL, X, h->W(L.g2.off), bb.stats);
-  h->mark("xf.groupnorm");
+  h->mark("xf.groupnorm", 0.0, 8.0 * B * n * 512);
   if (h->live()) launch_group_norm_apply(X, B, n, bb.stats, h->W(L.now.off), h->W(L.nob.off), h->stream);
   ++h->launches;
 }
 
 void xf_self(dmx_handle* h, const LayerW& L, float* X, int B, int n, const XfBufs& bb) {
-  h->mark("xf.layernorm");
+  h->mark("xf.layernorm", 0.0, 8.0 * B * n * 512);
   if (h->live()) launch_layer_norm(X, (int64_t)B * n, n, h->W(L.n1w.off), h->W(L.n1b.off), nullptr, bb.xn, h->stream);
   ++h->launches;
   const bool tc_attn = h->cfg.precision == DMX_TF32;
   xf_gemm(h, "xf.qkv", L.qkv, bb.xn, B, n, bb.qkv, EPI_STORE, nullptr, nullptr, nullptr, tc_attn,
           tc_attn ? bb.vt1 : nullptr, 1024);
-  h->mark("xf.attention");
+  h->mark("xf.attention", 4.0 * B * n * n * 512, 4.0 * B * n * 512 * 4);
   if (h->live() && !(tc_attn && launch_attention_tc(bb.qkv, 1536, 0, bb.qkv, 1536, 512, 1024, bb.vt1,
                                                      bb.att, 512, B, 8, n, n, 0.125f, h->err,
                                                      h->stream)))
@@ -761,7 +785,7 @@ void xf_self(dmx_handle* h, const LayerW& L, float* X, int B, int n, const XfBuf
 // kv projection of the other stream for a cross layer (LN2 of this layer).
 void xf_cross_kv(dmx_handle* h, const LayerW& L, const float* other, int B, int n_other,
                  float* kv_out, float* scratch, float* vt) {
-  h->mark("xf.layernorm");
+  h->mark("xf.layernorm", 0.0, 8.0 * B * n_other * 512);
   if (h->live())
     launch_layer_norm(other, (int64_t)B * n_other, n_other, h->W(L.n2w.off), h->W(L.n2b.off), nullptr,
                       scratch, h->stream);
@@ -773,12 +797,12 @@ void xf_cross_kv(dmx_handle* h, const LayerW& L, const float* other, int B, int 
 
 void xf_cross(dmx_handle* h, const LayerW& L, float* X, int B, int n, const float* kv,
               const float* vt, int n_other, const XfBufs& bb) {
-  h->mark("xf.layernorm");
+  h->mark("xf.layernorm", 0.0, 8.0 * B * n * 512);
   if (h->live()) launch_layer_norm(X, (int64_t)B * n, n, h->W(L.n1w.off), h->W(L.n1b.off), nullptr, bb.xn, h->stream);
   ++h->launches;
   const bool tc_attn = h->cfg.precision == DMX_TF32;
   xf_gemm(h, "xf.q", L.q, bb.xn, B, n, bb.qkv, EPI_STORE, nullptr, nullptr, nullptr, tc_attn);
-  h->mark("xf.attention");
+  h->mark("xf.attention", 4.0 * B * n * n_other * 512, 4.0 * B * (2.0 * n + 2.0 * n_other) * 512);
   if (h->live() && !(tc_attn && launch_attention_tc(bb.qkv, 512, 0, kv, 1024, 0, 512, vt, bb.att,
                                                      512, B, 8, n, n_other, 0.125f, h->err,
                                                      h->stream)))
@@ -804,7 +828,7 @@ void forward(dmx_handle* h, const float* mix, int G, float* out) {
   float4* norm_t = norm + G;
   float* X = h->falloc((size_t)G * kBins * kFrames * 4);
   h->zero(mom, (size_t)G * 4 * sizeof(double));
-  h->mark("spec.stft");
+  h->mark("spec.stft", 0.0, 4.0 * G * (2.0 * L + (double)kBins * kFrames * 4));
   if (h->live()) {
     launch_stft_cac(mix, G, h->W(m.window.off), tw, X, mom, s);
     launch_wave_moments(mix, G, 2LL * L, mom + 2 * G, s);
@@ -920,7 +944,7 @@ void forward(dmx_handle* h, const float* mix, int G, float* out) {
     set_input(q, tskip[3], G, 1, Tt, TCs[4]);
     set_output(q, bb.kv2, G, 1, Tt, D);
     h->gemm(q, PRO_NONE, EPI_STORE, "xf.upsample", &m.up_t);
-    h->mark("xf.layernorm");
+    h->mark("xf.layernorm", 0.0, 8.0 * G * (ntok + Tt) * D);
     if (h->live()) {
       launch_layer_norm(bb.kvn, (int64_t)G * ntok, ntok, h->W(m.norm_in_w.off), h->W(m.norm_in_b.off),
                         h->W(m.pos2d.off), S, s);
@@ -1050,7 +1074,7 @@ void forward(dmx_handle* h, const float* mix, int G, float* out) {
 
   // (g) iSTFT + branch sum (host.rs:466-519)
   float* frames = h->falloc((size_t)G * 8 * kFrames * kNfft);
-  h->mark("spec.istft");
+  h->mark("spec.istft", 0.0, 4.0 * G * ((double)kBins * kFrames * 16 + 16.0 * L));
   if (h->live()) {
     launch_istft(x, norm_f, h->W(m.window.off), tw, frames, h->W(m.env.off), xt, norm_t, out, G, s);
     h->after("istft");
@@ -1071,36 +1095,45 @@ void check_device_flag(dmx_handle* h) {
 
 void finish_stage_times(dmx_handle* h) {
   if (h->marks.empty()) return;
-  CK(cudaEventSynchronize(h->marks.back().second));
+  CK(cudaEventSynchronize(h->marks.back().ev));
   h->stage_names.clear();
   h->stage_ms.clear();
   h->stage_counts.clear();
+  h->stage_flops.clear();
+  h->stage_bytes.clear();
   std::map<std::string, size_t> index;
   for (size_t i = 0; i + 1 < h->marks.size(); ++i) {
+    const auto& mk = h->marks[i];
     float ms = 0.f;
-    CK(cudaEventElapsedTime(&ms, h->marks[i].second, h->marks[i + 1].second));
-    auto it = index.find(h->marks[i].first);
+    CK(cudaEventElapsedTime(&ms, mk.ev, h->marks[i + 1].ev));
+    auto it = index.find(mk.name);
     if (it == index.end()) {
-      index[h->marks[i].first] = h->stage_names.size();
-      h->stage_names.push_back(h->marks[i].first);
+      index[mk.name] = h->stage_names.size();
+      h->stage_names.push_back(mk.name);
       h->stage_ms.push_back(ms);
       h->stage_counts.push_back(1);
+      h->stage_flops.push_back(mk.flops);
+      h->stage_bytes.push_back(mk.bytes);
     } else {
       h->stage_ms[it->second] += ms;
       h->stage_counts[it->second] += 1;
+      h->stage_flops[it->second] += mk.flops;
+      h->stage_bytes[it->second] += mk.bytes;
     }
   }
-  for (auto& mk : h->marks) cudaEventDestroy(mk.second);
+  for (auto& mk : h->marks) cudaEventDestroy(mk.ev);
   h->marks.clear();
 }
 
 // Sizes the workspace for `G` segments by a dry run of the launch sequence.
 void ensure_workspace(dmx_handle* h, int G) {
+  const int64_t launches = h->launches;  // the dry run launches nothing
   h->measuring = true;
   h->ws_off = 0;
   h->ws_peak = 0;
   forward(h, nullptr, G, nullptr);
   h->measuring = false;
+  h->launches = launches;
   const size_t need = h->ws_peak + (1 << 20);
   if (need > h->ws_cap) {
     if (h->ws) CK(cudaFree(h->ws));
@@ -1707,13 +1740,16 @@ dmx_status dmx_separate_track(dmx_handle* h, const float* left, const float* rig
   }
 }
 
-int dmx_stage_times(dmx_handle* h, const char** names, float* ms, int* counts, int cap) {
+int dmx_stage_times(dmx_handle* h, const char** names, float* ms, int* counts, double* flops,
+                    double* bytes, int cap) {
   if (!h) return 0;
   const int n = std::min<int>(cap, (int)h->stage_names.size());
   for (int i = 0; i < n; ++i) {
     names[i] = h->stage_names[i].c_str();
     ms[i] = h->stage_ms[i];
     if (counts) counts[i] = h->stage_counts[i];
+    if (flops) flops[i] = h->stage_flops[i];
+    if (bytes) bytes[i] = h->stage_bytes[i];
   }
   return n;
 }

@@ -97,7 +97,8 @@ def lib():
                                       ctypes.c_int64, ctypes.c_int64]
         L.dmx_set_trace.argtypes = [ctypes.c_void_p, TRACE_FN, ctypes.c_void_p]
         L.dmx_stage_times.argtypes = [ctypes.c_void_p, ctypes.POINTER(ctypes.c_char_p), _f32p,
-                                      ctypes.POINTER(ctypes.c_int), ctypes.c_int]
+                                      ctypes.POINTER(ctypes.c_int), ctypes.POINTER(ctypes.c_double),
+                                      ctypes.POINTER(ctypes.c_double), ctypes.c_int]
         L.dmx_kernel_launches.restype = ctypes.c_int64
         L.dmx_kernel_launches.argtypes = [ctypes.c_void_p]
         _lib = L
@@ -223,12 +224,17 @@ class Handle:
     def set_stage_timing(self, on: bool):
         _check(lib().dmx_set_stage_timing(self._h, int(bool(on))))
 
-    def stage_times(self):
-        """{kernel tag: (total ms, launches)} of the last forward with timing on."""
+    def stage_times(self, work: bool = False):
+        """{kernel tag: (total ms, launches)} of the last forward with timing on;
+        with ``work`` the tuples also carry the tag's algorithmic FLOPs and bytes."""
         names = (ctypes.c_char_p * 64)()
         ms = (ctypes.c_float * 64)()
         counts = (ctypes.c_int * 64)()
-        n = lib().dmx_stage_times(self._h, names, ms, counts, 64)
+        flops = (ctypes.c_double * 64)()
+        nbytes = (ctypes.c_double * 64)()
+        n = lib().dmx_stage_times(self._h, names, ms, counts, flops, nbytes, 64)
+        if work:
+            return {names[i].decode(): (ms[i], counts[i], flops[i], nbytes[i]) for i in range(n)}
         return {names[i].decode(): (ms[i], counts[i]) for i in range(n)}
 
     @property

@@ -170,10 +170,14 @@ dmx_status dmx_set_trace(dmx_handle* h, dmx_trace_fn fn, void* user);
 /* Per-launch device timing (cudaEvents between consecutive launches on the
  * handle's stream), off by default; it serialises nothing but adds one event
  * per launch. dmx_stage_times then reports, for the last forward, each kernel
- * tag with its summed milliseconds and launch count; returns the count of
- * tags written (at most `cap`). */
+ * tag with its summed milliseconds, launch count, algorithmic FLOPs (2 per
+ * multiply-add) and minimum HBM bytes (every operand read once, every result
+ * written once); `counts`, `flops` and `bytes` may be NULL. Returns the count
+ * of tags written (at most `cap`). No counterpart in the reference (its
+ * per-stage timing is the TraceSink, host.rs:117-125). */
 dmx_status dmx_set_stage_timing(dmx_handle* h, int on);
-int dmx_stage_times(dmx_handle* h, const char** names, float* ms, int* counts, int cap);
+int dmx_stage_times(dmx_handle* h, const char** names, float* ms, int* counts, double* flops,
+                    double* bytes, int cap);
 
 /* Number of kernels the last forward launched. */
 int64_t dmx_kernel_launches(dmx_handle* h);
