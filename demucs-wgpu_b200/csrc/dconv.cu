@@ -1,0 +1,427 @@
+// DConv residual branch, fused (host.rs:985-1059; ops.rs:930-1094 for the
+// fused GroupNorm + GLU + LayerScale tail). Per DConv layer d (dilation 2^d):
+//
+//   y = conv1(x)                  k = 3, C -> hid = C/8, padding = dilation
+//   g = GELU(GroupNorm1(y))       one group over (hid, T) per row
+//   z = conv2(g)                  1x1, hid -> 2C
+//   x += gamma * GLU(GroupNorm1(z))   one group over (2C, T) per row
+//
+// x is channels-last (rows, T, C) and is updated in place; a row is one
+// (batch, frequency) line of the spectral branch or one batch item of the
+// waveform branch.
+//
+// Rows of at most kTile positions (the spectral branch: T = 336 frames) run in
+// ONE launch, one CTA per row: conv1 over the row, the row's moments reduced
+// in the CTA, g kept in shared memory, z computed twice (moments, then the
+// output) — x crosses HBM once each way (its second read, for the residual,
+// comes from L2). Longer rows (the waveform branch) are tiled in three
+// launches: conv1 + per-tile moments (y to HBM: C/8 channels), z moments per
+// tile, then the output; each tile reduces its row's per-tile moments in a
+// fixed order, so the result does not depend on scheduling.
+//
+// Arithmetic is fp32 with f64 moment sums (the reference's GroupNorm
+// accumulates in f64, ops.rs:930-1094); every build precision uses it.
+
+#include <cstdint>
+
+#include "common.cuh"
+#include "kernels.h"
+
+namespace dmx {
+namespace {
+
+constexpr int kThreads = 384;  // a multiple of every C (48, 96, 192, 384) and of 32
+constexpr int kWarps = kThreads / 32;
+constexpr int kTile = 384;     // positions per tile
+constexpr int kCC = 16;        // conv1 input channels staged per step
+constexpr int kMaxDil = 2;
+
+template <int C>
+struct Dc {
+  static constexpr int HID = C / 8;
+  static constexpr int HIDP = (HID + 3) / 4 * 4;  // g row stride in shared memory
+  // conv1: thread (hg, pg) computes HN hidden channels of PM positions
+  static constexpr int HN = HID <= 24 ? 6 : 12;
+  static constexpr int HG = HID / HN;
+  static constexpr int PG = kThreads / HG;
+  static constexpr int PM = kTile / PG;
+  // conv2: thread (g0, c) computes channel c of every G-th position
+  static constexpr int G = kThreads / C;
+  static constexpr int XS = (kTile + 2 * kMaxDil) * (kCC + 1);
+  static constexpr int WS = 3 * kCC * HID;
+  static constexpr int YS = kTile * HIDP;
+  static_assert(HID % HN == 0 && kThreads % HG == 0 && kTile % PG == 0, "conv1 tiling");
+  static_assert(kThreads % C == 0 && C % kCC == 0, "conv2 tiling");
+};
+
+DMX_DEVICE void warp_sum2(double& s, double& q) {
+#pragma unroll
+  for (int o = 16; o; o >>= 1) {
+    s += __shfl_xor_sync(0xffffffffu, s, o);
+    q += __shfl_xor_sync(0xffffffffu, q, o);
+  }
+}
+
+// CTA-wide sum of (s, q) in a fixed order; every thread gets the result.
+DMX_DEVICE void block_sum2(double& s, double& q, double* red) {
+  warp_sum2(s, q);
+  __syncthreads();  // red may still be read by a previous reduction
+  if ((threadIdx.x & 31) == 0) {
+    red[2 * (threadIdx.x >> 5)] = s;
+    red[2 * (threadIdx.x >> 5) + 1] = q;
+  }
+  __syncthreads();
+  s = 0.0;
+  q = 0.0;
+#pragma unroll
+  for (int w = 0; w < kWarps; ++w) {
+    s += red[2 * w];
+    q += red[2 * w + 1];
+  }
+}
+
+// Sum of a row's per-tile moments (fixed order) -> GroupNorm mean, 1/std.
+DMX_DEVICE void row_moments(const double* part, int tiles, double count, float& mean, float& inv,
+                            double* red) {
+  if (threadIdx.x < 32) {
+    double s = 0.0, q = 0.0;
+    for (int i = threadIdx.x; i < tiles; i += 32) {
+      s += part[2 * i];
+      q += part[2 * i + 1];
+    }
+    warp_sum2(s, q);
+    if (threadIdx.x == 0) {
+      red[0] = s;
+      red[1] = q;
+    }
+  }
+  __syncthreads();
+  const double m = red[0] / count;
+  const double var = fmax(red[1] / count - m * m, 0.0);
+  mean = (float)m;
+  inv = 1.0f / (float)sqrt(var + 1e-5);
+}
+
+DMX_DEVICE void moments_to_norm(double s, double q, double count, float& mean, float& inv) {
+  const double m = s / count;
+  const double var = fmax(q / count - m * m, 0.0);
+  mean = (float)m;
+  inv = 1.0f / (float)sqrt(var + 1e-5);
+}
+
+// conv1 of positions [t0, t0 + kTile) of one row (positions >= T read zeros
+// and are discarded by the caller). acc[i][j]: hidden channel hg*HN + j of
+// position pg + i*PG, bias included.
+template <int C>
+DMX_DEVICE void conv1_tile(const float* __restrict__ xr, int T, int t0, int dil,
+                           const DConvArgs& a, float* xs, float* ws,
+                           float2 (&acc)[Dc<C>::PM][Dc<C>::HN / 2]) {
+  using S = Dc<C>;
+  const int tid = threadIdx.x, hg = tid / S::PG, pg = tid % S::PG;
+#pragma unroll
+  for (int j = 0; j < S::HN / 2; ++j) {
+    const float2 b = make_float2(a.b1[hg * S::HN + 2 * j], a.b1[hg * S::HN + 2 * j + 1]);
+#pragma unroll
+    for (int i = 0; i < S::PM; ++i) acc[i][j] = b;
+  }
+  const int xrows = kTile + 2 * dil;
+  for (int c0 = 0; c0 < C; c0 += kCC) {
+    __syncthreads();  // the previous chunk is consumed
+    for (int i = tid; i < xrows * kCC; i += kThreads) {
+      const int r = i / kCC, cc = i - r * kCC;
+      const int t = t0 - dil + r;
+      xs[r * (kCC + 1) + cc] = (t >= 0 && t < T) ? xr[(int64_t)t * C + c0 + cc] : 0.f;
+    }
+    for (int i = tid; i < S::WS; i += kThreads) {
+      const int h = i % S::HID, kc = i / S::HID;
+      const int k = kc / kCC, cc = kc - k * kCC;
+      ws[i] = a.w1[(int64_t)(k * C + c0 + cc) * a.w1_ld + h];
+    }
+    __syncthreads();
+#pragma unroll
+    for (int k = 0; k < 3; ++k) {
+      const float* xk = xs + (pg + k * dil) * (kCC + 1);
+#pragma unroll 4
+      for (int cc = 0; cc < kCC; ++cc) {
+        float xv[S::PM];
+#pragma unroll
+        for (int i = 0; i < S::PM; ++i) xv[i] = xk[i * S::PG * (kCC + 1) + cc];
+        const float2* wr = reinterpret_cast<const float2*>(ws + (k * kCC + cc) * S::HID + hg * S::HN);
+        float2 wv[S::HN / 2];
+#pragma unroll
+        for (int j = 0; j < S::HN / 2; ++j) wv[j] = wr[j];
+#pragma unroll
+        for (int i = 0; i < S::PM; ++i) {
+          const float2 xx = make_float2(xv[i], xv[i]);
+#pragma unroll
+          for (int j = 0; j < S::HN / 2; ++j) acc[i][j] = __ffma2_rn(xx, wv[j], acc[i][j]);
+        }
+      }
+    }
+  }
+}
+
+// f64 moments of the valid conv1 outputs of this thread.
+template <int C>
+DMX_DEVICE void conv1_moments(const float2 (&acc)[Dc<C>::PM][Dc<C>::HN / 2], int np, double& s,
+                              double& q) {
+  using S = Dc<C>;
+  const int pg = threadIdx.x % S::PG;
+  s = 0.0;
+  q = 0.0;
+#pragma unroll
+  for (int i = 0; i < S::PM; ++i) {
+    if (pg + i * S::PG < np) {
+#pragma unroll
+      for (int j = 0; j < S::HN / 2; ++j) {
+        const double v0 = acc[i][j].x, v1 = acc[i][j].y;
+        s += v0 + v1;
+        q += v0 * v0 + v1 * v1;
+      }
+    }
+  }
+}
+
+// g = GELU(GroupNorm1(y)) of this thread's conv1 outputs into gs (kTile x HIDP).
+template <int C>
+DMX_DEVICE void store_g(const float2 (&acc)[Dc<C>::PM][Dc<C>::HN / 2], const DConvArgs& a,
+                        float mean, float inv, float* gs) {
+  using S = Dc<C>;
+  const int tid = threadIdx.x, hg = tid / S::PG, pg = tid % S::PG;
+#pragma unroll
+  for (int j = 0; j < S::HN; ++j) {
+    const int h = hg * S::HN + j;
+    const float scale = inv * a.n1w[h];
+    const float shift = a.n1b[h] - mean * scale;
+#pragma unroll
+    for (int i = 0; i < S::PM; ++i) {
+      const float y = (j & 1) ? acc[i][j / 2].y : acc[i][j / 2].x;
+      gs[(pg + i * S::PG) * S::HIDP + h] = gelu(y * scale + shift);
+    }
+  }
+  if (S::HIDP > S::HID)
+    for (int p = tid; p < kTile; p += kThreads)
+#pragma unroll
+      for (int h = S::HID; h < S::HIDP; ++h) gs[p * S::HIDP + h] = 0.f;
+}
+
+// conv2 over the g rows of a tile. OUT = false: this thread's f64 moments of
+// z (value and gate channels); OUT = true: x[p][c] += gamma * GLU(GN2(z)).
+template <int C, bool OUT>
+DMX_DEVICE void conv2_tile(const float* gs, int np, const DConvArgs& a, float* xt, float mean2,
+                           float inv2, double& s, double& q) {
+  using S = Dc<C>;
+  const int c = threadIdx.x % C, g0 = threadIdx.x / C;
+  float2 w[S::HID];  // (value, gate) weights of channel c
+#pragma unroll
+  for (int h = 0; h < S::HID; ++h)
+    w[h] = *reinterpret_cast<const float2*>(a.w2 + (int64_t)h * a.w2_ld + 2 * c);
+  const float2 bias = *reinterpret_cast<const float2*>(a.b2 + 2 * c);
+  float vs = 0.f, vsh = 0.f, gsc = 0.f, gsh = 0.f, gamma = 0.f;
+  if (OUT) {
+    vs = inv2 * a.n2w[c];
+    vsh = a.n2b[c] - mean2 * vs;
+    gsc = inv2 * a.n2w[c + C];
+    gsh = a.n2b[c + C] - mean2 * gsc;
+    gamma = a.gamma[c];
+  }
+  float fs = 0.f, fq = 0.f;
+  int run = 0;
+  s = 0.0;
+  q = 0.0;
+  for (int p = g0; p < np; p += S::G) {
+    const float* gp = gs + p * S::HIDP;
+    float2 z = bias;
+#pragma unroll
+    for (int h = 0; h < S::HIDP; h += 4) {
+      const float4 g4 = *reinterpret_cast<const float4*>(gp + h);
+      z = __ffma2_rn(w[h], make_float2(g4.x, g4.x), z);
+      if (h + 1 < S::HID) z = __ffma2_rn(w[h + 1], make_float2(g4.y, g4.y), z);
+      if (h + 2 < S::HID) z = __ffma2_rn(w[h + 2], make_float2(g4.z, g4.z), z);
+      if (h + 3 < S::HID) z = __ffma2_rn(w[h + 3], make_float2(g4.w, g4.w), z);
+    }
+    const float v = z.x, gt = z.y;
+    if (OUT) {
+      const float value = v * vs + vsh;
+      const float gate = gt * gsc + gsh;
+      float* o = xt + (int64_t)p * C + c;
+      *o = *o + gamma * (value * sigmoid(gate));
+    } else {
+      // short f32 runs (8 positions, 16 terms) folded into f64
+      fs += v + gt;
+      fq += fmaf(v, v, gt * gt);
+      if (++run == 8) {
+        s += (double)fs;
+        q += (double)fq;
+        fs = fq = 0.f;
+        run = 0;
+      }
+    }
+  }
+  if (!OUT) {
+    s += (double)fs;
+    q += (double)fq;
+  }
+}
+
+template <int C>
+struct Smem {
+  using S = Dc<C>;
+  static constexpr size_t kRow = sizeof(float) * (S::XS + S::WS + S::YS);
+  static constexpr size_t kConv1 = sizeof(float) * (S::XS + S::WS);
+  static constexpr size_t kConv2 = sizeof(float) * S::YS;
+};
+
+// One CTA per row of T <= kTile positions: the whole DConv layer.
+template <int C>
+__global__ void __launch_bounds__(kThreads, C >= 384 ? 1 : 2) dconv_row_kernel(const DConvArgs a) {
+  using S = Dc<C>;
+  extern __shared__ __align__(16) float smem[];
+  float* xs = smem;
+  float* ws = xs + S::XS;
+  float* gs = ws + S::WS;
+  __shared__ double red[2 * kWarps];
+  const int row = blockIdx.x, T = a.T;
+  float* xr = a.x + (int64_t)row * T * C;
+
+  float2 acc[S::PM][S::HN / 2];
+  conv1_tile<C>(xr, T, 0, a.dil, a, xs, ws, acc);
+  double s, q;
+  conv1_moments<C>(acc, T, s, q);
+  block_sum2(s, q, red);
+  float mean, inv;
+  moments_to_norm(s, q, (double)S::HID * T, mean, inv);
+  store_g<C>(acc, a, mean, inv, gs);
+  __syncthreads();
+
+  conv2_tile<C, false>(gs, T, a, xr, 0.f, 0.f, s, q);
+  block_sum2(s, q, red);
+  float mean2, inv2;
+  moments_to_norm(s, q, 2.0 * C * T, mean2, inv2);
+  conv2_tile<C, true>(gs, T, a, xr, mean2, inv2, s, q);
+}
+
+// Tiled, step 1: conv1 of one tile -> y (HBM, compact HID channels) and the
+// tile's moments.
+template <int C>
+__global__ void __launch_bounds__(kThreads, C >= 384 ? 1 : 2) dconv_conv1_kernel(const DConvArgs a) {
+  using S = Dc<C>;
+  extern __shared__ __align__(16) float smem[];
+  float* xs = smem;
+  float* ws = xs + S::XS;
+  __shared__ double red[2 * kWarps];
+  const int tile = blockIdx.x, row = blockIdx.y, T = a.T;
+  const int t0 = tile * kTile, np = min(kTile, T - t0);
+  const float* xr = a.x + (int64_t)row * T * C;
+
+  float2 acc[S::PM][S::HN / 2];
+  conv1_tile<C>(xr, T, t0, a.dil, a, xs, ws, acc);
+  double s, q;
+  conv1_moments<C>(acc, np, s, q);
+  block_sum2(s, q, red);
+  if (threadIdx.x == 0) {
+    double* part = a.part1 + 2 * ((int64_t)row * a.tiles + tile);
+    part[0] = s;
+    part[1] = q;
+  }
+  const int hg = threadIdx.x / S::PG, pg = threadIdx.x % S::PG;
+  float* yr = a.y + ((int64_t)row * T + t0) * S::HID;
+#pragma unroll
+  for (int i = 0; i < S::PM; ++i) {
+    const int p = pg + i * S::PG;
+    if (p < np)
+#pragma unroll
+      for (int j = 0; j < S::HN / 2; ++j)
+        *reinterpret_cast<float2*>(yr + (int64_t)p * S::HID + hg * S::HN + 2 * j) = acc[i][j];
+  }
+}
+
+// Tiled, steps 2 (OUT = false: z moments per tile) and 3 (OUT = true: the
+// residual update).
+template <int C, bool OUT>
+__global__ void __launch_bounds__(kThreads, C >= 384 ? 1 : 2) dconv_conv2_kernel(const DConvArgs a) {
+  using S = Dc<C>;
+  extern __shared__ __align__(16) float smem[];
+  float* gs = smem;
+  __shared__ double red[2 * kWarps];
+  const int tile = blockIdx.x, row = blockIdx.y, T = a.T;
+  const int t0 = tile * kTile, np = min(kTile, T - t0);
+
+  float mean, inv;
+  row_moments(a.part1 + 2 * (int64_t)row * a.tiles, a.tiles, (double)S::HID * T, mean, inv, red);
+  const float* yr = a.y + ((int64_t)row * T + t0) * S::HID;
+  for (int i = threadIdx.x; i < kTile * S::HIDP; i += kThreads) {
+    const int p = i / S::HIDP, h = i - p * S::HIDP;
+    float g = 0.f;
+    if (p < np && h < S::HID) {
+      const float scale = inv * a.n1w[h];
+      const float shift = a.n1b[h] - mean * scale;
+      g = gelu(yr[(int64_t)p * S::HID + h] * scale + shift);
+    }
+    gs[i] = g;
+  }
+  float mean2 = 0.f, inv2 = 0.f;
+  if (OUT) {
+    __syncthreads();  // red reused
+    row_moments(a.part2 + 2 * (int64_t)row * a.tiles, a.tiles, 2.0 * C * T, mean2, inv2, red + 2);
+  }
+  __syncthreads();
+  double s, q;
+  float* xt = a.x + ((int64_t)row * T + t0) * C;
+  conv2_tile<C, OUT>(gs, np, a, xt, mean2, inv2, s, q);
+  if (!OUT) {
+    block_sum2(s, q, red);
+    if (threadIdx.x == 0) {
+      double* part = a.part2 + 2 * ((int64_t)row * a.tiles + tile);
+      part[0] = s;
+      part[1] = q;
+    }
+  }
+}
+
+template <class K>
+void set_smem(K kernel, size_t bytes) {
+  if (bytes > 48 * 1024)
+    cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
+}
+
+template <int C>
+void launch_c(const DConvArgs& a, cudaStream_t s) {
+  using M = Smem<C>;
+  static bool configured = false;
+  if (!configured) {
+    set_smem(dconv_row_kernel<C>, M::kRow);
+    set_smem(dconv_conv1_kernel<C>, M::kConv1);
+    set_smem(dconv_conv2_kernel<C, false>, M::kConv2);
+    set_smem(dconv_conv2_kernel<C, true>, M::kConv2);
+    configured = true;
+  }
+  if (a.T <= kTile) {
+    dconv_row_kernel<C><<<a.rows, kThreads, M::kRow, s>>>(a);
+    return;
+  }
+  const dim3 grid(a.tiles, a.rows);
+  dconv_conv1_kernel<C><<<grid, kThreads, M::kConv1, s>>>(a);
+  dconv_conv2_kernel<C, false><<<grid, kThreads, M::kConv2, s>>>(a);
+  dconv_conv2_kernel<C, true><<<grid, kThreads, M::kConv2, s>>>(a);
+}
+
+}  // namespace
+
+int dconv_tiles(int T) { return (T + kTile - 1) / kTile; }
+
+bool dconv_row_fused(int T) { return T <= kTile; }
+
+bool launch_dconv(const DConvArgs& a, cudaStream_t s) {
+  if (a.dil < 1 || a.dil > kMaxDil || a.rows <= 0 || a.T <= 0) return false;
+  if (a.T > kTile && (!a.y || !a.part1 || !a.part2 || a.tiles != dconv_tiles(a.T))) return false;
+  switch (a.C) {
+    case 48: launch_c<48>(a, s); return true;
+    case 96: launch_c<96>(a, s); return true;
+    case 192: launch_c<192>(a, s); return true;
+    case 384: launch_c<384>(a, s); return true;
+    default: return false;
+  }
+}
+
+}  // namespace dmx

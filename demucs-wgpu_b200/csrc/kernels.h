@@ -19,6 +19,33 @@ void launch_istft(const float* spec, const float4* norm, const float* window, co
                   float* frames, const float* envelope, const float* time_branch,
                   const float4* norm_t, float* out, int B, cudaStream_t s);
 
+// dconv.cu — one DConv layer on x (rows, T, C) channels-last, in place.
+// Weights as packed for the GEMM path: w1[(k*C + c)*w1_ld + h] (k = tap),
+// w2[h*w2_ld + 2c] value / [h*w2_ld + 2c + 1] gate, b2 likewise interleaved;
+// n2w/n2b in the reference's order (value c, gate c + C). Rows longer than
+// one tile need y (rows*T*C/8 floats) and part1/part2 (rows*tiles*2 doubles).
+struct DConvArgs {
+  float* x;
+  int C, rows, T, dil, tiles;
+  const float* w1;
+  int w1_ld;
+  const float* b1;
+  const float* n1w;
+  const float* n1b;
+  const float* w2;
+  int w2_ld;
+  const float* b2;
+  const float* n2w;
+  const float* n2b;
+  const float* gamma;
+  float* y;
+  double* part1;
+  double* part2;
+};
+int dconv_tiles(int T);
+bool dconv_row_fused(int T);
+bool launch_dconv(const DConvArgs& a, cudaStream_t s);
+
 // transformer.cu
 void launch_gn_gelu_pad(const float* y, int64_t positions, int T, int hid, int hp,
                         const double* stats, const float* w, const float* b, float* out,

@@ -639,50 +639,49 @@ void set_output(ConvParams& p, float* out, int B, int Hq, int Wq, int Cout) {
 }
 
 // DConv residual branch in place on x (rows, T, C) channels-last
-// (host.rs:985-1059). Per layer: conv1 (k3, dilation 2^d) with its row
-// moments; GroupNorm + GELU materialised once into a zero-padded hidden
-// tensor; then the 1x1 GEMM twice — once for the moments of its output, once
-// for GroupNorm + GLU + LayerScale + residual straight into x.
+// (host.rs:985-1059): per layer one fused launch for rows of at most one tile
+// (the spectral branch), three tiled launches for longer rows (the waveform
+// branch); the kernels are in dconv.cu.
 void run_dconv(dmx_handle* h, const DConvFull& dc, float* x, int rows, int T) {
-  const int C = dc.C, hid = dc.hidden, hp = (hid + 15) / 16 * 16;
+  const int C = dc.C, hid = dc.hidden;
   const int64_t positions = (int64_t)rows * T;
-  float* y = h->falloc((size_t)positions * hid);
-  float* yp = h->falloc((size_t)positions * hp);
-  double* st = h->dalloc((size_t)rows * 4);
+  const bool fused = dconv_row_fused(T);
+  const int tiles = dconv_tiles(T);
+  float* y = fused ? nullptr : h->falloc((size_t)positions * hid);
+  double* part = fused ? nullptr : h->dalloc((size_t)rows * tiles * 4);
   for (int d = 0; d < 2; ++d) {
     const DConvLayerW& L = dc.layer[d];
-    h->zero(st, (size_t)rows * 4 * sizeof(double));
-    double* st1 = st;
-    double* st2 = st + 2 * rows;
-    {
-      ConvParams p = base_params(L.conv1, h->wdev);
-      set_input(p, x, rows, 1, T, C);
-      set_output(p, y, rows, 1, T, hid);
-      p.epi_stats = st1;
-      p.epi_rowlen = T;
-      h->gemm(p, PRO_NONE, EPI_STORE_STATS, "dconv.conv1", &L.conv1);
+    DConvArgs a;
+    std::memset(&a, 0, sizeof(a));
+    a.x = x;
+    a.C = C;
+    a.rows = rows;
+    a.T = T;
+    a.dil = 1 << d;
+    a.tiles = tiles;
+    a.w1 = h->W(L.conv1.w_off);
+    a.w1_ld = L.conv1.Npad;
+    a.b1 = h->W(L.conv1.b_off);
+    a.n1w = h->W(L.n1w.off);
+    a.n1b = h->W(L.n1b.off);
+    a.w2 = h->W(L.conv2.w_off);
+    a.w2_ld = L.conv2.Npad;
+    a.b2 = h->W(L.conv2.b_off);
+    a.n2w = h->W(L.n2w.off);
+    a.n2b = h->W(L.n2b.off);
+    a.gamma = h->W(L.gamma.off);
+    a.y = y;
+    a.part1 = part;
+    a.part2 = part ? part + 2 * (size_t)rows * tiles : nullptr;
+    // algorithmic work: conv1 (3C -> hid) + conv2 (hid -> 2C) per position;
+    // x read once and written once
+    h->mark(std::string(fused ? "dconv.row" : "dconv.tiled") + std::to_string(C),
+            10.0 * positions * C * hid, 8.0 * positions * C);
+    if (h->live()) {
+      if (!launch_dconv(a, h->stream)) throw Error(DMX_ERR_INVALID, "dconv: unsupported shape");
+      h->after("dconv");
     }
-    h->mark("dconv.gngelu", 0.0, 4.0 * positions * (hid + hp));
-    if (h->live())
-      launch_gn_gelu_pad(y, positions, T, hid, hp, st1, h->W(L.n1w.off), h->W(L.n1b.off), yp,
-                         h->stream);
-    ++h->launches;
-    ConvParams p = base_params(L.conv2, h->wdev);
-    set_input(p, yp, rows, 1, T, hp);
-    set_output(p, x, rows, 1, T, C);
-    p.epi_stats = st2;
-    p.epi_rowlen = T;
-    h->gemm(p, PRO_NONE, EPI_STATS, "dconv.stats", &L.conv2);
-    p.epi_stats = nullptr;
-    p.epi_nstats = st2;
-    p.epi_count = 2.0 * C * T;
-    p.epi_rowlen = T;
-    p.epi_gw = h->W(L.n2w.off);
-    p.epi_gb = h->W(L.n2b.off);
-    p.epi_half = C;
-    p.epi_gamma = h->W(L.gamma.off);
-    p.epi_res = x;
-    h->gemm(p, PRO_NONE, EPI_DCONV_TAIL, "dconv.tail", &L.conv2);
+    h->launches += fused ? 1 : 3;
   }
 }
 

@@ -164,8 +164,13 @@ __global__ void __launch_bounds__(192, 1)
           float4* a = reinterpret_cast<float4*>(smem + s * S::STAGE_BYTES + row * BK * 4);
           float4* alo = reinterpret_cast<float4*>(smem + s * S::STAGE_BYTES + S::A_BYTES +
                                                   S::B_BYTES + row * BK * 4);
+          // visit the row's 16-byte chunks in the order the TMA swizzle
+          // permutes them (chunk ^ (128-byte line % 8)), so the 8 lanes of a
+          // quarter-warp touch 8 different bank groups
+          const int swz = BK == 32 ? (row & 7) : ((row >> 1) & 3);
 #pragma unroll
-          for (int q = 0; q < BK / 4; ++q) {
+          for (int qq = 0; qq < BK / 4; ++qq) {
+            const int q = qq ^ swz;
             const float4 x = a[q];
             float4 hi;
             hi.x = round_tf32(x.x);
