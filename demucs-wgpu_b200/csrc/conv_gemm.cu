@@ -16,8 +16,7 @@ struct RowAcc {
 };
 
 template <int PRO>
-DMX_DEVICE float load_a(const ConvParams& p, int64_t boff, int y, int x, int b, int prow, int k,
-                        const RowNorm* rn) {
+DMX_DEVICE float load_a(const ConvParams& p, int64_t boff, int y, int x, int b, int k) {
   if (k >= p.K) return 0.f;
   const int tap = k / p.Cin;
   const int ci = k - tap * p.Cin;
@@ -31,11 +30,6 @@ DMX_DEVICE float load_a(const ConvParams& p, int64_t boff, int y, int x, int b, 
     const float4 nz = reinterpret_cast<const float4*>(p.pro_scale)[b];
     v = (v - nz.x) * nz.y;
   }
-  if (PRO == PRO_GN_GELU) {
-    const float scale = rn->inv * p.pro_scale[ci];
-    const float shift = p.pro_shift[ci] - rn->mean * scale;
-    v = gelu(v * scale + shift);
-  }
   return v;
 }
 
@@ -44,7 +38,7 @@ __global__ void __launch_bounds__(256) conv_gemm_kernel(const ConvParams p) {
   __shared__ __align__(16) float As[2][BK][AS];
   __shared__ __align__(16) float Bs[2][BK][BN];
   __shared__ int64_t s_boff[BM];
-  __shared__ int s_y[BM], s_x[BM], s_b[BM], s_row[BM];
+  __shared__ int s_y[BM], s_x[BM], s_b[BM];
   __shared__ double s_stats[4];
 
   const int tid = threadIdx.x;
@@ -63,12 +57,10 @@ __global__ void __launch_bounds__(256) conv_gemm_kernel(const ConvParams p) {
       s_y[tid] = (int)(rem / p.Wq);
       s_x[tid] = (int)(rem % p.Wq);
       s_boff[tid] = (int64_t)b * p.i_bs;
-      s_row[tid] = PRO == PRO_GN_GELU ? (int)(pos / p.pro_rowlen) : 0;
     } else {
       s_b[tid] = -1;
       s_y[tid] = s_x[tid] = 0;
       s_boff[tid] = 0;
-      s_row[tid] = 0;
     }
   }
   if (tid < 4) s_stats[tid] = 0.0;
@@ -78,23 +70,13 @@ __global__ void __launch_bounds__(256) conv_gemm_kernel(const ConvParams p) {
   const int lk = tid % 16, lm = tid / 16;
   const int lbk = tid / 16, lbn = (tid % 16) * 4;
 
-  RowNorm rn[TM];
-  if (PRO == PRO_GN_GELU) {
-#pragma unroll
-    for (int i = 0; i < TM; ++i) {
-      const int r = lm + 16 * i;
-      rn[i] = s_b[r] >= 0 ? row_norm(p.pro_stats, s_row[r], p.pro_count) : RowNorm{0.f, 0.f};
-    }
-  }
-
   float ra[TM];
   float4 rb;
   auto load_tiles = [&](int k0) {
 #pragma unroll
     for (int i = 0; i < TM; ++i) {
       const int r = lm + 16 * i;
-      ra[i] = s_b[r] >= 0 ? load_a<PRO>(p, s_boff[r], s_y[r], s_x[r], s_b[r], s_row[r], k0 + lk, &rn[i])
-                          : 0.f;
+      ra[i] = s_b[r] >= 0 ? load_a<PRO>(p, s_boff[r], s_y[r], s_x[r], s_b[r], k0 + lk) : 0.f;
     }
     rb = *reinterpret_cast<const float4*>(p.w + (int64_t)(k0 + lbk) * p.Npad + n0 + lbn);
   };
@@ -139,7 +121,7 @@ __global__ void __launch_bounds__(256) conv_gemm_kernel(const ConvParams p) {
 #pragma unroll
   for (int j = 0; j < TN; ++j) bias[j] = p.bias[nb + j];
 
-  constexpr bool kStats = EPI == EPI_STATS || EPI == EPI_STORE_STATS || EPI == EPI_RESIDUAL;
+  constexpr bool kStats = EPI == EPI_RESIDUAL;
   double ls[2] = {0.0, 0.0}, lq[2] = {0.0, 0.0};
   const int rowlen = kStats ? p.epi_rowlen : 1;
   const int64_t r0 = kStats ? m0 / rowlen : 0;
@@ -156,7 +138,7 @@ __global__ void __launch_bounds__(256) conv_gemm_kernel(const ConvParams p) {
     float v[TN];
 #pragma unroll
     for (int j = 0; j < TN; ++j) v[j] = acc[i][j] + bias[j];
-    if (EPI == EPI_STORE || EPI == EPI_GELU || EPI == EPI_STORE_STATS) {
+    if (EPI == EPI_STORE || EPI == EPI_GELU) {
       if (EPI == EPI_GELU) {
 #pragma unroll
         for (int j = 0; j < TN; ++j) v[j] = gelu(v[j]);
@@ -200,24 +182,6 @@ __global__ void __launch_bounds__(256) conv_gemm_kernel(const ConvParams p) {
           float g = v[j] * sigmoid(v[j + 1]);
           if (EPI == EPI_GLU_EMB) g += p.epi_emb[(int64_t)s_y[m] * (p.N / 2) + c];
           p.out[orow + c] = g;
-        }
-      }
-    }
-    if (EPI == EPI_DCONV_TAIL) {
-      const RowNorm nr = row_norm(p.epi_nstats, (int)(pos / p.epi_rowlen), p.epi_count);
-#pragma unroll
-      for (int j = 0; j < TN; j += 2) {
-        const int n = nb + j;
-        if (n < p.N) {
-          const int c = n / 2;
-          const float vs = nr.inv * p.epi_gw[c];
-          const float vsh = p.epi_gb[c] - nr.mean * vs;
-          const float gs = nr.inv * p.epi_gw[c + p.epi_half];
-          const float gsh = p.epi_gb[c + p.epi_half] - nr.mean * gs;
-          const float value = v[j] * vs + vsh;
-          const float gate = v[j + 1] * gs + gsh;
-          const int64_t o = orow + c;
-          p.out[o] = p.epi_res[o] + p.epi_gamma[c] * (value * sigmoid(gate));
         }
       }
     }
@@ -274,9 +238,6 @@ void dispatch_epi(const ConvParams& p, int epi, dim3 grid, cudaStream_t s) {
     case EPI_GELU: conv_gemm_kernel<PRO, EPI_GELU><<<grid, 256, 0, s>>>(p); break;
     case EPI_GLU: conv_gemm_kernel<PRO, EPI_GLU><<<grid, 256, 0, s>>>(p); break;
     case EPI_GLU_EMB: conv_gemm_kernel<PRO, EPI_GLU_EMB><<<grid, 256, 0, s>>>(p); break;
-    case EPI_STATS: conv_gemm_kernel<PRO, EPI_STATS><<<grid, 256, 0, s>>>(p); break;
-    case EPI_STORE_STATS: conv_gemm_kernel<PRO, EPI_STORE_STATS><<<grid, 256, 0, s>>>(p); break;
-    case EPI_DCONV_TAIL: conv_gemm_kernel<PRO, EPI_DCONV_TAIL><<<grid, 256, 0, s>>>(p); break;
     case EPI_RESIDUAL: conv_gemm_kernel<PRO, EPI_RESIDUAL><<<grid, 256, 0, s>>>(p); break;
   }
 }
@@ -290,7 +251,6 @@ void launch_conv_gemm(const ConvParams& p, int pro, int epi, cudaStream_t s) {
     case PRO_NONE: dispatch_epi<PRO_NONE>(p, epi, grid, s); break;
     case PRO_BATCH_AFFINE: dispatch_epi<PRO_BATCH_AFFINE>(p, epi, grid, s); break;
     case PRO_ADD: dispatch_epi<PRO_ADD>(p, epi, grid, s); break;
-    case PRO_GN_GELU: dispatch_epi<PRO_GN_GELU>(p, epi, grid, s); break;
   }
 }
 

@@ -19,8 +19,7 @@ constexpr int kMaxTaps = 16;
 enum ProMode : int {
   PRO_NONE = 0,
   PRO_BATCH_AFFINE = 1,  // (v - shift[b]) * scale[b]   (input normalisation)
-  PRO_ADD = 2,           // v + x2                      (decoder skip connection)
-  PRO_GN_GELU = 3        // gelu(v*inv*g[c] + (b[c] - mean*inv*g[c]))  (DConv norm1)
+  PRO_ADD = 2            // v + x2                      (decoder skip connection)
 };
 
 enum EpiMode : int {
@@ -28,10 +27,7 @@ enum EpiMode : int {
   EPI_GELU = 1,           // gelu(acc + bias)
   EPI_GLU = 2,            // value * sigmoid(gate), columns interleaved (2c, 2c+1)
   EPI_GLU_EMB = 3,        // GLU + emb[y, c]
-  EPI_STATS = 4,          // row moments of acc + bias, nothing stored
-  EPI_STORE_STATS = 5,    // store acc + bias and accumulate row moments
-  EPI_DCONV_TAIL = 6,     // out[c] = res[c] + gamma[c] * GLU(GN(acc + bias))
-  EPI_RESIDUAL = 7        // out = res + gamma[n] * (acc + bias) [+ row moments]
+  EPI_RESIDUAL = 4        // out = res + gamma[n] * (acc + bias) [+ row moments]
 };
 
 struct ConvParams {
@@ -55,19 +51,10 @@ struct ConvParams {
   float* out;
   int64_t o_bs, o_ys, o_xs, o_off;
   // prologue
-  const float* pro_scale;  // PRO_BATCH_AFFINE: float4 {mean, scale, ..} per segment; GN: gain
-  const float* pro_shift;  // GN: bias
-  const double* pro_stats;
-  int pro_rowlen;
-  double pro_count;
+  const float* pro_scale;  // PRO_BATCH_AFFINE: float4 {mean, scale, ..} per segment
   // epilogue
-  double* epi_stats;
+  double* epi_stats;  // EPI_RESIDUAL: per-row (sum, sum of squares) of the output
   int epi_rowlen;
-  const double* epi_nstats;
-  double epi_count;
-  const float* epi_gw;
-  const float* epi_gb;
-  int epi_half;  // C for the GLU-with-norm tail (gate channel = c + C)
   const float* epi_gamma;
   const float* epi_res;
   const float* epi_emb;

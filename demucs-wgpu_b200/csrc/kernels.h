@@ -47,9 +47,6 @@ bool dconv_row_fused(int T);
 bool launch_dconv(const DConvArgs& a, cudaStream_t s);
 
 // transformer.cu
-void launch_gn_gelu_pad(const float* y, int64_t positions, int T, int hid, int hp,
-                        const double* stats, const float* w, const float* b, float* out,
-                        cudaStream_t s);
 void launch_layer_norm(const float* x, int64_t rows, int ntok, const float* w, const float* b,
                        const float* pos, float* out, cudaStream_t s);
 void launch_group_norm_apply(float* x, int B, int64_t ntok, const double* stats, const float* w,

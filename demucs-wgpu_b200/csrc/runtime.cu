@@ -489,19 +489,19 @@ struct dmx_handle {
             const Packed* pk = nullptr) {
     ++launches;
     if (!live()) return;
-    if ((epi == EPI_STATS || epi == EPI_STORE_STATS || epi == EPI_RESIDUAL) && p.epi_stats &&
+    if (epi == EPI_RESIDUAL && p.epi_stats &&
         p.epi_rowlen < 128)
       throw Error(DMX_ERR_INVALID, "row statistics need rows of at least 128 positions");
     if (stage_timing) {
       const double M = (double)p.B * p.Hq * p.Wq;
       const int cin = pk ? pk->cin_real : p.Cin;
       const double K = (double)p.ntaps * cin;
-      const bool glu = epi == EPI_GLU || epi == EPI_GLU_EMB || epi == EPI_DCONV_TAIL;
+      const bool glu = epi == EPI_GLU || epi == EPI_GLU_EMB;
       const double nout = glu ? p.N / 2 : p.N;
       double bytes = 4.0 * ((double)p.B * p.Hin * p.Win * cin + K * p.N);
       if (pro == PRO_ADD) bytes += 4.0 * p.B * p.Hin * p.Win * cin;
-      if (epi != EPI_STATS) bytes += 4.0 * M * nout;
-      if (epi == EPI_RESIDUAL || epi == EPI_DCONV_TAIL) bytes += 4.0 * M * nout;
+      bytes += 4.0 * M * nout;
+      if (epi == EPI_RESIDUAL) bytes += 4.0 * M * nout;
       mark(tag, 2.0 * M * K * p.N, bytes);
     }
     if (pk && (cfg.precision == DMX_TF32 || cfg.precision == DMX_TF32X3) &&
@@ -513,7 +513,10 @@ struct dmx_handle {
   // The tensor-core path takes a launch when its A operand is a plain
   // channels-last tile read (no prologue transform) with stride-1 taps.
   bool try_tc(const ConvParams& p, int pro, int epi, const Packed& pk) {
-    if (pro != PRO_NONE || !pk.has_tc || p.i_cs != 1 || p.sy != 1 || p.sx != 1) return false;
+    if (pro != PRO_NONE || !pk.has_tc || p.i_cs != 1) return false;
+    if (epi != EPI_STORE && epi != EPI_GELU && epi != EPI_GLU && epi != EPI_GLU_EMB &&
+        epi != EPI_RESIDUAL)
+      return false;
     TcParams t;
     std::memset(&t, 0, sizeof(t));
     TcOperandA a;
@@ -551,6 +554,8 @@ struct dmx_handle {
     t.Hq = p.Hq;
     t.Wq = p.Wq;
     t.Cin = p.Cin;
+    t.sy = p.sy;
+    t.sx = p.sx;
     t.ntaps = p.ntaps;
     for (int i = 0; i < p.ntaps; ++i) {
       t.dy[i] = p.dy[i];
@@ -568,11 +573,6 @@ struct dmx_handle {
     t.o_off = p.o_off;
     t.epi_stats = p.epi_stats;
     t.epi_rowlen = p.epi_rowlen;
-    t.epi_nstats = p.epi_nstats;
-    t.epi_count = p.epi_count;
-    t.epi_gw = p.epi_gw;
-    t.epi_gb = p.epi_gb;
-    t.epi_half = p.epi_half;
     t.epi_gamma = p.epi_gamma;
     t.epi_res = p.epi_res;
     t.epi_emb = p.epi_emb;
@@ -873,13 +873,13 @@ void forward(dmx_handle* h, const float* mix, int G, float* out) {
       }
       p.sx = 4;
       set_output(p, y, G, 1, To, Co);
-      h->gemm(p, i == 0 ? PRO_BATCH_AFFINE : PRO_NONE, EPI_GELU, "tenc.conv", &E.conv);
+      h->gemm(p, i == 0 ? PRO_BATCH_AFFINE : PRO_NONE, EPI_GELU, ("tenc.conv" + std::to_string(i)).c_str(), &E.conv);
       run_dconv(h, h->tenc_dc[i], y, G, To);
       float* z = h->falloc((size_t)G * To * Co);
       ConvParams r = base_params(E.rewrite, h->wdev);
       set_input(r, y, G, 1, To, Co);
       set_output(r, z, G, 1, To, Co);
-      h->gemm(r, PRO_NONE, EPI_GLU, "tenc.rewrite", &E.rewrite);
+      h->gemm(r, PRO_NONE, EPI_GLU, ("tenc.rewrite" + std::to_string(i)).c_str(), &E.rewrite);
       tskip[i] = z;
       tin = z;
       Ts[i + 1] = To;
@@ -896,14 +896,14 @@ void forward(dmx_handle* h, const float* mix, int G, float* out) {
       p.sy = 4;
       if (i == 0) p.pro_scale = reinterpret_cast<const float*>(norm_f);
       set_output(p, y, G, Fo, kFrames, Co);
-      h->gemm(p, i == 0 ? PRO_BATCH_AFFINE : PRO_NONE, EPI_GELU, "enc.conv", &E.conv);
+      h->gemm(p, i == 0 ? PRO_BATCH_AFFINE : PRO_NONE, EPI_GELU, ("enc.conv" + std::to_string(i)).c_str(), &E.conv);
       run_dconv(h, h->enc_dc[i], y, G * Fo, kFrames);
       float* z = h->falloc((size_t)G * Fo * kFrames * Co);
       ConvParams r = base_params(E.rewrite, h->wdev);
       set_input(r, y, G, Fo, kFrames, Co);
       set_output(r, z, G, Fo, kFrames, Co);
       if (i == 0) r.epi_emb = h->W(m.emb.off);
-      h->gemm(r, PRO_NONE, i == 0 ? EPI_GLU_EMB : EPI_GLU, "enc.rewrite", &E.rewrite);
+      h->gemm(r, PRO_NONE, i == 0 ? EPI_GLU_EMB : EPI_GLU, ("enc.rewrite" + std::to_string(i)).c_str(), &E.rewrite);
       skip[i] = z;
       xin = z;
       Fs[i + 1] = Fo;
@@ -1008,7 +1008,7 @@ void forward(dmx_handle* h, const float* mix, int G, float* out) {
       ConvParams r = base_params(Dw.rewrite, h->wdev);
       set_input(r, x, G, F, kFrames, C);
       set_output(r, g, G, F, kFrames, C);
-      h->gemm(r, PRO_NONE, EPI_GLU, "dec.rewrite", &Dw.rewrite);
+      h->gemm(r, PRO_NONE, EPI_GLU, ("dec.rewrite" + std::to_string(e)).c_str(), &Dw.rewrite);
       run_dconv(h, h->dec_dc[e], g, G * F, kFrames);
       const int Co = Dw.cout, Fo = 4 * F;
       float* o = h->falloc((size_t)G * Fo * kFrames * Co);
@@ -1024,7 +1024,8 @@ void forward(dmx_handle* h, const float* mix, int G, float* out) {
         p.o_off = (int64_t)ph * kFrames * Co;
         p.o_bs = (int64_t)Fo * kFrames * Co;
         if (!last) p.epi_add = skip[j - 1];
-        h->gemm(p, PRO_NONE, last ? EPI_STORE : EPI_GELU, "dec.convtr", &Dw.convt[ph]);
+        h->gemm(p, PRO_NONE, last ? EPI_STORE : EPI_GELU, ("dec.convtr" + std::to_string(e)).c_str(),
+                &Dw.convt[ph]);
       }
       x = o;
       F = Fo;
@@ -1038,7 +1039,7 @@ void forward(dmx_handle* h, const float* mix, int G, float* out) {
       ConvParams r = base_params(Dw.rewrite, h->wdev);
       set_input(r, xt, G, 1, Tc, Ct);
       set_output(r, g, G, 1, Tc, Ct);
-      h->gemm(r, PRO_NONE, EPI_GLU, "tdec.rewrite", &Dw.rewrite);
+      h->gemm(r, PRO_NONE, EPI_GLU, ("tdec.rewrite" + std::to_string(e)).c_str(), &Dw.rewrite);
       run_dconv(h, h->tdec_dc[e], g, G, Tc);
       const int Co = Dw.cout, len = lengths_t[j];
       float* o = h->falloc((size_t)G * len * Co);
@@ -1061,7 +1062,8 @@ void forward(dmx_handle* h, const float* mix, int G, float* out) {
         p.o_off = (int64_t)ph * Co;
         p.o_bs = (int64_t)len * Co;
         if (!last) p.epi_add = tskip[j - 1];
-        h->gemm(p, PRO_NONE, last ? EPI_STORE : EPI_GELU, "tdec.convtr", &Dw.convt[ph]);
+        h->gemm(p, PRO_NONE, last ? EPI_STORE : EPI_GELU, ("tdec.convtr" + std::to_string(e)).c_str(),
+                &Dw.convt[ph]);
       }
       xt = o;
       Tc = len;

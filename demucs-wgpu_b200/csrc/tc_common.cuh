@@ -139,11 +139,16 @@ inline PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
   return fn;
 }
 
+// `elem_strides` (optional): traversal stride per dimension — a box of
+// extent e with stride s loads ceil(e / s) elements, every s-th one.
 inline bool make_tensor_map(CUtensorMap* map, const float* base, int rank, const cuuint64_t* dims,
-              const cuuint64_t* strides_bytes, const cuuint32_t* box, CUtensorMapSwizzle swz) {
+              const cuuint64_t* strides_bytes, const cuuint32_t* box, CUtensorMapSwizzle swz,
+              const cuuint32_t* elem_strides = nullptr) {
   auto fn = tensor_map_encoder();
   if (!fn) return false;
   cuuint32_t estr[5] = {1, 1, 1, 1, 1};
+  if (elem_strides)
+    for (int i = 0; i < rank; ++i) estr[i] = elem_strides[i];
   const CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, (cuuint32_t)rank,
                         const_cast<float*>(base), dims, strides_bytes, box, estr,
                         CU_TENSOR_MAP_INTERLEAVE_NONE, swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,

@@ -1,6 +1,7 @@
 // tcgen05 implicit-GEMM kernel (see tc_gemm.cuh for the design).
 #include <cudaTypedefs.h>
 
+#include <algorithm>
 #include <mutex>
 
 #include "tc_common.cuh"
@@ -11,6 +12,8 @@ namespace dmx {
 namespace {
 
 constexpr int BM = 128;
+constexpr int kThreads = 320;  // warp 0 TMA, warp 1 MMA, warps 2-5 converter, warps 6-9 epilogue
+
 template <int BN, int BK, int STAGES, bool SPLIT>
 struct Smem {
   static constexpr int A_BYTES = BM * BK * 4;
@@ -22,9 +25,30 @@ struct Smem {
   static constexpr int TOTAL = STAGES * STAGE_BYTES + 1024 /*align*/ + 512 /*barriers*/;
 };
 
+// Origin of output-row tile `mt` (see TcAMode).
+DMX_DEVICE void tile_origin(const TcParams& p, int mt, int& tb, int& ty0, int& tx0, int64_t& m0) {
+  tb = ty0 = tx0 = 0;
+  m0 = 0;
+  if (p.mode == TC_2D) {
+    const int nxb = (p.Wq + 15) / 16, nyb = (p.Hq + 7) / 8;
+    tx0 = (mt % nxb) * 16;
+    ty0 = ((mt / nxb) % nyb) * 8;
+    tb = mt / (nxb * nyb);
+  } else if (p.mode == TC_1D) {
+    const int nxb = (p.Wq + BM - 1) / BM;
+    tx0 = (mt % nxb) * BM;
+    tb = mt / nxb;
+  } else {
+    m0 = (int64_t)mt * BM;
+  }
+}
 
+// Persistent: CTA c computes tiles c, c + grid, ... of the (row tile, column
+// tile) space in row-major order, so the column tiles of one row tile run on
+// neighbouring SMs at the same time and its A rows come from HBM once. Two
+// TMEM accumulators: the epilogue of one tile overlaps the MMAs of the next.
 template <int BN, int BK, int STAGES, int EPI, bool SPLIT>
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(kThreads, 1)
     tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const __grid_constant__ CUtensorMap tmBlo, const TcParams p) {
   using S = Smem<BN, BK, STAGES, SPLIT>;
@@ -34,32 +58,14 @@ __global__ void __launch_bounds__(192, 1)
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * S::STAGE_BYTES);
   uint64_t* empty = full + STAGES;
   uint64_t* conv = empty + STAGES;
-  uint64_t* acc_full = conv + STAGES;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_full + 1);
+  uint64_t* acc_full = conv + STAGES;   // [2]
+  uint64_t* acc_empty = acc_full + 2;   // [2]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
   __shared__ double s_stats[4];
-  __shared__ int s_fail;
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-  const int n0 = blockIdx.y * BN;
-  // a previous CTA of this stream gave up: do nothing (uniform across the CTA)
+  // a previous launch on this stream gave up: do nothing (uniform across the CTA)
   if (p.err && *reinterpret_cast<volatile int*>(p.err) != 0) return;
-
-  // tile origin
-  int tb = 0, ty0 = 0, tx0 = 0;
-  int64_t m0 = 0;
-  if (p.mode == TC_2D) {
-    const int nxb = (p.Wq + 15) / 16, nyb = (p.Hq + 7) / 8;
-    const int idx = blockIdx.x;
-    tx0 = (idx % nxb) * 16;
-    ty0 = ((idx / nxb) % nyb) * 8;
-    tb = idx / (nxb * nyb);
-  } else if (p.mode == TC_1D) {
-    const int nxb = (p.Wq + BM - 1) / BM;
-    tx0 = (blockIdx.x % nxb) * BM;
-    tb = blockIdx.x / nxb;
-  } else {
-    m0 = (int64_t)blockIdx.x * BM;
-  }
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -67,15 +73,17 @@ __global__ void __launch_bounds__(192, 1)
       mbar_init(&empty[s], 1);
       mbar_init(&conv[s], 128);
     }
-    mbar_init(acc_full, 1);
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&acc_full[a], 1);
+      mbar_init(&acc_empty[a], 128);
+    }
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-    s_fail = 0;
   }
   if (threadIdx.x < 4) s_stats[threadIdx.x] = 0.0;
   if (warp == 1) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
                      smem_u32(tmem_slot)),
-                 "r"(BN));
+                 "r"(2 * BN));
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
   }
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
@@ -83,32 +91,46 @@ __global__ void __launch_bounds__(192, 1)
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
   const uint32_t tmem = *tmem_slot;
   const int ktiles = p.Kpad / BK;
+  const int total = p.mtiles * p.ntiles;
 
   if (warp == 0) {
     if (lane == 0) {
       // ---------------- TMA producer ----------------
-      for (int kt = 0; kt < ktiles; ++kt) {
-        const int s = kt % STAGES;
-        const uint32_t ph = (kt / STAGES) & 1;
-        if (!mbar_wait(&empty[s], ph ^ 1, p.err, 1)) {
-          s_fail = 1;
-          break;
+      uint32_t it = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
+        const int mt = t / p.ntiles, n0 = (t - mt * p.ntiles) * BN;
+        int tb, ty0, tx0;
+        int64_t m0;
+        tile_origin(p, mt, tb, ty0, tx0, m0);
+        for (int kt = 0; kt < ktiles; ++kt, ++it) {
+          const int s = it % STAGES;
+          const uint32_t ph = (it / STAGES) & 1;
+          if (!mbar_wait(&empty[s], ph ^ 1, p.err, 1)) {
+            ok = false;
+            break;
+          }
+          unsigned char* a_dst = smem + s * S::STAGE_BYTES;
+          unsigned char* b_dst = a_dst + S::A_BYTES;
+          mbar_expect_tx(&full[s], S::TMA_BYTES);
+          const int k0 = kt * BK;
+          if (p.mode == TC_2D) {
+            // with sy = 4 the map traverses H with stride 4: one box is 8 rows
+            const int tap = k0 / p.Cin, c0 = k0 - tap * p.Cin;
+            tma_load_4d(a_dst, &tmA, &full[s], c0, tx0 + p.dx[tap], ty0 * p.sy + p.dy[tap], tb);
+          } else if (p.mode == TC_1D) {
+            const int tap = k0 / p.Cin, c0 = k0 - tap * p.Cin;
+            const int x0 = tx0 * p.sx + p.dx[tap];
+            tma_load_3d(a_dst, &tmA, &full[s], c0, x0, tb);
+            // a strided box holds at most 256 / sx rows: two boxes of 64 rows
+            // (the swizzle pattern repeats every 8 rows, so the halves line up)
+            if (p.sx != 1) tma_load_3d(a_dst + 64 * BK * 4, &tmA, &full[s], c0, x0 + 64 * p.sx, tb);
+          } else {
+            tma_load_2d(a_dst, &tmA, &full[s], k0, (int)m0);
+          }
+          tma_load_2d(b_dst, &tmB, &full[s], k0, n0);
+          if (SPLIT) tma_load_2d(b_dst + S::B_BYTES + S::A_BYTES, &tmBlo, &full[s], k0, n0);
         }
-        unsigned char* a_dst = smem + s * S::STAGE_BYTES;
-        unsigned char* b_dst = a_dst + S::A_BYTES;
-        mbar_expect_tx(&full[s], S::TMA_BYTES);
-        const int k0 = kt * BK;
-        if (p.mode == TC_2D) {
-          const int tap = k0 / p.Cin, c0 = k0 - tap * p.Cin;
-          tma_load_4d(a_dst, &tmA, &full[s], c0, tx0 + p.dx[tap], ty0 + p.dy[tap], tb);
-        } else if (p.mode == TC_1D) {
-          const int tap = k0 / p.Cin, c0 = k0 - tap * p.Cin;
-          tma_load_3d(a_dst, &tmA, &full[s], c0, tx0 + p.dx[tap], tb);
-        } else {
-          tma_load_2d(a_dst, &tmA, &full[s], k0, (int)m0);
-        }
-        tma_load_2d(b_dst, &tmB, &full[s], k0, n0);
-        if (SPLIT) tma_load_2d(b_dst + S::B_BYTES + S::A_BYTES, &tmBlo, &full[s], k0, n0);
       }
     }
   } else if (warp == 1) {
@@ -116,58 +138,65 @@ __global__ void __launch_bounds__(192, 1)
       // ---------------- MMA issuer ----------------
       constexpr uint32_t idesc = (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)(BN >> 3) << 17) |
                                  ((uint32_t)(BM >> 4) << 24);
+      uint32_t it = 0;
+      int tl = 0;
       bool ok = true;
-      for (int kt = 0; kt < ktiles && ok; ++kt) {
-        const int s = kt % STAGES;
-        const uint32_t ph = (kt / STAGES) & 1;
-        if (!mbar_wait(&conv[s], ph, p.err, 2)) {
-          ok = false;
-          break;
-        }
+      for (int t = blockIdx.x; t < total && ok; t += gridDim.x, ++tl) {
+        const int acc = tl & 1;
+        if (!mbar_wait(&acc_empty[acc], ((tl >> 1) & 1) ^ 1, p.err, 5)) break;
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-        const uint32_t a_addr = smem_u32(smem + s * S::STAGE_BYTES);
-        const uint32_t b_addr = a_addr + S::A_BYTES;
-        const uint32_t alo_addr = b_addr + S::B_BYTES;
-        const uint32_t blo_addr = alo_addr + S::A_BYTES;
-#pragma unroll
-        for (int j = 0; j < BK / 8; ++j) {
-          const uint64_t ad = umma_desc_k(a_addr + j * 32, BK * 4);
-          const uint64_t bd = umma_desc_k(b_addr + j * 32, BK * 4);
-          if (SPLIT) {
-            // small terms first: lo*hi + hi*lo, then hi*hi
-            umma_tf32(tmem, umma_desc_k(alo_addr + j * 32, BK * 4), bd, idesc, (kt | j) != 0);
-            umma_tf32(tmem, ad, umma_desc_k(blo_addr + j * 32, BK * 4), idesc, 1);
-            umma_tf32(tmem, ad, bd, idesc, 1);
-          } else {
-            umma_tf32(tmem, ad, bd, idesc, (kt | j) != 0);
+        const uint32_t d = tmem + (uint32_t)(acc * BN);
+        for (int kt = 0; kt < ktiles; ++kt, ++it) {
+          const int s = it % STAGES;
+          const uint32_t ph = (it / STAGES) & 1;
+          if (!mbar_wait(&conv[s], ph, p.err, 2)) {
+            ok = false;
+            break;
           }
+          asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+          const uint32_t a_addr = smem_u32(smem + s * S::STAGE_BYTES);
+          const uint32_t b_addr = a_addr + S::A_BYTES;
+          const uint32_t alo_addr = b_addr + S::B_BYTES;
+          const uint32_t blo_addr = alo_addr + S::A_BYTES;
+#pragma unroll
+          for (int j = 0; j < BK / 8; ++j) {
+            const uint64_t ad = umma_desc_k(a_addr + j * 32, BK * 4);
+            const uint64_t bd = umma_desc_k(b_addr + j * 32, BK * 4);
+            if (SPLIT) {
+              // small terms first: lo*hi + hi*lo, then hi*hi
+              umma_tf32(d, umma_desc_k(alo_addr + j * 32, BK * 4), bd, idesc, (kt | j) != 0);
+              umma_tf32(d, ad, umma_desc_k(blo_addr + j * 32, BK * 4), idesc, 1);
+              umma_tf32(d, ad, bd, idesc, 1);
+            } else {
+              umma_tf32(d, ad, bd, idesc, (kt | j) != 0);
+            }
+          }
+          umma_commit(&empty[s]);
         }
-        umma_commit(&empty[s]);
+        if (ok) umma_commit(&acc_full[acc]);
       }
-      umma_commit(acc_full);
     }
-  } else {
-    // ---------------- epilogue: warps 2..5, one TMEM lane (row) per thread ----------------
-    const int quarter = warp % 4;  // TMEM lane group this warp may access
-    const int r = quarter * 32 + lane;
-    {
-      // converter: round each landed A row to nearest tf32 in place (the
-      // tensor core would otherwise truncate), and for SPLIT write the
-      // residual x - tf32(x) into the A_lo buffer at the same offset.
-      const int row = threadIdx.x - 64;
-      bool live = true;
-      for (int kt = 0; kt < ktiles; ++kt) {
-        const int s = kt % STAGES;
-        const uint32_t ph = (kt / STAGES) & 1;
+  } else if (warp < 6) {
+    // ---------------- converter: warps 2..5, one A row per thread ----------------
+    // Round each landed A row to nearest tf32 in place (the tensor core would
+    // otherwise truncate); for SPLIT write the residual x - tf32(x) into the
+    // A_lo buffer at the same offset.
+    const int row = threadIdx.x - 64;
+    // visit the row's 16-byte chunks in the order the TMA swizzle permutes
+    // them (chunk ^ (128-byte line % 8)), so the 8 lanes of a quarter-warp
+    // touch 8 different bank groups
+    const int swz = BK == 32 ? (row & 7) : ((row >> 1) & 3);
+    uint32_t it = 0;
+    bool live = true;
+    for (int t = blockIdx.x; t < total; t += gridDim.x) {
+      for (int kt = 0; kt < ktiles; ++kt, ++it) {
+        const int s = it % STAGES;
+        const uint32_t ph = (it / STAGES) & 1;
         if (live && !mbar_wait(&full[s], ph, p.err, 4)) live = false;
         if (live) {
           float4* a = reinterpret_cast<float4*>(smem + s * S::STAGE_BYTES + row * BK * 4);
           float4* alo = reinterpret_cast<float4*>(smem + s * S::STAGE_BYTES + S::A_BYTES +
                                                   S::B_BYTES + row * BK * 4);
-          // visit the row's 16-byte chunks in the order the TMA swizzle
-          // permutes them (chunk ^ (128-byte line % 8)), so the 8 lanes of a
-          // quarter-warp touch 8 different bank groups
-          const int swz = BK == 32 ? (row & 7) : ((row >> 1) & 3);
 #pragma unroll
           for (int qq = 0; qq < BK / 4; ++qq) {
             const int q = qq ^ swz;
@@ -186,155 +215,156 @@ __global__ void __launch_bounds__(192, 1)
                      : "memory");
       }
     }
-    const bool ok = mbar_wait(acc_full, 0, p.err, 3);
-    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-    int b, y, x;
-    int64_t pos;
-    bool valid;
-    if (p.mode == TC_2D) {
-      y = ty0 + r / 16;
-      x = tx0 + r % 16;
-      b = tb;
-      valid = y < p.Hq && x < p.Wq;
-      pos = ((int64_t)b * p.Hq + y) * p.Wq + x;
-    } else if (p.mode == TC_1D) {
-      y = 0;
-      x = tx0 + r;
-      b = tb;
-      valid = x < p.Wq;
-      pos = (int64_t)b * p.Wq + x;
-    } else {
-      pos = m0 + r;
-      const int64_t plane = (int64_t)p.Hq * p.Wq;
-      valid = pos < (int64_t)p.B * plane;
-      b = (int)(pos / plane);
-      const int64_t rem = pos - (int64_t)b * plane;
-      y = (int)(rem / p.Wq);
-      x = (int)(rem % p.Wq);
-    }
-    const int64_t orow = (int64_t)b * p.o_bs + (int64_t)y * p.o_ys + (int64_t)x * p.o_xs + p.o_off;
-    constexpr bool kStats = EPI == EPI_STATS || EPI == EPI_STORE_STATS || EPI == EPI_RESIDUAL;
-    double ls = 0.0, lq = 0.0;
-    RowNorm nr{0.f, 0.f};
-    if (EPI == EPI_DCONV_TAIL && valid) nr = row_norm(p.epi_nstats, (int)(pos / p.epi_rowlen), p.epi_count);
+  } else {
+    // ---------------- epilogue: warps 6..9, one TMEM lane (row) per thread ----------------
+    const int quarter = warp % 4;  // TMEM lane group this warp may access
+    const int r = quarter * 32 + lane;
     const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
-    for (int c0 = 0; c0 < BN; c0 += 32) {
-      float v[32];
-      __syncwarp();
-      tmem_ld32(tmem + lane_base + (uint32_t)c0, v);
-      const int nb = n0 + c0;
-      if (ok && valid && nb < p.N) {
-#pragma unroll
-      for (int j = 0; j < 32; ++j) v[j] += p.bias[nb + j];
-      if (EPI == EPI_STORE || EPI == EPI_GELU || EPI == EPI_STORE_STATS) {
-        if (EPI == EPI_GELU) {
-#pragma unroll
-          for (int j = 0; j < 32; ++j) v[j] = gelu(v[j]);
-        }
-        if (EPI == EPI_STORE && p.round_out) {
-#pragma unroll
-          for (int j = 0; j < 32; ++j) v[j] = round_tf32(v[j]);
-        }
-        if (EPI == EPI_STORE && p.vt_out && nb >= p.vt_col0) {
-          // whole 32-column chunks belong to one head (vt_col0 and 64 are multiples of 32)
-          const int c = nb - p.vt_col0, hh = c / 64, d0 = c % 64;
-          const int64_t row = pos;
-          const int64_t bb = row / p.vt_ntok, tok = row % p.vt_ntok;
-          float* vt = p.vt_out + ((bb * 8 + hh) * 64 + d0) * (int64_t)p.vt_ntok + tok;
-          for (int j = 0; j < 32; ++j)
-            if (nb + j < p.N) vt[(int64_t)j * p.vt_ntok] = v[j];
-        }
-        if (p.epi_add) {
-          const float* ad = p.epi_add + orow + nb;
-          for (int j = 0; j < 32; ++j)
-            if (nb + j < p.N) v[j] += ad[j];
-        }
-        float* o = p.out + orow + nb;
-        if (nb + 32 <= p.N && ((orow + nb) & 3) == 0) {
-#pragma unroll
-          for (int j = 0; j < 32; j += 4)
-            *reinterpret_cast<float4*>(o + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
-        } else {
-          for (int j = 0; j < 32; ++j)
-            if (nb + j < p.N) o[j] = v[j];
-        }
-      }
-      if (EPI == EPI_GLU || EPI == EPI_GLU_EMB) {
-#pragma unroll
-        for (int j = 0; j < 32; j += 2) {
-          if (nb + j >= p.N) break;
-          const int c = (nb + j) / 2;
-          float g = v[j] * sigmoid(v[j + 1]);
-          if (EPI == EPI_GLU_EMB) g += p.epi_emb[(int64_t)y * (p.N / 2) + c];
-          p.out[orow + c] = g;
-        }
-      }
-      if (EPI == EPI_DCONV_TAIL) {
-#pragma unroll
-        for (int j = 0; j < 32; j += 2) {
-          if (nb + j >= p.N) break;
-          const int c = (nb + j) / 2;
-          const float vs = nr.inv * p.epi_gw[c];
-          const float vsh = p.epi_gb[c] - nr.mean * vs;
-          const float gs = nr.inv * p.epi_gw[c + p.epi_half];
-          const float gsh = p.epi_gb[c + p.epi_half] - nr.mean * gs;
-          const float value = v[j] * vs + vsh;
-          const float gate = v[j + 1] * gs + gsh;
-          const int64_t o = orow + c;
-          p.out[o] = p.epi_res[o] + p.epi_gamma[c] * (value * sigmoid(gate));
-        }
-      }
-      if (EPI == EPI_RESIDUAL) {
-        float* o = p.out + orow + nb;
-        const float* rr = p.epi_res + orow + nb;
-        for (int j = 0; j < 32; ++j)
-          if (nb + j < p.N) {
-            v[j] = rr[j] + p.epi_gamma[nb + j] * v[j];
-            o[j] = v[j];
-          }
-      }
-      if (kStats) {
-        for (int j = 0; j < 32; ++j)
-          if (nb + j < p.N) {
-            ls += (double)v[j];
-            lq += (double)v[j] * v[j];
-          }
-      }
-      }  // ok && valid
-    }
-    __syncwarp();
-    if (kStats && p.epi_stats) {
-      // rows of one tile span at most two statistic rows (rowlen >= 128)
-      int64_t first;
+    constexpr bool kStats = EPI == EPI_RESIDUAL;
+    bool ok = true;
+    int tl = 0;
+    for (int t = blockIdx.x; t < total; t += gridDim.x, ++tl) {
+      const int mt = t / p.ntiles, n0 = (t - mt * p.ntiles) * BN;
+      int tb, ty0, tx0;
+      int64_t m0;
+      tile_origin(p, mt, tb, ty0, tx0, m0);
+      const int acc = tl & 1;
+      if (ok && !mbar_wait(&acc_full[acc], (tl >> 1) & 1, p.err, 3)) ok = false;
+      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+      int b, y, x;
+      int64_t pos;
+      bool valid;
       if (p.mode == TC_2D) {
-        const int64_t p0 = ((int64_t)tb * p.Hq + ty0) * p.Wq + tx0;
-        first = p0 / p.epi_rowlen;
+        y = ty0 + r / 16;
+        x = tx0 + r % 16;
+        b = tb;
+        valid = y < p.Hq && x < p.Wq;
+        pos = ((int64_t)b * p.Hq + y) * p.Wq + x;
       } else if (p.mode == TC_1D) {
-        first = ((int64_t)tb * p.Wq + tx0) / p.epi_rowlen;
+        y = 0;
+        x = tx0 + r;
+        b = tb;
+        valid = x < p.Wq;
+        pos = (int64_t)b * p.Wq + x;
       } else {
-        first = m0 / p.epi_rowlen;
+        pos = m0 + r;
+        const int64_t plane = (int64_t)p.Hq * p.Wq;
+        valid = pos < (int64_t)p.B * plane;
+        b = (int)(pos / plane);
+        const int64_t rem = pos - (int64_t)b * plane;
+        y = (int)(rem / p.Wq);
+        x = (int)(rem % p.Wq);
       }
-      const int slot = valid ? (int)(pos / p.epi_rowlen - first) : 0;
-      double s0 = slot == 0 ? ls : 0.0, q0 = slot == 0 ? lq : 0.0;
-      double s1 = slot == 1 ? ls : 0.0, q1 = slot == 1 ? lq : 0.0;
-      s0 = warp_sum(s0);
-      q0 = warp_sum(q0);
-      s1 = warp_sum(s1);
-      q1 = warp_sum(q1);
-      if (lane == 0) {
-        atomicAdd(&s_stats[0], s0);
-        atomicAdd(&s_stats[1], q0);
-        atomicAdd(&s_stats[2], s1);
-        atomicAdd(&s_stats[3], q1);
+      const int64_t orow = (int64_t)b * p.o_bs + (int64_t)y * p.o_ys + (int64_t)x * p.o_xs + p.o_off;
+      double ls = 0.0, lq = 0.0;
+      const uint32_t tacc = tmem + lane_base + (uint32_t)(acc * BN);
+      for (int c0 = 0; c0 < BN; c0 += 32) {
+        float v[32];
+        __syncwarp();
+        tmem_ld32(tacc + (uint32_t)c0, v);
+        const int nb = n0 + c0;
+        if (ok && valid && nb < p.N) {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) v[j] += p.bias[nb + j];
+          if (EPI == EPI_STORE || EPI == EPI_GELU) {
+            if (EPI == EPI_GELU) {
+#pragma unroll
+              for (int j = 0; j < 32; ++j) v[j] = gelu(v[j]);
+            }
+            if (EPI == EPI_STORE && p.round_out) {
+#pragma unroll
+              for (int j = 0; j < 32; ++j) v[j] = round_tf32(v[j]);
+            }
+            if (EPI == EPI_STORE && p.vt_out && nb >= p.vt_col0) {
+              // whole 32-column chunks belong to one head (vt_col0 and 64 are multiples of 32)
+              const int c = nb - p.vt_col0, hh = c / 64, d0 = c % 64;
+              const int64_t bb = pos / p.vt_ntok, tok = pos % p.vt_ntok;
+              float* vt = p.vt_out + ((bb * 8 + hh) * 64 + d0) * (int64_t)p.vt_ntok + tok;
+              for (int j = 0; j < 32; ++j)
+                if (nb + j < p.N) vt[(int64_t)j * p.vt_ntok] = v[j];
+            }
+            if (p.epi_add) {
+              const float* ad = p.epi_add + orow + nb;
+              for (int j = 0; j < 32; ++j)
+                if (nb + j < p.N) v[j] += ad[j];
+            }
+            float* o = p.out + orow + nb;
+            if (nb + 32 <= p.N && ((orow + nb) & 3) == 0) {
+#pragma unroll
+              for (int j = 0; j < 32; j += 4)
+                *reinterpret_cast<float4*>(o + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+            } else {
+              for (int j = 0; j < 32; ++j)
+                if (nb + j < p.N) o[j] = v[j];
+            }
+          }
+          if (EPI == EPI_GLU || EPI == EPI_GLU_EMB) {
+#pragma unroll
+            for (int j = 0; j < 32; j += 2) {
+              if (nb + j >= p.N) break;
+              const int c = (nb + j) / 2;
+              float g = v[j] * sigmoid(v[j + 1]);
+              if (EPI == EPI_GLU_EMB) g += p.epi_emb[(int64_t)y * (p.N / 2) + c];
+              p.out[orow + c] = g;
+            }
+          }
+          if (EPI == EPI_RESIDUAL) {
+            float* o = p.out + orow + nb;
+            const float* rr = p.epi_res + orow + nb;
+            for (int j = 0; j < 32; ++j)
+              if (nb + j < p.N) {
+                v[j] = rr[j] + p.epi_gamma[nb + j] * v[j];
+                o[j] = v[j];
+              }
+          }
+          if (kStats) {
+            for (int j = 0; j < 32; ++j)
+              if (nb + j < p.N) {
+                ls += (double)v[j];
+                lq += (double)v[j] * v[j];
+              }
+          }
+        }  // ok && valid
       }
-      asm volatile("bar.sync 1, 128;" ::: "memory");
-      if (warp == 2 && lane == 0) {
-        atomicAdd(&p.epi_stats[2 * first], s_stats[0]);
-        atomicAdd(&p.epi_stats[2 * first + 1], s_stats[1]);
-        if (s_stats[2] != 0.0 || s_stats[3] != 0.0) {
-          atomicAdd(&p.epi_stats[2 * (first + 1)], s_stats[2]);
-          atomicAdd(&p.epi_stats[2 * (first + 1) + 1], s_stats[3]);
+      // the accumulator may be overwritten by the next tile's MMAs
+      asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+      asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(&acc_empty[acc]))
+                   : "memory");
+      if (kStats && p.epi_stats) {
+        // rows of one tile span at most two statistic rows (rowlen >= 128)
+        int64_t first;
+        if (p.mode == TC_2D) {
+          const int64_t p0 = ((int64_t)tb * p.Hq + ty0) * p.Wq + tx0;
+          first = p0 / p.epi_rowlen;
+        } else if (p.mode == TC_1D) {
+          first = ((int64_t)tb * p.Wq + tx0) / p.epi_rowlen;
+        } else {
+          first = m0 / p.epi_rowlen;
         }
+        const int slot = valid ? (int)(pos / p.epi_rowlen - first) : 0;
+        double s0 = slot == 0 ? ls : 0.0, q0 = slot == 0 ? lq : 0.0;
+        double s1 = slot == 1 ? ls : 0.0, q1 = slot == 1 ? lq : 0.0;
+        s0 = warp_sum(s0);
+        q0 = warp_sum(q0);
+        s1 = warp_sum(s1);
+        q1 = warp_sum(q1);
+        if (lane == 0) {
+          atomicAdd(&s_stats[0], s0);
+          atomicAdd(&s_stats[1], q0);
+          atomicAdd(&s_stats[2], s1);
+          atomicAdd(&s_stats[3], q1);
+        }
+        asm volatile("bar.sync 1, 128;" ::: "memory");
+        if (warp == 6 && lane == 0) {
+          atomicAdd(&p.epi_stats[2 * first], s_stats[0]);
+          atomicAdd(&p.epi_stats[2 * first + 1], s_stats[1]);
+          if (s_stats[2] != 0.0 || s_stats[3] != 0.0) {
+            atomicAdd(&p.epi_stats[2 * (first + 1)], s_stats[2]);
+            atomicAdd(&p.epi_stats[2 * (first + 1) + 1], s_stats[3]);
+          }
+          s_stats[0] = s_stats[1] = s_stats[2] = s_stats[3] = 0.0;
+        }
+        asm volatile("bar.sync 1, 128;" ::: "memory");
       }
     }
   }
@@ -343,7 +373,7 @@ __global__ void __launch_bounds__(192, 1)
   if (warp == 1) {
     __syncwarp();
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(BN));
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(2 * BN));
   }
 }
 
@@ -362,7 +392,7 @@ void launch_cfg(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap&
                            cudaFuncAttributeMaxDynamicSharedMemorySize, smem);                \
       attr = true;                                                                            \
     }                                                                                         \
-    tc_gemm_kernel<BN, BK, STAGES, E, SPLIT><<<grid, 192, smem, s>>>(ma, mb, mblo, p);        \
+    tc_gemm_kernel<BN, BK, STAGES, E, SPLIT><<<grid, kThreads, smem, s>>>(ma, mb, mblo, p);   \
     break;                                                                                    \
   }
   switch (epi) {
@@ -370,15 +400,25 @@ void launch_cfg(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap&
     DMX_TC_CASE(EPI_GELU)
     DMX_TC_CASE(EPI_GLU)
     DMX_TC_CASE(EPI_GLU_EMB)
-    DMX_TC_CASE(EPI_STATS)
-    DMX_TC_CASE(EPI_STORE_STATS)
-    DMX_TC_CASE(EPI_DCONV_TAIL)
     DMX_TC_CASE(EPI_RESIDUAL)
   }
 #undef DMX_TC_CASE
 }
 
-int pick_bn(int N) { return N <= 128 ? 128 : 256; }
+int pick_bn(int N) { return N <= 64 ? 64 : (N <= 128 ? 128 : 256); }
+
+int sm_count() {
+  static int count[64] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) return 148;
+  if (!count[dev]) {
+    int n = 0;
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    count[dev] = n > 0 ? n : 148;
+  }
+  return count[dev];
+}
 
 }  // namespace
 
@@ -389,40 +429,45 @@ bool tc_gemm_supported(const TcOperandA& a, const TcParams& p) {
   if (p.mode == TC_2D || p.mode == TC_1D) {
     if (a.C != p.Cin) return false;
     if ((a.sw * 4) % 16 || (a.sh * 4) % 16 || (a.sb * 4) % 16) return false;
+    const bool strided = p.mode == TC_2D ? (p.sy == 4 && p.sx == 1) : (p.sx == 4 && p.sy == 1);
+    if (!strided && (p.sy != 1 || p.sx != 1)) return false;
   } else {
-    if (p.ntaps != 1) return false;
+    if (p.ntaps != 1 || p.sy != 1 || p.sx != 1) return false;
     if ((a.sw * 4) % 16) return false;
   }
   if ((reinterpret_cast<uintptr_t>(a.ptr) & 15) != 0) return false;
   return true;
 }
 
-void launch_tc_gemm(const TcOperandA& a, const float* wk, const float* wk_lo, const TcParams& p,
+void launch_tc_gemm(const TcOperandA& a, const float* wk, const float* wk_lo, const TcParams& p0,
                     int epi, cudaStream_t s) {
+  TcParams p = p0;
   const int bk = (p.Cin % 32 == 0) ? 32 : 16;
   const CUtensorMapSwizzle swz = bk == 32 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
   const int bn = pick_bn(p.N);
   CUtensorMap ma, mb, mblo;
   bool ok;
-  dim3 grid;
   if (p.mode == TC_2D) {
     const cuuint64_t dims[4] = {(cuuint64_t)a.C, (cuuint64_t)a.W, (cuuint64_t)a.H, (cuuint64_t)a.B};
     const cuuint64_t str[3] = {(cuuint64_t)a.sw * 4, (cuuint64_t)a.sh * 4, (cuuint64_t)a.sb * 4};
-    const cuuint32_t box[4] = {(cuuint32_t)bk, 16, 8, 1};
-    ok = make_tensor_map(&ma, a.ptr, 4, dims, str, box, swz);
-    grid.x = (unsigned)(((p.Wq + 15) / 16) * ((p.Hq + 7) / 8) * p.B);
+    const cuuint32_t box[4] = {(cuuint32_t)bk, 16, (cuuint32_t)(8 * p.sy), 1};
+    const cuuint32_t estr[4] = {1, 1, (cuuint32_t)p.sy, 1};
+    ok = make_tensor_map(&ma, a.ptr, 4, dims, str, box, swz, estr);
+    p.mtiles = ((p.Wq + 15) / 16) * ((p.Hq + 7) / 8) * p.B;
   } else if (p.mode == TC_1D) {
     const cuuint64_t dims[3] = {(cuuint64_t)a.C, (cuuint64_t)a.W, (cuuint64_t)a.B};
     const cuuint64_t str[2] = {(cuuint64_t)a.sw * 4, (cuuint64_t)a.sb * 4};
-    const cuuint32_t box[3] = {(cuuint32_t)bk, (cuuint32_t)BM, 1};
-    ok = make_tensor_map(&ma, a.ptr, 3, dims, str, box, swz);
-    grid.x = (unsigned)(((p.Wq + BM - 1) / BM) * p.B);
+    // strided: a box of 256 positions at stride 4 holds 64 rows (two per tile)
+    const cuuint32_t box[3] = {(cuuint32_t)bk, (cuuint32_t)(p.sx == 1 ? BM : 64 * p.sx), 1};
+    const cuuint32_t estr[3] = {1, (cuuint32_t)p.sx, 1};
+    ok = make_tensor_map(&ma, a.ptr, 3, dims, str, box, swz, estr);
+    p.mtiles = ((p.Wq + BM - 1) / BM) * p.B;
   } else {
     const cuuint64_t dims[2] = {(cuuint64_t)a.C, (cuuint64_t)a.W};
     const cuuint64_t str[1] = {(cuuint64_t)a.sw * 4};
     const cuuint32_t box[2] = {(cuuint32_t)bk, (cuuint32_t)BM};
     ok = make_tensor_map(&ma, a.ptr, 2, dims, str, box, swz);
-    grid.x = (unsigned)((a.W + BM - 1) / BM);
+    p.mtiles = (a.W + BM - 1) / BM;
   }
   {
     const cuuint64_t dims[2] = {(cuuint64_t)p.Kpad, (cuuint64_t)p.Npad};
@@ -432,16 +477,23 @@ void launch_tc_gemm(const TcOperandA& a, const float* wk, const float* wk_lo, co
     ok = ok && make_tensor_map(&mblo, wk_lo ? wk_lo : wk, 2, dims, str, box, swz);
   }
   if (!ok) return;  // caller checked tc_gemm_supported; a failed encode leaves the output untouched
-  grid.y = (unsigned)((p.N + bn - 1) / bn);
-  grid.z = 1;
+  p.ntiles = (p.N + bn - 1) / bn;
+  const int64_t total = (int64_t)p.mtiles * p.ntiles;
+  const dim3 grid((unsigned)std::min<int64_t>(total, sm_count()));
   if (wk_lo) {  // 3xTF32: split stages are twice the size
-    if (bn == 128) {
+    if (bn == 64) {
+      if (bk == 32) launch_cfg<64, 32, 4, true>(ma, mb, mblo, p, epi, grid, s);
+      else launch_cfg<64, 16, 8, true>(ma, mb, mblo, p, epi, grid, s);
+    } else if (bn == 128) {
       if (bk == 32) launch_cfg<128, 32, 3, true>(ma, mb, mblo, p, epi, grid, s);
       else launch_cfg<128, 16, 6, true>(ma, mb, mblo, p, epi, grid, s);
     } else {
       if (bk == 32) launch_cfg<256, 32, 2, true>(ma, mb, mblo, p, epi, grid, s);
       else launch_cfg<256, 16, 4, true>(ma, mb, mblo, p, epi, grid, s);
     }
+  } else if (bn == 64) {
+    if (bk == 32) launch_cfg<64, 32, 8, false>(ma, mb, mblo, p, epi, grid, s);
+    else launch_cfg<64, 16, 12, false>(ma, mb, mblo, p, epi, grid, s);
   } else if (bn == 128) {
     if (bk == 32) launch_cfg<128, 32, 6, false>(ma, mb, mblo, p, epi, grid, s);
     else launch_cfg<128, 16, 8, false>(ma, mb, mblo, p, epi, grid, s);

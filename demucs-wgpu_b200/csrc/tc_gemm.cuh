@@ -1,10 +1,12 @@
 // Tensor-core (tcgen05 / TMEM / TMA) implicit-GEMM convolution for sm_100a.
 //
-// One CTA computes a 128 x BN output tile with cta_group::1 UMMA (kind::tf32,
-// fp32 accumulate in TMEM). Warp 0 issues TMA tile loads into a STAGES-deep
-// shared-memory ring, warp 1 issues the MMAs (one elected thread), warps 2-5
-// drain the accumulator with tcgen05.ld and apply the same fused epilogues as
-// the SIMT path (conv_gemm.cuh). The A operand is an activation tile read
+// Persistent: one CTA per SM walks the 128 x BN output tiles (column tiles
+// fastest) with cta_group::1 UMMA (kind::tf32, fp32 accumulate in TMEM, two
+// accumulators). Warp 0 issues TMA tile loads into a STAGES-deep shared-memory
+// ring, warps 2-5 round each landed A tile to nearest tf32, warp 1 issues the
+// MMAs (one elected thread), and warps 6-9 drain the previous tile's
+// accumulator with tcgen05.ld and apply the same fused epilogues as the SIMT
+// path (conv_gemm.cuh) while the next tile's MMAs run. The A operand is an activation tile read
 // straight from the channels-last tensor by TMA — the convolution taps are
 // coordinate offsets and the padding is TMA's out-of-bounds zero fill, so no
 // patch matrix exists anywhere. No load uses cluster multicast.
@@ -26,6 +28,7 @@ struct TcParams {
   int mode;
   int B, Hq, Wq;     // output-position grid (TC_2D) ; rows = B*Hq*Wq (TC_ROWS: B=1,Hq=1)
   int Cin;           // channels per tap (K tile never straddles taps)
+  int sy, sx;        // tap stride along H (TC_2D) / W (TC_1D): 1 or 4; input = s*out + d
   int ntaps;
   int dy[kMaxTaps], dx[kMaxTaps];
   int K, Kpad, N, Npad;
@@ -35,11 +38,6 @@ struct TcParams {
   int64_t o_bs, o_ys, o_xs, o_off;
   double* epi_stats;
   int epi_rowlen;
-  const double* epi_nstats;
-  double epi_count;
-  const float* epi_gw;
-  const float* epi_gb;
-  int epi_half;
   const float* epi_gamma;
   const float* epi_res;
   const float* epi_emb;
@@ -48,6 +46,7 @@ struct TcParams {
   float* vt_out;  // EPI_STORE: V^T copy of columns >= vt_col0 (see ConvParams)
   int vt_col0, vt_ntok;
   int* err;  // set non-zero when a bounded wait gives up
+  int mtiles, ntiles;  // tile space (filled in by launch_tc_gemm)
 };
 
 // Host: build the two tensor maps and launch. `a` describes the A operand

@@ -201,38 +201,7 @@ __global__ void __launch_bounds__(256) flash_attention_kernel(
   }
 }
 
-// DConv norm1 + GELU, materialised once (host.rs:994-998): y (rows*T, hid)
-// -> out (rows*T, hp), channels >= hid zero so the next 1x1 GEMM can use a
-// K of hp (a multiple of 16) on the tensor cores.
-__global__ void gn_gelu_pad_kernel(const float* __restrict__ y, int64_t positions, int T, int hid,
-                                   int hp, const double* __restrict__ stats,
-                                   const float* __restrict__ w, const float* __restrict__ b,
-                                   float* __restrict__ out) {
-  const int64_t total = positions * hp;
-  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
-       i += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t pos = i / hp;
-    const int c = (int)(i - pos * hp);
-    float v = 0.f;
-    if (c < hid) {
-      const RowNorm rn = row_norm(stats, (int)(pos / T), (double)hid * T);
-      const float scale = rn.inv * w[c];
-      const float shift = b[c] - rn.mean * scale;
-      v = gelu(y[pos * hid + c] * scale + shift);
-    }
-    out[i] = v;
-  }
-}
-
 }  // namespace
-
-void launch_gn_gelu_pad(const float* y, int64_t positions, int T, int hid, int hp,
-                        const double* stats, const float* w, const float* b, float* out,
-                        cudaStream_t s) {
-  const int64_t total = positions * hp;
-  const int blocks = (int)std::min<int64_t>((total + 255) / 256, 148 * 32);
-  gn_gelu_pad_kernel<<<blocks, 256, 0, s>>>(y, positions, T, hid, hp, stats, w, b, out);
-}
 
 void launch_layer_norm(const float* x, int64_t rows, int ntok, const float* w, const float* b,
                        const float* pos, float* out, cudaStream_t s) {
