@@ -16,8 +16,8 @@ void launch_stft_cac(const float* mix, int B, const float* window, const float2*
 void launch_wave_moments(const float* mix, int B, int64_t n, double* stats, cudaStream_t s);
 void launch_norm_finalize(const double* stats, double count, int B, float4* norm, cudaStream_t s);
 void launch_istft(const float* spec, const float4* norm, const float* window, const float2* tw,
-                  float* frames, const float* envelope, const float* time_branch,
-                  const float4* norm_t, float* out, int B, cudaStream_t s);
+                  const float* envelope, const float* time_branch, const float4* norm_t, float* out,
+                  int B, cudaStream_t s);
 
 // dconv.cu — one DConv layer on x (rows, T, C) channels-last, in place.
 // Weights as packed for the GEMM path: w1[(k*C + c)*w1_ld + h] (k = tap),
@@ -41,6 +41,7 @@ struct DConvArgs {
   float* y;
   double* part1;
   double* part2;
+  int* err;  // raised when a bounded wait gives up
 };
 int dconv_tiles(int T);
 bool dconv_row_fused(int T);

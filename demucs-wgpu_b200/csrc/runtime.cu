@@ -673,6 +673,7 @@ void run_dconv(dmx_handle* h, const DConvFull& dc, float* x, int rows, int T) {
     a.y = y;
     a.part1 = part;
     a.part2 = part ? part + 2 * (size_t)rows * tiles : nullptr;
+    a.err = h->err;
     // algorithmic work: conv1 (3C -> hid) + conv2 (hid -> 2C) per position;
     // x read once and written once
     h->mark(std::string(fused ? "dconv.row" : "dconv.tiled") + std::to_string(C),
@@ -687,7 +688,8 @@ void run_dconv(dmx_handle* h, const DConvFull& dc, float* x, int rows, int T) {
 
 // Host-side tracing: copy a device tensor and hand it over in the reference's
 // layout. kind 0: freq (B, F, T, C) -> (B, C, F, T); kind 1: time (B, T, C)
-// -> (B, C, T); kind 2: as is with the given shape.
+// -> (B, C, T); kind 2: as is with the given shape; kind 3: frame-major freq
+// (B, T, F, C) -> (B, C, F, T), dims given as {B, F, T, C}.
 void trace_tensor(dmx_handle* h, const std::string& name, const float* dev, int kind,
                   std::vector<int64_t> dims, const float* minus = nullptr) {
   if (!h->trace || h->measuring) return;
@@ -709,6 +711,14 @@ void trace_tensor(dmx_handle* h, const std::string& name, const float* dev, int 
         for (int64_t t = 0; t < T; ++t)
           for (int64_t c = 0; c < C; ++c)
             out[((b * C + c) * F + f) * T + t] = host[((b * F + f) * T + t) * C + c];
+    shape = {B, C, F, T};
+  } else if (kind == 3) {
+    const int64_t B = dims[0], F = dims[1], T = dims[2], C = dims[3];
+    for (int64_t b = 0; b < B; ++b)
+      for (int64_t t = 0; t < T; ++t)
+        for (int64_t f = 0; f < F; ++f)
+          for (int64_t c = 0; c < C; ++c)
+            out[((b * C + c) * F + f) * T + t] = host[((b * T + t) * F + f) * C + c];
     shape = {B, C, F, T};
   } else if (kind == 1) {
     const int64_t B = dims[0], T = dims[1], C = dims[2];
@@ -1019,19 +1029,30 @@ void forward(dmx_handle* h, const float* mix, int G, float* out) {
         p.Hq = F;
         p.Wq = kFrames;
         p.out = o;
-        p.o_xs = Co;
-        p.o_ys = 4LL * kFrames * Co;
-        p.o_off = (int64_t)ph * kFrames * Co;
         p.o_bs = (int64_t)Fo * kFrames * Co;
-        if (!last) p.epi_add = skip[j - 1];
+        if (!last) {
+          // (b, f, t, c) with f = 4 f_in + phase
+          p.o_xs = Co;
+          p.o_ys = 4LL * kFrames * Co;
+          p.o_off = (int64_t)ph * kFrames * Co;
+          p.epi_add = skip[j - 1];
+        } else {
+          // the spectrogram for the iSTFT, frame-major (b, t, f, c): one
+          // frame's bins are contiguous
+          p.o_xs = (int64_t)Fo * Co;
+          p.o_ys = 4LL * Co;
+          p.o_off = (int64_t)ph * Co;
+        }
         h->gemm(p, PRO_NONE, last ? EPI_STORE : EPI_GELU, ("dec.convtr" + std::to_string(e)).c_str(),
                 &Dw.convt[ph]);
       }
       x = o;
       F = Fo;
       C = Co;
-      trace_tensor(h, "decoder." + std::to_string(j), x, 0, {G, F, kFrames, C},
-                   last ? nullptr : skip[j - 1]);
+      if (last)
+        trace_tensor(h, "decoder." + std::to_string(j), x, 3, {G, F, kFrames, C});
+      else
+        trace_tensor(h, "decoder." + std::to_string(j), x, 0, {G, F, kFrames, C}, skip[j - 1]);
     }
     {  // time decoder (host.rs:763-827)
       const DecW& Dw = m.tdec[e];
@@ -1074,13 +1095,12 @@ void forward(dmx_handle* h, const float* mix, int G, float* out) {
   }
 
   // (g) iSTFT + branch sum (host.rs:466-519)
-  float* frames = h->falloc((size_t)G * 8 * kFrames * kNfft);
   h->mark("spec.istft", 0.0, 4.0 * G * ((double)kBins * kFrames * 16 + 16.0 * L));
   if (h->live()) {
-    launch_istft(x, norm_f, h->W(m.window.off), tw, frames, h->W(m.env.off), xt, norm_t, out, G, s);
+    launch_istft(x, norm_f, h->W(m.window.off), tw, h->W(m.env.off), xt, norm_t, out, G, s);
     h->after("istft");
   }
-  h->launches += 2;
+  h->launches += 1;
 }
 
 // Raises DMX_ERR_TIMEOUT when a tensor-core kernel gave up a bounded wait.

@@ -5,11 +5,11 @@
 //    packed spectrogram accumulated in f64 on the way out (host.rs:523-543).
 //  * wave_moments: per-segment moments of the waveform.
 //  * norm_finalize: mean / unbiased std / 1/(1e-5+std) per segment.
-//  * istft_frames + istft_ola: denormalise (host.rs:466-469), unpack
-//    (spec.rs:268-300), zero Nyquist bin and border frames (spec.rs:312-340),
-//    inverse FFT x window x 1/64, overlap-add divided by the window-squared
-//    envelope, crop (stft.rs:204-295, spec.rs:117-175), plus the denormalised
-//    time branch (host.rs:499-512) into (b, source, channel, sample).
+//  * istft: denormalise (host.rs:466-469), unpack (spec.rs:268-300), zero
+//    Nyquist bin and border frames (spec.rs:312-340), inverse FFT x window x
+//    1/64, overlap-add divided by the window-squared envelope, crop
+//    (stft.rs:204-295, spec.rs:117-175), plus the denormalised time branch
+//    (host.rs:499-512) into (b, source, channel, sample), in one kernel.
 #include "common.cuh"
 #include "kernels.h"
 
@@ -149,86 +149,179 @@ __global__ void norm_finalize_kernel(const double* __restrict__ stats, double co
   norm[b] = r;
 }
 
-// One CTA per (b, source, frame t): both audio channels of the source in one
-// complex inverse FFT (z = A + iB for Hermitian A, B gives a + ib).
-__global__ void __launch_bounds__(512) istft_frames_kernel(const float* __restrict__ spec,
-                                                           const float4* __restrict__ norm,
-                                                           const float* __restrict__ window,
-                                                           const float2* __restrict__ tw,
-                                                           float* __restrict__ frames) {
-  __shared__ float re[kNfft], im[kNfft];
-  const int t = blockIdx.x, s = blockIdx.y, b = blockIdx.z;
-  const float4 nz = norm[b];
-  const float o2 = nz.w, sd = nz.z;
-  // spec (b, f, t, 16): channel s*4 + a*2 + {re, im}
-  for (int k = threadIdx.x; k < kNfft; k += blockDim.x) {
-    float zr = 0.f, zi = 0.f;
-    if (k < kBins) {
-      const float4 v = *reinterpret_cast<const float4*>(
-          spec + (((int64_t)b * kBins + k) * kFrames + t) * 16 + s * 4);
-      const float ar = (v.x - o2) * sd, ai = (v.y - o2) * sd;
-      const float br = (v.z - o2) * sd, bi = (v.w - o2) * sd;
-      if (k == 0) {  // irfft ignores the imaginary part of the DC bin
-        zr = ar;
-        zi = br;
-      } else {
-        zr = ar - bi;
-        zi = ai + br;
-      }
-    } else if (k > kBins) {
-      const int m = kNfft - k;  // Z[N-m] = conj(A[m]) + i conj(B[m])
-      const float4 v = *reinterpret_cast<const float4*>(
-          spec + (((int64_t)b * kBins + m) * kFrames + t) * 16 + s * 4);
-      const float ar = (v.x - o2) * sd, ai = (v.y - o2) * sd;
-      const float br = (v.z - o2) * sd, bi = (v.w - o2) * sd;
-      zr = ar + bi;
-      zi = -ai + br;
-    }  // k == 2048: the zero Nyquist bin
-    const int r = bitrev12(k);
-    re[r] = zr;
-    im[r] = zi;
-  }
-  __syncthreads();
-  fft4096(re, im, tw, +1.f);
-  const float inv_n = 64.0f / 4096.0f;
-  float* fa = frames + ((((int64_t)b * 4 + s) * 2 + 0) * kFrames + t) * kNfft;
-  float* fb = frames + ((((int64_t)b * 4 + s) * 2 + 1) * kFrames + t) * kNfft;
-  for (int n = threadIdx.x; n < kNfft; n += blockDim.x) {
-    const float w = window[n];
-    fa[n] = re[n] * inv_n * w;
-    fb[n] = im[n] * inv_n * w;
-  }
+// ---------------------------------------------------------------------------
+// iSTFT + overlap-add + time-branch sum, fused. One CTA per (source, 8 output
+// hops, segment): it inverts the 11 frames that overlap its hops
+// (both audio channels of the source in one complex inverse FFT, z = A + iB
+// for Hermitian A, B gives a + ib), windows them and overlap-adds them in
+// shared memory, then writes time + ola / envelope for its 8192 samples.
+// No frame buffer touches HBM; the 3 frames shared with each neighbouring CTA
+// are inverted twice.
+//
+// The 4096-point inverse FFT is 16 x 256 with 256 = 16 x 16: three passes of
+// 16-point DFTs held in registers (256 threads, one DFT each), with the
+// inter-pass twiddles between them; the work buffer's row stride (273) keeps
+// the passes' shared-memory accesses (nearly) conflict-free.
+constexpr int kIstftHops = 8;
+constexpr int kIstftThreads = 256;
+constexpr int kRow = 273;  // stride between the 16 rows of the FFT work buffer
+constexpr size_t kIstftSmem = sizeof(float) * (2 * 16 * kRow + 2 * kIstftHops * kHop);
+
+struct cpx {
+  float x, y;
+};
+DMX_DEVICE cpx cmul(cpx a, cpx b) { return {a.x * b.x - a.y * b.y, a.x * b.y + a.y * b.x}; }
+
+// inverse 4-point DFT in place: y_k = sum_n a_n i^(n k)
+DMX_DEVICE void idft4(cpx& a0, cpx& a1, cpx& a2, cpx& a3) {
+  const cpx s02 = {a0.x + a2.x, a0.y + a2.y}, d02 = {a0.x - a2.x, a0.y - a2.y};
+  const cpx s13 = {a1.x + a3.x, a1.y + a3.y}, d13 = {a1.x - a3.x, a1.y - a3.y};
+  a0 = {s02.x + s13.x, s02.y + s13.y};
+  a2 = {s02.x - s13.x, s02.y - s13.y};
+  a1 = {d02.x - d13.y, d02.y + d13.x};  // d02 + i d13
+  a3 = {d02.x + d13.y, d02.y - d13.x};  // d02 - i d13
 }
 
-// out (b, s, a, j) = time(b, j, s*2+a) denormalised + sum_f frames / env.
-__global__ void istft_ola_kernel(const float* __restrict__ frames,
-                                 const float* __restrict__ envelope,  // [1024]
-                                 const float* __restrict__ time_branch,  // (b, L, 8)
-                                 const float4* __restrict__ norm_t, float* __restrict__ out,
-                                 int B) {
-  const int64_t j = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  const int b = blockIdx.y;
-  if (j >= kSegment) return;
-  const int64_t i = j + kPad + kNfft / 2;  // index in the centred istft signal
-  const int fhi = (int)(i / kHop);
-  const float env = envelope[i % kHop];
-  const float4 nt = norm_t[b];
-  const float4 t0 = *reinterpret_cast<const float4*>(time_branch + ((int64_t)b * kSegment + j) * 8);
-  const float4 t1 = *reinterpret_cast<const float4*>(time_branch + ((int64_t)b * kSegment + j) * 8 + 4);
-  const float tv[8] = {t0.x, t0.y, t0.z, t0.w, t1.x, t1.y, t1.z, t1.w};
+// inverse 16-point DFT of v (input in natural order) as 4 x 4; output k is
+// left at v[4 (k % 4) + k / 4].
+DMX_DEVICE void idft16(cpx (&v)[16]) {
+  // e^(+2 pi i m / 16) for the products b*c of the twiddle step
+  constexpr float c1 = 0.92387953251128674f, s1 = 0.38268343236508977f;
+  constexpr float r2 = 0.70710678118654752f;
 #pragma unroll
-  for (int r = 0; r < 8; ++r) {
-    const float* fr = frames + ((int64_t)b * 8 + r) * kFrames * kNfft;
-    float y = 0.f;
+  for (int b = 0; b < 4; ++b) idft4(v[b], v[4 + b], v[8 + b], v[12 + b]);
+  v[5] = cmul(v[5], {c1, s1});     // b*c = 1
+  v[9] = cmul(v[9], {r2, r2});     // 2
+  v[13] = cmul(v[13], {s1, c1});   // 3
+  v[6] = cmul(v[6], {r2, r2});     // 2
+  v[10] = {-v[10].y, v[10].x};     // 4: times i
+  v[14] = cmul(v[14], {-r2, r2});  // 6
+  v[7] = cmul(v[7], {s1, c1});     // 3
+  v[11] = cmul(v[11], {-r2, r2});  // 6
+  v[15] = cmul(v[15], {-c1, -s1}); // 9
 #pragma unroll
-    for (int f = fhi - 3; f <= fhi; ++f) {
-      const int t = f - 2;
-      if (t >= 0 && t < kFrames) y += fr[(int64_t)t * kNfft + (i - (int64_t)f * kHop)];
-      else y += 0.f;
+  for (int c = 0; c < 4; ++c) idft4(v[4 * c], v[4 * c + 1], v[4 * c + 2], v[4 * c + 3]);
+}
+DMX_DEVICE int idft16_slot(int k) { return 4 * (k & 3) + (k >> 2); }
+
+// e^(+2 pi i j / 4096), j < 4096, from the forward table tw[k] = e^(-2 pi i k / 4096)
+DMX_DEVICE cpx w_inv(const float2* __restrict__ tw, int j) {
+  const float2 t = __ldg(tw + (j & 2047));
+  return j < 2048 ? cpx{t.x, -t.y} : cpx{-t.x, t.y};
+}
+
+// spec: the decoder output frame-major, (b, t, f, 16) with channel
+// source*4 + audio channel*2 + {re, im}.
+__global__ void __launch_bounds__(kIstftThreads, 2)
+    istft_kernel(const float* __restrict__ spec, const float4* __restrict__ norm,
+                 const float* __restrict__ window, const float2* __restrict__ tw,
+                 const float* __restrict__ envelope, const float* __restrict__ time_branch,
+                 const float4* __restrict__ norm_t, float* __restrict__ out) {
+  extern __shared__ float sm[];
+  float* bre = sm;                  // FFT work buffer, 16 rows x kRow
+  float* bim = sm + 16 * kRow;
+  float* acc = sm + 32 * kRow;      // overlap-add, 2 channels x (8 x 1024)
+  constexpr int AC = kIstftHops * kHop;
+  // source fastest: the 4 CTAs of one hop group read the same spectrogram
+  // sectors close together in time
+  const int tid = threadIdx.x, s = blockIdx.x, b = blockIdx.z;
+  const int H0 = 3 + blockIdx.y * kIstftHops;  // first hop: centred-signal index i / 1024
+  const float4 nz = norm[b];
+  const float o2 = nz.w, sd = nz.z;
+  const float inv_n = 64.0f / 4096.0f;
+  // kept frame t is torch frame f = t + 2 and covers hops f .. f + 3
+  const int t_lo = max(0, H0 - 5), t_hi = min(kFrames - 1, H0 + kIstftHops - 3);
+
+  {
+    for (int i = tid; i < 2 * AC; i += kIstftThreads) acc[i] = 0.f;
+    for (int t = t_lo; t <= t_hi; ++t) {
+      // pass 1: thread m = tid, Z[256 n2 + m] for n2 = 0..15 straight from the
+      // spectrogram; all 16 loads are issued before any is used
+      cpx v[16];
+      {
+        const float* fr = spec + ((int64_t)b * kFrames + t) * kBins * 16 + s * 4;
+        float4 q[16];
+#pragma unroll
+        for (int n2 = 0; n2 < 16; ++n2) {
+          const int k = 256 * n2 + tid;
+          const int bin = k < kBins ? k : (k == kBins ? 0 : kNfft - k);
+          q[n2] = *reinterpret_cast<const float4*>(fr + (int64_t)bin * 16);
+        }
+#pragma unroll
+        for (int n2 = 0; n2 < 16; ++n2) {
+          const int k = 256 * n2 + tid;
+          const float ar = (q[n2].x - o2) * sd, ai = (q[n2].y - o2) * sd;
+          const float br = (q[n2].z - o2) * sd, bi = (q[n2].w - o2) * sd;
+          cpx z;
+          if (n2 < 8) {
+            z = k == 0 ? cpx{ar, br}  // irfft ignores the imaginary part of the DC bin
+                       : cpx{ar - bi, ai + br};
+          } else {
+            z = k == kBins ? cpx{0.f, 0.f}        // the zero Nyquist bin
+                           : cpx{ar + bi, br - ai};  // Z[N-m] = conj(A[m]) + i conj(B[m])
+          }
+          v[n2] = z;
+        }
+      }
+      idft16(v);
+#pragma unroll
+      for (int k1 = 0; k1 < 16; ++k1) {
+        const cpx y = k1 == 0 ? v[idft16_slot(0)] : cmul(v[idft16_slot(k1)], w_inv(tw, tid * k1));
+        bre[k1 * kRow + tid] = y.x;
+        bim[k1 * kRow + tid] = y.y;
+      }
+      __syncthreads();
+      {
+        // pass 2: thread (k1, c), the 256-point DFT over m = 16 a + c, first level
+        const int k1 = tid >> 4, c = tid & 15;
+#pragma unroll
+        for (int a = 0; a < 16; ++a)
+          v[a] = {bre[k1 * kRow + 16 * a + c], bim[k1 * kRow + 16 * a + c]};
+        __syncthreads();
+        idft16(v);
+#pragma unroll
+        for (int d = 0; d < 16; ++d) {
+          const cpx u = (d == 0 || c == 0) ? v[idft16_slot(d)]
+                                           : cmul(v[idft16_slot(d)], w_inv(tw, 16 * c * d));
+          bre[k1 * kRow + 17 * d + c] = u.x;
+          bim[k1 * kRow + 17 * d + c] = u.y;
+        }
+      }
+      __syncthreads();
+      {
+        // pass 3: thread (d, k1), second level: X[k1 + 16 d + 256 e], e = 0..15
+        const int d = tid >> 4, k1 = tid & 15;
+#pragma unroll
+        for (int c = 0; c < 16; ++c) v[c] = {bre[k1 * kRow + 17 * d + c], bim[k1 * kRow + 17 * d + c]};
+        idft16(v);
+        const int f = t + 2;
+#pragma unroll
+        for (int e = 0; e < 16; ++e) {
+          const int hop = f + (e >> 2);
+          if (hop >= H0 && hop < H0 + kIstftHops) {
+            const int n = k1 + 16 * d + 256 * e;
+            const int idx = (hop - H0) * kHop + (n & (kHop - 1));
+            const float w = window[n] * inv_n;
+            const cpx x = v[idft16_slot(e)];
+            acc[idx] += x.x * w;
+            acc[AC + idx] += x.y * w;
+          }
+        }
+      }
+      __syncthreads();
     }
-    const float wave = y / env;
-    const float time = (tv[r] - nt.w) * nt.z;
-    out[((int64_t)b * 8 + r) * kSegment + j] = time + wave;
+    // time branch + overlap-add / envelope for this CTA's samples of source s
+    const float4 nt = norm_t[b];
+    for (int u = tid; u < AC; u += kIstftThreads) {
+      const int i = H0 * kHop + u;
+      const int j = i - (kPad + kNfft / 2);
+      if (j < 0 || j >= kSegment) continue;
+      const float env = envelope[i & (kHop - 1)];
+      const float2 tv = *reinterpret_cast<const float2*>(time_branch + ((int64_t)b * kSegment + j) * 8 + 2 * s);
+      out[((int64_t)b * 8 + 2 * s) * kSegment + j] = (tv.x - nt.w) * nt.z + acc[u] / env;
+      out[((int64_t)b * 8 + 2 * s + 1) * kSegment + j] = (tv.y - nt.w) * nt.z + acc[AC + u] / env;
+    }
+    __syncthreads();
   }
 }
 
@@ -249,11 +342,19 @@ void launch_norm_finalize(const double* stats, double count, int B, float4* norm
 }
 
 void launch_istft(const float* spec, const float4* norm, const float* window, const float2* tw,
-                  float* frames, const float* envelope, const float* time_branch,
-                  const float4* norm_t, float* out, int B, cudaStream_t s) {
-  istft_frames_kernel<<<dim3(kFrames, 4, B), 512, 0, s>>>(spec, norm, window, tw, frames);
-  istft_ola_kernel<<<dim3((kSegment + 255) / 256, B), 256, 0, s>>>(frames, envelope, time_branch,
-                                                                  norm_t, out, B);
+                  const float* envelope, const float* time_branch, const float4* norm_t, float* out,
+                  int B, cudaStream_t s) {
+  static bool configured = false;
+  if (!configured) {
+    cudaFuncSetAttribute(istft_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         (int)kIstftSmem);
+    configured = true;
+  }
+  // hops 3 .. 339 of the centred signal hold the segment's samples
+  const int groups = (337 + kIstftHops - 1) / kIstftHops;
+  istft_kernel<<<dim3(4, groups, B), kIstftThreads, kIstftSmem, s>>>(spec, norm, window, tw,
+                                                                     envelope, time_branch, norm_t,
+                                                                     out);
 }
 
 }  // namespace dmx
