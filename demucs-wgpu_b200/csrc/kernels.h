@@ -42,10 +42,20 @@ struct DConvArgs {
   double* part1;
   double* part2;
   int* err;  // raised when a bounded wait gives up
+  // tensor-core path (dconv_tc.cu): K-major weights rounded to nearest tf32
+  // ([w1_npad][3C], [w2_npad][16]) and their residuals w - tf32(w)
+  const float* w1_tc;
+  const float* w1_tc_lo;
+  int w1_npad;
+  const float* w2_tc;
+  const float* w2_tc_lo;
+  int w2_npad;
 };
 int dconv_tiles(int T);
 bool dconv_row_fused(int T);
 bool launch_dconv(const DConvArgs& a, cudaStream_t s);
+bool dconv_tc_supported(int C, int T);
+bool launch_dconv_tc(const DConvArgs& a, cudaStream_t s);
 
 // transformer.cu
 void launch_layer_norm(const float* x, int64_t rows, int ntok, const float* w, const float* b,

@@ -645,7 +645,10 @@ void set_output(ConvParams& p, float* out, int B, int Hq, int Wq, int Cout) {
 void run_dconv(dmx_handle* h, const DConvFull& dc, float* x, int rows, int T) {
   const int C = dc.C, hid = dc.hidden;
   const int64_t positions = (int64_t)rows * T;
-  const bool fused = dconv_row_fused(T);
+  // TF32 builds: tensor cores (3xTF32, fp32-accurate) where the kernel covers the shape
+  const bool tc = (h->cfg.precision == DMX_TF32 || h->cfg.precision == DMX_TF32X3) &&
+                  dconv_tc_supported(C, T) && dc.layer[0].conv1.has_tc && dc.layer[0].conv2.has_tc;
+  const bool fused = tc || dconv_row_fused(T);
   const int tiles = dconv_tiles(T);
   float* y = fused ? nullptr : h->falloc((size_t)positions * hid);
   double* part = fused ? nullptr : h->dalloc((size_t)rows * tiles * 4);
@@ -674,12 +677,19 @@ void run_dconv(dmx_handle* h, const DConvFull& dc, float* x, int rows, int T) {
     a.part1 = part;
     a.part2 = part ? part + 2 * (size_t)rows * tiles : nullptr;
     a.err = h->err;
+    a.w1_tc = h->W(L.conv1.tc_off);
+    a.w1_tc_lo = h->W(L.conv1.tc_lo_off);
+    a.w1_npad = L.conv1.Npad;
+    a.w2_tc = h->W(L.conv2.tc_off);
+    a.w2_tc_lo = h->W(L.conv2.tc_lo_off);
+    a.w2_npad = L.conv2.Npad;
     // algorithmic work: conv1 (3C -> hid) + conv2 (hid -> 2C) per position;
     // x read once and written once
-    h->mark(std::string(fused ? "dconv.row" : "dconv.tiled") + std::to_string(C),
+    h->mark(std::string(tc ? "dconv.tc" : (fused ? "dconv.row" : "dconv.tiled")) + std::to_string(C),
             10.0 * positions * C * hid, 8.0 * positions * C);
     if (h->live()) {
-      if (!launch_dconv(a, h->stream)) throw Error(DMX_ERR_INVALID, "dconv: unsupported shape");
+      if (!(tc ? launch_dconv_tc(a, h->stream) : launch_dconv(a, h->stream)))
+        throw Error(DMX_ERR_INVALID, "dconv: unsupported shape");
       h->after("dconv");
     }
     h->launches += fused ? 1 : 3;
@@ -1201,6 +1211,18 @@ void load_model(dmx_handle* h, const std::map<std::string, HostTensor>& t) {
       Lw.n1b = L.vec(at + ".1.bias", C / 8);
       Lw.conv2 = L.conv(at + ".3", {2 * C, C / 8, 1}, {{0, 0}}, {{0, 0}}, true,
                         (C / 8 + 15) / 16 * 16);
+      // tensor-core copy of conv2 (used only by the fused DConv kernel): the
+      // bias rides in the last, zero-padded input channel, which that kernel
+      // feeds with 1
+      if (Lw.conv2.has_tc && C / 8 < Lw.conv2.K) {
+        const int kb = Lw.conv2.K - 1;
+        for (int n = 0; n < 2 * C; ++n) {
+          const float b = wb.host[Lw.conv2.b_off + n];
+          const float hi = round_tf32_host(b);
+          wb.host[Lw.conv2.tc_off + (size_t)n * Lw.conv2.K + kb] = hi;
+          wb.host[Lw.conv2.tc_lo_off + (size_t)n * Lw.conv2.K + kb] = b - hi;
+        }
+      }
       Lw.n2w = L.vec(at + ".4.weight", 2 * C);
       Lw.n2b = L.vec(at + ".4.bias", 2 * C);
       Lw.gamma = L.vec(at + ".6.scale", C);
