@@ -39,9 +39,12 @@ SEGMENT = synth.SEGMENT_SAMPLES
 SEGMENT_GFLOP = 334.9  # algorithmic FLOPs of one segment forward (2*MAC over the layer table)
 METRIC = "audio-sec separated/sec (htdemucs)"
 UNIT = "audio-s/s"
-# DRAM bytes (read + write) per launch of the dominant kernel tag, from one ncu
-# capture of the same workload (None until captured): tag -> bytes per launch.
-TRAFFIC = {}
+# Measured DRAM bytes (read + write) per algorithmic byte for a kernel tag, from
+# one ncu capture of that kernel (profiles/): roofline.traffic = ratio x the
+# tag's algorithmic bytes per launch. The attention capture is the layer-0
+# spectral self-attention on a 3-chunk track (52.7 MB of DRAM traffic for
+# 66.1 MB of q, k, v, o); traffic scales with the chunks a launch processes.
+TRAFFIC_RATIO = {"xf.attention": 52.745 / 66.060}
 
 
 def workload(seconds):
@@ -60,7 +63,7 @@ def _peaks():
         return 6650.0, 1590.0, 1400.0, "fallback"
 
 
-def roofline(stages, traffic=None):
+def roofline(stages):
     """Roofline of the dominant kernel tag (most device time in the step).
 
     ``stages``: {tag: (ms, launches, flops, bytes)} from the runtime's
@@ -75,6 +78,8 @@ def roofline(stages, traffic=None):
         bound, achieved, peak, unit = "tensor", flops / s / 1e12, bf16_sustained, "TFLOP/s"
     else:
         bound, achieved, peak, unit = "hbm", nbytes / s / 1e9, hbm, "GB/s"
+    ratio = TRAFFIC_RATIO.get(tag)
+    traffic = round(ratio * nbytes / max(launches, 1)) if ratio else None
     return {"bound": bound, "achieved": round(achieved, 3), "peak": peak, "unit": unit,
             "frac": round(achieved / peak, 5), "traffic": traffic,
             "kernel": tag, "launches": launches,
@@ -323,7 +328,7 @@ def run_ours(args, rank, world, local_rank):
                     "h2d_bytes_per_step": int(2 * n * 4) * world, "d2h_bytes_per_step": int(8 * n * 4)},
             "gpu_launches": int(launches) * args.steps,
             "clocks": clocks.summary(),
-            "roofline": roofline(stages, TRAFFIC.get(max(stages, key=lambda k: stages[k][0]))),
+            "roofline": roofline(stages),
             "whole_forward": {"achieved": round(whole, 3), "unit": "TFLOP/s",
                               "frac": round(whole / bf16_sustained, 5),
                               "note": "334.9 GFLOP per segment over the whole step, rank 0's chunks"},
