@@ -12,7 +12,8 @@ namespace dmx {
 namespace {
 
 constexpr int BM = 128;
-constexpr int kThreads = 320;  // warp 0 TMA, warp 1 MMA, warps 2-5 converter, warps 6-9 epilogue
+constexpr int kThreads = 448;  // warp 0 TMA, warp 1 MMA, warps 2-5 converter, warps 6-13 epilogue
+constexpr int kEpiThreads = 256;
 
 template <int BN, int BK, int STAGES, bool SPLIT>
 struct Smem {
@@ -75,7 +76,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&acc_full[a], 1);
-      mbar_init(&acc_empty[a], 128);
+      mbar_init(&acc_empty[a], kEpiThreads);
     }
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
@@ -216,8 +217,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
   } else {
-    // ---------------- epilogue: warps 6..9, one TMEM lane (row) per thread ----------------
-    const int quarter = warp % 4;  // TMEM lane group this warp may access
+    // ---------------- epilogue: warps 6..13, one TMEM lane (row) per thread ----------------
+    // two warps per TMEM lane quarter; half hh takes the 32-column chunks
+    // 64 k + 32 hh of the tile
+    const int e = warp - 6, quarter = warp % 4, hh = e / 4;
     const int r = quarter * 32 + lane;
     const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
     constexpr bool kStats = EPI == EPI_RESIDUAL;
@@ -258,14 +261,28 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int64_t orow = (int64_t)b * p.o_bs + (int64_t)y * p.o_ys + (int64_t)x * p.o_xs + p.o_off;
       double ls = 0.0, lq = 0.0;
       const uint32_t tacc = tmem + lane_base + (uint32_t)(acc * BN);
-      for (int c0 = 0; c0 < BN; c0 += 32) {
+      for (int c0 = 32 * hh; c0 < BN; c0 += 64) {
         float v[32];
         __syncwarp();
         tmem_ld32(tacc + (uint32_t)c0, v);
         const int nb = n0 + c0;
         if (ok && valid && nb < p.N) {
+          // a full chunk whose row segment is 16-byte aligned moves as float4
+          const bool full = nb + 32 <= p.N;
+          const bool bias4 = full && ((reinterpret_cast<uintptr_t>(p.bias + nb) & 15) == 0);
+          if (bias4) {
 #pragma unroll
-          for (int j = 0; j < 32; ++j) v[j] += p.bias[nb + j];
+            for (int j = 0; j < 32; j += 4) {
+              const float4 bb = *reinterpret_cast<const float4*>(p.bias + nb + j);
+              v[j] += bb.x;
+              v[j + 1] += bb.y;
+              v[j + 2] += bb.z;
+              v[j + 3] += bb.w;
+            }
+          } else {
+            for (int j = 0; j < 32; ++j)
+              if (nb + j < p.N) v[j] += p.bias[nb + j];
+          }
           if (EPI == EPI_STORE || EPI == EPI_GELU) {
             if (EPI == EPI_GELU) {
 #pragma unroll
@@ -277,19 +294,31 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             if (EPI == EPI_STORE && p.vt_out && nb >= p.vt_col0) {
               // whole 32-column chunks belong to one head (vt_col0 and 64 are multiples of 32)
-              const int c = nb - p.vt_col0, hh = c / 64, d0 = c % 64;
+              const int c = nb - p.vt_col0, h2 = c / 64, d0 = c % 64;
               const int64_t bb = pos / p.vt_ntok, tok = pos % p.vt_ntok;
-              float* vt = p.vt_out + ((bb * 8 + hh) * 64 + d0) * (int64_t)p.vt_ntok + tok;
+              float* vt = p.vt_out + ((bb * 8 + h2) * 64 + d0) * (int64_t)p.vt_ntok + tok;
               for (int j = 0; j < 32; ++j)
                 if (nb + j < p.N) vt[(int64_t)j * p.vt_ntok] = v[j];
             }
+            const bool vec = full && ((orow + nb) & 3) == 0;
             if (p.epi_add) {
               const float* ad = p.epi_add + orow + nb;
-              for (int j = 0; j < 32; ++j)
-                if (nb + j < p.N) v[j] += ad[j];
+              if (vec) {
+#pragma unroll
+                for (int j = 0; j < 32; j += 4) {
+                  const float4 t4 = *reinterpret_cast<const float4*>(ad + j);
+                  v[j] += t4.x;
+                  v[j + 1] += t4.y;
+                  v[j + 2] += t4.z;
+                  v[j + 3] += t4.w;
+                }
+              } else {
+                for (int j = 0; j < 32; ++j)
+                  if (nb + j < p.N) v[j] += ad[j];
+              }
             }
             float* o = p.out + orow + nb;
-            if (nb + 32 <= p.N && ((orow + nb) & 3) == 0) {
+            if (vec) {
 #pragma unroll
               for (int j = 0; j < 32; j += 4)
                 *reinterpret_cast<float4*>(o + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
@@ -299,30 +328,71 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
           }
           if (EPI == EPI_GLU || EPI == EPI_GLU_EMB) {
+            // 16 outputs: channels nb/2 .. nb/2 + 15
+            float g[16];
 #pragma unroll
-            for (int j = 0; j < 32; j += 2) {
-              if (nb + j >= p.N) break;
-              const int c = (nb + j) / 2;
-              float g = v[j] * sigmoid(v[j + 1]);
-              if (EPI == EPI_GLU_EMB) g += p.epi_emb[(int64_t)y * (p.N / 2) + c];
-              p.out[orow + c] = g;
+            for (int j = 0; j < 16; ++j) g[j] = v[2 * j] * sigmoid(v[2 * j + 1]);
+            const int c0o = nb / 2;
+            const bool vec = full && ((orow + c0o) & 3) == 0;
+            if (EPI == EPI_GLU_EMB) {
+              const float* em = p.epi_emb + (int64_t)y * (p.N / 2) + c0o;
+              if (vec && ((((int64_t)y * (p.N / 2) + c0o) & 3) == 0)) {
+#pragma unroll
+                for (int j = 0; j < 16; j += 4) {
+                  const float4 t4 = *reinterpret_cast<const float4*>(em + j);
+                  g[j] += t4.x;
+                  g[j + 1] += t4.y;
+                  g[j + 2] += t4.z;
+                  g[j + 3] += t4.w;
+                }
+              } else {
+                for (int j = 0; j < 16; ++j)
+                  if (nb + 2 * j < p.N) g[j] += em[j];
+              }
+            }
+            float* o = p.out + orow + c0o;
+            if (vec) {
+#pragma unroll
+              for (int j = 0; j < 16; j += 4)
+                *reinterpret_cast<float4*>(o + j) = make_float4(g[j], g[j + 1], g[j + 2], g[j + 3]);
+            } else {
+              for (int j = 0; j < 16; ++j)
+                if (nb + 2 * j < p.N) o[j] = g[j];
             }
           }
           if (EPI == EPI_RESIDUAL) {
             float* o = p.out + orow + nb;
             const float* rr = p.epi_res + orow + nb;
-            for (int j = 0; j < 32; ++j)
-              if (nb + j < p.N) {
-                v[j] = rr[j] + p.epi_gamma[nb + j] * v[j];
-                o[j] = v[j];
+            const bool vec = full && ((orow + nb) & 3) == 0 &&
+                             ((reinterpret_cast<uintptr_t>(p.epi_gamma + nb) & 15) == 0);
+            if (vec) {
+#pragma unroll
+              for (int j = 0; j < 32; j += 4) {
+                const float4 r4 = *reinterpret_cast<const float4*>(rr + j);
+                const float4 g4 = *reinterpret_cast<const float4*>(p.epi_gamma + nb + j);
+                v[j] = fmaf(g4.x, v[j], r4.x);
+                v[j + 1] = fmaf(g4.y, v[j + 1], r4.y);
+                v[j + 2] = fmaf(g4.z, v[j + 2], r4.z);
+                v[j + 3] = fmaf(g4.w, v[j + 3], r4.w);
+                *reinterpret_cast<float4*>(o + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
               }
+            } else {
+              for (int j = 0; j < 32; ++j)
+                if (nb + j < p.N) {
+                  v[j] = rr[j] + p.epi_gamma[nb + j] * v[j];
+                  o[j] = v[j];
+                }
+            }
           }
           if (kStats) {
+            float fs = 0.f, fq = 0.f;
             for (int j = 0; j < 32; ++j)
               if (nb + j < p.N) {
-                ls += (double)v[j];
-                lq += (double)v[j] * v[j];
+                fs += v[j];
+                fq = fmaf(v[j], v[j], fq);
               }
+            ls += (double)fs;
+            lq += (double)fq;
           }
         }  // ok && valid
       }
@@ -354,7 +424,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           atomicAdd(&s_stats[2], s1);
           atomicAdd(&s_stats[3], q1);
         }
-        asm volatile("bar.sync 1, 128;" ::: "memory");
+        asm volatile("bar.sync 1, 256;" ::: "memory");
         if (warp == 6 && lane == 0) {
           atomicAdd(&p.epi_stats[2 * first], s_stats[0]);
           atomicAdd(&p.epi_stats[2 * first + 1], s_stats[1]);
@@ -364,7 +434,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           s_stats[0] = s_stats[1] = s_stats[2] = s_stats[3] = 0.0;
         }
-        asm volatile("bar.sync 1, 128;" ::: "memory");
+        asm volatile("bar.sync 1, 256;" ::: "memory");
       }
     }
   }
