@@ -135,6 +135,8 @@ __global__ void __launch_bounds__(256) conv_gemm_kernel(const ConvParams p) {
     const int64_t orow =
         (int64_t)b * p.o_bs + (int64_t)s_y[m] * p.o_ys + (int64_t)s_x[m] * p.o_xs + p.o_off;
     (void)pos;
+    // columns stored for this row (o_lim clips the positions 4x + i >= o_lim)
+    const int ncol = p.o_lim ? min(p.N, max(0, (p.o_lim - 4 * s_x[m]) * p.o_lim_ch)) : p.N;
     float v[TN];
 #pragma unroll
     for (int j = 0; j < TN; ++j) v[j] = acc[i][j] + bias[j];
@@ -152,7 +154,7 @@ __global__ void __launch_bounds__(256) conv_gemm_kernel(const ConvParams p) {
 #pragma unroll
         for (int j = 0; j < TN; ++j) {
           const int n = nb + j;
-          if (n >= p.vt_col0 && n < p.N) {
+          if (n >= p.vt_col0 && n < ncol) {
             const int c = n - p.vt_col0;
             p.vt_out[((bb * 8 + c / 64) * 64 + c % 64) * (int64_t)p.vt_ntok + tok] = v[j];
           }
@@ -162,22 +164,22 @@ __global__ void __launch_bounds__(256) conv_gemm_kernel(const ConvParams p) {
         const float* ad = p.epi_add + orow + nb;
 #pragma unroll
         for (int j = 0; j < TN; ++j)
-          if (nb + j < p.N) v[j] += ad[j];
+          if (nb + j < ncol) v[j] += ad[j];
       }
       float* o = p.out + orow + nb;
-      if (nb + TN <= p.N && ((orow & 3) == 0)) {
+      if (nb + TN <= ncol && ((orow & 3) == 0)) {
         *reinterpret_cast<float4*>(o) = make_float4(v[0], v[1], v[2], v[3]);
       } else {
 #pragma unroll
         for (int j = 0; j < TN; ++j)
-          if (nb + j < p.N) o[j] = v[j];
+          if (nb + j < ncol) o[j] = v[j];
       }
     }
     if (EPI == EPI_GLU || EPI == EPI_GLU_EMB) {
 #pragma unroll
       for (int j = 0; j < TN; j += 2) {
         const int n = nb + j;
-        if (n < p.N) {
+        if (n < ncol) {
           const int c = n / 2;
           float g = v[j] * sigmoid(v[j + 1]);
           if (EPI == EPI_GLU_EMB) g += p.epi_emb[(int64_t)s_y[m] * (p.N / 2) + c];
@@ -190,7 +192,7 @@ __global__ void __launch_bounds__(256) conv_gemm_kernel(const ConvParams p) {
       const float* r = p.epi_res + orow + nb;
 #pragma unroll
       for (int j = 0; j < TN; ++j)
-        if (nb + j < p.N) {
+        if (nb + j < ncol) {
           v[j] = r[j] + p.epi_gamma[nb + j] * v[j];
           o[j] = v[j];
         }
@@ -199,7 +201,7 @@ __global__ void __launch_bounds__(256) conv_gemm_kernel(const ConvParams p) {
       const int slot = (int)(pos / rowlen - r0);
 #pragma unroll
       for (int j = 0; j < TN; ++j)
-        if (nb + j < p.N) {
+        if (nb + j < ncol) {
           const double d = v[j];
           ls[slot] += d;
           lq[slot] += d * d;

@@ -64,6 +64,9 @@ struct ConvParams {
   // 64-wide head, vt[((b*heads + h)*64 + d)*vt_ntok + token] (attention's V^T)
   float* vt_out;
   int vt_col0, vt_ntok;
+  // o_lim > 0: output position x (along W) holds groups of o_lim_ch columns
+  // for positions 4x, 4x+1, ...; columns of positions >= o_lim are not stored
+  int o_lim, o_lim_ch;
 };
 
 void launch_conv_gemm(const ConvParams& p, int pro, int epi, cudaStream_t stream);

@@ -182,6 +182,7 @@ struct Packed {
   bool has_tc = false;
   int cin = 0;       // input channels as packed (zero rows pad it to a multiple of 16)
   int cin_real = 0;  // the layer's own input channels (for the work count)
+  double flop_scale = 1.0;  // algorithmic share of the packed K (structural zeros excluded)
   int K = 0, Kpad = 0, N = 0, Npad = 0;
   std::vector<Tap> taps;
   const float* w = nullptr;
@@ -229,6 +230,7 @@ struct EncW {
 struct DecW {
   Packed rewrite;
   Packed convt[4];  // per output phase
+  Packed convt_all;  // the four phases side by side (see Loader::convt_all)
   DConvW dconv;
   int cin = 0, cout = 0;
 };
@@ -353,6 +355,32 @@ struct Loader {
                   return w.data[((size_t)ci * cout + co) * k + kf[phase][tap]];
                 },
                 taps);
+  }
+
+  // All four output phases of the stride-4 ConvTranspose in one GEMM over the
+  // input positions q: taps q-1, q, q+1 (K = 3 Cin), columns phase * Cout + co;
+  // weights a phase does not use are zero (output 4q + phase reads q + dq).
+  Packed convt_all(const std::string& prefix, std::vector<int64_t> shape) {
+    const HostTensor& w = get(prefix + ".weight", shape);
+    const int cin = (int)shape[0], cout = (int)shape[1];
+    const HostTensor& b = get(prefix + ".bias", {cout});
+    const int k = (int)shape[2];
+    static const int kf[4][2] = {{2, 6}, {3, 7}, {0, 4}, {1, 5}};
+    static const int dq[4][2] = {{0, -1}, {0, -1}, {1, 0}, {1, 0}};
+    std::vector<float> bias4(4 * (size_t)cout);
+    for (int ph = 0; ph < 4; ++ph)
+      for (int co = 0; co < cout; ++co) bias4[ph * cout + co] = b.data[co];
+    Packed p = pack(3, cin, 4 * cout, false, bias4.data(),
+                    [&](int tap, int ci, int n) {
+                      const int ph = n / cout, co = n - ph * cout;
+                      for (int u = 0; u < 2; ++u)
+                        if (dq[ph][u] == tap - 1)
+                          return w.data[((size_t)ci * cout + co) * k + kf[ph][u]];
+                      return 0.0f;
+                    },
+                    {{-1, 0}, {0, 0}, {1, 0}});
+    p.flop_scale = 2.0 / 3.0;  // each phase uses two of the three taps
+    return p;
   }
 
   Packed linear(const std::string& wname, const std::string& bname, int out, int in, int row0,
@@ -502,7 +530,7 @@ struct dmx_handle {
       if (pro == PRO_ADD) bytes += 4.0 * p.B * p.Hin * p.Win * cin;
       bytes += 4.0 * M * nout;
       if (epi == EPI_RESIDUAL) bytes += 4.0 * M * nout;
-      mark(tag, 2.0 * M * K * p.N, bytes);
+      mark(tag, 2.0 * M * K * p.N * (pk ? pk->flop_scale : 1.0), bytes);
     }
     if (pk && (cfg.precision == DMX_TF32 || cfg.precision == DMX_TF32X3) &&
         try_tc(p, pro, epi, *pk))
@@ -581,6 +609,8 @@ struct dmx_handle {
     t.vt_out = p.vt_out;
     t.vt_col0 = p.vt_col0;
     t.vt_ntok = p.vt_ntok;
+    t.o_lim = p.o_lim;
+    t.o_lim_ch = p.o_lim_ch;
     t.err = err;
     if (!tc_gemm_supported(a, t)) return false;
     launch_tc_gemm(a, wdev + pk.tc_off,
@@ -1032,29 +1062,38 @@ void forward(dmx_handle* h, const float* mix, int G, float* out) {
       run_dconv(h, h->dec_dc[e], g, G * F, kFrames);
       const int Co = Dw.cout, Fo = 4 * F;
       float* o = h->falloc((size_t)G * Fo * kFrames * Co);
-      for (int ph = 0; ph < 4; ++ph) {
-        ConvParams p = base_params(Dw.convt[ph], h->wdev);
+      if (last) {
+        // the spectrogram for the iSTFT, frame-major (b, t, f, c): one GEMM
+        // over the input rows, whose 4 x Co outputs (f = 4 f_in + phase) are
+        // contiguous
+        ConvParams p = base_params(Dw.convt_all, h->wdev);
         set_input(p, g, G, F, kFrames, C);
         p.B = G;
         p.Hq = F;
         p.Wq = kFrames;
         p.out = o;
         p.o_bs = (int64_t)Fo * kFrames * Co;
-        if (!last) {
+        p.o_xs = (int64_t)Fo * Co;
+        p.o_ys = 4LL * Co;
+        p.o_off = 0;
+        h->gemm(p, PRO_NONE, EPI_STORE, ("dec.convtr" + std::to_string(e)).c_str(), &Dw.convt_all);
+      } else {
+        for (int ph = 0; ph < 4; ++ph) {
           // (b, f, t, c) with f = 4 f_in + phase
+          ConvParams p = base_params(Dw.convt[ph], h->wdev);
+          set_input(p, g, G, F, kFrames, C);
+          p.B = G;
+          p.Hq = F;
+          p.Wq = kFrames;
+          p.out = o;
+          p.o_bs = (int64_t)Fo * kFrames * Co;
           p.o_xs = Co;
           p.o_ys = 4LL * kFrames * Co;
           p.o_off = (int64_t)ph * kFrames * Co;
           p.epi_add = skip[j - 1];
-        } else {
-          // the spectrogram for the iSTFT, frame-major (b, t, f, c): one
-          // frame's bins are contiguous
-          p.o_xs = (int64_t)Fo * Co;
-          p.o_ys = 4LL * Co;
-          p.o_off = (int64_t)ph * Co;
+          h->gemm(p, PRO_NONE, EPI_GELU, ("dec.convtr" + std::to_string(e)).c_str(),
+                  &Dw.convt[ph]);
         }
-        h->gemm(p, PRO_NONE, last ? EPI_STORE : EPI_GELU, ("dec.convtr" + std::to_string(e)).c_str(),
-                &Dw.convt[ph]);
       }
       x = o;
       F = Fo;
@@ -1074,27 +1113,29 @@ void forward(dmx_handle* h, const float* mix, int G, float* out) {
       run_dconv(h, h->tdec_dc[e], g, G, Tc);
       const int Co = Dw.cout, len = lengths_t[j];
       float* o = h->falloc((size_t)G * len * Co);
-      for (int ph = 0; ph < 4; ++ph) {
-        const int nq = (len - ph + 3) / 4;
-        if (nq <= 0) continue;
-        ConvParams p = base_params(Dw.convt[ph], h->wdev);
+      {
+        // all four phases in one GEMM over the input positions t: outputs
+        // 4t + phase are contiguous in (b, len, c); the last input position's
+        // phases beyond len are clipped
+        ConvParams p = base_params(Dw.convt_all, h->wdev);
         set_input(p, g, G, 1, Tc, Ct);
-        // taps move along time for the waveform branch
-        for (int t = 0; t < p.ntaps; ++t) {
+        for (int t = 0; t < p.ntaps; ++t) {  // taps move along time for the waveform branch
           p.dx[t] = p.dy[t];
           p.dy[t] = 0;
         }
         p.B = G;
         p.Hq = 1;
-        p.Wq = nq;
+        p.Wq = Tc;
         p.out = o;
+        p.o_bs = (int64_t)len * Co;
         p.o_xs = 4LL * Co;
         p.o_ys = 0;
-        p.o_off = (int64_t)ph * Co;
-        p.o_bs = (int64_t)len * Co;
+        p.o_off = 0;
+        p.o_lim = len;
+        p.o_lim_ch = Co;
         if (!last) p.epi_add = tskip[j - 1];
         h->gemm(p, PRO_NONE, last ? EPI_STORE : EPI_GELU, ("tdec.convtr" + std::to_string(e)).c_str(),
-                &Dw.convt[ph]);
+                &Dw.convt_all);
       }
       xt = o;
       Tc = len;
@@ -1260,13 +1301,17 @@ void load_model(dmx_handle* h, const std::map<std::string, HostTensor>& t) {
         t9.push_back({ky - 1, kx - 1});
       }
     m.dec[e].rewrite = L.conv(d + ".rewrite", {2 * cin, cin, 3, 3}, k9, t9, true);
-    for (int ph = 0; ph < 4; ++ph) m.dec[e].convt[ph] = L.convt(d + ".conv_tr", {cin, cout_f, 8, 1}, ph);
+    if (e == 3)  // the last one writes the frame-major spectrogram: phases contiguous
+      m.dec[e].convt_all = L.convt_all(d + ".conv_tr", {cin, cout_f, 8, 1});
+    else
+      for (int ph = 0; ph < 4; ++ph)
+        m.dec[e].convt[ph] = L.convt(d + ".conv_tr", {cin, cout_f, 8, 1}, ph);
     m.dec[e].cin = cin;
     m.dec[e].cout = cout_f;
     load_dc(d, cin, &h->dec_dc[e]);
     m.tdec[e].rewrite = L.conv(td + ".rewrite", {2 * cin, cin, 3}, {{0, 0}, {0, 1}, {0, 2}},
                                {{0, -1}, {0, 0}, {0, 1}}, true);
-    for (int ph = 0; ph < 4; ++ph) m.tdec[e].convt[ph] = L.convt(td + ".conv_tr", {cin, cout_t, 8}, ph);
+    m.tdec[e].convt_all = L.convt_all(td + ".conv_tr", {cin, cout_t, 8});
     m.tdec[e].cin = cin;
     m.tdec[e].cout = cout_t;
     load_dc(td, cin, &h->tdec_dc[e]);

@@ -259,6 +259,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         x = (int)(rem % p.Wq);
       }
       const int64_t orow = (int64_t)b * p.o_bs + (int64_t)y * p.o_ys + (int64_t)x * p.o_xs + p.o_off;
+      // columns stored for this row (o_lim clips the positions 4x + i >= o_lim)
+      const int ncol = p.o_lim ? min(p.N, max(0, (p.o_lim - 4 * x) * p.o_lim_ch)) : p.N;
       double ls = 0.0, lq = 0.0;
       const uint32_t tacc = tmem + lane_base + (uint32_t)(acc * BN);
       for (int c0 = 32 * hh; c0 < BN; c0 += 64) {
@@ -266,9 +268,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         __syncwarp();
         tmem_ld32(tacc + (uint32_t)c0, v);
         const int nb = n0 + c0;
-        if (ok && valid && nb < p.N) {
+        if (ok && valid && nb < ncol) {
           // a full chunk whose row segment is 16-byte aligned moves as float4
-          const bool full = nb + 32 <= p.N;
+          const bool full = nb + 32 <= ncol;
           const bool bias4 = full && ((reinterpret_cast<uintptr_t>(p.bias + nb) & 15) == 0);
           if (bias4) {
 #pragma unroll
@@ -281,7 +283,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
           } else {
             for (int j = 0; j < 32; ++j)
-              if (nb + j < p.N) v[j] += p.bias[nb + j];
+              if (nb + j < ncol) v[j] += p.bias[nb + j];
           }
           if (EPI == EPI_STORE || EPI == EPI_GELU) {
             if (EPI == EPI_GELU) {
@@ -298,7 +300,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               const int64_t bb = pos / p.vt_ntok, tok = pos % p.vt_ntok;
               float* vt = p.vt_out + ((bb * 8 + h2) * 64 + d0) * (int64_t)p.vt_ntok + tok;
               for (int j = 0; j < 32; ++j)
-                if (nb + j < p.N) vt[(int64_t)j * p.vt_ntok] = v[j];
+                if (nb + j < ncol) vt[(int64_t)j * p.vt_ntok] = v[j];
             }
             const bool vec = full && ((orow + nb) & 3) == 0;
             if (p.epi_add) {
@@ -314,7 +316,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
               } else {
                 for (int j = 0; j < 32; ++j)
-                  if (nb + j < p.N) v[j] += ad[j];
+                  if (nb + j < ncol) v[j] += ad[j];
               }
             }
             float* o = p.out + orow + nb;
@@ -324,7 +326,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 *reinterpret_cast<float4*>(o + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
             } else {
               for (int j = 0; j < 32; ++j)
-                if (nb + j < p.N) o[j] = v[j];
+                if (nb + j < ncol) o[j] = v[j];
             }
           }
           if (EPI == EPI_GLU || EPI == EPI_GLU_EMB) {
@@ -347,7 +349,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
               } else {
                 for (int j = 0; j < 16; ++j)
-                  if (nb + 2 * j < p.N) g[j] += em[j];
+                  if (nb + 2 * j < ncol) g[j] += em[j];
               }
             }
             float* o = p.out + orow + c0o;
@@ -357,7 +359,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 *reinterpret_cast<float4*>(o + j) = make_float4(g[j], g[j + 1], g[j + 2], g[j + 3]);
             } else {
               for (int j = 0; j < 16; ++j)
-                if (nb + 2 * j < p.N) o[j] = g[j];
+                if (nb + 2 * j < ncol) o[j] = g[j];
             }
           }
           if (EPI == EPI_RESIDUAL) {
@@ -378,7 +380,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               }
             } else {
               for (int j = 0; j < 32; ++j)
-                if (nb + j < p.N) {
+                if (nb + j < ncol) {
                   v[j] = rr[j] + p.epi_gamma[nb + j] * v[j];
                   o[j] = v[j];
                 }
@@ -387,7 +389,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (kStats) {
             float fs = 0.f, fq = 0.f;
             for (int j = 0; j < 32; ++j)
-              if (nb + j < p.N) {
+              if (nb + j < ncol) {
                 fs += v[j];
                 fq = fmaf(v[j], v[j], fq);
               }

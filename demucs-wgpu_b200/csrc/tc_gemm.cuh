@@ -45,6 +45,7 @@ struct TcParams {
   int round_out;  // EPI_STORE: round stored values to nearest tf32 (attention operands)
   float* vt_out;  // EPI_STORE: V^T copy of columns >= vt_col0 (see ConvParams)
   int vt_col0, vt_ntok;
+  int o_lim, o_lim_ch;  // as in ConvParams
   int* err;  // set non-zero when a bounded wait gives up
   int mtiles, ntiles;  // tile space (filled in by launch_tc_gemm)
 };
