@@ -27,7 +27,11 @@ enum EpiMode : int {
   EPI_GELU = 1,           // gelu(acc + bias)
   EPI_GLU = 2,            // value * sigmoid(gate), columns interleaved (2c, 2c+1)
   EPI_GLU_EMB = 3,        // GLU + emb[y, c]
-  EPI_RESIDUAL = 4        // out = res + gamma[n] * (acc + bias) [+ row moments]
+  EPI_RESIDUAL = 4,       // out = res + gamma[n] * (acc + bias) [+ row moments]
+  // tensor-core path only (the DConv branch as GEMMs, see dmx_handle::run_dconv):
+  EPI_STORE_STATS = 5,    // store acc + bias and accumulate its row moments
+  EPI_STATS = 6,          // row moments of acc + bias, nothing stored
+  EPI_DCONV_TAIL = 7      // out[c] = res[c] + gamma[c] * GLU(GroupNorm(acc + bias))
 };
 
 struct ConvParams {

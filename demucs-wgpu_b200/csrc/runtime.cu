@@ -539,15 +539,26 @@ struct dmx_handle {
   }
 
   // The tensor-core path takes a launch when its A operand is a plain
-  // channels-last tile read (no prologue transform) with stride-1 taps.
+  // channels-last tile read (no prologue transform) with stride-1 taps (or
+  // the strided encoder taps).
   bool try_tc(const ConvParams& p, int pro, int epi, const Packed& pk) {
     if (pro != PRO_NONE || !pk.has_tc || p.i_cs != 1) return false;
     if (epi != EPI_STORE && epi != EPI_GELU && epi != EPI_GLU && epi != EPI_GLU_EMB &&
         epi != EPI_RESIDUAL)
       return false;
-    TcParams t;
-    std::memset(&t, 0, sizeof(t));
     TcOperandA a;
+    TcParams t;
+    if (!build_tc(p, pk, a, t)) return false;
+    launch_tc_gemm(a, wdev + pk.tc_off,
+                   cfg.precision == DMX_TF32X3 ? wdev + pk.tc_lo_off : nullptr, t, epi, stream);
+    ++tc_launches;
+    return true;
+  }
+
+  // ConvParams -> tensor-core operand and parameters; false when unsupported.
+  bool build_tc(const ConvParams& p, const Packed& pk, TcOperandA& a, TcParams& t) {
+    if (!pk.has_tc || p.i_cs != 1) return false;
+    std::memset(&t, 0, sizeof(t));
     a.ptr = p.x;
     a.C = p.Cin;
     bool taps_zero = true;
@@ -612,11 +623,7 @@ struct dmx_handle {
     t.o_lim = p.o_lim;
     t.o_lim_ch = p.o_lim_ch;
     t.err = err;
-    if (!tc_gemm_supported(a, t)) return false;
-    launch_tc_gemm(a, wdev + pk.tc_off,
-                   cfg.precision == DMX_TF32X3 ? wdev + pk.tc_lo_off : nullptr, t, epi, stream);
-    ++tc_launches;
-    return true;
+    return tc_gemm_supported(a, t);
   }
 
   void after(const char* what) {
@@ -672,12 +679,93 @@ void set_output(ConvParams& p, float* out, int B, int Hq, int Wq, int Cout) {
 // (host.rs:985-1059): per layer one fused launch for rows of at most one tile
 // (the spectral branch), three tiled launches for longer rows (the waveform
 // branch); the kernels are in dconv.cu.
+// One tensor-core GEMM of the DConv branch, always split 3xTF32 (the branch
+// stays fp32-accurate in every build); `ext` supplies the A transform and the
+// DConv epilogue fields.
+void dconv_gemm(dmx_handle* h, const ConvParams& p, int epi, const Packed& pk, const TcParams& ext) {
+  TcOperandA a;
+  TcParams t;
+  if (!h->build_tc(p, pk, a, t)) throw Error(DMX_ERR_INVALID, "dconv: tensor-core shape unsupported");
+  t.epi_nstats = ext.epi_nstats;
+  t.epi_count = ext.epi_count;
+  t.epi_gw = ext.epi_gw;
+  t.epi_gb = ext.epi_gb;
+  t.epi_half = ext.epi_half;
+  t.a_stats = ext.a_stats;
+  t.a_rowlen = ext.a_rowlen;
+  t.a_nvalid = ext.a_nvalid;
+  t.a_count = ext.a_count;
+  t.a_gw = ext.a_gw;
+  t.a_gb = ext.a_gb;
+  launch_tc_gemm(a, h->W(pk.tc_off), h->W(pk.tc_lo_off), t, epi, h->stream);
+  ++h->tc_launches;
+}
+
+// The DConv branch as three persistent tensor-core GEMMs per layer, for rows
+// of any length: conv1 (taps as TMA offsets) storing y and its row moments;
+// conv2 with GELU(GroupNorm1(y)) applied to each A tile by the converter
+// warps, epilogue = row moments of z; conv2 again, epilogue = GroupNorm2 +
+// GLU + LayerScale + residual into x. Moments are f64 atomics per row.
+void run_dconv_gemm(dmx_handle* h, const DConvFull& dc, float* x, int rows, int T) {
+  const int C = dc.C, hid = dc.hidden;
+  const int64_t positions = (int64_t)rows * T;
+  const int kg = dc.layer[0].conv2.K;  // y row width = conv2's padded K
+  float* y = h->falloc((size_t)positions * kg);
+  double* st = h->dalloc((size_t)rows * 4);
+  for (int d = 0; d < 2; ++d) {
+    const DConvLayerW& L = dc.layer[d];
+    h->mark("dconv.gemm" + std::to_string(C), 10.0 * positions * C * hid, 8.0 * positions * C);
+    h->launches += 3;
+    if (!h->live()) continue;
+    CK(cudaMemsetAsync(st, 0, (size_t)rows * 4 * sizeof(double), h->stream));
+    TcParams ext;
+    std::memset(&ext, 0, sizeof(ext));
+    {  // conv1: x (rows, T, C) -> y (rows, T, kg), the first hid columns
+      ConvParams p = base_params(L.conv1, h->wdev);
+      set_input(p, x, rows, 1, T, C);
+      set_output(p, y, rows, 1, T, kg);
+      p.epi_stats = st;
+      p.epi_rowlen = T;
+      dconv_gemm(h, p, EPI_STORE_STATS, L.conv1, ext);
+    }
+    ConvParams q = base_params(L.conv2, h->wdev);
+    set_input(q, y, 1, 1, (int)positions, kg);
+    set_output(q, x, 1, 1, (int)positions, C);
+    q.epi_rowlen = T;
+    ext.a_stats = st;
+    ext.a_rowlen = T;
+    ext.a_nvalid = hid;
+    ext.a_count = (double)hid * T;
+    ext.a_gw = h->W(L.n1w.off);
+    ext.a_gb = h->W(L.n1b.off);
+    q.epi_stats = st + 2 * rows;  // pass 1: moments of z
+    dconv_gemm(h, q, EPI_STATS, L.conv2, ext);
+    q.epi_stats = nullptr;  // pass 2: the output
+    ext.epi_nstats = st + 2 * rows;
+    ext.epi_count = 2.0 * C * T;
+    ext.epi_gw = h->W(L.n2w.off);
+    ext.epi_gb = h->W(L.n2b.off);
+    ext.epi_half = C;
+    q.epi_gamma = h->W(L.gamma.off);
+    q.epi_res = x;
+    dconv_gemm(h, q, EPI_DCONV_TAIL, L.conv2, ext);
+    h->after("dconv");
+  }
+}
+
 void run_dconv(dmx_handle* h, const DConvFull& dc, float* x, int rows, int T) {
   const int C = dc.C, hid = dc.hidden;
   const int64_t positions = (int64_t)rows * T;
-  // TF32 builds: tensor cores (3xTF32, fp32-accurate) where the kernel covers the shape
-  const bool tc = (h->cfg.precision == DMX_TF32 || h->cfg.precision == DMX_TF32X3) &&
-                  dconv_tc_supported(C, T) && dc.layer[0].conv1.has_tc && dc.layer[0].conv2.has_tc;
+  const bool tf32 = h->cfg.precision == DMX_TF32 || h->cfg.precision == DMX_TF32X3;
+  const bool has_tc = dc.layer[0].conv1.has_tc && dc.layer[0].conv2.has_tc;
+  // TF32 builds: tensor cores (3xTF32, fp32-accurate) for the narrow spectral
+  // layers (fused row kernel) and the widest layers (three GEMMs, where the
+  // SIMT kernels are compute-bound); the SIMT kernels are faster elsewhere
+  const bool tc = tf32 && has_tc && dconv_tc_supported(C, T);
+  if (tf32 && has_tc && !tc && C >= 384) {
+    run_dconv_gemm(h, dc, x, rows, T);
+    return;
+  }
   const bool fused = tc || dconv_row_fused(T);
   const int tiles = dconv_tiles(T);
   float* y = fused ? nullptr : h->falloc((size_t)positions * hid);

@@ -190,6 +190,18 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint32_t it = 0;
     bool live = true;
     for (int t = blockIdx.x; t < total; t += gridDim.x) {
+      // optional A transform (TC_ROWS): GELU(GroupNorm(a)) with this row's moments
+      float a_mean = 0.f, a_inv = 0.f;
+      bool a_row = false;
+      if (p.a_stats) {
+        const int64_t pos = (int64_t)(t / p.ntiles) * BM + row;
+        a_row = pos < (int64_t)p.B * p.Hq * p.Wq;
+        if (a_row) {
+          const RowNorm rn = row_norm(p.a_stats, (int)(pos / p.a_rowlen), p.a_count);
+          a_mean = rn.mean;
+          a_inv = rn.inv;
+        }
+      }
       for (int kt = 0; kt < ktiles; ++kt, ++it) {
         const int s = it % STAGES;
         const uint32_t ph = (it / STAGES) & 1;
@@ -201,7 +213,21 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int qq = 0; qq < BK / 4; ++qq) {
             const int q = qq ^ swz;
-            const float4 x = a[q];
+            float4 x = a[q];
+            if (p.a_stats) {
+              float xv[4] = {x.x, x.y, x.z, x.w};
+#pragma unroll
+              for (int e = 0; e < 4; ++e) {
+                const int k = kt * BK + qq * 4 + e;
+                float g = 0.f;
+                if (a_row && k < p.a_nvalid) {
+                  const float scale = a_inv * p.a_gw[k];
+                  g = gelu(xv[e] * scale + (p.a_gb[k] - a_mean * scale));
+                }
+                xv[e] = g;
+              }
+              x = make_float4(xv[0], xv[1], xv[2], xv[3]);
+            }
             float4 hi;
             hi.x = round_tf32(x.x);
             hi.y = round_tf32(x.y);
@@ -223,7 +249,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int e = warp - 6, quarter = warp % 4, hh = e / 4;
     const int r = quarter * 32 + lane;
     const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
-    constexpr bool kStats = EPI == EPI_RESIDUAL;
+    constexpr bool kStats = EPI == EPI_RESIDUAL || EPI == EPI_STORE_STATS || EPI == EPI_STATS;
     bool ok = true;
     int tl = 0;
     for (int t = blockIdx.x; t < total; t += gridDim.x, ++tl) {
@@ -285,7 +311,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int j = 0; j < 32; ++j)
               if (nb + j < ncol) v[j] += p.bias[nb + j];
           }
-          if (EPI == EPI_STORE || EPI == EPI_GELU) {
+          if (EPI == EPI_STORE || EPI == EPI_GELU || EPI == EPI_STORE_STATS) {
             if (EPI == EPI_GELU) {
 #pragma unroll
               for (int j = 0; j < 32; ++j) v[j] = gelu(v[j]);
@@ -360,6 +386,46 @@ __global__ void __launch_bounds__(kThreads, 1)
             } else {
               for (int j = 0; j < 16; ++j)
                 if (nb + 2 * j < ncol) o[j] = g[j];
+            }
+          }
+          if (EPI == EPI_DCONV_TAIL) {
+            // channels nb/2 .. nb/2 + 15: out = res + gamma * GLU(GroupNorm(v))
+            const RowNorm nr = row_norm(p.epi_nstats, (int)(pos / p.epi_rowlen), p.epi_count);
+            const int c0o = nb / 2;
+            float* o = p.out + orow + c0o;
+            const float* rr = p.epi_res + orow + c0o;
+            const bool vec = full && ((orow + c0o) & 3) == 0;
+            float res[16];
+            if (vec) {
+#pragma unroll
+              for (int j = 0; j < 16; j += 4) {
+                const float4 r4 = *reinterpret_cast<const float4*>(rr + j);
+                res[j] = r4.x;
+                res[j + 1] = r4.y;
+                res[j + 2] = r4.z;
+                res[j + 3] = r4.w;
+              }
+            } else {
+              for (int j = 0; j < 16; ++j) res[j] = nb + 2 * j < ncol ? rr[j] : 0.f;
+            }
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+              const int c = c0o + j;
+              if (nb + 2 * j < ncol) {
+                const float vs = nr.inv * p.epi_gw[c];
+                const float gsc = nr.inv * p.epi_gw[c + p.epi_half];
+                const float value = v[2 * j] * vs + (p.epi_gb[c] - nr.mean * vs);
+                const float gate = v[2 * j + 1] * gsc + (p.epi_gb[c + p.epi_half] - nr.mean * gsc);
+                res[j] += p.epi_gamma[c] * (value * sigmoid(gate));
+              }
+            }
+            if (vec) {
+#pragma unroll
+              for (int j = 0; j < 16; j += 4)
+                *reinterpret_cast<float4*>(o + j) = make_float4(res[j], res[j + 1], res[j + 2], res[j + 3]);
+            } else {
+              for (int j = 0; j < 16; ++j)
+                if (nb + 2 * j < ncol) o[j] = res[j];
             }
           }
           if (EPI == EPI_RESIDUAL) {
@@ -473,6 +539,9 @@ void launch_cfg(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap&
     DMX_TC_CASE(EPI_GLU)
     DMX_TC_CASE(EPI_GLU_EMB)
     DMX_TC_CASE(EPI_RESIDUAL)
+    DMX_TC_CASE(EPI_STORE_STATS)
+    DMX_TC_CASE(EPI_STATS)
+    DMX_TC_CASE(EPI_DCONV_TAIL)
   }
 #undef DMX_TC_CASE
 }

@@ -46,6 +46,22 @@ struct TcParams {
   float* vt_out;  // EPI_STORE: V^T copy of columns >= vt_col0 (see ConvParams)
   int vt_col0, vt_ntok;
   int o_lim, o_lim_ch;  // as in ConvParams
+  // EPI_DCONV_TAIL: row moments of the GLU input (sum, sum of squares per
+  // row of epi_rowlen positions, count values each), GroupNorm weight/bias in
+  // the reference's order (value c, gate c + epi_half)
+  const double* epi_nstats;
+  double epi_count;
+  const float* epi_gw;
+  const float* epi_gb;
+  int epi_half;
+  // A transform in the converter (TC_ROWS): a = GELU(GroupNorm(a)) with row
+  // moments a_stats (rows of a_rowlen positions, a_count values) and per-
+  // channel a_gw / a_gb for channels < a_nvalid; channels >= a_nvalid are 0
+  const double* a_stats;
+  int a_rowlen, a_nvalid;
+  double a_count;
+  const float* a_gw;
+  const float* a_gb;
   int* err;  // set non-zero when a bounded wait gives up
   int mtiles, ntiles;  // tile space (filled in by launch_tc_gemm)
 };
