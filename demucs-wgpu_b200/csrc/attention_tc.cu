@@ -247,9 +247,11 @@ __global__ void __launch_bounds__(192, 2)
       const float inv = l > 0.f ? 1.0f / l : 0.f;
       float* o = p.out + (int64_t)(b * p.nq + q0 + r) * p.ldo + h * HD;
 #pragma unroll
+      // the output feeds only the tf32 out-projection: rounded to nearest here
       for (int i = 0; i < HD; i += 4)
         *reinterpret_cast<float4*>(o + i) =
-            make_float4(ov[i] * inv, ov[i + 1] * inv, ov[i + 2] * inv, ov[i + 3] * inv);
+            make_float4(round_tf32(ov[i] * inv), round_tf32(ov[i + 1] * inv),
+                        round_tf32(ov[i + 2] * inv), round_tf32(ov[i + 3] * inv));
     }
   }
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");

@@ -71,6 +71,7 @@ struct ConvParams {
   // o_lim > 0: output position x (along W) holds groups of o_lim_ch columns
   // for positions 4x, 4x+1, ...; columns of positions >= o_lim are not stored
   int o_lim, o_lim_ch;
+  int a_rounded;  // tensor-core path: A already holds tf32-rounded values (no converter pass)
 };
 
 void launch_conv_gemm(const ConvParams& p, int pro, int epi, cudaStream_t stream);

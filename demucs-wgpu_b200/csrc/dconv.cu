@@ -245,7 +245,8 @@ DMX_DEVICE void conv2_tile(const float* gs, int np, const DConvArgs& a, float* x
       const float value = v * vs + vsh;
       const float gate = gt * gsc + gsh;
       float* o = xt + (int64_t)p * C + c;
-      *o = *o + gamma * (value * sigmoid(gate));
+      const float r = *o + gamma * (value * sigmoid(gate));
+      *o = a.round_out ? round_tf32(r) : r;
     } else {
       // short f32 runs (8 positions, 16 terms) folded into f64
       fs += v + gt;

@@ -529,6 +529,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const float gate = fmaf(z[2 * k + 1], f.z, f.w);
                 o[k] += __fdividef(value, 1.0f + __expf(-gate));
               }
+              if (a.round_out) {
+#pragma unroll
+                for (int k = 0; k < 8; ++k) o[k] = round_tf32(o[k]);
+              }
               float4* x4 = reinterpret_cast<float4*>(xp + 8 * sc);
               x4[0] = make_float4(o[0], o[1], o[2], o[3]);
               x4[1] = make_float4(o[4], o[5], o[6], o[7]);

@@ -42,6 +42,7 @@ struct DConvArgs {
   double* part1;
   double* part2;
   int* err;  // raised when a bounded wait gives up
+  int round_out;  // store the updated x rounded to nearest tf32 (it feeds only tf32 GEMMs)
   // tensor-core path (dconv_tc.cu): K-major weights rounded to nearest tf32
   // ([w1_npad][3C], [w2_npad][16]) and their residuals w - tf32(w)
   const float* w1_tc;
@@ -58,8 +59,9 @@ bool dconv_tc_supported(int C, int T);
 bool launch_dconv_tc(const DConvArgs& a, cudaStream_t s);
 
 // transformer.cu
+// round_out: store the output rounded to nearest tf32 (when it feeds only tf32 GEMMs)
 void launch_layer_norm(const float* x, int64_t rows, int ntok, const float* w, const float* b,
-                       const float* pos, float* out, cudaStream_t s);
+                       const float* pos, float* out, cudaStream_t s, bool round_out = false);
 void launch_group_norm_apply(float* x, int B, int64_t ntok, const double* stats, const float* w,
                              const float* b, cudaStream_t s);
 void launch_flash_attention(const float* q, int ldq, const float* k, const float* v, int ldkv,

@@ -622,6 +622,7 @@ struct dmx_handle {
     t.vt_ntok = p.vt_ntok;
     t.o_lim = p.o_lim;
     t.o_lim_ch = p.o_lim_ch;
+    t.a_rounded = p.a_rounded;
     t.err = err;
     return tc_gemm_supported(a, t);
   }
@@ -706,7 +707,8 @@ void dconv_gemm(dmx_handle* h, const ConvParams& p, int epi, const Packed& pk, c
 // conv2 with GELU(GroupNorm1(y)) applied to each A tile by the converter
 // warps, epilogue = row moments of z; conv2 again, epilogue = GroupNorm2 +
 // GLU + LayerScale + residual into x. Moments are f64 atomics per row.
-void run_dconv_gemm(dmx_handle* h, const DConvFull& dc, float* x, int rows, int T) {
+void run_dconv_gemm(dmx_handle* h, const DConvFull& dc, float* x, int rows, int T,
+                    bool round_out) {
   const int C = dc.C, hid = dc.hidden;
   const int64_t positions = (int64_t)rows * T;
   const int kg = dc.layer[0].conv2.K;  // y row width = conv2's padded K
@@ -748,12 +750,15 @@ void run_dconv_gemm(dmx_handle* h, const DConvFull& dc, float* x, int rows, int 
     ext.epi_half = C;
     q.epi_gamma = h->W(L.gamma.off);
     q.epi_res = x;
+    q.round_out = round_out && d == 1;
     dconv_gemm(h, q, EPI_DCONV_TAIL, L.conv2, ext);
     h->after("dconv");
   }
 }
 
-void run_dconv(dmx_handle* h, const DConvFull& dc, float* x, int rows, int T) {
+// round_out: the branch's output feeds only a tf32 GEMM (the TF32 build): the
+// last layer stores it rounded to nearest tf32 so that GEMM needs no converter.
+void run_dconv(dmx_handle* h, const DConvFull& dc, float* x, int rows, int T, bool round_out) {
   const int C = dc.C, hid = dc.hidden;
   const int64_t positions = (int64_t)rows * T;
   const bool tf32 = h->cfg.precision == DMX_TF32 || h->cfg.precision == DMX_TF32X3;
@@ -763,7 +768,7 @@ void run_dconv(dmx_handle* h, const DConvFull& dc, float* x, int rows, int T) {
   // SIMT kernels are compute-bound); the SIMT kernels are faster elsewhere
   const bool tc = tf32 && has_tc && dconv_tc_supported(C, T);
   if (tf32 && has_tc && !tc && C >= 384) {
-    run_dconv_gemm(h, dc, x, rows, T);
+    run_dconv_gemm(h, dc, x, rows, T, round_out);
     return;
   }
   const bool fused = tc || dconv_row_fused(T);
@@ -795,6 +800,7 @@ void run_dconv(dmx_handle* h, const DConvFull& dc, float* x, int rows, int T) {
     a.part1 = part;
     a.part2 = part ? part + 2 * (size_t)rows * tiles : nullptr;
     a.err = h->err;
+    a.round_out = round_out && d == 1;
     a.w1_tc = h->W(L.conv1.tc_off);
     a.w1_tc_lo = h->W(L.conv1.tc_lo_off);
     a.w1_npad = L.conv1.Npad;
@@ -868,12 +874,19 @@ struct XfBufs {
   double* stats;
 };
 
+// Transformer linear layers. In the TF32 build every A operand here (the
+// LayerNorm outputs, the first FFN layer's GELU output, the attention output)
+// is produced already rounded to nearest tf32, so the GEMM skips its converter
+// pass; the operands are the same values the converter would produce.
+bool xf_rounded(const dmx_handle* h) { return h->cfg.precision == DMX_TF32; }
+
 void xf_gemm(dmx_handle* h, const char* tag, const Packed& pk, const float* in, int B, int n,
              float* out, int epi, const float* res = nullptr, const float* gamma = nullptr,
              double* stats = nullptr, bool round_out = false, float* vt = nullptr,
              int vt_col0 = 0) {
   ConvParams p = base_params(pk, h->wdev);
   p.round_out = round_out;
+  p.a_rounded = xf_rounded(h);
   p.vt_out = vt;
   p.vt_col0 = vt_col0;
   p.vt_ntok = n;
@@ -892,9 +905,12 @@ void xf_tail(dmx_handle* h, const LayerW& L, float* X, int B, int n, const XfBuf
   // out-projection + LayerScale residual
   xf_gemm(h, "xf.outproj", L.out, bb.att, B, n, X, EPI_RESIDUAL, X, h->W(L.g1.off));
   h->mark("xf.layernorm", 0.0, 8.0 * B * n * 512);
-  if (h->live()) launch_layer_norm(X, (int64_t)B * n, n, h->W(nw.off), h->W(nb.off), nullptr, bb.xn, h->stream);
+  if (h->live())
+    launch_layer_norm(X, (int64_t)B * n, n, h->W(nw.off), h->W(nb.off), nullptr, bb.xn, h->stream,
+                      xf_rounded(h));
   ++h->launches;
-  xf_gemm(h, "xf.ffn1", L.lin1, bb.xn, B, n, bb.hid, EPI_GELU);
+  xf_gemm(h, "xf.ffn1", L.lin1, bb.xn, B, n, bb.hid, EPI_GELU, nullptr, nullptr, nullptr,
+          xf_rounded(h));
   h->zero(bb.stats, (size_t)B * 2 * sizeof(double));
   xf_gemm(h, "xf.ffn2", L.lin2, bb.hid, B, n, X, EPI_RESIDUAL, X, h->W(L.g2.off), bb.stats);
   h->mark("xf.groupnorm", 0.0, 8.0 * B * n * 512);
@@ -904,7 +920,8 @@ void xf_tail(dmx_handle* h, const LayerW& L, float* X, int B, int n, const XfBuf
 
 void xf_self(dmx_handle* h, const LayerW& L, float* X, int B, int n, const XfBufs& bb) {
   h->mark("xf.layernorm", 0.0, 8.0 * B * n * 512);
-  if (h->live()) launch_layer_norm(X, (int64_t)B * n, n, h->W(L.n1w.off), h->W(L.n1b.off), nullptr, bb.xn, h->stream);
+  if (h->live()) launch_layer_norm(X, (int64_t)B * n, n, h->W(L.n1w.off), h->W(L.n1b.off), nullptr, bb.xn,
+                                   h->stream, xf_rounded(h));
   ++h->launches;
   const bool tc_attn = h->cfg.precision == DMX_TF32;
   xf_gemm(h, "xf.qkv", L.qkv, bb.xn, B, n, bb.qkv, EPI_STORE, nullptr, nullptr, nullptr, tc_attn,
@@ -925,7 +942,7 @@ void xf_cross_kv(dmx_handle* h, const LayerW& L, const float* other, int B, int 
   h->mark("xf.layernorm", 0.0, 8.0 * B * n_other * 512);
   if (h->live())
     launch_layer_norm(other, (int64_t)B * n_other, n_other, h->W(L.n2w.off), h->W(L.n2b.off), nullptr,
-                      scratch, h->stream);
+                      scratch, h->stream, xf_rounded(h));
   ++h->launches;
   const bool tc_attn = h->cfg.precision == DMX_TF32;
   xf_gemm(h, "xf.kv", L.kv, scratch, B, n_other, kv_out, EPI_STORE, nullptr, nullptr, nullptr,
@@ -935,7 +952,8 @@ void xf_cross_kv(dmx_handle* h, const LayerW& L, const float* other, int B, int 
 void xf_cross(dmx_handle* h, const LayerW& L, float* X, int B, int n, const float* kv,
               const float* vt, int n_other, const XfBufs& bb) {
   h->mark("xf.layernorm", 0.0, 8.0 * B * n * 512);
-  if (h->live()) launch_layer_norm(X, (int64_t)B * n, n, h->W(L.n1w.off), h->W(L.n1b.off), nullptr, bb.xn, h->stream);
+  if (h->live()) launch_layer_norm(X, (int64_t)B * n, n, h->W(L.n1w.off), h->W(L.n1b.off), nullptr, bb.xn,
+                                   h->stream, xf_rounded(h));
   ++h->launches;
   const bool tc_attn = h->cfg.precision == DMX_TF32;
   xf_gemm(h, "xf.q", L.q, bb.xn, B, n, bb.qkv, EPI_STORE, nullptr, nullptr, nullptr, tc_attn);
@@ -1012,11 +1030,12 @@ void forward(dmx_handle* h, const float* mix, int G, float* out) {
       p.sx = 4;
       set_output(p, y, G, 1, To, Co);
       h->gemm(p, i == 0 ? PRO_BATCH_AFFINE : PRO_NONE, EPI_GELU, ("tenc.conv" + std::to_string(i)).c_str(), &E.conv);
-      run_dconv(h, h->tenc_dc[i], y, G, To);
+      run_dconv(h, h->tenc_dc[i], y, G, To, xf_rounded(h));
       float* z = h->falloc((size_t)G * To * Co);
       ConvParams r = base_params(E.rewrite, h->wdev);
       set_input(r, y, G, 1, To, Co);
       set_output(r, z, G, 1, To, Co);
+      r.a_rounded = xf_rounded(h);  // the DConv output, rounded
       h->gemm(r, PRO_NONE, EPI_GLU, ("tenc.rewrite" + std::to_string(i)).c_str(), &E.rewrite);
       tskip[i] = z;
       tin = z;
@@ -1035,12 +1054,13 @@ void forward(dmx_handle* h, const float* mix, int G, float* out) {
       if (i == 0) p.pro_scale = reinterpret_cast<const float*>(norm_f);
       set_output(p, y, G, Fo, kFrames, Co);
       h->gemm(p, i == 0 ? PRO_BATCH_AFFINE : PRO_NONE, EPI_GELU, ("enc.conv" + std::to_string(i)).c_str(), &E.conv);
-      run_dconv(h, h->enc_dc[i], y, G * Fo, kFrames);
+      run_dconv(h, h->enc_dc[i], y, G * Fo, kFrames, xf_rounded(h));
       float* z = h->falloc((size_t)G * Fo * kFrames * Co);
       ConvParams r = base_params(E.rewrite, h->wdev);
       set_input(r, y, G, Fo, kFrames, Co);
       set_output(r, z, G, Fo, kFrames, Co);
       if (i == 0) r.epi_emb = h->W(m.emb.off);
+      r.a_rounded = xf_rounded(h);  // the DConv output, rounded
       h->gemm(r, PRO_NONE, i == 0 ? EPI_GLU_EMB : EPI_GLU, ("enc.rewrite" + std::to_string(i)).c_str(), &E.rewrite);
       skip[i] = z;
       xin = z;
@@ -1127,11 +1147,13 @@ void forward(dmx_handle* h, const float* mix, int G, float* out) {
     p.i_bs = (int64_t)ntok * D;
     set_output(p, x, G, Fb, Tb, Cs[4]);
     p.epi_add = skip[3];
+    p.round_out = xf_rounded(h);  // feeds only the first decoder's rewrite
     h->gemm(p, PRO_NONE, EPI_STORE, "xf.downsample", &m.down);
     ConvParams q = base_params(m.down_t, h->wdev);
     set_input(q, Tk, G, 1, Tt, D);
     set_output(q, xt, G, 1, Tt, TCs[4]);
     q.epi_add = tskip[3];
+    q.round_out = xf_rounded(h);
     h->gemm(q, PRO_NONE, EPI_STORE, "xf.downsample", &m.down_t);
   }
 
@@ -1146,8 +1168,9 @@ void forward(dmx_handle* h, const float* mix, int G, float* out) {
       ConvParams r = base_params(Dw.rewrite, h->wdev);
       set_input(r, x, G, F, kFrames, C);
       set_output(r, g, G, F, kFrames, C);
+      r.a_rounded = xf_rounded(h);  // the down-sampler's or previous decoder's output, rounded
       h->gemm(r, PRO_NONE, EPI_GLU, ("dec.rewrite" + std::to_string(e)).c_str(), &Dw.rewrite);
-      run_dconv(h, h->dec_dc[e], g, G * F, kFrames);
+      run_dconv(h, h->dec_dc[e], g, G * F, kFrames, xf_rounded(h));
       const int Co = Dw.cout, Fo = 4 * F;
       float* o = h->falloc((size_t)G * Fo * kFrames * Co);
       if (last) {
@@ -1164,6 +1187,7 @@ void forward(dmx_handle* h, const float* mix, int G, float* out) {
         p.o_xs = (int64_t)Fo * Co;
         p.o_ys = 4LL * Co;
         p.o_off = 0;
+        p.a_rounded = xf_rounded(h);  // the DConv output, rounded
         h->gemm(p, PRO_NONE, EPI_STORE, ("dec.convtr" + std::to_string(e)).c_str(), &Dw.convt_all);
       } else {
         for (int ph = 0; ph < 4; ++ph) {
@@ -1179,6 +1203,8 @@ void forward(dmx_handle* h, const float* mix, int G, float* out) {
           p.o_ys = 4LL * kFrames * Co;
           p.o_off = (int64_t)ph * kFrames * Co;
           p.epi_add = skip[j - 1];
+          p.a_rounded = xf_rounded(h);  // the DConv output, rounded
+          p.round_out = xf_rounded(h);  // feeds only the next decoder's rewrite
           h->gemm(p, PRO_NONE, EPI_GELU, ("dec.convtr" + std::to_string(e)).c_str(),
                   &Dw.convt[ph]);
         }
@@ -1197,8 +1223,9 @@ void forward(dmx_handle* h, const float* mix, int G, float* out) {
       ConvParams r = base_params(Dw.rewrite, h->wdev);
       set_input(r, xt, G, 1, Tc, Ct);
       set_output(r, g, G, 1, Tc, Ct);
+      r.a_rounded = xf_rounded(h);  // the down-sampler's or previous decoder's output, rounded
       h->gemm(r, PRO_NONE, EPI_GLU, ("tdec.rewrite" + std::to_string(e)).c_str(), &Dw.rewrite);
-      run_dconv(h, h->tdec_dc[e], g, G, Tc);
+      run_dconv(h, h->tdec_dc[e], g, G, Tc, xf_rounded(h));
       const int Co = Dw.cout, len = lengths_t[j];
       float* o = h->falloc((size_t)G * len * Co);
       {
@@ -1222,6 +1249,8 @@ void forward(dmx_handle* h, const float* mix, int G, float* out) {
         p.o_lim = len;
         p.o_lim_ch = Co;
         if (!last) p.epi_add = tskip[j - 1];
+        p.a_rounded = xf_rounded(h);               // the DConv output, rounded
+        p.round_out = !last && xf_rounded(h);      // feeds only the next decoder's rewrite
         h->gemm(p, PRO_NONE, last ? EPI_STORE : EPI_GELU, ("tdec.convtr" + std::to_string(e)).c_str(),
                 &Dw.convt_all);
       }

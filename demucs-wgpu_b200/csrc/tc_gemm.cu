@@ -93,6 +93,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t tmem = *tmem_slot;
   const int ktiles = p.Kpad / BK;
   const int total = p.mtiles * p.ntiles;
+  // A already rounded to tf32 (and no split): the MMA consumes the TMA tile
+  // directly and the converter warps stay idle
+  const bool direct = !SPLIT && p.a_rounded && !p.a_stats;
 
   if (warp == 0) {
     if (lane == 0) {
@@ -150,7 +153,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int kt = 0; kt < ktiles; ++kt, ++it) {
           const int s = it % STAGES;
           const uint32_t ph = (it / STAGES) & 1;
-          if (!mbar_wait(&conv[s], ph, p.err, 2)) {
+          if (!mbar_wait(direct ? &full[s] : &conv[s], ph, p.err, 2)) {
             ok = false;
             break;
           }
@@ -189,7 +192,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int swz = BK == 32 ? (row & 7) : ((row >> 1) & 3);
     uint32_t it = 0;
     bool live = true;
-    for (int t = blockIdx.x; t < total; t += gridDim.x) {
+    for (int t = blockIdx.x; t < total && !direct; t += gridDim.x) {
       // optional A transform (TC_ROWS): GELU(GroupNorm(a)) with this row's moments
       float a_mean = 0.f, a_inv = 0.f;
       bool a_row = false;
@@ -316,18 +319,6 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
               for (int j = 0; j < 32; ++j) v[j] = gelu(v[j]);
             }
-            if (EPI == EPI_STORE && p.round_out) {
-#pragma unroll
-              for (int j = 0; j < 32; ++j) v[j] = round_tf32(v[j]);
-            }
-            if (EPI == EPI_STORE && p.vt_out && nb >= p.vt_col0) {
-              // whole 32-column chunks belong to one head (vt_col0 and 64 are multiples of 32)
-              const int c = nb - p.vt_col0, h2 = c / 64, d0 = c % 64;
-              const int64_t bb = pos / p.vt_ntok, tok = pos % p.vt_ntok;
-              float* vt = p.vt_out + ((bb * 8 + h2) * 64 + d0) * (int64_t)p.vt_ntok + tok;
-              for (int j = 0; j < 32; ++j)
-                if (nb + j < ncol) vt[(int64_t)j * p.vt_ntok] = v[j];
-            }
             const bool vec = full && ((orow + nb) & 3) == 0;
             if (p.epi_add) {
               const float* ad = p.epi_add + orow + nb;
@@ -344,6 +335,18 @@ __global__ void __launch_bounds__(kThreads, 1)
                 for (int j = 0; j < 32; ++j)
                   if (nb + j < ncol) v[j] += ad[j];
               }
+            }
+            if (p.round_out) {  // the output feeds only tf32 GEMMs: round to nearest once
+#pragma unroll
+              for (int j = 0; j < 32; ++j) v[j] = round_tf32(v[j]);
+            }
+            if (EPI == EPI_STORE && p.vt_out && nb >= p.vt_col0) {
+              // whole 32-column chunks belong to one head (vt_col0 and 64 are multiples of 32)
+              const int c = nb - p.vt_col0, h2 = c / 64, d0 = c % 64;
+              const int64_t bb = pos / p.vt_ntok, tok = pos % p.vt_ntok;
+              float* vt = p.vt_out + ((bb * 8 + h2) * 64 + d0) * (int64_t)p.vt_ntok + tok;
+              for (int j = 0; j < 32; ++j)
+                if (nb + j < ncol) vt[(int64_t)j * p.vt_ntok] = v[j];
             }
             float* o = p.out + orow + nb;
             if (vec) {
@@ -418,6 +421,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const float gate = v[2 * j + 1] * gsc + (p.epi_gb[c + p.epi_half] - nr.mean * gsc);
                 res[j] += p.epi_gamma[c] * (value * sigmoid(gate));
               }
+            }
+            if (p.round_out) {
+#pragma unroll
+              for (int j = 0; j < 16; ++j) res[j] = round_tf32(res[j]);
             }
             if (vec) {
 #pragma unroll

@@ -42,10 +42,11 @@ struct TcParams {
   const float* epi_res;
   const float* epi_emb;
   const float* epi_add;
-  int round_out;  // EPI_STORE: round stored values to nearest tf32 (attention operands)
+  int round_out;  // round stored values to nearest tf32 (the output feeds only tf32 GEMMs)
   float* vt_out;  // EPI_STORE: V^T copy of columns >= vt_col0 (see ConvParams)
   int vt_col0, vt_ntok;
   int o_lim, o_lim_ch;  // as in ConvParams
+  int a_rounded;  // A holds tf32-rounded values: the MMA reads the TMA tile as landed
   // EPI_DCONV_TAIL: row moments of the GLU input (sum, sum of squares per
   // row of epi_rowlen positions, count values each), GroupNorm weight/bias in
   // the reference's order (value c, gate c + epi_half)

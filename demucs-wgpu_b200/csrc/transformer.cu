@@ -19,7 +19,8 @@ namespace {
 // One warp per token of 512 channels.
 __global__ void layer_norm_kernel(const float* __restrict__ x, int64_t rows, int ntok,
                                   const float* __restrict__ w, const float* __restrict__ b,
-                                  const float* __restrict__ pos, float* __restrict__ out) {
+                                  const float* __restrict__ pos, float* __restrict__ out,
+                                  int round_out) {
   const int64_t row = (int64_t)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
   if (row >= rows) return;
   const int lane = threadIdx.x & 31;
@@ -57,6 +58,12 @@ __global__ void layer_norm_kernel(const float* __restrict__ x, int64_t rows, int
       r.y += pr[c + 1];
       r.z += pr[c + 2];
       r.w += pr[c + 3];
+    }
+    if (round_out) {  // the output feeds only tf32 GEMMs: round to nearest here, once
+      r.x = round_tf32(r.x);
+      r.y = round_tf32(r.y);
+      r.z = round_tf32(r.z);
+      r.w = round_tf32(r.w);
     }
     *reinterpret_cast<float4*>(o + c) = r;
   }
@@ -204,8 +211,9 @@ __global__ void __launch_bounds__(256) flash_attention_kernel(
 }  // namespace
 
 void launch_layer_norm(const float* x, int64_t rows, int ntok, const float* w, const float* b,
-                       const float* pos, float* out, cudaStream_t s) {
-  layer_norm_kernel<<<(unsigned)((rows + 7) / 8), 256, 0, s>>>(x, rows, ntok, w, b, pos, out);
+                       const float* pos, float* out, cudaStream_t s, bool round_out) {
+  layer_norm_kernel<<<(unsigned)((rows + 7) / 8), 256, 0, s>>>(x, rows, ntok, w, b, pos, out,
+                                                               round_out ? 1 : 0);
 }
 
 void launch_group_norm_apply(float* x, int B, int64_t ntok, const double* stats, const float* w,
