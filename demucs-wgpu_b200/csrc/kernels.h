@@ -51,11 +51,22 @@ struct DConvArgs {
   const float* w2_tc;
   const float* w2_tc_lo;
   int w2_npad;
+  // host memory: v (dconv_tc_slot order) then the packed upper triangle of M
+  // (off-diagonal doubled) for the moments of conv2's output (dconv_tc.cu)
+  const float* zq_host;
 };
+// K slot (of 16) of conv2 input i in the tensor-core weight copies of the
+// narrow layers: hidden channels i < hid/2 at slot i, the others at
+// 8 + i - hid/2, and i == hid (the constant-1 bias input) at slot 15.
+inline int dconv_tc_slot(int hid, int i) {
+  return i < hid / 2 ? i : (i < hid ? 8 + i - hid / 2 : 15);
+}
 int dconv_tiles(int T);
 bool dconv_row_fused(int T);
 bool launch_dconv(const DConvArgs& a, cudaStream_t s);
 bool dconv_tc_supported(int C, int T);
+// work items per row of the tensor-core DConv (rows of more than one need part1/part2)
+int dconv_tc_tiles(int T);
 bool launch_dconv_tc(const DConvArgs& a, cudaStream_t s);
 
 // transformer.cu

@@ -416,6 +416,7 @@ void load_dconv(Loader& L, const std::string& prefix, int C, DConvW* out, int d_
 struct DConvLayerW {
   Packed conv1, conv2;
   Vec n1w, n1b, n2w, n2b, gamma;
+  std::vector<float> zq;  // the fused tensor-core kernel's moment constants (host memory)
 };
 
 }  // namespace
@@ -763,17 +764,18 @@ void run_dconv(dmx_handle* h, const DConvFull& dc, float* x, int rows, int T, bo
   const int64_t positions = (int64_t)rows * T;
   const bool tf32 = h->cfg.precision == DMX_TF32 || h->cfg.precision == DMX_TF32X3;
   const bool has_tc = dc.layer[0].conv1.has_tc && dc.layer[0].conv2.has_tc;
-  // TF32 builds: tensor cores (3xTF32, fp32-accurate) for the narrow spectral
-  // layers (fused row kernel) and the widest layers (three GEMMs, where the
-  // SIMT kernels are compute-bound); the SIMT kernels are faster elsewhere
-  const bool tc = tf32 && has_tc && dconv_tc_supported(C, T);
+  // TF32 builds: tensor cores (3xTF32, fp32-accurate) for the narrow layers
+  // (the fused kernel: one launch per spectral row, three over the tiles of a
+  // waveform row) and the widest layers (three GEMMs, where the SIMT kernels
+  // are compute-bound); the SIMT kernels are faster elsewhere
+  const bool tc = tf32 && has_tc && !dc.layer[0].zq.empty() && dconv_tc_supported(C, T);
   if (tf32 && has_tc && !tc && C >= 384) {
     run_dconv_gemm(h, dc, x, rows, T, round_out);
     return;
   }
-  const bool fused = tc || dconv_row_fused(T);
-  const int tiles = dconv_tiles(T);
-  float* y = fused ? nullptr : h->falloc((size_t)positions * hid);
+  const int tiles = tc ? dconv_tc_tiles(T) : dconv_tiles(T);
+  const bool fused = tc ? tiles == 1 : dconv_row_fused(T);
+  float* y = (fused || tc) ? nullptr : h->falloc((size_t)positions * hid);
   double* part = fused ? nullptr : h->dalloc((size_t)rows * tiles * 4);
   for (int d = 0; d < 2; ++d) {
     const DConvLayerW& L = dc.layer[d];
@@ -807,9 +809,12 @@ void run_dconv(dmx_handle* h, const DConvFull& dc, float* x, int rows, int T, bo
     a.w2_tc = h->W(L.conv2.tc_off);
     a.w2_tc_lo = h->W(L.conv2.tc_lo_off);
     a.w2_npad = L.conv2.Npad;
+    a.zq_host = L.zq.empty() ? nullptr : L.zq.data();
     // algorithmic work: conv1 (3C -> hid) + conv2 (hid -> 2C) per position;
     // x read once and written once
-    h->mark(std::string(tc ? "dconv.tc" : (fused ? "dconv.row" : "dconv.tiled")) + std::to_string(C),
+    h->mark(std::string(tc ? (fused ? "dconv.tc" : "dconv.tctiled")
+                           : (fused ? "dconv.row" : "dconv.tiled")) +
+                std::to_string(C),
             10.0 * positions * C * hid, 8.0 * positions * C);
     if (h->live()) {
       if (!(tc ? launch_dconv_tc(a, h->stream) : launch_dconv(a, h->stream)))
@@ -1356,6 +1361,49 @@ void load_model(dmx_handle* h, const std::map<std::string, HostTensor>& t) {
     }
     return std::make_pair(k, taps);
   };
+  // The fused tensor-core DConv kernel (C = 48, 96) reads its hidden channels
+  // in K slots (dconv_tc_slot): conv1's output rows and conv2's input columns
+  // of the tensor-core copies move there, and the moments of conv2's output
+  // get their host-side constants v = sum_c w_c, M = sum_c w_c w_c'.
+  auto tc_dconv_slots = [&](int C, DConvLayerW& Lw) {
+    const int hid = C / 8, act = hid + 1;
+    int src[16];  // slot -> old slot (hidden channel h sat at h, the bias at 15)
+    for (int k = 0; k < 16; ++k) src[k] = -1;
+    for (int i = 0; i < act; ++i) src[dconv_tc_slot(hid, i)] = i < hid ? i : 15;
+    const Packed& p1 = Lw.conv1;
+    for (size_t off : {p1.tc_off, p1.tc_lo_off}) {
+      std::vector<float> old(wb.host.begin() + off, wb.host.begin() + off + (size_t)16 * p1.K);
+      for (int k = 0; k < 16; ++k)
+        for (int j = 0; j < p1.K; ++j)
+          wb.host[off + (size_t)k * p1.K + j] = src[k] >= 0 && src[k] < hid ? old[(size_t)src[k] * p1.K + j] : 0.f;
+    }
+    const Packed& p2 = Lw.conv2;
+    for (size_t off : {p2.tc_off, p2.tc_lo_off})
+      for (int n = 0; n < 2 * C; ++n) {
+        float* row = &wb.host[off + (size_t)n * 16];
+        float old[16];
+        std::copy(row, row + 16, old);
+        for (int k = 0; k < 16; ++k) row[k] = src[k] >= 0 ? old[src[k]] : 0.f;
+      }
+    std::vector<double> w((size_t)2 * C * act);
+    for (int n = 0; n < 2 * C; ++n)
+      for (int i = 0; i < act; ++i) {
+        const size_t e = (size_t)n * 16 + dconv_tc_slot(hid, i);
+        w[(size_t)n * act + i] = (double)wb.host[p2.tc_off + e] + (double)wb.host[p2.tc_lo_off + e];
+      }
+    Lw.zq.assign(act + act * (act + 1) / 2, 0.f);
+    for (int i = 0; i < act; ++i) {
+      double v = 0.0;
+      for (int n = 0; n < 2 * C; ++n) v += w[(size_t)n * act + i];
+      Lw.zq[i] = (float)v;
+    }
+    for (int i = 0, idx = act; i < act; ++i)
+      for (int j = i; j < act; ++j, ++idx) {
+        double m = 0.0;
+        for (int n = 0; n < 2 * C; ++n) m += w[(size_t)n * act + i] * w[(size_t)n * act + j];
+        Lw.zq[idx] = (float)(i == j ? m : 2.0 * m);
+      }
+  };
   auto load_dc = [&](const std::string& prefix, int C, DConvFull* dc) {
     dc->C = C;
     dc->hidden = C / 8;
@@ -1381,6 +1429,8 @@ void load_model(dmx_handle* h, const std::map<std::string, HostTensor>& t) {
           wb.host[Lw.conv2.tc_lo_off + (size_t)n * Lw.conv2.K + kb] = b - hi;
         }
       }
+      if ((C == 48 || C == 96) && Lw.conv1.has_tc && Lw.conv2.has_tc && Lw.conv2.K == 16)
+        tc_dconv_slots(C, Lw);
       Lw.n2w = L.vec(at + ".4.weight", 2 * C);
       Lw.n2b = L.vec(at + ".4.bias", 2 * C);
       Lw.gamma = L.vec(at + ".6.scale", C);
