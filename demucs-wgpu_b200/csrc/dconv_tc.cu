@@ -13,24 +13,24 @@
 // and their 2-frame halos are laid). Per item:
 //  * conv1 as tcgen05 MMAs (M = 128 frames x 3 blocks, N = the three taps'
 //    16-slot outputs side by side, K = C): warp 0 streams the x tiles with TMA
-//    (frames outside the row are TMA's zero fill) and the conv1 weights; warps
-//    2-5 write each tile's low part (x - tf32(x)); warp 1 issues the MMAs.
-//  * warps 6-13 read the conv1 accumulators out of TMEM (which frees them for
-//    the next item's conv1), combine the taps through shared memory, reduce
-//    the moments of y, and write g (and its low part) to shared memory as the
-//    A operand of conv2.
+//    (frames outside the row are TMA's zero fill) against conv1 weights that
+//    stay in shared memory; warps 2-3 write each tile's low part
+//    (x - tf32(x)); warp 1 issues the MMAs.
+//  * warps 4-15 read the conv1 accumulators out of TMEM (which frees them for
+//    the next item's conv1; warp 4 + 4b + q takes TMEM lanes 32q.. of block
+//    b), combine the taps through shared memory, reduce the moments of y, and
+//    write g (and its low part) to shared memory as the A operand of conv2.
 //  * the moments of z come from g alone. With w_c the conv2 weights of output
 //    column c (its bias on a constant-1 input slot), sum_c z_c = v.g and
 //    sum_c z_c^2 = g'Mg for v = sum_c w_c and M = sum_c w_c w_c', constants
 //    computed on the host; so z leaves TMEM once, for the output.
 //  * conv2 against the resident conv2 weights (N = 96 columns per MMA) is
-//    issued between the next item's conv1 stages; warps 6-13 combine it with
-//    the residual straight into x.
+//    issued between the next item's conv1 stages; warps 4-15 combine it with
+//    the residual (staged by TMA) straight into x, a third of the columns each.
 //
 // K slots: hidden channel h < HID/2 sits at slot h, the others at slot
-// 8 + h - HID/2, so each epilogue half (slots 0-7, 8-15) carries half of the
-// GroupNorm1 + GELU work; slot 15 is the constant 1 that carries conv2's bias.
-// The host packs the tensor-core weight copies in this order.
+// 8 + h - HID/2; slot 15 is the constant 1 that carries conv2's bias. The
+// host packs the tensor-core weight copies in this order.
 //
 // Precision: 3xTF32 (lo*hi + hi*lo + hi*hi). The high part of an fp32 operand
 // is the operand itself (the tensor core reads it truncated to tf32); the low
@@ -48,16 +48,18 @@ namespace dmx {
 
 namespace {
 
-constexpr int kThreads = 448;  // w0 TMA, w1 MMA, w2-5 converter, w6-13 epilogue
-constexpr int kEpiThreads = 256;
-constexpr int kEpiWarps = 8;
+constexpr int kThreads = 512;  // w0 TMA, w1 MMA, w2-3 converter, w4-15 epilogue
+constexpr int kEpiBase = 128;  // first epilogue thread
+constexpr int kEpiThreads = 384;
+constexpr int kEpiWarps = 12;
 
 template <int C>
 struct DcTc {
   static constexpr int HID = C / 8;
-  static constexpr int JA = HID / 2;              // hidden channels per epilogue half
+  static constexpr int JA = HID / 2;              // hidden channels below K slot 8
   static constexpr int ACT = HID + 1;             // conv2 K slots in use (hidden, bias)
   static constexpr int NQ = ACT * (ACT + 1) / 2;  // packed upper triangle of M
+  static constexpr int YS = (HID + 3) / 4 * 4;    // floats per frame of the y buffer
   static constexpr int HP = 16;                   // K slots of conv2 (conv1 N per tap)
   static constexpr int N1 = 3 * HP;               // conv1 N: the three taps' outputs side by side
   static constexpr int BK = C % 32 == 0 ? 32 : 16;  // conv1 K (channels) per stage
@@ -69,34 +71,41 @@ struct DcTc {
   // chunks through two TMEM buffers
   static constexpr bool ALL = NCHUNK == 1;
   static constexpr int A_BYTES = 128 * BK * 4;
-  static constexpr int B_BYTES = N1 * BK * 4;     // one 16-row box per tap
-  static constexpr int STAGE = 2 * A_BYTES + 2 * B_BYTES;  // A | A_lo | B | B_lo
-  static constexpr int STAGES = 3;
-  static constexpr int TX = A_BYTES + 2 * B_BYTES;         // bytes landed by TMA per stage
-  static constexpr int G_BYTES = 128 * HP * 4;             // one 128-frame block of g
+  static constexpr int STAGE = 2 * A_BYTES;  // x tile | its low part
+  static constexpr int STAGES = C == 48 ? 4 : 3;
+  static constexpr int W1_KB = N1 * BK * 4;        // conv1 weights of one K block (3 taps)
+  static constexpr int W1_BYTES = KB * W1_KB;      // [kb][tap][16 slots][BK], hi or lo
+  static constexpr int G_BYTES = 128 * HP * 4;     // one 128-frame block of g
   static constexpr int W2_BYTES = 2 * C * HP * 4;
+  static constexpr int OFF_W1 = STAGES * STAGE;    // w1 hi | w1 lo
   // g hi [3] | g lo [3]; before g is formed the same 48 KB holds the tap-0
   // and tap-2 outputs of all 384 frames for the neighbour exchange
-  static constexpr int OFF_G = STAGES * STAGE;
+  static constexpr int OFF_G = OFF_W1 + 2 * W1_BYTES;
   static constexpr int OFF_W2 = OFF_G + 6 * G_BYTES;       // w2 hi | w2 lo
   static constexpr int OFF_CH = OFF_W2 + 2 * W2_BYTES;     // per-channel constants [C][8]
   static constexpr int OFF_AFF = OFF_CH + C * 32;          // per-item GN2 affine [C] float4
-  // ALL: the epilogue threads' residual chunks, prefetched with cp.async
-  // while the moments of z are reduced: [18 chunks][256 threads][16 B]
-  static constexpr int OFF_RES = OFF_AFF + C * 16;
-  static constexpr int RES_BYTES = ALL ? 18 * 256 * 16 : 0;
+  // ALL: the item's x (the residual), 9 TMA boxes of 16 channels x 128
+  // frames, [block][channel group][frame][16], 64-byte swizzle
+  static constexpr int OFF_RES = (OFF_AFF + C * 16 + 1023) / 1024 * 1024;
+  static constexpr int RES_BOX = 128 * 64;
+  static constexpr int RES_BYTES = ALL ? 9 * RES_BOX : 0;
   static constexpr int SMEM = OFF_RES + RES_BYTES + 1024;
   static_assert(2 * C % NCH == 0 && HID % 2 == 0 && JA <= 7 && SMEM <= 227 * 1024, "shape");
+  static_assert(!ALL || BK == 16, "the residual boxes reuse the x map");
   // K slot of the i-th input of conv2 (the hidden channels, then the bias)
   static constexpr int act_slot(int i) { return i < JA ? i : (i < HID ? 8 + i - JA : 15); }
+  // 16-byte chunks (of a 16-slot row) that hold hidden channels
+  static constexpr bool chunk_used(int c) { return (c % 2) * 4 < JA; }
 };
 
-// The moments of z as functions of g (v and M above), over the active K slots
-// in act_slot order.
+// Per-layer constants, passed by value (they sit in the constant bank): the
+// moments of z as functions of g (v and M above, over the active K slots in
+// act_slot order) and GroupNorm1's per-channel terms with conv1's bias.
 template <int C>
-struct DcZq {
+struct DcConst {
   float v[DcTc<C>::ACT];
   float m[DcTc<C>::NQ];  // upper triangle by rows, off-diagonal entries doubled
+  float b1[DcTc<C>::HID], n1w[DcTc<C>::HID], n1b[DcTc<C>::HID];
 };
 
 __host__ __device__ constexpr uint32_t idesc_tf32(int M, int N) {
@@ -106,20 +115,20 @@ __host__ __device__ constexpr uint32_t idesc_tf32(int M, int N) {
 
 DMX_DEVICE float trunc_tf32(float x) { return __uint_as_float(__float_as_uint(x) & 0xFFFFE000u); }
 
-DMX_DEVICE void epi_bar() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
+DMX_DEVICE void epi_bar() { asm volatile("bar.sync 1, 384;" ::: "memory"); }
 
 DMX_DEVICE void mbar_arrive(uint64_t* bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 
-// Sum of (s, q) over the 256 epilogue threads, fixed order; all get the result.
+// Sum of (s, q) over the epilogue threads, fixed order; all get the result.
 DMX_DEVICE void epi_sum2(double& s, double& q, double* red) {
 #pragma unroll
   for (int o = 16; o; o >>= 1) {
     s += __shfl_xor_sync(0xffffffffu, s, o);
     q += __shfl_xor_sync(0xffffffffu, q, o);
   }
-  const int e = threadIdx.x / 32 - 6;
+  const int e = threadIdx.x / 32 - kEpiBase / 32;
   if ((threadIdx.x & 31) == 0) {
     red[2 * e] = s;
     red[2 * e + 1] = q;
@@ -147,9 +156,11 @@ DMX_DEVICE void norm_of(double s, double q, double inv_count, float& mean, float
 // row, ts = 380 tile - 2; the item owns local frames 2 .. 381 (those inside
 // the row). Rows of at most 380 frames are one item (mode DC_ROW, all of the
 // branch in one launch, row moments reduced inside the CTA). Longer rows run
-// three launches, each recomputing conv1 from x: DC_STATS1 (moments of y per
-// tile), DC_STATS2 (moments of z per tile, with the row's y moments summed
-// over its tiles in a fixed order) and DC_OUT (the output).
+// three launches: DC_STATS1 (conv1 from x: y into the y buffer and the
+// moments of y per tile), DC_STATS2 (g from y with the row's moments summed
+// over its tiles in a fixed order; the moments of z per tile) and DC_OUT
+// (conv2 and the output). Only DC_STATS1 reads the halo frames, so the
+// output written in place by one tile never reaches another tile's input.
 enum DcMode : int { DC_ROW = 0, DC_STATS1 = 1, DC_STATS2 = 2, DC_OUT = 3 };
 constexpr int kTileStride = 380;
 
@@ -160,13 +171,14 @@ __global__ void __launch_bounds__(kThreads, 1)
                         const __grid_constant__ CUtensorMap tmW1lo,
                         const __grid_constant__ CUtensorMap tmW2,
                         const __grid_constant__ CUtensorMap tmW2lo, const DConvArgs a,
-                        const __grid_constant__ DcZq<C> zq, int mode) {
+                        const __grid_constant__ DcConst<C> k, int mode) {
   using S = DcTc<C>;
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   unsigned char* smem = reinterpret_cast<unsigned char*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   __shared__ __align__(8) uint64_t full[S::STAGES], empty[S::STAGES], conv[S::STAGES];
-  __shared__ __align__(8) uint64_t w2_full, d1_full, d1_empty, g_ready, d2_full[2], d2_empty[2];
+  __shared__ __align__(8) uint64_t w1_full, w2_full, d1_full, d1_empty, g_ready, res_full;
+  __shared__ __align__(8) uint64_t d2_full[2], d2_empty[2];
   __shared__ uint32_t tmem_slot;
   __shared__ double red[2 * kEpiWarps];
 
@@ -176,12 +188,14 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int s = 0; s < S::STAGES; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
-      mbar_init(&conv[s], 128);
+      mbar_init(&conv[s], 64);
     }
+    mbar_init(&w1_full, 1);
     mbar_init(&w2_full, 1);
     mbar_init(&d1_full, 1);
     mbar_init(&d1_empty, kEpiThreads);
     mbar_init(&g_ready, kEpiThreads);
+    mbar_init(&res_full, 1);
     for (int j = 0; j < 2; ++j) {
       mbar_init(&d2_full[j], 1);
       mbar_init(&d2_empty[j], kEpiThreads);
@@ -203,6 +217,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t tm_d1 = tmem, tm_d2 = tmem + 256;
   const int T = a.T;
   const int items = a.rows * a.tiles;
+  const bool conv1 = mode == DC_ROW || mode == DC_STATS1;
   const bool conv2 = mode == DC_ROW || mode == DC_OUT;
 
   if (warp == 0) {
@@ -213,27 +228,29 @@ __global__ void __launch_bounds__(kThreads, 1)
         tma_load_2d(smem + S::OFF_W2, &tmW2, &w2_full, 0, 0);
         tma_load_2d(smem + S::OFF_W2 + S::W2_BYTES, &tmW2lo, &w2_full, 0, 0);
       }
-      uint32_t it = 0;
-      bool ok = true;
-      for (int w = blockIdx.x; w < items && ok; w += gridDim.x) {
-        const int row = w / a.tiles, ts = (w - row * a.tiles) * kTileStride - 2;
-        for (int m = 0; m < 3 && ok; ++m) {
-          for (int kb = 0; kb < S::KB; ++kb, ++it) {
-            const int s = it % S::STAGES;
-            if (!mbar_wait(&empty[s], ((it / S::STAGES) & 1) ^ 1, a.err, 31)) {
-              ok = false;
-              break;
-            }
-            unsigned char* st = smem + s * S::STAGE;
-            mbar_expect_tx(&full[s], S::TX);
-            const int c0 = kb * S::BK;
-            // frames ts + 128 m .. +127 (zero outside the row), channels c0 .. c0+BK
-            tma_load_3d(st, &tmX, &full[s], c0, ts + m * 128, row);
-            // B rows 16k .. 16k+15: tap k's weights for these channels
-            for (int tap = 0; tap < 3; ++tap) {
-              unsigned char* b = st + 2 * S::A_BYTES + tap * S::HP * S::BK * 4;
-              tma_load_2d(b, &tmW1, &full[s], tap * C + c0, 0);
-              tma_load_2d(b + S::B_BYTES, &tmW1lo, &full[s], tap * C + c0, 0);
+      if (conv1) {
+        // conv1 weights, once: K block kb's taps side by side (B rows 16 tap ..)
+        mbar_expect_tx(&w1_full, 2 * S::W1_BYTES);
+        for (int kb = 0; kb < S::KB; ++kb)
+          for (int tap = 0; tap < 3; ++tap) {
+            unsigned char* b = smem + S::OFF_W1 + kb * S::W1_KB + tap * S::HP * S::BK * 4;
+            tma_load_2d(b, &tmW1, &w1_full, tap * C + kb * S::BK, 0);
+            tma_load_2d(b + S::W1_BYTES, &tmW1lo, &w1_full, tap * C + kb * S::BK, 0);
+          }
+        uint32_t it = 0;
+        bool ok = true;
+        for (int w = blockIdx.x; w < items && ok; w += gridDim.x) {
+          const int row = w / a.tiles, ts = (w - row * a.tiles) * kTileStride - 2;
+          for (int m = 0; m < 3 && ok; ++m) {
+            for (int kb = 0; kb < S::KB; ++kb, ++it) {
+              const int s = it % S::STAGES;
+              if (!mbar_wait(&empty[s], ((it / S::STAGES) & 1) ^ 1, a.err, 31)) {
+                ok = false;
+                break;
+              }
+              mbar_expect_tx(&full[s], S::A_BYTES);
+              // frames ts + 128 m .. +127 (zero outside the row), channels kb BK ..
+              tma_load_3d(smem + s * S::STAGE, &tmX, &full[s], kb * S::BK, ts + m * 128, row);
             }
           }
         }
@@ -244,7 +261,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       // ---------------- MMA issuer ----------------
       constexpr uint32_t idesc1 = idesc_tf32(128, S::N1);
       constexpr uint32_t idesc2 = idesc_tf32(128, S::NCH);
-      bool ok = !conv2 || mbar_wait(&w2_full, 0, a.err, 32);
+      bool ok = (!conv1 || mbar_wait(&w1_full, 0, a.err, 29)) &&
+                (!conv2 || mbar_wait(&w2_full, 0, a.err, 32));
       uint32_t it = 0, u = 0;
       // conv2 of item `pend` (-1: none) is issued once its g is in shared
       // memory: `g_in` says that wait is over, `cur` counts its issued chunks
@@ -257,11 +275,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t w_hi = smem_u32(smem + S::OFF_W2 + ch * S::NCH * 64);
         const uint32_t w_lo = w_hi + S::W2_BYTES;
 #pragma unroll
-        for (int k = 0; k < 2; ++k) {
-          const uint64_t gh = umma_desc_k(g_hi + k * 32, 64);
-          const uint64_t wh = umma_desc_k(w_hi + k * 32, 64);
-          umma_tf32(d, umma_desc_k(g_lo + k * 32, 64), wh, idesc2, k != 0);
-          umma_tf32(d, gh, umma_desc_k(w_lo + k * 32, 64), idesc2, 1);
+        for (int kk = 0; kk < 2; ++kk) {
+          const uint64_t gh = umma_desc_k(g_hi + kk * 32, 64);
+          const uint64_t wh = umma_desc_k(w_hi + kk * 32, 64);
+          umma_tf32(d, umma_desc_k(g_lo + kk * 32, 64), wh, idesc2, kk != 0);
+          umma_tf32(d, gh, umma_desc_k(w_lo + kk * 32, 64), idesc2, 1);
           umma_tf32(d, gh, wh, idesc2, 1);
         }
       };
@@ -317,95 +335,114 @@ __global__ void __launch_bounds__(kThreads, 1)
         pend = -1;
       };
       int ri = 0;
-      for (int w = blockIdx.x; w < items && ok; w += gridDim.x, ++ri) {
-        // D1 is free once the epilogue has read the previous item's conv1
-        if (!mbar_wait(&d1_empty, (ri & 1) ^ 1, a.err, 30)) {
-          ok = false;
-          break;
-        }
-        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-        for (int m = 0; m < 3 && ok; ++m) {
-          const uint32_t d = tm_d1 + 64 * m;
-          for (int kb = 0; kb < S::KB; ++kb, ++it) {
-            conv2_progress(false);
-            const int s = it % S::STAGES;
-            if (!ok || !mbar_wait(&conv[s], (it / S::STAGES) & 1, a.err, 33)) {
-              ok = false;
-              break;
-            }
-            asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-            const uint32_t a_hi = smem_u32(smem + s * S::STAGE);
-            const uint32_t a_lo = a_hi + S::A_BYTES;
-            const uint32_t b_hi = a_hi + 2 * S::A_BYTES;
-            const uint32_t b_lo = b_hi + S::B_BYTES;
+      if (conv1) {
+        for (int w = blockIdx.x; w < items && ok; w += gridDim.x, ++ri) {
+          // D1 is free once the epilogue has read the previous item's conv1
+          if (!mbar_wait(&d1_empty, (ri & 1) ^ 1, a.err, 30)) {
+            ok = false;
+            break;
+          }
+          asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+          for (int m = 0; m < 3 && ok; ++m) {
+            const uint32_t d = tm_d1 + 64 * m;
+            for (int kb = 0; kb < S::KB; ++kb, ++it) {
+              conv2_progress(false);
+              const int s = it % S::STAGES;
+              const uint32_t par = (it / S::STAGES) & 1;
+              const uint32_t a_hi = smem_u32(smem + s * S::STAGE);
+              const uint32_t a_lo = a_hi + S::A_BYTES;
+              const uint32_t b_hi = smem_u32(smem + S::OFF_W1 + kb * S::W1_KB);
+              const uint32_t b_lo = b_hi + S::W1_BYTES;
+              // the x tile has landed: its high-part products
+              if (!ok || !mbar_wait(&full[s], par, a.err, 33)) {
+                ok = false;
+                break;
+              }
+              asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
 #pragma unroll
-            for (int j = 0; j < S::BK / 8; ++j) {
-              const uint64_t ah = umma_desc_k(a_hi + j * 32, S::BK * 4);
-              const uint64_t bh = umma_desc_k(b_hi + j * 32, S::BK * 4);
-              umma_tf32(d, umma_desc_k(a_lo + j * 32, S::BK * 4), bh, idesc1, (kb | j) != 0);
-              umma_tf32(d, ah, umma_desc_k(b_lo + j * 32, S::BK * 4), idesc1, 1);
-              umma_tf32(d, ah, bh, idesc1, 1);
+              for (int j = 0; j < S::BK / 8; ++j) {
+                const uint64_t ah = umma_desc_k(a_hi + j * 32, S::BK * 4);
+                umma_tf32(d, ah, umma_desc_k(b_hi + j * 32, S::BK * 4), idesc1, (kb | j) != 0);
+                umma_tf32(d, ah, umma_desc_k(b_lo + j * 32, S::BK * 4), idesc1, 1);
+              }
+              // its low part is written: the last product
+              if (!mbar_wait(&conv[s], par, a.err, 28)) {
+                ok = false;
+                break;
+              }
+              asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+#pragma unroll
+              for (int j = 0; j < S::BK / 8; ++j)
+                umma_tf32(d, umma_desc_k(a_lo + j * 32, S::BK * 4),
+                          umma_desc_k(b_hi + j * 32, S::BK * 4), idesc1, 1);
+              umma_commit(&empty[s]);
             }
-            umma_commit(&empty[s]);
+          }
+          if (!ok) break;
+          umma_commit(&d1_full);
+          conv2_progress(true);  // the rest of the previous item's conv2
+          if (conv2) {
+            pend = ri;
+            cur = 0;
+            g_in = false;
           }
         }
-        if (!ok) break;
-        umma_commit(&d1_full);
-        conv2_progress(true);  // the rest of the previous item's conv2
-        if (conv2) {
+        conv2_progress(true);
+      } else if (conv2) {
+        // DC_OUT: conv2 alone, item by item
+        for (int w = blockIdx.x; w < items && ok; w += gridDim.x, ++ri) {
           pend = ri;
           cur = 0;
           g_in = false;
+          conv2_progress(true);
         }
       }
-      conv2_progress(true);
     }
-  } else if (warp < 6) {
+  } else if (warp < 4) {
     // ---------------- converter: the low part of each x tile row ----------------
-    const int r = threadIdx.x - 64;
-    // visit the 16-byte chunks in swizzle order: 8 lanes, 8 bank groups
-    const int swz = S::BK == 32 ? (r & 7) : ((r >> 1) & 3);
-    uint32_t it = 0;
-    bool live = true;
-    for (int w = blockIdx.x; w < items; w += gridDim.x)
-      for (int m = 0; m < 3; ++m)
-        for (int kb = 0; kb < S::KB; ++kb, ++it) {
-          const int s = it % S::STAGES;
-          if (live && !mbar_wait(&full[s], (it / S::STAGES) & 1, a.err, 36)) live = false;
-          if (live) {
-            const float4* x4 = reinterpret_cast<const float4*>(smem + s * S::STAGE + r * S::BK * 4);
-            float4* lo4 = reinterpret_cast<float4*>(smem + s * S::STAGE + S::A_BYTES + r * S::BK * 4);
+    if (conv1) {
+      const int c = threadIdx.x - 64;  // rows c and c + 64 (the same swizzle phase)
+      const int swz = S::BK == 32 ? (c & 7) : ((c >> 1) & 3);
+      uint32_t it = 0;
+      bool live = true;
+      for (int w = blockIdx.x; w < items; w += gridDim.x)
+        for (int m = 0; m < 3; ++m)
+          for (int kb = 0; kb < S::KB; ++kb, ++it) {
+            const int s = it % S::STAGES;
+            if (live && !mbar_wait(&full[s], (it / S::STAGES) & 1, a.err, 36)) live = false;
+            if (live) {
 #pragma unroll
-            for (int qq = 0; qq < S::BK / 4; ++qq) {
-              const int q = qq ^ swz;
-              const float4 x = x4[q];
-              lo4[q] = make_float4(x.x - trunc_tf32(x.x), x.y - trunc_tf32(x.y),
-                                   x.z - trunc_tf32(x.z), x.w - trunc_tf32(x.w));
+              for (int h = 0; h < 2; ++h) {
+                const int r = c + 64 * h;
+                const float4* x4 = reinterpret_cast<const float4*>(smem + s * S::STAGE + r * S::BK * 4);
+                float4* lo4 = reinterpret_cast<float4*>(smem + s * S::STAGE + S::A_BYTES + r * S::BK * 4);
+#pragma unroll
+                for (int qq = 0; qq < S::BK / 4; ++qq) {
+                  const int q = qq ^ swz;
+                  const float4 x = x4[q];
+                  lo4[q] = make_float4(x.x - trunc_tf32(x.x), x.y - trunc_tf32(x.y),
+                                       x.z - trunc_tf32(x.z), x.w - trunc_tf32(x.w));
+                }
+              }
             }
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            mbar_arrive(&conv[s]);
           }
-          asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-          mbar_arrive(&conv[s]);
-        }
-  } else {
-    // ---------------- epilogue: warps 6-13 ----------------
-    // TMEM lane quarter q (rows 32q .. 32q+31 of each 128-frame block); half
-    // hh takes K slots 8hh .. 8hh+7 (conv1) and columns 48hh.. (conv2)
-    const int e = warp - 6, q = warp % 4, hh = e / 4;
-    const int r = q * 32 + lane;
-    const uint32_t lane_base = (uint32_t)(q * 32) << 16;
-    // hidden channels hh*JA + j sit in slots 8hh + j, j < JA
-    float b1[S::JA], n1w[S::JA], n1b[S::JA];
-#pragma unroll
-    for (int j = 0; j < S::JA; ++j) {
-      const int h = hh * S::JA + j;
-      b1[j] = a.b1[h];
-      n1w[j] = a.n1w[h];
-      n1b[j] = a.n1b[h];
     }
+  } else {
+    // ---------------- epilogue: warps 4-15 ----------------
+    // TMEM lane quarter q = warp % 4 (frames 32q .. 32q+31 of a block); b:
+    // the block of this warp's frames for conv1, its third of the columns of
+    // each 96-column conv2 chunk for the output
+    const int e = warp - 4, q = warp % 4, b = e / 4;
+    const int r = q * 32 + lane;
+    const int p = 128 * b + r;  // this thread's frame (conv1, g)
+    const int et = threadIdx.x - kEpiBase;
+    const uint32_t lane_base = (uint32_t)(q * 32) << 16;
     // per channel c: conv2 bias (value, gate), GN2 weight and bias (value,
     // gate), LayerScale
     float4* chan = reinterpret_cast<float4*>(smem + S::OFF_CH);
-    for (int c = threadIdx.x - 192; c < C; c += kEpiThreads) {
+    for (int c = et; c < C; c += kEpiThreads) {
       chan[2 * c] = make_float4(a.b2[2 * c], a.b2[2 * c + 1], a.n2w[c], a.n2w[c + C]);
       chan[2 * c + 1] = make_float4(a.n2b[c], a.n2b[c + C], a.gamma[c], 0.f);
     }
@@ -414,11 +451,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     // the row's moments from its tiles' partials, summed by one warp in a
     // fixed order; every epilogue thread gets them
     auto row_sum = [&](const double* part, int row, double& s, double& q2) {
-      if (threadIdx.x < 192 + 32) {
+      if (warp == kEpiBase / 32) {
         double ls = 0.0, lq = 0.0;
-        for (int k = lane; k < a.tiles; k += 32) {
-          ls += part[2 * ((int64_t)row * a.tiles + k)];
-          lq += part[2 * ((int64_t)row * a.tiles + k) + 1];
+        for (int t = lane; t < a.tiles; t += 32) {
+          ls += part[2 * ((int64_t)row * a.tiles + t)];
+          lq += part[2 * ((int64_t)row * a.tiles + t) + 1];
         }
 #pragma unroll
         for (int o = 16; o; o >>= 1) {
@@ -442,176 +479,172 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int row = w / a.tiles, ts = (w - row * a.tiles) * kTileStride - 2;
       // local frame i = 128 m + r is frame ts + i; owned: 2 <= i < 382, inside the row
       auto owned = [&](int i) { return i >= 2 && i < 382 && ts + i < T; };
-      // ---- y = conv1 + bias, its moments, g into shared memory ----
-      // D1 holds Y_k = W_k x (k = tap) per frame; y[p] = Y_0[p-d] + Y_1[p] +
-      // Y_2[p+d]. Y_0 and Y_2 go through shared memory to the neighbours
-      // (frames 384 x 16 slots each, 64-byte rows with the 64-byte swizzle).
-      if (ok && !mbar_wait(&d1_full, ri & 1, a.err, 37)) ok = false;
-      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-      float* x0s = reinterpret_cast<float*>(smem + S::OFF_G);
-      float* x2s = x0s + 384 * 16;
-      constexpr int NC = (S::JA + 3) / 4;  // 16-byte chunks of a half that hold channels
-      float y[3][8];
-      {
-        uint32_t d1[3][3][8];
-        __syncwarp();
-#pragma unroll
-        for (int m = 0; m < 3; ++m)
+      const bool mine = owned(p);
+      // the item's x for the residual, 9 boxes of 16 channels (ALL): issued
+      // once every thread is past the previous item's output
+      auto stage_residual = [&]() {
+        if constexpr (S::ALL) {
+          if (conv2 && threadIdx.x == kEpiBase) {
+            mbar_expect_tx(&res_full, S::RES_BYTES);
+            for (int m = 0; m < 3; ++m)
+              for (int g = 0; g < 3; ++g)
+                tma_load_3d(smem + S::OFF_RES + (3 * m + g) * S::RES_BOX, &tmX, &res_full, 16 * g,
+                            ts + 128 * m, row);
+          }
+        }
+      };
+      float yh[S::HID];  // y of frame p by hidden channel
+      double s, sq;
+      if (conv1) {
+        // ---- y = conv1 + bias ----
+        // D1 holds Y_k = W_k x (k = tap) per frame; y[p] = Y_0[p-d] + Y_1[p] +
+        // Y_2[p+d]. Y_0 and Y_2 go through shared memory to the neighbours
+        // (frames 384 x 16 slots each, 64-byte rows with the 64-byte swizzle).
+        if (ok && !mbar_wait(&d1_full, ri & 1, a.err, 37)) ok = false;
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        float* x0s = reinterpret_cast<float*>(smem + S::OFF_G);
+        float* x2s = x0s + 384 * 16;
+        float y1[16];
+        {
+          uint32_t d1[48];
+          __syncwarp();
 #pragma unroll
           for (int tap = 0; tap < 3; ++tap)
-            tmem_ld8_nw(tm_d1 + lane_base + 64 * m + 16 * tap + 8 * hh, d1[m][tap]);
-        tmem_ld_wait<72>(&d1[0][0][0]);
-        // D1 is read out: the next item's conv1 may overwrite it
-        asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-        mbar_arrive(&d1_empty);
+            tmem_ld16_nw(tm_d1 + lane_base + 64 * b + 16 * tap, d1 + 16 * tap);
+          tmem_ld_wait<48>(d1);
+          // D1 is read out: the next item's conv1 may overwrite it
+          asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+          mbar_arrive(&d1_empty);
 #pragma unroll
-        for (int m = 0; m < 3; ++m) {
-          const int p = 128 * m + r;
+          for (int j = 0; j < 16; ++j) y1[j] = __uint_as_float(d1[16 + j]);
 #pragma unroll
-          for (int j = 0; j < 8; ++j) y[m][j] = __uint_as_float(d1[m][1][j]);
-#pragma unroll
-          for (int c = 0; c < NC; ++c) {
-            const int off = p * 16 + (((2 * hh + c) ^ ((p >> 1) & 3)) << 2);
-            *reinterpret_cast<uint4*>(x0s + off) = make_uint4(
-                d1[m][0][4 * c], d1[m][0][4 * c + 1], d1[m][0][4 * c + 2], d1[m][0][4 * c + 3]);
-            *reinterpret_cast<uint4*>(x2s + off) = make_uint4(
-                d1[m][2][4 * c], d1[m][2][4 * c + 1], d1[m][2][4 * c + 2], d1[m][2][4 * c + 3]);
+          for (int c = 0; c < 4; ++c) {
+            if (!S::chunk_used(c)) continue;
+            const int off = p * 16 + ((c ^ ((p >> 1) & 3)) << 2);
+            *reinterpret_cast<uint4*>(x0s + off) =
+                make_uint4(d1[4 * c], d1[4 * c + 1], d1[4 * c + 2], d1[4 * c + 3]);
+            *reinterpret_cast<uint4*>(x2s + off) =
+                make_uint4(d1[32 + 4 * c], d1[32 + 4 * c + 1], d1[32 + 4 * c + 2], d1[32 + 4 * c + 3]);
           }
         }
-      }
-      epi_bar();
-      float fs1 = 0.f, fq1 = 0.f;
-#pragma unroll
-      for (int m = 0; m < 3; ++m) {
-        const int p = 128 * m + r;
+        epi_bar();
+        stage_residual();
         const int pl = p - a.dil, pr = p + a.dil;
 #pragma unroll
-        for (int c = 0; c < NC; ++c) {
-          float4 l = make_float4(0.f, 0.f, 0.f, 0.f), rgt = l;
+        for (int c = 0; c < 4; ++c) {
+          if (!S::chunk_used(c)) continue;
+          float4 l = make_float4(0.f, 0.f, 0.f, 0.f), rg = l;
           if (pl >= 0)
-            l = *reinterpret_cast<const float4*>(x0s + pl * 16 + (((2 * hh + c) ^ ((pl >> 1) & 3)) << 2));
+            l = *reinterpret_cast<const float4*>(x0s + pl * 16 + ((c ^ ((pl >> 1) & 3)) << 2));
           if (pr < 384)
-            rgt = *reinterpret_cast<const float4*>(x2s + pr * 16 + (((2 * hh + c) ^ ((pr >> 1) & 3)) << 2));
-          y[m][4 * c] += l.x + rgt.x;
-          y[m][4 * c + 1] += l.y + rgt.y;
-          y[m][4 * c + 2] += l.z + rgt.z;
-          y[m][4 * c + 3] += l.w + rgt.w;
+            rg = *reinterpret_cast<const float4*>(x2s + pr * 16 + ((c ^ ((pr >> 1) & 3)) << 2));
+          y1[4 * c] += l.x + rg.x;
+          y1[4 * c + 1] += l.y + rg.y;
+          y1[4 * c + 2] += l.z + rg.z;
+          y1[4 * c + 3] += l.w + rg.w;
         }
-        const bool valid = owned(p);
+        float fs = 0.f, fq = 0.f;
 #pragma unroll
-        for (int j = 0; j < S::JA; ++j) {
-          y[m][j] += b1[j];
-          if (valid) {
-            fs1 += y[m][j];
-            fq1 = fmaf(y[m][j], y[m][j], fq1);
+        for (int h = 0; h < S::HID; ++h) {
+          yh[h] = y1[S::act_slot(h)] + k.b1[h];
+          fs += yh[h];
+          fq = fmaf(yh[h], yh[h], fq);
+        }
+        s = mine ? fs : 0.f;
+        sq = mine ? fq : 0.f;
+        if (mode == DC_STATS1) {
+          // y of the owned frames for the later launches
+          if (mine) {
+            float4* yp = reinterpret_cast<float4*>(a.y + ((int64_t)row * T + ts + p) * S::YS);
+#pragma unroll
+            for (int c = 0; c < S::YS / 4; ++c) {
+              float t4[4];
+#pragma unroll
+              for (int i = 0; i < 4; ++i) t4[i] = 4 * c + i < S::HID ? yh[4 * c + i] : 0.f;
+              yp[c] = make_float4(t4[0], t4[1], t4[2], t4[3]);
+            }
           }
+          epi_sum2(s, sq, red);
+          if (threadIdx.x == kEpiBase) {
+            a.part1[2 * (int64_t)w] = s;
+            a.part1[2 * (int64_t)w + 1] = sq;
+          }
+          continue;
         }
-      }
-      double s = fs1, sq = fq1;  // values of one thread in f32, the CTA sum in f64
-      if (mode == DC_ROW || mode == DC_STATS1) epi_sum2(s, sq, red);
-      if (mode == DC_STATS1) {
-        if (threadIdx.x == 192) {
-          a.part1[2 * (int64_t)w] = s;
-          a.part1[2 * (int64_t)w + 1] = sq;
+        epi_sum2(s, sq, red);
+      } else {
+        // DC_STATS2, DC_OUT: y of the owned frames from the buffer
+        if (mine) {
+          const float4* yp = reinterpret_cast<const float4*>(a.y + ((int64_t)row * T + ts + p) * S::YS);
+#pragma unroll
+          for (int c = 0; c < S::YS / 4; ++c) {
+            const float4 v = yp[c];
+            const float t4[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+              if (4 * c + i < S::HID) yh[4 * c + i] = t4[i];
+          }
+        } else {
+#pragma unroll
+          for (int h = 0; h < S::HID; ++h) yh[h] = 0.f;
         }
-        continue;
+        row_sum(a.part1, row, s, sq);
+        stage_residual();
       }
-      if (mode != DC_ROW) row_sum(a.part1, row, s, sq);
+      // ---- g = GELU(GN1(y)) of frame p; conv2's A operand ----
       float mean, inv;
       norm_of(s, sq, ic1, mean, inv);
+      float ga[S::ACT];  // g by conv2 input (hidden channels, then the bias input 1)
 #pragma unroll
-      for (int m = 0; m < 3; ++m) {
-        float g[8];
+      for (int h = 0; h < S::HID; ++h) {
+        const float scale = inv * k.n1w[h];
+        ga[h] = mine ? gelu(yh[h] * scale + (k.n1b[h] - mean * scale)) : 0.f;
+      }
+      ga[S::HID] = 1.0f;
+      if (conv2) {
+        float gs[16];
 #pragma unroll
-        for (int j = 0; j < 8; ++j) g[j] = 0.f;
-        if (owned(m * 128 + r)) {
+        for (int j = 0; j < 16; ++j) gs[j] = 0.f;
 #pragma unroll
-          for (int j = 0; j < S::JA; ++j) {
-            const float scale = inv * n1w[j];
-            g[j] = gelu(y[m][j] * scale + (n1b[j] - mean * scale));
-          }
-        }
-        if (hh == 1) g[7] = 1.0f;  // slot 15: conv2's bias input
-        // row r of the 128 x 16 K-major tile, 64-byte swizzle: 16-byte chunk
-        // c lives at chunk c ^ ((r / 2) % 4)
-        unsigned char* hi = smem + S::OFF_G + m * S::G_BYTES + r * 64;
+        for (int i = 0; i < S::ACT; ++i) gs[S::act_slot(i)] = ga[i];
+        // row r of block b's 128 x 16 K-major tile, 64-byte swizzle: 16-byte
+        // chunk c lives at chunk c ^ ((r / 2) % 4)
+        unsigned char* hi = smem + S::OFF_G + b * S::G_BYTES + r * 64;
         unsigned char* lo = hi + 3 * S::G_BYTES;
 #pragma unroll
-        for (int c = 0; c < 2; ++c) {
-          const int phys = ((2 * hh + c) ^ ((r >> 1) & 3)) << 4;
-          const float4 v = make_float4(g[4 * c], g[4 * c + 1], g[4 * c + 2], g[4 * c + 3]);
+        for (int c = 0; c < 4; ++c) {
+          const int phys = (c ^ ((r >> 1) & 3)) << 4;
+          const float4 v = make_float4(gs[4 * c], gs[4 * c + 1], gs[4 * c + 2], gs[4 * c + 3]);
           *reinterpret_cast<float4*>(hi + phys) = v;
-          if (conv2)
-            *reinterpret_cast<float4*>(lo + phys) =
-                make_float4(v.x - trunc_tf32(v.x), v.y - trunc_tf32(v.y), v.z - trunc_tf32(v.z),
-                            v.w - trunc_tf32(v.w));
+          *reinterpret_cast<float4*>(lo + phys) =
+              make_float4(v.x - trunc_tf32(v.x), v.y - trunc_tf32(v.y), v.z - trunc_tf32(v.z),
+                          v.w - trunc_tf32(v.w));
         }
-      }
-      if (conv2) {
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
         asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
         mbar_arrive(&g_ready);
-      }
-      if constexpr (S::ALL) {
-        if (conv2) {
-          // this thread's residual x[p][24 hh .. 24 hh + 24) of the three
-          // blocks, landing while the moments of z are reduced
-          const int t = threadIdx.x - 192;
-          for (int m = 0; m < 3; ++m) {
-            const int p = 128 * m + r;
-            if (owned(p)) {
-              const float* src = a.x + ((int64_t)row * T + ts + p) * C + 24 * hh;
-#pragma unroll
-              for (int i = 0; i < 6; ++i) {
-                const uint32_t dst = smem_u32(smem + S::OFF_RES + ((6 * m + i) * 256 + t) * 16);
-                asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src + 4 * i)
-                             : "memory");
-              }
-            }
-          }
-          asm volatile("cp.async.commit_group;" ::: "memory");
-        }
       }
 
       // ---- moments of z: the sums of v.g and g'Mg over the owned frames ----
       if (mode == DC_OUT) {
         row_sum(a.part2, row, s, sq);
       } else {
-        epi_bar();  // g of every frame is in shared memory
-        float ls = 0.f, lq = 0.f;
-        for (int p = threadIdx.x - 192; p < 384; p += kEpiThreads) {
-          if (!owned(p)) continue;
-          const int rr = p & 127;
-          const unsigned char* gp = smem + S::OFF_G + (p >> 7) * S::G_BYTES + rr * 64;
-          float gs[16];
-#pragma unroll
-          for (int c = 0; c < 4; ++c) {
-            const float4 v = *reinterpret_cast<const float4*>(gp + ((c ^ ((rr >> 1) & 3)) << 4));
-            gs[4 * c] = v.x;
-            gs[4 * c + 1] = v.y;
-            gs[4 * c + 2] = v.z;
-            gs[4 * c + 3] = v.w;
-          }
-          float ga[S::ACT];
-#pragma unroll
-          for (int i = 0; i < S::ACT; ++i) ga[i] = gs[S::act_slot(i)];
-          float l = 0.f, qf = 0.f;
+        float l = 0.f, qf = 0.f;
+        if (mine) {
 #pragma unroll
           for (int i = 0, idx = 0; i < S::ACT; ++i) {
-            l = fmaf(zq.v[i], ga[i], l);
+            l = fmaf(k.v[i], ga[i], l);
             float t = 0.f;
 #pragma unroll
-            for (int j = i; j < S::ACT; ++j, ++idx) t = fmaf(zq.m[idx], ga[j], t);
+            for (int j = i; j < S::ACT; ++j, ++idx) t = fmaf(k.m[idx], ga[j], t);
             qf = fmaf(ga[i], t, qf);
           }
-          ls += l;
-          lq += qf;
         }
-        s = ls;
-        sq = lq;
+        s = l;
+        sq = qf;
         epi_sum2(s, sq, red);
         if (mode == DC_STATS2) {
-          if (threadIdx.x == 192) {
+          if (threadIdx.x == kEpiBase) {
             a.part2[2 * (int64_t)w] = s;
             a.part2[2 * (int64_t)w + 1] = sq;
           }
@@ -622,7 +655,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       norm_of(s, sq, ic2, mean2, inv2);
       // GN2 with LayerScale folded in: gamma * value = z_v * a + b, gate = z_g * c + d
       float4* aff = reinterpret_cast<float4*>(smem + S::OFF_AFF);
-      for (int c = threadIdx.x - 192; c < C; c += kEpiThreads) {
+      for (int c = et; c < C; c += kEpiThreads) {
         const float4 t0 = chan[2 * c], t1 = chan[2 * c + 1];
         const float vs = inv2 * t0.z, gs = inv2 * t0.w;
         aff[c] = make_float4(t1.z * vs, t1.z * (t1.x - mean2 * vs), gs, t1.y - mean2 * gs);
@@ -636,6 +669,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       };
       if (S::ALL) {
         if (ok && !mbar_wait(&d2_full[0], ri & 1, a.err, 38)) ok = false;
+        if (ok && !mbar_wait(&res_full, ri & 1, a.err, 27)) ok = false;
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
       }
       for (int m = 0; m < 3; ++m)
@@ -645,54 +679,52 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (ok && !mbar_wait(&d2_full[j], (u >> 1) & 1, a.err, 39)) ok = false;
             asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
           }
-          const int p = m * 128 + r;
-          const bool own = owned(p);
-          const int c0 = ch * (S::NCH / 2) + 24 * hh;  // first channel of this thread
-          float* xp = a.x + ((int64_t)row * T + (own ? ts + p : 0)) * C + c0;
-          uint32_t zr[48];
+          const int pm = m * 128 + r;
+          const bool own = owned(pm);
+          const int c0 = ch * (S::NCH / 2) + 16 * b;  // this thread's 16 channels
+          float* xp = a.x + ((int64_t)row * T + (own ? ts + pm : 0)) * C + c0;
+          uint32_t zr[32];
           __syncwarp();
-#pragma unroll
-          for (int c = 0; c < 48; c += 16)
-            tmem_ld16_nw(tmem + lane_base + d2_col(m, j) + 48 * hh + c, zr + c);
-          float4 res[6];
+          tmem_ld16_nw(tmem + lane_base + d2_col(m, j) + 32 * b, zr);
+          tmem_ld16_nw(tmem + lane_base + d2_col(m, j) + 32 * b + 16, zr + 16);
+          float4 res[4];
           if (S::ALL) {
-            if (m == 0) asm volatile("cp.async.wait_all;" ::: "memory");
-            const float4* st = reinterpret_cast<const float4*>(smem + S::OFF_RES) + 6 * m * 256 +
-                               (threadIdx.x - 192);
+            const unsigned char* rb = smem + S::OFF_RES + (3 * m + b) * S::RES_BOX + r * 64;
 #pragma unroll
-            for (int i = 0; i < 6; ++i) res[i] = st[i * 256];
+            for (int i = 0; i < 4; ++i)
+              res[i] = *reinterpret_cast<const float4*>(rb + ((i ^ ((r >> 1) & 3)) << 4));
           } else if (ok && own) {
 #pragma unroll
-            for (int i = 0; i < 6; ++i) res[i] = reinterpret_cast<const float4*>(xp)[i];
+            for (int i = 0; i < 4; ++i) res[i] = reinterpret_cast<const float4*>(xp)[i];
           }
-          tmem_ld_wait<48>(zr);
+          tmem_ld_wait<32>(zr);
           if (!S::ALL) {
             asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
             mbar_arrive(&d2_empty[j]);
             ++u;
           }
           if (ok && own) {
+            float o[16];
 #pragma unroll
-            for (int sc = 0; sc < 3; ++sc) {
-              float o[8] = {res[2 * sc].x, res[2 * sc].y, res[2 * sc].z, res[2 * sc].w,
-                            res[2 * sc + 1].x, res[2 * sc + 1].y, res[2 * sc + 1].z,
-                            res[2 * sc + 1].w};
-#pragma unroll
-              for (int k = 0; k < 8; ++k) {
-                const float4 f = aff[c0 + 8 * sc + k];
-                // gamma * GN2(value), GN2(gate)
-                const float value = fmaf(__uint_as_float(zr[16 * sc + 2 * k]), f.x, f.y);
-                const float gate = fmaf(__uint_as_float(zr[16 * sc + 2 * k + 1]), f.z, f.w);
-                o[k] += __fdividef(value, 1.0f + __expf(-gate));
-              }
-              if (a.round_out) {
-#pragma unroll
-                for (int k = 0; k < 8; ++k) o[k] = round_tf32(o[k]);
-              }
-              float4* x4 = reinterpret_cast<float4*>(xp + 8 * sc);
-              x4[0] = make_float4(o[0], o[1], o[2], o[3]);
-              x4[1] = make_float4(o[4], o[5], o[6], o[7]);
+            for (int i = 0; i < 4; ++i) {
+              o[4 * i] = res[i].x;
+              o[4 * i + 1] = res[i].y;
+              o[4 * i + 2] = res[i].z;
+              o[4 * i + 3] = res[i].w;
             }
+#pragma unroll
+            for (int kk = 0; kk < 16; ++kk) {
+              const float4 f = aff[c0 + kk];
+              // gamma * GN2(value), GN2(gate)
+              const float value = fmaf(__uint_as_float(zr[2 * kk]), f.x, f.y);
+              const float gate = fmaf(__uint_as_float(zr[2 * kk + 1]), f.z, f.w);
+              o[kk] += __fdividef(value, 1.0f + __expf(-gate));
+              if (a.round_out) o[kk] = round_tf32(o[kk]);
+            }
+            float4* x4 = reinterpret_cast<float4*>(xp);
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+              x4[i] = make_float4(o[4 * i], o[4 * i + 1], o[4 * i + 2], o[4 * i + 3]);
           }
         }
       if (S::ALL) {
@@ -738,9 +770,13 @@ bool launch_c(const DConvArgs& a, cudaStream_t s) {
     ok = ok && make_tensor_map(&m2lo, a.w2_tc_lo, 2, dims, str, box, CU_TENSOR_MAP_SWIZZLE_64B);
   }
   if (!ok) return false;
-  DcZq<C> zq;
-  for (int i = 0; i < S::ACT; ++i) zq.v[i] = a.zq_host[i];
-  for (int i = 0; i < S::NQ; ++i) zq.m[i] = a.zq_host[S::ACT + i];
+  DcConst<C> k;
+  const float* src = a.zq_host;
+  for (int i = 0; i < S::ACT; ++i) k.v[i] = *src++;
+  for (int i = 0; i < S::NQ; ++i) k.m[i] = *src++;
+  for (int i = 0; i < S::HID; ++i) k.b1[i] = *src++;
+  for (int i = 0; i < S::HID; ++i) k.n1w[i] = *src++;
+  for (int i = 0; i < S::HID; ++i) k.n1b[i] = *src++;
   static bool configured = false;
   if (!configured) {
     cudaFuncSetAttribute(dconv_tc_row_kernel<C>, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -753,10 +789,10 @@ bool launch_c(const DConvArgs& a, cudaStream_t s) {
   const int items = a.rows * a.tiles;
   const int grid = items < sms ? items : sms;
   if (a.tiles == 1) {
-    dconv_tc_row_kernel<C><<<grid, kThreads, S::SMEM, s>>>(mx, m1, m1lo, m2, m2lo, a, zq, DC_ROW);
+    dconv_tc_row_kernel<C><<<grid, kThreads, S::SMEM, s>>>(mx, m1, m1lo, m2, m2lo, a, k, DC_ROW);
   } else {
     for (int mode = DC_STATS1; mode <= DC_OUT; ++mode)
-      dconv_tc_row_kernel<C><<<grid, kThreads, S::SMEM, s>>>(mx, m1, m1lo, m2, m2lo, a, zq, mode);
+      dconv_tc_row_kernel<C><<<grid, kThreads, S::SMEM, s>>>(mx, m1, m1lo, m2, m2lo, a, k, mode);
   }
   return true;
 }
@@ -769,10 +805,17 @@ bool dconv_tc_supported(int C, int T) {
 
 int dconv_tc_tiles(int T) { return (T + kTileStride - 1) / kTileStride; }
 
+int dconv_tc_ystride(int C) { return (C / 8 + 3) / 4 * 4; }
+
+int dconv_tc_const_floats(int C) {
+  const int hid = C / 8, act = hid + 1;
+  return act + act * (act + 1) / 2 + 3 * hid;
+}
+
 bool launch_dconv_tc(const DConvArgs& a, cudaStream_t s) {
   if (!dconv_tc_supported(a.C, a.T) || a.dil < 1 || a.dil > 2 || !a.w1_tc || !a.w1_tc_lo ||
       !a.w2_tc || !a.w2_tc_lo || !a.zq_host || a.w1_npad < 16 || a.w2_npad < 2 * a.C ||
-      a.tiles != dconv_tc_tiles(a.T) || (a.tiles > 1 && (!a.part1 || !a.part2)) ||
+      a.tiles != dconv_tc_tiles(a.T) || (a.tiles > 1 && (!a.part1 || !a.part2 || !a.y)) ||
       (int64_t)a.rows * a.tiles > INT32_MAX)
     return false;
   switch (a.C) {

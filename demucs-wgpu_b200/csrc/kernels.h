@@ -51,8 +51,9 @@ struct DConvArgs {
   const float* w2_tc;
   const float* w2_tc_lo;
   int w2_npad;
-  // host memory: v (dconv_tc_slot order) then the packed upper triangle of M
-  // (off-diagonal doubled) for the moments of conv2's output (dconv_tc.cu)
+  // host memory, dconv_tc_const_floats(C) floats: v and the packed upper
+  // triangle of M (off-diagonal doubled; dconv_tc_slot order) for the moments
+  // of conv2's output, then conv1's bias and GroupNorm1's weight and bias
   const float* zq_host;
 };
 // K slot (of 16) of conv2 input i in the tensor-core weight copies of the
@@ -65,8 +66,11 @@ int dconv_tiles(int T);
 bool dconv_row_fused(int T);
 bool launch_dconv(const DConvArgs& a, cudaStream_t s);
 bool dconv_tc_supported(int C, int T);
-// work items per row of the tensor-core DConv (rows of more than one need part1/part2)
+// work items per row of the tensor-core DConv (rows of more than one need
+// part1/part2 and y: rows*T*dconv_tc_ystride(C) floats)
 int dconv_tc_tiles(int T);
+int dconv_tc_ystride(int C);
+int dconv_tc_const_floats(int C);
 bool launch_dconv_tc(const DConvArgs& a, cudaStream_t s);
 
 // transformer.cu

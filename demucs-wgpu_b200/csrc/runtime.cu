@@ -775,7 +775,7 @@ void run_dconv(dmx_handle* h, const DConvFull& dc, float* x, int rows, int T, bo
   }
   const int tiles = tc ? dconv_tc_tiles(T) : dconv_tiles(T);
   const bool fused = tc ? tiles == 1 : dconv_row_fused(T);
-  float* y = (fused || tc) ? nullptr : h->falloc((size_t)positions * hid);
+  float* y = fused ? nullptr : h->falloc((size_t)positions * (tc ? dconv_tc_ystride(C) : hid));
   double* part = fused ? nullptr : h->dalloc((size_t)rows * tiles * 4);
   for (int d = 0; d < 2; ++d) {
     const DConvLayerW& L = dc.layer[d];
@@ -1391,7 +1391,7 @@ void load_model(dmx_handle* h, const std::map<std::string, HostTensor>& t) {
         const size_t e = (size_t)n * 16 + dconv_tc_slot(hid, i);
         w[(size_t)n * act + i] = (double)wb.host[p2.tc_off + e] + (double)wb.host[p2.tc_lo_off + e];
       }
-    Lw.zq.assign(act + act * (act + 1) / 2, 0.f);
+    Lw.zq.assign(dconv_tc_const_floats(C), 0.f);
     for (int i = 0; i < act; ++i) {
       double v = 0.0;
       for (int n = 0; n < 2 * C; ++n) v += w[(size_t)n * act + i];
@@ -1403,6 +1403,12 @@ void load_model(dmx_handle* h, const std::map<std::string, HostTensor>& t) {
         for (int n = 0; n < 2 * C; ++n) m += w[(size_t)n * act + i] * w[(size_t)n * act + j];
         Lw.zq[idx] = (float)(i == j ? m : 2.0 * m);
       }
+    float* tail = Lw.zq.data() + act + act * (act + 1) / 2;
+    for (int h = 0; h < hid; ++h) {
+      tail[h] = wb.host[Lw.conv1.b_off + h];
+      tail[hid + h] = wb.host[Lw.n1w.off + h];
+      tail[2 * hid + h] = wb.host[Lw.n1b.off + h];
+    }
   };
   auto load_dc = [&](const std::string& prefix, int C, DConvFull* dc) {
     dc->C = C;
