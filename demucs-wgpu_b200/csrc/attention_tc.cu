@@ -41,6 +41,15 @@ constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + 256;
 constexpr uint32_t TM_Q = 0, TM_S = 64, TM_O = 192;  // S buffers at 64 and 128
 constexpr float kRescale = 8.0f;  // log2 of the largest P tolerated before O is rescaled
 
+// 2^x by the hardware approximation (PTX ex2.approx.ftz: relative error near
+// 2^-22, results below 2^-126 flushed to 0), ample for P that is rounded to
+// tf32 next.
+DMX_DEVICE float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
 struct AttnParams {
   const float* q;
   int ldq;
@@ -195,12 +204,18 @@ __global__ void __launch_bounds__(192, 2)
       __syncwarp();
       tmem_ld32(sb, sv);
       tmem_ld32(sb + 32, sv + 32);
-      float mx = -INFINITY;
+      // the row's maximum over raw scores (sl > 0 keeps the order), eight
+      // independent chains
+      float mx8[8];
 #pragma unroll
-      for (int i = 0; i < 64; ++i) {
-        sv[i] *= sl;
-        mx = fmaxf(mx, sv[i]);
-      }
+      for (int i = 0; i < 8; ++i) mx8[i] = sv[i];
+#pragma unroll
+      for (int i = 8; i < 64; ++i) mx8[i % 8] = fmaxf(mx8[i % 8], sv[i]);
+#pragma unroll
+      for (int w = 4; w; w >>= 1)
+#pragma unroll
+        for (int i = 0; i < w; ++i) mx8[i] = fmaxf(mx8[i], mx8[i + w]);
+      const float mx = mx8[0] * sl;
       const bool raise = mx > m + kRescale;
       if (__any_sync(0xffffffffu, raise)) {
         const float mnew = raise ? mx : m;
@@ -222,14 +237,21 @@ __global__ void __launch_bounds__(192, 2)
           }
         }
       }
-      // P = exp2(s - m), rounded to nearest tf32, over S in TMEM
-      float rs = 0.f;
+      // P = 2^(s sl - m), rounded to nearest tf32, over S in TMEM; the row
+      // sum in eight independent chains
+      float rs8[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) rs8[i] = 0.f;
 #pragma unroll
       for (int i = 0; i < 64; ++i) {
-        sv[i] = round_tf32(exp2f(sv[i] - m));
-        rs += sv[i];
+        sv[i] = round_tf32(ex2_approx(fmaf(sv[i], sl, -m)));
+        rs8[i % 8] += sv[i];
       }
-      l += rs;
+#pragma unroll
+      for (int w = 4; w; w >>= 1)
+#pragma unroll
+        for (int i = 0; i < w; ++i) rs8[i] += rs8[i + w];
+      l += rs8[0];
       tmem_st32(sb, sv);
       tmem_st32(sb + 32, sv + 32);
       tmem_st_wait();
