@@ -13,7 +13,8 @@
 // Warp 0 streams K and V^T with TMA; warp 1 issues the MMAs, S of key tile
 // j+1 ahead of P V of tile j; warps 2-5 own one query row each: they load the
 // row of Q into TMEM, then per key tile read S, run the online softmax and
-// write P (rounded to nearest tf32) back over S. The running max is only
+// write P back over S (truncated to tf32, as the tensor core reads it, so the
+// row sum adds exactly the weights the MMA uses). The running max is only
 // raised when a row's new maximum exceeds it by more than 2^8 (then O is
 // rescaled in TMEM); otherwise P = exp(s - m) with the stale m, which is
 // exact algebra and stays below 2^8. q, k, v arrive rounded to nearest tf32
@@ -44,6 +45,8 @@ constexpr float kRescale = 8.0f;  // log2 of the largest P tolerated before O is
 // 2^x by the hardware approximation (PTX ex2.approx.ftz: relative error near
 // 2^-22, results below 2^-126 flushed to 0), ample for P that is rounded to
 // tf32 next.
+DMX_DEVICE float trunc_tf32(float x) { return __uint_as_float(__float_as_uint(x) & 0xFFFFE000u); }
+
 DMX_DEVICE float ex2_approx(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
@@ -237,21 +240,23 @@ __global__ void __launch_bounds__(192, 2)
           }
         }
       }
-      // P = 2^(s sl - m), rounded to nearest tf32, over S in TMEM; the row
-      // sum in eight independent chains
-      float rs8[8];
+      // P = 2^(s sl - m) over S in TMEM, with paired f32 arithmetic. The
+      // tensor core reads P truncated to tf32, so the row sum adds the
+      // truncated values (four independent pair chains) and O / l stays an
+      // exact weighted mean of the V rows.
+      const float2 sl2 = make_float2(sl, sl), nm2 = make_float2(-m, -m);
+      float2 rs4[4];
 #pragma unroll
-      for (int i = 0; i < 8; ++i) rs8[i] = 0.f;
+      for (int i = 0; i < 4; ++i) rs4[i] = make_float2(0.f, 0.f);
 #pragma unroll
-      for (int i = 0; i < 64; ++i) {
-        sv[i] = round_tf32(ex2_approx(fmaf(sv[i], sl, -m)));
-        rs8[i % 8] += sv[i];
+      for (int i = 0; i < 32; ++i) {
+        const float2 t = __ffma2_rn(make_float2(sv[2 * i], sv[2 * i + 1]), sl2, nm2);
+        sv[2 * i] = trunc_tf32(ex2_approx(t.x));
+        sv[2 * i + 1] = trunc_tf32(ex2_approx(t.y));
+        rs4[i % 4] = __fadd2_rn(rs4[i % 4], make_float2(sv[2 * i], sv[2 * i + 1]));
       }
-#pragma unroll
-      for (int w = 4; w; w >>= 1)
-#pragma unroll
-        for (int i = 0; i < w; ++i) rs8[i] += rs8[i + w];
-      l += rs8[0];
+      rs4[0] = __fadd2_rn(__fadd2_rn(rs4[0], rs4[1]), __fadd2_rn(rs4[2], rs4[3]));
+      l += rs4[0].x + rs4[0].y;
       tmem_st32(sb, sv);
       tmem_st32(sb + 32, sv + 32);
       tmem_st_wait();
