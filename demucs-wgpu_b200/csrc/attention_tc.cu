@@ -45,6 +45,12 @@ constexpr float kRescale = 8.0f;  // log2 of the largest P tolerated before O is
 // 2^x by the hardware approximation (PTX ex2.approx.ftz: relative error near
 // 2^-22, results below 2^-126 flushed to 0), ample for P that is rounded to
 // tf32 next.
+DMX_DEVICE float fmax3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
 DMX_DEVICE float trunc_tf32(float x) { return __uint_as_float(__float_as_uint(x) & 0xFFFFE000u); }
 
 DMX_DEVICE float ex2_approx(float x) {
@@ -204,21 +210,24 @@ __global__ void __launch_bounds__(192, 2)
       asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
       const uint32_t sb = tmem + lane_base + TM_S + (uint32_t)((j & 1) * 64);
       float sv[64];
-      __syncwarp();
-      tmem_ld32(sb, sv);
-      tmem_ld32(sb + 32, sv + 32);
-      // the row's maximum over raw scores (sl > 0 keeps the order), eight
-      // independent chains
+      {
+        uint32_t sr[64];
+        __syncwarp();
+        tmem_ld32_nw(sb, sr);
+        tmem_ld32_nw(sb + 32, sr + 32);
+        tmem_ld_wait<64>(sr);
+#pragma unroll
+        for (int i = 0; i < 64; ++i) sv[i] = __uint_as_float(sr[i]);
+      }
+      // the row's maximum over raw scores (sl > 0 keeps the order): three-
+      // input max in eight independent chains
       float mx8[8];
 #pragma unroll
       for (int i = 0; i < 8; ++i) mx8[i] = sv[i];
 #pragma unroll
-      for (int i = 8; i < 64; ++i) mx8[i % 8] = fmaxf(mx8[i % 8], sv[i]);
-#pragma unroll
-      for (int w = 4; w; w >>= 1)
-#pragma unroll
-        for (int i = 0; i < w; ++i) mx8[i] = fmaxf(mx8[i], mx8[i + w]);
-      const float mx = mx8[0] * sl;
+      for (int i = 8; i < 64; i += 2) mx8[(i / 2) % 8] = fmax3(mx8[(i / 2) % 8], sv[i], sv[i + 1]);
+      const float mx = fmaxf(fmax3(mx8[0], mx8[1], mx8[2]),
+                             fmax3(fmax3(mx8[3], mx8[4], mx8[5]), mx8[6], mx8[7])) * sl;
       const bool raise = mx > m + kRescale;
       if (__any_sync(0xffffffffu, raise)) {
         const float mnew = raise ? mx : m;
