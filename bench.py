@@ -42,9 +42,9 @@ UNIT = "audio-s/s"
 # Measured DRAM bytes (read + write) per algorithmic byte for a kernel tag, from
 # one ncu capture of that kernel (profiles/): roofline.traffic = ratio x the
 # tag's algorithmic bytes per launch. The attention capture is the layer-0
-# spectral self-attention on a 3-chunk track (52.7 MB of DRAM traffic for
+# spectral self-attention on a 3-chunk track (50.4 MB of DRAM traffic for
 # 66.1 MB of q, k, v, o); traffic scales with the chunks a launch processes.
-TRAFFIC_RATIO = {"xf.attention": 52.745 / 66.060}
+TRAFFIC_RATIO = {"xf.attention": 50.393 / 66.060}
 
 
 def workload(seconds):
