@@ -75,5 +75,8 @@ struct ConvParams {
 };
 
 void launch_conv_gemm(const ConvParams& p, int pro, int epi, cudaStream_t stream);
+// The first encoder convolutions (Cin 2/4, 8 taps, 48 GELU outputs, normalised
+// input, dense channels-last output; first_conv.cu). False: not that shape.
+bool launch_first_conv(const ConvParams& p, int pro, int epi, cudaStream_t stream);
 
 }  // namespace dmx

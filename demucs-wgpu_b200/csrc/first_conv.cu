@@ -1,0 +1,106 @@
+// The first encoder convolutions of both branches (host.rs:577-622 and the
+// time-branch twin): Cin = 4 (the CaC spectrogram) or 2 (the waveform), eight
+// taps at stride 4 along one axis with padding 2, Cout = 48, the segment's
+// normalisation applied on load and GELU on the way out.
+//
+// With K = 8 Cin <= 32 these are too thin for the tensor-core GEMM (a 16-byte
+// A row) and the general SIMT GEMM spends its time on tile bookkeeping. Here
+// one CTA takes 128 consecutive output positions: each thread gathers the K
+// normalised inputs of one position into registers and accumulates 24 of the
+// 48 channels against weights held in shared memory (warp-uniform broadcast
+// reads); the 128 x 48 output tile is staged in shared memory and leaves as
+// one contiguous, coalesced 24 KB store. fp32 throughout.
+#include "common.cuh"
+#include "conv_gemm.cuh"
+
+namespace dmx {
+
+namespace {
+
+constexpr int kCo = 48, kBM = 128, kRow = kCo + 4;  // padded staging row (conflict-free)
+
+template <int CIN>
+__global__ void __launch_bounds__(256) first_conv_kernel(const ConvParams p) {
+  constexpr int K = 8 * CIN;
+  __shared__ __align__(16) float ws[K][kCo];
+  __shared__ float bs[kCo];
+  __shared__ __align__(16) float os[kBM * kRow];
+  const int tid = threadIdx.x;
+  for (int i = tid; i < K * kCo; i += blockDim.x) ws[i / kCo][i % kCo] = p.w[(i / kCo) * p.Npad + i % kCo];
+  if (tid < kCo) bs[tid] = p.bias[tid];
+
+  const int64_t M = (int64_t)p.B * p.Hq * p.Wq;
+  const int64_t m0 = (int64_t)blockIdx.x * kBM;
+  const int pl = tid % kBM, half = tid / kBM;  // position, channels 24 half .. +24
+  const int64_t pos = m0 + pl;
+  float in[K];
+  if (pos < M) {
+    const int64_t plane = (int64_t)p.Hq * p.Wq;
+    const int b = (int)(pos / plane);
+    const int64_t rem = pos - (int64_t)b * plane;
+    const int y = (int)(rem / p.Wq), x = (int)(rem % p.Wq);
+    const float4 nz = reinterpret_cast<const float4*>(p.pro_scale)[b];
+    const float* xb = p.x + (int64_t)b * p.i_bs;
+#pragma unroll
+    for (int tap = 0; tap < 8; ++tap) {
+      const int iy = y * p.sy + p.dy[tap], ix = x * p.sx + p.dx[tap];
+      const bool inside = iy >= 0 && iy < p.Hin && ix >= 0 && ix < p.Win;
+      const float* src = xb + (int64_t)iy * p.i_ys + (int64_t)ix * p.i_xs;
+#pragma unroll
+      for (int ci = 0; ci < CIN; ++ci)
+        in[tap * CIN + ci] = inside ? (__ldg(src + (int64_t)ci * p.i_cs) - nz.x) * nz.y : 0.f;
+    }
+  } else {
+#pragma unroll
+    for (int k = 0; k < K; ++k) in[k] = 0.f;
+  }
+  __syncthreads();
+
+  float acc[24];
+#pragma unroll
+  for (int j = 0; j < 24; ++j) acc[j] = bs[24 * half + j];
+#pragma unroll
+  for (int k = 0; k < K; ++k) {
+    const float4* wr = reinterpret_cast<const float4*>(&ws[k][24 * half]);
+#pragma unroll
+    for (int c = 0; c < 6; ++c) {
+      const float4 w = wr[c];
+      acc[4 * c] = fmaf(in[k], w.x, acc[4 * c]);
+      acc[4 * c + 1] = fmaf(in[k], w.y, acc[4 * c + 1]);
+      acc[4 * c + 2] = fmaf(in[k], w.z, acc[4 * c + 2]);
+      acc[4 * c + 3] = fmaf(in[k], w.w, acc[4 * c + 3]);
+    }
+  }
+  float4* orow = reinterpret_cast<float4*>(&os[pl * kRow + 24 * half]);
+#pragma unroll
+  for (int c = 0; c < 6; ++c)
+    orow[c] = make_float4(gelu(acc[4 * c]), gelu(acc[4 * c + 1]), gelu(acc[4 * c + 2]),
+                          gelu(acc[4 * c + 3]));
+  __syncthreads();
+  // the tile's positions are consecutive rows of the channels-last output
+  const int rows = M - m0 < kBM ? (int)(M - m0) : kBM;
+  float4* dst = reinterpret_cast<float4*>(p.out + m0 * kCo);
+  for (int i = tid; i < rows * (kCo / 4); i += blockDim.x) {
+    const int r = i / (kCo / 4), c = i % (kCo / 4);
+    dst[i] = *reinterpret_cast<const float4*>(&os[r * kRow + 4 * c]);
+  }
+}
+
+}  // namespace
+
+bool launch_first_conv(const ConvParams& p, int pro, int epi, cudaStream_t s) {
+  if (pro != PRO_BATCH_AFFINE || epi != EPI_GELU || (p.Cin != 2 && p.Cin != 4) || p.ntaps != 8 ||
+      p.K != 8 * p.Cin || p.N != kCo || p.Npad < kCo || p.epi_add || p.round_out || p.o_lim ||
+      p.o_off != 0 || p.o_xs != kCo || p.o_ys != (int64_t)p.Wq * kCo ||
+      p.o_bs != (int64_t)p.Hq * p.Wq * kCo || (reinterpret_cast<uintptr_t>(p.out) & 15))
+    return false;
+  const int64_t M = (int64_t)p.B * p.Hq * p.Wq;
+  const unsigned grid = (unsigned)((M + kBM - 1) / kBM);
+  if (p.Cin == 4)
+    first_conv_kernel<4><<<grid, 256, 0, s>>>(p);
+  else
+    first_conv_kernel<2><<<grid, 256, 0, s>>>(p);
+  return true;
+}
+
+}  // namespace dmx

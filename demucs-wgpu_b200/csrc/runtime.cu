@@ -536,6 +536,7 @@ struct dmx_handle {
     if (pk && (cfg.precision == DMX_TF32 || cfg.precision == DMX_TF32X3) &&
         try_tc(p, pro, epi, *pk))
       return;
+    if (launch_first_conv(p, pro, epi, stream)) return;
     launch_conv_gemm(p, pro, epi, stream);
   }
 
