@@ -76,7 +76,9 @@ struct ConvParams {
 
 void launch_conv_gemm(const ConvParams& p, int pro, int epi, cudaStream_t stream);
 // The first encoder convolutions (Cin 2/4, 8 taps, 48 GELU outputs, normalised
-// input, dense channels-last output; first_conv.cu). False: not that shape.
-bool launch_first_conv(const ConvParams& p, int pro, int epi, cudaStream_t stream);
+// input, dense channels-last output; first_conv.cu). w_host: [K][48] weights
+// then the 48 biases, in host memory. False: not that shape.
+bool launch_first_conv(const ConvParams& p, int pro, int epi, const float* w_host,
+                       cudaStream_t stream);
 
 }  // namespace dmx

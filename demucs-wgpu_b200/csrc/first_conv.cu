@@ -7,9 +7,10 @@
 // A row) and the general SIMT GEMM spends its time on tile bookkeeping. Here
 // one CTA takes 128 consecutive output positions: each thread gathers the K
 // normalised inputs of one position into registers and accumulates 24 of the
-// 48 channels against weights held in shared memory (warp-uniform broadcast
-// reads); the 128 x 48 output tile is staged in shared memory and leaves as
-// one contiguous, coalesced 24 KB store. fp32 throughout.
+// 48 channels; the weights (at most 6 KB) travel as a launch parameter, so the
+// FMAs read them straight from the constant bank. The 128 x 48 output tile is
+// staged in shared memory and leaves as one contiguous, coalesced 24 KB store.
+// fp32 throughout.
 #include "common.cuh"
 #include "conv_gemm.cuh"
 
@@ -20,14 +21,28 @@ namespace {
 constexpr int kCo = 48, kBM = 128, kRow = kCo + 4;  // padded staging row (conflict-free)
 
 template <int CIN>
-__global__ void __launch_bounds__(256) first_conv_kernel(const ConvParams p) {
+struct FirstConvW {
+  float w[8 * CIN][kCo];
+  float b[kCo];
+};
+
+// 24 channels from 24 h of one position, weights from the constant bank
+template <int CIN, int H>
+DMX_DEVICE void accumulate(const FirstConvW<CIN>& cw, const float* in, float* acc) {
+#pragma unroll
+  for (int j = 0; j < 24; ++j) acc[j] = cw.b[24 * H + j];
+#pragma unroll
+  for (int k = 0; k < 8 * CIN; ++k)
+#pragma unroll
+    for (int j = 0; j < 24; ++j) acc[j] = fmaf(in[k], cw.w[k][24 * H + j], acc[j]);
+}
+
+template <int CIN>
+__global__ void __launch_bounds__(256) first_conv_kernel(const ConvParams p,
+                                                         const __grid_constant__ FirstConvW<CIN> cw) {
   constexpr int K = 8 * CIN;
-  __shared__ __align__(16) float ws[K][kCo];
-  __shared__ float bs[kCo];
   __shared__ __align__(16) float os[kBM * kRow];
   const int tid = threadIdx.x;
-  for (int i = tid; i < K * kCo; i += blockDim.x) ws[i / kCo][i % kCo] = p.w[(i / kCo) * p.Npad + i % kCo];
-  if (tid < kCo) bs[tid] = p.bias[tid];
 
   const int64_t M = (int64_t)p.B * p.Hq * p.Wq;
   const int64_t m0 = (int64_t)blockIdx.x * kBM;
@@ -54,23 +69,12 @@ __global__ void __launch_bounds__(256) first_conv_kernel(const ConvParams p) {
 #pragma unroll
     for (int k = 0; k < K; ++k) in[k] = 0.f;
   }
-  __syncthreads();
 
   float acc[24];
-#pragma unroll
-  for (int j = 0; j < 24; ++j) acc[j] = bs[24 * half + j];
-#pragma unroll
-  for (int k = 0; k < K; ++k) {
-    const float4* wr = reinterpret_cast<const float4*>(&ws[k][24 * half]);
-#pragma unroll
-    for (int c = 0; c < 6; ++c) {
-      const float4 w = wr[c];
-      acc[4 * c] = fmaf(in[k], w.x, acc[4 * c]);
-      acc[4 * c + 1] = fmaf(in[k], w.y, acc[4 * c + 1]);
-      acc[4 * c + 2] = fmaf(in[k], w.z, acc[4 * c + 2]);
-      acc[4 * c + 3] = fmaf(in[k], w.w, acc[4 * c + 3]);
-    }
-  }
+  if (half == 0)  // warp-uniform
+    accumulate<CIN, 0>(cw, in, acc);
+  else
+    accumulate<CIN, 1>(cw, in, acc);
   float4* orow = reinterpret_cast<float4*>(&os[pl * kRow + 24 * half]);
 #pragma unroll
   for (int c = 0; c < 6; ++c)
@@ -86,9 +90,18 @@ __global__ void __launch_bounds__(256) first_conv_kernel(const ConvParams p) {
   }
 }
 
+template <int CIN>
+void launch_cin(const ConvParams& p, const float* w_host, unsigned grid, cudaStream_t s) {
+  FirstConvW<CIN> cw;
+  for (int k = 0; k < 8 * CIN; ++k)
+    for (int n = 0; n < kCo; ++n) cw.w[k][n] = w_host[k * kCo + n];
+  for (int n = 0; n < kCo; ++n) cw.b[n] = w_host[8 * CIN * kCo + n];
+  first_conv_kernel<CIN><<<grid, 256, 0, s>>>(p, cw);
+}
+
 }  // namespace
 
-bool launch_first_conv(const ConvParams& p, int pro, int epi, cudaStream_t s) {
+bool launch_first_conv(const ConvParams& p, int pro, int epi, const float* w_host, cudaStream_t s) {
   if (pro != PRO_BATCH_AFFINE || epi != EPI_GELU || (p.Cin != 2 && p.Cin != 4) || p.ntaps != 8 ||
       p.K != 8 * p.Cin || p.N != kCo || p.Npad < kCo || p.epi_add || p.round_out || p.o_lim ||
       p.o_off != 0 || p.o_xs != kCo || p.o_ys != (int64_t)p.Wq * kCo ||
@@ -97,9 +110,9 @@ bool launch_first_conv(const ConvParams& p, int pro, int epi, cudaStream_t s) {
   const int64_t M = (int64_t)p.B * p.Hq * p.Wq;
   const unsigned grid = (unsigned)((M + kBM - 1) / kBM);
   if (p.Cin == 4)
-    first_conv_kernel<4><<<grid, 256, 0, s>>>(p);
+    launch_cin<4>(p, w_host, grid, s);
   else
-    first_conv_kernel<2><<<grid, 256, 0, s>>>(p);
+    launch_cin<2>(p, w_host, grid, s);
   return true;
 }
 

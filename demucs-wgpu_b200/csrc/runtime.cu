@@ -187,6 +187,9 @@ struct Packed {
   std::vector<Tap> taps;
   const float* w = nullptr;
   const float* bias = nullptr;
+  // thin first convolutions (K <= 32, 48 outputs): [K][48] then the bias, in
+  // host memory, for the kernel that takes them as a launch parameter
+  std::vector<float> host_w;
 };
 
 struct Vec {  // a plain per-channel vector on the device
@@ -315,6 +318,12 @@ struct Loader {
           }
         }
       wb.host[p.b_off + n] = bias[co];
+    }
+    if (p.K <= 32 && cols == 48 && !glu) {
+      p.host_w.resize((size_t)p.K * 48 + 48);
+      for (int k = 0; k < p.K; ++k)
+        for (int n = 0; n < 48; ++n) p.host_w[(size_t)k * 48 + n] = wb.host[p.w_off + (size_t)k * p.Npad + n];
+      for (int n = 0; n < 48; ++n) p.host_w[(size_t)p.K * 48 + n] = wb.host[p.b_off + n];
     }
     return p;
   }
@@ -536,7 +545,8 @@ struct dmx_handle {
     if (pk && (cfg.precision == DMX_TF32 || cfg.precision == DMX_TF32X3) &&
         try_tc(p, pro, epi, *pk))
       return;
-    if (launch_first_conv(p, pro, epi, stream)) return;
+    if (pk && !pk->host_w.empty() && launch_first_conv(p, pro, epi, pk->host_w.data(), stream))
+      return;
     launch_conv_gemm(p, pro, epi, stream);
   }
 
