@@ -12,12 +12,13 @@
 //
 // Rows of at most kTile positions (the spectral branch: T = 336 frames) run in
 // ONE launch, one CTA per row: conv1 over the row, the row's moments reduced
-// in the CTA, g kept in shared memory, z computed twice (moments, then the
-// output) — x crosses HBM once each way (its second read, for the residual,
-// comes from L2). Longer rows (the waveform branch) are tiled in three
-// launches: conv1 + per-tile moments (y to HBM: C/8 channels), z moments per
-// tile, then the output; each tile reduces its row's per-tile moments in a
-// fixed order, so the result does not depend on scheduling.
+// in the CTA, g kept in shared memory, the moments of z taken from g alone
+// (sum z = v.g~, sum z^2 = g~'Mg~ with host-side v, M: z_moments below), then z
+// formed once, for the output — x crosses HBM once each way (its second read,
+// for the residual, comes from L2). Longer rows (the waveform branch) are
+// tiled in three launches: conv1 + per-tile moments (y to HBM: C/8 channels),
+// z moments per tile, then the output; each tile reduces its row's per-tile
+// moments in a fixed order, so the result does not depend on scheduling.
 //
 // Arithmetic is fp32 with f64 moment sums (the reference's GroupNorm
 // accumulates in f64, ops.rs:930-1094); every build precision uses it.
@@ -205,11 +206,10 @@ DMX_DEVICE void store_g(const float2 (&acc)[Dc<C>::PM][Dc<C>::HN / 2], const DCo
       for (int h = S::HID; h < S::HIDP; ++h) gs[p * S::HIDP + h] = 0.f;
 }
 
-// conv2 over the g rows of a tile. OUT = false: this thread's f64 moments of
-// z (value and gate channels); OUT = true: x[p][c] += gamma * GLU(GN2(z)).
-template <int C, bool OUT>
-DMX_DEVICE void conv2_tile(const float* gs, int np, const DConvArgs& a, float* xt, float mean2,
-                           float inv2, double& s, double& q) {
+// conv2 over the g rows of a tile: x[p][c] += gamma * GLU(GN2(z)).
+template <int C>
+DMX_DEVICE void conv2_out(const float* gs, int np, const DConvArgs& a, float* xt, float mean2,
+                          float inv2) {
   using S = Dc<C>;
   const int c = threadIdx.x % C, g0 = threadIdx.x / C;
   float2 w[S::HID];  // (value, gate) weights of channel c
@@ -217,18 +217,11 @@ DMX_DEVICE void conv2_tile(const float* gs, int np, const DConvArgs& a, float* x
   for (int h = 0; h < S::HID; ++h)
     w[h] = *reinterpret_cast<const float2*>(a.w2 + (int64_t)h * a.w2_ld + 2 * c);
   const float2 bias = *reinterpret_cast<const float2*>(a.b2 + 2 * c);
-  float vs = 0.f, vsh = 0.f, gsc = 0.f, gsh = 0.f, gamma = 0.f;
-  if (OUT) {
-    vs = inv2 * a.n2w[c];
-    vsh = a.n2b[c] - mean2 * vs;
-    gsc = inv2 * a.n2w[c + C];
-    gsh = a.n2b[c + C] - mean2 * gsc;
-    gamma = a.gamma[c];
-  }
-  float fs = 0.f, fq = 0.f;
-  int run = 0;
-  s = 0.0;
-  q = 0.0;
+  const float vs = inv2 * a.n2w[c];
+  const float vsh = a.n2b[c] - mean2 * vs;
+  const float gsc = inv2 * a.n2w[c + C];
+  const float gsh = a.n2b[c + C] - mean2 * gsc;
+  const float gamma = a.gamma[c];
   for (int p = g0; p < np; p += S::G) {
     const float* gp = gs + p * S::HIDP;
     float2 z = bias;
@@ -240,29 +233,63 @@ DMX_DEVICE void conv2_tile(const float* gs, int np, const DConvArgs& a, float* x
       if (h + 2 < S::HID) z = __ffma2_rn(w[h + 2], make_float2(g4.z, g4.z), z);
       if (h + 3 < S::HID) z = __ffma2_rn(w[h + 3], make_float2(g4.w, g4.w), z);
     }
-    const float v = z.x, gt = z.y;
-    if (OUT) {
-      const float value = v * vs + vsh;
-      const float gate = gt * gsc + gsh;
-      float* o = xt + (int64_t)p * C + c;
-      const float r = *o + gamma * (value * sigmoid(gate));
-      *o = a.round_out ? round_tf32(r) : r;
-    } else {
-      // short f32 runs (8 positions, 16 terms) folded into f64
-      fs += v + gt;
-      fq += fmaf(v, v, gt * gt);
-      if (++run == 8) {
-        s += (double)fs;
-        q += (double)fq;
-        fs = fq = 0.f;
-        run = 0;
+    const float value = z.x * vs + vsh;
+    const float gate = z.y * gsc + gsh;
+    float* o = xt + (int64_t)p * C + c;
+    const float r = *o + gamma * (value * sigmoid(gate));
+    *o = a.round_out ? round_tf32(r) : r;
+  }
+}
+
+// Moments of z = conv2(g) over the tile's positions p < np without forming z:
+// with g~ = (g, 1) and w~_n = (conv2 column n, its bias), sum_n z_n = v.g~ and
+// sum_n z_n^2 = g~'Mg~ (v, M from the host: zq holds v, then M row by row at a
+// stride of ZL floats, staged in shared memory). One position per thread and
+// pass, f32 per position, f64 across them.
+template <int C>
+struct Zq {
+  static constexpr int ACT = C / 8 + 1;
+  static constexpr int ZL = (ACT + 3) / 4 * 4;
+  static constexpr int N = ZL * (ACT + 1);
+};
+
+template <int C>
+DMX_DEVICE void z_moments(const float* gs, int np, const float* zq, double& s, double& q) {
+  using S = Dc<C>;
+  using Z = Zq<C>;
+  s = 0.0;
+  q = 0.0;
+  for (int p = threadIdx.x; p < np; p += kThreads) {
+    const float* gp = gs + p * S::HIDP;
+    float g[Z::ZL];
+#pragma unroll
+    for (int j = 0; j < Z::ZL; ++j) g[j] = j < S::HID ? gp[j] : (j == S::HID ? 1.0f : 0.f);
+    float l = 0.f;
+#pragma unroll
+    for (int j = 0; j < Z::ZL; ++j) l = fmaf(zq[j], g[j], l);
+    float qf = 0.f;
+#pragma unroll 1
+    for (int i = 0; i < Z::ACT; ++i) {
+      const float4* mr = reinterpret_cast<const float4*>(zq + Z::ZL * (1 + i));
+      float t = 0.f;
+#pragma unroll
+      for (int j4 = 0; j4 < Z::ZL / 4; ++j4) {
+        const float4 m = mr[j4];
+        t = fmaf(m.x, g[4 * j4], t);
+        t = fmaf(m.y, g[4 * j4 + 1], t);
+        t = fmaf(m.z, g[4 * j4 + 2], t);
+        t = fmaf(m.w, g[4 * j4 + 3], t);
       }
+      qf = fmaf(i < S::HID ? gp[i] : 1.0f, t, qf);
     }
+    s += (double)l;
+    q += (double)qf;
   }
-  if (!OUT) {
-    s += (double)fs;
-    q += (double)fq;
-  }
+}
+
+template <int C>
+DMX_DEVICE void stage_zq(const float* zq, float* zqs) {
+  for (int i = threadIdx.x; i < Zq<C>::N; i += kThreads) zqs[i] = zq[i];
 }
 
 template <int C>
@@ -282,8 +309,10 @@ __global__ void __launch_bounds__(kThreads, C >= 384 ? 1 : 2) dconv_row_kernel(c
   float* ws = xs + S::XS;
   float* gs = ws + S::WS;
   __shared__ double red[2 * kWarps];
+  __shared__ __align__(16) float zqs[Zq<C>::N];
   const int row = blockIdx.x, T = a.T;
   float* xr = a.x + (int64_t)row * T * C;
+  stage_zq<C>(a.zq_dev, zqs);
 
   float2 acc[S::PM][S::HN / 2];
   conv1_tile<C>(xr, T, 0, a.dil, a, xs, ws, acc);
@@ -295,11 +324,11 @@ __global__ void __launch_bounds__(kThreads, C >= 384 ? 1 : 2) dconv_row_kernel(c
   store_g<C>(acc, a, mean, inv, gs);
   __syncthreads();
 
-  conv2_tile<C, false>(gs, T, a, xr, 0.f, 0.f, s, q);
+  z_moments<C>(gs, T, zqs, s, q);
   block_sum2(s, q, red);
   float mean2, inv2;
   moments_to_norm(s, q, 2.0 * C * T, mean2, inv2);
-  conv2_tile<C, true>(gs, T, a, xr, mean2, inv2, s, q);
+  conv2_out<C>(gs, T, a, xr, mean2, inv2);
 }
 
 // Tiled, step 1: conv1 of one tile -> y (HBM, compact HID channels) and the
@@ -345,8 +374,10 @@ __global__ void __launch_bounds__(kThreads, C >= 384 ? 1 : 2) dconv_conv2_kernel
   extern __shared__ __align__(16) float smem[];
   float* gs = smem;
   __shared__ double red[2 * kWarps];
+  __shared__ __align__(16) float zqs[OUT ? 4 : Zq<C>::N];
   const int tile = blockIdx.x, row = blockIdx.y, T = a.T;
   const int t0 = tile * kTile, np = min(kTile, T - t0);
+  if (!OUT) stage_zq<C>(a.zq_dev, zqs);
 
   float mean, inv;
   row_moments(a.part1 + 2 * (int64_t)row * a.tiles, a.tiles, (double)S::HID * T, mean, inv, red);
@@ -369,7 +400,10 @@ __global__ void __launch_bounds__(kThreads, C >= 384 ? 1 : 2) dconv_conv2_kernel
   __syncthreads();
   double s, q;
   float* xt = a.x + ((int64_t)row * T + t0) * C;
-  conv2_tile<C, OUT>(gs, np, a, xt, mean2, inv2, s, q);
+  if (OUT)
+    conv2_out<C>(gs, np, a, xt, mean2, inv2);
+  else
+    z_moments<C>(gs, np, zqs, s, q);
   if (!OUT) {
     block_sum2(s, q, red);
     if (threadIdx.x == 0) {
@@ -414,7 +448,7 @@ int dconv_tiles(int T) { return (T + kTile - 1) / kTile; }
 bool dconv_row_fused(int T) { return T <= kTile; }
 
 bool launch_dconv(const DConvArgs& a, cudaStream_t s) {
-  if (a.dil < 1 || a.dil > kMaxDil || a.rows <= 0 || a.T <= 0) return false;
+  if (a.dil < 1 || a.dil > kMaxDil || a.rows <= 0 || a.T <= 0 || !a.zq_dev) return false;
   if (a.T > kTile && (!a.y || !a.part1 || !a.part2 || a.tiles != dconv_tiles(a.T))) return false;
   switch (a.C) {
     case 48: launch_c<48>(a, s); return true;

@@ -55,7 +55,13 @@ struct DConvArgs {
   // triangle of M (off-diagonal doubled; dconv_tc_slot order) for the moments
   // of conv2's output, then conv1's bias and GroupNorm1's weight and bias
   const float* zq_host;
+  // device memory, dconv_zq_floats(C) floats: the same moments for the SIMT
+  // kernels over g~ = (g_0 .. g_{C/8-1}, 1) with conv2's bias as the last
+  // input: v, then M row by row, each of dconv_zq_stride(C) floats (zero padded)
+  const float* zq_dev;
 };
+inline int dconv_zq_stride(int C) { return (C / 8 + 1 + 3) / 4 * 4; }
+inline int dconv_zq_floats(int C) { return dconv_zq_stride(C) * (C / 8 + 2); }
 // K slot (of 16) of conv2 input i in the tensor-core weight copies of the
 // narrow layers: hidden channels i < hid/2 at slot i, the others at
 // 8 + i - hid/2, and i == hid (the constant-1 bias input) at slot 15.

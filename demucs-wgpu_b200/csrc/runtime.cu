@@ -426,6 +426,7 @@ struct DConvLayerW {
   Packed conv1, conv2;
   Vec n1w, n1b, n2w, n2b, gamma;
   std::vector<float> zq;  // the fused tensor-core kernel's moment constants (host memory)
+  size_t zq_off = 0;      // the SIMT kernels' moment constants (weight arena)
 };
 
 }  // namespace
@@ -821,6 +822,7 @@ void run_dconv(dmx_handle* h, const DConvFull& dc, float* x, int rows, int T, bo
     a.w2_tc_lo = h->W(L.conv2.tc_lo_off);
     a.w2_npad = L.conv2.Npad;
     a.zq_host = L.zq.empty() ? nullptr : L.zq.data();
+    a.zq_dev = h->W(L.zq_off);
     // algorithmic work: conv1 (3C -> hid) + conv2 (hid -> 2C) per position;
     // x read once and written once
     h->mark(std::string(tc ? (fused ? "dconv.tc" : "dconv.tctiled")
@@ -1421,6 +1423,32 @@ void load_model(dmx_handle* h, const std::map<std::string, HostTensor>& t) {
       tail[2 * hid + h] = wb.host[Lw.n1b.off + h];
     }
   };
+  // The SIMT DConv kernels' GroupNorm2 moments from g: w~_n = (conv2 column
+  // n's weights, its bias) over all 2C columns; v = sum_n w~_n and
+  // M = sum_n w~_n w~_n' (f64, stored as f32).
+  auto simt_dconv_moments = [&](int C, DConvLayerW& Lw) {
+    const int hid = C / 8, act = hid + 1;
+    const Packed& p2 = Lw.conv2;
+    std::vector<double> w((size_t)2 * C * act);
+    for (int n = 0; n < 2 * C; ++n) {
+      for (int h = 0; h < hid; ++h) w[(size_t)n * act + h] = wb.host[p2.w_off + (size_t)h * p2.Npad + n];
+      w[(size_t)n * act + hid] = wb.host[p2.b_off + n];
+    }
+    const int ld = dconv_zq_stride(C);
+    Lw.zq_off = wb.alloc(dconv_zq_floats(C));
+    float* z = &wb.host[Lw.zq_off];  // zero filled by alloc
+    for (int i = 0; i < act; ++i) {
+      double v = 0.0;
+      for (int n = 0; n < 2 * C; ++n) v += w[(size_t)n * act + i];
+      z[i] = (float)v;
+    }
+    for (int i = 0; i < act; ++i)
+      for (int j = 0; j < act; ++j) {
+        double m = 0.0;
+        for (int n = 0; n < 2 * C; ++n) m += w[(size_t)n * act + i] * w[(size_t)n * act + j];
+        z[(size_t)ld * (1 + i) + j] = (float)m;
+      }
+  };
   auto load_dc = [&](const std::string& prefix, int C, DConvFull* dc) {
     dc->C = C;
     dc->hidden = C / 8;
@@ -1448,6 +1476,7 @@ void load_model(dmx_handle* h, const std::map<std::string, HostTensor>& t) {
       }
       if ((C == 48 || C == 96) && Lw.conv1.has_tc && Lw.conv2.has_tc && Lw.conv2.K == 16)
         tc_dconv_slots(C, Lw);
+      simt_dconv_moments(C, Lw);
       Lw.n2w = L.vec(at + ".4.weight", 2 * C);
       Lw.n2b = L.vec(at + ".4.bias", 2 * C);
       Lw.gamma = L.vec(at + ".6.scale", C);
