@@ -292,6 +292,79 @@ DMX_DEVICE void stage_zq(const float* zq, float* zqs) {
   for (int i = threadIdx.x; i < Zq<C>::N; i += kThreads) zqs[i] = zq[i];
 }
 
+// Row moments of z for the tensor-core DConv path (three GEMMs, runtime.cu):
+// y (positions, ld) is conv1's output with its row moments in st1 (sum, sum
+// of squares); per position g = GELU(GroupNorm1(y)) and the quadratic form
+// above; per CTA one f64 sum per row, added into st2 with f64 atomics (as the
+// GEMM epilogues do). Grid (ceil(T / 256), rows). Each thread keeps its g~ in
+// its own column of shared memory for the rolled loop over M's rows.
+template <int C>
+__global__ void __launch_bounds__(256) dconv_zstats_kernel(const float* y, int ld, int T,
+                                                           const float* n1w, const float* n1b,
+                                                           const double* st1, double* st2,
+                                                           const float* zq) {
+  using Z = Zq<C>;
+  constexpr int HID = C / 8;
+  extern __shared__ __align__(16) float zsm[];
+  float* zqs = zsm;              // Z::N
+  float* gcol = zsm + Z::N;      // [ZL][256]
+  __shared__ float sc[HID], sh[HID];
+  __shared__ double red[16];
+  const int row = blockIdx.y, tid = threadIdx.x;
+  for (int i = tid; i < Z::N; i += 256) zqs[i] = zq[i];
+  if (tid < HID) {
+    const double cnt = (double)HID * T;
+    const double m = st1[2 * row] / cnt;
+    const double var = fmax(st1[2 * row + 1] / cnt - m * m, 0.0);
+    const float inv = 1.0f / sqrtf((float)(var + 1e-5));
+    sc[tid] = inv * n1w[tid];
+    sh[tid] = n1b[tid] - (float)m * sc[tid];
+  }
+  __syncthreads();
+  const int t = blockIdx.x * 256 + tid;
+  float l = 0.f, qf = 0.f;
+  if (t < T) {
+    const float* yp = y + ((int64_t)row * T + t) * ld;
+    float g[Z::ZL];
+#pragma unroll
+    for (int j = 0; j < Z::ZL; ++j) {
+      g[j] = j < HID ? gelu(yp[j] * sc[j] + sh[j]) : (j == HID ? 1.0f : 0.f);
+      gcol[j * 256 + tid] = g[j];
+      l = fmaf(zqs[j], g[j], l);
+    }
+#pragma unroll 1
+    for (int i = 0; i < Z::ACT; ++i) {
+      const float4* mr = reinterpret_cast<const float4*>(zqs + Z::ZL * (1 + i));
+      float tt = 0.f;
+#pragma unroll
+      for (int j4 = 0; j4 < Z::ZL / 4; ++j4) {
+        const float4 m = mr[j4];
+        tt = fmaf(m.x, g[4 * j4], tt);
+        tt = fmaf(m.y, g[4 * j4 + 1], tt);
+        tt = fmaf(m.z, g[4 * j4 + 2], tt);
+        tt = fmaf(m.w, g[4 * j4 + 3], tt);
+      }
+      qf = fmaf(gcol[i * 256 + tid], tt, qf);
+    }
+  }
+  double ds = l, dq = qf;
+  warp_sum2(ds, dq);
+  if ((tid & 31) == 0) {
+    red[2 * (tid >> 5)] = ds;
+    red[2 * (tid >> 5) + 1] = dq;
+  }
+  __syncthreads();
+  if (tid == 0) {
+    double a0 = 0.0, a1 = 0.0;
+    for (int w = 0; w < 8; ++w) {
+      a0 += red[2 * w];
+      a1 += red[2 * w + 1];
+    }
+    atomicAdd(&st2[2 * row], a0);
+    atomicAdd(&st2[2 * row + 1], a1);
+  }
+}
+
 template <int C>
 struct Smem {
   using S = Dc<C>;
@@ -441,7 +514,31 @@ void launch_c(const DConvArgs& a, cudaStream_t s) {
   dconv_conv2_kernel<C, true><<<grid, kThreads, M::kConv2, s>>>(a);
 }
 
+template <int C>
+void launch_zstats_c(const float* y, int ld, int rows, int T, const float* n1w, const float* n1b,
+                     const double* st1, double* st2, const float* zq, cudaStream_t s) {
+  const size_t bytes = sizeof(float) * (Zq<C>::N + Zq<C>::ZL * 256);
+  static bool configured = false;
+  if (!configured) {
+    set_smem(dconv_zstats_kernel<C>, bytes);
+    configured = true;
+  }
+  dconv_zstats_kernel<C><<<dim3((T + 255) / 256, rows), 256, bytes, s>>>(y, ld, T, n1w, n1b, st1,
+                                                                         st2, zq);
+}
+
 }  // namespace
+
+bool launch_dconv_zstats(int C, const float* y, int ld, int rows, int T, const float* n1w,
+                         const float* n1b, const double* st1, double* st2, const float* zq,
+                         cudaStream_t s) {
+  if (!zq || rows <= 0 || T <= 0 || ld < C / 8) return false;
+  switch (C) {
+    case 192: launch_zstats_c<192>(y, ld, rows, T, n1w, n1b, st1, st2, zq, s); return true;
+    case 384: launch_zstats_c<384>(y, ld, rows, T, n1w, n1b, st1, st2, zq, s); return true;
+    default: return false;
+  }
+}
 
 int dconv_tiles(int T) { return (T + kTile - 1) / kTile; }
 

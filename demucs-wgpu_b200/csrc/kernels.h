@@ -71,6 +71,12 @@ inline int dconv_tc_slot(int hid, int i) {
 int dconv_tiles(int T);
 bool dconv_row_fused(int T);
 bool launch_dconv(const DConvArgs& a, cudaStream_t s);
+// Row moments of z = conv2(GELU(GroupNorm1(y))) added into st2 (rows x 2
+// doubles, zeroed by the caller) from y (rows*T, ld) and its moments st1, by
+// the quadratic form over zq (DConvArgs::zq_dev); C 192 or 384 (dconv.cu).
+bool launch_dconv_zstats(int C, const float* y, int ld, int rows, int T, const float* n1w,
+                         const float* n1b, const double* st1, double* st2, const float* zq,
+                         cudaStream_t s);
 bool dconv_tc_supported(int C, int T);
 // work items per row of the tensor-core DConv (rows of more than one need
 // part1/part2 and y: rows*T*dconv_tc_ystride(C) floats)

@@ -715,11 +715,12 @@ void dconv_gemm(dmx_handle* h, const ConvParams& p, int epi, const Packed& pk, c
   ++h->tc_launches;
 }
 
-// The DConv branch as three persistent tensor-core GEMMs per layer, for rows
-// of any length: conv1 (taps as TMA offsets) storing y and its row moments;
-// conv2 with GELU(GroupNorm1(y)) applied to each A tile by the converter
-// warps, epilogue = row moments of z; conv2 again, epilogue = GroupNorm2 +
-// GLU + LayerScale + residual into x. Moments are f64 atomics per row.
+// The DConv branch as two persistent tensor-core GEMMs per layer around a
+// SIMT pass, for rows of any length: conv1 (taps as TMA offsets) storing y
+// and its row moments; the row moments of z from g = GELU(GroupNorm1(y)) by
+// the quadratic form (dconv.cu); conv2 with GELU(GroupNorm1(y)) applied to
+// each A tile by the converter warps and a GroupNorm2 + GLU + LayerScale +
+// residual epilogue into x. Moments are f64 atomics per row.
 void run_dconv_gemm(dmx_handle* h, const DConvFull& dc, float* x, int rows, int T,
                     bool round_out) {
   const int C = dc.C, hid = dc.hidden;
@@ -753,9 +754,11 @@ void run_dconv_gemm(dmx_handle* h, const DConvFull& dc, float* x, int rows, int 
     ext.a_count = (double)hid * T;
     ext.a_gw = h->W(L.n1w.off);
     ext.a_gb = h->W(L.n1b.off);
-    q.epi_stats = st + 2 * rows;  // pass 1: moments of z
-    dconv_gemm(h, q, EPI_STATS, L.conv2, ext);
-    q.epi_stats = nullptr;  // pass 2: the output
+    // moments of z from g alone (v.g~, g~'Mg~), without a conv2 pass
+    if (!launch_dconv_zstats(C, y, kg, rows, T, h->W(L.n1w.off), h->W(L.n1b.off), st, st + 2 * rows,
+                             h->W(L.zq_off), h->stream))
+      throw Error(DMX_ERR_INVALID, "dconv: moments of z for this width");
+    q.epi_stats = nullptr;  // the output
     ext.epi_nstats = st + 2 * rows;
     ext.epi_count = 2.0 * C * T;
     ext.epi_gw = h->W(L.n2w.off);
