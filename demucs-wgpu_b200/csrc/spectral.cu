@@ -210,6 +210,21 @@ DMX_DEVICE cpx w_inv(const float2* __restrict__ tw, int j) {
   return j < 2048 ? cpx{t.x, -t.y} : cpx{-t.x, t.y};
 }
 
+// W^k for k = 0..15 from W^1, W^2, W^4, W^8 (at most three products deep,
+// so the error stays within a few roundings of the table's).
+DMX_DEVICE void powers16(cpx w1, cpx w2, cpx w4, cpx w8, cpx (&p)[16]) {
+  p[0] = {1.f, 0.f};
+  p[1] = w1;
+  p[2] = w2;
+  p[3] = cmul(w1, w2);
+  p[4] = w4;
+  p[5] = cmul(w1, w4);
+  p[6] = cmul(w2, w4);
+  p[7] = cmul(p[3], w4);
+#pragma unroll
+  for (int k = 0; k < 8; ++k) p[8 + k] = k == 0 ? w8 : cmul(p[k], w8);
+}
+
 // spec: the decoder output frame-major, (b, t, f, 16) with channel
 // source*4 + audio channel*2 + {re, im}.
 __global__ void __launch_bounds__(kIstftThreads, 2)
@@ -264,11 +279,16 @@ __global__ void __launch_bounds__(kIstftThreads, 2)
         }
       }
       idft16(v);
+      {
+        // twiddles e^(2 pi i tid k1 / 4096), k1 = 0..15, from four table entries
+        cpx wk[16];
+        powers16(w_inv(tw, tid), w_inv(tw, 2 * tid), w_inv(tw, 4 * tid), w_inv(tw, 8 * tid), wk);
 #pragma unroll
-      for (int k1 = 0; k1 < 16; ++k1) {
-        const cpx y = k1 == 0 ? v[idft16_slot(0)] : cmul(v[idft16_slot(k1)], w_inv(tw, tid * k1));
-        bre[k1 * kRow + tid] = y.x;
-        bim[k1 * kRow + tid] = y.y;
+        for (int k1 = 0; k1 < 16; ++k1) {
+          const cpx y = k1 == 0 ? v[idft16_slot(0)] : cmul(v[idft16_slot(k1)], wk[k1]);
+          bre[k1 * kRow + tid] = y.x;
+          bim[k1 * kRow + tid] = y.y;
+        }
       }
       __syncthreads();
       {
@@ -279,10 +299,12 @@ __global__ void __launch_bounds__(kIstftThreads, 2)
           v[a] = {bre[k1 * kRow + 16 * a + c], bim[k1 * kRow + 16 * a + c]};
         __syncthreads();
         idft16(v);
+        // twiddles e^(2 pi i 16 c d / 4096), d = 0..15
+        cpx wk[16];
+        powers16(w_inv(tw, 16 * c), w_inv(tw, 32 * c), w_inv(tw, 64 * c), w_inv(tw, 128 * c), wk);
 #pragma unroll
         for (int d = 0; d < 16; ++d) {
-          const cpx u = (d == 0 || c == 0) ? v[idft16_slot(d)]
-                                           : cmul(v[idft16_slot(d)], w_inv(tw, 16 * c * d));
+          const cpx u = (d == 0 || c == 0) ? v[idft16_slot(d)] : cmul(v[idft16_slot(d)], wk[d]);
           bre[k1 * kRow + 17 * d + c] = u.x;
           bim[k1 * kRow + 17 * d + c] = u.y;
         }
