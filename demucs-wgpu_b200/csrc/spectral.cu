@@ -17,87 +17,6 @@ namespace dmx {
 
 namespace {
 
-// Radix-2 decimation-in-time FFT of 4096 complex values in shared memory.
-// `sign` = -1 forward, +1 inverse; tw[k] = exp(-2 pi i k / 4096), k < 2048.
-DMX_DEVICE void fft4096(float* re, float* im, const float2* __restrict__ tw, float sign) {
-  for (int h = 1; h < kNfft; h <<= 1) {
-    const int step = kNfft / (2 * h);
-    for (int j = threadIdx.x; j < kNfft / 2; j += blockDim.x) {
-      const int k = j % h;
-      const int a = (j / h) * 2 * h + k;
-      const int b = a + h;
-      const float2 w = tw[k * step];
-      const float wr = w.x, wi = sign * -w.y;  // exp(sign * 2 pi i k / len)
-      const float xr = re[b] * wr - im[b] * wi;
-      const float xi = re[b] * wi + im[b] * wr;
-      re[b] = re[a] - xr;
-      im[b] = im[a] - xi;
-      re[a] += xr;
-      im[a] += xi;
-    }
-    __syncthreads();
-  }
-}
-
-DMX_DEVICE int bitrev12(int n) { return __brev(n) >> 20; }
-
-__global__ void __launch_bounds__(512) stft_cac_kernel(const float* __restrict__ mix,
-                                                       const float* __restrict__ window,
-                                                       const float2* __restrict__ tw,
-                                                       float* __restrict__ out,
-                                                       double* __restrict__ stats) {
-  __shared__ float re[kNfft], im[kNfft];
-  __shared__ double red[2][16];
-  const int t = blockIdx.x, b = blockIdx.y;
-  const float* x0 = mix + (int64_t)b * 2 * kSegment;
-  const float* x1 = x0 + kSegment;
-  for (int n = threadIdx.x; n < kNfft; n += blockDim.x) {
-    // kept frame t is torch frame t+2; its samples are the pad1d output
-    // [1024 t, 1024 t + 4096), i.e. mix index 1024 t + n - 1536 reflected.
-    int idx = t * kHop + n - kPad;
-    if (idx < 0) idx = -idx;
-    if (idx >= kSegment) idx = 2 * (kSegment - 1) - idx;
-    const float w = window[n];
-    const int r = bitrev12(n);
-    re[r] = x0[idx] * w;
-    im[r] = x1[idx] * w;
-  }
-  __syncthreads();
-  fft4096(re, im, tw, -1.f);
-  double s = 0.0, q = 0.0;
-  const float norm = 1.0f / 64.0f;
-  for (int k = threadIdx.x; k < kBins; k += blockDim.x) {
-    const int nk = (kNfft - k) & (kNfft - 1);
-    const float zr = re[k], zi = im[k], cr = re[nk], ci = im[nk];
-    float4 v;
-    v.x = 0.5f * (zr + cr) * norm;
-    v.y = 0.5f * (zi - ci) * norm;
-    v.z = 0.5f * (zi + ci) * norm;
-    v.w = -0.5f * (zr - cr) * norm;
-    *reinterpret_cast<float4*>(out + (((int64_t)b * kBins + k) * kFrames + t) * 4) = v;
-    s += (double)v.x + (double)v.y + (double)v.z + (double)v.w;
-    q += (double)v.x * v.x + (double)v.y * v.y + (double)v.z * v.z + (double)v.w * v.w;
-  }
-  s = warp_sum(s);
-  q = warp_sum(q);
-  if ((threadIdx.x & 31) == 0) {
-    red[0][threadIdx.x / 32] = s;
-    red[1][threadIdx.x / 32] = q;
-  }
-  __syncthreads();
-  if (threadIdx.x < 32) {
-    const int nw = blockDim.x / 32;
-    s = threadIdx.x < nw ? red[0][threadIdx.x] : 0.0;
-    q = threadIdx.x < nw ? red[1][threadIdx.x] : 0.0;
-    s = warp_sum(s);
-    q = warp_sum(q);
-    if (threadIdx.x == 0) {
-      atomicAdd(&stats[2 * b], s);
-      atomicAdd(&stats[2 * b + 1], q);
-    }
-  }
-}
-
 __global__ void wave_moments_kernel(const float* __restrict__ mix, int64_t n,
                                     double* __restrict__ stats) {
   __shared__ double red[2][32];
@@ -223,6 +142,112 @@ DMX_DEVICE void powers16(cpx w1, cpx w2, cpx w4, cpx w8, cpx (&p)[16]) {
   p[7] = cmul(p[3], w4);
 #pragma unroll
   for (int k = 0; k < 8; ++k) p[8 + k] = k == 0 ? w8 : cmul(p[k], w8);
+}
+
+// STFT of one frame per CTA (both audio channels in one complex FFT,
+// z = x0 + i x1), 256 threads. The forward 4096-point FFT is taken as the
+// conjugate of the inverse one of conj(z), with the same three radix-16
+// register passes and twiddles as the iSTFT below; X lands in the work
+// buffer in natural order for the CaC unpack (A[k] = (Z[k] + conj Z[N-k])/2,
+// B[k] = (Z[k] - conj Z[N-k])/2i), written channels-last (b, f, t, 4) with the
+// segment's moments summed in f64.
+__global__ void __launch_bounds__(256) stft_cac_kernel(const float* __restrict__ mix,
+                                                       const float* __restrict__ window,
+                                                       const float2* __restrict__ tw,
+                                                       float* __restrict__ out,
+                                                       double* __restrict__ stats) {
+  __shared__ float bre[16 * kRow], bim[16 * kRow];
+  __shared__ double red[2][8];
+  const int t = blockIdx.x, b = blockIdx.y, tid = threadIdx.x;
+  const float* x0 = mix + (int64_t)b * 2 * kSegment;
+  const float* x1 = x0 + kSegment;
+  cpx v[16];
+  // pass 1: thread m = tid, conj z[256 n2 + m]; kept frame t is torch frame
+  // t + 2, whose samples are the reflect-padded mix at 1024 t + n - 1536
+#pragma unroll
+  for (int n2 = 0; n2 < 16; ++n2) {
+    const int n = 256 * n2 + tid;
+    int idx = t * kHop + n - kPad;
+    if (idx < 0) idx = -idx;
+    if (idx >= kSegment) idx = 2 * (kSegment - 1) - idx;
+    const float w = __ldg(window + n);
+    v[n2] = {__ldg(x0 + idx) * w, -__ldg(x1 + idx) * w};
+  }
+  idft16(v);
+  {
+    cpx wk[16];
+    powers16(w_inv(tw, tid), w_inv(tw, 2 * tid), w_inv(tw, 4 * tid), w_inv(tw, 8 * tid), wk);
+#pragma unroll
+    for (int k1 = 0; k1 < 16; ++k1) {
+      const cpx y = k1 == 0 ? v[idft16_slot(0)] : cmul(v[idft16_slot(k1)], wk[k1]);
+      bre[k1 * kRow + tid] = y.x;
+      bim[k1 * kRow + tid] = y.y;
+    }
+  }
+  __syncthreads();
+  {
+    // pass 2: thread (k1, c), the 256-point DFT over m = 16 a + c, first level
+    const int k1 = tid >> 4, c = tid & 15;
+#pragma unroll
+    for (int a = 0; a < 16; ++a) v[a] = {bre[k1 * kRow + 16 * a + c], bim[k1 * kRow + 16 * a + c]};
+    __syncthreads();
+    idft16(v);
+    cpx wk[16];
+    powers16(w_inv(tw, 16 * c), w_inv(tw, 32 * c), w_inv(tw, 64 * c), w_inv(tw, 128 * c), wk);
+#pragma unroll
+    for (int d = 0; d < 16; ++d) {
+      const cpx u = (d == 0 || c == 0) ? v[idft16_slot(d)] : cmul(v[idft16_slot(d)], wk[d]);
+      bre[k1 * kRow + 17 * d + c] = u.x;
+      bim[k1 * kRow + 17 * d + c] = u.y;
+    }
+  }
+  __syncthreads();
+  {
+    // pass 3: thread (d, k1), second level: X[k1 + 16 d + 256 e], e = 0..15
+    const int d = tid >> 4, k1 = tid & 15;
+#pragma unroll
+    for (int c = 0; c < 16; ++c) v[c] = {bre[k1 * kRow + 17 * d + c], bim[k1 * kRow + 17 * d + c]};
+    idft16(v);
+    __syncthreads();
+#pragma unroll
+    for (int e = 0; e < 16; ++e) {  // X = conj of the inverse transform of conj z
+      const int k = k1 + 16 * d + 256 * e;
+      bre[k] = v[idft16_slot(e)].x;
+      bim[k] = -v[idft16_slot(e)].y;
+    }
+  }
+  __syncthreads();
+  double s = 0.0, q = 0.0;
+  const float norm = 1.0f / 64.0f;
+  for (int k = tid; k < kBins; k += 256) {
+    const int nk = (kNfft - k) & (kNfft - 1);
+    const float zr = bre[k], zi = bim[k], cr = bre[nk], ci = bim[nk];
+    float4 o;
+    o.x = 0.5f * (zr + cr) * norm;
+    o.y = 0.5f * (zi - ci) * norm;
+    o.z = 0.5f * (zi + ci) * norm;
+    o.w = -0.5f * (zr - cr) * norm;
+    *reinterpret_cast<float4*>(out + (((int64_t)b * kBins + k) * kFrames + t) * 4) = o;
+    s += (double)o.x + (double)o.y + (double)o.z + (double)o.w;
+    q += (double)o.x * o.x + (double)o.y * o.y + (double)o.z * o.z + (double)o.w * o.w;
+  }
+  s = warp_sum(s);
+  q = warp_sum(q);
+  if ((tid & 31) == 0) {
+    red[0][tid / 32] = s;
+    red[1][tid / 32] = q;
+  }
+  __syncthreads();
+  if (tid < 32) {
+    s = tid < 8 ? red[0][tid] : 0.0;
+    q = tid < 8 ? red[1][tid] : 0.0;
+    s = warp_sum(s);
+    q = warp_sum(q);
+    if (tid == 0) {
+      atomicAdd(&stats[2 * b], s);
+      atomicAdd(&stats[2 * b + 1], q);
+    }
+  }
 }
 
 // spec: the decoder output frame-major, (b, t, f, 16) with channel
@@ -351,7 +376,7 @@ __global__ void __launch_bounds__(kIstftThreads, 2)
 
 void launch_stft_cac(const float* mix, int B, const float* window, const float2* tw, float* out,
                      double* stats, cudaStream_t s) {
-  stft_cac_kernel<<<dim3(kFrames, B), 512, 0, s>>>(mix, window, tw, out, stats);
+  stft_cac_kernel<<<dim3(kFrames, B), 256, 0, s>>>(mix, window, tw, out, stats);
 }
 
 void launch_wave_moments(const float* mix, int B, int64_t n, double* stats, cudaStream_t s) {
