@@ -675,27 +675,29 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int m = 0; m < 3; ++m)
         for (int ch = 0; ch < S::NCHUNK; ++ch) {
           const int j = u & 1;
-          if (!S::ALL) {
-            if (ok && !mbar_wait(&d2_full[j], (u >> 1) & 1, a.err, 39)) ok = false;
-            asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-          }
           const int pm = m * 128 + r;
           const bool own = owned(pm);
           const int c0 = ch * (S::NCH / 2) + 16 * b;  // this thread's 16 channels
           float* xp = a.x + ((int64_t)row * T + (own ? ts + pm : 0)) * C + c0;
+          float4 res[4];
+          if (!S::ALL) {
+            // the residual from HBM, in flight while this chunk's conv2 completes
+            if (ok && own) {
+#pragma unroll
+              for (int i = 0; i < 4; ++i) res[i] = reinterpret_cast<const float4*>(xp)[i];
+            }
+            if (ok && !mbar_wait(&d2_full[j], (u >> 1) & 1, a.err, 39)) ok = false;
+            asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+          }
           uint32_t zr[32];
           __syncwarp();
           tmem_ld16_nw(tmem + lane_base + d2_col(m, j) + 32 * b, zr);
           tmem_ld16_nw(tmem + lane_base + d2_col(m, j) + 32 * b + 16, zr + 16);
-          float4 res[4];
           if (S::ALL) {
             const unsigned char* rb = smem + S::OFF_RES + (3 * m + b) * S::RES_BOX + r * 64;
 #pragma unroll
             for (int i = 0; i < 4; ++i)
               res[i] = *reinterpret_cast<const float4*>(rb + ((i ^ ((r >> 1) & 3)) << 4));
-          } else if (ok && own) {
-#pragma unroll
-            for (int i = 0; i < 4; ++i) res[i] = reinterpret_cast<const float4*>(xp)[i];
           }
           tmem_ld_wait<32>(zr);
           if (!S::ALL) {
