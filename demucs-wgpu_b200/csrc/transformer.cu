@@ -48,16 +48,19 @@ __global__ void layer_norm_kernel(const float* __restrict__ x, int64_t rows, int
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
     const int c = lane * 4 + i * 128;
+    const float4 w4 = __ldg(reinterpret_cast<const float4*>(w + c));
+    const float4 b4 = __ldg(reinterpret_cast<const float4*>(b + c));
     float4 r;
-    r.x = (v[4 * i] - mean) * inv * w[c] + b[c];
-    r.y = (v[4 * i + 1] - mean) * inv * w[c + 1] + b[c + 1];
-    r.z = (v[4 * i + 2] - mean) * inv * w[c + 2] + b[c + 2];
-    r.w = (v[4 * i + 3] - mean) * inv * w[c + 3] + b[c + 3];
+    r.x = (v[4 * i] - mean) * inv * w4.x + b4.x;
+    r.y = (v[4 * i + 1] - mean) * inv * w4.y + b4.y;
+    r.z = (v[4 * i + 2] - mean) * inv * w4.z + b4.z;
+    r.w = (v[4 * i + 3] - mean) * inv * w4.w + b4.w;
     if (pr) {
-      r.x += pr[c];
-      r.y += pr[c + 1];
-      r.z += pr[c + 2];
-      r.w += pr[c + 3];
+      const float4 p4 = __ldg(reinterpret_cast<const float4*>(pr + c));
+      r.x += p4.x;
+      r.y += p4.y;
+      r.z += p4.z;
+      r.w += p4.w;
     }
     if (round_out) {  // the output feeds only tf32 GEMMs: round to nearest here, once
       r.x = round_tf32(r.x);
