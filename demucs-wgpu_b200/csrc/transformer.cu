@@ -80,13 +80,15 @@ __global__ void group_norm_apply_kernel(float* __restrict__ x, int64_t ntok,
   float* base = x + (int64_t)bi * ntok * 512;
   for (int64_t i = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) * 4; i < ntok * 512;
        i += (int64_t)gridDim.x * blockDim.x * 4) {
-    const int c = (int)(i % 512);
+    const int c = (int)(i & 511);
     float4 v = *reinterpret_cast<float4*>(base + i);
+    const float4 w4 = __ldg(reinterpret_cast<const float4*>(w + c));
+    const float4 b4 = __ldg(reinterpret_cast<const float4*>(b + c));
     float sc, sh;
-    sc = rn.inv * w[c]; sh = b[c] - rn.mean * sc; v.x = v.x * sc + sh;
-    sc = rn.inv * w[c + 1]; sh = b[c + 1] - rn.mean * sc; v.y = v.y * sc + sh;
-    sc = rn.inv * w[c + 2]; sh = b[c + 2] - rn.mean * sc; v.z = v.z * sc + sh;
-    sc = rn.inv * w[c + 3]; sh = b[c + 3] - rn.mean * sc; v.w = v.w * sc + sh;
+    sc = rn.inv * w4.x; sh = b4.x - rn.mean * sc; v.x = v.x * sc + sh;
+    sc = rn.inv * w4.y; sh = b4.y - rn.mean * sc; v.y = v.y * sc + sh;
+    sc = rn.inv * w4.z; sh = b4.z - rn.mean * sc; v.z = v.z * sc + sh;
+    sc = rn.inv * w4.w; sh = b4.w - rn.mean * sc; v.w = v.w * sc + sh;
     *reinterpret_cast<float4*>(base + i) = v;
   }
 }
