@@ -291,6 +291,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       // columns stored for this row (o_lim clips the positions 4x + i >= o_lim)
       const int ncol = p.o_lim ? min(p.N, max(0, (p.o_lim - 4 * x) * p.o_lim_ch)) : p.N;
       double ls = 0.0, lq = 0.0;
+      // DConv tail: this row's GroupNorm2 statistics, once per tile
+      RowNorm nr{0.f, 0.f};
+      if (EPI == EPI_DCONV_TAIL && valid) nr = row_norm(p.epi_nstats, (int)(pos / p.epi_rowlen), p.epi_count);
       const uint32_t tacc = tmem + lane_base + (uint32_t)(acc * BN);
       for (int c0 = 32 * hh; c0 < BN; c0 += 64) {
         float v[32];
@@ -393,7 +396,6 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           if (EPI == EPI_DCONV_TAIL) {
             // channels nb/2 .. nb/2 + 15: out = res + gamma * GLU(GroupNorm(v))
-            const RowNorm nr = row_norm(p.epi_nstats, (int)(pos / p.epi_rowlen), p.epi_count);
             const int c0o = nb / 2;
             float* o = p.out + orow + c0o;
             const float* rr = p.epi_res + orow + c0o;
@@ -411,15 +413,40 @@ __global__ void __launch_bounds__(kThreads, 1)
             } else {
               for (int j = 0; j < 16; ++j) res[j] = nb + 2 * j < ncol ? rr[j] : 0.f;
             }
+            if (vec && (p.epi_half & 3) == 0) {
+              // per-channel GroupNorm weights / biases (value, gate) and LayerScale, 16 bytes at a time
 #pragma unroll
-            for (int j = 0; j < 16; ++j) {
-              const int c = c0o + j;
-              if (nb + 2 * j < ncol) {
-                const float vs = nr.inv * p.epi_gw[c];
-                const float gsc = nr.inv * p.epi_gw[c + p.epi_half];
-                const float value = v[2 * j] * vs + (p.epi_gb[c] - nr.mean * vs);
-                const float gate = v[2 * j + 1] * gsc + (p.epi_gb[c + p.epi_half] - nr.mean * gsc);
-                res[j] += p.epi_gamma[c] * (value * sigmoid(gate));
+              for (int j4 = 0; j4 < 16; j4 += 4) {
+                const int c = c0o + j4;
+                const float4 wv = __ldg(reinterpret_cast<const float4*>(p.epi_gw + c));
+                const float4 wg = __ldg(reinterpret_cast<const float4*>(p.epi_gw + c + p.epi_half));
+                const float4 bv = __ldg(reinterpret_cast<const float4*>(p.epi_gb + c));
+                const float4 bg = __ldg(reinterpret_cast<const float4*>(p.epi_gb + c + p.epi_half));
+                const float4 gm = __ldg(reinterpret_cast<const float4*>(p.epi_gamma + c));
+                const float awv[4] = {wv.x, wv.y, wv.z, wv.w}, awg[4] = {wg.x, wg.y, wg.z, wg.w};
+                const float abv[4] = {bv.x, bv.y, bv.z, bv.w}, abg[4] = {bg.x, bg.y, bg.z, bg.w};
+                const float agm[4] = {gm.x, gm.y, gm.z, gm.w};
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                  const int j = j4 + e;
+                  const float vs = nr.inv * awv[e];
+                  const float gsc = nr.inv * awg[e];
+                  const float value = v[2 * j] * vs + (abv[e] - nr.mean * vs);
+                  const float gate = v[2 * j + 1] * gsc + (abg[e] - nr.mean * gsc);
+                  res[j] += agm[e] * (value * sigmoid(gate));
+                }
+              }
+            } else {
+#pragma unroll
+              for (int j = 0; j < 16; ++j) {
+                const int c = c0o + j;
+                if (nb + 2 * j < ncol) {
+                  const float vs = nr.inv * p.epi_gw[c];
+                  const float gsc = nr.inv * p.epi_gw[c + p.epi_half];
+                  const float value = v[2 * j] * vs + (p.epi_gb[c] - nr.mean * vs);
+                  const float gate = v[2 * j + 1] * gsc + (p.epi_gb[c + p.epi_half] - nr.mean * gsc);
+                  res[j] += p.epi_gamma[c] * (value * sigmoid(gate));
+                }
               }
             }
             if (p.round_out) {
