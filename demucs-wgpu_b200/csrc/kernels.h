@@ -116,4 +116,21 @@ void launch_ola_finish(const float* acc, int64_t length, int64_t shift_offset, i
                        float scale, int mode, float* pass, float* stems, cudaStream_t s,
                        int64_t t_lo = 0, int64_t t_hi = -1);
 
+// bag.cu — the bag's per-source weighted combination (api.rs:319-361).
+// For source s: out = (sum over j < count[s] of out[net[s][j]] * weight[s][j])
+// / total[s], or zeros when count[s] == 0. Every out[] buffer and `out` is
+// (segments, sources, channels, samples) on the launching device.
+constexpr int kBagMaxNets = 8;
+constexpr int kBagMaxSources = 4;
+struct BagTerms {
+  const float* out[kBagMaxNets];
+  int net[kBagMaxSources][kBagMaxNets];
+  float weight[kBagMaxSources][kBagMaxNets];
+  int count[kBagMaxSources];
+  float total[kBagMaxSources];
+  int sources, channels;
+};
+void launch_bag_combine(const BagTerms& t, int64_t segments, int64_t samples, float* out,
+                        cudaStream_t s);
+
 }  // namespace dmx

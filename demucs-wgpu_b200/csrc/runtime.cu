@@ -488,6 +488,8 @@ struct dmx_handle {
   size_t norm_cap = 0;
   int* err = nullptr;  // device flag raised by bounded waits in the tensor-core kernels
   int64_t tc_launches = 0;
+  float* bag_out = nullptr;  // this network's own forward output when it runs inside a bag
+  int64_t bag_cap = 0;       // segments bag_out holds
 
   float* W(size_t off) const { return wdev + off; }
 
@@ -1718,6 +1720,7 @@ void dmx_destroy(dmx_handle* h) {
   cudaFree(h->track_ws);
   cudaFree(h->host_io);
   cudaFree(h->norm_scratch);
+  cudaFree(h->bag_out);
   cudaFreeHost(h->pinned_in);
   cudaFreeHost(h->pinned_out);
   if (h->stream) cudaStreamDestroy(h->stream);
@@ -1887,6 +1890,268 @@ int64_t dmx_num_chunks(int64_t view_length, int segment, double overlap) {
   return (view_length + stride - 1) / stride;
 }
 
+}  // extern "C"
+
+namespace {
+
+// The networks of a bag (htdemucs_ft) that run for the requested sources, and
+// how their outputs combine (BagCombineForward, api.rs:319-361). A network
+// runs only if it carries a nonzero weight on a requested source (api.rs:
+// 330-337); for source s the terms are the running networks with a nonzero
+// weight on s, in bag order, and their f32 weight sum.
+struct BagPlan {
+  std::vector<dmx_handle*> nets;  // the networks that run, in bag order
+  BagTerms terms{};               // terms.net[][] index `nets`
+  cudaEvent_t ev = nullptr;
+  ~BagPlan() {
+    if (ev) cudaEventDestroy(ev);
+  }
+};
+
+// Fills t.net / weight / count / total from `weights` (n_nets x sources, row
+// per network) and `requested` (sources flags, NULL = all); `slot[k]` is the
+// index network k gets in t.out (-1 = it does not run).
+BagTerms bag_terms(int n_nets, const float* weights, const int* requested, std::vector<int>* slot) {
+  if (n_nets < 1 || n_nets > kBagMaxNets)
+    throw Error(DMX_ERR_INVALID, "a bag holds 1 to " + std::to_string(kBagMaxNets) + " networks");
+  if (!weights) throw Error(DMX_ERR_INVALID, "bag weights are missing");
+  constexpr int S = kBagMaxSources;
+  auto req = [&](int s) { return requested == nullptr || requested[s] != 0; };
+  BagTerms t{};
+  t.sources = S;
+  t.channels = 2;
+  slot->assign(n_nets, -1);
+  int used = 0;
+  for (int k = 0; k < n_nets; ++k)
+    for (int s = 0; s < S; ++s)
+      if (weights[k * S + s] != 0.0f && req(s) && (*slot)[k] < 0) (*slot)[k] = used++;
+  for (int s = 0; s < S; ++s) {
+    if (!req(s)) continue;
+    float total = 0.0f;
+    int c = 0;
+    for (int k = 0; k < n_nets; ++k) {
+      const float w = weights[k * S + s];
+      if (w == 0.0f) continue;
+      t.net[s][c] = (*slot)[k];
+      t.weight[s][c] = w;
+      ++c;
+      total += w;
+    }
+    if (total == 0.0f)  // api.rs:355-359
+      throw Error(DMX_ERR_INVALID, "no network covers stem index " + std::to_string(s));
+    t.count[s] = c;
+    t.total[s] = total;
+  }
+  return t;
+}
+
+void make_bag(dmx_handle* const* nets, int n_nets, const float* weights, const int* requested,
+              BagPlan* b) {
+  if (!nets) throw Error(DMX_ERR_INVALID, "bag networks are missing");
+  std::vector<int> slot;
+  b->terms = bag_terms(n_nets, weights, requested, &slot);
+  for (int k = 0; k < n_nets; ++k) {
+    if (slot[k] < 0) continue;
+    dmx_handle* hk = nets[k];
+    if (!hk) throw Error(DMX_ERR_INVALID, "bag network " + std::to_string(k) + " is NULL");
+    if (!b->nets.empty() && hk->device != b->nets[0]->device)
+      throw Error(DMX_ERR_INVALID,
+                  "the networks of a bag must share one device (for one network per GPU run "
+                  "one process per GPU and combine with dmx_bag_combine_device)");
+    for (dmx_handle* o : b->nets)
+      if (o == hk) throw Error(DMX_ERR_INVALID, "each network of a bag needs its own handle");
+    b->nets.push_back(hk);
+  }
+  CK(cudaSetDevice(b->nets[0]->device));
+  CK(cudaEventCreateWithFlags(&b->ev, cudaEventDisableTiming));
+}
+
+void ensure_bag_out(dmx_handle* h, int64_t G) {
+  if (G <= h->bag_cap) return;
+  cudaFree(h->bag_out);
+  h->bag_out = nullptr;
+  h->bag_cap = 0;
+  CK(cudaMalloc(&h->bag_out, (size_t)G * 8 * kSegment * sizeof(float)));
+  h->bag_cap = G;
+}
+
+// BagCombineForward::start (api.rs:326-361) on device: each running network
+// forwards the same padded chunks (one after another, ordered by events on
+// their streams), then the per-source weighted combination is written to
+// `out` on the lead network's stream.
+void bag_forward(dmx_handle* lead, BagPlan& b, const float* in, int G, float* out) {
+  cudaStream_t prev = lead->stream;
+  for (size_t i = 0; i < b.nets.size(); ++i) {
+    dmx_handle* hk = b.nets[i];
+    CK(cudaSetDevice(hk->device));
+    ensure_bag_out(hk, G);
+    if (hk->stream != prev) {
+      CK(cudaEventRecord(b.ev, prev));
+      CK(cudaStreamWaitEvent(hk->stream, b.ev, 0));
+    }
+    const int64_t before = hk->launches;
+    run_forward(hk, in, G, hk->bag_out);
+    if (hk != lead) lead->launches += hk->launches - before;
+    b.terms.out[i] = hk->bag_out;
+    prev = hk->stream;
+  }
+  if (prev != lead->stream) {
+    CK(cudaEventRecord(b.ev, prev));
+    CK(cudaStreamWaitEvent(lead->stream, b.ev, 0));
+  }
+  int64_t reads = 0;
+  for (int s = 0; s < b.terms.sources; ++s) reads += b.terms.count[s];
+  lead->mark("bag.combine", 0.0, (double)G * 2 * kSegment * 4.0 * (double)(reads + 4));
+  launch_bag_combine(b.terms, G, kSegment, out, lead->stream);
+  ++lead->launches;
+  CK(cudaGetLastError());
+}
+
+// Chunks [chunk_lo, chunk_hi) of a shift view: gather, forward (one network,
+// or the bag when `bag` is set), overlap-add into acc_dev.
+void shard_chunks(dmx_handle* h, BagPlan* bag, const float* mix_norm_dev, int64_t length,
+                  int64_t shift_offset, int64_t max_shift, int segment, int64_t stride,
+                  int64_t chunk_lo, int64_t chunk_hi, int cap, float* acc_dev, int64_t view_lo,
+                  int64_t view_hi) {
+  ensure_io(h, cap);
+  for (int64_t c0 = chunk_lo; c0 < chunk_hi; c0 += cap) {
+    const int G = (int)std::min<int64_t>(cap, chunk_hi - c0);
+    h->mark("track.gather");
+    launch_gather_chunks(mix_norm_dev, length, shift_offset, max_shift, segment, stride, c0, G,
+                         h->io_in, h->stream);
+    ++h->launches;
+    if (bag)
+      bag_forward(h, *bag, h->io_in, G, h->io_out);
+    else
+      run_forward(h, h->io_in, G, h->io_out);
+    h->mark("track.ola");
+    launch_ola_accumulate(h->io_out, length, shift_offset, max_shift, segment, stride, c0, G,
+                          h->W(h->m.ola_w.off), acc_dev, view_lo, view_hi, h->stream);
+    ++h->launches;
+    CK(cudaGetLastError());
+  }
+}
+
+// Demucs::separate's device driver for one track (api.rs:438-545, 697-785;
+// pipeline.rs:380-515; streaming.rs:52-400) over one network or, with `bag`,
+// over the bag's lockstep combination; `h` is the network (the bag's lead)
+// whose stream, track workspace and OLA weights the driver uses.
+void separate_track_impl(dmx_handle* h, BagPlan* bag, const float* lr_dev, int64_t n,
+                         const dmx_separate_opts* opts, float* d_stems, dmx_progress_fn progress,
+                         void* user) {
+  dmx_separate_opts o{1, 0.25, 1.0, 0};
+  if (opts) o = *opts;
+  if (o.transition_power != 1.0) throw Error(DMX_ERR_INVALID, "transition_power must be 1");
+  if (o.shifts < 0) throw Error(DMX_ERR_INVALID, "shifts must be >= 0");
+  CK(cudaSetDevice(h->device));
+  const int seg = kSegment;
+  const int64_t stride = (int64_t)((1.0 - o.overlap) * (double)seg);
+  if (stride <= 0) throw Error(DMX_ERR_INVALID, "overlap leaves a zero stride");
+  const int64_t max_shift = o.shifts > 0 ? (int64_t)(0.5 * 44100.0) : 0;
+  const int64_t view_cap = n + max_shift;
+  // track-sized scratch, kept on the handle between calls
+  const size_t scratch_bytes = (size_t)track_normalize_scratch_doubles() * sizeof(double);
+  const size_t need = (size_t)(2 * n + 8 * view_cap + (o.shifts > 1 ? 8 * n : 0)) * sizeof(float) +
+                      scratch_bytes + 512;
+  if (need > h->track_cap) {
+    cudaFree(h->track_ws);
+    h->track_ws = nullptr;
+    h->track_cap = 0;
+    CK(cudaMalloc(&h->track_ws, need));
+    h->track_cap = need;
+  }
+  double* d_stats = reinterpret_cast<double*>(h->track_ws);
+  float2* d_norm = reinterpret_cast<float2*>(h->track_ws + scratch_bytes);
+  float* d_mix = reinterpret_cast<float*>(h->track_ws + scratch_bytes + 512);
+  float* d_acc = d_mix + 2 * n;
+  float* d_pass = o.shifts > 1 ? d_acc + 8 * view_cap : nullptr;
+  h->launches = 0;
+  if (d_pass) CK(cudaMemsetAsync(d_pass, 0, 8 * n * sizeof(float), h->stream));
+  h->mark("track.normalize");
+  launch_track_normalize(lr_dev, lr_dev + n, n, d_stats, d_mix, d_norm, h->stream);
+  h->launches += 2;
+  // ShiftRng (pipeline.rs:136-151), seed 0x5eed1234
+  uint64_t rng = 0x5eed1234ULL * 6364136223846793005ULL + 1ULL;
+  const int passes = std::max(1, o.shifts);
+  const float scale = o.shifts > 0 ? 1.0f / (float)o.shifts : 1.0f;
+  size_t done = 0, total = 0;
+  std::vector<int64_t> offsets;
+  for (int pass = 0; pass < passes; ++pass) {
+    int64_t offset = 0;
+    if (o.shifts > 0) {
+      rng = rng * 6364136223846793005ULL + 1442695040888963407ULL;
+      offset = (int64_t)((rng >> 33) % (uint64_t)(max_shift + 1));
+    }
+    offsets.push_back(offset);
+    const int64_t vlen = o.shifts > 0 ? n + max_shift - offset : n;
+    total += (size_t)dmx_num_chunks(vlen, seg, o.overlap);
+  }
+  int max_batch = h->cfg.max_batch;
+  if (bag)
+    for (dmx_handle* hk : bag->nets) max_batch = std::min(max_batch, hk->cfg.max_batch);
+  const int batch = std::max(1, o.batch > 0 ? std::min(o.batch, max_batch) : max_batch);
+  // progress counts every running network's chunks (api.rs:764-776)
+  const size_t active = bag ? bag->nets.size() : 1;
+  for (int pass = 0; pass < passes; ++pass) {
+    const int64_t offset = offsets[pass];
+    const int64_t vlen = o.shifts > 0 ? n + max_shift - offset : n;
+    const int64_t chunks = dmx_num_chunks(vlen, seg, o.overlap);
+    CK(cudaMemsetAsync(d_acc, 0, 8 * vlen * sizeof(float), h->stream));
+    for (int64_t c0 = 0; c0 < chunks; c0 += batch) {
+      const int64_t c1 = std::min<int64_t>(chunks, c0 + batch);
+      shard_chunks(h, bag, d_mix, n, offset, max_shift, seg, stride, c0, c1, batch, d_acc, 0, vlen);
+      done += (size_t)(c1 - c0);
+      if (progress) {
+        CK(cudaStreamSynchronize(h->stream));
+        progress(done * active, total * active, user);
+      }
+    }
+    const int mode = o.shifts == 0 ? 0 : (o.shifts == 1 ? 1 : 2);
+    h->mark("track.finish");
+    ++h->launches;
+    launch_ola_finish(d_acc, n, offset, max_shift, seg, stride, h->W(h->m.ola_w.off), d_norm, scale,
+                      mode, d_pass, d_stems, h->stream);
+  }
+  if (o.shifts > 1) ++h->launches;
+  if (o.shifts > 1)
+    launch_ola_finish(d_acc, n, 0, max_shift, seg, stride, h->W(h->m.ola_w.off), d_norm, scale, 3,
+                      d_pass, d_stems, h->stream);
+  h->mark("end");
+  CK(cudaGetLastError());
+}
+
+// Host arrays in, host stems out, through the handle's device staging.
+void separate_track_host(dmx_handle* h, BagPlan* bag, const float* left, const float* right,
+                         int64_t n, const dmx_separate_opts* opts, float* stems_out,
+                         dmx_progress_fn progress, void* user) {
+  CK(cudaSetDevice(h->device));
+  // host-track staging kept on the handle between calls (grown on demand)
+  const size_t need = (size_t)10 * n * sizeof(float);
+  if (need > h->host_io_cap) {
+    cudaFree(h->host_io);
+    h->host_io = nullptr;
+    h->host_io_cap = 0;
+    CK(cudaMalloc(&h->host_io, need));
+    h->host_io_cap = need;
+  }
+  float* d_lr = h->host_io;
+  float* d_stems = h->host_io + 2 * n;
+  CK(cudaMemcpyAsync(d_lr, left, n * sizeof(float), cudaMemcpyHostToDevice, h->stream));
+  CK(cudaMemcpyAsync(d_lr + n, right, n * sizeof(float), cudaMemcpyHostToDevice, h->stream));
+  separate_track_impl(h, bag, d_lr, n, opts, d_stems, progress, user);
+  CK(cudaMemcpyAsync(stems_out, d_stems, 8 * n * sizeof(float), cudaMemcpyDeviceToHost, h->stream));
+  CK(cudaStreamSynchronize(h->stream));
+  check_device_flag(h);
+  if (bag)
+    for (dmx_handle* hk : bag->nets)
+      if (hk != h) check_device_flag(hk);
+  finish_stage_times(h);
+}
+
+}  // namespace
+
+extern "C" {
+
 dmx_status dmx_track_shard(dmx_handle* h, const float* mix_norm_dev, int64_t length,
                            int64_t shift_offset, int64_t max_shift, int segment, double overlap,
                            double transition_power, int64_t chunk_lo, int64_t chunk_hi, int batch,
@@ -1898,20 +2163,8 @@ dmx_status dmx_track_shard(dmx_handle* h, const float* mix_norm_dev, int64_t len
     const int64_t stride = (int64_t)((1.0 - overlap) * (double)segment);
     if (stride <= 0) throw Error(DMX_ERR_INVALID, "overlap leaves a zero stride");
     const int cap = std::max(1, batch > 0 ? std::min(batch, h->cfg.max_batch) : h->cfg.max_batch);
-    ensure_io(h, cap);
-    for (int64_t c0 = chunk_lo; c0 < chunk_hi; c0 += cap) {
-      const int G = (int)std::min<int64_t>(cap, chunk_hi - c0);
-      h->mark("track.gather");
-      launch_gather_chunks(mix_norm_dev, length, shift_offset, max_shift, segment, stride, c0, G,
-                           h->io_in, h->stream);
-      ++h->launches;
-      run_forward(h, h->io_in, G, h->io_out);
-      h->mark("track.ola");
-      launch_ola_accumulate(h->io_out, length, shift_offset, max_shift, segment, stride, c0, G,
-                            h->W(h->m.ola_w.off), acc_dev, view_lo, view_hi, h->stream);
-      ++h->launches;
-      CK(cudaGetLastError());
-    }
+    shard_chunks(h, nullptr, mix_norm_dev, length, shift_offset, max_shift, segment, stride, chunk_lo,
+                 chunk_hi, cap, acc_dev, view_lo, view_hi);
     return DMX_OK;
   } catch (const Error& e) {
     return fail(e);
@@ -1926,82 +2179,93 @@ dmx_status dmx_separate_track_device(dmx_handle* h, const float* lr_dev, int64_t
   try {
     if (!h || !lr_dev || !d_stems || n <= 0)
       throw Error(DMX_ERR_INVALID, "dmx_separate_track_device: bad argument");
-    dmx_separate_opts o{1, 0.25, 1.0, 0};
-    if (opts) o = *opts;
-    if (o.transition_power != 1.0) throw Error(DMX_ERR_INVALID, "transition_power must be 1");
-    if (o.shifts < 0) throw Error(DMX_ERR_INVALID, "shifts must be >= 0");
-    CK(cudaSetDevice(h->device));
-    const int seg = kSegment;
-    const int64_t stride = (int64_t)((1.0 - o.overlap) * (double)seg);
-    if (stride <= 0) throw Error(DMX_ERR_INVALID, "overlap leaves a zero stride");
-    const int64_t max_shift = o.shifts > 0 ? (int64_t)(0.5 * 44100.0) : 0;
-    const int64_t view_cap = n + max_shift;
-    // track-sized scratch, kept on the handle between calls
-    const size_t scratch_bytes = (size_t)track_normalize_scratch_doubles() * sizeof(double);
-    const size_t need = (size_t)(2 * n + 8 * view_cap + (o.shifts > 1 ? 8 * n : 0)) * sizeof(float) +
-                        scratch_bytes + 512;
-    if (need > h->track_cap) {
-      cudaFree(h->track_ws);
-      h->track_ws = nullptr;
-      h->track_cap = 0;
-      CK(cudaMalloc(&h->track_ws, need));
-      h->track_cap = need;
+    separate_track_impl(h, nullptr, lr_dev, n, opts, d_stems, progress, user);
+    return DMX_OK;
+  } catch (const Error& e) {
+    return fail(e);
+  } catch (const std::exception& e) {
+    return fail_std(e);
+  }
+}
+
+dmx_status dmx_bag_combine_device(const float* const* outs_dev, int n_nets, const float* weights,
+                                  const int* requested, int64_t n_segments, int64_t samples,
+                                  float* combined_dev, void* stream) {
+  try {
+    if (!outs_dev || !combined_dev || n_segments <= 0 || samples <= 0)
+      throw Error(DMX_ERR_INVALID, "dmx_bag_combine_device: bad argument");
+    std::vector<int> slot;
+    BagTerms t = bag_terms(n_nets, weights, requested, &slot);
+    for (int k = 0; k < n_nets; ++k) {
+      if (slot[k] < 0) continue;
+      if (!outs_dev[k])
+        throw Error(DMX_ERR_INVALID, "bag output " + std::to_string(k) + " is NULL but weighted");
+      t.out[slot[k]] = outs_dev[k];
     }
-    double* d_stats = reinterpret_cast<double*>(h->track_ws);
-    float2* d_norm = reinterpret_cast<float2*>(h->track_ws + scratch_bytes);
-    float* d_mix = reinterpret_cast<float*>(h->track_ws + scratch_bytes + 512);
-    float* d_acc = d_mix + 2 * n;
-    float* d_pass = o.shifts > 1 ? d_acc + 8 * view_cap : nullptr;
-    h->launches = 0;
-    if (d_pass) CK(cudaMemsetAsync(d_pass, 0, 8 * n * sizeof(float), h->stream));
-    h->mark("track.normalize");
-    launch_track_normalize(lr_dev, lr_dev + n, n, d_stats, d_mix, d_norm, h->stream);
-    h->launches += 2;
-    // ShiftRng (pipeline.rs:136-151), seed 0x5eed1234
-    uint64_t rng = 0x5eed1234ULL * 6364136223846793005ULL + 1ULL;
-    const int passes = std::max(1, o.shifts);
-    const float scale = o.shifts > 0 ? 1.0f / (float)o.shifts : 1.0f;
-    size_t done = 0, total = 0;
-    std::vector<int64_t> offsets;
-    for (int pass = 0; pass < passes; ++pass) {
-      int64_t offset = 0;
-      if (o.shifts > 0) {
-        rng = rng * 6364136223846793005ULL + 1442695040888963407ULL;
-        offset = (int64_t)((rng >> 33) % (uint64_t)(max_shift + 1));
-      }
-      offsets.push_back(offset);
-      const int64_t vlen = o.shifts > 0 ? n + max_shift - offset : n;
-      total += (size_t)dmx_num_chunks(vlen, seg, o.overlap);
-    }
-    const int batch = o.batch > 0 ? std::min(o.batch, h->cfg.max_batch) : h->cfg.max_batch;
-    for (int pass = 0; pass < passes; ++pass) {
-      const int64_t offset = offsets[pass];
-      const int64_t vlen = o.shifts > 0 ? n + max_shift - offset : n;
-      const int64_t chunks = dmx_num_chunks(vlen, seg, o.overlap);
-      CK(cudaMemsetAsync(d_acc, 0, 8 * vlen * sizeof(float), h->stream));
-      for (int64_t c0 = 0; c0 < chunks; c0 += batch) {
-        const int64_t c1 = std::min<int64_t>(chunks, c0 + batch);
-        const dmx_status st = dmx_track_shard(h, d_mix, n, offset, max_shift, seg, o.overlap, 1.0, c0,
-                                              c1, batch, d_acc, 0, vlen);
-        if (st != DMX_OK) return st;
-        done += (size_t)(c1 - c0);
-        if (progress) {
-          CK(cudaStreamSynchronize(h->stream));
-          progress(done, total, user);
-        }
-      }
-      const int mode = o.shifts == 0 ? 0 : (o.shifts == 1 ? 1 : 2);
-      h->mark("track.finish");
-      ++h->launches;
-      launch_ola_finish(d_acc, n, offset, max_shift, seg, stride, h->W(h->m.ola_w.off), d_norm, scale,
-                        mode, d_pass, d_stems, h->stream);
-    }
-    if (o.shifts > 1) ++h->launches;
-    if (o.shifts > 1)
-      launch_ola_finish(d_acc, n, 0, max_shift, seg, stride, h->W(h->m.ola_w.off), d_norm, scale, 3,
-                        d_pass, d_stems, h->stream);
-    h->mark("end");
+    launch_bag_combine(t, n_segments, samples, combined_dev, static_cast<cudaStream_t>(stream));
     CK(cudaGetLastError());
+    return DMX_OK;
+  } catch (const Error& e) {
+    return fail(e);
+  } catch (const std::exception& e) {
+    return fail_std(e);
+  }
+}
+
+dmx_status dmx_bag_forward_device(dmx_handle* const* nets, int n_nets, const float* weights,
+                                  const int* requested, const float* mix_dev, int64_t n,
+                                  float* out_dev) {
+  try {
+    if (!mix_dev || !out_dev || n <= 0)
+      throw Error(DMX_ERR_INVALID, "dmx_bag_forward_device: bad argument");
+    BagPlan bag;
+    make_bag(nets, n_nets, weights, requested, &bag);
+    dmx_handle* lead = bag.nets[0];
+    lead->launches = 0;
+    int cap = lead->cfg.max_batch;
+    for (dmx_handle* hk : bag.nets) cap = std::min(cap, hk->cfg.max_batch);
+    cap = std::max(1, cap);
+    for (int64_t s0 = 0; s0 < n; s0 += cap) {
+      const int G = (int)std::min<int64_t>(cap, n - s0);
+      bag_forward(lead, bag, mix_dev + s0 * 2 * kSegment, G, out_dev + s0 * 8 * kSegment);
+    }
+    lead->mark("end");
+    return DMX_OK;
+  } catch (const Error& e) {
+    return fail(e);
+  } catch (const std::exception& e) {
+    return fail_std(e);
+  }
+}
+
+dmx_status dmx_separate_track_bag_device(dmx_handle* const* nets, int n_nets, const float* weights,
+                                         const int* requested, const float* lr_dev, int64_t n,
+                                         const dmx_separate_opts* opts, float* stems_dev,
+                                         dmx_progress_fn progress, void* user) {
+  try {
+    if (!lr_dev || !stems_dev || n <= 0)
+      throw Error(DMX_ERR_INVALID, "dmx_separate_track_bag_device: bad argument");
+    BagPlan bag;
+    make_bag(nets, n_nets, weights, requested, &bag);
+    separate_track_impl(bag.nets[0], &bag, lr_dev, n, opts, stems_dev, progress, user);
+    return DMX_OK;
+  } catch (const Error& e) {
+    return fail(e);
+  } catch (const std::exception& e) {
+    return fail_std(e);
+  }
+}
+
+dmx_status dmx_separate_track_bag(dmx_handle* const* nets, int n_nets, const float* weights,
+                                  const int* requested, const float* left, const float* right,
+                                  int64_t n, const dmx_separate_opts* opts, float* stems_out,
+                                  dmx_progress_fn progress, void* user) {
+  try {
+    if (!left || !right || !stems_out || n <= 0)
+      throw Error(DMX_ERR_INVALID, "dmx_separate_track_bag: bad argument");
+    BagPlan bag;
+    make_bag(nets, n_nets, weights, requested, &bag);
+    separate_track_host(bag.nets[0], &bag, left, right, n, opts, stems_out, progress, user);
     return DMX_OK;
   } catch (const Error& e) {
     return fail(e);
@@ -2016,26 +2280,7 @@ dmx_status dmx_separate_track(dmx_handle* h, const float* left, const float* rig
   try {
     if (!h || !left || !right || !stems_out || n <= 0)
       throw Error(DMX_ERR_INVALID, "dmx_separate_track: bad argument");
-    CK(cudaSetDevice(h->device));
-    // host-track staging kept on the handle between calls (grown on demand)
-    const size_t need = (size_t)10 * n * sizeof(float);
-    if (need > h->host_io_cap) {
-      cudaFree(h->host_io);
-      h->host_io = nullptr;
-      h->host_io_cap = 0;
-      CK(cudaMalloc(&h->host_io, need));
-      h->host_io_cap = need;
-    }
-    float* d_lr = h->host_io;
-    float* d_stems = h->host_io + 2 * n;
-    CK(cudaMemcpyAsync(d_lr, left, n * sizeof(float), cudaMemcpyHostToDevice, h->stream));
-    CK(cudaMemcpyAsync(d_lr + n, right, n * sizeof(float), cudaMemcpyHostToDevice, h->stream));
-    const dmx_status st = dmx_separate_track_device(h, d_lr, n, opts, d_stems, progress, user);
-    if (st != DMX_OK) return st;
-    CK(cudaMemcpyAsync(stems_out, d_stems, 8 * n * sizeof(float), cudaMemcpyDeviceToHost, h->stream));
-    CK(cudaStreamSynchronize(h->stream));
-    check_device_flag(h);
-    finish_stage_times(h);
+    separate_track_host(h, nullptr, left, right, n, opts, stems_out, progress, user);
     return DMX_OK;
   } catch (const Error& e) {
     return fail(e);

@@ -22,6 +22,8 @@ EXPORTS = (
     "dmx_default_config", "dmx_create", "dmx_destroy", "dmx_last_error", "dmx_forward_start",
     "dmx_forward_collect", "dmx_forward_device", "dmx_separate_track",
     "dmx_separate_track_device", "dmx_normalize_track_device", "dmx_normalize_track_noalloc",
+    "dmx_bag_combine_device", "dmx_bag_forward_device", "dmx_separate_track_bag",
+    "dmx_separate_track_bag_device",
     "dmx_num_chunks", "dmx_track_finish", "dmx_track_shard", "dmx_set_trace",
     "dmx_set_stage_timing", "dmx_stage_times", "dmx_kernel_launches", "dmx_stream",
     "dmx_synchronize",
@@ -80,6 +82,19 @@ def lib():
                                                  ctypes.c_void_p, ctypes.c_void_p]
         L.dmx_normalize_track_noalloc.argtypes = [ctypes.c_void_p, ctypes.c_int64, ctypes.c_void_p,
                                                   ctypes.c_void_p, ctypes.c_void_p]
+        _hpp = ctypes.POINTER(ctypes.c_void_p)
+        _ip = ctypes.POINTER(ctypes.c_int)
+        L.dmx_bag_combine_device.argtypes = [_hpp, ctypes.c_int, _f32p, _ip, ctypes.c_int64,
+                                             ctypes.c_int64, ctypes.c_void_p, ctypes.c_void_p]
+        L.dmx_bag_forward_device.argtypes = [_hpp, ctypes.c_int, _f32p, _ip, ctypes.c_void_p,
+                                             ctypes.c_int64, ctypes.c_void_p]
+        L.dmx_separate_track_bag.argtypes = [_hpp, ctypes.c_int, _f32p, _ip, _f32p, _f32p,
+                                             ctypes.c_int64, ctypes.POINTER(SeparateOpts), _f32p,
+                                             PROGRESS_FN, ctypes.c_void_p]
+        L.dmx_separate_track_bag_device.argtypes = [_hpp, ctypes.c_int, _f32p, _ip,
+                                                    ctypes.c_void_p, ctypes.c_int64,
+                                                    ctypes.POINTER(SeparateOpts), ctypes.c_void_p,
+                                                    PROGRESS_FN, ctypes.c_void_p]
         L.dmx_track_finish.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64,
                                        ctypes.c_int64, ctypes.c_int64, ctypes.c_int, ctypes.c_double,
                                        ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p,
@@ -246,6 +261,75 @@ class Handle:
 
     def kernel_launches(self) -> int:
         return lib().dmx_kernel_launches(self._h)
+
+
+SOURCES = ("drums", "bass", "other", "vocals")
+
+
+def _bag_args(weights, requested):
+    w = np.ascontiguousarray(weights, dtype=np.float32)
+    if w.ndim != 2 or w.shape[1] != len(SOURCES):
+        raise ValueError(f"bag weights must be (n_nets, {len(SOURCES)}), got {w.shape}")
+    req = None
+    if requested is not None:
+        flags = [1 if (s in requested or i in requested) else 0 for i, s in enumerate(SOURCES)]
+        req = (ctypes.c_int * len(SOURCES))(*flags)
+    return w, req
+
+
+class Bag:
+    """A bag of networks (htdemucs_ft): BagCombineForward (api.rs:319-371).
+
+    ``handles`` are loaded networks on one device, ``weights`` the
+    (n_nets, 4) per-source weight matrix (identity for htdemucs_ft) and
+    ``requested`` the stems wanted (names or indices; None = all), which
+    decides which networks run. The handles stay owned by the caller."""
+
+    def __init__(self, handles, weights, requested=None):
+        self.handles = list(handles)
+        self.weights, self._req = _bag_args(weights, requested)
+        if self.weights.shape[0] != len(self.handles):
+            raise ValueError("one weight row per network")
+        self._nets = (ctypes.c_void_p * len(self.handles))(*[h._h.value for h in self.handles])
+
+    def forward_device(self, mix_ptr: int, n: int, out_ptr: int):
+        """Enqueue the bag forward of n device segments (lead network's stream)."""
+        _check(lib().dmx_bag_forward_device(self._nets, len(self.handles), _ptr(self.weights),
+                                            self._req, ctypes.c_void_p(mix_ptr), n,
+                                            ctypes.c_void_p(out_ptr)))
+
+    def separate_track(self, left, right, shifts=1, overlap=0.25, transition_power=1.0,
+                       batch=0, progress=None, out=None):
+        left = np.ascontiguousarray(left, dtype=np.float32)
+        right = np.ascontiguousarray(right, dtype=np.float32)
+        n = left.shape[0]
+        stems = np.empty((4, 2, n), dtype=np.float32) if out is None else out
+        assert stems.shape == (4, 2, n) and stems.dtype == np.float32 and stems.flags.c_contiguous
+        opts = SeparateOpts(shifts, overlap, transition_power, batch)
+        cb = PROGRESS_FN(0) if progress is None else PROGRESS_FN(lambda d, t, _u: progress(d, t))
+        _check(lib().dmx_separate_track_bag(self._nets, len(self.handles), _ptr(self.weights),
+                                            self._req, _ptr(left), _ptr(right), n,
+                                            ctypes.byref(opts), _ptr(stems), cb, None))
+        return stems
+
+    def separate_track_device(self, lr_ptr: int, n: int, stems_ptr: int, shifts=1, overlap=0.25,
+                              batch=0):
+        opts = SeparateOpts(shifts, overlap, 1.0, batch)
+        _check(lib().dmx_separate_track_bag_device(self._nets, len(self.handles),
+                                                   _ptr(self.weights), self._req,
+                                                   ctypes.c_void_p(lr_ptr), n, ctypes.byref(opts),
+                                                   ctypes.c_void_p(stems_ptr), PROGRESS_FN(0),
+                                                   None))
+
+
+def bag_combine_device(out_ptrs, weights, requested, n_segments: int, samples: int,
+                       combined_ptr: int, stream: int = 0):
+    """dmx_bag_combine_device: ``out_ptrs`` are device pointers (0 for networks
+    that carry no requested weight), each (n_segments, 4, 2, samples)."""
+    w, req = _bag_args(weights, requested)
+    ptrs = (ctypes.c_void_p * len(out_ptrs))(*[p or None for p in out_ptrs])
+    _check(lib().dmx_bag_combine_device(ptrs, len(out_ptrs), _ptr(w), req, n_segments, samples,
+                                        ctypes.c_void_p(combined_ptr), ctypes.c_void_p(stream)))
 
 
 def normalize_track_noalloc(lr_ptr: int, n: int, mix_norm_ptr: int, mean_std_ptr: int,

@@ -100,24 +100,27 @@ def plan(length: int, world: int, shifts: int = 1, overlap: float = 0.25,
                      trim, chunks, ranks)
 
 
-def exchange_tails(dist, p: TrackPlan, rank: int, acc):
+def exchange_tails(dist, p: TrackPlan, rank: int, acc, ranks=None):
     """Rank r adds rank r-1's tail into its own head: ``acc`` is this rank's
-    (8, view_length) accumulator (torch tensor on the backend's device)."""
+    (8, view_length) accumulator (torch tensor on the backend's device).
+    ``rank`` is the index in the plan; ``ranks[i]`` is the process-group rank
+    of plan index i (default: the identity), so a plan can span a sub-group."""
     import torch
 
     world = len(p.ranks)
+    ranks = list(range(world)) if ranks is None else list(ranks)
     me = p.rank(rank)
     ops = []
     recv = None
     if rank + 1 < world and me.send_hi > me.send_lo and p.rank(rank + 1).chunk_hi > p.rank(rank + 1).chunk_lo:
         send = acc[:, me.send_lo:me.send_hi].contiguous()
-        ops.append(dist.P2POp(dist.isend, send, rank + 1))
+        ops.append(dist.P2POp(dist.isend, send, ranks[rank + 1]))
     if rank > 0:
         prev = p.rank(rank - 1)
         if prev.send_hi > prev.send_lo and me.chunk_hi > me.chunk_lo:
             recv = torch.empty((acc.shape[0], prev.send_hi - prev.send_lo), dtype=acc.dtype,
                                device=acc.device)
-            ops.append(dist.P2POp(dist.irecv, recv, rank - 1))
+            ops.append(dist.P2POp(dist.irecv, recv, ranks[rank - 1]))
     if ops:
         for req in dist.batch_isend_irecv(ops):
             req.wait()
@@ -126,11 +129,13 @@ def exchange_tails(dist, p: TrackPlan, rank: int, acc):
         acc[:, prev.send_lo:prev.send_hi] += recv
 
 
-def gather_stems(dist, p: TrackPlan, rank: int, stems):
-    """Rank 0 receives every rank's owned output samples into ``stems`` (8, length)."""
+def gather_stems(dist, p: TrackPlan, rank: int, stems, ranks=None):
+    """Plan index 0 receives every plan index's owned output samples into
+    ``stems`` (8, length); ``ranks`` as in exchange_tails."""
     import torch
 
     world = len(p.ranks)
+    ranks = list(range(world)) if ranks is None else list(ranks)
     me = p.rank(rank)
     if rank == 0:
         bufs = []
@@ -141,7 +146,7 @@ def gather_stems(dist, p: TrackPlan, rank: int, stems):
                 buf = torch.empty((stems.shape[0], q.t_hi - q.t_lo), dtype=stems.dtype,
                                   device=stems.device)
                 bufs.append((q, buf))
-                ops.append(dist.P2POp(dist.irecv, buf, r))
+                ops.append(dist.P2POp(dist.irecv, buf, ranks[r]))
         if ops:
             for req in dist.batch_isend_irecv(ops):
                 req.wait()
@@ -149,5 +154,85 @@ def gather_stems(dist, p: TrackPlan, rank: int, stems):
             stems[:, q.t_lo:q.t_hi] = buf
     elif me.t_hi > me.t_lo:
         send = stems[:, me.t_lo:me.t_hi].contiguous()
-        for req in dist.batch_isend_irecv([dist.P2POp(dist.isend, send, 0)]):
+        for req in dist.batch_isend_irecv([dist.P2POp(dist.isend, send, ranks[0])]):
             req.wait()
+
+
+# ---------------------------------------------------------------------------
+# Bags of networks (htdemucs_ft) over ranks
+# ---------------------------------------------------------------------------
+
+def needed_nets(weights, requested=None):
+    """Networks that carry a nonzero weight on a requested source
+    (api.rs:907-916); ``requested`` holds source indices (None = all)."""
+    return [k for k, row in enumerate(weights)
+            if any(w != 0 and (requested is None or s in requested) for s, w in enumerate(row))]
+
+
+@dataclass
+class BagAssignment:
+    nets: list    # the networks this rank runs, in bag order
+    group: list   # process-group ranks that shard each of those networks' chunks
+    index: int    # this rank's index in `group`
+    owner: dict   # network -> rank that holds its whole-track stems (its group's first)
+
+
+def bag_assign(n_nets: int, world: int, rank: int, weights=None, requested=None) -> BagAssignment:
+    """One network per GPU group: with at least as many ranks as running
+    networks (and a multiple of them), network j gets the ranks
+    [j*g, (j+1)*g), g = world // running, and its chunks are sharded over
+    them; with fewer ranks than networks, rank r runs networks r, r + world, ...
+    whole (each rank a group of one)."""
+    run = needed_nets(weights, requested) if weights is not None else list(range(n_nets))
+    if not run:
+        raise ValueError("no network carries a requested stem")
+    if world >= len(run):
+        if world % len(run):
+            raise ValueError(f"{world} ranks do not split evenly over {len(run)} networks")
+        g = world // len(run)
+        j = rank // g
+        owner = {k: i * g for i, k in enumerate(run)}
+        return BagAssignment([run[j]], list(range(j * g, (j + 1) * g)), rank - j * g, owner)
+    owner = {k: i % world for i, k in enumerate(run)}
+    mine = [k for i, k in enumerate(run) if i % world == rank]
+    return BagAssignment(mine, [rank], 0, owner)
+
+
+def bag_gather(dist, rank: int, assign: BagAssignment, stems_by_net: dict, weights, requested,
+               combine, like):
+    """Rank 0 receives, from each running network's owner, the stem lanes
+    that network is weighted on, then calls ``combine(outs, weights,
+    requested)`` with ``outs[k]`` a (4, 2, n) tensor per network (None for
+    networks that do not run) and returns its result; other ranks return
+    None. ``stems_by_net[k]`` is this rank's (4, 2, n) stems of network k
+    (ranks that own a network); ``like`` gives shape, dtype and device."""
+    import torch
+
+    sources = len(weights[0])
+    req = [requested is None or s in requested for s in range(sources)]
+    lanes = [(k, s) for k in sorted(assign.owner) for s in range(sources)
+             if weights[k][s] != 0 and req[s]]
+    if rank == 0:
+        outs = [None] * len(weights)
+        ops, recvs = [], []
+        for k, s in lanes:
+            if outs[k] is None:
+                outs[k] = torch.zeros_like(like)
+            if assign.owner[k] == 0:
+                outs[k][s] = stems_by_net[k][s]
+            else:
+                buf = torch.empty_like(like[0])
+                recvs.append((k, s, buf))
+                ops.append(dist.P2POp(dist.irecv, buf, assign.owner[k]))
+        if ops:
+            for work in dist.batch_isend_irecv(ops):
+                work.wait()
+        for k, s, buf in recvs:
+            outs[k][s] = buf
+        return combine(outs, weights, requested)
+    ops = [dist.P2POp(dist.isend, stems_by_net[k][s].contiguous(), 0)
+           for k, s in lanes if assign.owner[k] == rank]
+    if ops:
+        for work in dist.batch_isend_irecv(ops):
+            work.wait()
+    return None

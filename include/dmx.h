@@ -134,6 +134,57 @@ dmx_status dmx_normalize_track_device(dmx_handle* h, const float* lr_dev, int64_
 dmx_status dmx_normalize_track_noalloc(const float* lr_dev, int64_t n, float* mix_norm_dev,
                                        float* mean_std_dev, void* stream);
 
+/* Bags of networks (htdemucs_ft). A bag is `n_nets` (1..8) loaded networks and
+ * a weight matrix `weights` (n_nets x 4, one row per network, sources in the
+ * config's order drums, bass, other, vocals; htdemucs_ft ships the identity),
+ * plus `requested`, 4 flags for the stems the caller wants (NULL = all; the
+ * reference's StemSelection, api.rs:895-906). A network runs only when it
+ * carries a nonzero weight on a requested stem (api.rs:907-916); a requested
+ * stem whose weights sum to zero is rejected with DMX_ERR_INVALID ("no network
+ * covers stem", api.rs:954-960). Stems that are not requested come out as the
+ * zero signal (the track mean after denormalisation).
+ *
+ * The combination step of BagCombineForward::start (api.rs:326-361) on device
+ * buffers of the current device: for each stem s, combined = (sum over the
+ * networks k, in bag order, of outs[k][s] * w[k][s]) / (sum of those w), with
+ * the reference's f32 roundings (product, then sum, then quotient). outs_dev
+ * holds n_nets device pointers, each (n_segments, 4, 2, samples) — entries
+ * of networks that carry no requested weight may be NULL — and combined_dev
+ * is the same shape. Enqueued on `stream` (a cudaStream_t, NULL = legacy
+ * default stream); allocates nothing. Used per chunk batch by the lockstep
+ * driver below, and on rank 0 to combine whole-track stems gathered from
+ * one network per GPU. */
+dmx_status dmx_bag_combine_device(const float* const* outs_dev, int n_nets, const float* weights,
+                                  const int* requested, int64_t n_segments, int64_t samples,
+                                  float* combined_dev, void* stream);
+
+/* BagCombineForward as a SegmentForward (api.rs:319-371) on device buffers:
+ * every running network forwards mix_dev (n, 2, segment_samples), one after
+ * another on its own stream, and the combination is written to out_dev
+ * (n, 4, 2, segment_samples) on the stream of the first running network
+ * (the lead). All running networks must be handles on one device. */
+dmx_status dmx_bag_forward_device(dmx_handle* const* nets, int n_nets, const float* weights,
+                                  const int* requested, const float* mix_dev, int64_t n,
+                                  float* out_dev);
+
+/* Demucs::separate_with_options for an htdemucs_ft bag (api.rs:736-785:
+ * run_mix -> separate_streaming_normalized_mix -> separate_forwarding_emit
+ * over BagCombineForward): the dmx_separate_track driver with each chunk
+ * batch forwarded through every running network and combined before the
+ * overlap-add. The lead network's handle supplies the stream and the track
+ * staging. Progress counts chunks times running networks (api.rs:764-776). */
+dmx_status dmx_separate_track_bag(dmx_handle* const* nets, int n_nets, const float* weights,
+                                  const int* requested, const float* left, const float* right,
+                                  int64_t n, const dmx_separate_opts* opts, float* stems_out,
+                                  dmx_progress_fn progress, void* user);
+
+/* dmx_separate_track_bag on device buffers of the bag's device: lr_dev (2, n)
+ * -> stems_dev (4, 2, n), enqueued on the lead's stream. */
+dmx_status dmx_separate_track_bag_device(dmx_handle* const* nets, int n_nets, const float* weights,
+                                         const int* requested, const float* lr_dev, int64_t n,
+                                         const dmx_separate_opts* opts, float* stems_dev,
+                                         dmx_progress_fn progress, void* user);
+
 /* Chunk plan of a split pass (streaming.rs:88-94, 296-330): number of chunks
  * of a view of `view_length` samples. */
 int64_t dmx_num_chunks(int64_t view_length, int segment, double overlap);

@@ -140,3 +140,41 @@ def separate_with(forward, mix, segment, shifts=0, overlap=0.25, transition_powe
     m = OracleModel({}, segment)
     return m.separate(mix, shifts=shifts, overlap=overlap, transition_power=transition_power,
                       batch=batch, forward=forward)
+
+
+def bag_forward(forwards, weights, requested=None):
+    """BagCombineForward::start (api.rs:319-361) over per-network segment
+    forwards: returns a forward ``padded (G, 2, seg) -> (G, 4, 2, seg)``.
+
+    A network runs only if it carries a nonzero weight on a requested source
+    (api.rs:330-337); per source the combination starts from zeros, adds each
+    running network's lane times its weight (f32 product, then f32 sum) in bag
+    order, and divides by the f32 sum of those weights (api.rs:338-360);
+    sources that are not requested stay zero. ``requested`` is a sequence of
+    source indices (None = all four)."""
+    w = np.asarray(weights, dtype=np.float32)
+    sources = w.shape[1]
+    req = [requested is None or s in requested for s in range(sources)]
+
+    def forward(padded):
+        batch, channels, time = padded.shape
+        combined = np.zeros((batch, sources, channels, time), dtype=np.float32)
+        totals = [np.float32(0.0)] * sources
+        for k, fwd in enumerate(forwards):
+            if not any(w[k, s] != 0 and req[s] for s in range(sources)):
+                continue
+            out = np.asarray(fwd(padded), dtype=np.float32)
+            for s in range(sources):
+                if w[k, s] == 0 or not req[s]:
+                    continue
+                combined[:, s] += out[:, s] * w[k, s]
+                totals[s] = np.float32(totals[s] + w[k, s])
+        for s in range(sources):
+            if not req[s]:
+                continue
+            if totals[s] == 0:
+                raise ValueError(f"no network covers stem index {s}")
+            combined[:, s] /= totals[s]
+        return combined
+
+    return forward
