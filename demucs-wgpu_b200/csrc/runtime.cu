@@ -490,6 +490,10 @@ struct dmx_handle {
   int64_t tc_launches = 0;
   float* bag_out = nullptr;  // this network's own forward output when it runs inside a bag
   int64_t bag_cap = 0;       // segments bag_out holds
+  char* batch_ws = nullptr;  // per-track slots of dmx_separate_batch_device
+  size_t batch_cap = 0;
+  float* batch_io = nullptr;  // device staging of dmx_separate_batch's host tracks and stems
+  size_t batch_io_cap = 0;
 
   float* W(size_t off) const { return wdev + off; }
 
@@ -1721,6 +1725,8 @@ void dmx_destroy(dmx_handle* h) {
   cudaFree(h->host_io);
   cudaFree(h->norm_scratch);
   cudaFree(h->bag_out);
+  cudaFree(h->batch_ws);
+  cudaFree(h->batch_io);
   cudaFreeHost(h->pinned_in);
   cudaFreeHost(h->pinned_out);
   if (h->stream) cudaStreamDestroy(h->stream);
@@ -2148,9 +2154,249 @@ void separate_track_host(dmx_handle* h, BagPlan* bag, const float* left, const f
   finish_stage_times(h);
 }
 
+// Many tracks through one network with their chunks pooled into full
+// forwards (BASELINE config "throughput batch"). The work units are (track,
+// shift pass, chunk) in that order; consecutive units fill each forward of
+// `batch` chunks regardless of which track or pass they belong to. Every
+// track is driven exactly as separate_track_impl drives it — its own global
+// normalisation, the same ShiftRng offsets (a fresh ShiftRng per track, as
+// each Demucs::separate call seeds its own: pipeline.rs:416-418), its own
+// overlap-add accumulator and finish — so each track's stems equal
+// dmx_separate_track's on that track. A track holds one workspace slot
+// (normalised mix, moments, pass sum, accumulator) from the forward that
+// takes its first chunk to the one that takes its last.
+void separate_batch_impl(dmx_handle* h, const float* const* lr_dev, const int64_t* lengths,
+                         int n_tracks, const dmx_separate_opts* opts, float* const* stems_dev,
+                         dmx_progress_fn progress, void* user) {
+  if (!lr_dev || !lengths || !stems_dev || n_tracks < 1)
+    throw Error(DMX_ERR_INVALID, "dmx_separate_batch: bad argument");
+  dmx_separate_opts o{1, 0.25, 1.0, 0};
+  if (opts) o = *opts;
+  if (o.transition_power != 1.0) throw Error(DMX_ERR_INVALID, "transition_power must be 1");
+  if (o.shifts < 0) throw Error(DMX_ERR_INVALID, "shifts must be >= 0");
+  CK(cudaSetDevice(h->device));
+  const int seg = kSegment;
+  const int64_t stride = (int64_t)((1.0 - o.overlap) * (double)seg);
+  if (stride <= 0) throw Error(DMX_ERR_INVALID, "overlap leaves a zero stride");
+  const int64_t max_shift = o.shifts > 0 ? (int64_t)(0.5 * 44100.0) : 0;
+  const int passes = std::max(1, o.shifts);
+  const float scale = o.shifts > 0 ? 1.0f / (float)o.shifts : 1.0f;
+  // ShiftRng (pipeline.rs:136-151), seed 0x5eed1234: the same offsets for every track
+  std::vector<int64_t> offsets;
+  uint64_t rng = 0x5eed1234ULL * 6364136223846793005ULL + 1ULL;
+  for (int pass = 0; pass < passes; ++pass) {
+    int64_t offset = 0;
+    if (o.shifts > 0) {
+      rng = rng * 6364136223846793005ULL + 1442695040888963407ULL;
+      offset = (int64_t)((rng >> 33) % (uint64_t)(max_shift + 1));
+    }
+    offsets.push_back(offset);
+  }
+  auto view_len = [&](int64_t n, int pass) {
+    return o.shifts > 0 ? n + max_shift - offsets[pass] : n;
+  };
+  std::vector<std::vector<int64_t>> chunks(n_tracks);  // per track, per pass
+  std::vector<int64_t> first(n_tracks + 1, 0);         // first unit of each track
+  int64_t n_max = 0;
+  for (int i = 0; i < n_tracks; ++i) {
+    if (lengths[i] <= 0 || !lr_dev[i] || !stems_dev[i])
+      throw Error(DMX_ERR_INVALID, "track " + std::to_string(i) + " is empty or has no buffer");
+    n_max = std::max(n_max, lengths[i]);
+    int64_t units = 0;
+    for (int pass = 0; pass < passes; ++pass) {
+      chunks[i].push_back(dmx_num_chunks(view_len(lengths[i], pass), seg, o.overlap));
+      units += chunks[i].back();
+    }
+    first[i + 1] = first[i] + units;
+  }
+  const int64_t total = first[n_tracks];
+  const int batch = std::max(1, o.batch > 0 ? std::min(o.batch, h->cfg.max_batch) : h->cfg.max_batch);
+  // slots: the most tracks any one forward touches
+  int slots = 1;
+  for (int64_t u0 = 0, i = 0; u0 < total; u0 += batch) {
+    const int64_t u1 = std::min<int64_t>(total, u0 + batch);
+    while (first[i + 1] <= u0) ++i;
+    int64_t j = i;
+    while (j + 1 < n_tracks && first[j + 1] < u1) ++j;
+    slots = std::max(slots, (int)(j - i + 1));
+  }
+  const size_t scratch_bytes = (size_t)track_normalize_scratch_doubles() * sizeof(double);
+  const size_t slot_floats = (size_t)(2 * n_max + (o.shifts > 1 ? 8 * n_max : 0) + 8 * (n_max + max_shift));
+  const size_t slot_bytes = (scratch_bytes + 512 + slot_floats * sizeof(float) + 255) / 256 * 256;
+  if ((size_t)slots * slot_bytes > h->batch_cap) {
+    cudaFree(h->batch_ws);
+    h->batch_ws = nullptr;
+    h->batch_cap = 0;
+    CK(cudaMalloc(&h->batch_ws, (size_t)slots * slot_bytes));
+    h->batch_cap = (size_t)slots * slot_bytes;
+  }
+  struct Slot {
+    double* stats;
+    float2* norm;
+    float* mix;
+    float* pass;
+    float* acc;
+  };
+  auto slot_at = [&](int k) {
+    char* base = h->batch_ws + (size_t)k * slot_bytes;
+    Slot sl;
+    sl.stats = reinterpret_cast<double*>(base);
+    sl.norm = reinterpret_cast<float2*>(base + scratch_bytes);
+    sl.mix = reinterpret_cast<float*>(base + scratch_bytes + 512);
+    sl.pass = o.shifts > 1 ? sl.mix + 2 * n_max : nullptr;
+    sl.acc = sl.mix + 2 * n_max + (o.shifts > 1 ? 8 * n_max : 0);
+    return sl;
+  };
+  std::vector<int> free_slots;
+  for (int k = slots - 1; k >= 0; --k) free_slots.push_back(k);
+  std::vector<int> slot_of(n_tracks, -1);
+  ensure_io(h, batch);
+  h->launches = 0;
+  const float* w_ola = h->W(h->m.ola_w.off);
+  struct Run {
+    int track, pass;
+    int64_t c0, count, at;  // chunks [c0, c0 + count) of the pass, at forward row `at`
+  };
+  int ti = 0, tp = 0;
+  int64_t tc = 0;  // cursor: next unit is chunk tc of pass tp of track ti
+  for (int64_t u0 = 0; u0 < total; u0 += batch) {
+    const int G = (int)std::min<int64_t>(batch, total - u0);
+    std::vector<Run> runs;
+    for (int64_t left = G, at = 0; left > 0;) {
+      const int64_t take = std::min<int64_t>(left, chunks[ti][tp] - tc);
+      runs.push_back({ti, tp, tc, take, at});
+      at += take;
+      left -= take;
+      tc += take;
+      if (tc == chunks[ti][tp]) {
+        tc = 0;
+        if (++tp == passes) {
+          tp = 0;
+          ++ti;
+        }
+      }
+    }
+    // tracks that start here: a slot, the global normalisation, a cleared pass sum
+    for (const Run& r : runs) {
+      if (r.pass != 0 || r.c0 != 0) continue;
+      const int i = r.track;
+      slot_of[i] = free_slots.back();
+      free_slots.pop_back();
+      const Slot sl = slot_at(slot_of[i]);
+      h->mark("track.normalize");
+      launch_track_normalize(lr_dev[i], lr_dev[i] + lengths[i], lengths[i], sl.stats, sl.mix,
+                             sl.norm, h->stream);
+      h->launches += 2;
+      if (sl.pass) CK(cudaMemsetAsync(sl.pass, 0, 8 * lengths[i] * sizeof(float), h->stream));
+    }
+    for (const Run& r : runs) {
+      const Slot sl = slot_at(slot_of[r.track]);
+      h->mark("track.gather");
+      launch_gather_chunks(sl.mix, lengths[r.track], offsets[r.pass], max_shift, seg, stride, r.c0,
+                           (int)r.count, h->io_in + r.at * 2 * seg, h->stream);
+      ++h->launches;
+    }
+    run_forward(h, h->io_in, G, h->io_out);
+    for (const Run& r : runs) {
+      const int i = r.track;
+      const Slot sl = slot_at(slot_of[i]);
+      const int64_t n = lengths[i];
+      const int64_t vlen = view_len(n, r.pass);
+      if (r.c0 == 0) CK(cudaMemsetAsync(sl.acc, 0, 8 * vlen * sizeof(float), h->stream));
+      h->mark("track.ola");
+      launch_ola_accumulate(h->io_out + r.at * 8 * seg, n, offsets[r.pass], max_shift, seg, stride,
+                            r.c0, (int)r.count, w_ola, sl.acc, 0, vlen, h->stream);
+      ++h->launches;
+      if (r.c0 + r.count < chunks[i][r.pass]) continue;
+      const int mode = o.shifts == 0 ? 0 : (o.shifts == 1 ? 1 : 2);
+      h->mark("track.finish");
+      launch_ola_finish(sl.acc, n, offsets[r.pass], max_shift, seg, stride, w_ola, sl.norm, scale,
+                        mode, sl.pass, stems_dev[i], h->stream);
+      ++h->launches;
+      if (r.pass + 1 < passes) continue;
+      if (o.shifts > 1) {
+        launch_ola_finish(sl.acc, n, 0, max_shift, seg, stride, w_ola, sl.norm, scale, 3, sl.pass,
+                          stems_dev[i], h->stream);
+        ++h->launches;
+      }
+      free_slots.push_back(slot_of[i]);
+      slot_of[i] = -1;
+    }
+    CK(cudaGetLastError());
+    if (progress) {
+      CK(cudaStreamSynchronize(h->stream));
+      progress((size_t)(u0 + G), (size_t)total, user);
+    }
+  }
+  h->mark("end");
+}
+
 }  // namespace
 
 extern "C" {
+
+dmx_status dmx_separate_batch_device(dmx_handle* h, const float* const* lr_dev,
+                                     const int64_t* lengths, int n_tracks,
+                                     const dmx_separate_opts* opts, float* const* stems_dev,
+                                     dmx_progress_fn progress, void* user) {
+  try {
+    if (!h) throw Error(DMX_ERR_INVALID, "dmx_separate_batch_device: bad argument");
+    separate_batch_impl(h, lr_dev, lengths, n_tracks, opts, stems_dev, progress, user);
+    return DMX_OK;
+  } catch (const Error& e) {
+    return fail(e);
+  } catch (const std::exception& e) {
+    return fail_std(e);
+  }
+}
+
+dmx_status dmx_separate_batch(dmx_handle* h, const float* const* left, const float* const* right,
+                              const int64_t* lengths, int n_tracks, const dmx_separate_opts* opts,
+                              float* const* stems_out, dmx_progress_fn progress, void* user) {
+  try {
+    if (!h || !left || !right || !lengths || !stems_out || n_tracks < 1)
+      throw Error(DMX_ERR_INVALID, "dmx_separate_batch: bad argument");
+    CK(cudaSetDevice(h->device));
+    int64_t sum = 0;
+    for (int i = 0; i < n_tracks; ++i) {
+      if (lengths[i] <= 0 || !left[i] || !right[i] || !stems_out[i])
+        throw Error(DMX_ERR_INVALID, "track " + std::to_string(i) + " is empty or has no buffer");
+      sum += lengths[i];
+    }
+    // every track's input (2 n) and stems (8 n) stay on the device for the call
+    const size_t need = (size_t)10 * sum * sizeof(float);
+    if (need > h->batch_io_cap) {
+      cudaFree(h->batch_io);
+      h->batch_io = nullptr;
+      h->batch_io_cap = 0;
+      CK(cudaMalloc(&h->batch_io, need));
+      h->batch_io_cap = need;
+    }
+    std::vector<const float*> d_lr(n_tracks);
+    std::vector<float*> d_stems(n_tracks);
+    float* at = h->batch_io;
+    for (int i = 0; i < n_tracks; ++i) {
+      const int64_t n = lengths[i];
+      d_lr[i] = at;
+      CK(cudaMemcpyAsync(at, left[i], n * sizeof(float), cudaMemcpyHostToDevice, h->stream));
+      CK(cudaMemcpyAsync(at + n, right[i], n * sizeof(float), cudaMemcpyHostToDevice, h->stream));
+      d_stems[i] = at + 2 * n;
+      at += 10 * n;
+    }
+    separate_batch_impl(h, d_lr.data(), lengths, n_tracks, opts, d_stems.data(), progress, user);
+    for (int i = 0; i < n_tracks; ++i)
+      CK(cudaMemcpyAsync(stems_out[i], d_stems[i], 8 * lengths[i] * sizeof(float),
+                         cudaMemcpyDeviceToHost, h->stream));
+    CK(cudaStreamSynchronize(h->stream));
+    check_device_flag(h);
+    finish_stage_times(h);
+    return DMX_OK;
+  } catch (const Error& e) {
+    return fail(e);
+  } catch (const std::exception& e) {
+    return fail_std(e);
+  }
+}
 
 dmx_status dmx_track_shard(dmx_handle* h, const float* mix_norm_dev, int64_t length,
                            int64_t shift_offset, int64_t max_shift, int segment, double overlap,

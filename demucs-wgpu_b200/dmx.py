@@ -23,7 +23,7 @@ EXPORTS = (
     "dmx_forward_collect", "dmx_forward_device", "dmx_separate_track",
     "dmx_separate_track_device", "dmx_normalize_track_device", "dmx_normalize_track_noalloc",
     "dmx_bag_combine_device", "dmx_bag_forward_device", "dmx_separate_track_bag",
-    "dmx_separate_track_bag_device",
+    "dmx_separate_track_bag_device", "dmx_separate_batch", "dmx_separate_batch_device",
     "dmx_num_chunks", "dmx_track_finish", "dmx_track_shard", "dmx_set_trace",
     "dmx_set_stage_timing", "dmx_stage_times", "dmx_kernel_launches", "dmx_stream",
     "dmx_synchronize",
@@ -95,6 +95,13 @@ def lib():
                                                     ctypes.c_void_p, ctypes.c_int64,
                                                     ctypes.POINTER(SeparateOpts), ctypes.c_void_p,
                                                     PROGRESS_FN, ctypes.c_void_p]
+        _f32pp = ctypes.POINTER(_f32p)
+        L.dmx_separate_batch.argtypes = [ctypes.c_void_p, _f32pp, _f32pp, _i64p, ctypes.c_int,
+                                         ctypes.POINTER(SeparateOpts), _f32pp, PROGRESS_FN,
+                                         ctypes.c_void_p]
+        L.dmx_separate_batch_device.argtypes = [ctypes.c_void_p, _hpp, _i64p, ctypes.c_int,
+                                                ctypes.POINTER(SeparateOpts), _hpp, PROGRESS_FN,
+                                                ctypes.c_void_p]
         L.dmx_track_finish.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64,
                                        ctypes.c_int64, ctypes.c_int64, ctypes.c_int, ctypes.c_double,
                                        ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p,
@@ -198,6 +205,33 @@ class Handle:
         _check(lib().dmx_separate_track(self._h, _ptr(left), _ptr(right), n, ctypes.byref(opts),
                                         _ptr(stems), cb, None))
         return stems
+
+    def separate_batch(self, tracks, shifts=1, overlap=0.25, transition_power=1.0, batch=0,
+                       progress=None, outs=None):
+        """Many (2, n_i) host tracks in one call with their chunks pooled into
+        full forwards (dmx_separate_batch); returns a list of (4, 2, n_i)."""
+        lefts = [np.ascontiguousarray(t[0], dtype=np.float32) for t in tracks]
+        rights = [np.ascontiguousarray(t[1], dtype=np.float32) for t in tracks]
+        lengths = (ctypes.c_int64 * len(tracks))(*[x.shape[0] for x in lefts])
+        if outs is None:
+            outs = [np.empty((4, 2, x.shape[0]), dtype=np.float32) for x in lefts]
+        for o, x in zip(outs, lefts):
+            assert o.shape == (4, 2, x.shape[0]) and o.dtype == np.float32 and o.flags.c_contiguous
+        arr = lambda xs: (_f32p * len(xs))(*[_ptr(x) for x in xs])  # noqa: E731
+        opts = SeparateOpts(shifts, overlap, transition_power, batch)
+        cb = PROGRESS_FN(0) if progress is None else PROGRESS_FN(lambda d, t, _u: progress(d, t))
+        _check(lib().dmx_separate_batch(self._h, arr(lefts), arr(rights), lengths, len(tracks),
+                                        ctypes.byref(opts), arr(outs), cb, None))
+        return outs
+
+    def separate_batch_device(self, lr_ptrs, lengths, stems_ptrs, shifts=1, overlap=0.25,
+                              batch=0):
+        """Enqueue dmx_separate_batch_device on device buffers (returns at once)."""
+        n = len(lr_ptrs)
+        opts = SeparateOpts(shifts, overlap, 1.0, batch)
+        _check(lib().dmx_separate_batch_device(
+            self._h, (ctypes.c_void_p * n)(*lr_ptrs), (ctypes.c_int64 * n)(*lengths), n,
+            ctypes.byref(opts), (ctypes.c_void_p * n)(*stems_ptrs), PROGRESS_FN(0), None))
 
     def track_shard(self, mix_norm_ptr, length, shift_offset, max_shift, overlap, chunk_lo,
                     chunk_hi, batch, acc_ptr, view_lo, view_hi):

@@ -106,6 +106,33 @@ dmx_status dmx_separate_track_device(dmx_handle* h, const float* lr_dev, int64_t
                                      const dmx_separate_opts* opts, float* stems_dev,
                                      dmx_progress_fn progress, void* user);
 
+/* Many tracks in one call, with their chunks pooled (the `dmx_separate_batch`
+ * of the drop-in plan; in the reference each track is one
+ * Demucs::separate_with_options call, api.rs:438-545). The work units —
+ * (track, shift pass, chunk), in that order — fill every forward of
+ * opts->batch chunks (0 = max_batch) regardless of which track they belong to,
+ * so short tracks and the tails of shift passes do not leave forwards
+ * half-empty. Each track is otherwise driven exactly as dmx_separate_track
+ * drives it (its own global normalisation, the ShiftRng offsets of a fresh
+ * seed 0x5eed1234, its own overlap-add), so its stems match that call's.
+ * left[i] / right[i] hold lengths[i] samples; stems_out[i] receives
+ * (4, 2, lengths[i]). All tracks' inputs and stems stay in device memory for
+ * the call (10 floats per sample), plus one workspace slot (about 18 floats
+ * per sample of the longest track) per track that a single forward touches.
+ * Progress counts units. */
+dmx_status dmx_separate_batch(dmx_handle* h, const float* const* left, const float* const* right,
+                              const int64_t* lengths, int n_tracks, const dmx_separate_opts* opts,
+                              float* const* stems_out, dmx_progress_fn progress, void* user);
+
+/* dmx_separate_batch on device buffers of the handle's GPU: lr_dev[i] is the
+ * raw (2, lengths[i]) track i, stems_dev[i] receives (4, 2, lengths[i]).
+ * Enqueued on the handle's stream; returns without waiting unless `progress`
+ * is set. */
+dmx_status dmx_separate_batch_device(dmx_handle* h, const float* const* lr_dev,
+                                     const int64_t* lengths, int n_tracks,
+                                     const dmx_separate_opts* opts, float* const* stems_dev,
+                                     dmx_progress_fn progress, void* user);
+
 /* Global normalisation of a raw stereo track on the device (Separator's
  * normalisation: streaming.rs:52-85 scan_norm + apply_norm_inplace): from
  * lr_dev (2, n) writes (x - mean) / std into mix_norm_dev (2, n) and
