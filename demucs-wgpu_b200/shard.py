@@ -19,6 +19,32 @@ from dataclasses import dataclass
 SEGMENT = 343980
 SR = 44100
 SHIFT_SEED = 0x5EED1234
+# Bound on every point-to-point wait of the exchange and the gathers: a peer
+# whose data never arrives (a rank that died or skipped the step) turns into
+# ShardTimeout instead of a hang.
+WAIT_SECONDS = 120.0
+
+
+class ShardTimeout(TimeoutError):
+    """A bounded wait for a peer's data gave up (the C ABI's DMX_ERR_TIMEOUT)."""
+
+    code = 4  # DMX_ERR_TIMEOUT
+
+
+def _wait_all(works, what, timeout=None):
+    """Waits for every request, each at most ``timeout`` seconds (default
+    WAIT_SECONDS); a request that does not complete raises ShardTimeout."""
+    import datetime
+
+    limit = datetime.timedelta(seconds=WAIT_SECONDS if timeout is None else timeout)
+    for work in works:
+        try:
+            ok = work.wait(timeout=limit)
+        except RuntimeError as exc:  # gloo / NCCL report an expired wait by raising
+            raise ShardTimeout(f"{what}: no data from the peer within {limit.total_seconds():g} s "
+                               f"({exc})") from exc
+        if ok is False:
+            raise ShardTimeout(f"{what}: no data from the peer within {limit.total_seconds():g} s")
 
 
 def shift_offsets(shifts: int, max_shift: int, seed: int = SHIFT_SEED):
@@ -100,11 +126,12 @@ def plan(length: int, world: int, shifts: int = 1, overlap: float = 0.25,
                      trim, chunks, ranks)
 
 
-def exchange_tails(dist, p: TrackPlan, rank: int, acc, ranks=None):
+def exchange_tails(dist, p: TrackPlan, rank: int, acc, ranks=None, timeout=None):
     """Rank r adds rank r-1's tail into its own head: ``acc`` is this rank's
     (8, view_length) accumulator (torch tensor on the backend's device).
     ``rank`` is the index in the plan; ``ranks[i]`` is the process-group rank
-    of plan index i (default: the identity), so a plan can span a sub-group."""
+    of plan index i (default: the identity), so a plan can span a sub-group.
+    Each wait is bounded (``timeout`` seconds, default WAIT_SECONDS)."""
     import torch
 
     world = len(p.ranks)
@@ -122,14 +149,13 @@ def exchange_tails(dist, p: TrackPlan, rank: int, acc, ranks=None):
                                device=acc.device)
             ops.append(dist.P2POp(dist.irecv, recv, ranks[rank - 1]))
     if ops:
-        for req in dist.batch_isend_irecv(ops):
-            req.wait()
+        _wait_all(dist.batch_isend_irecv(ops), "overlap-add boundary exchange", timeout)
     if recv is not None:
         prev = p.rank(rank - 1)
         acc[:, prev.send_lo:prev.send_hi] += recv
 
 
-def gather_stems(dist, p: TrackPlan, rank: int, stems, ranks=None):
+def gather_stems(dist, p: TrackPlan, rank: int, stems, ranks=None, timeout=None):
     """Plan index 0 receives every plan index's owned output samples into
     ``stems`` (8, length); ``ranks`` as in exchange_tails."""
     import torch
@@ -148,14 +174,13 @@ def gather_stems(dist, p: TrackPlan, rank: int, stems, ranks=None):
                 bufs.append((q, buf))
                 ops.append(dist.P2POp(dist.irecv, buf, ranks[r]))
         if ops:
-            for req in dist.batch_isend_irecv(ops):
-                req.wait()
+            _wait_all(dist.batch_isend_irecv(ops), "stem gather", timeout)
         for q, buf in bufs:
             stems[:, q.t_lo:q.t_hi] = buf
     elif me.t_hi > me.t_lo:
         send = stems[:, me.t_lo:me.t_hi].contiguous()
-        for req in dist.batch_isend_irecv([dist.P2POp(dist.isend, send, ranks[0])]):
-            req.wait()
+        _wait_all(dist.batch_isend_irecv([dist.P2POp(dist.isend, send, ranks[0])]), "stem gather",
+                  timeout)
 
 
 # ---------------------------------------------------------------------------
@@ -225,14 +250,12 @@ def bag_gather(dist, rank: int, assign: BagAssignment, stems_by_net: dict, weigh
                 recvs.append((k, s, buf))
                 ops.append(dist.P2POp(dist.irecv, buf, assign.owner[k]))
         if ops:
-            for work in dist.batch_isend_irecv(ops):
-                work.wait()
+            _wait_all(dist.batch_isend_irecv(ops), "bag lane gather")
         for k, s, buf in recvs:
             outs[k][s] = buf
         return combine(outs, weights, requested)
     ops = [dist.P2POp(dist.isend, stems_by_net[k][s].contiguous(), 0)
            for k, s in lanes if assign.owner[k] == rank]
     if ops:
-        for work in dist.batch_isend_irecv(ops):
-            work.wait()
+        _wait_all(dist.batch_isend_irecv(ops), "bag lane gather")
     return None

@@ -121,3 +121,46 @@ def test_plan_partitions_every_chunk_once():
         for a, b in zip(p.ranks, p.ranks[1:]):
             assert a.t_hi == b.t_lo and a.own_hi == b.own_lo
             assert a.send_hi - a.send_lo <= p.segment - p.stride
+
+
+def _fault_worker(rank, world, port, store_port, out_path):
+    # rank 0 "dies" between steps: it skips the boundary exchange, so rank 1's
+    # receive never completes and its bounded wait must end in ShardTimeout
+    import datetime
+    import sys
+
+    import torch.distributed as dist
+
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    sys.path[:0] = [os.path.join(root, "demucs-wgpu_b200")]
+    import shard
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    store = dist.TCPStore("127.0.0.1", store_port, world, rank == 0,
+                          timeout=datetime.timedelta(seconds=60))
+    dist.init_process_group("gloo", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=60))
+    p = shard.plan(SEG * 7 + 123, world, shifts=1, overlap=0.25, segment=SEG)
+    acc = torch.zeros((8, p.view_length), dtype=torch.float32)
+    if rank == 1:
+        try:
+            shard.exchange_tails(dist, p, rank, acc, timeout=2.0)
+            result = "completed"
+        except shard.ShardTimeout as exc:
+            result = f"timeout {exc.code}"
+        with open(out_path, "w") as f:
+            f.write(result)
+        store.set("rank1_done", "1")
+    else:
+        store.wait(["rank1_done"], datetime.timedelta(seconds=60))
+    # the unmatched receive is still posted on rank 1: leave without a collective
+    os._exit(0)
+
+
+def test_missing_boundary_send_ends_in_a_bounded_timeout(tmp_path):
+    out_path = str(tmp_path / "fault.txt")
+    mp.start_processes(_fault_worker, args=(2, _free_port(), _free_port(), out_path), nprocs=2,
+                       join=True,
+                       start_method="spawn")
+    assert open(out_path).read() == "timeout 4"
