@@ -45,7 +45,8 @@ struct Error : std::runtime_error {
 // ---------------------------------------------------------------------------
 struct HostTensor {
   std::vector<int64_t> shape;
-  const float* data = nullptr;
+  const float* data = nullptr;                  // into the blob (F32) or into `owned`
+  std::shared_ptr<std::vector<float>> owned;  // the f32 copy of a tensor stored in another dtype
   size_t count() const {
     size_t n = 1;
     for (int64_t s : shape) n *= (size_t)s;
@@ -106,6 +107,72 @@ struct Json {
   }
 };
 
+// IEEE 754 binary16 -> binary32 (subnormals, infinities and NaN included):
+// value = (-1)^s * 2^(e-15) * (1 + m/1024), or 2^-14 * m/1024 when e == 0.
+float half_bits_to_float(uint16_t h) {
+  const uint32_t sign = (uint32_t)(h >> 15) << 31;
+  const uint32_t e = (h >> 10) & 0x1f, m = h & 0x3ff;
+  uint32_t bits;
+  if (e == 0x1f) {
+    bits = sign | 0x7f800000u | (m << 13);  // infinity, or NaN with its payload
+  } else if (e != 0) {
+    bits = sign | ((e + 112u) << 23) | (m << 13);  // rebias 15 -> 127
+  } else {
+    float v = (float)m * (1.0f / 16777216.0f);  // m * 2^-24, exact in f32
+    std::memcpy(&bits, &v, 4);
+    bits |= sign;
+  }
+  float f;
+  std::memcpy(&f, &bits, 4);
+  return f;
+}
+
+// Element width of a safetensors dtype this loader reads, 0 if unsupported
+// (safetensors.rs:110-135 reads the same set).
+int dtype_width(const std::string& d) {
+  if (d == "F32" || d == "I32") return 4;
+  if (d == "F64" || d == "I64") return 8;
+  if (d == "F16" || d == "BF16" || d == "I16") return 2;
+  if (d == "U8" || d == "I8" || d == "BOOL") return 1;
+  return 0;
+}
+
+// Upcasts one non-F32 tensor to f32 (safetensors.rs:110-135).
+std::vector<float> decode_tensor(const char* raw, size_t n, const std::string& d) {
+  std::vector<float> v(n);
+  for (size_t i = 0; i < n; ++i) {
+    if (d == "F16" || d == "BF16" || d == "I16") {
+      uint16_t u;
+      std::memcpy(&u, raw + 2 * i, 2);
+      if (d == "F16") {
+        v[i] = half_bits_to_float(u);
+      } else if (d == "BF16") {
+        const uint32_t b = (uint32_t)u << 16;
+        std::memcpy(&v[i], &b, 4);
+      } else {
+        v[i] = (float)(int16_t)u;
+      }
+    } else if (d == "F64") {
+      double x;
+      std::memcpy(&x, raw + 8 * i, 8);
+      v[i] = (float)x;
+    } else if (d == "I64") {
+      int64_t x;
+      std::memcpy(&x, raw + 8 * i, 8);
+      v[i] = (float)x;
+    } else if (d == "I32") {
+      int32_t x;
+      std::memcpy(&x, raw + 4 * i, 4);
+      v[i] = (float)x;
+    } else if (d == "I8") {
+      v[i] = (float)(int8_t)raw[i];
+    } else {  // U8, BOOL
+      v[i] = (float)(uint8_t)raw[i];
+    }
+  }
+  return v;
+}
+
 std::map<std::string, HostTensor> parse_safetensors(const void* blob, size_t len) {
   if (len < 8) throw Error(DMX_ERR_WEIGHTS, "safetensors blob shorter than its header size");
   uint64_t n;
@@ -151,12 +218,18 @@ std::map<std::string, HostTensor> parse_safetensors(const void* blob, size_t len
         j.expect('}');
         break;
       }
-      if (dtype != "F32") throw Error(DMX_ERR_WEIGHTS, name + ": dtype " + dtype + " is not F32");
-      if (b < a || b > data_len || b - a != t.count() * 4)
+      const int width = dtype_width(dtype);
+      if (width == 0) throw Error(DMX_ERR_WEIGHTS, name + ": unsupported safetensors dtype " + dtype);
+      if (b < a || b > data_len || b - a != t.count() * (size_t)width)
         throw Error(DMX_ERR_WEIGHTS, name + ": data_offsets do not match the shape");
-      if ((reinterpret_cast<uintptr_t>(base + a) & 3) != 0)
-        throw Error(DMX_ERR_WEIGHTS, name + ": tensor data is not 4-byte aligned");
-      t.data = reinterpret_cast<const float*>(base + a);
+      if (dtype == "F32" && (reinterpret_cast<uintptr_t>(base + a) & 3) == 0) {
+        t.data = reinterpret_cast<const float*>(base + a);
+      } else {  // other dtypes (F16 in the published checkpoints), or unaligned F32: an f32 copy
+        t.owned = std::make_shared<std::vector<float>>(
+            dtype == "F32" ? std::vector<float>(t.count()) : decode_tensor(base + a, t.count(), dtype));
+        if (dtype == "F32") std::memcpy(t.owned->data(), base + a, t.count() * 4);
+        t.data = t.owned->data();
+      }
       out[name] = t;
     }
     if (j.peek(',')) { j.expect(','); continue; }
@@ -490,6 +563,8 @@ struct dmx_handle {
   int64_t tc_launches = 0;
   float* bag_out = nullptr;  // this network's own forward output when it runs inside a bag
   int64_t bag_cap = 0;       // segments bag_out holds
+  cudaStream_t copy_stream = nullptr;  // device-to-host copies that overlap the forwards
+  cudaEvent_t copy_ev = nullptr;
   char* batch_ws = nullptr;  // per-track slots of dmx_separate_batch_device
   size_t batch_cap = 0;
   float* batch_io = nullptr;  // device staging of dmx_separate_batch's host tracks and stems
@@ -1694,11 +1769,11 @@ dmx_status dmx_create(const dmx_config* cfg, const void* blob, size_t len, int d
       throw Error(DMX_ERR_INVALID, "max_batch must be in [1, 256]");
     h->cfg = *cfg;
     h->device = device;
+    const auto tensors = parse_safetensors(blob, len);  // validated before any CUDA call
     CK(cudaSetDevice(device));
     CK(cudaStreamCreateWithFlags(&h->stream, cudaStreamNonBlocking));
     CK(cudaMalloc(&h->err, sizeof(int)));
     CK(cudaMemset(h->err, 0, sizeof(int)));
-    const auto tensors = parse_safetensors(blob, len);
     load_model(h.get(), tensors);
     const char* st = getenv("DMX_STAGE_TIMING");
     h->stage_timing = st && st[0] == '1';
@@ -1725,6 +1800,9 @@ void dmx_destroy(dmx_handle* h) {
   cudaFree(h->host_io);
   cudaFree(h->norm_scratch);
   cudaFree(h->bag_out);
+  if (h->copy_stream) cudaStreamSynchronize(h->copy_stream);
+  if (h->copy_ev) cudaEventDestroy(h->copy_ev);
+  if (h->copy_stream) cudaStreamDestroy(h->copy_stream);
   cudaFree(h->batch_ws);
   cudaFree(h->batch_io);
   cudaFreeHost(h->pinned_in);
@@ -2038,13 +2116,23 @@ void shard_chunks(dmx_handle* h, BagPlan* bag, const float* mix_norm_dev, int64_
   }
 }
 
+// Pinned host stems that a single-pass separation fills while it runs: after
+// each forward batch the output samples that no later chunk touches are
+// finished and copied on the handle's copy stream, so the device-to-host
+// copy overlaps the remaining forwards (the reference emits frames the same
+// way as soon as they are final: streaming.rs:219-260).
+struct HostSink {
+  float* host = nullptr;  // (8, n) pinned host stems
+};
+
 // Demucs::separate's device driver for one track (api.rs:438-545, 697-785;
 // pipeline.rs:380-515; streaming.rs:52-400) over one network or, with `bag`,
 // over the bag's lockstep combination; `h` is the network (the bag's lead)
-// whose stream, track workspace and OLA weights the driver uses.
+// whose stream, track workspace and OLA weights the driver uses. With `sink`
+// (single pass only) the stems are also copied to the host as they finish.
 void separate_track_impl(dmx_handle* h, BagPlan* bag, const float* lr_dev, int64_t n,
                          const dmx_separate_opts* opts, float* d_stems, dmx_progress_fn progress,
-                         void* user) {
+                         void* user, const HostSink* sink = nullptr) {
   dmx_separate_opts o{1, 0.25, 1.0, 0};
   if (opts) o = *opts;
   if (o.transition_power != 1.0) throw Error(DMX_ERR_INVALID, "transition_power must be 1");
@@ -2098,21 +2186,45 @@ void separate_track_impl(dmx_handle* h, BagPlan* bag, const float* lr_dev, int64
   const int batch = std::max(1, o.batch > 0 ? std::min(o.batch, max_batch) : max_batch);
   // progress counts every running network's chunks (api.rs:764-776)
   const size_t active = bag ? bag->nets.size() : 1;
+  const bool stream_out = sink && sink->host && passes == 1;
+  if (stream_out && !h->copy_stream) {
+    CK(cudaStreamCreateWithFlags(&h->copy_stream, cudaStreamNonBlocking));
+    CK(cudaEventCreateWithFlags(&h->copy_ev, cudaEventDisableTiming));
+  }
   for (int pass = 0; pass < passes; ++pass) {
     const int64_t offset = offsets[pass];
     const int64_t vlen = o.shifts > 0 ? n + max_shift - offset : n;
     const int64_t chunks = dmx_num_chunks(vlen, seg, o.overlap);
+    const int mode = o.shifts == 0 ? 0 : (o.shifts == 1 ? 1 : 2);
+    const int64_t trim = o.shifts > 0 ? max_shift - offset : 0;
+    int64_t t_done = 0;  // output samples already finished (and copied) by the sink
     CK(cudaMemsetAsync(d_acc, 0, 8 * vlen * sizeof(float), h->stream));
     for (int64_t c0 = 0; c0 < chunks; c0 += batch) {
       const int64_t c1 = std::min<int64_t>(chunks, c0 + batch);
       shard_chunks(h, bag, d_mix, n, offset, max_shift, seg, stride, c0, c1, batch, d_acc, 0, vlen);
+      if (stream_out) {
+        // view samples below chunk c1's start get no further contribution
+        const int64_t t_hi = c1 == chunks ? n : std::min<int64_t>(n, std::max<int64_t>(0, c1 * stride - trim));
+        if (t_hi > t_done) {
+          h->mark("track.finish");
+          ++h->launches;
+          launch_ola_finish(d_acc, n, offset, max_shift, seg, stride, h->W(h->m.ola_w.off), d_norm,
+                            scale, mode, d_pass, d_stems, h->stream, t_done, t_hi);
+          CK(cudaEventRecord(h->copy_ev, h->stream));
+          CK(cudaStreamWaitEvent(h->copy_stream, h->copy_ev, 0));
+          CK(cudaMemcpy2DAsync(sink->host + t_done, (size_t)n * sizeof(float), d_stems + t_done,
+                               (size_t)n * sizeof(float), (size_t)(t_hi - t_done) * sizeof(float),
+                               8, cudaMemcpyDeviceToHost, h->copy_stream));
+          t_done = t_hi;
+        }
+      }
       done += (size_t)(c1 - c0);
       if (progress) {
         CK(cudaStreamSynchronize(h->stream));
         progress(done * active, total * active, user);
       }
     }
-    const int mode = o.shifts == 0 ? 0 : (o.shifts == 1 ? 1 : 2);
+    if (stream_out) continue;
     h->mark("track.finish");
     ++h->launches;
     launch_ola_finish(d_acc, n, offset, max_shift, seg, stride, h->W(h->m.ola_w.off), d_norm, scale,
@@ -2144,8 +2256,28 @@ void separate_track_host(dmx_handle* h, BagPlan* bag, const float* left, const f
   float* d_stems = h->host_io + 2 * n;
   CK(cudaMemcpyAsync(d_lr, left, n * sizeof(float), cudaMemcpyHostToDevice, h->stream));
   CK(cudaMemcpyAsync(d_lr + n, right, n * sizeof(float), cudaMemcpyHostToDevice, h->stream));
-  separate_track_impl(h, bag, d_lr, n, opts, d_stems, progress, user);
-  CK(cudaMemcpyAsync(stems_out, d_stems, 8 * n * sizeof(float), cudaMemcpyDeviceToHost, h->stream));
+  // pinned stems are copied while the forwards run; pageable ones once at the end (a copy
+  // to pageable memory would block this thread before the next forward is enqueued)
+  cudaPointerAttributes attr{};
+  const bool pinned = cudaPointerGetAttributes(&attr, stems_out) == cudaSuccess &&
+                      attr.type == cudaMemoryTypeHost;
+  cudaGetLastError();  // a pageable pointer may leave an error behind on some drivers
+  const int shifts = opts ? opts->shifts : 1;
+  HostSink sink;
+  sink.host = stems_out;
+  const bool streamed = pinned && shifts <= 1;
+  try {
+    separate_track_impl(h, bag, d_lr, n, opts, d_stems, progress, user, streamed ? &sink : nullptr);
+  } catch (...) {
+    if (h->copy_stream) cudaStreamSynchronize(h->copy_stream);  // no copy outlives the call
+    throw;
+  }
+  if (streamed) {
+    CK(cudaStreamSynchronize(h->copy_stream));
+  } else {
+    CK(cudaMemcpyAsync(stems_out, d_stems, 8 * n * sizeof(float), cudaMemcpyDeviceToHost,
+                       h->stream));
+  }
   CK(cudaStreamSynchronize(h->stream));
   check_device_flag(h);
   if (bag)

@@ -259,3 +259,34 @@ def bag_gather(dist, rank: int, assign: BagAssignment, stems_by_net: dict, weigh
     if ops:
         _wait_all(dist.batch_isend_irecv(ops), "bag lane gather")
     return None
+
+
+# ---------------------------------------------------------------------------
+# Many tracks (the throughput batch) over ranks
+# ---------------------------------------------------------------------------
+
+def track_units(length: int, shifts: int, overlap: float = 0.25, segment: int = SEGMENT,
+                samplerate: int = SR) -> int:
+    """Forward units (chunks over all shift passes) of one track: one
+    split pass per shift, each of ceil(view / stride) chunks
+    (streaming.rs:88-94), the view lengthened by max_shift - offset."""
+    stride = int((1.0 - overlap) * segment)
+    if shifts == 0:
+        return -(-length // stride)
+    max_shift = int(0.5 * samplerate)
+    return sum(-(-(length + max_shift - o) // stride) for o in shift_offsets(shifts, max_shift))
+
+
+def assign_tracks(lengths, world: int, shifts: int, overlap: float = 0.25):
+    """Tracks are independent units: rank r gets a list of track indices so
+    that the forward units per rank are balanced (longest track first onto
+    the least-loaded rank; ties to the lower rank, so every rank computes the
+    same assignment). Each rank then runs dmx_separate_batch on its tracks."""
+    units = [track_units(n, shifts, overlap) for n in lengths]
+    load = [0] * world
+    out = [[] for _ in range(world)]
+    for i in sorted(range(len(lengths)), key=lambda i: (-units[i], i)):
+        r = min(range(world), key=lambda r: (load[r], r))
+        out[r].append(i)
+        load[r] += units[i]
+    return [sorted(x) for x in out]

@@ -157,15 +157,32 @@ def random_weights(seed: int = 0, layer_scale: float = 1e-4, norm_jitter: float 
     return out
 
 
-def write_safetensors(tensors, metadata=None) -> bytes:
-    """Serialise ``{name: f32 array}`` as a safetensors blob."""
+def _encode(value, dtype):
+    """Raw little-endian bytes of an f32 array stored as ``dtype``."""
+    if dtype == "F32":
+        return np.ascontiguousarray(value, dtype="<f4").tobytes()
+    if dtype == "F16":
+        return np.ascontiguousarray(value, dtype="<f2").tobytes()
+    if dtype == "BF16":  # round to nearest even on the upper 16 bits
+        u = np.ascontiguousarray(value, dtype=np.float32).view(np.uint32).astype(np.uint64)
+        u = (u + 0x7FFF + ((u >> 16) & 1)) >> 16
+        return u.astype("<u2").tobytes()
+    if dtype == "F64":
+        return np.ascontiguousarray(value, dtype="<f8").tobytes()
+    raise ValueError(dtype)
+
+
+def write_safetensors(tensors, metadata=None, dtype: str = "F32") -> bytes:
+    """Serialise ``{name: f32 array}`` as a safetensors blob, every tensor
+    stored as ``dtype`` (F32, F16 — the published checkpoints' format — BF16
+    or F64)."""
     header = OrderedDict()
     offset = 0
     chunks = []
     for name, value in tensors.items():
         value = np.ascontiguousarray(value, dtype=np.float32)
-        raw = value.tobytes()
-        header[name] = {"dtype": "F32", "shape": list(value.shape),
+        raw = _encode(value, dtype)
+        header[name] = {"dtype": dtype, "shape": list(value.shape),
                         "data_offsets": [offset, offset + len(raw)]}
         offset += len(raw)
         chunks.append(raw)

@@ -36,3 +36,29 @@ def test_chunk_plan_matches_the_reference_count():
     for length in (1, stride, stride + 1, 10_584_000, 10_584_000 + 22050):
         assert dmx.num_chunks(length) == -(-length // stride)
     assert dmx.num_chunks(0) == 0
+
+
+def test_weight_blob_dtypes_are_checked_before_the_device_is_touched():
+    # dmx_create parses and validates the safetensors blob (safetensors.rs:110-135 dtypes)
+    # before any CUDA call, so malformed blobs fail with DMX_ERR_WEIGHTS on any host
+    import json
+    import struct
+
+    import numpy as np
+    import pytest
+    import synth
+
+    def blob(header, data):
+        text = json.dumps(header).encode()
+        return struct.pack("<Q", len(text)) + text + data
+
+    bad_dtype = blob({"w": {"dtype": "F8_E4M3", "shape": [2], "data_offsets": [0, 2]}}, b"\0\0")
+    short_f16 = blob({"w": {"dtype": "F16", "shape": [4], "data_offsets": [0, 6]}}, b"\0" * 6)
+    for b, msg in ((bad_dtype, "unsupported safetensors dtype F8_E4M3"),
+                   (short_f16, "data_offsets do not match the shape")):
+        with pytest.raises(dmx.DmxError, match=msg) as e:
+            dmx.Handle(b, device=0, max_batch=1)
+        assert e.value.code == 2  # DMX_ERR_WEIGHTS
+    # a well-formed F16 blob gets past parsing (on a host without a GPU the next step fails)
+    w = {"x": np.array([1.0, -2.0, 0.5, 0.0], np.float32)}
+    assert synth.write_safetensors(w, dtype="F16")[8:].startswith(b'{"x":{"dtype":"F16"')

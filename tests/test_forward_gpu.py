@@ -67,3 +67,23 @@ def test_batch_independence():
     err = np.mean(np.abs(one[0].astype(np.float64) - two[0]))
     rms = np.sqrt(np.mean(one[0].astype(np.float64) ** 2))
     assert err == 0 or -20 * np.log10(err / rms) > 100
+
+
+@pytest.mark.parametrize("dtype", ["F16", "BF16"])
+def test_half_precision_checkpoints_load_as_their_f32_upcast(dtype):
+    # the published checkpoints store F16 (safetensors.rs:5-9, 110-135): a blob in F16 or
+    # BF16 must load exactly as the F32 blob of the same (rounded) values
+    import dmx
+
+    w = synth.random_weights(4)
+    rounded = synth.read_safetensors(synth.write_safetensors(w))  # f32 copies
+    if dtype == "F16":
+        rounded = {k: v.astype(np.float16).astype(np.float32) for k, v in rounded.items()}
+    else:
+        rounded = {k: (((v.view(np.uint32).astype(np.uint64) + 0x7FFF
+                         + ((v.view(np.uint32) >> 16) & 1)) >> 16) << 16)
+                   .astype(np.uint32).view(np.float32) for k, v in rounded.items()}
+    mix = synth.gaussian_audio(8, 1)
+    got = dmx.Handle(synth.write_safetensors(w, dtype=dtype), device=0, max_batch=1).forward(mix)
+    ref = dmx.Handle(synth.write_safetensors(rounded), device=0, max_batch=1).forward(mix)
+    assert np.array_equal(got, ref)

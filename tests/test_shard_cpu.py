@@ -164,3 +164,22 @@ def test_missing_boundary_send_ends_in_a_bounded_timeout(tmp_path):
                        join=True,
                        start_method="spawn")
     assert open(out_path).read() == "timeout 4"
+
+
+def test_track_assignment_balances_units_and_covers_every_track():
+    import shard
+
+    # 64 tracks of 180 s with shifts 2 (the throughput batch): 8 per GPU
+    lengths = [180 * 44100] * 64
+    per = shard.assign_tracks(lengths, 8, shifts=2)
+    assert sorted(i for r in per for i in r) == list(range(64))
+    assert [len(r) for r in per] == [8] * 8
+    units = shard.track_units(180 * 44100, 2)
+    assert units == 2 * 31  # 31 chunks per shift pass
+    # ragged lengths: no rank carries more than the lightest rank plus one longest track
+    rng = np.random.default_rng(3)
+    lengths = [int(x) for x in rng.integers(5 * 44100, 400 * 44100, size=37)]
+    per = shard.assign_tracks(lengths, 6, shifts=1)
+    loads = [sum(shard.track_units(lengths[i], 1) for i in r) for r in per]
+    assert sorted(i for r in per for i in r) == list(range(37))
+    assert max(loads) - min(loads) <= max(shard.track_units(n, 1) for n in lengths)

@@ -76,3 +76,25 @@ def test_normalize_track_matches_oracle_scan_norm():
     assert abs(got[1] - std.value) <= 1e-6 * std.value, (got, std.value)
     ref = (track - mean.value) / std.value
     np.testing.assert_allclose(norm.cpu().numpy(), ref, rtol=1e-6, atol=1e-7)
+
+
+@pytest.mark.parametrize("shifts,batch", [(0, 2), (1, 2), (1, 1), (2, 2)])
+def test_pinned_host_stems_stream_back_during_the_forwards(shifts, batch):
+    # with pinned host stems, dmx_separate_track finishes and copies each batch's final
+    # samples while later batches run; the result is the device entry point's
+    import torch
+
+    h = _handle(synth.random_weights(25))
+    track = synth.pink_noise(37, int(44100 * 20))
+    n = track.shape[1]
+    out = torch.full((4, 2, n), float("nan")).pin_memory()
+    got = h.separate_track(track[0], track[1], shifts=shifts, batch=batch, out=out.numpy())
+    lr = torch.from_numpy(track).cuda()
+    stems = torch.empty((4, 2, n), device="cuda")
+    torch.cuda.synchronize()
+    h.separate_track_device(lr.data_ptr(), n, stems.data_ptr(), shifts=shifts, batch=batch)
+    h.synchronize()
+    ref = stems.cpu().numpy()
+    assert np.isfinite(got).all()
+    err = np.abs(got.astype(np.float64) - ref).max()
+    assert err <= 1e-6, err
