@@ -60,10 +60,14 @@ def build(verbose: bool = False, ptxas_info: bool = False) -> str:
                 print(f"== {os.path.basename(futs[f])}\n{log}")
     objs = [os.path.join(BUILD, os.path.basename(s) + ".o") for s in sources]
     if jobs or not os.path.exists(LIB):
-        cmd = [NVCC, *ARCH, "-shared", "-o", LIB, *objs, "-lcudart"]
+        # link beside the library and rename over it, so a process that loads the
+        # library (or a copy of the tree taken meanwhile) never sees a partial file
+        tmp = LIB + f".tmp{os.getpid()}"
+        cmd = [NVCC, *ARCH, "-shared", "-o", tmp, *objs, "-lcudart"]
         if verbose:
             print(" ".join(cmd), flush=True)
         subprocess.run(cmd, check=True)
+        os.replace(tmp, LIB)
     return LIB
 
 

@@ -565,6 +565,9 @@ struct dmx_handle {
   int64_t bag_cap = 0;       // segments bag_out holds
   cudaStream_t copy_stream = nullptr;  // device-to-host copies that overlap the forwards
   cudaEvent_t copy_ev = nullptr;
+  float* emit_pin[2] = {nullptr, nullptr};  // pinned staging of dmx_separate_track_emit's blocks
+  cudaEvent_t emit_ev[2] = {nullptr, nullptr};
+  int64_t emit_cap = 0;                     // samples per staging block
   char* batch_ws = nullptr;  // per-track slots of dmx_separate_batch_device
   size_t batch_cap = 0;
   float* batch_io = nullptr;  // device staging of dmx_separate_batch's host tracks and stems
@@ -1802,6 +1805,10 @@ void dmx_destroy(dmx_handle* h) {
   cudaFree(h->bag_out);
   if (h->copy_stream) cudaStreamSynchronize(h->copy_stream);
   if (h->copy_ev) cudaEventDestroy(h->copy_ev);
+  for (int i = 0; i < 2; ++i) {
+    if (h->emit_ev[i]) cudaEventDestroy(h->emit_ev[i]);
+    cudaFreeHost(h->emit_pin[i]);
+  }
   if (h->copy_stream) cudaStreamDestroy(h->copy_stream);
   cudaFree(h->batch_ws);
   cudaFree(h->batch_io);
@@ -2122,7 +2129,39 @@ void shard_chunks(dmx_handle* h, BagPlan* bag, const float* mix_norm_dev, int64_
 // copy overlaps the remaining forwards (the reference emits frames the same
 // way as soon as they are final: streaming.rs:219-260).
 struct HostSink {
-  float* host = nullptr;  // (8, n) pinned host stems
+  float* host = nullptr;  // (8, n) pinned host stems, or
+  // blocks of finished stems handed to a callback through two pinned staging
+  // buffers: block k is copied while the host hands block k - 1 over and the
+  // device already runs the next forward
+  dmx_frames_fn emit = nullptr;
+  void* user = nullptr;
+  int64_t pending_t0 = 0, pending_count = 0;  // the block in flight (count 0: none)
+  int pending_slot = 0, next_slot = 0;
+
+  // Waits for the block in flight and hands it over.
+  void flush(dmx_handle* h) {
+    if (pending_count == 0) return;
+    CK(cudaEventSynchronize(h->emit_ev[pending_slot]));
+    emit(pending_t0, pending_count, h->emit_pin[pending_slot], user);
+    pending_count = 0;
+  }
+  // Samples [t0, t1) of d_stems (8, n) are final: copy them out as blocks.
+  void put(dmx_handle* h, const float* d_stems, int64_t n, int64_t t0, int64_t t1) {
+    for (int64_t a = t0; a < t1; a += h->emit_cap) {
+      const int64_t count = std::min<int64_t>(h->emit_cap, t1 - a);
+      const int slot = next_slot;
+      next_slot ^= 1;
+      // the slot's previous block was handed over before the block after it was queued
+      CK(cudaMemcpy2DAsync(h->emit_pin[slot], (size_t)count * sizeof(float), d_stems + a,
+                           (size_t)n * sizeof(float), (size_t)count * sizeof(float), 8,
+                           cudaMemcpyDeviceToHost, h->copy_stream));
+      CK(cudaEventRecord(h->emit_ev[slot], h->copy_stream));
+      flush(h);
+      pending_t0 = a;
+      pending_count = count;
+      pending_slot = slot;
+    }
+  }
 };
 
 // Demucs::separate's device driver for one track (api.rs:438-545, 697-785;
@@ -2186,8 +2225,8 @@ void separate_track_impl(dmx_handle* h, BagPlan* bag, const float* lr_dev, int64
   const int batch = std::max(1, o.batch > 0 ? std::min(o.batch, max_batch) : max_batch);
   // progress counts every running network's chunks (api.rs:764-776)
   const size_t active = bag ? bag->nets.size() : 1;
-  const bool stream_out = sink && sink->host && passes == 1;
-  if (stream_out && !h->copy_stream) {
+  const bool stream_out = sink && (sink->host || sink->emit) && passes == 1;
+  if (sink && !h->copy_stream) {
     CK(cudaStreamCreateWithFlags(&h->copy_stream, cudaStreamNonBlocking));
     CK(cudaEventCreateWithFlags(&h->copy_ev, cudaEventDisableTiming));
   }
@@ -2212,9 +2251,12 @@ void separate_track_impl(dmx_handle* h, BagPlan* bag, const float* lr_dev, int64
                             scale, mode, d_pass, d_stems, h->stream, t_done, t_hi);
           CK(cudaEventRecord(h->copy_ev, h->stream));
           CK(cudaStreamWaitEvent(h->copy_stream, h->copy_ev, 0));
-          CK(cudaMemcpy2DAsync(sink->host + t_done, (size_t)n * sizeof(float), d_stems + t_done,
-                               (size_t)n * sizeof(float), (size_t)(t_hi - t_done) * sizeof(float),
-                               8, cudaMemcpyDeviceToHost, h->copy_stream));
+          if (sink->host)
+            CK(cudaMemcpy2DAsync(sink->host + t_done, (size_t)n * sizeof(float), d_stems + t_done,
+                                 (size_t)n * sizeof(float), (size_t)(t_hi - t_done) * sizeof(float),
+                                 8, cudaMemcpyDeviceToHost, h->copy_stream));
+          else
+            const_cast<HostSink*>(sink)->put(h, d_stems, n, t_done, t_hi);
           t_done = t_hi;
         }
       }
@@ -2234,6 +2276,14 @@ void separate_track_impl(dmx_handle* h, BagPlan* bag, const float* lr_dev, int64
   if (o.shifts > 1)
     launch_ola_finish(d_acc, n, 0, max_shift, seg, stride, h->W(h->m.ola_w.off), d_norm, scale, 3,
                       d_pass, d_stems, h->stream);
+  if (sink && sink->emit) {
+    if (!stream_out) {  // several shift passes: every sample is final only now
+      CK(cudaEventRecord(h->copy_ev, h->stream));
+      CK(cudaStreamWaitEvent(h->copy_stream, h->copy_ev, 0));
+      const_cast<HostSink*>(sink)->put(h, d_stems, n, 0, n);
+    }
+    const_cast<HostSink*>(sink)->flush(h);
+  }
   h->mark("end");
   CK(cudaGetLastError());
 }
@@ -2659,6 +2709,64 @@ dmx_status dmx_separate_track(dmx_handle* h, const float* left, const float* rig
     if (!h || !left || !right || !stems_out || n <= 0)
       throw Error(DMX_ERR_INVALID, "dmx_separate_track: bad argument");
     separate_track_host(h, nullptr, left, right, n, opts, stems_out, progress, user);
+    return DMX_OK;
+  } catch (const Error& e) {
+    return fail(e);
+  } catch (const std::exception& e) {
+    return fail_std(e);
+  }
+}
+
+dmx_status dmx_separate_track_emit(dmx_handle* h, const float* left, const float* right, int64_t n,
+                                   const dmx_separate_opts* opts, dmx_frames_fn on_frames,
+                                   dmx_progress_fn progress, void* user) {
+  try {
+    if (!h || !left || !right || !on_frames || n <= 0)
+      throw Error(DMX_ERR_INVALID, "dmx_separate_track_emit: bad argument");
+    CK(cudaSetDevice(h->device));
+    dmx_separate_opts o{1, 0.25, 1.0, 0};
+    if (opts) o = *opts;
+    const int64_t stride = (int64_t)((1.0 - o.overlap) * (double)kSegment);
+    if (stride <= 0) throw Error(DMX_ERR_INVALID, "overlap leaves a zero stride");
+    const int batch = std::max(1, o.batch > 0 ? std::min(o.batch, h->cfg.max_batch) : h->cfg.max_batch);
+    // a block holds what one forward finishes: at most `batch` strides plus one segment
+    const int64_t cap = std::min<int64_t>(n, (int64_t)batch * stride + kSegment);
+    if (cap > h->emit_cap) {
+      for (int i = 0; i < 2; ++i) {
+        cudaFreeHost(h->emit_pin[i]);
+        h->emit_pin[i] = nullptr;
+      }
+      h->emit_cap = 0;
+      for (int i = 0; i < 2; ++i) {
+        CK(cudaMallocHost(&h->emit_pin[i], (size_t)8 * cap * sizeof(float)));
+        if (!h->emit_ev[i]) CK(cudaEventCreateWithFlags(&h->emit_ev[i], cudaEventDisableTiming));
+      }
+      h->emit_cap = cap;
+    }
+    const size_t need = (size_t)10 * n * sizeof(float);
+    if (need > h->host_io_cap) {
+      cudaFree(h->host_io);
+      h->host_io = nullptr;
+      h->host_io_cap = 0;
+      CK(cudaMalloc(&h->host_io, need));
+      h->host_io_cap = need;
+    }
+    float* d_lr = h->host_io;
+    float* d_stems = h->host_io + 2 * n;
+    CK(cudaMemcpyAsync(d_lr, left, n * sizeof(float), cudaMemcpyHostToDevice, h->stream));
+    CK(cudaMemcpyAsync(d_lr + n, right, n * sizeof(float), cudaMemcpyHostToDevice, h->stream));
+    HostSink sink;
+    sink.emit = on_frames;
+    sink.user = user;
+    try {
+      separate_track_impl(h, nullptr, d_lr, n, &o, d_stems, progress, user, &sink);
+    } catch (...) {
+      cudaStreamSynchronize(h->copy_stream);  // no copy into the staging outlives the call
+      throw;
+    }
+    CK(cudaStreamSynchronize(h->stream));
+    check_device_flag(h);
+    finish_stage_times(h);
     return DMX_OK;
   } catch (const Error& e) {
     return fail(e);

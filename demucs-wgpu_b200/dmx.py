@@ -24,6 +24,7 @@ EXPORTS = (
     "dmx_separate_track_device", "dmx_normalize_track_device", "dmx_normalize_track_noalloc",
     "dmx_bag_combine_device", "dmx_bag_forward_device", "dmx_separate_track_bag",
     "dmx_separate_track_bag_device", "dmx_separate_batch", "dmx_separate_batch_device",
+    "dmx_separate_track_emit",
     "dmx_num_chunks", "dmx_track_finish", "dmx_track_shard", "dmx_set_trace",
     "dmx_set_stage_timing", "dmx_stage_times", "dmx_kernel_launches", "dmx_stream",
     "dmx_synchronize",
@@ -33,6 +34,7 @@ _f32p = ctypes.POINTER(ctypes.c_float)
 _i64p = ctypes.POINTER(ctypes.c_int64)
 TRACE_FN = ctypes.CFUNCTYPE(None, ctypes.c_char_p, _f32p, _i64p, ctypes.c_int, ctypes.c_void_p)
 PROGRESS_FN = ctypes.CFUNCTYPE(None, ctypes.c_size_t, ctypes.c_size_t, ctypes.c_void_p)
+FRAMES_FN = ctypes.CFUNCTYPE(None, ctypes.c_int64, ctypes.c_int64, _f32p, ctypes.c_void_p)
 
 
 class Config(ctypes.Structure):
@@ -95,6 +97,9 @@ def lib():
                                                     ctypes.c_void_p, ctypes.c_int64,
                                                     ctypes.POINTER(SeparateOpts), ctypes.c_void_p,
                                                     PROGRESS_FN, ctypes.c_void_p]
+        L.dmx_separate_track_emit.argtypes = [ctypes.c_void_p, _f32p, _f32p, ctypes.c_int64,
+                                              ctypes.POINTER(SeparateOpts), FRAMES_FN,
+                                              PROGRESS_FN, ctypes.c_void_p]
         _f32pp = ctypes.POINTER(_f32p)
         L.dmx_separate_batch.argtypes = [ctypes.c_void_p, _f32pp, _f32pp, _i64p, ctypes.c_int,
                                          ctypes.POINTER(SeparateOpts), _f32pp, PROGRESS_FN,
@@ -205,6 +210,29 @@ class Handle:
         _check(lib().dmx_separate_track(self._h, _ptr(left), _ptr(right), n, ctypes.byref(opts),
                                         _ptr(stems), cb, None))
         return stems
+
+    def separate_track_emit(self, left, right, on_frames, shifts=1, overlap=0.25,
+                            transition_power=1.0, batch=0, progress=None):
+        """Demucs::separate_streaming: ``on_frames(t0, block)`` receives each
+        finished (8, count) block of denormalised stems in ascending order
+        (the block is copied out of the library's staging first)."""
+        left = np.ascontiguousarray(left, dtype=np.float32)
+        right = np.ascontiguousarray(right, dtype=np.float32)
+        error = []
+
+        def _frames(t0, count, block, _u):
+            try:
+                on_frames(t0, np.ctypeslib.as_array(block, shape=(8, count)).copy())
+            except Exception as exc:  # pragma: no cover - surfaced below
+                error.append(exc)
+
+        fcb = FRAMES_FN(_frames)
+        pcb = PROGRESS_FN(0) if progress is None else PROGRESS_FN(lambda d, t, _u: progress(d, t))
+        opts = SeparateOpts(shifts, overlap, transition_power, batch)
+        _check(lib().dmx_separate_track_emit(self._h, _ptr(left), _ptr(right), left.shape[0],
+                                             ctypes.byref(opts), fcb, pcb, None))
+        if error:
+            raise error[0]
 
     def separate_batch(self, tracks, shifts=1, overlap=0.25, transition_power=1.0, batch=0,
                        progress=None, outs=None):

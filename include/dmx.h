@@ -57,8 +57,10 @@ void dmx_default_config(dmx_config* cfg);
 
 /* Demucs::load / GpuHtdemucsRunner::with_selector + GpuWeights::load
  * (api.rs:394-420, gpu/htdemucs.rs:536-660, 2377-2388): parse a safetensors
- * blob holding the PyTorch-named F32 tensors (weights.rs:211-578), repack and
- * upload them once to `device`. */
+ * blob holding the PyTorch-named tensors (weights.rs:211-578) — F32, or F16
+ * (the published checkpoints), BF16, F64 and integer types upcast to f32 as
+ * safetensors.rs:110-135 does — repack and upload them once to `device`. The
+ * blob is validated (DMX_ERR_WEIGHTS) before any CUDA call. */
 dmx_status dmx_create(const dmx_config* cfg, const void* safetensors_blob, size_t blob_len,
                       int device, dmx_handle** out);
 void dmx_destroy(dmx_handle* h);
@@ -98,6 +100,25 @@ typedef void (*dmx_progress_fn)(size_t done, size_t total, void* user);
 dmx_status dmx_separate_track(dmx_handle* h, const float* left, const float* right, int64_t n,
                               const dmx_separate_opts* opts, float* stems_out,
                               dmx_progress_fn progress, void* user);
+
+/* A block of finished stems for dmx_separate_track_emit: output samples
+ * [t0, t0 + count) of the track, `block` is (8, count) row-major — rows
+ * drums L, drums R, bass L, bass R, other L, other R, vocals L, vocals R —
+ * denormalised, valid only during the call. */
+typedef void (*dmx_frames_fn)(int64_t t0, int64_t count, const float* block, void* user);
+
+/* Demucs::separate_streaming (api.rs:600-650 over separate_forwarding_emit,
+ * pipeline.rs:380-515, and the OLA ring's in-order emission, streaming.rs:
+ * 96-261): the dmx_separate_track driver, but the stems are handed to
+ * `on_frames` in ascending blocks as soon as no later chunk can change them
+ * (after every forward of opts->batch chunks for shifts 0 or 1; after the
+ * last pass for shifts > 1), so host memory holds two blocks of at most
+ * opts->batch strides each instead of the whole (4, 2, n) result. Blocks are
+ * copied on a side stream and handed over while the next forward runs.
+ * `progress` and `on_frames` receive the same `user`. */
+dmx_status dmx_separate_track_emit(dmx_handle* h, const float* left, const float* right, int64_t n,
+                                   const dmx_separate_opts* opts, dmx_frames_fn on_frames,
+                                   dmx_progress_fn progress, void* user);
 
 /* dmx_separate_track on device buffers of the handle's GPU: lr_dev holds the
  * raw (2, n) stereo track, stems_dev receives (4, 2, n). Enqueued on the

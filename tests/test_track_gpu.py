@@ -98,3 +98,28 @@ def test_pinned_host_stems_stream_back_during_the_forwards(shifts, batch):
     assert np.isfinite(got).all()
     err = np.abs(got.astype(np.float64) - ref).max()
     assert err <= 1e-6, err
+
+
+@pytest.mark.parametrize("shifts,batch", [(0, 2), (1, 1), (2, 2)])
+def test_emitted_blocks_reassemble_the_separated_track(shifts, batch):
+    # Demucs::separate_streaming: ascending blocks of finished stems, each at most one
+    # forward's worth (single pass), that put together are dmx_separate_track's result
+    h = _handle(synth.random_weights(26))
+    track = synth.pink_noise(38, int(44100 * 21))
+    n = track.shape[1]
+    blocks = []
+    h.separate_track_emit(track[0], track[1], lambda t0, b: blocks.append((t0, b)),
+                          shifts=shifts, batch=batch)
+    ref = h.separate_track(track[0], track[1], shifts=shifts, batch=batch)
+    assert [t0 for t0, _ in blocks] == sorted(t0 for t0, _ in blocks)
+    assert blocks[0][0] == 0 and blocks[-1][0] + blocks[-1][1].shape[1] == n
+    for (t0, b), (t1, _) in zip(blocks, blocks[1:]):
+        assert t0 + b.shape[1] == t1
+    if shifts <= 1:
+        assert len(blocks) > 1
+        assert max(b.shape[1] for _, b in blocks) <= batch * int(0.75 * synth.SEGMENT_SAMPLES)
+    got = np.concatenate([b for _, b in blocks], axis=1).reshape(4, 2, n)
+    # two runs of the forward may differ in the last bits (f64 atomics in the
+    # spectrogram moments), as in the other driver comparisons
+    err = np.abs(got.astype(np.float64) - ref).max()
+    assert err <= 1e-6, err
