@@ -72,6 +72,12 @@ struct ConvParams {
   // for positions 4x, 4x+1, ...; columns of positions >= o_lim are not stored
   int o_lim, o_lim_ch;
   int a_rounded;  // tensor-core path: A already holds tf32-rounded values (no converter pass)
+  // tensor-core path, EPI_STORE / EPI_GELU: o_pcols > 0 splits the columns into
+  // groups of o_pcols (a multiple of 16) stored o_pstride elements apart —
+  // column g * o_pcols + c goes to element row + g * o_pstride + c (the four
+  // output phases of a stride-4 ConvTranspose landing on rows 4 f + phase)
+  int o_pcols;
+  int64_t o_pstride;
 };
 
 void launch_conv_gemm(const ConvParams& p, int pro, int epi, cudaStream_t stream);

@@ -291,15 +291,8 @@ struct WeightBuilder {
   }
 };
 
-struct DConvW {
-  Packed conv1, conv2;  // conv1: 3 taps C -> C/8; conv2: 1x1 C/8 -> 2C (GLU interleaved)
-  Vec n1w, n1b, n2w, n2b, gamma;
-  int C = 0, hidden = 0;
-};
-
 struct EncW {
   Packed conv, rewrite;
-  DConvW dconv;
   int cin = 0, cout = 0;
 };
 
@@ -307,7 +300,6 @@ struct DecW {
   Packed rewrite;
   Packed convt[4];  // per output phase
   Packed convt_all;  // the four phases side by side (see Loader::convt_all)
-  DConvW dconv;
   int cin = 0, cout = 0;
 };
 
@@ -474,26 +466,7 @@ struct Loader {
                 {{0, 0}});
   }
 
-  DConvW dconv(const std::string& prefix, int C, bool freq) {
-    DConvW d;
-    d.C = C;
-    d.hidden = C / 8;
-    (void)freq;
-    return d;
-  }
 };
-
-std::vector<std::pair<int, int>> kidx_line(int k, bool along_h) {
-  std::vector<std::pair<int, int>> v;
-  for (int i = 0; i < k; ++i) v.push_back(along_h ? std::make_pair(i, 0) : std::make_pair(0, i));
-  return v;
-}
-
-void load_dconv(Loader& L, const std::string& prefix, int C, DConvW* out, int d_unused = 0) {
-  (void)d_unused;
-  out->C = C;
-  out->hidden = C / 8;
-}
 
 struct DConvLayerW {
   Packed conv1, conv2;
@@ -635,6 +608,34 @@ struct dmx_handle {
     launch_conv_gemm(p, pro, epi, stream);
   }
 
+  // The tensor-core path alone, for launches the SIMT kernel cannot express
+  // (split output columns): false, with nothing launched, when the
+  // tensor-core kernel does not take it; the caller then issues another form.
+  bool gemm_tc(const ConvParams& p, int epi, const char* tag, const Packed& pk) {
+    if (cfg.precision != DMX_TF32 && cfg.precision != DMX_TF32X3) return false;
+    if (epi != EPI_STORE && epi != EPI_GELU) return false;
+    if (p.o_pcols % 16 != 0 || p.o_lim != 0 || p.vt_out) return false;
+    if (!live()) {
+      ++launches;
+      return true;
+    }
+    TcOperandA a;
+    TcParams t;
+    if (!build_tc(p, pk, a, t)) return false;
+    ++launches;
+    if (stage_timing) {
+      const double M = (double)p.B * p.Hq * p.Wq;
+      const double K = (double)p.ntaps * pk.cin_real;
+      double bytes = 4.0 * ((double)p.B * p.Hin * p.Win * pk.cin_real + K * p.N) + 4.0 * M * p.N;
+      if (p.epi_add) bytes += 4.0 * M * p.N;
+      mark(tag, 2.0 * M * K * p.N * pk.flop_scale, bytes);
+    }
+    launch_tc_gemm(a, wdev + pk.tc_off, cfg.precision == DMX_TF32X3 ? wdev + pk.tc_lo_off : nullptr,
+                   t, epi, stream);
+    ++tc_launches;
+    return true;
+  }
+
   // The tensor-core path takes a launch when its A operand is a plain
   // channels-last tile read (no prologue transform) with stride-1 taps (or
   // the strided encoder taps).
@@ -720,6 +721,8 @@ struct dmx_handle {
     t.o_lim = p.o_lim;
     t.o_lim_ch = p.o_lim_ch;
     t.a_rounded = p.a_rounded;
+    t.o_pcols = p.o_pcols;
+    t.o_pstride = p.o_pstride;
     t.err = err;
     return tc_gemm_supported(a, t);
   }
@@ -1295,7 +1298,31 @@ void forward(dmx_handle* h, const float* mix, int G, float* out) {
         p.a_rounded = xf_rounded(h);  // the DConv output, rounded
         h->gemm(p, PRO_NONE, EPI_STORE, ("dec.convtr" + std::to_string(e)).c_str(), &Dw.convt_all);
       } else {
-        for (int ph = 0; ph < 4; ++ph) {
+        // tensor-core builds: all four phases in one GEMM over the input rows
+        // (the input read once, not once per phase); output columns
+        // phase * Co + c go to row f = 4 f_in + phase of (b, f, t, c)
+        ConvParams p = base_params(Dw.convt_all, h->wdev);
+        set_input(p, g, G, F, kFrames, C);
+        p.B = G;
+        p.Hq = F;
+        p.Wq = kFrames;
+        p.out = o;
+        p.o_bs = (int64_t)Fo * kFrames * Co;
+        p.o_xs = Co;
+        p.o_ys = 4LL * kFrames * Co;
+        p.o_off = 0;
+        p.o_pcols = Co;
+        p.o_pstride = (int64_t)kFrames * Co;
+        p.epi_add = skip[j - 1];
+        p.a_rounded = xf_rounded(h);  // the DConv output, rounded
+        p.round_out = xf_rounded(h);  // feeds only the next decoder's rewrite
+        // Only the narrowest of these layers (Cin 96, the largest output) gains: measured on
+        // B200, dec.convtr2 1.96 -> 1.19 ms per 42 segments, while at Cin 192 the combined
+        // form's zero taps (1.5x the tensor work) made dec.convtr1 slower (0.78 -> 0.96 ms).
+        const bool combined =
+            C <= 96 &&
+            h->gemm_tc(p, EPI_GELU, ("dec.convtr" + std::to_string(e)).c_str(), Dw.convt_all);
+        for (int ph = 0; ph < 4 && !combined; ++ph) {
           // (b, f, t, c) with f = 4 f_in + phase
           ConvParams p = base_params(Dw.convt[ph], h->wdev);
           set_input(p, g, G, F, kFrames, C);
@@ -1601,9 +1628,10 @@ void load_model(dmx_handle* h, const std::map<std::string, HostTensor>& t) {
         t9.push_back({ky - 1, kx - 1});
       }
     m.dec[e].rewrite = L.conv(d + ".rewrite", {2 * cin, cin, 3, 3}, k9, t9, true);
-    if (e == 3)  // the last one writes the frame-major spectrogram: phases contiguous
-      m.dec[e].convt_all = L.convt_all(d + ".conv_tr", {cin, cout_f, 8, 1});
-    else
+    // all four phases in one GEMM: the last decoder writes the frame-major
+    // spectrogram (phases contiguous), the others split the columns per phase
+    m.dec[e].convt_all = L.convt_all(d + ".conv_tr", {cin, cout_f, 8, 1});
+    if (e != 3)  // per-phase GEMMs: the FP32 (SIMT) build
       for (int ph = 0; ph < 4; ++ph)
         m.dec[e].convt[ph] = L.convt(d + ".conv_tr", {cin, cout_f, 8, 1}, ph);
     m.dec[e].cin = cin;

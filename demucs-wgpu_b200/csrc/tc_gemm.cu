@@ -317,7 +317,56 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int j = 0; j < 32; ++j)
               if (nb + j < ncol) v[j] += p.bias[nb + j];
           }
-          if (EPI == EPI_STORE || EPI == EPI_GELU || EPI == EPI_STORE_STATS) {
+          if ((EPI == EPI_STORE || EPI == EPI_GELU) && p.o_pcols) {
+            // split columns: each 16-column half lies in one group of o_pcols
+            // (a multiple of 16) and goes to row orow + group * o_pstride
+            if (EPI == EPI_GELU) {
+#pragma unroll
+              for (int j = 0; j < 32; ++j) v[j] = gelu(v[j]);
+            }
+#pragma unroll
+            for (int hf = 0; hf < 2; ++hf) {
+              const int n = nb + 16 * hf;
+              if (n < ncol) {
+                const int grp = n / p.o_pcols;
+                const int64_t at = orow + (int64_t)grp * p.o_pstride + (n - grp * p.o_pcols);
+                const bool v4 = n + 16 <= ncol && (at & 3) == 0;
+                if (p.epi_add) {
+                  const float* ad = p.epi_add + at;
+                  if (v4) {
+#pragma unroll
+                    for (int j = 0; j < 16; j += 4) {
+                      const float4 t4 = *reinterpret_cast<const float4*>(ad + j);
+                      v[16 * hf + j] += t4.x;
+                      v[16 * hf + j + 1] += t4.y;
+                      v[16 * hf + j + 2] += t4.z;
+                      v[16 * hf + j + 3] += t4.w;
+                    }
+                  } else {
+#pragma unroll
+                    for (int j = 0; j < 16; ++j)
+                      if (n + j < ncol) v[16 * hf + j] += ad[j];
+                  }
+                }
+                if (p.round_out) {
+#pragma unroll
+                  for (int j = 0; j < 16; ++j) v[16 * hf + j] = round_tf32(v[16 * hf + j]);
+                }
+                float* o = p.out + at;
+                if (v4) {
+#pragma unroll
+                  for (int j = 0; j < 16; j += 4)
+                    *reinterpret_cast<float4*>(o + j) =
+                        make_float4(v[16 * hf + j], v[16 * hf + j + 1], v[16 * hf + j + 2],
+                                    v[16 * hf + j + 3]);
+                } else {
+#pragma unroll
+                  for (int j = 0; j < 16; ++j)
+                    if (n + j < ncol) o[j] = v[16 * hf + j];
+                }
+              }
+            }
+          } else if (EPI == EPI_STORE || EPI == EPI_GELU || EPI == EPI_STORE_STATS) {
             if (EPI == EPI_GELU) {
 #pragma unroll
               for (int j = 0; j < 32; ++j) v[j] = gelu(v[j]);

@@ -47,6 +47,8 @@ struct TcParams {
   int vt_col0, vt_ntok;
   int o_lim, o_lim_ch;  // as in ConvParams
   int a_rounded;  // A holds tf32-rounded values: the MMA reads the TMA tile as landed
+  int o_pcols;          // as in ConvParams: column groups stored o_pstride apart (0 = off)
+  int64_t o_pstride;
   // EPI_DCONV_TAIL: row moments of the GLU input (sum, sum of squares per
   // row of epi_rowlen positions, count values each), GroupNorm weight/bias in
   // the reference's order (value c, gate c + epi_half)
