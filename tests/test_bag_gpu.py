@@ -115,3 +115,22 @@ def test_bag_forward_device_is_the_lockstep_segment_forward():
     ref = oracle.bag_forward([h.forward for h in hs], w)(mix)
     err = np.abs(out.cpu().numpy().astype(np.float64) - ref).max()
     assert err <= 1e-6, err
+
+
+def test_bag_device_entry_point_matches_host_entry_point():
+    import torch
+    import dmx
+
+    hs = _handles([61, 62], max_batch=2)
+    w = np.array([[1.0, 1.0, 0.0, 0.0], [0.0, 0.0, 1.0, 1.0]], dtype=np.float32)
+    bag = dmx.Bag(hs, w)
+    track = synth.pink_noise(39, int(44100 * 12))
+    n = track.shape[1]
+    ref = bag.separate_track(track[0], track[1], shifts=1, batch=2)
+    lr = torch.from_numpy(track).cuda()
+    stems = torch.full((4, 2, n), float("nan"), device="cuda")
+    torch.cuda.synchronize()
+    bag.separate_track_device(lr.data_ptr(), n, stems.data_ptr(), shifts=1, batch=2)
+    hs[0].synchronize()
+    err = np.abs(stems.cpu().numpy().astype(np.float64) - ref).max()
+    assert err <= 1e-6, err

@@ -123,3 +123,39 @@ def test_emitted_blocks_reassemble_the_separated_track(shifts, batch):
     # spectrogram moments), as in the other driver comparisons
     err = np.abs(got.astype(np.float64) - ref).max()
     assert err <= 1e-6, err
+
+
+@pytest.mark.parametrize("n", [1, 1000, 22050, synth.SEGMENT_SAMPLES + 1])
+def test_short_and_ragged_tracks_match_the_oracle_driver(n):
+    # one chunk or barely more (the view is padded with zeros on both sides,
+    # mix.rs:552-633). A one-sample track normalises to an all-zero segment,
+    # whose std is 0: the reference denormalises with affine_in_place(x,
+    # -mean / std, std) (host.rs:466-509), which is 0/0 there, so its stems are
+    # NaN; the device reproduces that, as the oracle does
+    h = _handle(synth.random_weights(27), max_batch=2)
+    track = synth.pink_noise(40, max(n, 2))[:, :n].copy() if n > 1 else np.full((2, 1), 0.05, np.float32)
+    for shifts in (0, 1):
+        got = h.separate_track(track[0], track[1], shifts=shifts)
+        ref = oracle.separate_with(h.forward, track, synth.SEGMENT_SAMPLES, shifts=shifts)
+        assert got.shape == ref.shape == (4, 2, n)
+        assert np.array_equal(np.isnan(got), np.isnan(ref))
+        assert np.isnan(got).all() if n == 1 else np.isfinite(got).all()
+        ok = ~np.isnan(ref)
+        if ok.any():
+            err = np.abs(got[ok].astype(np.float64) - ref[ok]).max()
+            assert err <= 1e-6 * max(1.0, np.abs(ref[ok]).max()), err
+
+
+def test_invalid_driver_arguments_are_rejected():
+    import dmx
+
+    h = _handle(synth.random_weights(28), max_batch=1)
+    x = synth.pink_noise(41, 5000)
+    with pytest.raises(dmx.DmxError, match="bad argument"):
+        h.separate_track(x[0][:0], x[1][:0])
+    with pytest.raises(dmx.DmxError, match="zero stride"):
+        h.separate_track(x[0], x[1], overlap=1.0)
+    with pytest.raises(dmx.DmxError, match="transition_power"):
+        h.separate_track(x[0], x[1], transition_power=2.0)
+    with pytest.raises(dmx.DmxError, match="shifts"):
+        h.separate_track(x[0], x[1], shifts=-1)
