@@ -2199,7 +2199,7 @@ struct HostSink {
 // (single pass only) the stems are also copied to the host as they finish.
 void separate_track_impl(dmx_handle* h, BagPlan* bag, const float* lr_dev, int64_t n,
                          const dmx_separate_opts* opts, float* d_stems, dmx_progress_fn progress,
-                         void* user, const HostSink* sink = nullptr) {
+                         void* user, HostSink* sink = nullptr) {
   dmx_separate_opts o{1, 0.25, 1.0, 0};
   if (opts) o = *opts;
   if (o.transition_power != 1.0) throw Error(DMX_ERR_INVALID, "transition_power must be 1");
@@ -2284,7 +2284,7 @@ void separate_track_impl(dmx_handle* h, BagPlan* bag, const float* lr_dev, int64
                                  (size_t)n * sizeof(float), (size_t)(t_hi - t_done) * sizeof(float),
                                  8, cudaMemcpyDeviceToHost, h->copy_stream));
           else
-            const_cast<HostSink*>(sink)->put(h, d_stems, n, t_done, t_hi);
+            sink->put(h, d_stems, n, t_done, t_hi);
           t_done = t_hi;
         }
       }
@@ -2308,9 +2308,9 @@ void separate_track_impl(dmx_handle* h, BagPlan* bag, const float* lr_dev, int64
     if (!stream_out) {  // several shift passes: every sample is final only now
       CK(cudaEventRecord(h->copy_ev, h->stream));
       CK(cudaStreamWaitEvent(h->copy_stream, h->copy_ev, 0));
-      const_cast<HostSink*>(sink)->put(h, d_stems, n, 0, n);
+      sink->put(h, d_stems, n, 0, n);
     }
-    const_cast<HostSink*>(sink)->flush(h);
+    sink->flush(h);
   }
   h->mark("end");
   CK(cudaGetLastError());
