@@ -290,3 +290,34 @@ def assign_tracks(lengths, world: int, shifts: int, overlap: float = 0.25):
         out[r].append(i)
         load[r] += units[i]
     return [sorted(x) for x in out]
+
+
+def gather_tracks(dist, rank: int, per_rank, stems_by_track: dict, lengths, like=None,
+                  timeout=None):
+    """Rank 0 receives the (4, 2, n_i) stems of every track the other ranks
+    separated (``per_rank`` from assign_tracks) and returns {track: stems};
+    other ranks send theirs and return {}. ``stems_by_track`` holds this
+    rank's own tracks; ``like`` gives dtype and device (default: any of them).
+    Every receive waits at most ``timeout`` seconds (ShardTimeout)."""
+    import torch
+
+    if rank == 0:
+        out = dict(stems_by_track)
+        proto = like if like is not None else next(iter(stems_by_track.values()), None)
+        ops, recvs = [], []
+        for r, tracks in enumerate(per_rank):
+            if r == 0:
+                continue
+            for i in tracks:
+                buf = torch.empty((4, 2, lengths[i]), dtype=torch.float32,
+                                  device=proto.device if proto is not None else "cpu")
+                recvs.append((i, buf))
+                ops.append(dist.P2POp(dist.irecv, buf, r))
+        if ops:
+            _wait_all(dist.batch_isend_irecv(ops), "track gather", timeout)
+        out.update(dict(recvs))
+        return out
+    ops = [dist.P2POp(dist.isend, stems_by_track[i].contiguous(), 0) for i in per_rank[rank]]
+    if ops:
+        _wait_all(dist.batch_isend_irecv(ops), "track gather", timeout)
+    return {}

@@ -183,3 +183,45 @@ def test_track_assignment_balances_units_and_covers_every_track():
     loads = [sum(shard.track_units(lengths[i], 1) for i in r) for r in per]
     assert sorted(i for r in per for i in r) == list(range(37))
     assert max(loads) - min(loads) <= max(shard.track_units(n, 1) for n in lengths)
+
+
+def _tracks_worker(rank, world, port, out_path):
+    # the throughput batch over ranks: each rank separates its share of the tracks (here
+    # with the oracle driver over a stand-in forward), rank 0 gathers every track's stems
+    import datetime
+    import sys
+
+    import torch.distributed as dist
+
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    sys.path[:0] = [os.path.join(root, "demucs-wgpu_b200"), os.path.join(root, "oracle")]
+    import oracle
+    import shard
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=60))
+    lengths = [SEG * k + 17 * k for k in (1, 5, 2, 7, 3)]
+    tracks = [_track()[:, :n].copy() for n in lengths]
+    per_rank = shard.assign_tracks(lengths, world, shifts=2)
+    mine = {i: torch.from_numpy(oracle.separate_with(_forward, tracks[i], SEG, shifts=2))
+            for i in per_rank[rank]}
+    got = shard.gather_tracks(dist, rank, per_rank, mine, lengths, timeout=30)
+    if rank == 0:
+        np.savez(out_path, *[got[i].numpy() for i in range(len(lengths))])
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+def test_tracks_over_ranks_gather_to_rank0(tmp_path):
+    import oracle
+
+    out_path = str(tmp_path / "tracks.npz")
+    mp.start_processes(_tracks_worker, args=(3, _free_port(), out_path), nprocs=3, join=True,
+                       start_method="spawn")
+    got = np.load(out_path)
+    lengths = [SEG * k + 17 * k for k in (1, 5, 2, 7, 3)]
+    for i, n in enumerate(lengths):
+        ref = oracle.separate_with(_forward, _track()[:, :n].copy(), SEG, shifts=2)
+        assert np.array_equal(got[f"arr_{i}"], ref)
