@@ -116,6 +116,10 @@ void launch_ola_finish(const float* acc, int64_t length, int64_t shift_offset, i
                        float scale, int mode, float* pass, float* stems, cudaStream_t s,
                        int64_t t_lo = 0, int64_t t_hi = -1);
 
+// selftest.cu — one warp waits on a device flag nothing sets and, after
+// limit_ns, stores `code` into err and returns (the bounded-wait error path).
+void launch_selftest_wait(uint64_t limit_ns, int code, int* err, cudaStream_t s);
+
 // bag.cu — the bag's per-source weighted combination (api.rs:319-361).
 // For source s: out = (sum over j < count[s] of out[net[s][j]] * weight[s][j])
 // / total[s], or zeros when count[s] == 0. Every out[] buffer and `out` is

@@ -1404,13 +1404,16 @@ void forward(dmx_handle* h, const float* mix, int G, float* out) {
 }
 
 // Raises DMX_ERR_TIMEOUT when a tensor-core kernel gave up a bounded wait.
+constexpr int kSelftestCode = 99;  // the error code dmx_selftest_wait_timeout's kernel raises
+
 void check_device_flag(dmx_handle* h) {
   int flag = 0;
   CK(cudaMemcpy(&flag, h->err, sizeof(int), cudaMemcpyDeviceToHost));
   if (flag) {
     CK(cudaMemset(h->err, 0, sizeof(int)));
-    throw Error(DMX_ERR_TIMEOUT, "a tensor-core kernel gave up a bounded wait (code " +
-                                     std::to_string(flag) + ")");
+    throw Error(DMX_ERR_TIMEOUT, std::string(flag == kSelftestCode ? "the self-test kernel"
+                                                                   : "a tensor-core kernel") +
+                                     " gave up a bounded wait (code " + std::to_string(flag) + ")");
   }
 }
 
@@ -2796,6 +2799,23 @@ dmx_status dmx_separate_track_emit(dmx_handle* h, const float* left, const float
     check_device_flag(h);
     finish_stage_times(h);
     return DMX_OK;
+  } catch (const Error& e) {
+    return fail(e);
+  } catch (const std::exception& e) {
+    return fail_std(e);
+  }
+}
+
+dmx_status dmx_selftest_wait_timeout(dmx_handle* h, int wait_ms) {
+  try {
+    if (!h || wait_ms < 1 || wait_ms > 5000)
+      throw Error(DMX_ERR_INVALID, "dmx_selftest_wait_timeout: wait_ms must be in [1, 5000]");
+    CK(cudaSetDevice(h->device));
+    launch_selftest_wait((uint64_t)wait_ms * 1000000ull, kSelftestCode, h->err, h->stream);
+    CK(cudaGetLastError());
+    CK(cudaStreamSynchronize(h->stream));  // ends: the kernel's wait is bounded
+    check_device_flag(h);                  // turns the raised flag into DMX_ERR_TIMEOUT
+    throw Error(DMX_ERR_INVALID, "dmx_selftest_wait_timeout: the wait did not report giving up");
   } catch (const Error& e) {
     return fail(e);
   } catch (const std::exception& e) {

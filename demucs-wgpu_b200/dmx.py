@@ -24,7 +24,7 @@ EXPORTS = (
     "dmx_separate_track_device", "dmx_normalize_track_device", "dmx_normalize_track_noalloc",
     "dmx_bag_combine_device", "dmx_bag_forward_device", "dmx_separate_track_bag",
     "dmx_separate_track_bag_device", "dmx_separate_batch", "dmx_separate_batch_device",
-    "dmx_separate_track_emit",
+    "dmx_separate_track_emit", "dmx_selftest_wait_timeout",
     "dmx_num_chunks", "dmx_track_finish", "dmx_track_shard", "dmx_set_trace",
     "dmx_set_stage_timing", "dmx_stage_times", "dmx_kernel_launches", "dmx_stream",
     "dmx_synchronize",
@@ -112,6 +112,7 @@ def lib():
                                        ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p,
                                        ctypes.c_int64, ctypes.c_int64]
         L.dmx_set_stage_timing.argtypes = [ctypes.c_void_p, ctypes.c_int]
+        L.dmx_selftest_wait_timeout.argtypes = [ctypes.c_void_p, ctypes.c_int]
         L.dmx_stream.restype = ctypes.c_void_p
         L.dmx_stream.argtypes = [ctypes.c_void_p]
         L.dmx_synchronize.argtypes = [ctypes.c_void_p]
@@ -297,6 +298,11 @@ class Handle:
                                       max_shift, SEGMENT, overlap, shifts,
                                       ctypes.c_void_p(mean_std_ptr), ctypes.c_void_p(stems_ptr),
                                       t_lo, t_hi))
+
+    def selftest_wait_timeout(self, wait_ms: int = 200):
+        """dmx_selftest_wait_timeout: raises DmxError with code 4 (DMX_ERR_TIMEOUT)
+        after a device wait that nothing satisfies gives up."""
+        _check(lib().dmx_selftest_wait_timeout(self._h, wait_ms))
 
     def set_stage_timing(self, on: bool):
         _check(lib().dmx_set_stage_timing(self._h, int(bool(on))))

@@ -278,6 +278,17 @@ dmx_status dmx_set_stage_timing(dmx_handle* h, int on);
 int dmx_stage_times(dmx_handle* h, const char** names, float* ms, int* counts, double* flops,
                     double* bytes, int cap);
 
+/* Self-test of the bounded-wait error path; no counterpart in the reference
+ * (its device path has no waits that can time out). Every wait in this
+ * library's tensor-core kernels gives up after a fixed time, raises the
+ * handle's device error flag and returns, so a stuck pipeline becomes
+ * DMX_ERR_TIMEOUT on the host instead of a hung GPU. Those waits only run out
+ * when something is broken; this entry point runs one that always does: one
+ * warp on the handle's stream waits on a device flag that nothing sets, gives
+ * up after `wait_ms` (1..5000), and raises the flag. Returns DMX_ERR_TIMEOUT
+ * (with dmx_last_error() naming the self-test) and leaves the handle usable. */
+dmx_status dmx_selftest_wait_timeout(dmx_handle* h, int wait_ms);
+
 /* Number of kernels the last forward launched. */
 int64_t dmx_kernel_launches(dmx_handle* h);
 

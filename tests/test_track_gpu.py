@@ -159,3 +159,25 @@ def test_invalid_driver_arguments_are_rejected():
         h.separate_track(x[0], x[1], transition_power=2.0)
     with pytest.raises(dmx.DmxError, match="shifts"):
         h.separate_track(x[0], x[1], shifts=-1)
+
+
+def test_a_device_wait_that_runs_out_reports_timeout_and_the_handle_stays_usable():
+    # the bounded-wait error path: a kernel waits on a device flag nothing sets, gives up
+    # after 200 ms and raises the handle's error flag; the host reports DMX_ERR_TIMEOUT
+    # and the next work on the same handle runs normally
+    import time
+
+    import dmx
+
+    h = _handle(synth.random_weights(29), max_batch=1)
+    mix = synth.gaussian_audio(9, 1)
+    before = h.forward(mix)
+    t0 = time.perf_counter()
+    with pytest.raises(dmx.DmxError, match="self-test kernel gave up a bounded wait") as e:
+        h.selftest_wait_timeout(200)
+    assert e.value.code == 4
+    assert 0.15 < time.perf_counter() - t0 < 30
+    after = h.forward(mix)
+    assert np.abs(after.astype(np.float64) - before).max() <= 1e-6
+    with pytest.raises(dmx.DmxError, match="wait_ms"):
+        h.selftest_wait_timeout(0)
