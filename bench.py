@@ -1,6 +1,6 @@
 """Benchmark: audio-seconds separated per second by the B200 HTDemucs v4 backend.
 
-Workload (BASELINE configuration "full-track htdemucs"): one 240 s stereo
+Workload (the full-track htdemucs configuration of the benchmark): one 240 s stereo
 44.1 kHz seeded pink-noise track (RMS 0.1), 7.8 s segments, overlap 0.25,
 shifts 1 (ShiftRng seed 0x5eed1234), all chunks of the track batched into one
 forward; random-init weights (seeded, LayerScale 1e-4). A step is one

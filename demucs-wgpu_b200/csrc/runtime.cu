@@ -2368,7 +2368,7 @@ void separate_track_host(dmx_handle* h, BagPlan* bag, const float* left, const f
 }
 
 // Many tracks through one network with their chunks pooled into full
-// forwards (BASELINE config "throughput batch"). The work units are (track,
+// forwards (the many-track throughput configuration). The work units are (track,
 // shift pass, chunk) in that order; consecutive units fill each forward of
 // `batch` chunks regardless of which track or pass they belong to. Every
 // track is driven exactly as separate_track_impl drives it — its own global
