@@ -2084,6 +2084,8 @@ void make_bag(dmx_handle* const* nets, int n_nets, const float* weights, const i
       if (o == hk) throw Error(DMX_ERR_INVALID, "each network of a bag needs its own handle");
     b->nets.push_back(hk);
   }
+  if (b->nets.empty())
+    throw Error(DMX_ERR_INVALID, "no stem is requested, so no network of the bag would run");
   CK(cudaSetDevice(b->nets[0]->device));
   CK(cudaEventCreateWithFlags(&b->ev, cudaEventDisableTiming));
 }

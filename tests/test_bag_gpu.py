@@ -134,3 +134,14 @@ def test_bag_device_entry_point_matches_host_entry_point():
     hs[0].synchronize()
     err = np.abs(stems.cpu().numpy().astype(np.float64) - ref).max()
     assert err <= 1e-6, err
+
+
+def test_bag_with_no_requested_stem_is_rejected():
+    import dmx
+
+    hs = _handles([71], max_batch=1)
+    bag = dmx.Bag(hs, IDENTITY[:1], requested=[])
+    track = synth.pink_noise(6, 44100)
+    with pytest.raises(dmx.DmxError, match="no stem is requested") as e:
+        bag.separate_track(track[0], track[1])
+    assert e.value.code == 1
