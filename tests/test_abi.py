@@ -62,3 +62,18 @@ def test_weight_blob_dtypes_are_checked_before_the_device_is_touched():
     # a well-formed F16 blob gets past parsing (on a host without a GPU the next step fails)
     w = {"x": np.array([1.0, -2.0, 0.5, 0.0], np.float32)}
     assert synth.write_safetensors(w, dtype="F16")[8:].startswith(b'{"x":{"dtype":"F16"')
+
+
+def test_bag_arguments_map_stem_names_to_flags():
+    # StemSelection (api.rs:895-906) as the C ABI's four `requested` flags
+    import numpy as np
+    import pytest
+
+    w, req = dmx._bag_args(np.eye(4), ["vocals", "bass"])
+    assert w.dtype == np.float32 and w.flags.c_contiguous and w.shape == (4, 4)
+    assert list(req) == [0, 1, 0, 1]
+    assert list(dmx._bag_args(np.eye(4), [0, 2])[1]) == [1, 0, 1, 0]
+    assert dmx._bag_args(np.eye(4), None)[1] is None
+    assert list(dmx._bag_args(np.eye(4), [])[1]) == [0, 0, 0, 0]
+    with pytest.raises(ValueError):
+        dmx._bag_args(np.ones((2, 3)), None)
