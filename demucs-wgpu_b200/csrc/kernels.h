@@ -116,6 +116,11 @@ void launch_ola_finish(const float* acc, int64_t length, int64_t shift_offset, i
                        float scale, int mode, float* pass, float* stems, cudaStream_t s,
                        int64_t t_lo = 0, int64_t t_hi = -1);
 
+// multi.cu — acc[r * ld + c] += tail[r * width + c] (rows x width), the
+// boundary merge of the multi-GPU track driver.
+void launch_tail_add(float* acc, int64_t ld, const float* tail, int64_t width, int rows,
+                     cudaStream_t s);
+
 // selftest.cu — one warp waits on a device flag nothing sets and, after
 // limit_ns, stores `code` into err and returns (the bounded-wait error path).
 void launch_selftest_wait(uint64_t limit_ns, int code, int* err, cudaStream_t s);

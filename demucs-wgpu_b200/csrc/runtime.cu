@@ -543,6 +543,9 @@ struct dmx_handle {
   int64_t emit_cap = 0;                     // samples per staging block
   char* batch_ws = nullptr;  // per-track slots of dmx_separate_batch_device
   size_t batch_cap = 0;
+  float* tail_buf = nullptr;  // the left neighbour's overlap tail (dmx_separate_track_multi)
+  size_t tail_cap = 0;
+  cudaEvent_t shard_done = nullptr;  // this handle's chunks are accumulated (multi driver)
   float* batch_io = nullptr;  // device staging of dmx_separate_batch's host tracks and stems
   size_t batch_io_cap = 0;
 
@@ -1842,6 +1845,8 @@ void dmx_destroy(dmx_handle* h) {
   }
   if (h->copy_stream) cudaStreamDestroy(h->copy_stream);
   cudaFree(h->batch_ws);
+  cudaFree(h->tail_buf);
+  if (h->shard_done) cudaEventDestroy(h->shard_done);
   cudaFree(h->batch_io);
   cudaFreeHost(h->pinned_in);
   cudaFreeHost(h->pinned_out);
@@ -2549,6 +2554,171 @@ void separate_batch_impl(dmx_handle* h, const float* const* lr_dev, const int64_
 }  // namespace
 
 extern "C" {
+
+dmx_status dmx_separate_track_multi(dmx_handle* const* hs, int n_handles, const float* left,
+                                    const float* right, int64_t n, const dmx_separate_opts* opts,
+                                    float* stems_out) {
+  std::vector<dmx_handle*> H;
+  try {
+    if (!hs || n_handles < 1 || n_handles > 64 || !left || !right || !stems_out || n <= 0)
+      throw Error(DMX_ERR_INVALID, "dmx_separate_track_multi: bad argument");
+    for (int k = 0; k < n_handles; ++k) {
+      if (!hs[k]) throw Error(DMX_ERR_INVALID, "handle " + std::to_string(k) + " is NULL");
+      for (dmx_handle* o : H)
+        if (o == hs[k]) throw Error(DMX_ERR_INVALID, "each rank needs its own handle");
+      H.push_back(hs[k]);
+    }
+    dmx_separate_opts o{1, 0.25, 1.0, 0};
+    if (opts) o = *opts;
+    if (o.transition_power != 1.0) throw Error(DMX_ERR_INVALID, "transition_power must be 1");
+    if (o.shifts < 0 || o.shifts > 1)
+      throw Error(DMX_ERR_INVALID,
+                  "dmx_separate_track_multi runs one pass (shifts 0 or 1); for more shift passes "
+                  "use dmx_separate_track or dmx_separate_batch per GPU");
+    const int seg = kSegment;
+    const int64_t stride = (int64_t)((1.0 - o.overlap) * (double)seg);
+    if (stride <= 0) throw Error(DMX_ERR_INVALID, "overlap leaves a zero stride");
+    // the single pass's view (ShiftRng's first draw, pipeline.rs:136-151, 416-418)
+    const int64_t max_shift = o.shifts > 0 ? (int64_t)(0.5 * 44100.0) : 0;
+    int64_t offset = 0;
+    if (o.shifts > 0) {
+      uint64_t rng = 0x5eed1234ULL * 6364136223846793005ULL + 1ULL;
+      rng = rng * 6364136223846793005ULL + 1442695040888963407ULL;
+      offset = (int64_t)((rng >> 33) % (uint64_t)(max_shift + 1));
+    }
+    const int64_t vlen = o.shifts > 0 ? n + max_shift - offset : n;
+    const int64_t trim = o.shifts > 0 ? max_shift - offset : 0;
+    const int64_t chunks = dmx_num_chunks(vlen, seg, o.overlap);
+    const int mode = o.shifts == 0 ? 0 : 1;
+    // contiguous chunk ranges, the first `extra` ranks one chunk more
+    struct Rank {
+      int64_t lo, hi, own_hi, send_lo, send_hi, t_lo, t_hi;
+      double* stats;
+      float2* norm;
+      float *lr, *mix, *acc, *stems;
+    };
+    std::vector<Rank> R(n_handles);
+    const int64_t base = chunks / n_handles, extra = chunks % n_handles;
+    int64_t c = 0;
+    for (int k = 0; k < n_handles; ++k) {
+      Rank& r = R[k];
+      r.lo = c;
+      r.hi = c + base + (k < extra ? 1 : 0);
+      c = r.hi;
+      const bool any = r.hi > r.lo;
+      const int64_t span_hi = any ? std::min(vlen, (r.hi - 1) * stride + seg) : 0;
+      r.own_hi = !any ? 0 : (r.hi == chunks ? vlen : r.hi * stride);
+      r.send_lo = r.own_hi;
+      r.send_hi = any && r.hi < chunks ? span_hi : r.own_hi;
+      const int64_t own_lo = r.lo * stride;
+      r.t_lo = any ? std::max<int64_t>(0, own_lo - trim) : 0;
+      r.t_hi = any ? std::max(r.t_lo, std::min(n, r.own_hi - trim)) : 0;
+    }
+    // per rank: the whole track, normalised (deterministic, so every rank agrees), and this
+    // rank's chunks overlap-added into a view-sized accumulator
+    const size_t scratch_bytes = (size_t)track_normalize_scratch_doubles() * sizeof(double);
+    for (int k = 0; k < n_handles; ++k) {
+      dmx_handle* h = H[k];
+      Rank& r = R[k];
+      CK(cudaSetDevice(h->device));
+      const size_t need_ws = (size_t)(2 * n + 8 * (n + max_shift)) * sizeof(float) + scratch_bytes + 512;
+      if (need_ws > h->track_cap) {
+        cudaFree(h->track_ws);
+        h->track_ws = nullptr;
+        h->track_cap = 0;
+        CK(cudaMalloc(&h->track_ws, need_ws));
+        h->track_cap = need_ws;
+      }
+      const size_t need_io = (size_t)10 * n * sizeof(float);
+      if (need_io > h->host_io_cap) {
+        cudaFree(h->host_io);
+        h->host_io = nullptr;
+        h->host_io_cap = 0;
+        CK(cudaMalloc(&h->host_io, need_io));
+        h->host_io_cap = need_io;
+      }
+      if (!h->shard_done) CK(cudaEventCreateWithFlags(&h->shard_done, cudaEventDisableTiming));
+      r.stats = reinterpret_cast<double*>(h->track_ws);
+      r.norm = reinterpret_cast<float2*>(h->track_ws + scratch_bytes);
+      r.mix = reinterpret_cast<float*>(h->track_ws + scratch_bytes + 512);
+      r.acc = r.mix + 2 * n;
+      r.lr = h->host_io;
+      r.stems = h->host_io + 2 * n;
+      h->launches = 0;
+      CK(cudaMemcpyAsync(r.lr, left, n * sizeof(float), cudaMemcpyHostToDevice, h->stream));
+      CK(cudaMemcpyAsync(r.lr + n, right, n * sizeof(float), cudaMemcpyHostToDevice, h->stream));
+      h->mark("track.normalize");
+      launch_track_normalize(r.lr, r.lr + n, n, r.stats, r.mix, r.norm, h->stream);
+      h->launches += 2;
+      CK(cudaMemsetAsync(r.acc, 0, 8 * vlen * sizeof(float), h->stream));
+      if (r.hi > r.lo) {
+        const int cap = std::max(1, o.batch > 0 ? std::min(o.batch, h->cfg.max_batch) : h->cfg.max_batch);
+        shard_chunks(h, nullptr, r.mix, n, offset, max_shift, seg, stride, r.lo, r.hi, cap, r.acc, 0,
+                     vlen);
+      }
+      CK(cudaEventRecord(h->shard_done, h->stream));
+    }
+    // boundary: rank k + 1 copies rank k's tail (after rank k's chunks) and adds it
+    for (int k = 0; k + 1 < n_handles; ++k) {
+      const Rank& a = R[k];
+      Rank& b = R[k + 1];
+      const int64_t w = a.send_hi - a.send_lo;
+      if (w <= 0 || b.hi <= b.lo) continue;
+      dmx_handle* hb = H[k + 1];
+      CK(cudaSetDevice(hb->device));
+      const size_t need = (size_t)8 * w * sizeof(float);
+      if (need > hb->tail_cap) {
+        cudaFree(hb->tail_buf);
+        hb->tail_buf = nullptr;
+        hb->tail_cap = 0;
+        CK(cudaMalloc(&hb->tail_buf, need));
+        hb->tail_cap = need;
+      }
+      CK(cudaStreamWaitEvent(hb->stream, H[k]->shard_done, 0));
+      for (int row = 0; row < 8; ++row)
+        CK(cudaMemcpyPeerAsync(hb->tail_buf + row * w, hb->device, a.acc + row * vlen + a.send_lo,
+                               H[k]->device, (size_t)w * sizeof(float), hb->stream));
+      hb->mark("track.merge");
+      launch_tail_add(b.acc + a.send_lo, vlen, hb->tail_buf, w, 8, hb->stream);
+      ++hb->launches;
+      CK(cudaGetLastError());
+    }
+    // each rank finishes the samples it owns and copies them straight to the host stems
+    for (int k = 0; k < n_handles; ++k) {
+      dmx_handle* h = H[k];
+      const Rank& r = R[k];
+      if (r.t_hi <= r.t_lo) continue;
+      CK(cudaSetDevice(h->device));
+      h->mark("track.finish");
+      launch_ola_finish(r.acc, n, offset, max_shift, seg, stride, h->W(h->m.ola_w.off), r.norm, 1.0f,
+                        mode, nullptr, r.stems, h->stream, r.t_lo, r.t_hi);
+      ++h->launches;
+      CK(cudaMemcpy2DAsync(stems_out + r.t_lo, (size_t)n * sizeof(float), r.stems + r.t_lo,
+                           (size_t)n * sizeof(float), (size_t)(r.t_hi - r.t_lo) * sizeof(float), 8,
+                           cudaMemcpyDeviceToHost, h->stream));
+      h->mark("end");
+    }
+    for (dmx_handle* h : H) {
+      CK(cudaSetDevice(h->device));
+      CK(cudaStreamSynchronize(h->stream));
+      check_device_flag(h);
+      finish_stage_times(h);
+    }
+    return DMX_OK;
+  } catch (const Error& e) {
+    for (dmx_handle* h : H) {  // no copy into the caller's memory outlives the call
+      cudaSetDevice(h->device);
+      cudaStreamSynchronize(h->stream);
+    }
+    return fail(e);
+  } catch (const std::exception& e) {
+    for (dmx_handle* h : H) {
+      cudaSetDevice(h->device);
+      cudaStreamSynchronize(h->stream);
+    }
+    return fail_std(e);
+  }
+}
 
 dmx_status dmx_separate_batch_device(dmx_handle* h, const float* const* lr_dev,
                                      const int64_t* lengths, int n_tracks,

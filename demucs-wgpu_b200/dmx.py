@@ -24,7 +24,7 @@ EXPORTS = (
     "dmx_separate_track_device", "dmx_normalize_track_device", "dmx_normalize_track_noalloc",
     "dmx_bag_combine_device", "dmx_bag_forward_device", "dmx_separate_track_bag",
     "dmx_separate_track_bag_device", "dmx_separate_batch", "dmx_separate_batch_device",
-    "dmx_separate_track_emit", "dmx_selftest_wait_timeout",
+    "dmx_separate_track_emit", "dmx_selftest_wait_timeout", "dmx_separate_track_multi",
     "dmx_num_chunks", "dmx_track_finish", "dmx_track_shard", "dmx_set_trace",
     "dmx_set_stage_timing", "dmx_stage_times", "dmx_kernel_launches", "dmx_stream",
     "dmx_synchronize",
@@ -113,6 +113,9 @@ def lib():
                                        ctypes.c_int64, ctypes.c_int64]
         L.dmx_set_stage_timing.argtypes = [ctypes.c_void_p, ctypes.c_int]
         L.dmx_selftest_wait_timeout.argtypes = [ctypes.c_void_p, ctypes.c_int]
+        L.dmx_separate_track_multi.argtypes = [ctypes.POINTER(ctypes.c_void_p), ctypes.c_int,
+                                               _f32p, _f32p, ctypes.c_int64,
+                                               ctypes.POINTER(SeparateOpts), _f32p]
         L.dmx_stream.restype = ctypes.c_void_p
         L.dmx_stream.argtypes = [ctypes.c_void_p]
         L.dmx_synchronize.argtypes = [ctypes.c_void_p]
@@ -388,6 +391,21 @@ class Bag:
                                                    ctypes.c_void_p(lr_ptr), n, ctypes.byref(opts),
                                                    ctypes.c_void_p(stems_ptr), PROGRESS_FN(0),
                                                    None))
+
+
+def separate_track_multi(handles, left, right, shifts=1, overlap=0.25, batch=0, out=None):
+    """dmx_separate_track_multi: one track over several handles (one per GPU,
+    the same network on each) from this thread; returns (4, 2, n)."""
+    left = np.ascontiguousarray(left, dtype=np.float32)
+    right = np.ascontiguousarray(right, dtype=np.float32)
+    n = left.shape[0]
+    stems = np.empty((4, 2, n), dtype=np.float32) if out is None else out
+    assert stems.shape == (4, 2, n) and stems.dtype == np.float32 and stems.flags.c_contiguous
+    hs = (ctypes.c_void_p * len(handles))(*[h._h.value for h in handles])
+    opts = SeparateOpts(shifts, overlap, 1.0, batch)
+    _check(lib().dmx_separate_track_multi(hs, len(handles), _ptr(left), _ptr(right), n,
+                                          ctypes.byref(opts), _ptr(stems)))
+    return stems
 
 
 def bag_combine_device(out_ptrs, weights, requested, n_segments: int, samples: int,

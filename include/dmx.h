@@ -120,6 +120,21 @@ dmx_status dmx_separate_track_emit(dmx_handle* h, const float* left, const float
                                    const dmx_separate_opts* opts, dmx_frames_fn on_frames,
                                    dmx_progress_fn progress, void* user);
 
+/* dmx_separate_track over several GPUs from one host thread (the whole-track
+ * multi-GPU entry of the drop-in plan; the reference runs one device:
+ * api.rs:438-545, streaming.rs:296-400). hs[k] holds the same network on
+ * rank k's GPU (handles may share a GPU). The single pass's chunks are split
+ * into contiguous ranges, one per rank; every rank normalises the whole track
+ * (a deterministic reduction, so all agree), overlap-adds its chunks, receives
+ * its left neighbour's overlap tail by a peer copy and adds it (at most two
+ * contributions per sample, so the sums equal one GPU's), finishes the
+ * samples it owns and copies them straight into `stems_out` (4, 2, n), all
+ * ranks at once. shifts must be 0 or 1 (one pass); for more shift passes use
+ * dmx_separate_track or dmx_separate_batch per GPU. */
+dmx_status dmx_separate_track_multi(dmx_handle* const* hs, int n_handles, const float* left,
+                                    const float* right, int64_t n, const dmx_separate_opts* opts,
+                                    float* stems_out);
+
 /* dmx_separate_track on device buffers of the handle's GPU: lr_dev holds the
  * raw (2, n) stereo track, stems_dev receives (4, 2, n). Enqueued on the
  * handle's stream; returns without waiting unless `progress` is set. */

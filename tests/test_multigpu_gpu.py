@@ -91,3 +91,27 @@ def test_two_gpu_sharding_matches_one_gpu(tmp_path):
     rms = np.sqrt(np.mean(single.astype(np.float64) ** 2))
     print(f"2-GPU vs 1-GPU: max-abs {err.max():.3e}, mean-abs SNR {-20 * np.log10(max(err.mean(), 1e-30) / rms):.1f} dB")
     assert err.max() == 0 or -20 * np.log10(err.mean() / rms) > 100
+
+
+@pytest.mark.parametrize("ranks,shifts,batch", [(2, 1, 2), (3, 0, 1), (4, 1, 4)])
+def test_single_process_multi_handle_driver_matches_one_handle(ranks, shifts, batch):
+    # dmx_separate_track_multi with every rank's handle on GPU 0 (or spread over the
+    # visible GPUs): the chunk split, the peer-copied boundary tails and the per-rank
+    # finish must reproduce dmx_separate_track; ranks without chunks (4 ranks, 3 chunks)
+    # contribute nothing
+    import dmx
+    import synth
+
+    gpus = torch.cuda.device_count()
+    blob = synth.write_safetensors(synth.random_weights(5))
+    hs = [dmx.Handle(blob, device=k % gpus, max_batch=2, precision=dmx.TF32) for k in range(ranks)]
+    seconds = 14 if ranks == 4 else 21
+    track = synth.pink_noise(8, 44100 * seconds)
+    got = dmx.separate_track_multi(hs, track[0], track[1], shifts=shifts, batch=batch)
+    ref = hs[0].separate_track(track[0], track[1], shifts=shifts, batch=batch)
+    assert np.isfinite(got).all()
+    err = np.abs(got.astype(np.float64) - ref)
+    rms = np.sqrt(np.mean(ref.astype(np.float64) ** 2))
+    assert err.max() == 0 or -20 * np.log10(err.mean() / rms) > 100, err.max()
+    for h in hs:
+        h.close()
