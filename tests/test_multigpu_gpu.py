@@ -5,6 +5,9 @@ tail crosses to the neighbour, each rank finalises the samples it owns
 (dmx_track_finish) and rank 0 gathers the stems, which are compared with
 dmx_separate_track on one GPU. Skipped with fewer than two visible GPUs.
 
+The single-process multi-GPU entry point (dmx_separate_track_multi) is tested
+with 2-4 handles placed on the visible GPUs in turn, so it also runs on one GPU.
+
 The OLA sums are order-independent, but the forward reduces its per-segment
 moments with f64 atomics whose order varies from run to run, so the two runs
 agree to that rounding (the same > 100 dB bar as the batch-independence
