@@ -327,3 +327,17 @@ def test_grouped_chunks_match_one_at_a_time_bitwise(oracle_mod):
     one = oracle_mod.separate_with(fwd, mix, seg, shifts=1, batch=1)
     three = oracle_mod.separate_with(fwd, mix, seg, shifts=1, batch=3)
     assert np.array_equal(one, three)
+
+
+def test_half_decoding_known_answers():
+    # safetensors.rs:196-203 and 226-232: binary16 -> binary32, subnormals and infinities
+    # included. The product's F16 loader is checked against numpy's IEEE float16 upcast on
+    # the GPU (test_forward_gpu.py); these are the reference's own known answers for it.
+    import numpy as np
+
+    bits = np.array([0x3C00, 0xC000, 0x3800, 0x0000, 0x0001, 0x7C00, 0xFC00, 0x7E00],
+                    dtype="<u2")
+    v = bits.view(np.float16).astype(np.float32)
+    assert list(v[:4]) == [1.0, -2.0, 0.5, 0.0]
+    assert v[4] == np.float32(2.0 ** -24)
+    assert np.isposinf(v[5]) and np.isneginf(v[6]) and np.isnan(v[7])
