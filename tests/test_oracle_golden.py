@@ -330,7 +330,7 @@ def test_grouped_chunks_match_one_at_a_time_bitwise(oracle_mod):
 
 
 def test_half_decoding_known_answers():
-    # safetensors.rs:196-203 and 226-232: binary16 -> binary32, subnormals and infinities
+    # safetensors.rs:194-203 and 228-234: binary16 -> binary32, subnormals and infinities
     # included. The product's F16 loader is checked against numpy's IEEE float16 upcast on
     # the GPU (test_forward_gpu.py); these are the reference's own known answers for it.
     import numpy as np
