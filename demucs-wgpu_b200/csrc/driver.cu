@@ -74,9 +74,15 @@ __global__ void track_normalize_kernel(const float* __restrict__ left,
   }
 }
 
+// segment: the samples each chunk is cut to (its window and the OLA weights);
+// row: the samples of one forward row (the model's training length). A chunk
+// shorter than a row (a `segment` override) is centred in `segment` samples
+// and zero padded at the end of the row, as Htdemucs::forward pads a short
+// input (host.rs:217-229); only the row's first `segment` output samples are
+// used.
 struct ChunkGeom {
   int64_t length, view_length, shift_offset, max_shift, stride;
-  int segment;
+  int segment, row;
 };
 
 DMX_DEVICE int64_t chunk_len(const ChunkGeom& g, int64_t c) {
@@ -92,15 +98,15 @@ __global__ void gather_chunks_kernel(const float* __restrict__ mix_norm, ChunkGe
   const int64_t vstart = chunk * g.stride;
   const int64_t len = chunk_len(g, chunk);
   const int64_t start = vstart - (g.segment - len) / 2;
-  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < g.segment;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < g.row;
        i += (int64_t)gridDim.x * blockDim.x) {
     const int64_t v = start + i;
     float sample = 0.f;
-    if (v >= 0 && v < g.view_length) {
+    if (i < g.segment && v >= 0 && v < g.view_length) {
       const int64_t mi = g.max_shift ? g.shift_offset + v - g.max_shift : v;
       if (mi >= 0 && mi < g.length) sample = mix_norm[(int64_t)c * g.length + mi];
     }
-    out[((int64_t)slot * 2 + c) * g.segment + i] = sample;
+    out[((int64_t)slot * 2 + c) * g.row + i] = sample;
   }
 }
 
@@ -127,9 +133,9 @@ __global__ void ola_accumulate_kernel(const float* __restrict__ chunks, ChunkGeo
     if (u < 0 || u >= len) continue;
     const int64_t trim = (g.segment - len) / 2;
     const float w = weight[u];
-    const float* src = chunks + (c - chunk0) * 8 * (int64_t)g.segment + trim + u;
+    const float* src = chunks + (c - chunk0) * 8 * (int64_t)g.row + trim + u;
 #pragma unroll
-    for (int r = 0; r < 8; ++r) vals[r] += w * src[(int64_t)r * g.segment];
+    for (int r = 0; r < 8; ++r) vals[r] += w * src[(int64_t)r * g.row];
   }
 #pragma unroll
   for (int r = 0; r < 8; ++r) acc[(int64_t)r * (view_hi - view_lo) + (v - view_lo)] = vals[r];
@@ -191,8 +197,9 @@ void launch_track_normalize_blocks(const float* left, const float* right, int64_
 }
 
 static ChunkGeom geom(int64_t length, int64_t shift_offset, int64_t max_shift, int segment,
-                      int64_t stride) {
+                      int64_t stride, int row = 0) {
   ChunkGeom g;
+  g.row = row > 0 ? row : segment;
   g.length = length;
   g.shift_offset = shift_offset;
   g.max_shift = max_shift;
@@ -204,16 +211,16 @@ static ChunkGeom geom(int64_t length, int64_t shift_offset, int64_t max_shift, i
 
 void launch_gather_chunks(const float* mix_norm, int64_t length, int64_t shift_offset,
                           int64_t max_shift, int segment, int64_t stride, int64_t chunk0,
-                          int count, float* out, cudaStream_t s) {
-  const ChunkGeom g = geom(length, shift_offset, max_shift, segment, stride);
+                          int count, float* out, cudaStream_t s, int row) {
+  const ChunkGeom g = geom(length, shift_offset, max_shift, segment, stride, row);
   gather_chunks_kernel<<<dim3(84, count, 2), 1024, 0, s>>>(mix_norm, g, chunk0, out);
 }
 
 void launch_ola_accumulate(const float* chunks, int64_t length, int64_t shift_offset,
                            int64_t max_shift, int segment, int64_t stride, int64_t chunk0,
                            int count, const float* weight, float* acc, int64_t view_lo,
-                           int64_t view_hi, cudaStream_t s) {
-  const ChunkGeom g = geom(length, shift_offset, max_shift, segment, stride);
+                           int64_t view_hi, cudaStream_t s, int row) {
+  const ChunkGeom g = geom(length, shift_offset, max_shift, segment, stride, row);
   const int64_t span = (count - 1) * stride + segment;
   ola_accumulate_kernel<<<(unsigned)((span + 255) / 256), 256, 0, s>>>(
       chunks, g, chunk0, count, weight, acc, view_lo, view_hi);

@@ -7,7 +7,7 @@
 
 namespace dmx {
 
-// Sets the thread-local message dmx_last_error() returns (runtime.cu).
+// Sets the thread-local message dmx_last_error() returns (abi.cu).
 void set_last_error(const char* msg);
 
 // spectral.cu
@@ -103,13 +103,16 @@ int track_normalize_scratch_doubles();
 // The same two kernels on `blocks` blocks; scratch holds 2*blocks doubles.
 void launch_track_normalize_blocks(const float* left, const float* right, int64_t n, int blocks,
                                    double* scratch, float* mix_norm, float2* norm, cudaStream_t s);
+// `segment`: samples per chunk; `row`: samples per forward row (0 = segment),
+// longer than `segment` when the chunks are cut shorter than the model's
+// training length (zero padded at the row's end).
 void launch_gather_chunks(const float* mix_norm, int64_t length, int64_t shift_offset,
                           int64_t max_shift, int segment, int64_t stride, int64_t chunk0,
-                          int count, float* out, cudaStream_t s);
+                          int count, float* out, cudaStream_t s, int row = 0);
 void launch_ola_accumulate(const float* chunks, int64_t length, int64_t shift_offset,
                            int64_t max_shift, int segment, int64_t stride, int64_t chunk0,
                            int count, const float* weight, float* acc, int64_t view_lo,
-                           int64_t view_hi, cudaStream_t s);
+                           int64_t view_hi, cudaStream_t s, int row = 0);
 // output samples [t_lo, t_hi) only (t_hi < 0: to the end)
 void launch_ola_finish(const float* acc, int64_t length, int64_t shift_offset, int64_t max_shift,
                        int segment, int64_t stride, const float* weight, const float2* norm,

@@ -11,7 +11,6 @@
 // of the moment reduction — in a file-scope device array that every GPU which
 // loads the library holds until the process exits.
 #include <cstdio>
-#include <mutex>
 
 #include "dmx.h"
 #include "kernels.h"
@@ -23,9 +22,6 @@ constexpr int kMaxBlocks = 8192;             // => at most 536,870,912 samples p
 
 // 2 * 8192 doubles = 128 KiB, shared by every call on a device.
 static __device__ __align__(256) double g_norm_partials[2 * kMaxBlocks];
-
-std::mutex g_mutex;
-void* g_scratch[64] = {};  // device address of g_norm_partials per device ordinal
 
 thread_local char g_msg[256];
 
@@ -51,31 +47,19 @@ extern "C" dmx_status dmx_normalize_track_noalloc(const float* lr_dev, int64_t n
     dmx::set_last_error("dmx_normalize_track_noalloc: mean_std_dev must be 8-byte aligned");
     return DMX_ERR_INVALID;
   }
-  int dev = 0;
-  cudaError_t e = cudaGetDevice(&dev);
-  if (e != cudaSuccess || dev < 0 || dev >= 64) {
-    snprintf(g_msg, sizeof(g_msg), "dmx_normalize_track_noalloc: no usable current device (%s)",
+  // The device address of the file-scope array on the current device (host
+  // code only sees a stand-in symbol). Resolved on every call, with the
+  // caller's device current, so a device reset or a new primary context
+  // never leaves a stale address behind; once the library's module is loaded
+  // on the device this allocates nothing. The very first call on a device may
+  // load the module, so it should come before any stream capture.
+  void* scratch = nullptr;
+  cudaError_t e = cudaGetSymbolAddress(&scratch, g_norm_partials);
+  if (e != cudaSuccess) {
+    snprintf(g_msg, sizeof(g_msg), "dmx_normalize_track_noalloc: cudaGetSymbolAddress failed (%s)",
              cudaGetErrorString(e));
     dmx::set_last_error(g_msg);
     return DMX_ERR_CUDA;
-  }
-  void* scratch = nullptr;
-  {
-    // First call on a device: resolve the device address of the file-scope
-    // array with that device current (host code only sees a stand-in symbol).
-    std::lock_guard<std::mutex> lock(g_mutex);
-    if (!g_scratch[dev]) {
-      e = cudaGetSymbolAddress(&g_scratch[dev], g_norm_partials);
-      if (e != cudaSuccess) {
-        g_scratch[dev] = nullptr;
-        snprintf(g_msg, sizeof(g_msg),
-                 "dmx_normalize_track_noalloc: cudaGetSymbolAddress failed (%s)",
-                 cudaGetErrorString(e));
-        dmx::set_last_error(g_msg);
-        return DMX_ERR_CUDA;
-      }
-    }
-    scratch = g_scratch[dev];
   }
   const int blocks = (int)((n + kSamplesPerBlock - 1) / kSamplesPerBlock);
   // Every block overwrites its own two partials before they are read, so the

@@ -27,7 +27,7 @@ EXPORTS = (
     "dmx_separate_track_emit", "dmx_selftest_wait_timeout", "dmx_separate_track_multi",
     "dmx_num_chunks", "dmx_track_finish", "dmx_track_shard", "dmx_set_trace",
     "dmx_set_stage_timing", "dmx_stage_times", "dmx_kernel_launches", "dmx_stream",
-    "dmx_synchronize",
+    "dmx_synchronize", "dmx_read_tensor", "dmx_shift_offsets",
 )
 
 _f32p = ctypes.POINTER(ctypes.c_float)
@@ -45,7 +45,8 @@ class Config(ctypes.Structure):
 
 class SeparateOpts(ctypes.Structure):
     _fields_ = [("shifts", ctypes.c_int), ("overlap", ctypes.c_double),
-                ("transition_power", ctypes.c_double), ("batch", ctypes.c_int)]
+                ("transition_power", ctypes.c_double), ("batch", ctypes.c_int),
+                ("segment", ctypes.c_double)]
 
 
 class DmxError(RuntimeError):
@@ -109,8 +110,11 @@ def lib():
                                                 ctypes.c_void_p]
         L.dmx_track_finish.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64,
                                        ctypes.c_int64, ctypes.c_int64, ctypes.c_int, ctypes.c_double,
-                                       ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p,
-                                       ctypes.c_int64, ctypes.c_int64]
+                                       ctypes.c_double, ctypes.c_int, ctypes.c_void_p,
+                                       ctypes.c_void_p, ctypes.c_int64, ctypes.c_int64]
+        L.dmx_read_tensor.argtypes = [ctypes.c_void_p, ctypes.c_size_t, ctypes.c_char_p, _f32p,
+                                      ctypes.c_int64, _i64p, ctypes.POINTER(ctypes.c_int)]
+        L.dmx_shift_offsets.argtypes = [ctypes.c_int, ctypes.c_int64, _i64p]
         L.dmx_set_stage_timing.argtypes = [ctypes.c_void_p, ctypes.c_int]
         L.dmx_selftest_wait_timeout.argtypes = [ctypes.c_void_p, ctypes.c_int]
         L.dmx_separate_track_multi.argtypes = [ctypes.POINTER(ctypes.c_void_p), ctypes.c_int,
@@ -134,6 +138,12 @@ def lib():
         L.dmx_kernel_launches.argtypes = [ctypes.c_void_p]
         _lib = L
     return _lib
+
+
+def _opts(shifts=1, overlap=0.25, transition_power=1.0, batch=0, segment=0.0):
+    """dmx_separate_opts (SeparateOptions, pipeline.rs:17-38); ``segment`` in
+    seconds, 0 = the model's."""
+    return SeparateOpts(shifts, overlap, transition_power, batch, segment or 0.0)
 
 
 def _check(rc):
@@ -201,7 +211,7 @@ class Handle:
                                         ctypes.c_void_p(out_ptr), ctypes.c_void_p(stream)))
 
     def separate_track(self, left, right, shifts=1, overlap=0.25, transition_power=1.0,
-                       batch=0, progress=None, out=None):
+                       batch=0, progress=None, out=None, segment=0.0):
         """Whole-track separation of host arrays; ``out`` (4, 2, n) float32 may
         be supplied (e.g. pinned memory) to avoid a fresh allocation."""
         left = np.ascontiguousarray(left, dtype=np.float32)
@@ -209,14 +219,14 @@ class Handle:
         n = left.shape[0]
         stems = np.empty((4, 2, n), dtype=np.float32) if out is None else out
         assert stems.shape == (4, 2, n) and stems.dtype == np.float32 and stems.flags.c_contiguous
-        opts = SeparateOpts(shifts, overlap, transition_power, batch)
+        opts = _opts(shifts, overlap, transition_power, batch, segment)
         cb = PROGRESS_FN(0) if progress is None else PROGRESS_FN(lambda d, t, _u: progress(d, t))
         _check(lib().dmx_separate_track(self._h, _ptr(left), _ptr(right), n, ctypes.byref(opts),
                                         _ptr(stems), cb, None))
         return stems
 
     def separate_track_emit(self, left, right, on_frames, shifts=1, overlap=0.25,
-                            transition_power=1.0, batch=0, progress=None):
+                            transition_power=1.0, batch=0, progress=None, segment=0.0):
         """Demucs::separate_streaming: ``on_frames(t0, block)`` receives each
         finished (8, count) block of denormalised stems in ascending order
         (the block is copied out of the library's staging first)."""
@@ -232,14 +242,14 @@ class Handle:
 
         fcb = FRAMES_FN(_frames)
         pcb = PROGRESS_FN(0) if progress is None else PROGRESS_FN(lambda d, t, _u: progress(d, t))
-        opts = SeparateOpts(shifts, overlap, transition_power, batch)
+        opts = _opts(shifts, overlap, transition_power, batch, segment)
         _check(lib().dmx_separate_track_emit(self._h, _ptr(left), _ptr(right), left.shape[0],
                                              ctypes.byref(opts), fcb, pcb, None))
         if error:
             raise error[0]
 
     def separate_batch(self, tracks, shifts=1, overlap=0.25, transition_power=1.0, batch=0,
-                       progress=None, outs=None):
+                       progress=None, outs=None, segment=0.0):
         """Many (2, n_i) host tracks in one call with their chunks pooled into
         full forwards (dmx_separate_batch); returns a list of (4, 2, n_i)."""
         lefts = [np.ascontiguousarray(t[0], dtype=np.float32) for t in tracks]
@@ -250,26 +260,28 @@ class Handle:
         for o, x in zip(outs, lefts):
             assert o.shape == (4, 2, x.shape[0]) and o.dtype == np.float32 and o.flags.c_contiguous
         arr = lambda xs: (_f32p * len(xs))(*[_ptr(x) for x in xs])  # noqa: E731
-        opts = SeparateOpts(shifts, overlap, transition_power, batch)
+        opts = _opts(shifts, overlap, transition_power, batch, segment)
         cb = PROGRESS_FN(0) if progress is None else PROGRESS_FN(lambda d, t, _u: progress(d, t))
         _check(lib().dmx_separate_batch(self._h, arr(lefts), arr(rights), lengths, len(tracks),
                                         ctypes.byref(opts), arr(outs), cb, None))
         return outs
 
     def separate_batch_device(self, lr_ptrs, lengths, stems_ptrs, shifts=1, overlap=0.25,
-                              batch=0):
+                              batch=0, transition_power=1.0, segment=0.0):
         """Enqueue dmx_separate_batch_device on device buffers (returns at once)."""
         n = len(lr_ptrs)
-        opts = SeparateOpts(shifts, overlap, 1.0, batch)
+        opts = _opts(shifts, overlap, transition_power, batch, segment)
         _check(lib().dmx_separate_batch_device(
             self._h, (ctypes.c_void_p * n)(*lr_ptrs), (ctypes.c_int64 * n)(*lengths), n,
             ctypes.byref(opts), (ctypes.c_void_p * n)(*stems_ptrs), PROGRESS_FN(0), None))
 
     def track_shard(self, mix_norm_ptr, length, shift_offset, max_shift, overlap, chunk_lo,
-                    chunk_hi, batch, acc_ptr, view_lo, view_hi):
+                    chunk_hi, batch, acc_ptr, view_lo, view_hi, transition_power=1.0,
+                    segment_samples=SEGMENT):
         _check(lib().dmx_track_shard(self._h, ctypes.c_void_p(mix_norm_ptr), length, shift_offset,
-                                     max_shift, SEGMENT, overlap, 1.0, chunk_lo, chunk_hi, batch,
-                                     ctypes.c_void_p(acc_ptr), view_lo, view_hi))
+                                     max_shift, segment_samples, overlap, transition_power,
+                                     chunk_lo, chunk_hi, batch, ctypes.c_void_p(acc_ptr), view_lo,
+                                     view_hi))
 
     def set_trace(self, store: dict | None):
         if store is None:
@@ -282,9 +294,9 @@ class Handle:
         _check(lib().dmx_set_trace(self._h, self._trace_cb, None))
 
     def separate_track_device(self, lr_ptr: int, n: int, stems_ptr: int, shifts=1,
-                              overlap=0.25, batch=0):
+                              overlap=0.25, batch=0, transition_power=1.0, segment=0.0):
         """Enqueue a whole-track separation on device buffers (returns at once)."""
-        opts = SeparateOpts(shifts, overlap, 1.0, batch)
+        opts = _opts(shifts, overlap, transition_power, batch, segment)
         _check(lib().dmx_separate_track_device(self._h, ctypes.c_void_p(lr_ptr), n,
                                                ctypes.byref(opts), ctypes.c_void_p(stems_ptr),
                                                PROGRESS_FN(0), None))
@@ -296,11 +308,12 @@ class Handle:
                                                 ctypes.c_void_p(mean_std_ptr)))
 
     def track_finish(self, acc_ptr, length, shift_offset, max_shift, overlap, shifts,
-                     mean_std_ptr, stems_ptr, t_lo=0, t_hi=-1):
+                     mean_std_ptr, stems_ptr, t_lo=0, t_hi=-1, transition_power=1.0,
+                     segment_samples=SEGMENT):
         _check(lib().dmx_track_finish(self._h, ctypes.c_void_p(acc_ptr), length, shift_offset,
-                                      max_shift, SEGMENT, overlap, shifts,
-                                      ctypes.c_void_p(mean_std_ptr), ctypes.c_void_p(stems_ptr),
-                                      t_lo, t_hi))
+                                      max_shift, segment_samples, overlap, transition_power,
+                                      shifts, ctypes.c_void_p(mean_std_ptr),
+                                      ctypes.c_void_p(stems_ptr), t_lo, t_hi))
 
     def selftest_wait_timeout(self, wait_ms: int = 200):
         """dmx_selftest_wait_timeout: raises DmxError with code 4 (DMX_ERR_TIMEOUT)
@@ -370,13 +383,13 @@ class Bag:
                                             ctypes.c_void_p(out_ptr)))
 
     def separate_track(self, left, right, shifts=1, overlap=0.25, transition_power=1.0,
-                       batch=0, progress=None, out=None):
+                       batch=0, progress=None, out=None, segment=0.0):
         left = np.ascontiguousarray(left, dtype=np.float32)
         right = np.ascontiguousarray(right, dtype=np.float32)
         n = left.shape[0]
         stems = np.empty((4, 2, n), dtype=np.float32) if out is None else out
         assert stems.shape == (4, 2, n) and stems.dtype == np.float32 and stems.flags.c_contiguous
-        opts = SeparateOpts(shifts, overlap, transition_power, batch)
+        opts = _opts(shifts, overlap, transition_power, batch, segment)
         cb = PROGRESS_FN(0) if progress is None else PROGRESS_FN(lambda d, t, _u: progress(d, t))
         _check(lib().dmx_separate_track_bag(self._nets, len(self.handles), _ptr(self.weights),
                                             self._req, _ptr(left), _ptr(right), n,
@@ -384,8 +397,8 @@ class Bag:
         return stems
 
     def separate_track_device(self, lr_ptr: int, n: int, stems_ptr: int, shifts=1, overlap=0.25,
-                              batch=0):
-        opts = SeparateOpts(shifts, overlap, 1.0, batch)
+                              batch=0, transition_power=1.0, segment=0.0):
+        opts = _opts(shifts, overlap, transition_power, batch, segment)
         _check(lib().dmx_separate_track_bag_device(self._nets, len(self.handles),
                                                    _ptr(self.weights), self._req,
                                                    ctypes.c_void_p(lr_ptr), n, ctypes.byref(opts),
@@ -393,7 +406,8 @@ class Bag:
                                                    None))
 
 
-def separate_track_multi(handles, left, right, shifts=1, overlap=0.25, batch=0, out=None):
+def separate_track_multi(handles, left, right, shifts=1, overlap=0.25, batch=0, out=None,
+                         transition_power=1.0, segment=0.0):
     """dmx_separate_track_multi: one track over several handles (one per GPU,
     the same network on each) from this thread; returns (4, 2, n)."""
     left = np.ascontiguousarray(left, dtype=np.float32)
@@ -402,7 +416,7 @@ def separate_track_multi(handles, left, right, shifts=1, overlap=0.25, batch=0, 
     stems = np.empty((4, 2, n), dtype=np.float32) if out is None else out
     assert stems.shape == (4, 2, n) and stems.dtype == np.float32 and stems.flags.c_contiguous
     hs = (ctypes.c_void_p * len(handles))(*[h._h.value for h in handles])
-    opts = SeparateOpts(shifts, overlap, 1.0, batch)
+    opts = _opts(shifts, overlap, transition_power, batch, segment)
     _check(lib().dmx_separate_track_multi(hs, len(handles), _ptr(left), _ptr(right), n,
                                           ctypes.byref(opts), _ptr(stems)))
     return stems
@@ -427,6 +441,27 @@ def normalize_track_noalloc(lr_ptr: int, n: int, mix_norm_ptr: int, mean_std_ptr
                                              ctypes.c_void_p(mix_norm_ptr),
                                              ctypes.c_void_p(mean_std_ptr),
                                              ctypes.c_void_p(stream)))
+
+
+def read_tensor(blob: bytes, name: str):
+    """dmx_read_tensor: one tensor of a safetensors blob as float32, decoded by
+    the library's loader (no GPU needed)."""
+    buf = ctypes.create_string_buffer(blob, len(blob))
+    cap = max(1, len(blob))
+    out = np.empty(cap, dtype=np.float32)
+    shape = (ctypes.c_int64 * 8)()
+    ndim = ctypes.c_int()
+    _check(lib().dmx_read_tensor(ctypes.cast(buf, ctypes.c_void_p), len(blob), name.encode(),
+                                 _ptr(out), cap, shape, ctypes.byref(ndim)))
+    dims = tuple(shape[i] for i in range(ndim.value))
+    return out[:int(np.prod(dims, dtype=np.int64))].reshape(dims).copy()
+
+
+def shift_offsets(passes: int, max_shift: int = 22050):
+    """dmx_shift_offsets: the ShiftRng offsets of each shift pass."""
+    out = (ctypes.c_int64 * max(1, passes))()
+    _check(lib().dmx_shift_offsets(passes, max_shift, out))
+    return [int(out[i]) for i in range(passes)]
 
 
 def num_chunks(view_length: int, segment: int = SEGMENT, overlap: float = 0.25) -> int:

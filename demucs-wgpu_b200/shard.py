@@ -18,7 +18,6 @@ from dataclasses import dataclass
 
 SEGMENT = 343980
 SR = 44100
-SHIFT_SEED = 0x5EED1234
 # Bound on every point-to-point wait of the exchange and the gathers: a peer
 # whose data never arrives (a rank that died or skipped the step) turns into
 # ShardTimeout instead of a hang.
@@ -47,15 +46,13 @@ def _wait_all(works, what, timeout=None):
             raise ShardTimeout(f"{what}: no data from the peer within {limit.total_seconds():g} s")
 
 
-def shift_offsets(shifts: int, max_shift: int, seed: int = SHIFT_SEED):
-    """The offsets ShiftRng draws for each pass (pipeline.rs:136-151, 416-418)."""
-    mask = (1 << 64) - 1
-    state = (seed * 6364136223846793005 + 1) & mask
-    out = []
-    for _ in range(shifts):
-        state = (state * 6364136223846793005 + 1442695040888963407) & mask
-        out.append((state >> 33) % (max_shift + 1))
-    return out
+def shift_offsets(shifts: int, max_shift: int):
+    """The offsets ShiftRng draws for each pass (pipeline.rs:136-151, 416-418),
+    from the library's own generator (dmx_shift_offsets), so every rank and
+    the device drivers use one definition."""
+    import dmx
+
+    return dmx.shift_offsets(shifts, max_shift)
 
 
 @dataclass
@@ -93,12 +90,18 @@ class TrackPlan:
 
 def plan(length: int, world: int, shifts: int = 1, overlap: float = 0.25,
          segment: int = SEGMENT, samplerate: int = SR) -> TrackPlan:
-    """Single-pass plan (shifts 0 or 1) of a ``length``-sample track over ``world`` ranks."""
+    """Single-pass plan (shifts 0 or 1) of a ``length``-sample track over ``world`` ranks.
+
+    The stride must exceed half a segment (overlap < 0.5): then every sample
+    has at most two contributions and a rank's overlap tail ends inside its
+    right neighbour's own span, which is what the boundary exchange assumes."""
     if shifts not in (0, 1):
         raise ValueError("sharding covers one pass: shifts must be 0 or 1")
     stride = int((1.0 - overlap) * segment)
     if stride <= 0:
         raise ValueError("overlap leaves a zero stride")
+    if 2 * stride <= segment:
+        raise ValueError("chunk sharding needs overlap < 0.5 (a stride longer than half a segment)")
     max_shift = int(0.5 * samplerate) if shifts else 0
     offset = shift_offsets(1, max_shift)[0] if shifts else 0
     view_length = length + max_shift - offset if shifts else length

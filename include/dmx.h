@@ -69,12 +69,20 @@ const char* dmx_last_error(void);
 /* SegmentForward::start (demucs/pipeline.rs:178-190; DeviceForward::start,
  * gpu/htdemucs.rs:2824-2847): queue one forward of `mix`, a host
  * (n_segments, 2, segment_samples) array of already-normalised padded chunks,
- * and return with the work in flight. The caller keeps `mix` alive until
- * collect. */
+ * and return with the work in flight. `mix` is copied into the pending
+ * forward's own staging before this returns, so the caller may free or reuse
+ * it at once (the reference drops its batch before collect, pipeline.rs:
+ * 596-623). Up to two forwards may be in flight on one handle, each with its
+ * own staging (PendingStems, gpu/htdemucs.rs:2744-2782), so the reference's
+ * queue-one-ahead loop — start(group n), then collect(group n - 1) — works
+ * as is; a third start before a collect fails with DMX_ERR_INVALID. The
+ * forwards run in start order on the handle's stream. */
 dmx_status dmx_forward_start(dmx_handle* h, const float* mix, int64_t n_segments,
                              dmx_pending** out);
-/* SegmentForward::collect: wait (bounded) and write (n_segments, 4, 2,
- * segment_samples) stems in normalised units to host `out`. */
+/* SegmentForward::collect: wait (bounded) for that forward and write its
+ * (n_segments, 4, 2, segment_samples) stems in normalised units to host
+ * `out`. Each pending forward is collected once; pending forwards may be
+ * collected in any order. */
 dmx_status dmx_forward_collect(dmx_pending* p, float* out);
 
 /* The same forward on device buffers of the handle's GPU (no host copies):
@@ -85,9 +93,13 @@ dmx_status dmx_forward_device(dmx_handle* h, const float* mix_dev, int64_t n_seg
 
 typedef struct {
   int shifts;              /* SeparateOptions::shifts (pipeline.rs:17-38) */
-  double overlap;          /* 0.25 */
-  double transition_power; /* 1.0 */
-  int batch;               /* chunks per forward (DEMUCS_BATCH); 0 = all */
+  double overlap;          /* 0.25; in [0, 1) */
+  double transition_power; /* 1.0; the triangular window's exponent (pipeline.rs:117-131) */
+  int batch;               /* chunks per forward (DEMUCS_BATCH); 0 = max_batch */
+  double segment;          /* SeparateOptions::segment, seconds; 0 = the model's 7.8 s.
+                              Chunks of int(44100 * segment) samples (at most the model's
+                              343980) are zero padded to the model's length for the forward
+                              and trimmed back, as Htdemucs::forward does (host.rs:210-229) */
 } dmx_separate_opts;
 
 typedef void (*dmx_progress_fn)(size_t done, size_t total, void* user);
@@ -130,7 +142,9 @@ dmx_status dmx_separate_track_emit(dmx_handle* h, const float* left, const float
  * contributions per sample, so the sums equal one GPU's), finishes the
  * samples it owns and copies them straight into `stems_out` (4, 2, n), all
  * ranks at once. shifts must be 0 or 1 (one pass); for more shift passes use
- * dmx_separate_track or dmx_separate_batch per GPU. */
+ * dmx_separate_track or dmx_separate_batch per GPU. The overlap must be below
+ * 0.5 (stride > segment / 2): a larger one would let a rank's tail reach past
+ * its neighbour's own span, and is rejected with DMX_ERR_INVALID. */
 dmx_status dmx_separate_track_multi(dmx_handle* const* hs, int n_handles, const float* left,
                                     const float* right, int64_t n, const dmx_separate_opts* opts,
                                     float* stems_out);
@@ -183,17 +197,20 @@ dmx_status dmx_normalize_track_device(dmx_handle* h, const float* lr_dev, int64_
  * exists for callers that cannot allocate device memory when they need it —
  * real-time audio hosts whose processing callback must not block on the
  * driver's allocator, and applications that reserve their whole device budget
- * up front — and so cannot create a dmx_handle either. Same result as
- * dmx_normalize_track_device on the current device's buffers (lr_dev (2, n)
- * -> mix_norm_dev (2, n), mean_std_dev {mean, std}), enqueued on `stream`
- * (a cudaStream_t, NULL = legacy default stream), with no cudaMalloc/cudaFree:
- * its scratch is a 128 KiB file-scope device array (partials of one block per
- * 65,536 samples), so n is limited to 536,870,912 samples per channel and
- * larger tracks are rejected with DMX_ERR_INVALID. The first call on a device
- * resolves that array's device address (cudaGetSymbolAddress) with the device
- * current, and should come before any stream capture. All calls on a device
- * share the array: calls that overlap on the GPU (different streams, no
- * ordering between them) race and must be serialised by the caller. */
+ * up front — and so cannot create a dmx_handle either. It computes what
+ * dmx_normalize_track_device computes on the current device's buffers (lr_dev
+ * (2, n) -> mix_norm_dev (2, n), mean_std_dev {mean, std}), equal to it up to
+ * the rounding of the f64 reduction (its per-block partials group the samples
+ * differently), enqueued on `stream` (a cudaStream_t, NULL = legacy default
+ * stream), with no cudaMalloc/cudaFree: its scratch is a 128 KiB file-scope
+ * device array (partials of one block per 65,536 samples), so n is limited to
+ * 536,870,912 samples per channel and larger tracks are rejected with
+ * DMX_ERR_INVALID. Every call resolves that array's device address
+ * (cudaGetSymbolAddress) with the caller's device current, so a device reset
+ * leaves nothing stale; the first call on a device may load the library's
+ * module there and should come before any stream capture. All calls on a
+ * device share the array: calls that overlap on the GPU (different streams,
+ * no ordering between them) race and must be serialised by the caller. */
 dmx_status dmx_normalize_track_noalloc(const float* lr_dev, int64_t n, float* mix_norm_dev,
                                        float* mean_std_dev, void* stream);
 
@@ -248,12 +265,20 @@ dmx_status dmx_separate_track_bag_device(dmx_handle* const* nets, int n_nets, co
                                          const dmx_separate_opts* opts, float* stems_dev,
                                          dmx_progress_fn progress, void* user);
 
+/* ShiftRng (pipeline.rs:136-151, 416-418): the offsets, each in
+ * [0, max_shift], that the separation drivers draw for `passes` shift passes
+ * (every separation seeds a fresh generator with 0x5eed_1234), written to
+ * out[0 .. passes). For callers that spread the passes or chunks of a track
+ * over processes themselves. */
+dmx_status dmx_shift_offsets(int passes, int64_t max_shift, int64_t* out);
+
 /* Chunk plan of a split pass (streaming.rs:88-94, 296-330): number of chunks
  * of a view of `view_length` samples. */
 int64_t dmx_num_chunks(int64_t view_length, int segment, double overlap);
 
 /* One shard of a track for multi-GPU chunk sharding: forward chunks
- * [chunk_lo, chunk_hi) of the shift view of the (device, normalised) mix and
+ * [chunk_lo, chunk_hi) (chunks of `segment` samples, at most 343980) of the
+ * shift view of the (device, normalised) mix and
  * overlap-add them, unnormalised by the window sum, into `acc_dev` over view
  * samples [view_lo, view_hi) — (8, view_hi - view_lo) floats — adding to what
  * is there. The window sums are analytic (dmx_ola_finish divides by them). */
@@ -272,8 +297,17 @@ dmx_status dmx_track_shard(dmx_handle* h, const float* mix_norm_dev, int64_t len
  * shift_offset); scale 1/shifts = 1. */
 dmx_status dmx_track_finish(dmx_handle* h, const float* acc_dev, int64_t length,
                             int64_t shift_offset, int64_t max_shift, int segment, double overlap,
-                            int shifts, const float* mean_std_dev, float* stems_dev, int64_t t_lo,
-                            int64_t t_hi);
+                            double transition_power, int shifts, const float* mean_std_dev,
+                            float* stems_dev, int64_t t_lo, int64_t t_hi);
+
+/* SafeTensors::parse + get (safetensors.rs:38-108, 110-160): tensor `name` of
+ * a safetensors blob as f32, decoded by the loader dmx_create uses (F32, F16,
+ * BF16, F64 and integer types upcast as safetensors.rs:110-135 does). Writes
+ * the element count's floats to `out` (DMX_ERR_INVALID if more than `cap`),
+ * the shape to `shape` (up to 8 dimensions) and its rank to `*ndim`; a
+ * missing tensor or a malformed blob is DMX_ERR_WEIGHTS. Makes no CUDA call. */
+dmx_status dmx_read_tensor(const void* safetensors_blob, size_t blob_len, const char* name,
+                           float* out, int64_t cap, int64_t* shape, int* ndim);
 
 /* Optional activation tracing (mirrors TraceSink, demucs/host.rs:117-125):
  * named intermediates copied to host in the reference's own layouts. */

@@ -1153,6 +1153,13 @@ void padded_chunk(const f32* mix, int channels, int64_t length, int64_t shift_of
     }
 }
 
+// center_trim(tensor, reference) (pipeline.rs:105-113): the first kept
+// sample of a `length`-sample signal trimmed to `reference`; the larger half
+// of an odd excess is removed at the end.
+int64_t center_trim_start(int64_t length, int64_t reference) {
+  return length <= reference ? 0 : (length - reference) / 2;
+}
+
 // One streaming split pass over the (optionally shifted) normalised mix;
 // returns (sources, 2, view_length) OLA-finalised output in view coordinates.
 int split_pass(const f32* mix, int64_t length, int segment, f64 overlap, f64 power, int batch,
@@ -1183,7 +1190,7 @@ int split_pass(const f32* mix, int64_t length, int segment, f64 overlap, f64 pow
     for (int slot = 0; slot < group; ++slot) {
       const int64_t vstart = starts[g0 + slot];
       const int64_t chunk = std::min<int64_t>(view_length - vstart, segment);
-      const int64_t trim = (segment - chunk) / 2;  // center_trim (pipeline.rs:105-113)
+      const int64_t trim = center_trim_start(segment, chunk);
       for (int r = 0; r < S * CH; ++r) {
         const f32* src = &outb[((size_t)slot * S * CH + r) * segment + trim];
         f32* dst = &view_out[(size_t)r * view_length + vstart];
@@ -1396,6 +1403,14 @@ int orc_istft(const float* spec, int rows, int bins, int frames, int n_fft, int 
   std::memcpy(out, y.data(), y.size() * sizeof(f32));
   return (int)(y.size() / rows);
 }
+// center_trim of rows x length to rows x reference (pipeline.rs:105-113).
+int orc_center_trim(const float* x, int rows, int64_t length, int64_t reference, float* out) {
+  const int64_t keep = std::min(length, reference), start = center_trim_start(length, reference);
+  for (int r = 0; r < rows; ++r)
+    for (int64_t t = 0; t < keep; ++t) out[(size_t)r * keep + t] = x[(size_t)r * length + start + t];
+  return (int)keep;
+}
+
 int orc_transition_weight(int segment, double power, float* out) {
   std::vector<f32> w = transition_weight(segment, power);
   std::memcpy(out, w.data(), w.size() * sizeof(f32));

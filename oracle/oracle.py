@@ -52,6 +52,7 @@ def lib():
                                    ctypes.c_double, ctypes.c_double, ctypes.c_int, SEGMENT_FN,
                                    ctypes.c_void_p, _f32p]
         L.orc_transition_weight.argtypes = [ctypes.c_int, ctypes.c_double, _f32p]
+        L.orc_center_trim.argtypes = [_f32p, ctypes.c_int, ctypes.c_int64, ctypes.c_int64, _f32p]
         L.orc_shift_randint.argtypes = [ctypes.c_uint64, ctypes.c_int, ctypes.c_uint64,
                                         ctypes.POINTER(ctypes.c_uint64)]
         L.orc_pos2d.argtypes = [ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_float, _f32p]

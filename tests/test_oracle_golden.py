@@ -163,18 +163,52 @@ def test_chunk_at_start_is_zero_padded_on_the_left(oracle_mod):
     assert _padded_chunk(oracle_mod, np.arange(6), 0, 3, 7) == [0, 0, 0, 1, 2, 3, 4]
 
 
-def test_center_trim_removes_the_larger_half_first():
-    # center_trim keeps [delta/2, delta/2 + reference) (pipeline.rs:105-113);
-    # the oracle's split pass uses the same start.
-    x = np.array([0.0, 1.0, 2.0, 3.0, 4.0])
-    delta = 5 - 3
-    assert x[delta // 2: delta // 2 + 3].tolist() == [1.0, 2.0, 3.0]
+def test_center_trim_removes_the_larger_half_first(oracle_mod):
+    # pipeline.rs:765-771: center_trim of [0, 1, 2, 3, 4] to 3 samples is [1, 2, 3]; the
+    # oracle's split pass trims each chunk's output with the same function
+    x = f32([[0.0, 1.0, 2.0, 3.0, 4.0]])
+    out = np.full((1, 5), -1.0, np.float32)
+    kept = oracle_mod.lib().orc_center_trim(P(x), 1, 5, 3, P(out))
+    assert kept == 3 and out[0, :3].tolist() == [1.0, 2.0, 3.0]
+    out = np.full((2, 4), -1.0, np.float32)  # an even excess: one sample off each end
+    x2 = f32([[0, 1, 2, 3, 4, 5], [6, 7, 8, 9, 10, 11]])
+    assert oracle_mod.lib().orc_center_trim(P(x2), 2, 6, 4, P(out)) == 4
+    assert out.tolist() == [[1, 2, 3, 4], [7, 8, 9, 10]]
 
 
 def test_shift_rng_stays_in_range(oracle_mod):
+    # pipeline.rs:773-780
     out = (ctypes.c_uint64 * 1000)()
     oracle_mod.lib().orc_shift_randint(7, 1000, 22050, out)
     assert max(out) <= 22050 and len(set(out)) > 100
+
+
+# ShiftRng (pipeline.rs:136-151): state0 = seed*A + 1; per draw state = state*A + C (mod
+# 2^64), value = (state >> 33) % (max + 1), A = 6364136223846793005,
+# C = 1442695040888963407. From seed 0x5eed_1234 (pipeline.rs:417) with max 22050 the first
+# draws are, worked out by hand with exact integer arithmetic:
+#   state0 = 0x5eed1234*A + 1 mod 2^64, state1 = state0*A + C mod 2^64, ...
+SHIFT_DRAWS_5EED1234 = [11660, 18630, 3283, 15206]
+SHIFT_DRAWS_SEED_7 = [17341, 18673, 12503]
+
+
+def test_shift_rng_first_draws_are_pinned(oracle_mod):
+    out = (ctypes.c_uint64 * 4)()
+    oracle_mod.lib().orc_shift_randint(0x5EED1234, 4, 22050, out)
+    assert list(out) == SHIFT_DRAWS_5EED1234
+    out = (ctypes.c_uint64 * 3)()
+    oracle_mod.lib().orc_shift_randint(7, 3, 22050, out)
+    assert list(out) == SHIFT_DRAWS_SEED_7
+
+
+def test_product_shift_offsets_are_the_pinned_draws():
+    # the one generator the device drivers and the rank planner use (dmx_shift_offsets)
+    import dmx
+    import shard
+
+    assert dmx.shift_offsets(4, 22050) == SHIFT_DRAWS_5EED1234
+    assert shard.shift_offsets(2, 22050) == SHIFT_DRAWS_5EED1234[:2]
+    assert shard.plan(10_584_000, 1, shifts=1).offset == SHIFT_DRAWS_5EED1234[0]
 
 
 def test_normalisation_round_trips(oracle_mod):
@@ -329,15 +363,74 @@ def test_grouped_chunks_match_one_at_a_time_bitwise(oracle_mod):
     assert np.array_equal(one, three)
 
 
-def test_half_decoding_known_answers():
-    # safetensors.rs:194-203 and 228-234: binary16 -> binary32, subnormals and infinities
-    # included. The product's F16 loader is checked against numpy's IEEE float16 upcast on
-    # the GPU (test_forward_gpu.py); these are the reference's own known answers for it.
-    import numpy as np
+def _st_blob(header, data):
+    # safetensors.rs:172-177: 8-byte little-endian header size, JSON header, data
+    import json
+    import struct
 
-    bits = np.array([0x3C00, 0xC000, 0x3800, 0x0000, 0x0001, 0x7C00, 0xFC00, 0x7E00],
-                    dtype="<u2")
-    v = bits.view(np.float16).astype(np.float32)
+    text = json.dumps(header, separators=(",", ":")).encode()
+    return struct.pack("<Q", len(text)) + text + data
+
+
+def test_half_decoding_known_answers_through_the_product_loader():
+    # safetensors.rs:194-203 and 228-234: binary16 -> binary32, subnormals and infinities
+    # included, decoded by the library's own loader (dmx_read_tensor, the path dmx_create
+    # takes for F16 checkpoints)
+    import dmx
+
+    bits = np.array([0x3C00, 0xC000, 0x3800, 0x0000, 0x0001, 0x7C00, 0xFC00, 0x7E00, 0x8000,
+                     0x7BFF, 0x03FF], dtype="<u2")
+    blob = _st_blob({"w": {"dtype": "F16", "shape": [len(bits)],
+                           "data_offsets": [0, 2 * len(bits)]}}, bits.tobytes())
+    v = dmx.read_tensor(blob, "w")
+    assert v.dtype == np.float32 and v.shape == (len(bits),)
     assert list(v[:4]) == [1.0, -2.0, 0.5, 0.0]
-    assert v[4] == np.float32(2.0 ** -24)
+    assert v[4] == np.float32(2.0 ** -24)                      # smallest subnormal
     assert np.isposinf(v[5]) and np.isneginf(v[6]) and np.isnan(v[7])
+    assert v[8] == 0.0 and np.signbit(v[8])                    # negative zero
+    assert v[9] == np.float32(65504.0)                         # largest finite
+    assert v[10] == np.float32(1023 * 2.0 ** -24)              # largest subnormal
+
+
+def test_safetensors_known_answers_through_the_product_loader():
+    # safetensors.rs:179-225: an F32 tensor round trips with its shape, __metadata__ is
+    # not a tensor, truncated data and a header longer than the file are rejected
+    import struct
+
+    import pytest
+
+    import dmx
+
+    data = np.array([1.0, 2.0, 3.0, 4.0], "<f4").tobytes()
+    blob = _st_blob({"w": {"dtype": "F32", "shape": [2, 2], "data_offsets": [0, 16]}}, data)
+    w = dmx.read_tensor(blob, "w")
+    assert w.shape == (2, 2) and w[0, 1] == 2.0 and w[1, 1] == 4.0
+    meta = _st_blob({"__metadata__": {"klass": "demucs.htdemucs.HTDemucs"},
+                     "w": {"dtype": "F32", "shape": [1], "data_offsets": [0, 4]}},
+                    np.array([0.5], "<f4").tobytes())
+    assert dmx.read_tensor(meta, "w").tolist() == [0.5]
+    with pytest.raises(dmx.DmxError, match="missing tensor __metadata__") as e:
+        dmx.read_tensor(meta, "__metadata__")
+    assert e.value.code == 2
+    short = _st_blob({"w": {"dtype": "F32", "shape": [4], "data_offsets": [0, 16]}}, b"\0" * 8)
+    with pytest.raises(dmx.DmxError, match="data_offsets") as e:
+        dmx.read_tensor(short, "w")
+    assert e.value.code == 2
+    with pytest.raises(dmx.DmxError, match="header runs past the blob"):
+        dmx.read_tensor(struct.pack("<Q", 4096), "w")
+    # a header size near 2^64 must not wrap the bounds check
+    with pytest.raises(dmx.DmxError, match="header runs past the blob"):
+        dmx.read_tensor(struct.pack("<Q", (1 << 64) - 4) + b"{}", "w")
+    # a shape whose element count overflows is rejected, not wrapped
+    huge = _st_blob({"w": {"dtype": "F32", "shape": [1 << 40, 1 << 40], "data_offsets": [0, 0]}}, b"")
+    with pytest.raises(dmx.DmxError, match="shape larger than the blob"):
+        dmx.read_tensor(huge, "w")
+
+
+def test_chunk_counts_are_the_reference_known_answers():
+    # streaming.rs:856-861 through the product's dmx_num_chunks (stride from the overlap)
+    import dmx
+
+    assert dmx.num_chunks(100, 200, 0.25) == 1
+    assert dmx.num_chunks(200, 200, 0.25) == 2
+    assert dmx.num_chunks(343980 * 2, 343980, 0.25) == 3

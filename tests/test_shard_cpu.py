@@ -109,6 +109,19 @@ def test_sharded_track_matches_single_process_driver(world, tmp_path):
     np.testing.assert_allclose(got, ref, rtol=0, atol=2e-6)
 
 
+def test_plan_rejects_overlaps_of_half_a_segment_or_more():
+    # the boundary exchange assumes stride > segment / 2: with more overlap a rank's tail
+    # can reach past its neighbour's own span (and a sample gets three contributions)
+    import pytest
+
+    import shard
+
+    for overlap in (0.5, 0.6, 0.9):
+        with pytest.raises(ValueError, match="overlap < 0.5"):
+            shard.plan(10_584_000, 8, shifts=1, overlap=overlap)
+    shard.plan(10_584_000, 8, shifts=1, overlap=0.49)
+
+
 def test_plan_partitions_every_chunk_once():
     import shard
 
