@@ -5,7 +5,10 @@ oracle's driver (GPU).
   driver — global normalisation, ShiftRng shift view, centred chunks,
   triangular overlap-add, trim, denormalisation — must reproduce the oracle's
   driver (streaming.rs:52-400, pipeline.rs:380-515) to f32 rounding.
-* End to end against the oracle's own forward, within the 1e-4 gate.
+* End to end against the oracle's own forward, within the 1e-4 gate for the
+  FP32 and TF32X3 builds and the per-stem SNR >= 60 dB gate for TF32, the
+  benchmarked build, including at the benchmark's batching (every chunk of
+  the track in one forward).
 """
 
 import numpy as np
@@ -17,15 +20,36 @@ import synth
 pytestmark = pytest.mark.gpu
 
 
-def _handle(weights, max_batch=4):
+PRECISIONS = ["FP32", "TF32", "TF32X3"]
+
+
+def _handle(weights, max_batch=4, precision="FP32"):
     import dmx
-    return dmx.Handle(synth.write_safetensors(weights), device=0, max_batch=max_batch)
+    return dmx.Handle(synth.write_safetensors(weights), device=0, max_batch=max_batch,
+                      precision=getattr(dmx, precision))
 
 
+def snr_db(ref, x):
+    """Energy SNR, 10 log10(sum ref^2 / sum (ref - x)^2)."""
+    ref = ref.astype(np.float64)
+    return 10 * np.log10(np.sum(ref ** 2) / max(np.sum((ref - x) ** 2), 1e-300))
+
+
+def _assert_stems_within_gate(got, ref, precision):
+    # FP32 / TF32X3: max-abs <= 1e-4 per stem; TF32: per-stem energy SNR >= 60 dB
+    if precision == "TF32":
+        per_stem = [snr_db(ref[s], got[s]) for s in range(4)]
+        assert min(per_stem) >= 60.0, per_stem
+    else:
+        err = np.abs(got.astype(np.float64) - ref).reshape(4, -1).max(axis=1)
+        assert err.max() <= 1e-4, err
+
+
+@pytest.mark.parametrize("precision", PRECISIONS)
 @pytest.mark.parametrize("shifts", [0, 1, 2])
-def test_device_driver_matches_oracle_driver(shifts):
+def test_device_driver_matches_oracle_driver(shifts, precision):
     w = synth.random_weights(21)
-    h = _handle(w)
+    h = _handle(w, precision=precision)
     track = synth.pink_noise(31, int(44100 * 20))
     got = h.separate_track(track[0], track[1], shifts=shifts, batch=2)
     ref = oracle.separate_with(h.forward, track, synth.SEGMENT_SAMPLES, shifts=shifts, batch=3)
@@ -34,13 +58,32 @@ def test_device_driver_matches_oracle_driver(shifts):
     assert err <= 1e-6, err
 
 
-def test_track_matches_oracle_end_to_end():
+@pytest.mark.parametrize("precision", PRECISIONS)
+def test_track_matches_oracle_end_to_end(precision):
     w = synth.random_weights(22)
     track = synth.pink_noise(32, int(44100 * 11))
-    got = _handle(w).separate_track(track[0], track[1], shifts=1)
+    got = _handle(w, precision=precision).separate_track(track[0], track[1], shifts=1)
     ref = oracle.OracleModel(w).separate(track, shifts=1)
-    err = np.abs(got.astype(np.float64) - ref).reshape(4, -1).max(axis=1)
-    assert err.max() <= 1e-4, err
+    _assert_stems_within_gate(got, ref, precision)
+
+
+def test_benchmarked_tf32_path_at_full_batch_meets_the_gate():
+    # the path bench.py times: the TF32 build, dmx_separate_track with every chunk of a
+    # pink-noise track in one forward (here 60 s: 11 chunks with shifts 1), against the
+    # oracle's own end-to-end separation; then the same build one chunk per forward
+    w = synth.random_weights(0)
+    track = synth.pink_noise(2024, int(44100 * 60))
+    import dmx
+
+    chunks = dmx.num_chunks(track.shape[1] + 22050 - dmx.shift_offsets(1)[0])
+    h = _handle(w, max_batch=chunks, precision="TF32")
+    got = h.separate_track(track[0], track[1], shifts=1, batch=chunks)
+    ref = oracle.OracleModel(w).separate(track, shifts=1, batch=4)
+    per_stem = [snr_db(ref[s], got[s]) for s in range(4)]
+    print("TF32 full-batch per-stem SNR (dB):", [round(x, 2) for x in per_stem])
+    assert min(per_stem) >= 60.0, per_stem
+    one = h.separate_track(track[0], track[1], shifts=1, batch=1)
+    assert min(snr_db(one[s], got[s]) for s in range(4)) > 100.0
 
 
 def test_progress_reports_every_chunk():
@@ -84,7 +127,7 @@ def test_pinned_host_stems_stream_back_during_the_forwards(shifts, batch):
     # samples while later batches run; the result is the device entry point's
     import torch
 
-    h = _handle(synth.random_weights(25))
+    h = _handle(synth.random_weights(25), precision="TF32")
     track = synth.pink_noise(37, int(44100 * 20))
     n = track.shape[1]
     out = torch.full((4, 2, n), float("nan")).pin_memory()
@@ -104,7 +147,7 @@ def test_pinned_host_stems_stream_back_during_the_forwards(shifts, batch):
 def test_emitted_blocks_reassemble_the_separated_track(shifts, batch):
     # Demucs::separate_streaming: ascending blocks of finished stems, each at most one
     # forward's worth (single pass), that put together are dmx_separate_track's result
-    h = _handle(synth.random_weights(26))
+    h = _handle(synth.random_weights(26), precision="TF32")
     track = synth.pink_noise(38, int(44100 * 21))
     n = track.shape[1]
     blocks = []
@@ -156,9 +199,11 @@ def test_invalid_driver_arguments_are_rejected():
     with pytest.raises(dmx.DmxError, match="zero stride"):
         h.separate_track(x[0], x[1], overlap=1.0)
     with pytest.raises(dmx.DmxError, match="transition_power"):
-        h.separate_track(x[0], x[1], transition_power=2.0)
+        h.separate_track(x[0], x[1], transition_power=0.0)
     with pytest.raises(dmx.DmxError, match="shifts"):
         h.separate_track(x[0], x[1], shifts=-1)
+    with pytest.raises(dmx.DmxError, match="model segment is 343980"):
+        h.separate_track(x[0], x[1], segment=8.0)
 
 
 def test_a_device_wait_that_runs_out_reports_timeout_and_the_handle_stays_usable():
