@@ -383,6 +383,20 @@ def run_ours(args, rank, world, local_rank):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         e2e_s = float(t.item())
 
+    # N > 1: rank 0 separates the same track alone (one handle, the same build) and the
+    # gathered stems must equal it bit for bit (batch-invariant forward, exact OLA merge)
+    match = None
+    if world > 1 and rank == 0:
+        with torch.cuda.stream(stream):
+            alone = torch.empty_like(stems)
+        h.synchronize()
+        torch.cuda.synchronize()
+        h.separate_track_device(lr.data_ptr(), n, alone.data_ptr(), shifts=shifts, overlap=overlap,
+                                batch=max(1, mine))
+        h.synchronize()
+        match = bool(torch.equal(alone, stems))
+        del alone
+
     # per-kernel device timing of one more (untimed) step for the roofline
     h.set_stage_timing(True)
     step()
@@ -415,6 +429,8 @@ def run_ours(args, rank, world, local_rank):
                             "tflops": round(v[2] / (v[0] / 1e3) / 1e12, 2) if v[0] else None,
                             "gbs": round(v[3] / (v[0] / 1e3) / 1e9, 1) if v[0] else None}
                         for k, v in sorted(stages.items(), key=lambda kv: -kv[1][0])}}
+    if match is not None:
+        line["stems_match_1gpu"] = match
     if world == 1 and args.precision == "TF32" and not args.no_fp32_class:
         line["fp32_class"] = fp32_class_leg(lr, n, p.chunks, dev)
     if rank == 0 and world == 1 and not args.no_cpu:

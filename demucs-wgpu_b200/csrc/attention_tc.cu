@@ -337,12 +337,10 @@ bool launch_attention_tc(const float* q, int ldq, int q_col, const float* kv, in
   p.ldo = ldo;
   p.scale = scale;
   p.err = err;
-  static bool attr = false;
-  if (!attr) {
+  static PerDevice attr;
+  if (attr.first())
     cudaFuncSetAttribute(attention_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                          SMEM_BYTES);
-    attr = true;
-  }
   attention_tc_kernel<<<dim3((nq + QT - 1) / QT, heads, B), 192, SMEM_BYTES, s>>>(mkv, mv, p);
   return true;
 }

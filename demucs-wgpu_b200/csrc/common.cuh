@@ -4,9 +4,25 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <atomic>
+
 #define DMX_DEVICE __device__ __forceinline__
 
 namespace dmx {
+
+// Once per device for per-context settings such as a kernel's dynamic
+// shared-memory limit: a function attribute belongs to the context of the
+// device that was current when it was set, so each GPU a process launches on
+// needs its own. `first()` is true the first time it is asked on a device.
+struct PerDevice {
+  std::atomic<uint64_t> done{0};
+  bool first() {
+    int d = 0;
+    cudaGetDevice(&d);
+    const uint64_t bit = 1ull << (d & 63);
+    return (done.fetch_or(bit) & bit) == 0;
+  }
+};
 
 constexpr int kSegment = 343980;  // int(39/5 * 44100)
 constexpr int kHop = 1024;

@@ -2,6 +2,7 @@
 // contraction). Tile 128 positions x 64 columns x 16 taps-channels, 256
 // threads, 8x4 outputs per thread, register-staged double buffering.
 #include "conv_gemm.cuh"
+#include "kernels.h"
 
 namespace dmx {
 
@@ -39,7 +40,6 @@ __global__ void __launch_bounds__(256) conv_gemm_kernel(const ConvParams p) {
   __shared__ __align__(16) float Bs[2][BK][BN];
   __shared__ int64_t s_boff[BM];
   __shared__ int s_y[BM], s_x[BM], s_b[BM];
-  __shared__ double s_stats[4];
 
   const int tid = threadIdx.x;
   const int tx = tid % 16, ty = tid / 16;
@@ -63,7 +63,6 @@ __global__ void __launch_bounds__(256) conv_gemm_kernel(const ConvParams p) {
       s_boff[tid] = 0;
     }
   }
-  if (tid < 4) s_stats[tid] = 0.0;
   __syncthreads();
 
   // Loader mapping: A element (row lm + 16*i, k lk), B float4 (row lbk, col lbn).
@@ -122,9 +121,9 @@ __global__ void __launch_bounds__(256) conv_gemm_kernel(const ConvParams p) {
   for (int j = 0; j < TN; ++j) bias[j] = p.bias[nb + j];
 
   constexpr bool kStats = EPI == EPI_RESIDUAL;
-  double ls[2] = {0.0, 0.0}, lq[2] = {0.0, 0.0};
-  const int rowlen = kStats ? p.epi_rowlen : 1;
-  const int64_t r0 = kStats ? m0 / rowlen : 0;
+  double rs[TM], rq[TM];  // per row: this thread's TN columns, in order
+#pragma unroll
+  for (int i = 0; i < TM; ++i) rs[i] = rq[i] = 0.0;
 
 #pragma unroll
   for (int i = 0; i < TM; ++i) {
@@ -198,36 +197,31 @@ __global__ void __launch_bounds__(256) conv_gemm_kernel(const ConvParams p) {
         }
     }
     if (kStats && p.epi_stats) {
-      const int slot = (int)(pos / rowlen - r0);
 #pragma unroll
       for (int j = 0; j < TN; ++j)
         if (nb + j < ncol) {
           const double d = v[j];
-          ls[slot] += d;
-          lq[slot] += d * d;
+          rs[i] += d;
+          rq[i] += d * d;
         }
     }
   }
   if (kStats && p.epi_stats) {
+    // the 16 threads of a row (tx, one half-warp) combine their column sums in a
+    // fixed butterfly; one partial per (position, column tile) goes to the
+    // scratch for the ordered reduction after the launch (no atomics)
 #pragma unroll
-    for (int s = 0; s < 2; ++s) {
-      ls[s] = warp_sum(ls[s]);
-      lq[s] = warp_sum(lq[s]);
-    }
-    if ((tid & 31) == 0) {
-      atomicAdd(&s_stats[0], ls[0]);
-      atomicAdd(&s_stats[1], lq[0]);
-      atomicAdd(&s_stats[2], ls[1]);
-      atomicAdd(&s_stats[3], lq[1]);
-    }
-    __syncthreads();
-    if (tid == 0) {
-      const int64_t rows_total = (M + rowlen - 1) / rowlen;
-      atomicAdd(&p.epi_stats[2 * r0], s_stats[0]);
-      atomicAdd(&p.epi_stats[2 * r0 + 1], s_stats[1]);
-      if (r0 + 1 < rows_total && (s_stats[2] != 0.0 || s_stats[3] != 0.0)) {
-        atomicAdd(&p.epi_stats[2 * (r0 + 1)], s_stats[2]);
-        atomicAdd(&p.epi_stats[2 * (r0 + 1) + 1], s_stats[3]);
+    for (int i = 0; i < TM; ++i) {
+#pragma unroll
+      for (int o = 8; o > 0; o >>= 1) {
+        rs[i] += __shfl_xor_sync(0xffffffffu, rs[i], o);
+        rq[i] += __shfl_xor_sync(0xffffffffu, rq[i], o);
+      }
+      const int m = ty * TM + i;
+      if (tx == 0 && s_b[m] >= 0) {
+        double* e = p.epi_rowpart + ((m0 + m) * gridDim.y + blockIdx.y) * 2;
+        e[0] = rs[i];
+        e[1] = rq[i];
       }
     }
   }
@@ -246,6 +240,8 @@ void dispatch_epi(const ConvParams& p, int epi, dim3 grid, cudaStream_t s) {
 
 }  // namespace
 
+int conv_gemm_stat_slots(int N) { return (N + BN - 1) / BN; }
+
 void launch_conv_gemm(const ConvParams& p, int pro, int epi, cudaStream_t s) {
   const int64_t M = (int64_t)p.B * p.Hq * p.Wq;
   dim3 grid((unsigned)((M + BM - 1) / BM), (unsigned)((p.N + BN - 1) / BN));
@@ -254,6 +250,9 @@ void launch_conv_gemm(const ConvParams& p, int pro, int epi, cudaStream_t s) {
     case PRO_BATCH_AFFINE: dispatch_epi<PRO_BATCH_AFFINE>(p, epi, grid, s); break;
     case PRO_ADD: dispatch_epi<PRO_ADD>(p, epi, grid, s); break;
   }
+  if (epi == EPI_RESIDUAL && p.epi_stats)
+    launch_row_stats_reduce(p.epi_rowpart, (int)grid.y, p.epi_rowlen, (int)(M / p.epi_rowlen),
+                            p.epi_stats, s);
 }
 
 }  // namespace dmx

@@ -59,6 +59,10 @@ struct ConvParams {
   // epilogue
   double* epi_stats;  // EPI_RESIDUAL: per-row (sum, sum of squares) of the output
   int epi_rowlen;
+  // scratch of the row moments: one partial (2 doubles) per output position and
+  // column tile (conv_gemm_stat_slots(N) of them; the tensor-core kernel needs
+  // tc_gemm_stat_slots(N)), reduced in a fixed order after the launch
+  double* epi_rowpart;
   const float* epi_gamma;
   const float* epi_res;
   const float* epi_emb;
@@ -81,6 +85,7 @@ struct ConvParams {
 };
 
 void launch_conv_gemm(const ConvParams& p, int pro, int epi, cudaStream_t stream);
+int conv_gemm_stat_slots(int N);
 // The first encoder convolutions (Cin 2/4, 8 taps, 48 GELU outputs, normalised
 // input, dense channels-last output; first_conv.cu). w_host: [K][48] weights
 // then the 48 biases, in host memory. False: not that shape.

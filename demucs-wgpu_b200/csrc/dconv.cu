@@ -295,13 +295,14 @@ DMX_DEVICE void stage_zq(const float* zq, float* zqs) {
 // Row moments of z for the tensor-core DConv path (three GEMMs, runtime.cu):
 // y (positions, ld) is conv1's output with its row moments in st1 (sum, sum
 // of squares); per position g = GELU(GroupNorm1(y)) and the quadratic form
-// above; per CTA one f64 sum per row, added into st2 with f64 atomics (as the
-// GEMM epilogues do). Grid (ceil(T / 256), rows). Each thread keeps its g~ in
+// above; per CTA one f64 partial per row, part[row][blockIdx.x], added in
+// order afterwards (stats.cu), so the moments do not depend on scheduling or
+// on the other rows of the launch. Grid (ceil(T / 256), rows). Each thread keeps its g~ in
 // its own column of shared memory for the rolled loop over M's rows.
 template <int C>
 __global__ void __launch_bounds__(256) dconv_zstats_kernel(const float* y, int ld, int T,
                                                            const float* n1w, const float* n1b,
-                                                           const double* st1, double* st2,
+                                                           const double* st1, double* part,
                                                            const float* zq) {
   using Z = Zq<C>;
   constexpr int HID = C / 8;
@@ -360,8 +361,9 @@ __global__ void __launch_bounds__(256) dconv_zstats_kernel(const float* y, int l
       a0 += red[2 * w];
       a1 += red[2 * w + 1];
     }
-    atomicAdd(&st2[2 * row], a0);
-    atomicAdd(&st2[2 * row + 1], a1);
+    double* e = part + ((int64_t)row * gridDim.x + blockIdx.x) * 2;
+    e[0] = a0;
+    e[1] = a1;
   }
 }
 
@@ -496,13 +498,12 @@ void set_smem(K kernel, size_t bytes) {
 template <int C>
 void launch_c(const DConvArgs& a, cudaStream_t s) {
   using M = Smem<C>;
-  static bool configured = false;
-  if (!configured) {
+  static PerDevice configured;
+  if (configured.first()) {
     set_smem(dconv_row_kernel<C>, M::kRow);
     set_smem(dconv_conv1_kernel<C>, M::kConv1);
     set_smem(dconv_conv2_kernel<C, false>, M::kConv2);
     set_smem(dconv_conv2_kernel<C, true>, M::kConv2);
-    configured = true;
   }
   if (a.T <= kTile) {
     dconv_row_kernel<C><<<a.rows, kThreads, M::kRow, s>>>(a);
@@ -516,26 +517,27 @@ void launch_c(const DConvArgs& a, cudaStream_t s) {
 
 template <int C>
 void launch_zstats_c(const float* y, int ld, int rows, int T, const float* n1w, const float* n1b,
-                     const double* st1, double* st2, const float* zq, cudaStream_t s) {
+                     const double* st1, double* st2, double* part, const float* zq,
+                     cudaStream_t s) {
   const size_t bytes = sizeof(float) * (Zq<C>::N + Zq<C>::ZL * 256);
-  static bool configured = false;
-  if (!configured) {
-    set_smem(dconv_zstats_kernel<C>, bytes);
-    configured = true;
-  }
-  dconv_zstats_kernel<C><<<dim3((T + 255) / 256, rows), 256, bytes, s>>>(y, ld, T, n1w, n1b, st1,
-                                                                         st2, zq);
+  static PerDevice configured;
+  if (configured.first()) set_smem(dconv_zstats_kernel<C>, bytes);
+  dconv_zstats_kernel<C><<<dim3(dconv_zstats_parts(T), rows), 256, bytes, s>>>(y, ld, T, n1w, n1b,
+                                                                              st1, part, zq);
+  launch_sum_partials(part, dconv_zstats_parts(T), rows, st2, s);
 }
 
 }  // namespace
 
+int dconv_zstats_parts(int T) { return (T + 255) / 256; }
+
 bool launch_dconv_zstats(int C, const float* y, int ld, int rows, int T, const float* n1w,
-                         const float* n1b, const double* st1, double* st2, const float* zq,
-                         cudaStream_t s) {
-  if (!zq || rows <= 0 || T <= 0 || ld < C / 8) return false;
+                         const float* n1b, const double* st1, double* st2, double* part,
+                         const float* zq, cudaStream_t s) {
+  if (!zq || !part || rows <= 0 || T <= 0 || ld < C / 8) return false;
   switch (C) {
-    case 192: launch_zstats_c<192>(y, ld, rows, T, n1w, n1b, st1, st2, zq, s); return true;
-    case 384: launch_zstats_c<384>(y, ld, rows, T, n1w, n1b, st1, st2, zq, s); return true;
+    case 192: launch_zstats_c<192>(y, ld, rows, T, n1w, n1b, st1, st2, part, zq, s); return true;
+    case 384: launch_zstats_c<384>(y, ld, rows, T, n1w, n1b, st1, st2, part, zq, s); return true;
     default: return false;
   }
 }

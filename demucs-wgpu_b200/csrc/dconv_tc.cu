@@ -779,12 +779,10 @@ bool launch_c(const DConvArgs& a, cudaStream_t s) {
   for (int i = 0; i < S::HID; ++i) k.b1[i] = *src++;
   for (int i = 0; i < S::HID; ++i) k.n1w[i] = *src++;
   for (int i = 0; i < S::HID; ++i) k.n1b[i] = *src++;
-  static bool configured = false;
-  if (!configured) {
+  static PerDevice configured;
+  if (configured.first())
     cudaFuncSetAttribute(dconv_tc_row_kernel<C>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                          S::SMEM);
-    configured = true;
-  }
   int dev = 0, sms = 148;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);

@@ -134,8 +134,12 @@ __global__ void ola_accumulate_kernel(const float* __restrict__ chunks, ChunkGeo
     const int64_t trim = (g.segment - len) / 2;
     const float w = weight[u];
     const float* src = chunks + (c - chunk0) * 8 * (int64_t)g.row + trim + u;
+    // product and sum rounded separately, as the reference's `acc += w * x` does
+    // (no contraction into an FMA): each contribution is round(w * x), so a sample's
+    // two contributions sum to the same bits in either order, and a sharded run's
+    // boundary merge (acc + tail) reproduces the one-GPU sum exactly
 #pragma unroll
-    for (int r = 0; r < 8; ++r) vals[r] += w * src[(int64_t)r * g.row];
+    for (int r = 0; r < 8; ++r) vals[r] = __fadd_rn(vals[r], __fmul_rn(w, src[(int64_t)r * g.row]));
   }
 #pragma unroll
   for (int r = 0; r < 8; ++r) acc[(int64_t)r * (view_hi - view_lo) + (v - view_lo)] = vals[r];
@@ -145,6 +149,8 @@ __global__ void ola_accumulate_kernel(const float* __restrict__ chunks, ChunkGeo
 // mode 1: stems = ((acc/sw) * scale) * std + mean  (shifts == 1)
 // mode 2: pass  += acc/sw                          (one of several shifts)
 // mode 3: stems = (pass * scale) * std + mean      (after the last shift)
+// Every product and sum is rounded on its own, as the reference's f32 loops
+// (streaming.rs:219-260, pipeline.rs:60-67) round them: no FMA contraction.
 __global__ void ola_finish_kernel(const float* __restrict__ acc, ChunkGeom g, int64_t trim,
                                   const float* __restrict__ weight, const float2* __restrict__ norm,
                                   float scale, int mode, float* __restrict__ pass,
@@ -155,7 +161,8 @@ __global__ void ola_finish_kernel(const float* __restrict__ acc, ChunkGeom g, in
   if (mode == 3) {
 #pragma unroll
     for (int r = 0; r < 8; ++r)
-      stems[(int64_t)r * g.length + t] = (pass[(int64_t)r * g.length + t] * scale) * nz.y + nz.x;
+      stems[(int64_t)r * g.length + t] =
+          __fadd_rn(__fmul_rn(__fmul_rn(pass[(int64_t)r * g.length + t], scale), nz.y), nz.x);
     return;
   }
   const int64_t v = t + trim;
@@ -173,9 +180,10 @@ __global__ void ola_finish_kernel(const float* __restrict__ acc, ChunkGeom g, in
 #pragma unroll
   for (int r = 0; r < 8; ++r) {
     const float y = acc[(int64_t)r * g.view_length + v] / sw;
-    if (mode == 0) stems[(int64_t)r * g.length + t] = y * nz.y + nz.x;
-    else if (mode == 1) stems[(int64_t)r * g.length + t] = (y * scale) * nz.y + nz.x;
-    else pass[(int64_t)r * g.length + t] += y;
+    if (mode == 0) stems[(int64_t)r * g.length + t] = __fadd_rn(__fmul_rn(y, nz.y), nz.x);
+    else if (mode == 1)
+      stems[(int64_t)r * g.length + t] = __fadd_rn(__fmul_rn(__fmul_rn(y, scale), nz.y), nz.x);
+    else pass[(int64_t)r * g.length + t] = __fadd_rn(pass[(int64_t)r * g.length + t], y);
   }
 }
 

@@ -10,9 +10,17 @@
 
 using namespace dmx;
 
-void dmx_handle::gemm(const ConvParams& p, int pro, int epi, const char* tag,
+void dmx_handle::gemm(const ConvParams& p0, int pro, int epi, const char* tag,
                       const Packed* pk) {
+  ConvParams p = p0;
+  if (p.epi_stats && !p.epi_rowpart) {
+    // scratch of the row moments, sized for either kernel's partials
+    const int64_t M = (int64_t)p.B * p.Hq * p.Wq;
+    const int slots = std::max(tc_gemm_stat_slots(p.N), conv_gemm_stat_slots(p.N));
+    p.epi_rowpart = dalloc((size_t)M * slots * 2);
+  }
   ++launches;
+  if (p.epi_stats && epi == EPI_RESIDUAL) ++launches;  // the ordered reduction of the moments
   if (!live()) return;
   if (epi == EPI_RESIDUAL && p.epi_stats &&
       p.epi_rowlen < 128)
@@ -139,6 +147,8 @@ bool dmx_handle::build_tc(const ConvParams& p, const Packed& pk, TcOperandA& a, 
   t.o_off = p.o_off;
   t.epi_stats = p.epi_stats;
   t.epi_rowlen = p.epi_rowlen;
+  t.epi_rowpart = p.epi_rowpart;
+  t.epi_nslots = tc_gemm_stat_slots(p.N);
   t.epi_gamma = p.epi_gamma;
   t.epi_res = p.epi_res;
   t.epi_emb = p.epi_emb;
@@ -232,7 +242,8 @@ void dconv_gemm(dmx_handle* h, const ConvParams& p, int epi, const Packed& pk, c
 // and its row moments; the row moments of z from g = GELU(GroupNorm1(y)) by
 // the quadratic form (dconv.cu); conv2 with GELU(GroupNorm1(y)) applied to
 // each A tile by the converter warps and a GroupNorm2 + GLU + LayerScale +
-// residual epilogue into x. Moments are f64 atomics per row.
+// residual epilogue into x. Moments are f64 partials per position (conv1) or
+// per block (z), added in a fixed order per row.
 void run_dconv_gemm(dmx_handle* h, const DConvFull& dc, float* x, int rows, int T,
                     bool round_out) {
   const int C = dc.C, hid = dc.hidden;
@@ -240,12 +251,13 @@ void run_dconv_gemm(dmx_handle* h, const DConvFull& dc, float* x, int rows, int 
   const int kg = dc.layer[0].conv2.K;  // y row width = conv2's padded K
   float* y = h->falloc((size_t)positions * kg);
   double* st = h->dalloc((size_t)rows * 4);
+  double* ypart = h->dalloc((size_t)positions * tc_gemm_stat_slots(dc.layer[0].conv1.N) * 2);
+  double* zpart = h->dalloc((size_t)rows * dconv_zstats_parts(T) * 2);
   for (int d = 0; d < 2; ++d) {
     const DConvLayerW& L = dc.layer[d];
     h->mark("dconv.gemm" + std::to_string(C), 10.0 * positions * C * hid, 8.0 * positions * C);
-    h->launches += 3;
+    h->launches += 5;
     if (!h->live()) continue;
-    CK(cudaMemsetAsync(st, 0, (size_t)rows * 4 * sizeof(double), h->stream));
     TcParams ext;
     std::memset(&ext, 0, sizeof(ext));
     {  // conv1: x (rows, T, C) -> y (rows, T, kg), the first hid columns
@@ -254,6 +266,7 @@ void run_dconv_gemm(dmx_handle* h, const DConvFull& dc, float* x, int rows, int 
       set_output(p, y, rows, 1, T, kg);
       p.epi_stats = st;
       p.epi_rowlen = T;
+      p.epi_rowpart = ypart;
       dconv_gemm(h, p, EPI_STORE_STATS, L.conv1, ext);
     }
     ConvParams q = base_params(L.conv2, h->wdev);
@@ -268,7 +281,7 @@ void run_dconv_gemm(dmx_handle* h, const DConvFull& dc, float* x, int rows, int 
     ext.a_gb = h->W(L.n1b.off);
     // moments of z from g alone (v.g~, g~'Mg~), without a conv2 pass
     if (!launch_dconv_zstats(C, y, kg, rows, T, h->W(L.n1w.off), h->W(L.n1b.off), st, st + 2 * rows,
-                             h->W(L.zq_off), h->stream))
+                             zpart, h->W(L.zq_off), h->stream))
       throw Error(DMX_ERR_INVALID, "dconv: moments of z for this width");
     q.epi_stats = nullptr;  // the output
     ext.epi_nstats = st + 2 * rows;
@@ -444,7 +457,6 @@ void xf_tail(dmx_handle* h, const LayerW& L, float* X, int B, int n, const XfBuf
   ++h->launches;
   xf_gemm(h, "xf.ffn1", L.lin1, bb.xn, B, n, bb.hid, EPI_GELU, nullptr, nullptr, nullptr,
           xf_rounded(h));
-  h->zero(bb.stats, (size_t)B * 2 * sizeof(double));
   xf_gemm(h, "xf.ffn2", L.lin2, bb.hid, B, n, X, EPI_RESIDUAL, X, h->W(L.g2.off), bb.stats);
   h->mark("xf.groupnorm", 0.0, 8.0 * B * n * 512);
   if (h->live()) launch_group_norm_apply(X, B, n, bb.stats, h->W(L.now.off), h->W(L.nob.off), h->stream);
@@ -509,19 +521,19 @@ void forward(dmx_handle* h, const float* mix, int G, float* out) {
   cudaStream_t s = h->stream;
   const float2* tw = reinterpret_cast<const float2*>(h->W(m.tw_off));
 
-  // (a) spectrogram + moments
-  double* mom = h->dalloc((size_t)G * 4);
+  // (a) spectrogram + moments (per-segment partials, added in a fixed order)
+  double* part_f = h->dalloc((size_t)G * kFrames * 2);
+  double* part_t = h->dalloc((size_t)G * kWaveMomentBlocks * 2);
   float4* norm = static_cast<float4*>(h->alloc((size_t)G * 2 * sizeof(float4)));
   float4* norm_f = norm;
   float4* norm_t = norm + G;
   float* X = h->falloc((size_t)G * kBins * kFrames * 4);
-  h->zero(mom, (size_t)G * 4 * sizeof(double));
   h->mark("spec.stft", 0.0, 4.0 * G * (2.0 * L + (double)kBins * kFrames * 4));
   if (h->live()) {
-    launch_stft_cac(mix, G, h->W(m.window.off), tw, X, mom, s);
-    launch_wave_moments(mix, G, 2LL * L, mom + 2 * G, s);
-    launch_norm_finalize(mom, (double)kBins * kFrames * 4, G, norm_f, s);
-    launch_norm_finalize(mom + 2 * G, 2.0 * L, G, norm_t, s);
+    launch_stft_cac(mix, G, h->W(m.window.off), tw, X, part_f, s);
+    launch_wave_moments(mix, G, 2LL * L, part_t, s);
+    launch_norm_finalize(part_f, kFrames, (double)kBins * kFrames * 4, G, norm_f, s);
+    launch_norm_finalize(part_t, kWaveMomentBlocks, 2.0 * L, G, norm_t, s);
     h->after("spectrogram");
   }
   h->launches += 4;

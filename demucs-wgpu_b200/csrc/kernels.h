@@ -10,11 +10,16 @@ namespace dmx {
 // Sets the thread-local message dmx_last_error() returns (abi.cu).
 void set_last_error(const char* msg);
 
-// spectral.cu
+// spectral.cu. The moments come as partials (sum, sum of squares; f64):
+// launch_stft_cac writes B * kFrames of them (one per segment and frame),
+// launch_wave_moments B * kWaveMomentBlocks; launch_norm_finalize adds a
+// segment's `nparts` partials in order.
+constexpr int kWaveMomentBlocks = 148;
 void launch_stft_cac(const float* mix, int B, const float* window, const float2* tw, float* out,
                      double* stats, cudaStream_t s);
 void launch_wave_moments(const float* mix, int B, int64_t n, double* stats, cudaStream_t s);
-void launch_norm_finalize(const double* stats, double count, int B, float4* norm, cudaStream_t s);
+void launch_norm_finalize(const double* part, int nparts, double count, int B, float4* norm,
+                          cudaStream_t s);
 void launch_istft(const float* spec, const float4* norm, const float* window, const float2* tw,
                   const float* envelope, const float* time_branch, const float4* norm_t, float* out,
                   int B, cudaStream_t s);
@@ -71,12 +76,14 @@ inline int dconv_tc_slot(int hid, int i) {
 int dconv_tiles(int T);
 bool dconv_row_fused(int T);
 bool launch_dconv(const DConvArgs& a, cudaStream_t s);
-// Row moments of z = conv2(GELU(GroupNorm1(y))) added into st2 (rows x 2
-// doubles, zeroed by the caller) from y (rows*T, ld) and its moments st1, by
-// the quadratic form over zq (DConvArgs::zq_dev); C 192 or 384 (dconv.cu).
+// Row moments of z = conv2(GELU(GroupNorm1(y))) into st2 (rows x 2 doubles)
+// from y (rows*T, ld) and its moments st1, by the quadratic form over zq
+// (DConvArgs::zq_dev); C 192 or 384 (dconv.cu). `part` holds
+// rows * dconv_zstats_parts(T) partials (2 doubles each), added in order.
+int dconv_zstats_parts(int T);
 bool launch_dconv_zstats(int C, const float* y, int ld, int rows, int T, const float* n1w,
-                         const float* n1b, const double* st1, double* st2, const float* zq,
-                         cudaStream_t s);
+                         const float* n1b, const double* st1, double* st2, double* part,
+                         const float* zq, cudaStream_t s);
 bool dconv_tc_supported(int C, int T);
 // work items per row of the tensor-core DConv (rows of more than one need
 // part1/part2 and y: rows*T*dconv_tc_ystride(C) floats)
@@ -118,6 +125,14 @@ void launch_ola_finish(const float* acc, int64_t length, int64_t shift_offset, i
                        int segment, int64_t stride, const float* weight, const float2* norm,
                        float scale, int mode, float* pass, float* stems, cudaStream_t s,
                        int64_t t_lo = 0, int64_t t_hi = -1);
+
+// stats.cu — fixed-order moment reductions. part is (rows * rowlen positions,
+// nslots, 2) doubles; stats[row] = (sum, sum of squares) over the row's
+// positions and slots, in an order fixed by the position inside the row.
+void launch_row_stats_reduce(const double* part, int nslots, int64_t rowlen, int rows,
+                             double* stats, cudaStream_t s);
+// stats[row] = sum over k < nparts of part[row][k] (2 doubles each), in order.
+void launch_sum_partials(const double* part, int nparts, int rows, double* stats, cudaStream_t s);
 
 // multi.cu — acc[r * ld + c] += tail[r * width + c] (rows x width), the
 // boundary merge of the multi-GPU track driver.

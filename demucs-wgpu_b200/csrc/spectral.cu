@@ -2,9 +2,13 @@
 //  * stft_cac: reflect pad (spec.rs:62-113, 204-236) + periodic Hann +
 //    4096-point FFT + 1/64 normalisation + CaC packing (spec.rs:240-254),
 //    written channels-last (b, f, t, 4), with the per-segment moments of the
-//    packed spectrogram accumulated in f64 on the way out (host.rs:523-543).
-//  * wave_moments: per-segment moments of the waveform.
-//  * norm_finalize: mean / unbiased std / 1/(1e-5+std) per segment.
+//    packed spectrogram formed in f64 on the way out (host.rs:523-543): one
+//    partial per (segment, frame).
+//  * wave_moments: per-segment moments of the waveform, one partial per
+//    (segment, block of a fixed grid).
+//  * norm_finalize: adds a segment's partials in order, then mean / unbiased
+//    std / 1/(1e-5+std). No atomics: a segment's moments do not depend on the
+//    other segments of the batch or on scheduling.
 //  * istft: denormalise (host.rs:466-469), unpack (spec.rs:268-300), zero
 //    Nyquist bin and border frames (spec.rs:312-340), inverse FFT x window x
 //    1/64, overlap-add divided by the window-squared envelope, crop
@@ -43,19 +47,24 @@ __global__ void wave_moments_kernel(const float* __restrict__ mix, int64_t n,
     s = warp_sum(s);
     q = warp_sum(q);
     if (threadIdx.x == 0) {
-      atomicAdd(&stats[2 * b], s);
-      atomicAdd(&stats[2 * b + 1], q);
+      stats[((int64_t)b * gridDim.x + blockIdx.x) * 2] = s;
+      stats[((int64_t)b * gridDim.x + blockIdx.x) * 2 + 1] = q;
     }
   }
 }
 
 // norm[b] = {mean, 1/(1e-5 + std), std, -mean/std} (host.rs:250-261, 466-469;
 // ops.rs:1494-1509, 1585-1590).
-__global__ void norm_finalize_kernel(const double* __restrict__ stats, double count, int B,
-                                     float4* __restrict__ norm) {
+__global__ void norm_finalize_kernel(const double* __restrict__ part, int nparts, double count,
+                                     int B, float4* __restrict__ norm) {
   const int b = blockIdx.x * blockDim.x + threadIdx.x;
   if (b >= B) return;
-  const double sum = stats[2 * b], sq = stats[2 * b + 1];
+  double sum = 0.0, sq = 0.0;
+  const double* e = part + (int64_t)b * nparts * 2;
+  for (int k = 0; k < nparts; ++k) {
+    sum += e[2 * k];
+    sq += e[2 * k + 1];
+  }
   const double mean = sum / count;
   const double var = fmax((sq - sum * sum / count) / (count - 1.0), 0.0);
   const float meanf = (float)mean;
@@ -244,8 +253,8 @@ __global__ void __launch_bounds__(256) stft_cac_kernel(const float* __restrict__
     s = warp_sum(s);
     q = warp_sum(q);
     if (tid == 0) {
-      atomicAdd(&stats[2 * b], s);
-      atomicAdd(&stats[2 * b + 1], q);
+      stats[((int64_t)b * kFrames + t) * 2] = s;
+      stats[((int64_t)b * kFrames + t) * 2 + 1] = q;
     }
   }
 }
@@ -380,23 +389,21 @@ void launch_stft_cac(const float* mix, int B, const float* window, const float2*
 }
 
 void launch_wave_moments(const float* mix, int B, int64_t n, double* stats, cudaStream_t s) {
-  wave_moments_kernel<<<dim3(148, B), 512, 0, s>>>(mix, n, stats);
+  wave_moments_kernel<<<dim3(kWaveMomentBlocks, B), 512, 0, s>>>(mix, n, stats);
 }
 
-void launch_norm_finalize(const double* stats, double count, int B, float4* norm,
+void launch_norm_finalize(const double* part, int nparts, double count, int B, float4* norm,
                           cudaStream_t s) {
-  norm_finalize_kernel<<<(B + 63) / 64, 64, 0, s>>>(stats, count, B, norm);
+  norm_finalize_kernel<<<(B + 63) / 64, 64, 0, s>>>(part, nparts, count, B, norm);
 }
 
 void launch_istft(const float* spec, const float4* norm, const float* window, const float2* tw,
                   const float* envelope, const float* time_branch, const float4* norm_t, float* out,
                   int B, cudaStream_t s) {
-  static bool configured = false;
-  if (!configured) {
+  static PerDevice configured;
+  if (configured.first())
     cudaFuncSetAttribute(istft_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                          (int)kIstftSmem);
-    configured = true;
-  }
   // hops 3 .. 339 of the centred signal hold the segment's samples
   const int groups = (337 + kIstftHops - 1) / kIstftHops;
   istft_kernel<<<dim3(4, groups, B), kIstftThreads, kIstftSmem, s>>>(spec, norm, window, tw,

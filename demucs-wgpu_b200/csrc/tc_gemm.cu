@@ -4,6 +4,7 @@
 #include <algorithm>
 #include <mutex>
 
+#include "kernels.h"
 #include "tc_common.cuh"
 #include "tc_gemm.cuh"
 
@@ -62,7 +63,6 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* acc_full = conv + STAGES;   // [2]
   uint64_t* acc_empty = acc_full + 2;   // [2]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
-  __shared__ double s_stats[4];
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   // a previous launch on this stream gave up: do nothing (uniform across the CTA)
@@ -80,7 +80,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
-  if (threadIdx.x < 4) s_stats[threadIdx.x] = 0.0;
   if (warp == 1) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
                      smem_u32(tmem_slot)),
@@ -551,41 +550,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
       asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(&acc_empty[acc]))
                    : "memory");
-      if (kStats && p.epi_stats) {
-        // rows of one tile span at most two statistic rows (rowlen >= 128)
-        int64_t first;
-        if (p.mode == TC_2D) {
-          const int64_t p0 = ((int64_t)tb * p.Hq + ty0) * p.Wq + tx0;
-          first = p0 / p.epi_rowlen;
-        } else if (p.mode == TC_1D) {
-          first = ((int64_t)tb * p.Wq + tx0) / p.epi_rowlen;
-        } else {
-          first = m0 / p.epi_rowlen;
-        }
-        const int slot = valid ? (int)(pos / p.epi_rowlen - first) : 0;
-        double s0 = slot == 0 ? ls : 0.0, q0 = slot == 0 ? lq : 0.0;
-        double s1 = slot == 1 ? ls : 0.0, q1 = slot == 1 ? lq : 0.0;
-        s0 = warp_sum(s0);
-        q0 = warp_sum(q0);
-        s1 = warp_sum(s1);
-        q1 = warp_sum(q1);
-        if (lane == 0) {
-          atomicAdd(&s_stats[0], s0);
-          atomicAdd(&s_stats[1], q0);
-          atomicAdd(&s_stats[2], s1);
-          atomicAdd(&s_stats[3], q1);
-        }
-        asm volatile("bar.sync 1, 256;" ::: "memory");
-        if (warp == 6 && lane == 0) {
-          atomicAdd(&p.epi_stats[2 * first], s_stats[0]);
-          atomicAdd(&p.epi_stats[2 * first + 1], s_stats[1]);
-          if (s_stats[2] != 0.0 || s_stats[3] != 0.0) {
-            atomicAdd(&p.epi_stats[2 * (first + 1)], s_stats[2]);
-            atomicAdd(&p.epi_stats[2 * (first + 1) + 1], s_stats[3]);
-          }
-          s_stats[0] = s_stats[1] = s_stats[2] = s_stats[3] = 0.0;
-        }
-        asm volatile("bar.sync 1, 256;" ::: "memory");
+      if (kStats && p.epi_rowpart && valid) {
+        // this thread's share of the row's moments: one partial per position and
+        // (column tile, epilogue half), reduced in a fixed order after the launch
+        // (stats.cu), so no atomics and no dependence on the tile's neighbours
+        double* e = p.epi_rowpart + (pos * p.epi_nslots + (n0 / BN) * 2 + hh) * 2;
+        e[0] = ls;
+        e[1] = lq;
       }
     }
   }
@@ -607,12 +578,10 @@ void launch_cfg(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap&
   const int smem = Smem<BN, BK, STAGES, SPLIT>::TOTAL;
 #define DMX_TC_CASE(E)                                                                        \
   case E: {                                                                                   \
-    static bool attr = false;                                                                 \
-    if (!attr) {                                                                              \
+    static PerDevice attr;                                                                    \
+    if (attr.first())                                                                         \
       cudaFuncSetAttribute(tc_gemm_kernel<BN, BK, STAGES, E, SPLIT>,                          \
-                           cudaFuncAttributeMaxDynamicSharedMemorySize, smem);                \
-      attr = true;                                                                            \
-    }                                                                                         \
+                           cudaFuncAttributeMaxDynamicSharedMemorySize, smem);                                                                                         \
     tc_gemm_kernel<BN, BK, STAGES, E, SPLIT><<<grid, kThreads, smem, s>>>(ma, mb, mblo, p);   \
     break;                                                                                    \
   }
@@ -631,6 +600,8 @@ void launch_cfg(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap&
 
 int pick_bn(int N) { return N <= 64 ? 64 : (N <= 128 ? 128 : 256); }
 
+bool stats_epi(int epi) { return epi == EPI_RESIDUAL || epi == EPI_STORE_STATS || epi == EPI_STATS; }
+
 int sm_count() {
   static int count[64] = {0};
   int dev = 0;
@@ -646,8 +617,13 @@ int sm_count() {
 
 }  // namespace
 
+int tc_gemm_stat_slots(int N) { return (N + pick_bn(N) - 1) / pick_bn(N) * 2; }
+
 bool tc_gemm_supported(const TcOperandA& a, const TcParams& p) {
   if (!tensor_map_encoder()) return false;
+  // row moments: positions of one statistic row are contiguous in the TC_ROWS
+  // and TC_1D orders (not across the 8-row boxes of TC_2D)
+  if (p.epi_stats && (p.mode == TC_2D || !p.epi_rowpart || p.epi_rowlen <= 0)) return false;
   const int bk = (p.Cin % 32 == 0) ? 32 : (p.Cin % 16 == 0 ? 16 : 0);
   if (bk == 0) return false;
   if (p.mode == TC_2D || p.mode == TC_1D) {
@@ -724,6 +700,11 @@ void launch_tc_gemm(const TcOperandA& a, const float* wk, const float* wk_lo, co
   } else {
     if (bk == 32) launch_cfg<256, 32, 4, false>(ma, mb, mblo, p, epi, grid, s);
     else launch_cfg<256, 16, 6, false>(ma, mb, mblo, p, epi, grid, s);
+  }
+  if (p.epi_stats && stats_epi(epi)) {
+    const int64_t positions = (int64_t)p.B * p.Hq * p.Wq;
+    launch_row_stats_reduce(p.epi_rowpart, p.epi_nslots, p.epi_rowlen,
+                            (int)(positions / p.epi_rowlen), p.epi_stats, s);
   }
 }
 

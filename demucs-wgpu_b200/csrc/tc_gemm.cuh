@@ -36,8 +36,10 @@ struct TcParams {
   // output addressing and epilogue, as in ConvParams
   float* out;
   int64_t o_bs, o_ys, o_xs, o_off;
-  double* epi_stats;
+  double* epi_stats;   // row moments (sum, sum of squares) per statistic row of epi_rowlen positions
   int epi_rowlen;
+  double* epi_rowpart;  // scratch: positions x tc_gemm_stat_slots(N) partials (2 doubles each)
+  int epi_nslots;
   const float* epi_gamma;
   const float* epi_res;
   const float* epi_emb;
@@ -79,6 +81,8 @@ struct TcOperandA {
   int64_t sb, sh, sw;       // element strides of b, h, w (channels contiguous)
 };
 bool tc_gemm_supported(const TcOperandA& a, const TcParams& p);
+// Partials per output position of the row-moment epilogues (two per column tile).
+int tc_gemm_stat_slots(int N);
 // wk: K-major weights rounded to nearest tf32; wk_lo: their residuals
 // (w - tf32(w)) for the 3xTF32 split, or null for single-pass TF32.
 void launch_tc_gemm(const TcOperandA& a, const float* wk, const float* wk_lo, const TcParams& p,

@@ -230,12 +230,10 @@ void launch_flash_attention(const float* q, int ldq, const float* k, const float
                             float* o, int ldo, int B, int heads, int nq, int nk, float scale,
                             cudaStream_t s) {
   const size_t smem = sizeof(float) * (AD * (AQ + 4) + AD * (AK + 4) + AK * AD + AK * (AQ + 4));
-  static bool configured = false;
-  if (!configured) {
+  static PerDevice configured;
+  if (configured.first())
     cudaFuncSetAttribute(flash_attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                          (int)smem);
-    configured = true;
-  }
   flash_attention_kernel<<<dim3((nq + AQ - 1) / AQ, heads, B), 256, smem, s>>>(
       q, ldq, k, v, ldkv, o, ldo, nq, nk, scale);
 }

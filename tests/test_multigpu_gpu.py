@@ -1,17 +1,18 @@
-"""Chunk-sharded separation over 2 GPUs (NCCL) reproduces the 1-GPU result.
+"""Chunk-sharded separation over 2, 4 or 8 GPUs (NCCL) reproduces the 1-GPU result.
 
 Each rank forwards its contiguous chunk range (dmx_track_shard), the boundary
 tail crosses to the neighbour, each rank finalises the samples it owns
 (dmx_track_finish) and rank 0 gathers the stems, which are compared with
-dmx_separate_track on one GPU. Skipped with fewer than two visible GPUs.
+dmx_separate_track on one GPU. Each rank count runs when that many GPUs are
+visible.
 
 The single-process multi-GPU entry point (dmx_separate_track_multi) is tested
 with 2-4 handles placed on the visible GPUs in turn, so it also runs on one GPU.
 
-The OLA sums are order-independent, but the forward reduces its per-segment
-moments with f64 atomics whose order varies from run to run, so the two runs
-agree to that rounding (the same > 100 dB bar as the batch-independence
-test), not bit for bit.
+Both must match bit for bit: a segment's forward output does not depend on
+which chunks share its forward (every per-segment moment is reduced in an
+order fixed by the position inside the segment), and every overlap-add sample
+has at most two contributions, whose IEEE sum is the same in either order.
 """
 
 import os
@@ -51,7 +52,7 @@ def _worker(rank, world, port, out_path):
     dist.init_process_group("nccl", rank=rank, world_size=world,
                             timeout=datetime.timedelta(seconds=120),
                             device_id=torch.device(f"cuda:{rank}"))
-    n = 44100 * SECONDS
+    n = 44100 * max(SECONDS, 6 * world)  # at least one chunk per rank
     track = synth.pink_noise(7, n)
     p = shard.plan(n, world, shifts=1)
     me = p.rank(rank)
@@ -82,18 +83,16 @@ def _worker(rank, world, port, out_path):
     dist.destroy_process_group()
 
 
-def test_two_gpu_sharding_matches_one_gpu(tmp_path):
-    if torch.cuda.device_count() < 2:
-        pytest.skip("needs two GPUs")
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_sharding_over_gpus_matches_one_gpu(world, tmp_path):
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
     out_path = str(tmp_path / "stems.npy")
-    mp.start_processes(_worker, args=(2, _free_port(), out_path), nprocs=2, join=True,
+    mp.start_processes(_worker, args=(world, _free_port(), out_path), nprocs=world, join=True,
                        start_method="spawn")
     sharded, single = np.load(out_path)
     assert np.isfinite(sharded).all()
-    err = np.abs(sharded.astype(np.float64) - single)
-    rms = np.sqrt(np.mean(single.astype(np.float64) ** 2))
-    print(f"2-GPU vs 1-GPU: max-abs {err.max():.3e}, mean-abs SNR {-20 * np.log10(max(err.mean(), 1e-30) / rms):.1f} dB")
-    assert err.max() == 0 or -20 * np.log10(err.mean() / rms) > 100
+    assert np.array_equal(sharded, single)
 
 
 @pytest.mark.parametrize("ranks,shifts,batch", [(2, 1, 2), (3, 0, 1), (4, 1, 4)])
@@ -113,8 +112,6 @@ def test_single_process_multi_handle_driver_matches_one_handle(ranks, shifts, ba
     got = dmx.separate_track_multi(hs, track[0], track[1], shifts=shifts, batch=batch)
     ref = hs[0].separate_track(track[0], track[1], shifts=shifts, batch=batch)
     assert np.isfinite(got).all()
-    err = np.abs(got.astype(np.float64) - ref)
-    rms = np.sqrt(np.mean(ref.astype(np.float64) ** 2))
-    assert err.max() == 0 or -20 * np.log10(err.mean() / rms) > 100, err.max()
+    assert np.array_equal(got, ref)
     for h in hs:
         h.close()

@@ -36,12 +36,24 @@ def _padded_chunk(mix, start, chunk):
     return out
 
 
-def _split_pass_queue_one_ahead(h, track, batch):
-    """stream_split_pass_meta's loop (shifts 0): start(n) before collect(n - 1)."""
+def _normalised(track):
     mean, std = ctypes.c_float(), ctypes.c_float()
     oracle.lib().orc_scan_norm(oracle.ptr(track), 2, ctypes.c_int64(track.shape[1]),
                                ctypes.byref(mean), ctypes.byref(std))
-    mix = ((track - mean.value) / std.value).astype(np.float32)
+    return ((track - mean.value) / std.value).astype(np.float32), mean.value, std.value
+
+
+def _groups(track, batch):
+    mix, _, _ = _normalised(track)
+    n = mix.shape[1]
+    starts = list(range(0, n, int(0.75 * SEG)))
+    return [np.stack([_padded_chunk(mix, s, min(n - s, SEG)) for s in starts[i:i + batch]])
+            for i in range(0, len(starts), batch)]
+
+
+def _split_pass_queue_one_ahead(h, track, batch):
+    """stream_split_pass_meta's loop (shifts 0): start(n) before collect(n - 1)."""
+    mix, mean, std = _normalised(track)
     n = mix.shape[1]
     stride = int(0.75 * SEG)
     weight = np.empty(SEG, np.float32)
@@ -72,7 +84,7 @@ def _split_pass_queue_one_ahead(h, track, batch):
             trim = (SEG - c) // 2
             acc[:, s:s + c] += weight[:c] * y[slot].reshape(8, SEG)[:, trim:trim + c]
             wsum[s:s + c] += weight[:c]
-    stems = (acc / wsum) * std.value + mean.value
+    stems = (acc / wsum) * std + mean
     return stems.reshape(4, 2, n), outs
 
 
@@ -81,6 +93,10 @@ def test_queue_one_ahead_loop_matches_the_track_driver():
     track = synth.pink_noise(92, int(44100 * 30))  # 6 chunks: three groups of two
     got, outs = _split_pass_queue_one_ahead(h, track, batch=2)
     assert len(outs) == 3
+    # each queued group's output is the synchronous forward's, bit for bit
+    mix_groups = _groups(track, batch=2)
+    for y, g in zip(outs, mix_groups):
+        assert np.array_equal(y, h.forward(g))
     ref = h.separate_track(track[0], track[1], shifts=0, batch=2)
     scale = np.abs(ref).max()
     err = np.abs(got.astype(np.float64) - ref).max()
@@ -102,9 +118,8 @@ def test_two_forwards_in_flight_return_their_own_results_in_any_order():
         h.forward_start(a)
     got_b = h.forward_collect(pb)  # collected out of order
     got_a = h.forward_collect(pa)
-    assert np.abs(got_a.astype(np.float64) - ya).max() <= 1e-6
-    assert np.abs(got_b.astype(np.float64) - yb).max() <= 1e-6
+    assert np.array_equal(got_a, ya) and np.array_equal(got_b, yb)
     # both slots are free again
     pc = h.forward_start(b)
-    assert np.abs(h.forward_collect(pc).astype(np.float64) - yb).max() <= 1e-6
+    assert np.array_equal(h.forward_collect(pc), yb)
     h.close()

@@ -83,7 +83,7 @@ def test_benchmarked_tf32_path_at_full_batch_meets_the_gate():
     print("TF32 full-batch per-stem SNR (dB):", [round(x, 2) for x in per_stem])
     assert min(per_stem) >= 60.0, per_stem
     one = h.separate_track(track[0], track[1], shifts=1, batch=1)
-    assert min(snr_db(one[s], got[s]) for s in range(4)) > 100.0
+    assert np.array_equal(one, got)  # batch composition changes no output bit
 
 
 def test_progress_reports_every_chunk():
@@ -162,10 +162,7 @@ def test_emitted_blocks_reassemble_the_separated_track(shifts, batch):
         assert len(blocks) > 1
         assert max(b.shape[1] for _, b in blocks) <= batch * int(0.75 * synth.SEGMENT_SAMPLES)
     got = np.concatenate([b for _, b in blocks], axis=1).reshape(4, 2, n)
-    # two runs of the forward may differ in the last bits (f64 atomics in the
-    # spectrogram moments), as in the other driver comparisons
-    err = np.abs(got.astype(np.float64) - ref).max()
-    assert err <= 1e-6, err
+    assert np.array_equal(got, ref)
 
 
 @pytest.mark.parametrize("n", [1, 1000, 22050, synth.SEGMENT_SAMPLES + 1])
