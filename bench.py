@@ -263,6 +263,43 @@ def run_reference(args, rank, world):
     print(json.dumps(line), flush=True)
 
 
+class SharedHostStems:
+    """(8, n) float32 host stems in a shared-memory file that every rank maps and
+    registers as pinned memory: each rank copies its own span of the result over its
+    own PCIe link, and the whole result is in host memory once all ranks are done
+    (the multi-process counterpart of dmx_separate_track_multi's per-rank copies)."""
+
+    def __init__(self, dist, rank, n):
+        import torch
+
+        self.path = f"/dev/shm/dmx_bench_{os.environ.get('MASTER_PORT', '0')}_stems"
+        self.rank = rank
+        nbytes = 8 * n * 4
+        if rank == 0:
+            with open(self.path, "wb") as f:
+                f.truncate(nbytes)
+        dist.barrier()
+        self.array = np.memmap(self.path, dtype=np.float32, mode="r+", shape=(8, n))
+        self.tensor = torch.from_numpy(self.array)
+        rc = torch.cuda.cudart().cudaHostRegister(self.tensor.data_ptr(), nbytes, 0)
+        self.registered = int(rc) == 0
+
+    def close(self, dist):
+        import torch
+
+        if self.registered:
+            torch.cuda.cudart().cudaHostUnregister(self.tensor.data_ptr())
+        del self.tensor
+        del self.array
+        dist.barrier()
+        if self.rank == 0:
+            os.unlink(self.path)
+
+
+def _event_ms(torch, events):
+    return [round(a.elapsed_time(b), 3) for a, b in zip(events, events[1:])]
+
+
 def run_ours(args, rank, world, local_rank):
     import datetime
 
@@ -278,6 +315,10 @@ def run_ours(args, rank, world, local_rank):
 
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180),
                                 device_id=torch.device(f"cuda:{dev}"))
+    if args.workload == "bag":
+        return run_bag(args, rank, world, dev, dist)
+    if args.workload == "batch":
+        return run_batch(args, rank, world, dev, dist)
     seconds = args.seconds
     n = int(seconds * SR)
     track = synth.pink_noise(2024, n)
@@ -301,24 +342,54 @@ def run_ours(args, rank, world, local_rank):
         mix_norm = torch.empty_like(lr)
         mean_std = torch.empty(2, dtype=torch.float32, device=cuda)
         acc = torch.empty((8, p.view_length), dtype=torch.float32, device=cuda)
+        flag = torch.zeros(1, dtype=torch.float32, device=cuda)
     torch.cuda.synchronize()
+    peers_acc = peers_stems = None
+    if world > 1 and args.exchange == "peer":
+        # every rank maps its neighbours' accumulator and stems (CUDA IPC): the boundary
+        # tail and the gather are SM loads over NVLink between on-stream barriers
+        peers_acc = shard.PeerBuffers(dist, dev, acc.data_ptr())
+        peers_stems = shard.PeerBuffers(dist, dev, stems.data_ptr())
+    phase_events = None  # set to a list to record (start, forward, exchange, finish, gather)
+
+    def mark():
+        if phase_events is not None:
+            e = torch.cuda.Event(enable_timing=True)
+            e.record(stream)
+            phase_events.append(e)
+
+    def shard_step(gather=True):
+        with torch.cuda.stream(stream):
+            mark()
+            h.normalize_track_device(lr.data_ptr(), n, mix_norm.data_ptr(), mean_std.data_ptr())
+            if mine:
+                acc[:, me.span_lo:me.span_hi].zero_()  # the only part of the view this rank writes
+                h.track_shard(mix_norm.data_ptr(), n, p.offset, p.max_shift, overlap, me.chunk_lo,
+                              me.chunk_hi, mine, acc.data_ptr(), 0, p.view_length)
+            mark()
+            if peers_acc is not None:
+                shard.exchange_tails_peer(dist, p, rank, h, acc.data_ptr(), peers_acc, flag)
+            else:
+                shard.exchange_tails(dist, p, rank, acc)
+            mark()
+            if me.t_hi > me.t_lo:
+                h.track_finish(acc.data_ptr(), n, p.offset, p.max_shift, overlap, shifts,
+                               mean_std.data_ptr(), stems.data_ptr(), me.t_lo, me.t_hi)
+            mark()
+            if gather and peers_stems is not None:
+                shard.gather_stems_peer(dist, p, rank, h, stems.data_ptr(), peers_stems, flag)
+            elif gather:
+                shard.gather_stems(dist, p, rank, stems.view(8, n))
+            elif peers_acc is not None:
+                shard.device_barrier(dist, flag)  # the neighbour's tail read is done before reuse
+            mark()
 
     def step():
         if world == 1:
             h.separate_track_device(lr.data_ptr(), n, stems.data_ptr(), shifts=shifts,
                                     overlap=overlap, batch=p.chunks)
             return
-        with torch.cuda.stream(stream):
-            h.normalize_track_device(lr.data_ptr(), n, mix_norm.data_ptr(), mean_std.data_ptr())
-            acc.zero_()
-            if mine:
-                h.track_shard(mix_norm.data_ptr(), n, p.offset, p.max_shift, overlap, me.chunk_lo,
-                              me.chunk_hi, mine, acc.data_ptr(), 0, p.view_length)
-            shard.exchange_tails(dist, p, rank, acc)
-            if me.t_hi > me.t_lo:
-                h.track_finish(acc.data_ptr(), n, p.offset, p.max_shift, overlap, shifts,
-                               mean_std.data_ptr(), stems.data_ptr(), me.t_lo, me.t_hi)
-            shard.gather_stems(dist, p, rank, stems.view(8, n))
+        shard_step()
 
     def barrier():
         if dist is not None:
@@ -350,13 +421,29 @@ def run_ours(args, rank, world, local_rank):
         ms = float(t.item())
     value = seconds / (ms / 1e3)
 
-    # e2e through the public host API: pinned host track in, stems back in pinned host memory
+    # N > 1: where one step's time goes on each rank (one more, untimed step)
+    phases = None
+    if world > 1:
+        phase_events = []
+        barrier()
+        step()
+        h.synchronize()
+        torch.cuda.synchronize()
+        mine_ms = torch.tensor(_event_ms(torch, phase_events), device=cuda)
+        phase_events = None
+        everyone = [torch.empty_like(mine_ms) for _ in range(world)]
+        dist.all_gather(everyone, mine_ms)
+        phases = {"unit": "ms", "order": ["normalise+forward+overlap-add", "boundary exchange",
+                                          "finish", "gather to rank 0"],
+                  "per_rank": [[round(float(x), 3) for x in t.cpu()] for t in everyone]}
+
+    # e2e through the public host API
     pin = torch.from_numpy(track).pin_memory()
-    out_pin = torch.empty((4, 2, n), dtype=torch.float32).pin_memory()
     e2e_batch = p.chunks
     if world == 1:
-        # the host entry point copies finished stems back while later forwards run, so
-        # the track goes through it in forwards of e2e_batch chunks
+        # pinned host track in, pinned host stems out: the host entry point copies finished
+        # stems back while later forwards run, in forwards of e2e_batch chunks
+        out_pin = torch.empty((4, 2, n), dtype=torch.float32).pin_memory()
         e2e_batch = args.e2e_batch or -(-p.chunks // 2)
         left, right, out_np = pin[0].numpy(), pin[1].numpy(), out_pin.numpy()
         h.separate_track(left, right, shifts=shifts, overlap=overlap, batch=e2e_batch, out=out_np)
@@ -364,14 +451,23 @@ def run_ours(args, rank, world, local_rank):
         for _ in range(args.steps):
             h.separate_track(left, right, shifts=shifts, overlap=overlap, batch=e2e_batch, out=out_np)
         e2e_s = (time.perf_counter() - t0) / args.steps
+        e2e_api = "dmx_separate_track (pinned host track in, pinned host stems out)"
+        h2d, d2h = 2 * n * 4, 8 * n * 4
+        del out_pin
     else:
+        # every rank copies the track in from its pinned host memory and its own span of the
+        # finished stems out into shared pinned host memory (no device gather)
+        host = SharedHostStems(dist, rank, n)
+
         def e2e_step():
             with torch.cuda.stream(stream):
                 lr.copy_(pin, non_blocking=True)
-            step()
-            if rank == 0:
-                with torch.cuda.stream(stream):
-                    out_pin.copy_(stems, non_blocking=True)
+            shard_step(gather=False)
+            with torch.cuda.stream(stream):
+                flat = stems.view(8, n)
+                for row in range(8):
+                    host.tensor[row, me.t_lo:me.t_hi].copy_(flat[row, me.t_lo:me.t_hi],
+                                                            non_blocking=True)
             h.synchronize()
         e2e_step()
         barrier()
@@ -382,20 +478,28 @@ def run_ours(args, rank, world, local_rank):
         t = torch.tensor([(time.perf_counter() - t0) / args.steps], device=cuda)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         e2e_s = float(t.item())
+        e2e_api = ("per rank: track copied in from pinned host memory, its chunk shard, boundary "
+                   "exchange, its span of the stems copied out into shared pinned host memory "
+                   f"(registered: {host.registered})")
+        h2d, d2h = 2 * n * 4 * world, 8 * n * 4
+        host.close(dist)
 
     # N > 1: rank 0 separates the same track alone (one handle, the same build) and the
     # gathered stems must equal it bit for bit (batch-invariant forward, exact OLA merge)
     match = None
-    if world > 1 and rank == 0:
-        with torch.cuda.stream(stream):
-            alone = torch.empty_like(stems)
+    if world > 1:
+        step()  # the device path again: stems gathered on rank 0
         h.synchronize()
-        torch.cuda.synchronize()
-        h.separate_track_device(lr.data_ptr(), n, alone.data_ptr(), shifts=shifts, overlap=overlap,
-                                batch=max(1, mine))
-        h.synchronize()
-        match = bool(torch.equal(alone, stems))
-        del alone
+        if rank == 0:
+            with torch.cuda.stream(stream):
+                alone = torch.empty_like(stems)
+            h.synchronize()
+            torch.cuda.synchronize()
+            h.separate_track_device(lr.data_ptr(), n, alone.data_ptr(), shifts=shifts,
+                                    overlap=overlap, batch=max(1, mine))
+            h.synchronize()
+            match = bool(torch.equal(alone, stems))
+            del alone
 
     # per-kernel device timing of one more (untimed) step for the roofline
     h.set_stage_timing(True)
@@ -412,13 +516,13 @@ def run_ours(args, rank, world, local_rank):
             "dtype": {"FP32": "f32", "TF32": "tf32", "TF32X3": "tf32x3"}[args.precision],
             "data": "synthetic",
             "config": track_config(seconds),
-            "precision": args.precision, "parallelism": f"chunk-sharded x{world}",
+            "precision": args.precision,
+            "parallelism": f"chunk-sharded x{world}" + (
+                f", boundary tail and stem gather over NVLink ({args.exchange})" if world > 1 else ""),
             "chunks_per_gpu": [r.chunk_hi - r.chunk_lo for r in p.ranks],
             "e2e": {"value": round(seconds / e2e_s, 3), "unit": UNIT,
-                    "h2d_bytes_per_step": int(2 * n * 4) * world, "d2h_bytes_per_step": int(8 * n * 4),
-                    "chunks_per_forward": e2e_batch,
-                    "api": "dmx_separate_track (pinned host track in, pinned host stems out)" if world == 1
-                    else "track copied in, shards, stems copied out on rank 0"},
+                    "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h),
+                    "chunks_per_forward": e2e_batch, "api": e2e_api},
             "gpu_launches": int(launches) * args.steps,
             "clocks": clocks.summary(),
             "roofline": roofline(stages),
@@ -429,6 +533,8 @@ def run_ours(args, rank, world, local_rank):
                             "tflops": round(v[2] / (v[0] / 1e3) / 1e12, 2) if v[0] else None,
                             "gbs": round(v[3] / (v[0] / 1e3) / 1e9, 1) if v[0] else None}
                         for k, v in sorted(stages.items(), key=lambda kv: -kv[1][0])}}
+    if phases is not None:
+        line["phases"] = phases
     if match is not None:
         line["stems_match_1gpu"] = match
     if world == 1 and args.precision == "TF32" and not args.no_fp32_class:
@@ -439,7 +545,186 @@ def run_ours(args, rank, world, local_rank):
         print(json.dumps(line), flush=True)
     h.synchronize()
     torch.cuda.synchronize()
-    del lr, stems, mix_norm, mean_std, acc, pin, out_pin
+    if peers_acc is not None:
+        dist.barrier()  # no rank unmaps while another may still read
+        peers_acc.close()
+        peers_stems.close()
+        dist.barrier()
+    del lr, stems, mix_norm, mean_std, acc, pin
+    torch.cuda.empty_cache()
+    h.close()
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def _timed(torch, stream, dev, dist, step, steps, warmup):
+    """W warm-up steps, then K steps between events on `stream`, max over ranks (ms)."""
+    cuda = f"cuda:{dev}"
+    for _ in range(warmup):
+        step()
+    torch.cuda.synchronize()
+    if dist is not None:
+        dist.barrier()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(dev) as clocks:
+        start.record(stream)
+        for _ in range(steps):
+            step()
+        end.record(stream)
+        torch.cuda.synchronize()
+    ms = start.elapsed_time(end) / steps
+    if dist is not None:
+        t = torch.tensor([ms], device=cuda)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    return ms, clocks.summary()
+
+
+def run_bag(args, rank, world, dev, dist):
+    """htdemucs_ft bag (the bag configuration of the benchmark): four independently
+    seeded networks, identity weights (network k gives stem k), one 240 s pink-noise
+    track, shifts 0. One GPU: the lockstep bag driver (every network forwards each
+    chunk batch, combined before the overlap-add). Fewer GPUs than networks: whole
+    networks per GPU. 4 GPUs: one network per GPU. 8 GPUs: one network per GPU pair,
+    its chunks sharded inside the pair. The weighted stem lanes meet on rank 0, which
+    combines them (dmx_bag_combine_device)."""
+    import torch
+    import dmx
+    import shard
+
+    seconds = args.seconds
+    n = int(seconds * SR)
+    track = synth.pink_noise(2024, n)
+    weights = np.eye(4, dtype=np.float32)
+    cuda = f"cuda:{dev}"
+    lr = torch.from_numpy(track).to(cuda)
+    stems = torch.zeros((4, 2, n), dtype=torch.float32, device=cuda)
+    chunks = shard.plan(n, 1, shifts=0).chunks
+    if world == 1:
+        hs = [dmx.Handle(synth.write_safetensors(synth.random_weights(k)), device=dev,
+                         max_batch=chunks, precision=getattr(dmx, args.precision)) for k in range(4)]
+        bag = dmx.Bag(hs, weights)
+        stream = torch.cuda.ExternalStream(hs[0].stream, device=cuda)
+        torch.cuda.synchronize()
+
+        def step():
+            bag.separate_track_device(lr.data_ptr(), n, stems.data_ptr(), shifts=0, batch=chunks)
+        parallelism = "lockstep bag on one GPU"
+    else:
+        assign = shard.bag_assign(4, world, rank, weights)
+        group = assign.group
+        p = shard.plan(n, len(group), shifts=0)
+        me = p.rank(assign.index)
+        mine = me.chunk_hi - me.chunk_lo
+        hs = [dmx.Handle(synth.write_safetensors(synth.random_weights(k)), device=dev,
+                         max_batch=max(1, mine if len(group) > 1 else chunks),
+                         precision=getattr(dmx, args.precision)) for k in assign.nets]
+        stream = torch.cuda.ExternalStream(hs[0].stream, device=cuda)
+        own = {k: torch.zeros((4, 2, n), dtype=torch.float32, device=cuda) for k in assign.nets}
+        mix_norm = torch.empty_like(lr)
+        mean_std = torch.empty(2, dtype=torch.float32, device=cuda)
+        acc = torch.zeros((8, p.view_length), dtype=torch.float32, device=cuda)
+        torch.cuda.synchronize()
+
+        def combine(outs, w, req):
+            ptrs = [o.data_ptr() if o is not None else 0 for o in outs]
+            dmx.bag_combine_device(ptrs, w, None, 1, n, stems.data_ptr(),
+                                   torch.cuda.current_stream().cuda_stream)
+            return stems
+
+        def step():
+            with torch.cuda.stream(stream):
+                for k, h in zip(assign.nets, hs):
+                    if len(group) == 1:
+                        h.separate_track_device(lr.data_ptr(), n, own[k].data_ptr(), shifts=0,
+                                                batch=chunks)
+                        continue
+                    h.normalize_track_device(lr.data_ptr(), n, mix_norm.data_ptr(),
+                                             mean_std.data_ptr())
+                    if mine:
+                        acc[:, me.span_lo:me.span_hi].zero_()
+                        h.track_shard(mix_norm.data_ptr(), n, 0, 0, 0.25, me.chunk_lo, me.chunk_hi,
+                                      mine, acc.data_ptr(), 0, p.view_length)
+                    shard.exchange_tails(dist, p, assign.index, acc, ranks=group)
+                    if me.t_hi > me.t_lo:
+                        h.track_finish(acc.data_ptr(), n, 0, 0, 0.25, 0, mean_std.data_ptr(),
+                                       own[k].data_ptr(), me.t_lo, me.t_hi)
+                    shard.gather_stems(dist, p, assign.index, own[k].view(8, n), ranks=group)
+                shard.bag_gather(dist, rank, assign, own, weights, None, combine, stems)
+        parallelism = (f"whole networks per GPU x{world}" if world < 4 else
+                       f"one network per GPU{' pair' if world == 8 else ''}, x{world}")
+    ms, clocks = _timed(torch, stream, dev, dist, step, args.steps, args.warmup)
+    value = seconds / (ms / 1e3)
+    line = {"metric": METRIC + ", htdemucs_ft bag of 4", "value": round(value, 3), "unit": UNIT,
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(ms, 3), "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": args.precision.lower(), "data": "synthetic",
+            "config": {"workload": f"htdemucs_ft bag: 4 random-init networks (seeds 0-3), identity "
+                                   f"4x4 bag weights, {seconds:g} s stereo pink noise, shifts 0, "
+                                   "overlap 0.25", "chunks_per_network": chunks,
+                       "l2": "inputs and workspace larger than L2 (126 MB)"},
+            "parallelism": parallelism, "clocks": clocks}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    torch.cuda.synchronize()
+    for h in hs:
+        h.synchronize()
+    del lr, stems
+    torch.cuda.empty_cache()
+    for h in hs:
+        h.close()
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def run_batch(args, rank, world, dev, dist):
+    """Throughput batch (the many-track configuration of the benchmark): seeded pink-noise
+    tracks, shifts 2, segment 7.8 s, overlap 0.25; every rank takes a balanced share of
+    the tracks (shard.assign_tracks) and pools all their (track, shift pass, chunk) units
+    into full forwards (dmx_separate_batch_device); the stems stay on each rank's GPU.
+    The default is the full 64 x 180 s batch; --tracks / --seconds shrink it."""
+    import torch
+    import dmx
+    import shard
+
+    n = int(args.seconds * SR)
+    tracks = [synth.pink_noise(5000 + i, n) for i in range(args.tracks)]
+    per_rank = shard.assign_tracks([n] * len(tracks), world, shifts=2)
+    mine = per_rank[rank]
+    units = sum(shard.track_units(n, 2) for _ in mine)
+    batch = min(args.max_batch, max(1, units))
+    cuda = f"cuda:{dev}"
+    h = dmx.Handle(synth.write_safetensors(synth.random_weights(0)), device=dev, max_batch=batch,
+                   precision=getattr(dmx, args.precision))
+    stream = torch.cuda.ExternalStream(h.stream, device=cuda)
+    lrs = [torch.from_numpy(tracks[i]).to(cuda) for i in mine]
+    outs = [torch.empty((4, 2, n), dtype=torch.float32, device=cuda) for _ in mine]
+    torch.cuda.synchronize()
+
+    def step():
+        if mine:
+            h.separate_batch_device([x.data_ptr() for x in lrs], [n] * len(mine),
+                                    [o.data_ptr() for o in outs], shifts=2, batch=batch)
+    ms, clocks = _timed(torch, stream, dev, dist, step, args.steps, args.warmup)
+    audio = len(tracks) * args.seconds
+    line = {"metric": METRIC + ", many-track batch", "value": round(audio / (ms / 1e3), 3),
+            "unit": UNIT, "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(ms, 3), "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": args.precision.lower(), "data": "synthetic",
+            "config": {"workload": f"throughput batch: {len(tracks)} pink-noise tracks of "
+                                   f"{args.seconds:g} s, shifts 2, segment 7.8 s, overlap 0.25, "
+                                   "units pooled into full forwards", "forwards_per_step_rank0":
+                                   -(-shard.track_units(n, 2) * len(per_rank[0]) // batch),
+                       "chunks_per_forward": batch, "tracks_per_gpu": [len(t) for t in per_rank],
+                       "l2": "inputs and workspace larger than L2 (126 MB)"},
+            "parallelism": f"tracks over ranks x{world}", "clocks": clocks}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    h.synchronize()
+    torch.cuda.synchronize()
+    del lrs, outs
     torch.cuda.empty_cache()
     h.close()
     if dist is not None:
@@ -460,9 +745,21 @@ def main():
                     help="reference arm: chunks of the workload's track per step (a prefix)")
     ap.add_argument("--e2e-batch", type=int, default=0,
                     help="chunks per forward in the host-API (e2e) leg; 0 = half the track's")
-    ap.add_argument("--seconds", type=float, default=TRACK_SECONDS,
-                    help="track length (the benchmark is 240 s; shorter tracks are for profiling)")
+    ap.add_argument("--seconds", type=float, default=None,
+                    help="track length (the benchmark is 240 s, 180 s per track for --workload "
+                         "batch; shorter tracks are for profiling)")
+    ap.add_argument("--workload", default="track", choices=["track", "bag", "batch"],
+                    help="track: one 240 s track (the headline); bag: the htdemucs_ft bag of 4; "
+                         "batch: the many-track throughput batch")
+    ap.add_argument("--tracks", type=int, default=64, help="--workload batch: tracks")
+    ap.add_argument("--exchange", default="peer", choices=["peer", "nccl"],
+                    help="N > 1: boundary tail and stem gather as SM loads from mapped peer "
+                         "memory (peer) or as NCCL point-to-point messages (nccl)")
+    ap.add_argument("--max-batch", type=int, default=42,
+                    help="--workload batch: chunks per forward")
     args = ap.parse_args()
+    if args.seconds is None:
+        args.seconds = 180.0 if args.workload == "batch" else TRACK_SECONDS
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", str(args.gpus)))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))

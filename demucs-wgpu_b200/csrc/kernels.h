@@ -138,6 +138,10 @@ void launch_sum_partials(const double* part, int nparts, int rows, double* stats
 // boundary merge of the multi-GPU track driver.
 void launch_tail_add(float* acc, int64_t ld, const float* tail, int64_t width, int rows,
                      cudaStream_t s);
+// dst (rows, width; row stride dld) = src, or += src with `add` (each sum
+// rounded on its own); src may be a peer GPU's memory mapped into this process.
+void launch_rows(bool add, float* dst, int64_t dld, const float* src, int64_t sld, int rows,
+                 int64_t width, cudaStream_t s);
 
 // selftest.cu — one warp waits on a device flag nothing sets and, after
 // limit_ns, stores `code` into err and returns (the bounded-wait error path).

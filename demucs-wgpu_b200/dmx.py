@@ -27,7 +27,8 @@ EXPORTS = (
     "dmx_separate_track_emit", "dmx_selftest_wait_timeout", "dmx_separate_track_multi",
     "dmx_num_chunks", "dmx_track_finish", "dmx_track_shard", "dmx_set_trace",
     "dmx_set_stage_timing", "dmx_stage_times", "dmx_kernel_launches", "dmx_stream",
-    "dmx_synchronize", "dmx_read_tensor", "dmx_shift_offsets",
+    "dmx_synchronize", "dmx_read_tensor", "dmx_shift_offsets", "dmx_ipc_export", "dmx_ipc_open",
+    "dmx_ipc_close", "dmx_rows_copy", "dmx_rows_add",
 )
 
 _f32p = ctypes.POINTER(ctypes.c_float)
@@ -115,6 +116,14 @@ def lib():
         L.dmx_read_tensor.argtypes = [ctypes.c_void_p, ctypes.c_size_t, ctypes.c_char_p, _f32p,
                                       ctypes.c_int64, _i64p, ctypes.POINTER(ctypes.c_int)]
         L.dmx_shift_offsets.argtypes = [ctypes.c_int, ctypes.c_int64, _i64p]
+        L.dmx_ipc_export.argtypes = [ctypes.c_int, ctypes.c_void_p, ctypes.c_char_p, _i64p]
+        L.dmx_ipc_open.argtypes = [ctypes.c_int, ctypes.c_char_p, ctypes.c_int64,
+                                   ctypes.POINTER(ctypes.c_void_p)]
+        L.dmx_ipc_close.argtypes = [ctypes.c_int, ctypes.c_void_p, ctypes.c_int64]
+        for name in ("dmx_rows_copy", "dmx_rows_add"):
+            getattr(L, name).argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64,
+                                         ctypes.c_void_p, ctypes.c_int64, ctypes.c_int,
+                                         ctypes.c_int64]
         L.dmx_set_stage_timing.argtypes = [ctypes.c_void_p, ctypes.c_int]
         L.dmx_selftest_wait_timeout.argtypes = [ctypes.c_void_p, ctypes.c_int]
         L.dmx_separate_track_multi.argtypes = [ctypes.POINTER(ctypes.c_void_p), ctypes.c_int,
@@ -320,6 +329,16 @@ class Handle:
         after a device wait that nothing satisfies gives up."""
         _check(lib().dmx_selftest_wait_timeout(self._h, wait_ms))
 
+    def rows_copy(self, dst_ptr, dst_ld, src_ptr, src_ld, rows, width):
+        """dmx_rows_copy on the handle's stream (src may be a mapped peer buffer)."""
+        _check(lib().dmx_rows_copy(self._h, ctypes.c_void_p(dst_ptr), dst_ld,
+                                   ctypes.c_void_p(src_ptr), src_ld, rows, width))
+
+    def rows_add(self, dst_ptr, dst_ld, src_ptr, src_ld, rows, width):
+        """dmx_rows_add: dst += src, each sum rounded on its own."""
+        _check(lib().dmx_rows_add(self._h, ctypes.c_void_p(dst_ptr), dst_ld,
+                                  ctypes.c_void_p(src_ptr), src_ld, rows, width))
+
     def set_stage_timing(self, on: bool):
         _check(lib().dmx_set_stage_timing(self._h, int(bool(on))))
 
@@ -455,6 +474,25 @@ def read_tensor(blob: bytes, name: str):
                                  _ptr(out), cap, shape, ctypes.byref(ndim)))
     dims = tuple(shape[i] for i in range(ndim.value))
     return out[:int(np.prod(dims, dtype=np.int64))].reshape(dims).copy()
+
+
+def ipc_export(device: int, ptr: int):
+    """dmx_ipc_export: (64-byte handle, offset) of a device buffer of `device`."""
+    handle = ctypes.create_string_buffer(64)
+    offset = ctypes.c_int64()
+    _check(lib().dmx_ipc_export(device, ctypes.c_void_p(ptr), handle, ctypes.byref(offset)))
+    return handle.raw, offset.value
+
+
+def ipc_open(device: int, handle: bytes, offset: int) -> int:
+    """dmx_ipc_open: maps another process's exported buffer on `device`."""
+    ptr = ctypes.c_void_p()
+    _check(lib().dmx_ipc_open(device, handle, offset, ctypes.byref(ptr)))
+    return ptr.value
+
+
+def ipc_close(device: int, ptr: int, offset: int):
+    _check(lib().dmx_ipc_close(device, ctypes.c_void_p(ptr), offset))
 
 
 def shift_offsets(passes: int, max_shift: int = 22050):

@@ -134,7 +134,9 @@ def exchange_tails(dist, p: TrackPlan, rank: int, acc, ranks=None, timeout=None)
     (8, view_length) accumulator (torch tensor on the backend's device).
     ``rank`` is the index in the plan; ``ranks[i]`` is the process-group rank
     of plan index i (default: the identity), so a plan can span a sub-group.
-    Each wait is bounded (``timeout`` seconds, default WAIT_SECONDS)."""
+    Each of the 8 rows goes as its own message straight from ``acc`` (a row
+    slice is contiguous), so the sender copies nothing. Each wait is bounded
+    (``timeout`` seconds, default WAIT_SECONDS)."""
     import torch
 
     world = len(p.ranks)
@@ -143,14 +145,15 @@ def exchange_tails(dist, p: TrackPlan, rank: int, acc, ranks=None, timeout=None)
     ops = []
     recv = None
     if rank + 1 < world and me.send_hi > me.send_lo and p.rank(rank + 1).chunk_hi > p.rank(rank + 1).chunk_lo:
-        send = acc[:, me.send_lo:me.send_hi].contiguous()
-        ops.append(dist.P2POp(dist.isend, send, ranks[rank + 1]))
+        for row in range(acc.shape[0]):
+            ops.append(dist.P2POp(dist.isend, acc[row, me.send_lo:me.send_hi], ranks[rank + 1]))
     if rank > 0:
         prev = p.rank(rank - 1)
         if prev.send_hi > prev.send_lo and me.chunk_hi > me.chunk_lo:
             recv = torch.empty((acc.shape[0], prev.send_hi - prev.send_lo), dtype=acc.dtype,
                                device=acc.device)
-            ops.append(dist.P2POp(dist.irecv, recv, ranks[rank - 1]))
+            for row in range(acc.shape[0]):
+                ops.append(dist.P2POp(dist.irecv, recv[row], ranks[rank - 1]))
     if ops:
         _wait_all(dist.batch_isend_irecv(ops), "overlap-add boundary exchange", timeout)
     if recv is not None:
@@ -160,30 +163,98 @@ def exchange_tails(dist, p: TrackPlan, rank: int, acc, ranks=None, timeout=None)
 
 def gather_stems(dist, p: TrackPlan, rank: int, stems, ranks=None, timeout=None):
     """Plan index 0 receives every plan index's owned output samples into
-    ``stems`` (8, length); ``ranks`` as in exchange_tails."""
-    import torch
-
+    ``stems`` (8, length); ``ranks`` as in exchange_tails. Each row of a span
+    travels as its own message, from the sender's stems row straight into the
+    receiver's (both row slices are contiguous): no staging copies."""
     world = len(p.ranks)
     ranks = list(range(world)) if ranks is None else list(ranks)
     me = p.rank(rank)
     if rank == 0:
-        bufs = []
         ops = []
         for r in range(1, world):
             q = p.rank(r)
             if q.t_hi > q.t_lo:
-                buf = torch.empty((stems.shape[0], q.t_hi - q.t_lo), dtype=stems.dtype,
-                                  device=stems.device)
-                bufs.append((q, buf))
-                ops.append(dist.P2POp(dist.irecv, buf, ranks[r]))
+                for row in range(stems.shape[0]):
+                    ops.append(dist.P2POp(dist.irecv, stems[row, q.t_lo:q.t_hi], ranks[r]))
         if ops:
             _wait_all(dist.batch_isend_irecv(ops), "stem gather", timeout)
-        for q, buf in bufs:
-            stems[:, q.t_lo:q.t_hi] = buf
     elif me.t_hi > me.t_lo:
-        send = stems[:, me.t_lo:me.t_hi].contiguous()
-        _wait_all(dist.batch_isend_irecv([dist.P2POp(dist.isend, send, ranks[0])]), "stem gather",
-                  timeout)
+        ops = [dist.P2POp(dist.isend, stems[row, me.t_lo:me.t_hi], ranks[0])
+               for row in range(stems.shape[0])]
+        _wait_all(dist.batch_isend_irecv(ops), "stem gather", timeout)
+
+
+# ---------------------------------------------------------------------------
+# The same exchange and gather as SM loads over NVLink from peer memory
+# ---------------------------------------------------------------------------
+
+class PeerBuffers:
+    """Every rank's copy of one device buffer, mapped into this process over CUDA
+    IPC (dmx_ipc_export / dmx_ipc_open), so a rank reads its neighbours' buffers
+    directly. ``ptrs[r]`` is rank r's buffer as this process addresses it (its own
+    is the local pointer). Collective: every rank constructs it with its own
+    buffer, in the same order."""
+
+    def __init__(self, dist, device: int, ptr: int):
+        import dmx
+
+        self.device = device
+        self.rank = dist.get_rank()
+        mine = dmx.ipc_export(device, ptr)
+        everyone = [None] * dist.get_world_size()
+        dist.all_gather_object(everyone, mine)
+        self.offsets = [off for _, off in everyone]
+        self.ptrs = [ptr if r == self.rank else dmx.ipc_open(device, hnd, off)
+                     for r, (hnd, off) in enumerate(everyone)]
+
+    def close(self):
+        import dmx
+
+        for r, ptr in enumerate(self.ptrs):
+            if r != self.rank and ptr:
+                dmx.ipc_close(self.device, ptr, self.offsets[r])
+        self.ptrs = []
+
+
+def device_barrier(dist, flag):
+    """A one-element all-reduce on the current stream: when it completes on a GPU,
+    every rank's earlier work on its own stream has completed. Orders peer reads
+    after the peer's writes (and the peer's next writes after the reads) without
+    a host wait. ``flag`` is a one-element tensor on this rank's GPU."""
+    dist.all_reduce(flag)
+
+
+def exchange_tails_peer(dist, p: TrackPlan, rank: int, h, acc_ptr: int, peers: PeerBuffers,
+                        flag, rows: int = 8):
+    """exchange_tails over NVLink: after a barrier, rank r adds rank r-1's tail into
+    its own accumulator with SM loads straight from the neighbour's (dmx_rows_add).
+    ``acc_ptr`` / ``peers`` address the (rows, view_length) accumulators."""
+    device_barrier(dist, flag)
+    if rank == 0:
+        return
+    prev, me = p.rank(rank - 1), p.rank(rank)
+    width = prev.send_hi - prev.send_lo
+    if width > 0 and me.chunk_hi > me.chunk_lo:
+        lo = prev.send_lo * 4
+        h.rows_add(acc_ptr + lo, p.view_length, peers.ptrs[rank - 1] + lo, p.view_length, rows,
+                   width)
+
+
+def gather_stems_peer(dist, p: TrackPlan, rank: int, h, stems_ptr: int, peers: PeerBuffers,
+                      flag, rows: int = 8):
+    """gather_stems over NVLink: after a barrier, rank 0 copies every rank's owned
+    span of its (rows, length) stems straight from that rank's buffer
+    (dmx_rows_copy); a second barrier keeps every rank from overwriting its stems
+    before rank 0 has read them."""
+    device_barrier(dist, flag)
+    if rank == 0:
+        for r in range(1, len(p.ranks)):
+            q = p.rank(r)
+            if q.t_hi > q.t_lo:
+                off = q.t_lo * 4
+                h.rows_copy(stems_ptr + off, p.length, peers.ptrs[r] + off, p.length, rows,
+                            q.t_hi - q.t_lo)
+    device_barrier(dist, flag)
 
 
 # ---------------------------------------------------------------------------

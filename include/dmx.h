@@ -272,6 +272,32 @@ dmx_status dmx_separate_track_bag_device(dmx_handle* const* nets, int n_nets, co
  * over processes themselves. */
 dmx_status dmx_shift_offsets(int passes, int64_t max_shift, int64_t* out);
 
+/* Peer memory for one process per GPU (the multi-process form of the track
+ * sharding; the reference runs one device: streaming.rs:296-400). A rank
+ * exports a device buffer of its GPU (`device`) as a 64-byte CUDA IPC handle
+ * and the offset of dev_ptr inside its allocation; another process on the
+ * same node maps it with dmx_ipc_open on its own GPU (peer access over
+ * NVLink enabled lazily) and unmaps it with dmx_ipc_close (the same offset).
+ * The exporting process must keep the buffer alive while it is mapped. */
+dmx_status dmx_ipc_export(int device, const void* dev_ptr, unsigned char handle[64],
+                          int64_t* offset);
+dmx_status dmx_ipc_open(int device, const unsigned char handle[64], int64_t offset, void** ptr);
+dmx_status dmx_ipc_close(int device, void* ptr, int64_t offset);
+
+/* The multi-process boundary merge and stem gather (the overlap-add tail a
+ * rank adds from its left neighbour, streaming.rs:219-260, and the gather of
+ * the stems to one rank): dst (rows x width, row stride dst_ld floats) =
+ * src (row stride src_ld), or dst += src for dmx_rows_add (each sum rounded on
+ * its own, so a merged sample equals the one-GPU overlap-add's bit for bit),
+ * on the handle's stream, with the SMs reading src — typically a peer GPU's
+ * buffer mapped by dmx_ipc_open — over NVLink. The caller orders the reads
+ * after the peer's writes (e.g. a collective on both streams) and the peer's
+ * next writes after the reads. */
+dmx_status dmx_rows_copy(dmx_handle* h, float* dst, int64_t dst_ld, const float* src,
+                         int64_t src_ld, int rows, int64_t width);
+dmx_status dmx_rows_add(dmx_handle* h, float* dst, int64_t dst_ld, const float* src,
+                        int64_t src_ld, int rows, int64_t width);
+
 /* Chunk plan of a split pass (streaming.rs:88-94, 296-330): number of chunks
  * of a view of `view_length` samples. */
 int64_t dmx_num_chunks(int64_t view_length, int segment, double overlap);

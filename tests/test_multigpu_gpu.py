@@ -34,7 +34,7 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def _worker(rank, world, port, out_path):
+def _worker(rank, world, port, out_path, mode="nccl"):
     import datetime
     import sys
 
@@ -66,30 +66,53 @@ def _worker(rank, world, port, out_path):
         ms = torch.empty(2, device="cuda")
         acc = torch.zeros((8, p.view_length), device="cuda")
         stems = torch.zeros((8, n), device="cuda")
-        h.normalize_track_device(lr.data_ptr(), n, mix_norm.data_ptr(), ms.data_ptr())
-        h.track_shard(mix_norm.data_ptr(), n, p.offset, p.max_shift, 0.25, me.chunk_lo,
-                      me.chunk_hi, 4, acc.data_ptr(), 0, p.view_length)
-        shard.exchange_tails(dist, p, rank, acc)
-        h.track_finish(acc.data_ptr(), n, p.offset, p.max_shift, 0.25, 1, ms.data_ptr(),
-                       stems.data_ptr(), me.t_lo, me.t_hi)
-        shard.gather_stems(dist, p, rank, stems)
+        flag = torch.zeros(1, device="cuda")
+    h.synchronize()
+    peers_acc = peers_stems = None
+    if mode == "peer":
+        peers_acc = shard.PeerBuffers(dist, rank, acc.data_ptr())
+        peers_stems = shard.PeerBuffers(dist, rank, stems.data_ptr())
+    for _ in range(2):  # twice: the second step reuses every buffer (the barriers order it)
+        with torch.cuda.stream(stream):
+            h.normalize_track_device(lr.data_ptr(), n, mix_norm.data_ptr(), ms.data_ptr())
+            acc.zero_()
+            h.track_shard(mix_norm.data_ptr(), n, p.offset, p.max_shift, 0.25, me.chunk_lo,
+                          me.chunk_hi, 4, acc.data_ptr(), 0, p.view_length)
+            if mode == "peer":
+                shard.exchange_tails_peer(dist, p, rank, h, acc.data_ptr(), peers_acc, flag)
+            else:
+                shard.exchange_tails(dist, p, rank, acc)
+            h.track_finish(acc.data_ptr(), n, p.offset, p.max_shift, 0.25, 1, ms.data_ptr(),
+                           stems.data_ptr(), me.t_lo, me.t_hi)
+            if mode == "peer":
+                shard.gather_stems_peer(dist, p, rank, h, stems.data_ptr(), peers_stems, flag)
+            else:
+                shard.gather_stems(dist, p, rank, stems)
     h.synchronize()
     torch.cuda.synchronize()
     if rank == 0:
         single = h.separate_track(track[0], track[1], shifts=1)
         np.save(out_path, np.stack([stems.cpu().numpy().reshape(4, 2, n), single]))
     dist.barrier()
+    if peers_acc is not None:
+        peers_acc.close()
+        peers_stems.close()
+    dist.barrier()
     h.close()
     dist.destroy_process_group()
 
 
+@pytest.mark.parametrize("mode", ["nccl", "peer"])
 @pytest.mark.parametrize("world", [2, 4, 8])
-def test_sharding_over_gpus_matches_one_gpu(world, tmp_path):
+def test_sharding_over_gpus_matches_one_gpu(world, mode, tmp_path):
+    # mode nccl: boundary tails and stems as NCCL point-to-point messages; mode peer:
+    # every rank maps its neighbours' buffers (CUDA IPC) and reads them over NVLink
+    # between on-stream barriers
     if torch.cuda.device_count() < world:
         pytest.skip(f"needs {world} GPUs")
     out_path = str(tmp_path / "stems.npy")
-    mp.start_processes(_worker, args=(world, _free_port(), out_path), nprocs=world, join=True,
-                       start_method="spawn")
+    mp.start_processes(_worker, args=(world, _free_port(), out_path, mode), nprocs=world,
+                       join=True, start_method="spawn")
     sharded, single = np.load(out_path)
     assert np.isfinite(sharded).all()
     assert np.array_equal(sharded, single)
