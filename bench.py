@@ -513,7 +513,8 @@ def run_ours(args, rank, world, local_rank):
     line = {"metric": METRIC, "value": round(value, 3), "unit": UNIT, "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 3),
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
-            "dtype": {"FP32": "f32", "TF32": "tf32", "TF32X3": "tf32x3"}[args.precision],
+            "dtype": {"FP32": "f32", "TF32": "tf32", "TF32X3": "tf32x3",
+                      "BF16": "bf16 transformer linears, tf32 elsewhere"}[args.precision],
             "data": "synthetic",
             "config": track_config(seconds),
             "precision": args.precision,
@@ -738,7 +739,7 @@ def main():
     ap.add_argument("--steps", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--precision", default="TF32", choices=["FP32", "TF32", "TF32X3"])
+    ap.add_argument("--precision", default="TF32", choices=["FP32", "TF32", "TF32X3", "BF16"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU-baseline leg")
     ap.add_argument("--no-fp32-class", action="store_true", help="skip the TF32X3 leg")
     ap.add_argument("--ref-chunks", type=int, default=2,

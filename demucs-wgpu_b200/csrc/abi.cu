@@ -56,8 +56,8 @@ dmx_status dmx_create(const dmx_config* cfg, const void* blob, size_t len, int d
                   "only the default htdemucs configuration is supported (4 sources, stereo, "
                   "44100 Hz, 343980-sample segments)");
     if (cfg->precision != DMX_FP32 && cfg->precision != DMX_TF32 &&
-        cfg->precision != DMX_TF32X3)
-      throw Error(DMX_ERR_INVALID, "precision must be DMX_FP32, DMX_TF32 or DMX_TF32X3");
+        cfg->precision != DMX_TF32X3 && cfg->precision != DMX_BF16)
+      throw Error(DMX_ERR_INVALID, "precision must be DMX_FP32, DMX_TF32, DMX_BF16 or DMX_TF32X3");
     if (cfg->max_batch < 1 || cfg->max_batch > 256)
       throw Error(DMX_ERR_INVALID, "max_batch must be in [1, 256]");
     h->cfg = *cfg;

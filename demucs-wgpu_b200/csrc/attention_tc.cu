@@ -23,6 +23,8 @@
 #include <cudaTypedefs.h>
 
 #include "common.cuh"
+#include <cuda_bf16.h>
+
 #include "tc_common.cuh"
 #include "tc_gemm.cuh"
 
@@ -66,6 +68,7 @@ struct AttnParams {
   int nq, nk;
   int q_col, k_col, v_col;  // column of head 0 in each source matrix
   float* out;
+  uint16_t* out16;  // bf16 output instead of `out` (the A operand of a bf16 GEMM)
   int ldo;
   float scale;
   int* err;
@@ -279,7 +282,19 @@ __global__ void __launch_bounds__(192, 2)
     __syncwarp();
     tmem_ld32(tmem + lane_base + TM_O, ov);
     tmem_ld32(tmem + lane_base + TM_O + 32, ov + 32);
-    if (ok && qvalid) {
+    if (ok && qvalid && p.out16) {
+      // the output feeds only the bf16 out-projection: stored as bf16
+      const float inv = l > 0.f ? 1.0f / l : 0.f;
+      uint16_t* o = p.out16 + (int64_t)(b * p.nq + q0 + r) * p.ldo + h * HD;
+#pragma unroll
+      for (int i = 0; i < HD; i += 8) {
+        __nv_bfloat162 w[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e)
+          w[e] = __float22bfloat162_rn(make_float2(ov[i + 2 * e] * inv, ov[i + 2 * e + 1] * inv));
+        *reinterpret_cast<uint4*>(o + i) = *reinterpret_cast<const uint4*>(w);
+      }
+    } else if (ok && qvalid) {
       const float inv = l > 0.f ? 1.0f / l : 0.f;
       float* o = p.out + (int64_t)(b * p.nq + q0 + r) * p.ldo + h * HD;
 #pragma unroll
@@ -305,8 +320,9 @@ __global__ void __launch_bounds__(192, 2)
 // at k_col / v_col + 64h; out (rows, ldo). nk must be a multiple of 64.
 bool launch_attention_tc(const float* q, int ldq, int q_col, const float* kv, int ldkv, int k_col,
                          int v_col, const float* vt, float* out, int ldo, int B, int heads, int nq,
-                         int nk, float scale, int* err, cudaStream_t s) {
+                         int nk, float scale, int* err, cudaStream_t s, uint16_t* out16) {
   if (nk % KT != 0 || ldq % 4 || (q_col % 4) || (ldkv * 4) % 16 || ldkv % 32) return false;
+  if (out16 && ((reinterpret_cast<uintptr_t>(out16) & 15) || ldo % 8)) return false;
   if ((reinterpret_cast<uintptr_t>(q) & 15) || (reinterpret_cast<uintptr_t>(kv) & 15) ||
       (reinterpret_cast<uintptr_t>(vt) & 15) || heads * HD > 4096)
     return false;
@@ -334,6 +350,7 @@ bool launch_attention_tc(const float* q, int ldq, int q_col, const float* kv, in
   p.k_col = k_col;
   p.v_col = v_col;
   p.out = out;
+  p.out16 = out16;
   p.ldo = ldo;
   p.scale = scale;
   p.err = err;

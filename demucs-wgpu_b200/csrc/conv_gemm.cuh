@@ -76,6 +76,10 @@ struct ConvParams {
   // for positions 4x, 4x+1, ...; columns of positions >= o_lim are not stored
   int o_lim, o_lim_ch;
   int a_rounded;  // tensor-core path: A already holds tf32-rounded values (no converter pass)
+  // tensor-core path, BF16 build: A is a bf16 matrix (x points at uint16 values,
+  // row pitch i_xs elements), the GEMM runs kind::f16 on the layer's bf16 weights
+  int a_bf16;
+  uint16_t* out16;  // EPI_STORE / EPI_GELU: bf16 output instead of `out` (same element offsets)
   // tensor-core path, EPI_STORE / EPI_GELU: o_pcols > 0 splits the columns into
   // groups of o_pcols (a multiple of 16) stored o_pstride elements apart —
   // column g * o_pcols + c goes to element row + g * o_pstride + c (the four

@@ -37,9 +37,11 @@ void dmx_handle::gemm(const ConvParams& p0, int pro, int epi, const char* tag,
     if (epi == EPI_RESIDUAL) bytes += 4.0 * M * nout;
     mark(tag, 2.0 * M * K * p.N * (pk ? pk->flop_scale : 1.0), bytes);
   }
-  if (pk && (cfg.precision == DMX_TF32 || cfg.precision == DMX_TF32X3) &&
+  if (pk && (cfg.precision == DMX_TF32 || cfg.precision == DMX_TF32X3 || cfg.precision == DMX_BF16) &&
       try_tc(p, pro, epi, *pk))
     return;
+  if (p.a_bf16 || p.out16)
+    throw Error(DMX_ERR_INVALID, std::string(tag) + ": bf16 operands need the tensor-core kernel");
   if (pk && !pk->host_w.empty() && launch_first_conv(p, pro, epi, pk->host_w.data(), stream))
     return;
   launch_conv_gemm(p, pro, epi, stream);
@@ -49,7 +51,8 @@ void dmx_handle::gemm(const ConvParams& p0, int pro, int epi, const char* tag,
 // (split output columns): false, with nothing launched, when the
 // tensor-core kernel does not take it; the caller then issues another form.
 bool dmx_handle::gemm_tc(const ConvParams& p, int epi, const char* tag, const Packed& pk) {
-  if (cfg.precision != DMX_TF32 && cfg.precision != DMX_TF32X3) return false;
+  if (cfg.precision != DMX_TF32 && cfg.precision != DMX_TF32X3 && cfg.precision != DMX_BF16)
+    return false;
   if (epi != EPI_STORE && epi != EPI_GELU) return false;
   if (p.o_pcols % 16 != 0 || p.o_lim != 0 || p.vt_out) return false;
   if (!live()) {
@@ -84,8 +87,11 @@ bool dmx_handle::try_tc(const ConvParams& p, int pro, int epi, const Packed& pk)
   TcOperandA a;
   TcParams t;
   if (!build_tc(p, pk, a, t)) return false;
-  launch_tc_gemm(a, wdev + pk.tc_off,
-                 cfg.precision == DMX_TF32X3 ? wdev + pk.tc_lo_off : nullptr, t, epi, stream);
+  // BF16 build: the layers with a bf16 weight copy (the transformer linears) run
+  // kind::f16; everything else single-pass tf32 as in the TF32 build
+  const float* wk = t.bf16 ? wdev + pk.bf_off : wdev + pk.tc_off;
+  launch_tc_gemm(a, wk, cfg.precision == DMX_TF32X3 ? wdev + pk.tc_lo_off : nullptr, t, epi,
+                 stream);
   ++tc_launches;
   return true;
 }
@@ -163,6 +169,9 @@ bool dmx_handle::build_tc(const ConvParams& p, const Packed& pk, TcOperandA& a, 
   t.o_pcols = p.o_pcols;
   t.o_pstride = p.o_pstride;
   t.err = err;
+  t.bf16 = p.a_bf16;
+  t.out16 = p.out16;
+  if (t.bf16 && !pk.has_bf) return false;
   return tc_gemm_supported(a, t);
 }
 
@@ -302,7 +311,8 @@ void run_dconv_gemm(dmx_handle* h, const DConvFull& dc, float* x, int rows, int 
 void run_dconv(dmx_handle* h, const DConvFull& dc, float* x, int rows, int T, bool round_out) {
   const int C = dc.C, hid = dc.hidden;
   const int64_t positions = (int64_t)rows * T;
-  const bool tf32 = h->cfg.precision == DMX_TF32 || h->cfg.precision == DMX_TF32X3;
+  const bool tf32 = h->cfg.precision == DMX_TF32 || h->cfg.precision == DMX_TF32X3 ||
+                    h->cfg.precision == DMX_BF16;
   const bool has_tc = dc.layer[0].conv1.has_tc && dc.layer[0].conv2.has_tc;
   // TF32 builds: tensor cores (3xTF32, fp32-accurate) for the narrow layers
   // (the fused kernel: one launch per spectral row, three over the tiles of a
@@ -425,14 +435,27 @@ struct XfBufs {
 // is produced already rounded to nearest tf32, so the GEMM skips its converter
 // pass; the operands are the same values the converter would produce.
 bool xf_rounded(const dmx_handle* h) { return h->cfg.precision == DMX_TF32; }
+// The convolution GEMMs run single-pass tf32 in the TF32 and BF16 builds: their
+// producers store operands rounded to nearest tf32 the same way.
+bool conv_rounded(const dmx_handle* h) {
+  return h->cfg.precision == DMX_TF32 || h->cfg.precision == DMX_BF16;
+}
+// The tensor-core attention (tf32) runs in the TF32 and BF16 builds.
+bool tc_attention(const dmx_handle* h) { return conv_rounded(h); }
+// BF16 build: the transformer's linears take bf16 A operands, which their
+// producers (LayerNorm, the first FFN layer, attention) store as bf16.
+bool xf_bf16(const dmx_handle* h) { return h->cfg.precision == DMX_BF16; }
+uint16_t* u16(float* p) { return reinterpret_cast<uint16_t*>(p); }
 
 void xf_gemm(dmx_handle* h, const char* tag, const Packed& pk, const float* in, int B, int n,
              float* out, int epi, const float* res = nullptr, const float* gamma = nullptr,
              double* stats = nullptr, bool round_out = false, float* vt = nullptr,
-             int vt_col0 = 0) {
+             int vt_col0 = 0, bool out_bf16 = false) {
   ConvParams p = base_params(pk, h->wdev);
   p.round_out = round_out;
   p.a_rounded = xf_rounded(h);
+  p.a_bf16 = xf_bf16(h);
+  p.out16 = out_bf16 ? u16(out) : nullptr;
   p.vt_out = vt;
   p.vt_col0 = vt_col0;
   p.vt_ntok = n;
@@ -453,10 +476,10 @@ void xf_tail(dmx_handle* h, const LayerW& L, float* X, int B, int n, const XfBuf
   h->mark("xf.layernorm", 0.0, 8.0 * B * n * 512);
   if (h->live())
     launch_layer_norm(X, (int64_t)B * n, n, h->W(nw.off), h->W(nb.off), nullptr, bb.xn, h->stream,
-                      xf_rounded(h));
+                      xf_rounded(h), xf_bf16(h) ? u16(bb.xn) : nullptr);
   ++h->launches;
   xf_gemm(h, "xf.ffn1", L.lin1, bb.xn, B, n, bb.hid, EPI_GELU, nullptr, nullptr, nullptr,
-          xf_rounded(h));
+          xf_rounded(h), nullptr, 0, xf_bf16(h));
   xf_gemm(h, "xf.ffn2", L.lin2, bb.hid, B, n, X, EPI_RESIDUAL, X, h->W(L.g2.off), bb.stats);
   h->mark("xf.groupnorm", 0.0, 8.0 * B * n * 512);
   if (h->live()) launch_group_norm_apply(X, B, n, bb.stats, h->W(L.now.off), h->W(L.nob.off), h->stream);
@@ -466,17 +489,19 @@ void xf_tail(dmx_handle* h, const LayerW& L, float* X, int B, int n, const XfBuf
 void xf_self(dmx_handle* h, const LayerW& L, float* X, int B, int n, const XfBufs& bb) {
   h->mark("xf.layernorm", 0.0, 8.0 * B * n * 512);
   if (h->live()) launch_layer_norm(X, (int64_t)B * n, n, h->W(L.n1w.off), h->W(L.n1b.off), nullptr, bb.xn,
-                                   h->stream, xf_rounded(h));
+                                   h->stream, xf_rounded(h), xf_bf16(h) ? u16(bb.xn) : nullptr);
   ++h->launches;
-  const bool tc_attn = h->cfg.precision == DMX_TF32;
+  const bool tc_attn = tc_attention(h);
   xf_gemm(h, "xf.qkv", L.qkv, bb.xn, B, n, bb.qkv, EPI_STORE, nullptr, nullptr, nullptr, tc_attn,
           tc_attn ? bb.vt1 : nullptr, 1024);
   h->mark("xf.attention", 4.0 * B * n * n * 512, 4.0 * B * n * 512 * 4);
   if (h->live() && !(tc_attn && launch_attention_tc(bb.qkv, 1536, 0, bb.qkv, 1536, 512, 1024, bb.vt1,
                                                      bb.att, 512, B, 8, n, n, 0.125f, h->err,
-                                                     h->stream)))
+                                                     h->stream, xf_bf16(h) ? u16(bb.att) : nullptr))) {
+    if (xf_bf16(h)) throw Error(DMX_ERR_INVALID, "attention: the bf16 output needs the tensor-core kernel");
     launch_flash_attention(bb.qkv, 1536, bb.qkv + 512, bb.qkv + 1024, 1536, bb.att, 512, B, 8, n, n,
                            0.125f, h->stream);
+  }
   ++h->launches;
   xf_tail(h, L, X, B, n, bb, L.n2w, L.n2b);
 }
@@ -487,9 +512,9 @@ void xf_cross_kv(dmx_handle* h, const LayerW& L, const float* other, int B, int 
   h->mark("xf.layernorm", 0.0, 8.0 * B * n_other * 512);
   if (h->live())
     launch_layer_norm(other, (int64_t)B * n_other, n_other, h->W(L.n2w.off), h->W(L.n2b.off), nullptr,
-                      scratch, h->stream, xf_rounded(h));
+                      scratch, h->stream, xf_rounded(h), xf_bf16(h) ? u16(scratch) : nullptr);
   ++h->launches;
-  const bool tc_attn = h->cfg.precision == DMX_TF32;
+  const bool tc_attn = tc_attention(h);
   xf_gemm(h, "xf.kv", L.kv, scratch, B, n_other, kv_out, EPI_STORE, nullptr, nullptr, nullptr,
           tc_attn, tc_attn ? vt : nullptr, 512);
 }
@@ -498,16 +523,18 @@ void xf_cross(dmx_handle* h, const LayerW& L, float* X, int B, int n, const floa
               const float* vt, int n_other, const XfBufs& bb) {
   h->mark("xf.layernorm", 0.0, 8.0 * B * n * 512);
   if (h->live()) launch_layer_norm(X, (int64_t)B * n, n, h->W(L.n1w.off), h->W(L.n1b.off), nullptr, bb.xn,
-                                   h->stream, xf_rounded(h));
+                                   h->stream, xf_rounded(h), xf_bf16(h) ? u16(bb.xn) : nullptr);
   ++h->launches;
-  const bool tc_attn = h->cfg.precision == DMX_TF32;
+  const bool tc_attn = tc_attention(h);
   xf_gemm(h, "xf.q", L.q, bb.xn, B, n, bb.qkv, EPI_STORE, nullptr, nullptr, nullptr, tc_attn);
   h->mark("xf.attention", 4.0 * B * n * n_other * 512, 4.0 * B * (2.0 * n + 2.0 * n_other) * 512);
   if (h->live() && !(tc_attn && launch_attention_tc(bb.qkv, 512, 0, kv, 1024, 0, 512, vt, bb.att,
                                                      512, B, 8, n, n_other, 0.125f, h->err,
-                                                     h->stream)))
+                                                     h->stream, xf_bf16(h) ? u16(bb.att) : nullptr))) {
+    if (xf_bf16(h)) throw Error(DMX_ERR_INVALID, "attention: the bf16 output needs the tensor-core kernel");
     launch_flash_attention(bb.qkv, 512, kv, kv + 512, 1024, bb.att, 512, B, 8, n, n_other, 0.125f,
                            h->stream);
+  }
   ++h->launches;
   xf_tail(h, L, X, B, n, bb, L.n3w, L.n3b);
 }
@@ -575,12 +602,12 @@ void forward(dmx_handle* h, const float* mix, int G, float* out) {
       p.sx = 4;
       set_output(p, y, G, 1, To, Co);
       h->gemm(p, i == 0 ? PRO_BATCH_AFFINE : PRO_NONE, EPI_GELU, ("tenc.conv" + std::to_string(i)).c_str(), &E.conv);
-      run_dconv(h, h->tenc_dc[i], y, G, To, xf_rounded(h));
+      run_dconv(h, h->tenc_dc[i], y, G, To, conv_rounded(h));
       float* z = h->falloc((size_t)G * To * Co);
       ConvParams r = base_params(E.rewrite, h->wdev);
       set_input(r, y, G, 1, To, Co);
       set_output(r, z, G, 1, To, Co);
-      r.a_rounded = xf_rounded(h);  // the DConv output, rounded
+      r.a_rounded = conv_rounded(h);  // the DConv output, rounded
       h->gemm(r, PRO_NONE, EPI_GLU, ("tenc.rewrite" + std::to_string(i)).c_str(), &E.rewrite);
       tskip[i] = z;
       tin = z;
@@ -599,13 +626,13 @@ void forward(dmx_handle* h, const float* mix, int G, float* out) {
       if (i == 0) p.pro_scale = reinterpret_cast<const float*>(norm_f);
       set_output(p, y, G, Fo, kFrames, Co);
       h->gemm(p, i == 0 ? PRO_BATCH_AFFINE : PRO_NONE, EPI_GELU, ("enc.conv" + std::to_string(i)).c_str(), &E.conv);
-      run_dconv(h, h->enc_dc[i], y, G * Fo, kFrames, xf_rounded(h));
+      run_dconv(h, h->enc_dc[i], y, G * Fo, kFrames, conv_rounded(h));
       float* z = h->falloc((size_t)G * Fo * kFrames * Co);
       ConvParams r = base_params(E.rewrite, h->wdev);
       set_input(r, y, G, Fo, kFrames, Co);
       set_output(r, z, G, Fo, kFrames, Co);
       if (i == 0) r.epi_emb = h->W(m.emb.off);
-      r.a_rounded = xf_rounded(h);  // the DConv output, rounded
+      r.a_rounded = conv_rounded(h);  // the DConv output, rounded
       h->gemm(r, PRO_NONE, i == 0 ? EPI_GLU_EMB : EPI_GLU, ("enc.rewrite" + std::to_string(i)).c_str(), &E.rewrite);
       skip[i] = z;
       xin = z;
@@ -692,13 +719,13 @@ void forward(dmx_handle* h, const float* mix, int G, float* out) {
     p.i_bs = (int64_t)ntok * D;
     set_output(p, x, G, Fb, Tb, Cs[4]);
     p.epi_add = skip[3];
-    p.round_out = xf_rounded(h);  // feeds only the first decoder's rewrite
+    p.round_out = conv_rounded(h);  // feeds only the first decoder's rewrite
     h->gemm(p, PRO_NONE, EPI_STORE, "xf.downsample", &m.down);
     ConvParams q = base_params(m.down_t, h->wdev);
     set_input(q, Tk, G, 1, Tt, D);
     set_output(q, xt, G, 1, Tt, TCs[4]);
     q.epi_add = tskip[3];
-    q.round_out = xf_rounded(h);
+    q.round_out = conv_rounded(h);
     h->gemm(q, PRO_NONE, EPI_STORE, "xf.downsample", &m.down_t);
   }
 
@@ -713,9 +740,9 @@ void forward(dmx_handle* h, const float* mix, int G, float* out) {
       ConvParams r = base_params(Dw.rewrite, h->wdev);
       set_input(r, x, G, F, kFrames, C);
       set_output(r, g, G, F, kFrames, C);
-      r.a_rounded = xf_rounded(h);  // the down-sampler's or previous decoder's output, rounded
+      r.a_rounded = conv_rounded(h);  // the down-sampler's or previous decoder's output, rounded
       h->gemm(r, PRO_NONE, EPI_GLU, ("dec.rewrite" + std::to_string(e)).c_str(), &Dw.rewrite);
-      run_dconv(h, h->dec_dc[e], g, G * F, kFrames, xf_rounded(h));
+      run_dconv(h, h->dec_dc[e], g, G * F, kFrames, conv_rounded(h));
       const int Co = Dw.cout, Fo = 4 * F;
       float* o = h->falloc((size_t)G * Fo * kFrames * Co);
       if (last) {
@@ -732,7 +759,7 @@ void forward(dmx_handle* h, const float* mix, int G, float* out) {
         p.o_xs = (int64_t)Fo * Co;
         p.o_ys = 4LL * Co;
         p.o_off = 0;
-        p.a_rounded = xf_rounded(h);  // the DConv output, rounded
+        p.a_rounded = conv_rounded(h);  // the DConv output, rounded
         h->gemm(p, PRO_NONE, EPI_STORE, ("dec.convtr" + std::to_string(e)).c_str(), &Dw.convt_all);
       } else {
         // tensor-core builds: all four phases in one GEMM over the input rows
@@ -751,8 +778,8 @@ void forward(dmx_handle* h, const float* mix, int G, float* out) {
         p.o_pcols = Co;
         p.o_pstride = (int64_t)kFrames * Co;
         p.epi_add = skip[j - 1];
-        p.a_rounded = xf_rounded(h);  // the DConv output, rounded
-        p.round_out = xf_rounded(h);  // feeds only the next decoder's rewrite
+        p.a_rounded = conv_rounded(h);  // the DConv output, rounded
+        p.round_out = conv_rounded(h);  // feeds only the next decoder's rewrite
         // Only the narrowest of these layers (Cin 96, the largest output) gains: measured on
         // B200, dec.convtr2 1.96 -> 1.19 ms per 42 segments, while at Cin 192 the combined
         // form's zero taps (1.5x the tensor work) made dec.convtr1 slower (0.78 -> 0.96 ms).
@@ -772,8 +799,8 @@ void forward(dmx_handle* h, const float* mix, int G, float* out) {
           p.o_ys = 4LL * kFrames * Co;
           p.o_off = (int64_t)ph * kFrames * Co;
           p.epi_add = skip[j - 1];
-          p.a_rounded = xf_rounded(h);  // the DConv output, rounded
-          p.round_out = xf_rounded(h);  // feeds only the next decoder's rewrite
+          p.a_rounded = conv_rounded(h);  // the DConv output, rounded
+          p.round_out = conv_rounded(h);  // feeds only the next decoder's rewrite
           h->gemm(p, PRO_NONE, EPI_GELU, ("dec.convtr" + std::to_string(e)).c_str(),
                   &Dw.convt[ph]);
         }
@@ -792,9 +819,9 @@ void forward(dmx_handle* h, const float* mix, int G, float* out) {
       ConvParams r = base_params(Dw.rewrite, h->wdev);
       set_input(r, xt, G, 1, Tc, Ct);
       set_output(r, g, G, 1, Tc, Ct);
-      r.a_rounded = xf_rounded(h);  // the down-sampler's or previous decoder's output, rounded
+      r.a_rounded = conv_rounded(h);  // the down-sampler's or previous decoder's output, rounded
       h->gemm(r, PRO_NONE, EPI_GLU, ("tdec.rewrite" + std::to_string(e)).c_str(), &Dw.rewrite);
-      run_dconv(h, h->tdec_dc[e], g, G, Tc, xf_rounded(h));
+      run_dconv(h, h->tdec_dc[e], g, G, Tc, conv_rounded(h));
       const int Co = Dw.cout, len = lengths_t[j];
       float* o = h->falloc((size_t)G * len * Co);
       {
@@ -818,8 +845,8 @@ void forward(dmx_handle* h, const float* mix, int G, float* out) {
         p.o_lim = len;
         p.o_lim_ch = Co;
         if (!last) p.epi_add = tskip[j - 1];
-        p.a_rounded = xf_rounded(h);               // the DConv output, rounded
-        p.round_out = !last && xf_rounded(h);      // feeds only the next decoder's rewrite
+        p.a_rounded = conv_rounded(h);               // the DConv output, rounded
+        p.round_out = !last && conv_rounded(h);      // feeds only the next decoder's rewrite
         h->gemm(p, PRO_NONE, last ? EPI_STORE : EPI_GELU, ("tdec.convtr" + std::to_string(e)).c_str(),
                 &Dw.convt_all);
       }

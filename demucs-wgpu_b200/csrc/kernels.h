@@ -93,9 +93,11 @@ int dconv_tc_const_floats(int C);
 bool launch_dconv_tc(const DConvArgs& a, cudaStream_t s);
 
 // transformer.cu
-// round_out: store the output rounded to nearest tf32 (when it feeds only tf32 GEMMs)
+// round_out: store the output rounded to nearest tf32 (when it feeds only tf32 GEMMs);
+// out16: store it as bf16 there instead of `out` (when it feeds only bf16 GEMMs)
 void launch_layer_norm(const float* x, int64_t rows, int ntok, const float* w, const float* b,
-                       const float* pos, float* out, cudaStream_t s, bool round_out = false);
+                       const float* pos, float* out, cudaStream_t s, bool round_out = false,
+                       uint16_t* out16 = nullptr);
 void launch_group_norm_apply(float* x, int B, int64_t ntok, const double* stats, const float* w,
                              const float* b, cudaStream_t s);
 void launch_flash_attention(const float* q, int ldq, const float* k, const float* v, int ldkv,

@@ -363,12 +363,32 @@ struct Loader {
   }
 
   Packed linear(const std::string& wname, const std::string& bname, int out, int in, int row0,
-                int rows) {
+                int rows, bool bf16 = false) {
     const HostTensor& w = get(wname, {out, in});
     const HostTensor& b = get(bname, {out});
-    return pack(1, in, rows, false, b.data + row0,
-                [&](int, int ci, int co) { return w.data[(size_t)(row0 + co) * in + ci]; },
-                {{0, 0}});
+    Packed p = pack(1, in, rows, false, b.data + row0,
+                    [&](int, int ci, int co) { return w.data[(size_t)(row0 + co) * in + ci]; },
+                    {{0, 0}});
+    if (bf16 && p.has_tc) add_bf16(p, [&](int n, int k) { return w.data[(size_t)(row0 + n) * in + k]; });
+    return p;
+  }
+
+  // bf16 copy of a packed layer's K-major weights, [Npad][K] (zero rows past N):
+  // two bf16 per float slot of the arena, rounded to nearest even.
+  template <class F>
+  void add_bf16(Packed& p, F value) {
+    const size_t count = (size_t)p.Npad * p.K;
+    p.bf_off = wb.alloc((count + 1) / 2);
+    uint16_t* dst = reinterpret_cast<uint16_t*>(&wb.host[p.bf_off]);
+    for (int n = 0; n < p.Npad; ++n)
+      for (int k = 0; k < p.K; ++k) {
+        const float v = n < p.N ? value(n, k) : 0.0f;
+        uint32_t u;
+        std::memcpy(&u, &v, 4);
+        u += 0x7FFFu + ((u >> 16) & 1u);
+        dst[(size_t)n * p.K + k] = (uint16_t)(u >> 16);
+      }
+    p.has_bf = true;
   }
 
 };
@@ -555,6 +575,8 @@ void load_model(dmx_handle* h, const std::map<std::string, HostTensor>& t) {
   m.norm_in_b = L.vec("crosstransformer.norm_in.bias", 512);
   m.norm_in_t_w = L.vec("crosstransformer.norm_in_t.weight", 512);
   m.norm_in_t_b = L.vec("crosstransformer.norm_in_t.bias", 512);
+  // the BF16 build keeps bf16 copies of the transformer linears (kind::f16 GEMMs)
+  const bool bf = h->cfg.precision == DMX_BF16;
   for (int s = 0; s < 2; ++s)
     for (int l = 0; l < 5; ++l) {
       LayerW& Lw = s == 0 ? m.layers[l] : m.layers_t[l];
@@ -562,16 +584,16 @@ void load_model(dmx_handle* h, const std::map<std::string, HostTensor>& t) {
       Lw.cross = l % 2 == 1;
       const std::string attn = at + (Lw.cross ? ".cross_attn" : ".self_attn");
       if (Lw.cross) {
-        Lw.q = L.linear(attn + ".in_proj_weight", attn + ".in_proj_bias", 1536, 512, 0, 512);
-        Lw.kv = L.linear(attn + ".in_proj_weight", attn + ".in_proj_bias", 1536, 512, 512, 1024);
+        Lw.q = L.linear(attn + ".in_proj_weight", attn + ".in_proj_bias", 1536, 512, 0, 512, bf);
+        Lw.kv = L.linear(attn + ".in_proj_weight", attn + ".in_proj_bias", 1536, 512, 512, 1024, bf);
         Lw.n3w = L.vec(at + ".norm3.weight", 512);
         Lw.n3b = L.vec(at + ".norm3.bias", 512);
       } else {
-        Lw.qkv = L.linear(attn + ".in_proj_weight", attn + ".in_proj_bias", 1536, 512, 0, 1536);
+        Lw.qkv = L.linear(attn + ".in_proj_weight", attn + ".in_proj_bias", 1536, 512, 0, 1536, bf);
       }
-      Lw.out = L.linear(attn + ".out_proj.weight", attn + ".out_proj.bias", 512, 512, 0, 512);
-      Lw.lin1 = L.linear(at + ".linear1.weight", at + ".linear1.bias", 2048, 512, 0, 2048);
-      Lw.lin2 = L.linear(at + ".linear2.weight", at + ".linear2.bias", 512, 2048, 0, 512);
+      Lw.out = L.linear(attn + ".out_proj.weight", attn + ".out_proj.bias", 512, 512, 0, 512, bf);
+      Lw.lin1 = L.linear(at + ".linear1.weight", at + ".linear1.bias", 2048, 512, 0, 2048, bf);
+      Lw.lin2 = L.linear(at + ".linear2.weight", at + ".linear2.bias", 512, 2048, 0, 512, bf);
       Lw.n1w = L.vec(at + ".norm1.weight", 512);
       Lw.n1b = L.vec(at + ".norm1.bias", 512);
       Lw.n2w = L.vec(at + ".norm2.weight", 512);

@@ -64,7 +64,9 @@ struct Packed {
   size_t w_off = 0, b_off = 0;  // float offsets into the weight arena
   size_t tc_off = 0;            // K-major copy [Npad][K], rounded to nearest tf32
   size_t tc_lo_off = 0;         // its residual w - tf32(w) (3xTF32 split)
+  size_t bf_off = 0;            // bf16 copy [Npad][K], round to nearest even (BF16 build)
   bool has_tc = false;
+  bool has_bf = false;
   int cin = 0;       // input channels as packed (zero rows pad it to a multiple of 16)
   int cin_real = 0;  // the layer's own input channels (for the work count)
   double flop_scale = 1.0;  // algorithmic share of the packed K (structural zeros excluded)

@@ -115,6 +115,15 @@ DMX_DEVICE void umma_tf32(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint3
       "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
       "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate));
 }
+// D (+)= A * B^T with bf16 A and B (K = 16 per instruction), f32 accumulate.
+DMX_DEVICE void umma_bf16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                          uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate));
+}
 // Same MMA with the A operand in tensor memory (M = 128 lanes, K columns).
 DMX_DEVICE void umma_tf32_ta(uint32_t tmem_d, uint32_t tmem_a, uint64_t bdesc, uint32_t idesc,
                              uint32_t accumulate) {
@@ -249,16 +258,17 @@ inline PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
 
 // `elem_strides` (optional): traversal stride per dimension — a box of
 // extent e with stride s loads ceil(e / s) elements, every s-th one.
-inline bool make_tensor_map(CUtensorMap* map, const float* base, int rank, const cuuint64_t* dims,
+inline bool make_tensor_map(CUtensorMap* map, const void* base, int rank, const cuuint64_t* dims,
               const cuuint64_t* strides_bytes, const cuuint32_t* box, CUtensorMapSwizzle swz,
-              const cuuint32_t* elem_strides = nullptr) {
+              const cuuint32_t* elem_strides = nullptr,
+              CUtensorMapDataType dtype = CU_TENSOR_MAP_DATA_TYPE_FLOAT32) {
   auto fn = tensor_map_encoder();
   if (!fn) return false;
   cuuint32_t estr[5] = {1, 1, 1, 1, 1};
   if (elem_strides)
     for (int i = 0; i < rank; ++i) estr[i] = elem_strides[i];
-  const CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, (cuuint32_t)rank,
-                        const_cast<float*>(base), dims, strides_bytes, box, estr,
+  const CUresult r = fn(map, dtype, (cuuint32_t)rank, const_cast<void*>(base), dims,
+                        strides_bytes, box, estr,
                         CU_TENSOR_MAP_INTERLEAVE_NONE, swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS;

@@ -1,4 +1,5 @@
 // tcgen05 implicit-GEMM kernel (see tc_gemm.cuh for the design).
+#include <cuda_bf16.h>
 #include <cudaTypedefs.h>
 
 #include <algorithm>
@@ -16,16 +17,32 @@ constexpr int BM = 128;
 constexpr int kThreads = 448;  // warp 0 TMA, warp 1 MMA, warps 2-5 converter, warps 6-13 epilogue
 constexpr int kEpiThreads = 256;
 
-template <int BN, int BK, int STAGES, bool SPLIT>
+// Arithmetic of the contraction: MODE_TF32 (operands rounded to nearest tf32),
+// MODE_SPLIT (3xTF32: hi*hi + hi*lo + lo*hi), MODE_BF16 (kind::f16: A is a
+// bf16 activation tile and B a bf16 weight tile, both loaded by TMA as they
+// lie in HBM, f32 accumulate; no converter pass).
+constexpr int MODE_TF32 = 0, MODE_SPLIT = 1, MODE_BF16 = 2;
+
+template <int BN, int BK, int STAGES, int MODE>
 struct Smem {
-  static constexpr int A_BYTES = BM * BK * 4;
-  static constexpr int B_BYTES = BN * BK * 4;
+  static constexpr bool SPLIT = MODE == MODE_SPLIT, BF = MODE == MODE_BF16;
+  static constexpr int ELEM = BF ? 2 : 4;
+  static constexpr int A_BYTES = BM * BK * ELEM;
+  static constexpr int B_BYTES = BN * BK * ELEM;
   // stage: A | B [| A_lo | B_lo]; TMA fills A, B (and B_lo), the converter
   // warps round A in place (and write A_lo)
   static constexpr int STAGE_BYTES = SPLIT ? 2 * (A_BYTES + B_BYTES) : A_BYTES + B_BYTES;
   static constexpr int TMA_BYTES = SPLIT ? A_BYTES + 2 * B_BYTES : A_BYTES + B_BYTES;
   static constexpr int TOTAL = STAGES * STAGE_BYTES + 1024 /*align*/ + 512 /*barriers*/;
+  static_assert(!BF || BK == 32, "bf16 tiles are 32 channels: 64-byte swizzled rows");
+  static_assert(STAGE_BYTES % 1024 == 0, "stages keep the 1024-byte swizzle alignment");
 };
+
+// two fp32 -> one bf16x2 word, round to nearest even (lo in the low half)
+DMX_DEVICE uint32_t pack_bf16(float lo, float hi) {
+  const __nv_bfloat162 v = __float22bfloat162_rn(make_float2(lo, hi));
+  return *reinterpret_cast<const uint32_t*>(&v);
+}
 
 // Origin of output-row tile `mt` (see TcAMode).
 DMX_DEVICE void tile_origin(const TcParams& p, int mt, int& tb, int& ty0, int& tx0, int64_t& m0) {
@@ -49,11 +66,12 @@ DMX_DEVICE void tile_origin(const TcParams& p, int mt, int& tb, int& ty0, int& t
 // tile) space in row-major order, so the column tiles of one row tile run on
 // neighbouring SMs at the same time and its A rows come from HBM once. Two
 // TMEM accumulators: the epilogue of one tile overlaps the MMAs of the next.
-template <int BN, int BK, int STAGES, int EPI, bool SPLIT>
+template <int BN, int BK, int STAGES, int EPI, int MODE>
 __global__ void __launch_bounds__(kThreads, 1)
     tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const __grid_constant__ CUtensorMap tmBlo, const TcParams p) {
-  using S = Smem<BN, BK, STAGES, SPLIT>;
+  using S = Smem<BN, BK, STAGES, MODE>;
+  constexpr bool SPLIT = S::SPLIT, BF = S::BF;
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   unsigned char* smem = reinterpret_cast<unsigned char*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
@@ -94,7 +112,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int total = p.mtiles * p.ntiles;
   // A already rounded to tf32 (and no split): the MMA consumes the TMA tile
   // directly and the converter warps stay idle
-  const bool direct = !SPLIT && p.a_rounded && !p.a_stats;
+  const bool direct = BF || (!SPLIT && p.a_rounded && !p.a_stats);
 
   if (warp == 0) {
     if (lane == 0) {
@@ -139,7 +157,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (warp == 1) {
     if (lane == 0) {
       // ---------------- MMA issuer ----------------
-      constexpr uint32_t idesc = (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)(BN >> 3) << 17) |
+      // instruction descriptor: f32 accumulator; A and B both tf32 (2) or both bf16 (1)
+      constexpr uint32_t ab = BF ? 1u : 2u;
+      constexpr uint32_t idesc = (1u << 4) | (ab << 7) | (ab << 10) | ((uint32_t)(BN >> 3) << 17) |
                                  ((uint32_t)(BM >> 4) << 24);
       uint32_t it = 0;
       int tl = 0;
@@ -161,8 +181,15 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint32_t b_addr = a_addr + S::A_BYTES;
           const uint32_t alo_addr = b_addr + S::B_BYTES;
           const uint32_t blo_addr = alo_addr + S::A_BYTES;
+          if (BF) {
+            // two K = 16 steps across the 64-byte bf16 rows of A and B
 #pragma unroll
-          for (int j = 0; j < BK / 8; ++j) {
+            for (int j = 0; j < BK / 16; ++j)
+              umma_bf16(d, umma_desc_k(a_addr + j * 32, BK * 2), umma_desc_k(b_addr + j * 32, BK * 2),
+                        idesc, (kt | j) != 0);
+          }
+#pragma unroll
+          for (int j = 0; j < (BF ? 0 : BK / 8); ++j) {
             const uint64_t ad = umma_desc_k(a_addr + j * 32, BK * 4);
             const uint64_t bd = umma_desc_k(b_addr + j * 32, BK * 4);
             if (SPLIT) {
@@ -399,14 +426,29 @@ __global__ void __launch_bounds__(kThreads, 1)
               for (int j = 0; j < 32; ++j)
                 if (nb + j < ncol) vt[(int64_t)j * p.vt_ntok] = v[j];
             }
-            float* o = p.out + orow + nb;
-            if (vec) {
+            if (p.out16) {
+              // bf16 output (the A operand of a bf16 GEMM): 32 values in 64 bytes
+              uint16_t* o16 = p.out16 + orow + nb;
+              if (full && ((orow + nb) & 7) == 0) {
 #pragma unroll
-              for (int j = 0; j < 32; j += 4)
-                *reinterpret_cast<float4*>(o + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+                for (int j = 0; j < 32; j += 8)
+                  *reinterpret_cast<uint4*>(o16 + j) =
+                      make_uint4(pack_bf16(v[j], v[j + 1]), pack_bf16(v[j + 2], v[j + 3]),
+                                 pack_bf16(v[j + 4], v[j + 5]), pack_bf16(v[j + 6], v[j + 7]));
+              } else {
+                for (int j = 0; j < 32; ++j)
+                  if (nb + j < ncol) o16[j] = (uint16_t)(pack_bf16(v[j], 0.f) & 0xFFFFu);
+              }
             } else {
-              for (int j = 0; j < 32; ++j)
-                if (nb + j < ncol) o[j] = v[j];
+              float* o = p.out + orow + nb;
+              if (vec) {
+#pragma unroll
+                for (int j = 0; j < 32; j += 4)
+                  *reinterpret_cast<float4*>(o + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+              } else {
+                for (int j = 0; j < 32; ++j)
+                  if (nb + j < ncol) o[j] = v[j];
+              }
             }
           }
           if (EPI == EPI_GLU || EPI == EPI_GLU_EMB) {
@@ -572,17 +614,17 @@ __global__ void __launch_bounds__(kThreads, 1)
 // ---------------------------------------------------------------------------
 // host side
 // ---------------------------------------------------------------------------
-template <int BN, int BK, int STAGES, bool SPLIT>
+template <int BN, int BK, int STAGES, int MODE>
 void launch_cfg(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mblo,
                 const TcParams& p, int epi, dim3 grid, cudaStream_t s) {
-  const int smem = Smem<BN, BK, STAGES, SPLIT>::TOTAL;
+  const int smem = Smem<BN, BK, STAGES, MODE>::TOTAL;
 #define DMX_TC_CASE(E)                                                                        \
   case E: {                                                                                   \
     static PerDevice attr;                                                                    \
     if (attr.first())                                                                         \
-      cudaFuncSetAttribute(tc_gemm_kernel<BN, BK, STAGES, E, SPLIT>,                          \
+      cudaFuncSetAttribute(tc_gemm_kernel<BN, BK, STAGES, E, MODE>,                          \
                            cudaFuncAttributeMaxDynamicSharedMemorySize, smem);                                                                                         \
-    tc_gemm_kernel<BN, BK, STAGES, E, SPLIT><<<grid, kThreads, smem, s>>>(ma, mb, mblo, p);   \
+    tc_gemm_kernel<BN, BK, STAGES, E, MODE><<<grid, kThreads, smem, s>>>(ma, mb, mblo, p);   \
     break;                                                                                    \
   }
   switch (epi) {
@@ -626,6 +668,13 @@ bool tc_gemm_supported(const TcOperandA& a, const TcParams& p) {
   if (p.epi_stats && (p.mode == TC_2D || !p.epi_rowpart || p.epi_rowlen <= 0)) return false;
   const int bk = (p.Cin % 32 == 0) ? 32 : (p.Cin % 16 == 0 ? 16 : 0);
   if (bk == 0) return false;
+  // bf16: row-major bf16 activations [rows][C] (16-byte row pitch) times the bf16
+  // weight copy; stores fp32 or (STORE / GELU, unsplit columns) bf16
+  if (p.bf16 && (p.mode != TC_ROWS || bk != 32 || p.Kpad % 32 != 0 || p.a_stats ||
+                 (a.sw * 2) % 16 != 0 || p.vt_out || p.o_pcols || p.o_lim || p.epi_add ||
+                 p.round_out))
+    return false;
+  if (p.out16 && !p.bf16) return false;
   if (p.mode == TC_2D || p.mode == TC_1D) {
     if (a.C != p.Cin) return false;
     if ((a.sw * 4) % 16 || (a.sh * 4) % 16 || (a.sb * 4) % 16) return false;
@@ -633,7 +682,7 @@ bool tc_gemm_supported(const TcOperandA& a, const TcParams& p) {
     if (!strided && (p.sy != 1 || p.sx != 1)) return false;
   } else {
     if (p.ntaps != 1 || p.sy != 1 || p.sx != 1) return false;
-    if ((a.sw * 4) % 16) return false;
+    if (!p.bf16 && (a.sw * 4) % 16) return false;
   }
   if ((reinterpret_cast<uintptr_t>(a.ptr) & 15) != 0) return false;
   return true;
@@ -662,6 +711,13 @@ void launch_tc_gemm(const TcOperandA& a, const float* wk, const float* wk_lo, co
     const cuuint32_t estr[3] = {1, (cuuint32_t)p.sx, 1};
     ok = make_tensor_map(&ma, a.ptr, 3, dims, str, box, swz, estr);
     p.mtiles = ((p.Wq + BM - 1) / BM) * p.B;
+  } else if (p.bf16) {  // bf16 activations [rows][C]: 64-byte rows of 32 channels
+    const cuuint64_t dims[2] = {(cuuint64_t)a.C, (cuuint64_t)a.W};
+    const cuuint64_t str[1] = {(cuuint64_t)a.sw * 2};
+    const cuuint32_t box[2] = {32, (cuuint32_t)BM};
+    ok = make_tensor_map(&ma, a.ptr, 2, dims, str, box, CU_TENSOR_MAP_SWIZZLE_64B, nullptr,
+                         CU_TENSOR_MAP_DATA_TYPE_BFLOAT16);
+    p.mtiles = (a.W + BM - 1) / BM;
   } else {
     const cuuint64_t dims[2] = {(cuuint64_t)a.C, (cuuint64_t)a.W};
     const cuuint64_t str[1] = {(cuuint64_t)a.sw * 4};
@@ -669,7 +725,14 @@ void launch_tc_gemm(const TcOperandA& a, const float* wk, const float* wk_lo, co
     ok = make_tensor_map(&ma, a.ptr, 2, dims, str, box, swz);
     p.mtiles = (a.W + BM - 1) / BM;
   }
-  {
+  if (p.bf16) {  // bf16 weights [Npad][Kpad]: 64-byte rows of 32 channels
+    const cuuint64_t dims[2] = {(cuuint64_t)p.Kpad, (cuuint64_t)p.Npad};
+    const cuuint64_t str[1] = {(cuuint64_t)p.Kpad * 2};
+    const cuuint32_t box[2] = {32, (cuuint32_t)bn};
+    ok = ok && make_tensor_map(&mb, wk, 2, dims, str, box, CU_TENSOR_MAP_SWIZZLE_64B, nullptr,
+                               CU_TENSOR_MAP_DATA_TYPE_BFLOAT16);
+    mblo = mb;
+  } else {
     const cuuint64_t dims[2] = {(cuuint64_t)p.Kpad, (cuuint64_t)p.Npad};
     const cuuint64_t str[1] = {(cuuint64_t)p.Kpad * 4};
     const cuuint32_t box[2] = {(cuuint32_t)bk, (cuuint32_t)bn};
@@ -680,26 +743,30 @@ void launch_tc_gemm(const TcOperandA& a, const float* wk, const float* wk_lo, co
   p.ntiles = (p.N + bn - 1) / bn;
   const int64_t total = (int64_t)p.mtiles * p.ntiles;
   const dim3 grid((unsigned)std::min<int64_t>(total, sm_count()));
-  if (wk_lo) {  // 3xTF32: split stages are twice the size
+  if (p.bf16) {  // bf16 operands: 32-channel K tiles only (checked by tc_gemm_supported)
+    if (bn == 64) launch_cfg<64, 32, 12, MODE_BF16>(ma, mb, mblo, p, epi, grid, s);
+    else if (bn == 128) launch_cfg<128, 32, 10, MODE_BF16>(ma, mb, mblo, p, epi, grid, s);
+    else launch_cfg<256, 32, 8, MODE_BF16>(ma, mb, mblo, p, epi, grid, s);
+  } else if (wk_lo) {  // 3xTF32: split stages are twice the size
     if (bn == 64) {
-      if (bk == 32) launch_cfg<64, 32, 4, true>(ma, mb, mblo, p, epi, grid, s);
-      else launch_cfg<64, 16, 8, true>(ma, mb, mblo, p, epi, grid, s);
+      if (bk == 32) launch_cfg<64, 32, 4, MODE_SPLIT>(ma, mb, mblo, p, epi, grid, s);
+      else launch_cfg<64, 16, 8, MODE_SPLIT>(ma, mb, mblo, p, epi, grid, s);
     } else if (bn == 128) {
-      if (bk == 32) launch_cfg<128, 32, 3, true>(ma, mb, mblo, p, epi, grid, s);
-      else launch_cfg<128, 16, 6, true>(ma, mb, mblo, p, epi, grid, s);
+      if (bk == 32) launch_cfg<128, 32, 3, MODE_SPLIT>(ma, mb, mblo, p, epi, grid, s);
+      else launch_cfg<128, 16, 6, MODE_SPLIT>(ma, mb, mblo, p, epi, grid, s);
     } else {
-      if (bk == 32) launch_cfg<256, 32, 2, true>(ma, mb, mblo, p, epi, grid, s);
-      else launch_cfg<256, 16, 4, true>(ma, mb, mblo, p, epi, grid, s);
+      if (bk == 32) launch_cfg<256, 32, 2, MODE_SPLIT>(ma, mb, mblo, p, epi, grid, s);
+      else launch_cfg<256, 16, 4, MODE_SPLIT>(ma, mb, mblo, p, epi, grid, s);
     }
   } else if (bn == 64) {
-    if (bk == 32) launch_cfg<64, 32, 8, false>(ma, mb, mblo, p, epi, grid, s);
-    else launch_cfg<64, 16, 12, false>(ma, mb, mblo, p, epi, grid, s);
+    if (bk == 32) launch_cfg<64, 32, 8, MODE_TF32>(ma, mb, mblo, p, epi, grid, s);
+    else launch_cfg<64, 16, 12, MODE_TF32>(ma, mb, mblo, p, epi, grid, s);
   } else if (bn == 128) {
-    if (bk == 32) launch_cfg<128, 32, 6, false>(ma, mb, mblo, p, epi, grid, s);
-    else launch_cfg<128, 16, 8, false>(ma, mb, mblo, p, epi, grid, s);
+    if (bk == 32) launch_cfg<128, 32, 6, MODE_TF32>(ma, mb, mblo, p, epi, grid, s);
+    else launch_cfg<128, 16, 8, MODE_TF32>(ma, mb, mblo, p, epi, grid, s);
   } else {
-    if (bk == 32) launch_cfg<256, 32, 4, false>(ma, mb, mblo, p, epi, grid, s);
-    else launch_cfg<256, 16, 6, false>(ma, mb, mblo, p, epi, grid, s);
+    if (bk == 32) launch_cfg<256, 32, 4, MODE_TF32>(ma, mb, mblo, p, epi, grid, s);
+    else launch_cfg<256, 16, 6, MODE_TF32>(ma, mb, mblo, p, epi, grid, s);
   }
   if (p.epi_stats && stats_epi(epi)) {
     const int64_t positions = (int64_t)p.B * p.Hq * p.Wq;

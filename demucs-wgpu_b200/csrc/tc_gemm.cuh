@@ -49,6 +49,8 @@ struct TcParams {
   int vt_col0, vt_ntok;
   int o_lim, o_lim_ch;  // as in ConvParams
   int a_rounded;  // A holds tf32-rounded values: the MMA reads the TMA tile as landed
+  int bf16;       // kind::f16: A is a bf16 activation matrix (TC_ROWS), wk the bf16 weight copy
+  uint16_t* out16;  // EPI_STORE / EPI_GELU: store bf16 values here instead of `out`
   int o_pcols;          // as in ConvParams: column groups stored o_pstride apart (0 = off)
   int64_t o_pstride;
   // EPI_DCONV_TAIL: row moments of the GLU input (sum, sum of squares per
@@ -83,16 +85,18 @@ struct TcOperandA {
 bool tc_gemm_supported(const TcOperandA& a, const TcParams& p);
 // Partials per output position of the row-moment epilogues (two per column tile).
 int tc_gemm_stat_slots(int N);
-// wk: K-major weights rounded to nearest tf32; wk_lo: their residuals
-// (w - tf32(w)) for the 3xTF32 split, or null for single-pass TF32.
+// wk: K-major weights rounded to nearest tf32 (or, with p.bf16, their bf16
+// copy [Npad][Kpad]); wk_lo: their residuals (w - tf32(w)) for the 3xTF32
+// split, or null.
 void launch_tc_gemm(const TcOperandA& a, const float* wk, const float* wk_lo, const TcParams& p,
                     int epi, cudaStream_t s);
 
 // Tensor-core flash attention (attention_tc.cu). Returns false when the shape
 // is not supported (the caller then uses the SIMT kernel).
 // vt: V^T as (segment, head, dim, key), written by the projection epilogue.
+// out16: store the output as bf16 there instead of `out` (row pitch ldo elements).
 bool launch_attention_tc(const float* q, int ldq, int q_col, const float* kv, int ldkv, int k_col,
                          int v_col, const float* vt, float* out, int ldo, int B, int heads, int nq,
-                         int nk, float scale, int* err, cudaStream_t s);
+                         int nk, float scale, int* err, cudaStream_t s, uint16_t* out16 = nullptr);
 
 }  // namespace dmx

@@ -7,6 +7,8 @@
 //  * flash_attention: softmax(q k^T / 8) v for 8 heads of 64 with an online
 //    softmax, never materialising the score matrix (host.rs:1199-1312,
 //    ops.rs:1350-1458).
+#include <cuda_bf16.h>
+
 #include "common.cuh"
 #include "kernels.h"
 
@@ -20,7 +22,7 @@ namespace {
 __global__ void layer_norm_kernel(const float* __restrict__ x, int64_t rows, int ntok,
                                   const float* __restrict__ w, const float* __restrict__ b,
                                   const float* __restrict__ pos, float* __restrict__ out,
-                                  int round_out) {
+                                  int round_out, uint16_t* __restrict__ out16) {
   const int64_t row = (int64_t)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
   if (row >= rows) return;
   const int lane = threadIdx.x & 31;
@@ -61,6 +63,15 @@ __global__ void layer_norm_kernel(const float* __restrict__ x, int64_t rows, int
       r.y += p4.y;
       r.z += p4.z;
       r.w += p4.w;
+    }
+    if (out16) {  // the output feeds only bf16 GEMMs: stored as bf16
+      const __nv_bfloat162 lo = __float22bfloat162_rn(make_float2(r.x, r.y));
+      const __nv_bfloat162 hi = __float22bfloat162_rn(make_float2(r.z, r.w));
+      uint2 u;
+      u.x = *reinterpret_cast<const uint32_t*>(&lo);
+      u.y = *reinterpret_cast<const uint32_t*>(&hi);
+      *reinterpret_cast<uint2*>(out16 + row * 512 + c) = u;
+      continue;
     }
     if (round_out) {  // the output feeds only tf32 GEMMs: round to nearest here, once
       r.x = round_tf32(r.x);
@@ -216,9 +227,10 @@ __global__ void __launch_bounds__(256) flash_attention_kernel(
 }  // namespace
 
 void launch_layer_norm(const float* x, int64_t rows, int ntok, const float* w, const float* b,
-                       const float* pos, float* out, cudaStream_t s, bool round_out) {
+                       const float* pos, float* out, cudaStream_t s, bool round_out,
+                       uint16_t* out16) {
   layer_norm_kernel<<<(unsigned)((rows + 7) / 8), 256, 0, s>>>(x, rows, ntok, w, b, pos, out,
-                                                               round_out ? 1 : 0);
+                                                               round_out ? 1 : 0, out16);
 }
 
 void launch_group_norm_apply(float* x, int B, int64_t ntok, const double* stats, const float* w,

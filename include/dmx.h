@@ -37,7 +37,10 @@ enum {
  *       accumulate (the SNR >= 60 dB build).
  * TF32X3: tcgen05 kind::tf32 on split operands, hi*hi + hi*lo + lo*hi
  *       (fp32-class accuracy on the tensor cores).
- * BF16: reserved. */
+ * BF16: the TF32 build with the transformer's linears (q/k/v, output
+ *       projection, both FFN layers) on tcgen05 kind::f16 with bf16 operands
+ *       (activations packed to bf16 in shared memory, bf16 weight copies) and
+ *       fp32 accumulate; convolutions, DConv and attention as in TF32. */
 typedef enum { DMX_FP32 = 0, DMX_TF32 = 1, DMX_BF16 = 2, DMX_TF32X3 = 3 } dmx_precision;
 
 typedef struct {

