@@ -671,10 +671,10 @@ bool tc_gemm_supported(const TcOperandA& a, const TcParams& p) {
   // bf16: row-major bf16 activations [rows][C] (16-byte row pitch) times the bf16
   // weight copy; stores fp32 or (STORE / GELU, unsplit columns) bf16
   if (p.bf16 && (p.mode != TC_ROWS || bk != 32 || p.Kpad % 32 != 0 || p.a_stats ||
-                 (a.sw * 2) % 16 != 0 || p.vt_out || p.o_pcols || p.o_lim || p.epi_add ||
-                 p.round_out))
+                 (a.sw * 2) % 16 != 0))
     return false;
-  if (p.out16 && !p.bf16) return false;
+  if (p.out16 && (!p.bf16 || p.vt_out || p.o_pcols || p.o_lim || p.epi_add || p.round_out))
+    return false;
   if (p.mode == TC_2D || p.mode == TC_1D) {
     if (a.C != p.Cin) return false;
     if ((a.sw * 4) % 16 || (a.sh * 4) % 16 || (a.sb * 4) % 16) return false;
