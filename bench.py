@@ -132,15 +132,16 @@ def roofline(stages):
     return out
 
 
-def fp32_class_leg(track_dev, n, chunks, dev, steps=2):
-    """The fp32-accurate tensor-core build (TF32X3: split operands, the max-abs 1e-4
-    gate) on the same workload, device-timed with CUDA events, so the fp32-class
-    throughput is measured beside the TF32 headline."""
+def build_leg(track_dev, n, chunks, dev, precision, gate, steps=2):
+    """Another build on the same workload, device-timed with CUDA events: the
+    fp32-accurate tensor-core build (TF32X3, the max-abs 1e-4 gate) and the BF16
+    build (bf16 transformer linears, the SNR >= 60 dB gate) beside the TF32
+    headline."""
     import torch
     import dmx
 
     h = dmx.Handle(synth.write_safetensors(synth.random_weights(0)), device=dev, max_batch=chunks,
-                   precision=dmx.TF32X3)
+                   precision=getattr(dmx, precision))
     stems = torch.empty((4, 2, n), dtype=torch.float32, device=f"cuda:{dev}")
     stream = torch.cuda.ExternalStream(h.stream, device=f"cuda:{dev}")
     torch.cuda.synchronize()
@@ -156,9 +157,8 @@ def fp32_class_leg(track_dev, n, chunks, dev, steps=2):
     del stems
     torch.cuda.empty_cache()
     h.close()
-    return {"precision": "TF32X3", "value": round(n / SR / (ms / 1e3), 3), "unit": UNIT,
-            "ms_per_step": round(ms, 3), "steps": steps, "warmup": 1,
-            "gate": "per-stem max-abs <= 1e-4 vs the oracle (tests/test_track_gpu.py)"}
+    return {"precision": precision, "value": round(n / SR / (ms / 1e3), 3), "unit": UNIT,
+            "ms_per_step": round(ms, 3), "steps": steps, "warmup": 1, "gate": gate}
 
 
 class ClockSampler:
@@ -539,7 +539,11 @@ def run_ours(args, rank, world, local_rank):
     if match is not None:
         line["stems_match_1gpu"] = match
     if world == 1 and args.precision == "TF32" and not args.no_fp32_class:
-        line["fp32_class"] = fp32_class_leg(lr, n, p.chunks, dev)
+        line["fp32_class"] = build_leg(lr, n, p.chunks, dev, "TF32X3",
+                                       "per-stem max-abs <= 1e-4 vs the oracle (tests/test_track_gpu.py)")
+        line["bf16_build"] = build_leg(lr, n, p.chunks, dev, "BF16",
+                                       "per-stem SNR >= 60 dB vs the oracle (tests/test_track_gpu.py, "
+                                       "tests/test_tf32_gpu.py)", steps=3)
     if rank == 0 and world == 1 and not args.no_cpu:
         line["cpu_baseline"] = cpu_baseline()
     if rank == 0:
@@ -741,7 +745,7 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--precision", default="TF32", choices=["FP32", "TF32", "TF32X3", "BF16"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU-baseline leg")
-    ap.add_argument("--no-fp32-class", action="store_true", help="skip the TF32X3 leg")
+    ap.add_argument("--no-fp32-class", action="store_true", help="skip the TF32X3 and BF16 legs")
     ap.add_argument("--ref-chunks", type=int, default=2,
                     help="reference arm: chunks of the workload's track per step (a prefix)")
     ap.add_argument("--e2e-batch", type=int, default=0,
