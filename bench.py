@@ -737,6 +737,67 @@ def run_batch(args, rank, world, dev, dist):
         dist.destroy_process_group()
 
 
+def run_suite(args):
+    """Kernel suite (the benchmark's isolated-kernel configuration): every launch of a
+    one-segment forward (config 1 shapes: the conv implicit GEMMs such as enc1 96 x 43008 x
+    384, the 3x3 decoder rewrites, the transformer linears M = 2688 / 1344, K = 512,
+    N = 512 / 1536 / 2048 and FFN2 K = 2048, attention 8 x 64 over 2688^2, 1344^2 and the
+    cross shapes) timed with CUDA events, for each build. The GPU is held behind a sleep
+    kernel while the host enqueues the forward, so consecutive events bracket kernels that
+    run back to back. Inputs: N(0, 0.1^2) audio; random-init weights (LayerScale 1e-4)."""
+    import torch
+    import dmx
+
+    dev = 0
+    torch.cuda.set_device(dev)
+    hbm, bf16_burst, _, kind = _peaks()
+    blob = synth.write_safetensors(synth.random_weights(0))
+    G = args.suite_batch
+    mix = torch.from_numpy(synth.gaussian_audio(1, G)).to(f"cuda:{dev}")
+    out = torch.empty((G, 4, 2, SEGMENT), dtype=torch.float32, device=f"cuda:{dev}")
+    builds = {}
+    for prec in args.suite_builds.split(","):
+        h = dmx.Handle(blob, device=dev, max_batch=G, precision=getattr(dmx, prec))
+        stream = torch.cuda.ExternalStream(h.stream, device=f"cuda:{dev}")
+        torch.cuda.synchronize()
+        for _ in range(args.warmup):
+            h.forward_device(mix.data_ptr(), G, out.data_ptr())
+        h.synchronize()
+        h.set_stage_timing(True)
+        runs = []
+        for _ in range(args.steps):
+            with torch.cuda.stream(stream):
+                torch.cuda._sleep(60_000_000)  # ~30 ms: the whole forward is enqueued behind it
+            h.forward_device(mix.data_ptr(), G, out.data_ptr())
+            h.synchronize()
+            runs.append(h.stage_times(work=True))
+        h.set_stage_timing(False)
+        tags = {}
+        for tag in runs[0]:
+            ms = float(np.median([r[tag][0] for r in runs]))
+            _, launches, flops, nbytes = runs[0][tag]
+            e = {"ms": round(ms, 4), "launches": launches, "us_per_launch": round(1e3 * ms / launches, 2)}
+            if flops:
+                tf = flops / (ms / 1e3) / 1e12
+                e.update(tflops=round(tf, 2), frac_of_bf16_burst=round(tf / bf16_burst, 4),
+                         gflop=round(flops / 1e9, 3))
+            if nbytes:
+                gbs = nbytes / (ms / 1e3) / 1e9
+                e.update(gbs=round(gbs, 1), frac_of_hbm=round(gbs / hbm, 4))
+            tags[tag] = e
+        total = sum(v["ms"] for v in tags.values())
+        builds[prec] = {"forward_ms": round(total, 3),
+                        "kernels": dict(sorted(tags.items(), key=lambda kv: -kv[1]["ms"]))}
+        h.close()
+    line = {"suite": "kernels", "segments": G, "steps": args.steps, "warmup": args.warmup,
+            "peaks": {"hbm_gbs": hbm, "bf16_tflops_burst": bf16_burst, "kind": kind},
+            "note": "per-launch CUDA events with the GPU held behind a sleep kernel while the "
+                    "forward is enqueued; TFLOP/s from the algorithmic FLOPs of each launch; "
+                    "tf32 dense peak is half the bf16 one (datasheet ratio)",
+            "builds": builds}
+    print(json.dumps(line), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -753,6 +814,10 @@ def main():
     ap.add_argument("--seconds", type=float, default=None,
                     help="track length (the benchmark is 240 s, 180 s per track for --workload "
                          "batch; shorter tracks are for profiling)")
+    ap.add_argument("--suite", default=None, choices=["kernels"],
+                    help="kernels: time every launch of a forward of --suite-batch segments per build")
+    ap.add_argument("--suite-batch", type=int, default=1)
+    ap.add_argument("--suite-builds", default="TF32,BF16,TF32X3,FP32")
     ap.add_argument("--workload", default="track", choices=["track", "bag", "batch"],
                     help="track: one 240 s track (the headline); bag: the htdemucs_ft bag of 4; "
                          "batch: the many-track throughput batch")
@@ -768,7 +833,9 @@ def main():
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", str(args.gpus)))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
-    if args.impl == "reference":
+    if args.suite == "kernels":
+        run_suite(args)
+    elif args.impl == "reference":
         run_reference(args, rank, world)
     else:
         run_ours(args, rank, world, local_rank)
