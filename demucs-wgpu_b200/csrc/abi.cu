@@ -62,7 +62,7 @@ dmx_status dmx_create(const dmx_config* cfg, const void* blob, size_t len, int d
       throw Error(DMX_ERR_INVALID, "max_batch must be in [1, 256]");
     h->cfg = *cfg;
     h->device = device;
-    const auto tensors = parse_safetensors(blob, len);  // validated before any CUDA call
+    const auto tensors = parse_checkpoint(blob, len);  // validated before any CUDA call
     CK(cudaSetDevice(device));
     CK(cudaStreamCreateWithFlags(&h->stream, cudaStreamNonBlocking));
     CK(cudaMalloc(&h->err, sizeof(int)));
@@ -293,7 +293,7 @@ dmx_status dmx_read_tensor(const void* blob, size_t len, const char* name, float
   try {
     if (!blob || !name || !out || !shape || !ndim || cap < 0)
       throw Error(DMX_ERR_INVALID, "dmx_read_tensor: bad argument");
-    const auto tensors = parse_safetensors(blob, len);
+    const auto tensors = parse_checkpoint(blob, len);
     auto it = tensors.find(name);
     if (it == tensors.end()) throw Error(DMX_ERR_WEIGHTS, std::string("missing tensor ") + name);
     const HostTensor& t = it->second;

@@ -94,6 +94,8 @@ int dtype_width(const std::string& d) {
   return 0;
 }
 
+}  // namespace
+
 // Upcasts one non-F32 tensor to f32 (safetensors.rs:110-135).
 std::vector<float> decode_tensor(const char* raw, size_t n, const std::string& d) {
   std::vector<float> v(n);
@@ -130,8 +132,6 @@ std::vector<float> decode_tensor(const char* raw, size_t n, const std::string& d
   return v;
 }
 
-}  // namespace
-
 std::map<std::string, HostTensor> parse_safetensors(const void* blob, size_t len) {
   if (len < 8) throw Error(DMX_ERR_WEIGHTS, "safetensors blob shorter than its header size");
   uint64_t n;
@@ -147,7 +147,25 @@ std::map<std::string, HostTensor> parse_safetensors(const void* blob, size_t len
     const std::string name = j.str();
     j.expect(':');
     if (name == "__metadata__") {
-      j.skip();
+      // string -> string map; `kwargs` holds the model configuration as JSON
+      j.expect('{');
+      if (j.peek('}')) {
+        j.expect('}');
+      } else {
+        while (true) {
+          const std::string key = j.str();
+          j.expect(':');
+          if (j.peek('"')) {
+            const std::string value = j.str();
+            if (key == "kwargs") check_kwargs_json(value);
+          } else {
+            j.skip();
+          }
+          if (j.peek(',')) { j.expect(','); continue; }
+          j.expect('}');
+          break;
+        }
+      }
     } else {
       HostTensor t;
       std::string dtype;

@@ -51,8 +51,19 @@ struct HostTensor {
 };
 
 // Parses and validates a safetensors blob (8-byte little-endian header size,
-// JSON header, raw data); every tensor comes back as f32.
+// JSON header, raw data); every tensor comes back as f32. Its
+// __metadata__["kwargs"] is checked with check_kwargs_json.
 std::map<std::string, HostTensor> parse_safetensors(const void* blob, size_t len);
+// Upcasts n elements of a safetensors dtype ("F16", "BF16", "F64", "I64", ...) to f32.
+std::vector<float> decode_tensor(const char* raw, size_t n, const std::string& dtype);
+// ckpt.cu: a torch.save zip's state dict as f32 tensors (its kwargs checked).
+bool is_torch_zip(const void* blob, size_t len);
+std::map<std::string, HostTensor> parse_torch_zip(const void* blob, size_t len);
+// Either container, by its first bytes.
+std::map<std::string, HostTensor> parse_checkpoint(const void* blob, size_t len);
+// Rejects model kwargs (a JSON object) of an architecture other than the
+// htdemucs default the kernels implement (DMX_ERR_INVALID naming the field).
+void check_kwargs_json(const std::string& text);
 
 constexpr int kBK = 16, kBN = 64;
 

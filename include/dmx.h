@@ -59,11 +59,18 @@ typedef struct dmx_pending dmx_pending;
 void dmx_default_config(dmx_config* cfg);
 
 /* Demucs::load / GpuHtdemucsRunner::with_selector + GpuWeights::load
- * (api.rs:394-420, gpu/htdemucs.rs:536-660, 2377-2388): parse a safetensors
- * blob holding the PyTorch-named tensors (weights.rs:211-578) — F32, or F16
- * (the published checkpoints), BF16, F64 and integer types upcast to f32 as
- * safetensors.rs:110-135 does — repack and upload them once to `device`. The
- * blob is validated (DMX_ERR_WEIGHTS) before any CUDA call. */
+ * (api.rs:394-420, gpu/htdemucs.rs:536-660, 2377-2388; weights.rs:28-80):
+ * parse a checkpoint blob holding the PyTorch-named tensors (weights.rs:
+ * 211-578), repack them and upload them once to `device`. The blob is either
+ * a safetensors file — F32, or F16 (the published checkpoints), BF16, F64 and
+ * integer types upcast to f32 as safetensors.rs:110-135 does — or a torch.save
+ * zip (`.th` / `.pth`, recognised by its first bytes; ckpt/mod.rs,
+ * ckpt/pickle.rs) whose state dict is the top level or sits under `state`,
+ * `state_dict` or `model_state_dict`. The model kwargs (safetensors
+ * __metadata__["kwargs"] JSON, or the .th package's pickled kwargs dict;
+ * config.rs:150-215) must describe the htdemucs default architecture these
+ * kernels implement; a checkpoint of another shape is DMX_ERR_INVALID naming
+ * the field. The blob is validated (DMX_ERR_WEIGHTS) before any CUDA call. */
 dmx_status dmx_create(const dmx_config* cfg, const void* safetensors_blob, size_t blob_len,
                       int device, dmx_handle** out);
 void dmx_destroy(dmx_handle* h);
@@ -329,9 +336,12 @@ dmx_status dmx_track_finish(dmx_handle* h, const float* acc_dev, int64_t length,
                             double transition_power, int shifts, const float* mean_std_dev,
                             float* stems_dev, int64_t t_lo, int64_t t_hi);
 
-/* SafeTensors::parse + get (safetensors.rs:38-108, 110-160): tensor `name` of
- * a safetensors blob as f32, decoded by the loader dmx_create uses (F32, F16,
- * BF16, F64 and integer types upcast as safetensors.rs:110-135 does). Writes
+/* SafeTensors::parse + get (safetensors.rs:38-108, 110-160) and
+ * Checkpoint::from_bytes + get (ckpt/mod.rs:44-130): tensor `name` of a
+ * checkpoint blob (safetensors or torch.save zip, as dmx_create reads them) as
+ * f32, decoded by the loader dmx_create uses (F32, F16, BF16, F64 and integer
+ * types upcast as safetensors.rs:110-135 does; views gathered through their
+ * strides). Writes
  * the element count's floats to `out` (DMX_ERR_INVALID if more than `cap`),
  * the shape to `shape` (up to 8 dimensions) and its rank to `*ndim`; a
  * missing tensor or a malformed blob is DMX_ERR_WEIGHTS. Makes no CUDA call. */

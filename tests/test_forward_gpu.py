@@ -94,3 +94,24 @@ def test_half_precision_checkpoints_load_as_their_f32_upcast(dtype):
     got = dmx.Handle(synth.write_safetensors(w, dtype=dtype), device=0, max_batch=1).forward(mix)
     ref = dmx.Handle(synth.write_safetensors(rounded), device=0, max_batch=1).forward(mix)
     assert np.array_equal(got, ref)
+
+
+def test_torch_zip_checkpoint_loads_as_the_safetensors_blob():
+    # a torch.save archive of the same state dict (the demucs .th package layout) gives
+    # the same network: the forward is bit for bit the safetensors blob's
+    import fractions
+    import io
+    from collections import OrderedDict
+
+    import torch
+    import dmx
+
+    w = synth.random_weights(6)
+    buf = io.BytesIO()
+    torch.save({"klass": fractions.Fraction, "args": (),
+                "kwargs": {"channels": 48, "segment": fractions.Fraction(39, 5)},
+                "state": OrderedDict((k, torch.from_numpy(v.copy())) for k, v in w.items())}, buf)
+    mix = synth.gaussian_audio(10, 1)
+    got = dmx.Handle(buf.getvalue(), device=0, max_batch=1, precision=dmx.TF32).forward(mix)
+    ref = dmx.Handle(synth.write_safetensors(w), device=0, max_batch=1, precision=dmx.TF32).forward(mix)
+    assert np.array_equal(got, ref)
