@@ -1,10 +1,12 @@
-"""Builds libdmx_cuda.so (the C-ABI library of include/dmx.h) for sm_100a.
+"""Builds libdmx_cuda.so (the C-ABI library of include/dmx.h) for sm_100a,
+and the ``dmx`` command-line tool over it.
 
 Every .cu under csrc/ is compiled by nvcc with
 ``-gencode arch=compute_100a,code=sm_100a -lineinfo -O3`` into _build/ and
 linked into ``libdmx_cuda.so`` next to this file (in-tree, so it travels with
-the repository snapshot). Objects are rebuilt only when a source or header is
-newer than them.
+the repository snapshot). ``cli/dmx_cli.cpp`` is compiled by g++ into the
+executable ``dmx`` beside the library, which it finds through an $ORIGIN
+rpath. Objects are rebuilt only when a source or header is newer than them.
 """
 
 from __future__ import annotations
@@ -20,7 +22,10 @@ ROOT = os.path.dirname(HERE)
 CSRC = os.path.join(HERE, "csrc")
 BUILD = os.path.join(HERE, "_build")
 LIB = os.path.join(HERE, "libdmx_cuda.so")
+CLI_SRC = os.path.join(HERE, "cli", "dmx_cli.cpp")
+CLI = os.path.join(HERE, "dmx")
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
+CXX = os.environ.get("CXX", "g++")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "--expt-relaxed-constexpr",
          "-I", os.path.join(ROOT, "include"), "-I", CSRC]
@@ -68,7 +73,26 @@ def build(verbose: bool = False, ptxas_info: bool = False) -> str:
             print(" ".join(cmd), flush=True)
         subprocess.run(cmd, check=True)
         os.replace(tmp, LIB)
+    build_cli(verbose)
     return LIB
+
+
+def build_cli(verbose: bool = False) -> str:
+    """Compiles the ``dmx`` executable (cli/dmx_cli.cpp) against libdmx_cuda.so."""
+    newest = max(os.path.getmtime(CLI_SRC), os.path.getmtime(LIB),
+                 os.path.getmtime(os.path.join(ROOT, "include", "dmx.h")))
+    if os.path.exists(CLI) and os.path.getmtime(CLI) >= newest:
+        return CLI
+    tmp = CLI + f".tmp{os.getpid()}"
+    cmd = [CXX, "-std=c++17", "-O2", "-Wall", "-I", os.path.join(ROOT, "include"), CLI_SRC,
+           "-o", tmp, "-L", HERE, "-ldmx_cuda", "-Wl,-rpath,$ORIGIN"]
+    if verbose:
+        print(" ".join(cmd), flush=True)
+    r = subprocess.run(cmd, capture_output=True, text=True)
+    if r.returncode != 0:
+        raise RuntimeError(f"g++ failed on dmx_cli.cpp:\n{r.stdout}\n{r.stderr}")
+    os.replace(tmp, CLI)
+    return CLI
 
 
 if __name__ == "__main__":

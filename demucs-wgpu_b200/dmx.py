@@ -58,6 +58,15 @@ class DmxError(RuntimeError):
 
 _lib = None
 
+CLI_PATH = os.path.join(HERE, "dmx")
+
+
+def cli_path():
+    """Path of the ``dmx`` command-line tool (built by build.py beside the library)."""
+    if not os.path.exists(CLI_PATH):
+        raise ImportError(f"{CLI_PATH} is not built; run demucs-wgpu_b200/build.py")
+    return CLI_PATH
+
 
 def lib():
     """Load libdmx_cuda.so (raises if it is absent: there is no fallback)."""
