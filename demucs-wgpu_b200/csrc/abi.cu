@@ -107,6 +107,12 @@ void dmx_destroy(dmx_handle* h) {
     cudaFreeHost(h->emit_pin[i]);
   }
   if (h->copy_stream) cudaStreamDestroy(h->copy_stream);
+  cudaFree(h->win_ws);
+  for (int i = 0; i < 2; ++i) {
+    cudaFreeHost(h->win_pin[i]);
+    if (h->win_ev[i]) cudaEventDestroy(h->win_ev[i]);
+    if (h->out_ev[i]) cudaEventDestroy(h->out_ev[i]);
+  }
   cudaFree(h->batch_ws);
   cudaFree(h->tail_buf);
   if (h->shard_done) cudaEventDestroy(h->shard_done);
@@ -576,19 +582,7 @@ dmx_status dmx_separate_track_emit(dmx_handle* h, const float* left, const float
     const PassGeom pg = pass_geom(h, chunk_samples(o), o.overlap, o.transition_power);
     const int batch = std::max(1, o.batch > 0 ? std::min(o.batch, h->cfg.max_batch) : h->cfg.max_batch);
     // a block holds what one forward finishes: at most `batch` strides plus one segment
-    const int64_t cap = std::min<int64_t>(n, (int64_t)batch * pg.stride + pg.chunk);
-    if (cap > h->emit_cap) {
-      for (int i = 0; i < 2; ++i) {
-        cudaFreeHost(h->emit_pin[i]);
-        h->emit_pin[i] = nullptr;
-      }
-      h->emit_cap = 0;
-      for (int i = 0; i < 2; ++i) {
-        CK(cudaMallocHost(&h->emit_pin[i], (size_t)8 * cap * sizeof(float)));
-        if (!h->emit_ev[i]) CK(cudaEventCreateWithFlags(&h->emit_ev[i], cudaEventDisableTiming));
-      }
-      h->emit_cap = cap;
-    }
+    ensure_emit(h, std::min<int64_t>(n, (int64_t)batch * pg.stride + pg.chunk));
     const size_t need = (size_t)10 * n * sizeof(float);
     if (need > h->host_io_cap) {
       cudaFree(h->host_io);

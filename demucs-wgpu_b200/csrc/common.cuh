@@ -43,7 +43,6 @@ DMX_DEVICE float round_tf32(float x) {
   return __uint_as_float(b & 0xFFFFE000u);
 }
 
-
 DMX_DEVICE double warp_sum(double v) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);

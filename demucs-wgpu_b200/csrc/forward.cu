@@ -175,7 +175,6 @@ bool dmx_handle::build_tc(const ConvParams& p, const Packed& pk, TcOperandA& a, 
   return tc_gemm_supported(a, t);
 }
 
-
 namespace dmx {
 
 namespace {

@@ -112,12 +112,33 @@ int track_normalize_scratch_doubles();
 // The same two kernels on `blocks` blocks; scratch holds 2*blocks doubles.
 void launch_track_normalize_blocks(const float* left, const float* right, int64_t n, int blocks,
                                    double* scratch, float* mix_norm, float2* norm, cudaStream_t s);
+// The moments of a track read in windows: state holds moments_state_doubles()
+// doubles, zeroed before the first window; every window but the last holds a
+// multiple of moments_grid() samples. launch_moments_final writes the same
+// (mean, std) launch_track_normalize computes for the whole track.
+int64_t moments_grid();
+int64_t moments_state_doubles();
+void launch_moments_window(const float* left, const float* right, int64_t count, double* state,
+                           cudaStream_t s);
+void launch_moments_final(double* state, int64_t n, float2* norm, cudaStream_t s);
+// (x - mean) / std in place over two rows of `count` samples, `ld` apart
+void launch_normalize_window(float* x, int64_t ld, int64_t count, const float2* norm, cudaStream_t s);
+// Windowed buffers of the streaming driver (NULL: whole-track buffers): the
+// normalised mix holds samples [mix_lo, mix_lo + mix_n) in rows of mix_ld;
+// the accumulator holds view samples from acc_lo in rows of acc_ld; finished
+// sample t goes to column t - out_lo of rows out_ld apart.
+struct DriverWindow {
+  int64_t mix_lo = 0, mix_ld = 0, mix_n = 0;
+  int64_t acc_lo = 0, acc_ld = 0;
+  int64_t out_lo = 0, out_ld = 0;
+};
 // `segment`: samples per chunk; `row`: samples per forward row (0 = segment),
 // longer than `segment` when the chunks are cut shorter than the model's
 // training length (zero padded at the row's end).
 void launch_gather_chunks(const float* mix_norm, int64_t length, int64_t shift_offset,
                           int64_t max_shift, int segment, int64_t stride, int64_t chunk0,
-                          int count, float* out, cudaStream_t s, int row = 0);
+                          int count, float* out, cudaStream_t s, int row = 0,
+                          const DriverWindow* win = nullptr);
 void launch_ola_accumulate(const float* chunks, int64_t length, int64_t shift_offset,
                            int64_t max_shift, int segment, int64_t stride, int64_t chunk0,
                            int count, const float* weight, float* acc, int64_t view_lo,
@@ -126,7 +147,7 @@ void launch_ola_accumulate(const float* chunks, int64_t length, int64_t shift_of
 void launch_ola_finish(const float* acc, int64_t length, int64_t shift_offset, int64_t max_shift,
                        int segment, int64_t stride, const float* weight, const float2* norm,
                        float scale, int mode, float* pass, float* stems, cudaStream_t s,
-                       int64_t t_lo = 0, int64_t t_hi = -1);
+                       int64_t t_lo = 0, int64_t t_hi = -1, const DriverWindow* win = nullptr);
 
 // stats.cu — fixed-order moment reductions. part is (rows * rowlen positions,
 // nslots, 2) doubles; stats[row] = (sum, sum of squares) over the row's

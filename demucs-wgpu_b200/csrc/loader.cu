@@ -411,7 +411,6 @@ struct Loader {
 
 };
 
-
 }  // namespace
 
 float round_tf32_host(float x) { return round_tf32_impl(x); }

@@ -222,6 +222,14 @@ struct dmx_handle {
   float* ola_w_custom = nullptr;  // transition weight of a non-default segment / power
   int ola_w_len = 0;
   double ola_w_power = 1.0;
+  // dmx_separate_track_windowed: device window, accumulators and output blocks,
+  // and the pinned staging its read callback fills
+  char* win_ws = nullptr;
+  size_t win_cap = 0;
+  float* win_pin[2] = {nullptr, nullptr};
+  cudaEvent_t win_ev[2] = {nullptr, nullptr};  // the copy that last read win_pin[i]
+  cudaEvent_t out_ev[2] = {nullptr, nullptr};  // the copy that last read output block i
+  int64_t win_pin_cap = 0;                     // floats per pinned window buffer
 
   float* W(size_t off) const { return wdev + off; }
 
@@ -367,8 +375,12 @@ struct HostSink {
   int64_t pending_t0 = 0, pending_count = 0;  // the block in flight (count 0: none)
   int pending_slot = 0, next_slot = 0;
   void flush(dmx_handle* h);
-  void put(dmx_handle* h, const float* d_stems, int64_t n, int64_t t0, int64_t t1);
+  // samples [t0, t1) of 8 device rows `ld` apart whose column 0 is sample col0
+  void put(dmx_handle* h, const float* d_stems, int64_t ld, int64_t t0, int64_t t1,
+           int64_t col0 = 0);
 };
+
+void ensure_emit(dmx_handle* h, int64_t cap);
 
 void separate_track_impl(dmx_handle* h, BagPlan* bag, const float* lr_dev, int64_t n,
                          const dmx_separate_opts* opts, float* d_stems, dmx_progress_fn progress,
@@ -379,6 +391,9 @@ void separate_track_host(dmx_handle* h, BagPlan* bag, const float* left, const f
 void separate_batch_impl(dmx_handle* h, const float* const* lr_dev, const int64_t* lengths,
                          int n_tracks, const dmx_separate_opts* opts, float* const* stems_dev,
                          dmx_progress_fn progress, void* user);
+void separate_windowed_impl(dmx_handle* h, dmx_read_fn read, int64_t n,
+                             const dmx_separate_opts* opts, dmx_frames_fn on_frames,
+                             dmx_progress_fn progress, void* user);
 void separate_track_multi_impl(const std::vector<dmx_handle*>& H, const float* left,
                                const float* right, int64_t n, const dmx_separate_opts* opts,
                                float* stems_out);

@@ -238,10 +238,6 @@ DMX_DEVICE void tmem_st32(uint32_t taddr, const float* v) {
 }
 DMX_DEVICE void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
-
-
-
-
 inline PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
   static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
   static std::once_flag once;
@@ -273,6 +269,5 @@ inline bool make_tensor_map(CUtensorMap* map, const void* base, int rank, const 
                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS;
 }
-
 
 }  // namespace dmx

@@ -223,15 +223,17 @@ void HostSink::flush(dmx_handle* h) {
   pending_count = 0;
 }
 
-// Samples [t0, t1) of d_stems (8, n) are final: copy them out as blocks.
-void HostSink::put(dmx_handle* h, const float* d_stems, int64_t n, int64_t t0, int64_t t1) {
+// Samples [t0, t1) of d_stems (8 rows `ld` apart, column 0 = sample col0)
+// are final: copy them out as blocks.
+void HostSink::put(dmx_handle* h, const float* d_stems, int64_t ld, int64_t t0, int64_t t1,
+                   int64_t col0) {
   for (int64_t a = t0; a < t1; a += h->emit_cap) {
     const int64_t count = std::min<int64_t>(h->emit_cap, t1 - a);
     const int slot = next_slot;
     next_slot ^= 1;
     // the slot's previous block was handed over before the block after it was queued
-    CK(cudaMemcpy2DAsync(h->emit_pin[slot], (size_t)count * sizeof(float), d_stems + a,
-                         (size_t)n * sizeof(float), (size_t)count * sizeof(float), 8,
+    CK(cudaMemcpy2DAsync(h->emit_pin[slot], (size_t)count * sizeof(float), d_stems + (a - col0),
+                         (size_t)ld * sizeof(float), (size_t)count * sizeof(float), 8,
                          cudaMemcpyDeviceToHost, h->copy_stream));
     CK(cudaEventRecord(h->emit_ev[slot], h->copy_stream));
     flush(h);
@@ -567,7 +569,6 @@ void separate_batch_impl(dmx_handle* h, const float* const* lr_dev, const int64_
   }
   h->mark("end");
 }
-
 
 // dmx_separate_track over several handles from one host thread (see
 // include/dmx.h): contiguous chunk ranges, one per handle; every handle

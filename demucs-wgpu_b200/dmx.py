@@ -28,7 +28,7 @@ EXPORTS = (
     "dmx_num_chunks", "dmx_track_finish", "dmx_track_shard", "dmx_set_trace",
     "dmx_set_stage_timing", "dmx_stage_times", "dmx_kernel_launches", "dmx_stream",
     "dmx_synchronize", "dmx_read_tensor", "dmx_shift_offsets", "dmx_ipc_export", "dmx_ipc_open",
-    "dmx_ipc_close", "dmx_rows_copy", "dmx_rows_add",
+    "dmx_ipc_close", "dmx_rows_copy", "dmx_rows_add", "dmx_separate_track_windowed",
 )
 
 _f32p = ctypes.POINTER(ctypes.c_float)
@@ -36,6 +36,8 @@ _i64p = ctypes.POINTER(ctypes.c_int64)
 TRACE_FN = ctypes.CFUNCTYPE(None, ctypes.c_char_p, _f32p, _i64p, ctypes.c_int, ctypes.c_void_p)
 PROGRESS_FN = ctypes.CFUNCTYPE(None, ctypes.c_size_t, ctypes.c_size_t, ctypes.c_void_p)
 FRAMES_FN = ctypes.CFUNCTYPE(None, ctypes.c_int64, ctypes.c_int64, _f32p, ctypes.c_void_p)
+READ_FN = ctypes.CFUNCTYPE(ctypes.c_int, ctypes.c_int64, ctypes.c_int64, _f32p, _f32p,
+                           ctypes.c_void_p)
 
 
 class Config(ctypes.Structure):
@@ -111,6 +113,9 @@ def lib():
         L.dmx_separate_track_emit.argtypes = [ctypes.c_void_p, _f32p, _f32p, ctypes.c_int64,
                                               ctypes.POINTER(SeparateOpts), FRAMES_FN,
                                               PROGRESS_FN, ctypes.c_void_p]
+        L.dmx_separate_track_windowed.argtypes = [ctypes.c_void_p, READ_FN, ctypes.c_int64,
+                                                  ctypes.POINTER(SeparateOpts), FRAMES_FN,
+                                                  PROGRESS_FN, ctypes.c_void_p]
         _f32pp = ctypes.POINTER(_f32p)
         L.dmx_separate_batch.argtypes = [ctypes.c_void_p, _f32pp, _f32pp, _i64p, ctypes.c_int,
                                          ctypes.POINTER(SeparateOpts), _f32pp, PROGRESS_FN,
@@ -265,6 +270,40 @@ class Handle:
                                              ctypes.byref(opts), fcb, pcb, None))
         if error:
             raise error[0]
+
+    def separate_track_windowed(self, read, n, on_frames, shifts=1, overlap=0.25,
+                                transition_power=1.0, batch=0, progress=None, segment=0.0):
+        """Demucs::separate_streaming over a windowed source: ``read(t0, count)``
+        returns the track's samples [t0, t0 + count) as (left, right) arrays;
+        ``on_frames(t0, block)`` receives each finished (8, count) block in
+        ascending order. The track is never held whole by the library."""
+        error = []
+
+        def _read(t0, count, left, right, _u):
+            try:
+                lr = read(t0, count)
+                np.ctypeslib.as_array(left, shape=(count,))[:] = lr[0]
+                np.ctypeslib.as_array(right, shape=(count,))[:] = lr[1]
+                return 0
+            except Exception as exc:
+                error.append(exc)
+                return 1
+
+        def _frames(t0, count, block, _u):
+            try:
+                on_frames(t0, np.ctypeslib.as_array(block, shape=(8, count)).copy())
+            except Exception as exc:  # pragma: no cover - surfaced below
+                error.append(exc)
+
+        rcb = READ_FN(_read)
+        fcb = FRAMES_FN(_frames)
+        pcb = PROGRESS_FN(0) if progress is None else PROGRESS_FN(lambda d, t, _u: progress(d, t))
+        opts = _opts(shifts, overlap, transition_power, batch, segment)
+        status = lib().dmx_separate_track_windowed(self._h, rcb, n, ctypes.byref(opts), fcb, pcb,
+                                                   None)
+        if error:
+            raise error[0]
+        _check(status)
 
     def separate_batch(self, tracks, shifts=1, overlap=0.25, transition_power=1.0, batch=0,
                        progress=None, outs=None, segment=0.0):

@@ -142,6 +142,30 @@ dmx_status dmx_separate_track_emit(dmx_handle* h, const float* left, const float
                                    const dmx_separate_opts* opts, dmx_frames_fn on_frames,
                                    dmx_progress_fn progress, void* user);
 
+/* Reads samples [t0, t0 + count) of the track's two channels into `left` and
+ * `right` (pinned host buffers the library owns, valid during the call) and
+ * returns 0, or nonzero to stop the separation with DMX_ERR_INVALID
+ * (MixSamples::at over a WindowedMix, mix.rs:18-60, 265-360). */
+typedef int (*dmx_read_fn)(int64_t t0, int64_t count, float* left, float* right, void* user);
+
+/* Demucs::separate_streaming over a windowed source (the reference CLI's
+ * separate: scan_norm_file, mix.rs:61-120, then separate_streaming_normalized_mix
+ * over WindowedMix, api.rs:600-650, mix.rs:265-360, with the OLA ring of
+ * streaming.rs:96-261): the track of `n` samples is never held whole. A first
+ * pass reads it through `read` in windows for the global moments; the split
+ * passes then read, for each forward of opts->batch chunks, only the samples
+ * those chunks cover, and overlap-add in a device window that slides with
+ * the chunks. Device memory is O(batch x segment) — about 0.3 GB at batch 16,
+ * 50 MB at batch 1 — and independent of n; finished stems reach `on_frames`
+ * in ascending blocks as dmx_separate_track_emit hands them over. With
+ * shifts > 1 the passes are summed in host memory (8 n floats, as the
+ * reference's O(T) pass sum, pipeline.rs:451-513) and emitted after the last
+ * pass. The stems equal dmx_separate_track's bit for bit. `read`, `progress`
+ * and `on_frames` receive the same `user`. */
+dmx_status dmx_separate_track_windowed(dmx_handle* h, dmx_read_fn read, int64_t n,
+                                       const dmx_separate_opts* opts, dmx_frames_fn on_frames,
+                                       dmx_progress_fn progress, void* user);
+
 /* dmx_separate_track over several GPUs from one host thread (the whole-track
  * multi-GPU entry of the drop-in plan; the reference runs one device:
  * api.rs:438-545, streaming.rs:296-400). hs[k] holds the same network on
