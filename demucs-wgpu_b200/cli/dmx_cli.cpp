@@ -14,9 +14,11 @@
 // OUT is a directory (one <stem>.wav per source, float32) or, for a single stem
 // or --stem, a file path. WAV input: PCM 16 / 24 / 32-bit, IEEE float 32 / 64-bit and the
 // extensible header's 32-bit float (audio.rs:184-360); mono is duplicated to
-// stereo; the sample rate must be the model's 44100 Hz. The stems are written
-// while the device still separates: dmx_separate_track_emit hands over each
-// block of finished frames (audio.rs:559-670, FloatWavWriter).
+// stereo; the sample rate must be the model's 44100 Hz. `separate` never holds
+// the track: dmx_separate_track_windowed reads the windows it needs from the
+// file (WindowedMix, mix.rs:265-360) and hands over each block of finished
+// frames, which is written while the device still separates (FloatWavWriter,
+// audio.rs:559-670).
 #include <algorithm>
 #include <chrono>
 #include <cmath>
@@ -27,6 +29,7 @@
 #include <set>
 #include <string>
 #include <sys/stat.h>
+#include <sys/types.h>
 #include <vector>
 
 #include "dmx.h"
@@ -53,79 +56,129 @@ uint32_t le(const unsigned char* p, int n) {
   return v;
 }
 
-// RIFF chunks: fmt then data (audio.rs:209-274), frames decoded as soundfile
-// scales them (audio.rs:276-313).
-Audio read_wav(const std::string& path) {
-  FILE* f = std::fopen(path.c_str(), "rb");
-  if (!f) throw Fail("cannot open " + path);
-  std::vector<unsigned char> b;
-  unsigned char buf[1 << 16];
-  size_t n;
-  while ((n = std::fread(buf, 1, sizeof(buf), f)) > 0) b.insert(b.end(), buf, buf + n);
-  std::fclose(f);
-  if (b.size() < 12 || std::memcmp(b.data(), "RIFF", 4) || std::memcmp(b.data() + 8, "WAVE", 4))
-    throw Fail(path + ": not a RIFF/WAVE file (only uncompressed WAV is supported)");
-  int tag = -1, channels = 0, bits = 0;
-  uint32_t rate = 0;
-  size_t data_pos = 0, data_len = 0;
-  bool have_data = false;
-  for (size_t p = 12; p + 8 <= b.size();) {
-    const uint32_t size = le(&b[p + 4], 4);
-    const size_t body = p + 8;
-    if (!std::memcmp(&b[p], "fmt ", 4)) {
-      if (size < 16 || body + size > b.size()) throw Fail(path + ": truncated fmt chunk");
-      tag = (int)le(&b[body], 2);
-      channels = (int)le(&b[body + 2], 2);
-      rate = le(&b[body + 4], 4);
-      bits = (int)le(&b[body + 14], 2);
-    } else if (!std::memcmp(&b[p], "data", 4)) {
-      data_pos = body;
-      data_len = std::min<size_t>(size, b.size() - body);
-      have_data = true;
-      if (tag >= 0) break;
+// A WAV file read in windows of frames (the reference CLI's WindowedMix over
+// probe_audio, mix.rs:265-360): the RIFF chunks are walked once for fmt and
+// data (audio.rs:209-274), then each window is decoded where it lies, scaled
+// as soundfile scales it (audio.rs:276-313).
+struct WavSource {
+  std::string path;
+  FILE* f = nullptr;
+  int tag = -1, channels = 0, bits = 0, rate = 0;
+  int64_t frames = 0;
+  off_t data_pos = 0;
+  std::vector<unsigned char> buf;
+
+  explicit WavSource(const std::string& p) : path(p) {
+    f = std::fopen(p.c_str(), "rb");
+    if (!f) throw Fail("cannot open " + p);
+    unsigned char h[16];
+    if (std::fread(h, 1, 12, f) != 12 || std::memcmp(h, "RIFF", 4) || std::memcmp(h + 8, "WAVE", 4)) {
+      std::fclose(f);
+      f = nullptr;
+      throw Fail(p + ": not a RIFF/WAVE file (only uncompressed WAV is supported)");
     }
-    p = body + size + (size & 1);
-  }
-  if (tag < 0) throw Fail(path + ": missing fmt chunk");
-  if (!have_data) throw Fail(path + ": missing data chunk");
-  if (channels <= 0) throw Fail(path + ": zero channels");
-  const bool ok = (tag == 3 && (bits == 32 || bits == 64)) ||
-                  (tag == 1 && (bits == 16 || bits == 24 || bits == 32)) ||
-                  (tag == 0xFFFE && bits == 32);
-  if (!ok)
-    throw Fail(path + ": unsupported WAV format " + std::to_string(tag) + " with " +
-               std::to_string(bits) + " bits per sample");
-  const int bps = bits / 8, bpf = bps * channels;
-  if (data_len % bpf)
-    throw Fail(path + ": data chunk is not a whole number of " + std::to_string(channels) +
-               "-channel frames");
-  Audio a;
-  a.rate = (int)rate;
-  a.channels = channels;
-  a.frames = (int64_t)(data_len / bpf);
-  a.data.resize((size_t)a.frames * channels);
-  for (int64_t t = 0; t < a.frames; ++t)
-    for (int c = 0; c < channels; ++c) {
-      const unsigned char* s = &b[data_pos + (size_t)t * bpf + (size_t)c * bps];
-      float v;
-      if (tag != 1 && bits == 32) {
-        const uint32_t u = le(s, 4);
-        std::memcpy(&v, &u, 4);
-      } else if (bits == 64) {
-        uint64_t u = (uint64_t)le(s, 4) | ((uint64_t)le(s + 4, 4) << 32);
-        double d;
-        std::memcpy(&d, &u, 8);
-        v = (float)d;
-      } else if (bits == 16) {
-        v = (float)(int16_t)le(s, 2) / 32768.0f;
-      } else if (bits == 24) {
-        const int32_t raw = (int32_t)(le(s, 3) << 8) >> 8;  // sign extension
-        v = (float)raw / 8388608.0f;
-      } else {
-        v = (float)(int32_t)le(s, 4) / 2147483648.0f;
+    fseeko(f, 0, SEEK_END);
+    const off_t size = ftello(f);
+    off_t data_len = 0;
+    bool have_data = false;
+    for (off_t pos = 12; pos + 8 <= size;) {
+      fseeko(f, pos, SEEK_SET);
+      if (std::fread(h, 1, 8, f) != 8) break;
+      const uint32_t csize = le(h + 4, 4);
+      const off_t body = pos + 8;
+      if (!std::memcmp(h, "fmt ", 4)) {
+        if (csize < 16 || body + (off_t)csize > size || std::fread(h, 1, 16, f) != 16)
+          fail(p + ": truncated fmt chunk");
+        tag = (int)le(h, 2);
+        channels = (int)le(h + 2, 2);
+        rate = (int)le(h + 4, 4);
+        bits = (int)le(h + 14, 2);
+      } else if (!std::memcmp(h, "data", 4)) {
+        data_pos = body;
+        data_len = std::min<off_t>(csize, size - body);
+        have_data = true;
+        if (tag >= 0) break;
       }
-      a.data[(size_t)c * a.frames + t] = v;
+      pos = body + csize + (csize & 1);
     }
+    if (tag < 0) fail(p + ": missing fmt chunk");
+    if (!have_data) fail(p + ": missing data chunk");
+    if (channels <= 0) fail(p + ": zero channels");
+    const bool ok = (tag == 3 && (bits == 32 || bits == 64)) ||
+                    (tag == 1 && (bits == 16 || bits == 24 || bits == 32)) ||
+                    (tag == 0xFFFE && bits == 32);
+    if (!ok)
+      fail(p + ": unsupported WAV format " + std::to_string(tag) + " with " + std::to_string(bits) +
+           " bits per sample");
+    if (data_len % (bits / 8 * channels))
+      fail(p + ": data chunk is not a whole number of " + std::to_string(channels) +
+           "-channel frames");
+    frames = (int64_t)(data_len / (bits / 8 * channels));
+  }
+  ~WavSource() {
+    if (f) std::fclose(f);
+  }
+  WavSource(const WavSource&) = delete;
+  WavSource& operator=(const WavSource&) = delete;
+
+  [[noreturn]] void fail(const std::string& why) {
+    std::fclose(f);
+    f = nullptr;
+    throw Fail(why);
+  }
+
+  // frames [t0, t0 + count) of channel c into out[c][0 .. count)
+  void read(int64_t t0, int64_t count, float* const* out) {
+    if (t0 < 0 || count < 0 || t0 + count > frames) throw Fail(path + ": read past the end");
+    const int bps = bits / 8, bpf = bps * channels;
+    buf.resize((size_t)count * bpf);
+    if (fseeko(f, data_pos + (off_t)t0 * bpf, SEEK_SET) != 0 ||
+        std::fread(buf.data(), 1, buf.size(), f) != buf.size())
+      throw Fail(path + ": read failed");
+    for (int64_t t = 0; t < count; ++t)
+      for (int c = 0; c < channels; ++c) {
+        const unsigned char* s = &buf[(size_t)t * bpf + (size_t)c * bps];
+        float v;
+        if (tag != 1 && bits == 32) {
+          const uint32_t u = le(s, 4);
+          std::memcpy(&v, &u, 4);
+        } else if (bits == 64) {
+          uint64_t u = (uint64_t)le(s, 4) | ((uint64_t)le(s + 4, 4) << 32);
+          double d;
+          std::memcpy(&d, &u, 8);
+          v = (float)d;
+        } else if (bits == 16) {
+          v = (float)(int16_t)le(s, 2) / 32768.0f;
+        } else if (bits == 24) {
+          const int32_t raw = (int32_t)(le(s, 3) << 8) >> 8;  // sign extension
+          v = (float)raw / 8388608.0f;
+        } else {
+          v = (float)(int32_t)le(s, 4) / 2147483648.0f;
+        }
+        out[c][t] = v;
+      }
+  }
+
+  // both channels of the stereo model: mono is duplicated (audio.rs:38-60)
+  void read_stereo(int64_t t0, int64_t count, float* left, float* right) {
+    float* out[2] = {left, right};
+    read(t0, count, out);
+    if (channels == 1) std::memcpy(right, left, (size_t)count * sizeof(float));
+  }
+};
+
+Audio read_wav(const std::string& path) {
+  WavSource src(path);
+  Audio a;
+  a.rate = src.rate;
+  a.channels = src.channels;
+  a.frames = src.frames;
+  a.data.resize((size_t)a.frames * a.channels);
+  std::vector<float*> out(a.channels);
+  for (int64_t t0 = 0; t0 < a.frames; t0 += 1 << 18) {
+    for (int c = 0; c < a.channels; ++c) out[c] = a.data.data() + (size_t)c * a.frames + t0;
+    src.read(t0, std::min<int64_t>(1 << 18, a.frames - t0), out.data());
+  }
   return a;
 }
 
@@ -270,10 +323,22 @@ struct EmitState {
   int stem_index = -1;
   WavWriter* companion = nullptr;
   std::string method;
-  const Audio* mix = nullptr;
-  std::vector<float> frame;
+  WavSource* mix = nullptr;
+  std::vector<float> frame, raw;
   std::string error;
 };
+
+// dmx_read_fn over the input file: the library asks for the windows it needs
+int read_frames(int64_t t0, int64_t count, float* left, float* right, void* user) {
+  EmitState& st = *static_cast<EmitState*>(user);
+  try {
+    st.mix->read_stereo(t0, count, left, right);
+    return 0;
+  } catch (const std::exception& e) {
+    st.error = e.what();
+    return 1;
+  }
+}
 
 void on_frames(int64_t t0, int64_t count, const float* block, void* user) {
   EmitState& st = *static_cast<EmitState*>(user);
@@ -290,6 +355,10 @@ void on_frames(int64_t t0, int64_t count, const float* block, void* user) {
       st.writers[s]->write(st.frame.data(), count);
     }
     if (st.companion) {
+      if (st.method == "minus") {  // the raw mix of the block, read again from the file
+        st.raw.resize((size_t)count * 2);
+        st.mix->read_stereo(t0, count, st.raw.data(), st.raw.data() + count);
+      }
       for (int64_t i = 0; i < count; ++i)
         for (int c = 0; c < 2; ++c) {
           float v = 0.f;
@@ -297,8 +366,7 @@ void on_frames(int64_t t0, int64_t count, const float* block, void* user) {
             for (int s = 0; s < 4; ++s)
               if (s != st.stem_index) v += block[(2 * s + c) * count + i];
           } else {  // minus: the raw mix less the stem
-            const Audio& m = *st.mix;
-            v = m.data[(size_t)c * m.frames + t0 + i] - block[(2 * st.stem_index + c) * count + i];
+            v = st.raw[(size_t)c * count + i] - block[(2 * st.stem_index + c) * count + i];
           }
           st.frame[2 * i + c] = v;
         }
@@ -378,7 +446,12 @@ int cmd_separate(const Args& a) {
   if (a.pos.size() != 1) throw Fail("usage: dmx separate INPUT.wav -o OUT -m CHECKPOINT [options]");
   if (a.output.empty()) throw Fail("-o OUT is required");
   if (!a.stem.empty() && !a.two_stems.empty()) throw Fail("--stem and --two-stems exclude each other");
-  const Audio mix = read_mix(a.pos[0]);
+  WavSource mix(a.pos[0]);
+  if (mix.rate != 44100)
+    throw Fail(a.pos[0] + " is at " + std::to_string(mix.rate) + " Hz but the model wants 44100 Hz");
+  if (mix.channels > 2)
+    throw Fail(a.pos[0] + " has " + std::to_string(mix.channels) + " channels; the model is stereo");
+  if (mix.frames == 0) throw Fail(a.pos[0] + " holds no samples");
   const std::string named = !a.stem.empty() ? a.stem : a.two_stems;
   int stem_index = -1;
   if (!named.empty()) {
@@ -423,10 +496,11 @@ int cmd_separate(const Args& a) {
   }
   dmx_separate_opts o{a.shifts, a.overlap, 1.0, batch, a.segment};
   const auto t0 = std::chrono::steady_clock::now();
-  const dmx_status rc = dmx_separate_track_emit(h, mix.data.data(), mix.data.data() + mix.frames,
-                                                mix.frames, &o, on_frames, nullptr, &st);
+  // the track is read window by window, never whole (host or device)
+  const dmx_status rc =
+      dmx_separate_track_windowed(h, read_frames, mix.frames, &o, on_frames, nullptr, &st);
   const double elapsed = std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
-  const std::string err = rc != DMX_OK ? dmx_last_error() : st.error;
+  const std::string err = !st.error.empty() ? st.error : rc != DMX_OK ? dmx_last_error() : "";
   std::vector<WavWriter*> all = st.writers;
   all.push_back(st.companion);
   std::string list;

@@ -1,6 +1,7 @@
 """The ``dmx`` command-line tool end to end on the GPU: ``dmx separate``
-writes, block by block as dmx_separate_track_emit hands them over, exactly
-the stems dmx_separate_track returns for the same WAV (main.rs:313-602 of the
+reads the WAV in windows and writes, block by block as
+dmx_separate_track_windowed hands them over, exactly the stems
+dmx_separate_track returns for the same samples (main.rs:313-602 of the
 reference CLI: all four stems, ``--stem`` into one file, ``--two-stems`` with
 the ``add`` and ``minus`` companions, mono input, ``--segment``,
 ``--dump-trace``); ``dmx bench`` and ``dmx profile`` run and report."""
