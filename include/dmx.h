@@ -39,8 +39,9 @@ enum {
  *       (fp32-class accuracy on the tensor cores).
  * BF16: the TF32 build with the transformer's linears (q/k/v, output
  *       projection, both FFN layers) on tcgen05 kind::f16 with bf16 operands
- *       (activations packed to bf16 in shared memory, bf16 weight copies) and
- *       fp32 accumulate; convolutions, DConv and attention as in TF32. */
+ *       (bf16 activations stored by their producers — LayerNorm, the FFN's
+ *       GELU, attention — and bf16 weight copies) and fp32 accumulate;
+ *       convolutions, DConv and attention as in TF32. */
 typedef enum { DMX_FP32 = 0, DMX_TF32 = 1, DMX_BF16 = 2, DMX_TF32X3 = 3 } dmx_precision;
 
 typedef struct {
