@@ -822,7 +822,7 @@ def main():
                     help="track: one 240 s track (the headline); bag: the htdemucs_ft bag of 4; "
                          "batch: the many-track throughput batch")
     ap.add_argument("--tracks", type=int, default=64, help="--workload batch: tracks")
-    ap.add_argument("--exchange", default="peer", choices=["peer", "nccl"],
+    ap.add_argument("--exchange", default="nccl", choices=["peer", "nccl"],
                     help="N > 1: boundary tail and stem gather as SM loads from mapped peer "
                          "memory (peer) or as NCCL point-to-point messages (nccl)")
     ap.add_argument("--max-batch", type=int, default=42,
