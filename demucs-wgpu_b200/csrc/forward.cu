@@ -305,6 +305,12 @@ void run_dconv_gemm(dmx_handle* h, const DConvFull& dc, float* x, int rows, int 
   }
 }
 
+// The narrowest DConv width that runs as the three tensor-core GEMMs of
+// run_dconv_gemm when the fused kernel does not take it.
+#ifndef DMX_DCONV_GEMM_MIN_C
+#define DMX_DCONV_GEMM_MIN_C 384
+#endif
+
 // round_out: the branch's output feeds only a tf32 GEMM (the TF32 build): the
 // last layer stores it rounded to nearest tf32 so that GEMM needs no converter.
 void run_dconv(dmx_handle* h, const DConvFull& dc, float* x, int rows, int T, bool round_out) {
@@ -318,7 +324,7 @@ void run_dconv(dmx_handle* h, const DConvFull& dc, float* x, int rows, int T, bo
   // waveform row) and the widest layers (three GEMMs, where the SIMT kernels
   // are compute-bound); the SIMT kernels are faster elsewhere
   const bool tc = tf32 && has_tc && !dc.layer[0].zq.empty() && dconv_tc_supported(C, T);
-  if (tf32 && has_tc && !tc && C >= 384) {
+  if (tf32 && has_tc && !tc && C >= DMX_DCONV_GEMM_MIN_C) {
     run_dconv_gemm(h, dc, x, rows, T, round_out);
     return;
   }
