@@ -23,7 +23,11 @@ constexpr int kEpiThreads = 256;
 // lie in HBM, f32 accumulate; no converter pass).
 constexpr int MODE_TF32 = 0, MODE_SPLIT = 1, MODE_BF16 = 2;
 
-template <int BN, int BK, int STAGES, int MODE>
+// RB (resident B): the single column tile's whole B (every K block) is
+// loaded once per CTA and stays in shared memory after the barrier block;
+// stages carry A only. For narrow layers (N = 96, 16-channel K blocks) whose
+// B is re-read per output tile otherwise.
+template <int BN, int BK, int STAGES, int MODE, bool RB = false>
 struct Smem {
   static constexpr bool SPLIT = MODE == MODE_SPLIT, BF = MODE == MODE_BF16;
   static constexpr int ELEM = BF ? 2 : 4;
@@ -31,10 +35,17 @@ struct Smem {
   static constexpr int B_BYTES = BN * BK * ELEM;
   // stage: A | B [| A_lo | B_lo]; TMA fills A, B (and B_lo), the converter
   // warps round A in place (and write A_lo)
-  static constexpr int STAGE_BYTES = SPLIT ? 2 * (A_BYTES + B_BYTES) : A_BYTES + B_BYTES;
-  static constexpr int TMA_BYTES = SPLIT ? A_BYTES + 2 * B_BYTES : A_BYTES + B_BYTES;
-  static constexpr int TOTAL = STAGES * STAGE_BYTES + 1024 /*align*/ + 512 /*barriers*/;
-  static_assert(!BF || BK == 32, "bf16 tiles are 32 channels: 64-byte swizzled rows");
+  static constexpr int STAGE_BYTES =
+      RB ? A_BYTES : (SPLIT ? 2 * (A_BYTES + B_BYTES) : A_BYTES + B_BYTES);
+  static constexpr int TMA_BYTES = RB ? A_BYTES : (SPLIT ? A_BYTES + 2 * B_BYTES : A_BYTES + B_BYTES);
+  // stages, then the barrier block (1024 bytes, keeping resident B aligned)
+  static constexpr int TOTAL = STAGES * STAGE_BYTES + 1024 /*align*/ + 1024 /*barriers*/;
+  // TMEM columns: two accumulators, rounded up to a power of two
+  static constexpr uint32_t TMEM_COLS =
+      2 * BN <= 64 ? 64u : (2 * BN <= 128 ? 128u : (2 * BN <= 256 ? 256u : 512u));
+  static_assert(!RB || MODE == MODE_TF32, "resident B: single-pass tf32 only");
+  static_assert(!BF || BK == 32 || BK == 64,
+                "bf16 tiles are 32 or 64 channels: 64- or 128-byte swizzled rows");
   static_assert(STAGE_BYTES % 1024 == 0, "stages keep the 1024-byte swizzle alignment");
 };
 
@@ -66,11 +77,11 @@ DMX_DEVICE void tile_origin(const TcParams& p, int mt, int& tb, int& ty0, int& t
 // tile) space in row-major order, so the column tiles of one row tile run on
 // neighbouring SMs at the same time and its A rows come from HBM once. Two
 // TMEM accumulators: the epilogue of one tile overlaps the MMAs of the next.
-template <int BN, int BK, int STAGES, int EPI, int MODE>
+template <int BN, int BK, int STAGES, int EPI, int MODE, bool RB = false>
 __global__ void __launch_bounds__(kThreads, 1)
     tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const __grid_constant__ CUtensorMap tmBlo, const TcParams p) {
-  using S = Smem<BN, BK, STAGES, MODE>;
+  using S = Smem<BN, BK, STAGES, MODE, RB>;
   constexpr bool SPLIT = S::SPLIT, BF = S::BF;
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   unsigned char* smem = reinterpret_cast<unsigned char*>(
@@ -80,7 +91,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* conv = empty + STAGES;
   uint64_t* acc_full = conv + STAGES;   // [2]
   uint64_t* acc_empty = acc_full + 2;   // [2]
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
+  uint64_t* bres_full = acc_empty + 2;  // resident B has landed (RB)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bres_full + 1);
+  unsigned char* bres = smem + STAGES * S::STAGE_BYTES + 1024;  // resident B (RB)
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   // a previous launch on this stream gave up: do nothing (uniform across the CTA)
@@ -96,12 +109,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&acc_full[a], 1);
       mbar_init(&acc_empty[a], kEpiThreads);
     }
+    mbar_init(bres_full, 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   if (warp == 1) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
                      smem_u32(tmem_slot)),
-                 "r"(2 * BN));
+                 "r"(S::TMEM_COLS));
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
   }
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
@@ -119,6 +133,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       // ---------------- TMA producer ----------------
       uint32_t it = 0;
       bool ok = true;
+      if (RB) {
+        // the whole B of the single column tile, once: K block kt at bres + kt B_BYTES
+        mbar_expect_tx(bres_full, (uint32_t)ktiles * S::B_BYTES);
+        for (int kt = 0; kt < ktiles; ++kt)
+          tma_load_2d(bres + kt * S::B_BYTES, &tmB, bres_full, kt * BK, 0);
+      }
       for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
         const int mt = t / p.ntiles, n0 = (t - mt * p.ntiles) * BN;
         int tb, ty0, tx0;
@@ -149,7 +169,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           } else {
             tma_load_2d(a_dst, &tmA, &full[s], k0, (int)m0);
           }
-          tma_load_2d(b_dst, &tmB, &full[s], k0, n0);
+          if (!RB) tma_load_2d(b_dst, &tmB, &full[s], k0, n0);
           if (SPLIT) tma_load_2d(b_dst + S::B_BYTES + S::A_BYTES, &tmBlo, &full[s], k0, n0);
         }
       }
@@ -163,7 +183,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                                  ((uint32_t)(BM >> 4) << 24);
       uint32_t it = 0;
       int tl = 0;
-      bool ok = true;
+      bool ok = !RB || mbar_wait(bres_full, 0, p.err, 6);
       for (int t = blockIdx.x; t < total && ok; t += gridDim.x, ++tl) {
         const int acc = tl & 1;
         if (!mbar_wait(&acc_empty[acc], ((tl >> 1) & 1) ^ 1, p.err, 5)) break;
@@ -178,11 +198,11 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
           const uint32_t a_addr = smem_u32(smem + s * S::STAGE_BYTES);
-          const uint32_t b_addr = a_addr + S::A_BYTES;
+          const uint32_t b_addr = RB ? smem_u32(bres + kt * S::B_BYTES) : a_addr + S::A_BYTES;
           const uint32_t alo_addr = b_addr + S::B_BYTES;
           const uint32_t blo_addr = alo_addr + S::A_BYTES;
           if (BF) {
-            // two K = 16 steps across the 64-byte bf16 rows of A and B
+            // K = 16 steps across the 64- or 128-byte bf16 rows of A and B
 #pragma unroll
             for (int j = 0; j < BK / 16; ++j)
               umma_bf16(d, umma_desc_k(a_addr + j * 32, BK * 2), umma_desc_k(b_addr + j * 32, BK * 2),
@@ -607,24 +627,31 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 1) {
     __syncwarp();
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(2 * BN));
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
+                 "r"(S::TMEM_COLS));
   }
 }
 
 // ---------------------------------------------------------------------------
 // host side
 // ---------------------------------------------------------------------------
-template <int BN, int BK, int STAGES, int MODE>
+// resident B's shared memory: every K block of one column tile
+template <int BN, int BK, int MODE>
+int resident_b_bytes(const TcParams& p) {
+  return (p.Kpad / BK) * Smem<BN, BK, 1, MODE>::B_BYTES;
+}
+
+template <int BN, int BK, int STAGES, int MODE, bool RB = false>
 void launch_cfg(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mblo,
                 const TcParams& p, int epi, dim3 grid, cudaStream_t s) {
-  const int smem = Smem<BN, BK, STAGES, MODE>::TOTAL;
+  const int smem = Smem<BN, BK, STAGES, MODE, RB>::TOTAL + (RB ? resident_b_bytes<BN, BK, MODE>(p) : 0);
 #define DMX_TC_CASE(E)                                                                        \
   case E: {                                                                                   \
     static PerDevice attr;                                                                    \
     if (attr.first())                                                                         \
-      cudaFuncSetAttribute(tc_gemm_kernel<BN, BK, STAGES, E, MODE>,                          \
-                           cudaFuncAttributeMaxDynamicSharedMemorySize, smem);                                                                                         \
-    tc_gemm_kernel<BN, BK, STAGES, E, MODE><<<grid, kThreads, smem, s>>>(ma, mb, mblo, p);   \
+      cudaFuncSetAttribute(tc_gemm_kernel<BN, BK, STAGES, E, MODE, RB>,                      \
+                           cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);          \
+    tc_gemm_kernel<BN, BK, STAGES, E, MODE, RB><<<grid, kThreads, smem, s>>>(ma, mb, mblo, p); \
     break;                                                                                    \
   }
   switch (epi) {
@@ -688,12 +715,23 @@ bool tc_gemm_supported(const TcOperandA& a, const TcParams& p) {
   return true;
 }
 
+// K channels per stage of a bf16 GEMM: 64 (128-byte rows, half the TMA
+// requests per byte) when K allows it, else 32
+int bf16_bk(const TcParams& p) { return p.Kpad % 64 == 0 && p.Cin % 64 == 0 ? 64 : 32; }
+
 void launch_tc_gemm(const TcOperandA& a, const float* wk, const float* wk_lo, const TcParams& p0,
                     int epi, cudaStream_t s) {
   TcParams p = p0;
   const int bk = (p.Cin % 32 == 0) ? 32 : 16;
+  const int bkb = p.bf16 ? bf16_bk(p) : 0;
+  const CUtensorMapSwizzle swz_bf = bkb == 64 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
+  // resident B: a narrow layer (N = 96 in one exact column tile, 16-channel K
+  // blocks) whose whole B fits in shared memory beside six A stages
+  const bool rb = !p.bf16 && !wk_lo && bk == 16 && p.N == 96 && p.Npad >= 96 && !p.epi_stats &&
+                  Smem<96, 16, 6, MODE_TF32, true>::TOTAL + resident_b_bytes<96, 16, MODE_TF32>(p) <=
+                      227 * 1024;
   const CUtensorMapSwizzle swz = bk == 32 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
-  const int bn = pick_bn(p.N);
+  const int bn = rb ? 96 : pick_bn(p.N);
   CUtensorMap ma, mb, mblo;
   bool ok;
   if (p.mode == TC_2D) {
@@ -711,11 +749,11 @@ void launch_tc_gemm(const TcOperandA& a, const float* wk, const float* wk_lo, co
     const cuuint32_t estr[3] = {1, (cuuint32_t)p.sx, 1};
     ok = make_tensor_map(&ma, a.ptr, 3, dims, str, box, swz, estr);
     p.mtiles = ((p.Wq + BM - 1) / BM) * p.B;
-  } else if (p.bf16) {  // bf16 activations [rows][C]: 64-byte rows of 32 channels
+  } else if (p.bf16) {  // bf16 activations [rows][C]: rows of bkb channels
     const cuuint64_t dims[2] = {(cuuint64_t)a.C, (cuuint64_t)a.W};
     const cuuint64_t str[1] = {(cuuint64_t)a.sw * 2};
-    const cuuint32_t box[2] = {32, (cuuint32_t)BM};
-    ok = make_tensor_map(&ma, a.ptr, 2, dims, str, box, CU_TENSOR_MAP_SWIZZLE_64B, nullptr,
+    const cuuint32_t box[2] = {(cuuint32_t)bkb, (cuuint32_t)BM};
+    ok = make_tensor_map(&ma, a.ptr, 2, dims, str, box, swz_bf, nullptr,
                          CU_TENSOR_MAP_DATA_TYPE_BFLOAT16);
     p.mtiles = (a.W + BM - 1) / BM;
   } else {
@@ -725,11 +763,11 @@ void launch_tc_gemm(const TcOperandA& a, const float* wk, const float* wk_lo, co
     ok = make_tensor_map(&ma, a.ptr, 2, dims, str, box, swz);
     p.mtiles = (a.W + BM - 1) / BM;
   }
-  if (p.bf16) {  // bf16 weights [Npad][Kpad]: 64-byte rows of 32 channels
+  if (p.bf16) {  // bf16 weights [Npad][Kpad]: rows of bkb channels
     const cuuint64_t dims[2] = {(cuuint64_t)p.Kpad, (cuuint64_t)p.Npad};
     const cuuint64_t str[1] = {(cuuint64_t)p.Kpad * 2};
-    const cuuint32_t box[2] = {32, (cuuint32_t)bn};
-    ok = ok && make_tensor_map(&mb, wk, 2, dims, str, box, CU_TENSOR_MAP_SWIZZLE_64B, nullptr,
+    const cuuint32_t box[2] = {(cuuint32_t)bkb, (cuuint32_t)bn};
+    ok = ok && make_tensor_map(&mb, wk, 2, dims, str, box, swz_bf, nullptr,
                                CU_TENSOR_MAP_DATA_TYPE_BFLOAT16);
     mblo = mb;
   } else {
@@ -743,10 +781,16 @@ void launch_tc_gemm(const TcOperandA& a, const float* wk, const float* wk_lo, co
   p.ntiles = (p.N + bn - 1) / bn;
   const int64_t total = (int64_t)p.mtiles * p.ntiles;
   const dim3 grid((unsigned)std::min<int64_t>(total, sm_count()));
-  if (p.bf16) {  // bf16 operands: 32-channel K tiles only (checked by tc_gemm_supported)
+  if (p.bf16 && bkb == 64) {  // bf16 operands, 64-channel K tiles (192 KB of stages)
+    if (bn == 64) launch_cfg<64, 64, 8, MODE_BF16>(ma, mb, mblo, p, epi, grid, s);
+    else if (bn == 128) launch_cfg<128, 64, 6, MODE_BF16>(ma, mb, mblo, p, epi, grid, s);
+    else launch_cfg<256, 64, 4, MODE_BF16>(ma, mb, mblo, p, epi, grid, s);
+  } else if (p.bf16) {  // bf16 operands, 32-channel K tiles
     if (bn == 64) launch_cfg<64, 32, 12, MODE_BF16>(ma, mb, mblo, p, epi, grid, s);
     else if (bn == 128) launch_cfg<128, 32, 10, MODE_BF16>(ma, mb, mblo, p, epi, grid, s);
     else launch_cfg<256, 32, 8, MODE_BF16>(ma, mb, mblo, p, epi, grid, s);
+  } else if (rb) {
+    launch_cfg<96, 16, 6, MODE_TF32, true>(ma, mb, mblo, p, epi, grid, s);
   } else if (wk_lo) {  // 3xTF32: split stages are twice the size
     if (bn == 64) {
       if (bk == 32) launch_cfg<64, 32, 4, MODE_SPLIT>(ma, mb, mblo, p, epi, grid, s);
