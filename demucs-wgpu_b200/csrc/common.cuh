@@ -36,6 +36,26 @@ constexpr int kStftLen = 347136;  // 343980 + 1536 + 1620
 DMX_DEVICE float gelu(float x) { return 0.5f * x * (1.0f + erff(x * 0.70710678118654752f)); }
 DMX_DEVICE float sigmoid(float g) { return 1.0f / (1.0f + expf(-g)); }
 
+// The tensor-core builds' epilogue activations, in fewer instructions: their
+// inputs carry tf32 rounding (2^-11 relative), far above these functions'
+// errors. erf by Abramowitz & Stegun, Handbook of Mathematical Functions,
+// eq. 7.1.26 (|error| <= 1.5e-7): erf(z) = 1 - t (a1 + t (a2 + t (a3 + t (a4 +
+// t a5)))) exp(-z^2), t = 1 / (1 + p z), z >= 0, odd in z; the exponential and
+// the reciprocal on the special-function unit.
+DMX_DEVICE float erf_as(float z) {
+  const float a = fabsf(z);
+  const float t = __fdividef(1.0f, fmaf(0.3275911f, a, 1.0f));
+  float q = fmaf(1.061405429f, t, -1.453152027f);
+  q = fmaf(q, t, 1.421413741f);
+  q = fmaf(q, t, -0.284496736f);
+  q = fmaf(q, t, 0.254829592f);
+  const float r = 1.0f - q * t * __expf(-a * a);
+  return copysignf(r, z);
+}
+DMX_DEVICE float gelu_tc(float x) { return 0.5f * x * (1.0f + erf_as(x * 0.70710678118654752f)); }
+// value * sigmoid(gate); 0 once exp(-gate) overflows (gate < -87)
+DMX_DEVICE float glu_tc(float value, float gate) { return __fdividef(value, 1.0f + __expf(-gate)); }
+
 // fp32 -> nearest tf32 (ties to even), kept in an fp32 container.
 DMX_DEVICE float round_tf32(float x) {
   uint32_t b = __float_as_uint(x);

@@ -598,7 +598,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
       for (int h = 0; h < S::HID; ++h) {
         const float scale = inv * k.n1w[h];
-        ga[h] = mine ? gelu(yh[h] * scale + (k.n1b[h] - mean * scale)) : 0.f;
+        ga[h] = mine ? gelu_tc(yh[h] * scale + (k.n1b[h] - mean * scale)) : 0.f;
       }
       ga[S::HID] = 1.0f;
       if (conv2) {
@@ -720,7 +720,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               // gamma * GN2(value), GN2(gate)
               const float value = fmaf(__uint_as_float(zr[2 * kk]), f.x, f.y);
               const float gate = fmaf(__uint_as_float(zr[2 * kk + 1]), f.z, f.w);
-              o[kk] += __fdividef(value, 1.0f + __expf(-gate));
+              o[kk] += glu_tc(value, gate);
               if (a.round_out) o[kk] = round_tf32(o[kk]);
             }
             float4* x4 = reinterpret_cast<float4*>(xp);

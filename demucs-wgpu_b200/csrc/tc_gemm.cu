@@ -271,7 +271,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 float g = 0.f;
                 if (a_row && k < p.a_nvalid) {
                   const float scale = a_inv * p.a_gw[k];
-                  g = gelu(xv[e] * scale + (p.a_gb[k] - a_mean * scale));
+                  g = gelu_tc(xv[e] * scale + (p.a_gb[k] - a_mean * scale));
                 }
                 xv[e] = g;
               }
@@ -368,7 +368,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             // (a multiple of 16) and goes to row orow + group * o_pstride
             if (EPI == EPI_GELU) {
 #pragma unroll
-              for (int j = 0; j < 32; ++j) v[j] = gelu(v[j]);
+              for (int j = 0; j < 32; ++j) v[j] = gelu_tc(v[j]);
             }
 #pragma unroll
             for (int hf = 0; hf < 2; ++hf) {
@@ -415,7 +415,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           } else if (EPI == EPI_STORE || EPI == EPI_GELU || EPI == EPI_STORE_STATS) {
             if (EPI == EPI_GELU) {
 #pragma unroll
-              for (int j = 0; j < 32; ++j) v[j] = gelu(v[j]);
+              for (int j = 0; j < 32; ++j) v[j] = gelu_tc(v[j]);
             }
             const bool vec = full && ((orow + nb) & 3) == 0;
             if (p.epi_add) {
@@ -475,7 +475,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             // 16 outputs: channels nb/2 .. nb/2 + 15
             float g[16];
 #pragma unroll
-            for (int j = 0; j < 16; ++j) g[j] = v[2 * j] * sigmoid(v[2 * j + 1]);
+            for (int j = 0; j < 16; ++j) g[j] = glu_tc(v[2 * j], v[2 * j + 1]);
             const int c0o = nb / 2;
             const bool vec = full && ((orow + c0o) & 3) == 0;
             if (EPI == EPI_GLU_EMB) {
@@ -543,7 +543,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                   const float gsc = nr.inv * awg[e];
                   const float value = v[2 * j] * vs + (abv[e] - nr.mean * vs);
                   const float gate = v[2 * j + 1] * gsc + (abg[e] - nr.mean * gsc);
-                  res[j] += agm[e] * (value * sigmoid(gate));
+                  res[j] += agm[e] * glu_tc(value, gate);
                 }
               }
             } else {
@@ -555,7 +555,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                   const float gsc = nr.inv * p.epi_gw[c + p.epi_half];
                   const float value = v[2 * j] * vs + (p.epi_gb[c] - nr.mean * vs);
                   const float gate = v[2 * j + 1] * gsc + (p.epi_gb[c + p.epi_half] - nr.mean * gsc);
-                  res[j] += p.epi_gamma[c] * (value * sigmoid(gate));
+                  res[j] += p.epi_gamma[c] * glu_tc(value, gate);
                 }
               }
             }
