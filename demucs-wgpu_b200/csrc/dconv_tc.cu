@@ -158,7 +158,9 @@ DMX_DEVICE void norm_of(double s, double q, double inv_count, float& mean, float
 // branch in one launch, row moments reduced inside the CTA). Longer rows run
 // three launches: DC_STATS1 (conv1 from x: y into the y buffer and the
 // moments of y per tile), DC_STATS2 (g from y with the row's moments summed
-// over its tiles in a fixed order; the moments of z per tile) and DC_OUT
+// over its tiles in a fixed order; the moments of z per tile — launched as
+// dconv_tc_stats2_kernel, which runs the same arithmetic many blocks per SM)
+// and DC_OUT
 // (conv2 and the output). Only DC_STATS1 reads the halo frames, so the
 // output written in place by one tile never reaches another tile's input.
 enum DcMode : int { DC_ROW = 0, DC_STATS1 = 1, DC_STATS2 = 2, DC_OUT = 3 };
@@ -745,6 +747,102 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
+// DC_STATS2 as a plain kernel: one 384-thread block per tile, thread p on
+// local frame p, the same arithmetic in the same order as the persistent
+// kernel's epilogue warps (thread p there is epilogue thread p): the row's
+// y moments summed over its tiles by one warp, g = GELU(GroupNorm1(y)), the
+// quadratic form for the moments of z, and the block sum (lanes, then warps
+// in order) into part2. Blocks run many per SM, so the pass moves at the
+// speed of its loads instead of one tile per SM at a time.
+template <int C>
+__global__ void __launch_bounds__(kEpiThreads)
+    dconv_tc_stats2_kernel(const DConvArgs a, const __grid_constant__ DcConst<C> k) {
+  using S = DcTc<C>;
+  __shared__ double red[2 * kEpiWarps];
+  const int w = blockIdx.x, p = threadIdx.x, warp = p / 32, lane = p % 32;
+  const int T = a.T;
+  const int row = w / a.tiles, ts = (w - row * a.tiles) * kTileStride - 2;
+  const bool mine = p >= 2 && p < 382 && ts + p < T;
+  float yh[S::HID];
+  if (mine) {
+    const float4* yp = reinterpret_cast<const float4*>(a.y + ((int64_t)row * T + ts + p) * S::YS);
+#pragma unroll
+    for (int c = 0; c < S::YS / 4; ++c) {
+      const float4 v = yp[c];
+      const float t4[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+        if (4 * c + i < S::HID) yh[4 * c + i] = t4[i];
+    }
+  } else {
+#pragma unroll
+    for (int h = 0; h < S::HID; ++h) yh[h] = 0.f;
+  }
+  // the row's y moments over its tiles, in tile order per lane, then the lanes
+  if (warp == 0) {
+    double ls = 0.0, lq = 0.0;
+    for (int t = lane; t < a.tiles; t += 32) {
+      ls += a.part1[2 * ((int64_t)row * a.tiles + t)];
+      lq += a.part1[2 * ((int64_t)row * a.tiles + t) + 1];
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) {
+      ls += __shfl_xor_sync(0xffffffffu, ls, o);
+      lq += __shfl_xor_sync(0xffffffffu, lq, o);
+    }
+    if (lane == 0) {
+      red[0] = ls;
+      red[1] = lq;
+    }
+  }
+  __syncthreads();
+  const double s1 = red[0], q1 = red[1];
+  __syncthreads();
+  const double ic1 = 1.0 / ((double)S::HID * T);
+  float mean, inv;
+  norm_of(s1, q1, ic1, mean, inv);
+  float ga[S::ACT];
+#pragma unroll
+  for (int h = 0; h < S::HID; ++h) {
+    const float scale = inv * k.n1w[h];
+    ga[h] = mine ? gelu_tc(yh[h] * scale + (k.n1b[h] - mean * scale)) : 0.f;
+  }
+  ga[S::HID] = 1.0f;
+  float l = 0.f, qf = 0.f;
+  if (mine) {
+#pragma unroll
+    for (int i = 0, idx = 0; i < S::ACT; ++i) {
+      l = fmaf(k.v[i], ga[i], l);
+      float t = 0.f;
+#pragma unroll
+      for (int j = i; j < S::ACT; ++j, ++idx) t = fmaf(k.m[idx], ga[j], t);
+      qf = fmaf(ga[i], t, qf);
+    }
+  }
+  double s = l, q = qf;
+#pragma unroll
+  for (int o = 16; o; o >>= 1) {
+    s += __shfl_xor_sync(0xffffffffu, s, o);
+    q += __shfl_xor_sync(0xffffffffu, q, o);
+  }
+  if (lane == 0) {
+    red[2 * warp] = s;
+    red[2 * warp + 1] = q;
+  }
+  __syncthreads();
+  if (p == 0) {
+    s = 0.0;
+    q = 0.0;
+#pragma unroll
+    for (int ww = 0; ww < kEpiWarps; ++ww) {
+      s += red[2 * ww];
+      q += red[2 * ww + 1];
+    }
+    a.part2[2 * (int64_t)w] = s;
+    a.part2[2 * (int64_t)w + 1] = q;
+  }
+}
+
 template <int C>
 bool launch_c(const DConvArgs& a, cudaStream_t s) {
   using S = DcTc<C>;
@@ -791,8 +889,9 @@ bool launch_c(const DConvArgs& a, cudaStream_t s) {
   if (a.tiles == 1) {
     dconv_tc_row_kernel<C><<<grid, kThreads, S::SMEM, s>>>(mx, m1, m1lo, m2, m2lo, a, k, DC_ROW);
   } else {
-    for (int mode = DC_STATS1; mode <= DC_OUT; ++mode)
-      dconv_tc_row_kernel<C><<<grid, kThreads, S::SMEM, s>>>(mx, m1, m1lo, m2, m2lo, a, k, mode);
+    dconv_tc_row_kernel<C><<<grid, kThreads, S::SMEM, s>>>(mx, m1, m1lo, m2, m2lo, a, k, DC_STATS1);
+    dconv_tc_stats2_kernel<C><<<items, kEpiThreads, 0, s>>>(a, k);
+    dconv_tc_row_kernel<C><<<grid, kThreads, S::SMEM, s>>>(mx, m1, m1lo, m2, m2lo, a, k, DC_OUT);
   }
   return true;
 }
