@@ -37,7 +37,9 @@
 // part is x - trunc_tf32(x), exact in fp32. The weights' high parts are
 // rounded to nearest on the host and their residuals stored beside them. The
 // result agrees with fp32 arithmetic to ~1e-6 relative; moments are summed in
-// f64 as the reference's GroupNorm does. No load uses cluster multicast.
+// f64 as the reference's GroupNorm does. With SPLIT off (the BF16 build) the
+// contractions are single-pass tf32: no low parts, one product per K step.
+// No load uses cluster multicast.
 #include <cudaTypedefs.h>
 
 #include "common.cuh"
@@ -166,7 +168,7 @@ DMX_DEVICE void norm_of(double s, double q, double inv_count, float& mean, float
 enum DcMode : int { DC_ROW = 0, DC_STATS1 = 1, DC_STATS2 = 2, DC_OUT = 3 };
 constexpr int kTileStride = 380;
 
-template <int C>
+template <int C, bool SPLIT>
 __global__ void __launch_bounds__(kThreads, 1)
     dconv_tc_row_kernel(const __grid_constant__ CUtensorMap tmX,
                         const __grid_constant__ CUtensorMap tmW1,
@@ -226,18 +228,18 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) {
       // ---------------- TMA producer ----------------
       if (conv2) {
-        mbar_expect_tx(&w2_full, 2 * S::W2_BYTES);
+        mbar_expect_tx(&w2_full, (SPLIT ? 2 : 1) * S::W2_BYTES);
         tma_load_2d(smem + S::OFF_W2, &tmW2, &w2_full, 0, 0);
-        tma_load_2d(smem + S::OFF_W2 + S::W2_BYTES, &tmW2lo, &w2_full, 0, 0);
+        if (SPLIT) tma_load_2d(smem + S::OFF_W2 + S::W2_BYTES, &tmW2lo, &w2_full, 0, 0);
       }
       if (conv1) {
         // conv1 weights, once: K block kb's taps side by side (B rows 16 tap ..)
-        mbar_expect_tx(&w1_full, 2 * S::W1_BYTES);
+        mbar_expect_tx(&w1_full, (SPLIT ? 2 : 1) * S::W1_BYTES);
         for (int kb = 0; kb < S::KB; ++kb)
           for (int tap = 0; tap < 3; ++tap) {
             unsigned char* b = smem + S::OFF_W1 + kb * S::W1_KB + tap * S::HP * S::BK * 4;
             tma_load_2d(b, &tmW1, &w1_full, tap * C + kb * S::BK, 0);
-            tma_load_2d(b + S::W1_BYTES, &tmW1lo, &w1_full, tap * C + kb * S::BK, 0);
+            if (SPLIT) tma_load_2d(b + S::W1_BYTES, &tmW1lo, &w1_full, tap * C + kb * S::BK, 0);
           }
         uint32_t it = 0;
         bool ok = true;
@@ -280,9 +282,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int kk = 0; kk < 2; ++kk) {
           const uint64_t gh = umma_desc_k(g_hi + kk * 32, 64);
           const uint64_t wh = umma_desc_k(w_hi + kk * 32, 64);
-          umma_tf32(d, umma_desc_k(g_lo + kk * 32, 64), wh, idesc2, kk != 0);
-          umma_tf32(d, gh, umma_desc_k(w_lo + kk * 32, 64), idesc2, 1);
-          umma_tf32(d, gh, wh, idesc2, 1);
+          if (SPLIT) {
+            umma_tf32(d, umma_desc_k(g_lo + kk * 32, 64), wh, idesc2, kk != 0);
+            umma_tf32(d, gh, umma_desc_k(w_lo + kk * 32, 64), idesc2, 1);
+            umma_tf32(d, gh, wh, idesc2, 1);
+          } else {
+            umma_tf32(d, gh, wh, idesc2, kk != 0);
+          }
         }
       };
       // Issues what it can of item pend's conv2; with `block`, all of it.
@@ -365,18 +371,20 @@ __global__ void __launch_bounds__(kThreads, 1)
               for (int j = 0; j < S::BK / 8; ++j) {
                 const uint64_t ah = umma_desc_k(a_hi + j * 32, S::BK * 4);
                 umma_tf32(d, ah, umma_desc_k(b_hi + j * 32, S::BK * 4), idesc1, (kb | j) != 0);
-                umma_tf32(d, ah, umma_desc_k(b_lo + j * 32, S::BK * 4), idesc1, 1);
+                if (SPLIT) umma_tf32(d, ah, umma_desc_k(b_lo + j * 32, S::BK * 4), idesc1, 1);
               }
-              // its low part is written: the last product
-              if (!mbar_wait(&conv[s], par, a.err, 28)) {
-                ok = false;
-                break;
-              }
-              asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+              if (SPLIT) {
+                // its low part is written: the last product
+                if (!mbar_wait(&conv[s], par, a.err, 28)) {
+                  ok = false;
+                  break;
+                }
+                asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
 #pragma unroll
-              for (int j = 0; j < S::BK / 8; ++j)
-                umma_tf32(d, umma_desc_k(a_lo + j * 32, S::BK * 4),
-                          umma_desc_k(b_hi + j * 32, S::BK * 4), idesc1, 1);
+                for (int j = 0; j < S::BK / 8; ++j)
+                  umma_tf32(d, umma_desc_k(a_lo + j * 32, S::BK * 4),
+                            umma_desc_k(b_hi + j * 32, S::BK * 4), idesc1, 1);
+              }
               umma_commit(&empty[s]);
             }
           }
@@ -402,7 +410,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else if (warp < 4) {
     // ---------------- converter: the low part of each x tile row ----------------
-    if (conv1) {
+    if (conv1 && SPLIT) {
       const int c = threadIdx.x - 64;  // rows c and c + 64 (the same swizzle phase)
       const int swz = S::BK == 32 ? (c & 7) : ((c >> 1) & 3);
       uint32_t it = 0;
@@ -618,9 +626,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           const int phys = (c ^ ((r >> 1) & 3)) << 4;
           const float4 v = make_float4(gs[4 * c], gs[4 * c + 1], gs[4 * c + 2], gs[4 * c + 3]);
           *reinterpret_cast<float4*>(hi + phys) = v;
-          *reinterpret_cast<float4*>(lo + phys) =
-              make_float4(v.x - trunc_tf32(v.x), v.y - trunc_tf32(v.y), v.z - trunc_tf32(v.z),
-                          v.w - trunc_tf32(v.w));
+          if (SPLIT)
+            *reinterpret_cast<float4*>(lo + phys) =
+                make_float4(v.x - trunc_tf32(v.x), v.y - trunc_tf32(v.y), v.z - trunc_tf32(v.z),
+                            v.w - trunc_tf32(v.w));
         }
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
         asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
@@ -878,20 +887,24 @@ bool launch_c(const DConvArgs& a, cudaStream_t s) {
   for (int i = 0; i < S::HID; ++i) k.n1w[i] = *src++;
   for (int i = 0; i < S::HID; ++i) k.n1b[i] = *src++;
   static PerDevice configured;
-  if (configured.first())
-    cudaFuncSetAttribute(dconv_tc_row_kernel<C>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+  if (configured.first()) {
+    cudaFuncSetAttribute(dconv_tc_row_kernel<C, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                          S::SMEM);
+    cudaFuncSetAttribute(dconv_tc_row_kernel<C, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         S::SMEM);
+  }
+  auto row_kernel = a.single ? dconv_tc_row_kernel<C, false> : dconv_tc_row_kernel<C, true>;
   int dev = 0, sms = 148;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   const int items = a.rows * a.tiles;
   const int grid = items < sms ? items : sms;
   if (a.tiles == 1) {
-    dconv_tc_row_kernel<C><<<grid, kThreads, S::SMEM, s>>>(mx, m1, m1lo, m2, m2lo, a, k, DC_ROW);
+    row_kernel<<<grid, kThreads, S::SMEM, s>>>(mx, m1, m1lo, m2, m2lo, a, k, DC_ROW);
   } else {
-    dconv_tc_row_kernel<C><<<grid, kThreads, S::SMEM, s>>>(mx, m1, m1lo, m2, m2lo, a, k, DC_STATS1);
+    row_kernel<<<grid, kThreads, S::SMEM, s>>>(mx, m1, m1lo, m2, m2lo, a, k, DC_STATS1);
     dconv_tc_stats2_kernel<C><<<items, kEpiThreads, 0, s>>>(a, k);
-    dconv_tc_row_kernel<C><<<grid, kThreads, S::SMEM, s>>>(mx, m1, m1lo, m2, m2lo, a, k, DC_OUT);
+    row_kernel<<<grid, kThreads, S::SMEM, s>>>(mx, m1, m1lo, m2, m2lo, a, k, DC_OUT);
   }
   return true;
 }

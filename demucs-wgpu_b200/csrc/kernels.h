@@ -48,6 +48,9 @@ struct DConvArgs {
   double* part2;
   int* err;  // raised when a bounded wait gives up
   int round_out;  // store the updated x rounded to nearest tf32 (it feeds only tf32 GEMMs)
+  // tensor-core path: single-pass tf32 (x read by the tensor core as tf32, the
+  // weights' high parts only) instead of 3xTF32; the BF16 build's choice
+  int single;
   // tensor-core path (dconv_tc.cu): K-major weights rounded to nearest tf32
   // ([w1_npad][3C], [w2_npad][16]) and their residuals w - tf32(w)
   const float* w1_tc;
