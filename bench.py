@@ -344,11 +344,26 @@ def run_ours(args, rank, world, local_rank):
         flag = torch.zeros(1, dtype=torch.float32, device=cuda)
     torch.cuda.synchronize()
     peers_acc = peers_stems = None
-    if world > 1 and args.exchange == "peer":
+    exchange = args.exchange if world > 1 else None
+    if exchange == "peer":
         # every rank maps its neighbours' accumulator and stems (CUDA IPC): the boundary
-        # tail and the gather are SM loads over NVLink between on-stream barriers
-        peers_acc = shard.PeerBuffers(dist, dev, acc.data_ptr())
-        peers_stems = shard.PeerBuffers(dist, dev, stems.data_ptr())
+        # tail and the gather are SM loads over NVLink between on-stream barriers. If any
+        # rank cannot map them, every rank uses the NCCL exchange instead (the decision
+        # is collective, so all ranks take the same path)
+        err = ""
+        try:
+            peers_acc = shard.PeerBuffers(dist, dev, acc.data_ptr())
+            peers_stems = shard.PeerBuffers(dist, dev, stems.data_ptr())
+        except Exception as exc:  # mapping refused by the driver or the platform
+            err = f"{type(exc).__name__}: {exc}"
+        failed = torch.tensor([1.0 if err else 0.0], device=cuda)
+        dist.all_reduce(failed, op=dist.ReduceOp.MAX)
+        if failed.item() > 0:
+            for pb in (peers_acc, peers_stems):
+                if pb is not None:
+                    pb.close()
+            peers_acc = peers_stems = None
+            exchange = "nccl (peer mapping failed" + (f": {err[:120]}" if err else " on another rank") + ")"
     phase_events = None  # set to a list to record (start, forward, exchange, finish, gather)
 
     def mark():
@@ -518,7 +533,7 @@ def run_ours(args, rank, world, local_rank):
             "config": track_config(seconds),
             "precision": args.precision,
             "parallelism": f"chunk-sharded x{world}" + (
-                f", boundary tail and stem gather over NVLink ({args.exchange})" if world > 1 else ""),
+                f", boundary tail and stem gather over NVLink ({exchange})" if world > 1 else ""),
             "chunks_per_gpu": [r.chunk_hi - r.chunk_lo for r in p.ranks],
             "e2e": {"value": round(seconds / e2e_s, 3), "unit": UNIT,
                     "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h),
@@ -826,7 +841,7 @@ def main():
                     help="track: one 240 s track (the headline); bag: the htdemucs_ft bag of 4; "
                          "batch: the many-track throughput batch")
     ap.add_argument("--tracks", type=int, default=64, help="--workload batch: tracks")
-    ap.add_argument("--exchange", default="nccl", choices=["peer", "nccl"],
+    ap.add_argument("--exchange", default="peer", choices=["peer", "nccl"],
                     help="N > 1: boundary tail and stem gather as SM loads from mapped peer "
                          "memory (peer) or as NCCL point-to-point messages (nccl)")
     ap.add_argument("--max-batch", type=int, default=42,

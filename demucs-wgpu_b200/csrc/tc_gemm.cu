@@ -49,6 +49,16 @@ struct Smem {
   static_assert(STAGE_BYTES % 1024 == 0, "stages keep the 1024-byte swizzle alignment");
 };
 
+// GELU of the GEMM epilogue: on the A&S erf (fewer instructions, two of them
+// on the special-function unit) in the tf32 GEMMs, on erff in the bf16 GEMMs,
+// where the faster MMAs leave the epilogue's special-function operations the
+// limit (measured on B200: the BF16 FFN1 took 3.14 ms on the A&S erf, 3.01 ms
+// on erff)
+template <int MODE>
+DMX_DEVICE float gelu_epi(float x) {
+  return MODE == MODE_BF16 ? gelu(x) : gelu_tc(x);
+}
+
 // two fp32 -> one bf16x2 word, round to nearest even (lo in the low half)
 DMX_DEVICE uint32_t pack_bf16(float lo, float hi) {
   const __nv_bfloat162 v = __float22bfloat162_rn(make_float2(lo, hi));
@@ -368,7 +378,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             // (a multiple of 16) and goes to row orow + group * o_pstride
             if (EPI == EPI_GELU) {
 #pragma unroll
-              for (int j = 0; j < 32; ++j) v[j] = gelu_tc(v[j]);
+              for (int j = 0; j < 32; ++j) v[j] = gelu_epi<MODE>(v[j]);
             }
 #pragma unroll
             for (int hf = 0; hf < 2; ++hf) {
@@ -415,7 +425,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           } else if (EPI == EPI_STORE || EPI == EPI_GELU || EPI == EPI_STORE_STATS) {
             if (EPI == EPI_GELU) {
 #pragma unroll
-              for (int j = 0; j < 32; ++j) v[j] = gelu_tc(v[j]);
+              for (int j = 0; j < 32; ++j) v[j] = gelu_epi<MODE>(v[j]);
             }
             const bool vec = full && ((orow + nb) & 3) == 0;
             if (p.epi_add) {

@@ -200,12 +200,25 @@ class PeerBuffers:
 
         self.device = device
         self.rank = dist.get_rank()
-        mine = dmx.ipc_export(device, ptr)
+        # every rank takes part in the exchange even when its own export failed,
+        # so a failure raises on every rank instead of leaving the others waiting
+        try:
+            mine = dmx.ipc_export(device, ptr)
+        except Exception as exc:
+            mine = ("error", f"{type(exc).__name__}: {exc}")
         everyone = [None] * dist.get_world_size()
         dist.all_gather_object(everyone, mine)
+        failed = [e[1] for e in everyone if isinstance(e[0], str)]
+        if failed:
+            raise RuntimeError("peer buffer export failed: " + failed[0])
         self.offsets = [off for _, off in everyone]
-        self.ptrs = [ptr if r == self.rank else dmx.ipc_open(device, hnd, off)
-                     for r, (hnd, off) in enumerate(everyone)]
+        self.ptrs = []
+        try:
+            for r, (hnd, off) in enumerate(everyone):
+                self.ptrs.append(ptr if r == self.rank else dmx.ipc_open(device, hnd, off))
+        except Exception:
+            self.close()
+            raise
 
     def close(self):
         import dmx

@@ -238,3 +238,37 @@ def test_tracks_over_ranks_gather_to_rank0(tmp_path):
     for i, n in enumerate(lengths):
         ref = oracle.separate_with(_forward, _track()[:, :n].copy(), SEG, shifts=2)
         assert np.array_equal(got[f"arr_{i}"], ref)
+
+
+def _peer_fail_worker(rank, world, port, out_dir):
+    # no GPU here, so exporting a device buffer fails on every rank: each rank must
+    # still join the handle exchange and then raise, none may be left waiting
+    import datetime
+    import sys
+
+    import torch.distributed as dist
+
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    sys.path[:0] = [os.path.join(root, "demucs-wgpu_b200")]
+    import shard
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=60))
+    try:
+        shard.PeerBuffers(dist, 0, 0x1000)
+        result = "mapped"
+    except RuntimeError as exc:
+        result = "raised: " + str(exc).split(":")[0]
+    with open(os.path.join(out_dir, f"rank{rank}.txt"), "w") as f:
+        f.write(result)
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+def test_peer_buffer_setup_fails_on_every_rank_together(tmp_path):
+    mp.start_processes(_peer_fail_worker, args=(2, _free_port(), str(tmp_path)), nprocs=2,
+                       join=True, start_method="spawn")
+    for r in range(2):
+        assert open(tmp_path / f"rank{r}.txt").read() == "raised: peer buffer export failed"
