@@ -19,7 +19,13 @@
 // rescaled in TMEM); otherwise P = exp(s - m) with the stale m, which is
 // exact algebra and stays below 2^8. q, k, v arrive rounded to nearest tf32
 // by the projection GEMM, so the tensor core's operand truncation is exact.
-// No load uses cluster multicast.
+//
+// The bf16 variant (the BF16 build) runs both products on kind::f16 with
+// bf16 q, k and V^T stored so by the projection GEMMs: TMA also brings the
+// CTA's Q tile into shared memory, and the softmax warps write P, rounded to
+// bf16 (the row sum adds the rounded values), into a shared-memory buffer
+// per S buffer instead of over S; both are K-major, 128-byte swizzled A
+// operands. No load uses cluster multicast.
 #include <cudaTypedefs.h>
 
 #include "common.cuh"
@@ -37,9 +43,20 @@ constexpr int KT = 64;    // keys per tile
 constexpr int HD = 64;    // head dim
 constexpr int STAGES = 3;
 constexpr int KCHUNK = KT * 128;             // one 64-row x 128-byte swizzled chunk
-constexpr int KV_BYTES = 2 * KCHUNK;         // 64 x 64 fp32 (two 32-column boxes)
-constexpr int STAGE_BYTES = 2 * KV_BYTES;    // K then V^T
-constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + 256;
+
+// Shared memory: the K / V^T ring (fp32: two 32-column chunks per operand;
+// bf16: one 64-column chunk), then for bf16 the Q tile and two P buffers.
+template <bool BF>
+struct AttnSmem {
+  static constexpr int KV_BYTES = BF ? KCHUNK : 2 * KCHUNK;  // 64 x 64 values
+  static constexpr int STAGE_BYTES = 2 * KV_BYTES;            // K then V^T
+  static constexpr int Q_BYTES = BF ? QT * 128 : 0;           // 128 rows x 64 bf16
+  static constexpr int P_BYTES = BF ? QT * 128 : 0;           // one P buffer, 128 x 64 bf16
+  static constexpr int OFF_Q = STAGES * STAGE_BYTES;
+  static constexpr int OFF_P = OFF_Q + Q_BYTES;
+  static constexpr int OFF_BAR = OFF_P + 2 * P_BYTES;
+  static constexpr int TOTAL = OFF_BAR + 256 + 1024 /*align*/;
+};
 // TMEM columns
 constexpr uint32_t TM_Q = 0, TM_S = 64, TM_O = 192;  // S buffers at 64 and 128
 constexpr float kRescale = 8.0f;  // log2 of the largest P tolerated before O is rescaled
@@ -62,7 +79,7 @@ DMX_DEVICE float ex2_approx(float x) {
 }
 
 struct AttnParams {
-  const float* q;
+  const float* q;  // fp32 variant: the q rows (the bf16 variant loads Q by TMA)
   int ldq;
   int heads;
   int nq, nk;
@@ -74,14 +91,20 @@ struct AttnParams {
   int* err;
 };
 
+template <bool BF>
 __global__ void __launch_bounds__(192, 2)
     attention_tc_kernel(const __grid_constant__ CUtensorMap tmKV,
-                        const __grid_constant__ CUtensorMap tmV, const AttnParams p) {
+                        const __grid_constant__ CUtensorMap tmV,
+                        const __grid_constant__ CUtensorMap tmQ, const AttnParams p) {
+  using L = AttnSmem<BF>;
+  constexpr int STAGE_BYTES = L::STAGE_BYTES, KV_BYTES = L::KV_BYTES;
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   unsigned char* smem = reinterpret_cast<unsigned char*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   unsigned char* KVs = smem;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(KVs + STAGES * STAGE_BYTES);
+  unsigned char* Qs = smem + L::OFF_Q;  // bf16: the Q tile
+  unsigned char* Ps = smem + L::OFF_P;  // bf16: P buffers [2]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::OFF_BAR);
   uint64_t* q_full = bars;                // Q rows in TMEM (128 arrivals)
   uint64_t* kv_full = q_full + 1;         // [STAGES]
   uint64_t* kv_empty = kv_full + STAGES;  // [STAGES]
@@ -96,7 +119,7 @@ __global__ void __launch_bounds__(192, 2)
   if (p.err && *reinterpret_cast<volatile int*>(p.err) != 0) return;
 
   if (threadIdx.x == 0) {
-    mbar_init(q_full, 128);
+    mbar_init(q_full, BF ? 1 : 128);
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&kv_full[s], 1);
       mbar_init(&kv_empty[s], 1);
@@ -124,24 +147,39 @@ __global__ void __launch_bounds__(192, 2)
 
   if (warp == 0) {
     if (lane == 0) {
+      if (BF) {
+        // the Q tile: queries q0 .. q0 + 127 of this (segment, head), two 64-row boxes
+        // (rows past the segment's queries are read but their outputs are dropped)
+        mbar_expect_tx(q_full, L::Q_BYTES);
+        for (int c = 0; c < 2; ++c)
+          tma_load_2d(Qs + c * KCHUNK, &tmQ, q_full, p.q_col + h * HD, b * p.nq + q0 + 64 * c);
+      }
       for (int j = 0; j < ntiles; ++j) {
         const int s = j % STAGES;
         const uint32_t ph = (j / STAGES) & 1;
         if (!mbar_wait(&kv_empty[s], ph ^ 1, p.err, 11)) break;
         unsigned char* st = KVs + s * STAGE_BYTES;
         mbar_expect_tx(&kv_full[s], STAGE_BYTES);
-        for (int c = 0; c < 2; ++c)
-          tma_load_2d(st + c * KCHUNK, &tmKV, &kv_full[s], p.k_col + h * HD + 32 * c, krow0 + j * KT);
-        // V^T rows (b, h, dim), keys 32c..32c+31 of this tile per box
-        for (int c = 0; c < 2; ++c)
-          tma_load_2d(st + KV_BYTES + c * KCHUNK, &tmV, &kv_full[s], j * KT + 32 * c,
-                      (b * p.heads + h) * HD);
+        if (BF) {
+          // 64 keys x 64 dims of k, and V^T rows (b, h, dim) over this tile's 64 keys
+          tma_load_2d(st, &tmKV, &kv_full[s], p.k_col + h * HD, krow0 + j * KT);
+          tma_load_2d(st + KV_BYTES, &tmV, &kv_full[s], j * KT, (b * p.heads + h) * HD);
+        } else {
+          for (int c = 0; c < 2; ++c)
+            tma_load_2d(st + c * KCHUNK, &tmKV, &kv_full[s], p.k_col + h * HD + 32 * c, krow0 + j * KT);
+          // V^T rows (b, h, dim), keys 32c..32c+31 of this tile per box
+          for (int c = 0; c < 2; ++c)
+            tma_load_2d(st + KV_BYTES + c * KCHUNK, &tmV, &kv_full[s], j * KT + 32 * c,
+                        (b * p.heads + h) * HD);
+        }
       }
     }
   } else if (warp == 1) {
     if (lane == 0) {
-      // S = Q K^T and O = P V: M=128, N=64; A from TMEM, B K-major in smem.
-      constexpr uint32_t idesc = (1u << 4) | (2u << 7) | (2u << 10) | ((64u >> 3) << 17) |
+      // S = Q K^T and O = P V: M=128, N=64; B K-major in smem; A from TMEM
+      // (tf32) or K-major in smem (bf16)
+      constexpr uint32_t ab = BF ? 1u : 2u;
+      constexpr uint32_t idesc = (1u << 4) | (ab << 7) | (ab << 10) | ((64u >> 3) << 17) |
                                  ((128u >> 4) << 24);
       bool ok = mbar_wait(q_full, 0, p.err, 12);
       asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
@@ -154,10 +192,18 @@ __global__ void __launch_bounds__(192, 2)
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
         const uint32_t k_addr = smem_u32(KVs + s * STAGE_BYTES);
         const uint32_t d = tmem + TM_S + (uint32_t)((j & 1) * 64);
+        if (BF) {
+          const uint32_t q_addr = smem_u32(Qs);
 #pragma unroll
-        for (int kk = 0; kk < 8; ++kk)
-          umma_tf32_ta(d, tmem + TM_Q + 8 * kk,
-                       umma_desc_k(k_addr + (kk / 4) * KCHUNK + (kk % 4) * 32, 128), idesc, kk != 0);
+          for (int kk = 0; kk < 4; ++kk)
+            umma_bf16(d, umma_desc_k(q_addr + kk * 32, 128), umma_desc_k(k_addr + kk * 32, 128), idesc,
+                      kk != 0);
+        } else {
+#pragma unroll
+          for (int kk = 0; kk < 8; ++kk)
+            umma_tf32_ta(d, tmem + TM_Q + 8 * kk,
+                         umma_desc_k(k_addr + (kk / 4) * KCHUNK + (kk % 4) * 32, 128), idesc, kk != 0);
+        }
         umma_commit(&s_full[j & 1]);
         return true;
       };
@@ -167,14 +213,23 @@ __global__ void __launch_bounds__(192, 2)
         if (!mbar_wait(&p_full[j & 1], (j >> 1) & 1, p.err, 14)) break;
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
         const uint32_t v_addr = smem_u32(KVs + (j % STAGES) * STAGE_BYTES) + KV_BYTES;
-        const uint32_t pa = tmem + TM_S + (uint32_t)((j & 1) * 64);
-        // K = 64 keys in steps of 8: V^T chunk kc holds keys 32kc..32kc+31,
-        // 32 bytes per step inside its 128-byte rows
+        if (BF) {
+          // K = 64 keys in steps of 16 across P's and V^T's 128-byte rows
+          const uint32_t p_addr = smem_u32(Ps + (j & 1) * L::P_BYTES);
 #pragma unroll
-        for (int kk = 0; kk < 8; ++kk)
-          umma_tf32_ta(tmem + TM_O, pa + 8 * kk,
-                       umma_desc_k(v_addr + (kk / 4) * KCHUNK + (kk % 4) * 32, 128), idesc,
-                       (j | kk) != 0);
+          for (int kk = 0; kk < 4; ++kk)
+            umma_bf16(tmem + TM_O, umma_desc_k(p_addr + kk * 32, 128),
+                      umma_desc_k(v_addr + kk * 32, 128), idesc, (j | kk) != 0);
+        } else {
+          const uint32_t pa = tmem + TM_S + (uint32_t)((j & 1) * 64);
+          // K = 64 keys in steps of 8: V^T chunk kc holds keys 32kc..32kc+31,
+          // 32 bytes per step inside its 128-byte rows
+#pragma unroll
+          for (int kk = 0; kk < 8; ++kk)
+            umma_tf32_ta(tmem + TM_O, pa + 8 * kk,
+                         umma_desc_k(v_addr + (kk / 4) * KCHUNK + (kk % 4) * 32, 128), idesc,
+                         (j | kk) != 0);
+        }
         umma_commit(&pv_done[j & 1]);
         umma_commit(&kv_empty[j % STAGES]);
       }
@@ -187,7 +242,7 @@ __global__ void __launch_bounds__(192, 2)
     const float kLog2e = 1.4426950408889634f;
     const float sl = p.scale * kLog2e;  // scores in log2 units
     const bool qvalid = q0 + r < p.nq;
-    {
+    if (!BF) {
       // this row of Q into TMEM columns [TM_Q, TM_Q + 64)
       float qv[64];
       const float* src = p.q + (int64_t)(b * p.nq + q0 + r) * p.ldq + p.q_col + h * HD;
@@ -260,18 +315,37 @@ __global__ void __launch_bounds__(192, 2)
       float2 rs4[4];
 #pragma unroll
       for (int i = 0; i < 4; ++i) rs4[i] = make_float2(0.f, 0.f);
+      if (BF) {
+        // P rounded to bf16 into row r of P buffer j%2 (128-byte rows, 16-byte
+        // chunk c at chunk c ^ (r % 8)); the row sum adds the rounded values
+        uint32_t pk[32];
 #pragma unroll
-      for (int i = 0; i < 32; ++i) {
-        const float2 t = __ffma2_rn(make_float2(sv[2 * i], sv[2 * i + 1]), sl2, nm2);
-        sv[2 * i] = trunc_tf32(ex2_approx(t.x));
-        sv[2 * i + 1] = trunc_tf32(ex2_approx(t.y));
-        rs4[i % 4] = __fadd2_rn(rs4[i % 4], make_float2(sv[2 * i], sv[2 * i + 1]));
+        for (int i = 0; i < 32; ++i) {
+          const float2 t = __ffma2_rn(make_float2(sv[2 * i], sv[2 * i + 1]), sl2, nm2);
+          const __nv_bfloat162 pb = __floats2bfloat162_rn(ex2_approx(t.x), ex2_approx(t.y));
+          pk[i] = *reinterpret_cast<const uint32_t*>(&pb);
+          rs4[i % 4] = __fadd2_rn(rs4[i % 4], __bfloat1622float2(pb));
+        }
+        unsigned char* prow = Ps + (j & 1) * L::P_BYTES + r * 128;
+#pragma unroll
+        for (int c = 0; c < 8; ++c)
+          *reinterpret_cast<uint4*>(prow + ((c ^ (r & 7)) << 4)) =
+              make_uint4(pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]);
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      } else {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const float2 t = __ffma2_rn(make_float2(sv[2 * i], sv[2 * i + 1]), sl2, nm2);
+          sv[2 * i] = trunc_tf32(ex2_approx(t.x));
+          sv[2 * i + 1] = trunc_tf32(ex2_approx(t.y));
+          rs4[i % 4] = __fadd2_rn(rs4[i % 4], make_float2(sv[2 * i], sv[2 * i + 1]));
+        }
+        tmem_st32(sb, sv);
+        tmem_st32(sb + 32, sv + 32);
+        tmem_st_wait();
       }
       rs4[0] = __fadd2_rn(__fadd2_rn(rs4[0], rs4[1]), __fadd2_rn(rs4[2], rs4[3]));
       l += rs4[0].x + rs4[0].y;
-      tmem_st32(sb, sv);
-      tmem_st32(sb + 32, sv + 32);
-      tmem_st_wait();
       asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
       asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(&p_full[j & 1]))
                    : "memory");
@@ -318,27 +392,42 @@ __global__ void __launch_bounds__(192, 2)
 
 // q (rows, ldq) with head h at column q_col + 64h; k / v in `kv` (rows, ldkv)
 // at k_col / v_col + 64h; out (rows, ldo). nk must be a multiple of 64.
+// bf16_in: q, kv and vt hold bf16 values (the kind::f16 variant).
 bool launch_attention_tc(const float* q, int ldq, int q_col, const float* kv, int ldkv, int k_col,
                          int v_col, const float* vt, float* out, int ldo, int B, int heads, int nq,
-                         int nk, float scale, int* err, cudaStream_t s, uint16_t* out16) {
+                         int nk, float scale, int* err, cudaStream_t s, uint16_t* out16,
+                         bool bf16_in) {
   if (nk % KT != 0 || ldq % 4 || (q_col % 4) || (ldkv * 4) % 16 || ldkv % 32) return false;
   if (out16 && ((reinterpret_cast<uintptr_t>(out16) & 15) || ldo % 8)) return false;
   if ((reinterpret_cast<uintptr_t>(q) & 15) || (reinterpret_cast<uintptr_t>(kv) & 15) ||
       (reinterpret_cast<uintptr_t>(vt) & 15) || heads * HD > 4096)
     return false;
-  CUtensorMap mkv;
+  const int esz = bf16_in ? 2 : 4;
+  const CUtensorMapDataType dt = bf16_in ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
+  // boxes of 64 rows x 128 bytes: 32 fp32 or 64 bf16 columns
+  const cuuint32_t bw = bf16_in ? 64 : 32;
+  CUtensorMap mkv, mv, mq;
   {
     const cuuint64_t dims[2] = {(cuuint64_t)ldkv, (cuuint64_t)B * nk};
-    const cuuint64_t str[1] = {(cuuint64_t)ldkv * 4};
-    const cuuint32_t box[2] = {32, KT};
-    if (!make_tensor_map(&mkv, kv, 2, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B)) return false;
+    const cuuint64_t str[1] = {(cuuint64_t)ldkv * esz};
+    const cuuint32_t box[2] = {bw, KT};
+    if (!make_tensor_map(&mkv, kv, 2, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B, nullptr, dt))
+      return false;
   }
-  CUtensorMap mv;
   {
     const cuuint64_t dims[2] = {(cuuint64_t)nk, (cuuint64_t)B * heads * HD};
-    const cuuint64_t str[1] = {(cuuint64_t)nk * 4};
-    const cuuint32_t box[2] = {32, HD};
-    if (!make_tensor_map(&mv, vt, 2, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B)) return false;
+    const cuuint64_t str[1] = {(cuuint64_t)nk * esz};
+    const cuuint32_t box[2] = {bw, HD};
+    if (!make_tensor_map(&mv, vt, 2, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B, nullptr, dt))
+      return false;
+  }
+  mq = mkv;
+  if (bf16_in) {
+    const cuuint64_t dims[2] = {(cuuint64_t)ldq, (cuuint64_t)B * nq};
+    const cuuint64_t str[1] = {(cuuint64_t)ldq * 2};
+    const cuuint32_t box[2] = {64, 64};
+    if (!make_tensor_map(&mq, q, 2, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B, nullptr, dt))
+      return false;
   }
   AttnParams p;
   p.q = q;
@@ -355,10 +444,17 @@ bool launch_attention_tc(const float* q, int ldq, int q_col, const float* kv, in
   p.scale = scale;
   p.err = err;
   static PerDevice attr;
-  if (attr.first())
-    cudaFuncSetAttribute(attention_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         SMEM_BYTES);
-  attention_tc_kernel<<<dim3((nq + QT - 1) / QT, heads, B), 192, SMEM_BYTES, s>>>(mkv, mv, p);
+  if (attr.first()) {
+    cudaFuncSetAttribute(attention_tc_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         AttnSmem<false>::TOTAL);
+    cudaFuncSetAttribute(attention_tc_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         AttnSmem<true>::TOTAL);
+  }
+  const dim3 grid((nq + QT - 1) / QT, heads, B);
+  if (bf16_in)
+    attention_tc_kernel<true><<<grid, 192, AttnSmem<true>::TOTAL, s>>>(mkv, mv, mq, p);
+  else
+    attention_tc_kernel<false><<<grid, 192, AttnSmem<false>::TOTAL, s>>>(mkv, mv, mq, p);
   return true;
 }
 

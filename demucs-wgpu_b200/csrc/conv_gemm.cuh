@@ -72,6 +72,7 @@ struct ConvParams {
   // 64-wide head, vt[((b*heads + h)*64 + d)*vt_ntok + token] (attention's V^T)
   float* vt_out;
   int vt_col0, vt_ntok;
+  int vt16;  // vt_out holds bf16 values (the tensor-core kernel only)
   // o_lim > 0: output position x (along W) holds groups of o_lim_ch columns
   // for positions 4x, 4x+1, ...; columns of positions >= o_lim are not stored
   int o_lim, o_lim_ch;

@@ -163,6 +163,7 @@ bool dmx_handle::build_tc(const ConvParams& p, const Packed& pk, TcOperandA& a, 
   t.vt_out = p.vt_out;
   t.vt_col0 = p.vt_col0;
   t.vt_ntok = p.vt_ntok;
+  t.vt16 = p.vt16;
   t.o_lim = p.o_lim;
   t.o_lim_ch = p.o_lim_ch;
   t.a_rounded = p.a_rounded;
@@ -462,7 +463,7 @@ uint16_t* u16(float* p) { return reinterpret_cast<uint16_t*>(p); }
 void xf_gemm(dmx_handle* h, const char* tag, const Packed& pk, const float* in, int B, int n,
              float* out, int epi, const float* res = nullptr, const float* gamma = nullptr,
              double* stats = nullptr, bool round_out = false, float* vt = nullptr,
-             int vt_col0 = 0, bool out_bf16 = false) {
+             int vt_col0 = 0, bool out_bf16 = false, bool vt16 = false) {
   ConvParams p = base_params(pk, h->wdev);
   p.round_out = round_out;
   p.a_rounded = xf_rounded(h);
@@ -471,6 +472,7 @@ void xf_gemm(dmx_handle* h, const char* tag, const Packed& pk, const float* in, 
   p.vt_out = vt;
   p.vt_col0 = vt_col0;
   p.vt_ntok = n;
+  p.vt16 = vt16 ? 1 : 0;
   const int cin = pk.K;
   set_input(p, in, B, 1, n, cin);
   set_output(p, out, B, 1, n, pk.N);
@@ -504,12 +506,14 @@ void xf_self(dmx_handle* h, const LayerW& L, float* X, int B, int n, const XfBuf
                                    h->stream, xf_rounded(h), xf_bf16(h) ? u16(bb.xn) : nullptr);
   ++h->launches;
   const bool tc_attn = tc_attention(h);
-  xf_gemm(h, "xf.qkv", L.qkv, bb.xn, B, n, bb.qkv, EPI_STORE, nullptr, nullptr, nullptr, tc_attn,
-          tc_attn ? bb.vt1 : nullptr, 1024);
-  h->mark("xf.attention", 4.0 * B * n * n * 512, 4.0 * B * n * 512 * 4);
+  const bool bfa = tc_attn && xf_bf16(h);  // q, k, v and V^T stored as bf16 for kind::f16
+  xf_gemm(h, "xf.qkv", L.qkv, bb.xn, B, n, bb.qkv, EPI_STORE, nullptr, nullptr, nullptr,
+          tc_attn && !bfa, tc_attn ? bb.vt1 : nullptr, 1024, bfa, bfa);
+  h->mark("xf.attention", 4.0 * B * n * n * 512, (bfa ? 2.0 : 4.0) * B * n * 512 * 4);
   if (h->live() && !(tc_attn && launch_attention_tc(bb.qkv, 1536, 0, bb.qkv, 1536, 512, 1024, bb.vt1,
                                                      bb.att, 512, B, 8, n, n, 0.125f, h->err,
-                                                     h->stream, xf_bf16(h) ? u16(bb.att) : nullptr))) {
+                                                     h->stream, xf_bf16(h) ? u16(bb.att) : nullptr,
+                                                     bfa))) {
     if (xf_bf16(h)) throw Error(DMX_ERR_INVALID, "attention: the bf16 output needs the tensor-core kernel");
     launch_flash_attention(bb.qkv, 1536, bb.qkv + 512, bb.qkv + 1024, 1536, bb.att, 512, B, 8, n, n,
                            0.125f, h->stream);
@@ -527,8 +531,9 @@ void xf_cross_kv(dmx_handle* h, const LayerW& L, const float* other, int B, int 
                       scratch, h->stream, xf_rounded(h), xf_bf16(h) ? u16(scratch) : nullptr);
   ++h->launches;
   const bool tc_attn = tc_attention(h);
+  const bool bfa = tc_attn && xf_bf16(h);
   xf_gemm(h, "xf.kv", L.kv, scratch, B, n_other, kv_out, EPI_STORE, nullptr, nullptr, nullptr,
-          tc_attn, tc_attn ? vt : nullptr, 512);
+          tc_attn && !bfa, tc_attn ? vt : nullptr, 512, bfa, bfa);
 }
 
 void xf_cross(dmx_handle* h, const LayerW& L, float* X, int B, int n, const float* kv,
@@ -538,11 +543,15 @@ void xf_cross(dmx_handle* h, const LayerW& L, float* X, int B, int n, const floa
                                    h->stream, xf_rounded(h), xf_bf16(h) ? u16(bb.xn) : nullptr);
   ++h->launches;
   const bool tc_attn = tc_attention(h);
-  xf_gemm(h, "xf.q", L.q, bb.xn, B, n, bb.qkv, EPI_STORE, nullptr, nullptr, nullptr, tc_attn);
-  h->mark("xf.attention", 4.0 * B * n * n_other * 512, 4.0 * B * (2.0 * n + 2.0 * n_other) * 512);
+  const bool bfa = tc_attn && xf_bf16(h);
+  xf_gemm(h, "xf.q", L.q, bb.xn, B, n, bb.qkv, EPI_STORE, nullptr, nullptr, nullptr,
+          tc_attn && !bfa, nullptr, 0, bfa);
+  h->mark("xf.attention", 4.0 * B * n * n_other * 512,
+          (bfa ? 2.0 : 4.0) * B * (2.0 * n + 2.0 * n_other) * 512);
   if (h->live() && !(tc_attn && launch_attention_tc(bb.qkv, 512, 0, kv, 1024, 0, 512, vt, bb.att,
                                                      512, B, 8, n, n_other, 0.125f, h->err,
-                                                     h->stream, xf_bf16(h) ? u16(bb.att) : nullptr))) {
+                                                     h->stream, xf_bf16(h) ? u16(bb.att) : nullptr,
+                                                     bfa))) {
     if (xf_bf16(h)) throw Error(DMX_ERR_INVALID, "attention: the bf16 output needs the tensor-core kernel");
     launch_flash_attention(bb.qkv, 512, kv, kv + 512, 1024, bb.att, 512, B, 8, n, n_other, 0.125f,
                            h->stream);

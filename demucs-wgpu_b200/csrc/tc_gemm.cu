@@ -452,9 +452,16 @@ __global__ void __launch_bounds__(kThreads, 1)
               // whole 32-column chunks belong to one head (vt_col0 and 64 are multiples of 32)
               const int c = nb - p.vt_col0, h2 = c / 64, d0 = c % 64;
               const int64_t bb = pos / p.vt_ntok, tok = pos % p.vt_ntok;
-              float* vt = p.vt_out + ((bb * 8 + h2) * 64 + d0) * (int64_t)p.vt_ntok + tok;
-              for (int j = 0; j < 32; ++j)
-                if (nb + j < ncol) vt[(int64_t)j * p.vt_ntok] = v[j];
+              const int64_t at = ((bb * 8 + h2) * 64 + d0) * (int64_t)p.vt_ntok + tok;
+              if (p.vt16) {
+                uint16_t* vt = reinterpret_cast<uint16_t*>(p.vt_out) + at;
+                for (int j = 0; j < 32; ++j)
+                  if (nb + j < ncol) vt[(int64_t)j * p.vt_ntok] = (uint16_t)(pack_bf16(v[j], 0.f) & 0xFFFFu);
+              } else {
+                float* vt = p.vt_out + at;
+                for (int j = 0; j < 32; ++j)
+                  if (nb + j < ncol) vt[(int64_t)j * p.vt_ntok] = v[j];
+              }
             }
             if (p.out16) {
               // bf16 output (the A operand of a bf16 GEMM): 32 values in 64 bytes
@@ -710,7 +717,8 @@ bool tc_gemm_supported(const TcOperandA& a, const TcParams& p) {
   if (p.bf16 && (p.mode != TC_ROWS || bk != 32 || p.Kpad % 32 != 0 || p.a_stats ||
                  (a.sw * 2) % 16 != 0))
     return false;
-  if (p.out16 && (!p.bf16 || p.vt_out || p.o_pcols || p.o_lim || p.epi_add || p.round_out))
+  if (p.out16 && (!p.bf16 || (p.vt_out && !p.vt16) || p.o_pcols || p.o_lim || p.epi_add ||
+                  p.round_out))
     return false;
   if (p.mode == TC_2D || p.mode == TC_1D) {
     if (a.C != p.Cin) return false;

@@ -47,6 +47,7 @@ struct TcParams {
   int round_out;  // round stored values to nearest tf32 (the output feeds only tf32 GEMMs)
   float* vt_out;  // EPI_STORE: V^T copy of columns >= vt_col0 (see ConvParams)
   int vt_col0, vt_ntok;
+  int vt16;       // vt_out holds bf16 values (the bf16 attention's V^T)
   int o_lim, o_lim_ch;  // as in ConvParams
   int a_rounded;  // A holds tf32-rounded values: the MMA reads the TMA tile as landed
   int bf16;       // kind::f16: A is a bf16 activation matrix (TC_ROWS), wk the bf16 weight copy
@@ -95,8 +96,11 @@ void launch_tc_gemm(const TcOperandA& a, const float* wk, const float* wk_lo, co
 // is not supported (the caller then uses the SIMT kernel).
 // vt: V^T as (segment, head, dim, key), written by the projection epilogue.
 // out16: store the output as bf16 there instead of `out` (row pitch ldo elements).
+// bf16_in: q, kv and vt hold bf16 values (pitches still in elements); both
+// products then run on kind::f16.
 bool launch_attention_tc(const float* q, int ldq, int q_col, const float* kv, int ldkv, int k_col,
                          int v_col, const float* vt, float* out, int ldo, int B, int heads, int nq,
-                         int nk, float scale, int* err, cudaStream_t s, uint16_t* out16 = nullptr);
+                         int nk, float scale, int* err, cudaStream_t s, uint16_t* out16 = nullptr,
+                         bool bf16_in = false);
 
 }  // namespace dmx

@@ -42,7 +42,8 @@ enum {
  *       (bf16 activations stored by their producers — LayerNorm, the FFN's
  *       GELU, attention — and bf16 weight copies) and fp32 accumulate;
  *       the DConv branches' contractions single-pass tf32 (TF32 and TF32X3
- *       split them); convolutions and attention as in TF32. */
+ *       split them); attention on kind::f16 with bf16 q, k, V^T and P;
+ *       convolutions as in TF32. */
 typedef enum { DMX_FP32 = 0, DMX_TF32 = 1, DMX_BF16 = 2, DMX_TF32X3 = 3 } dmx_precision;
 
 typedef struct {
