@@ -93,9 +93,8 @@ void launch_conv_gemm(const ConvParams& p, int pro, int epi, cudaStream_t stream
 int conv_gemm_stat_slots(int N);
 // The first encoder convolutions (Cin 2/4, 8 taps, 48 GELU outputs, normalised
 // input, dense channels-last output; first_conv.cu). w_host: [K][48] weights
-// then the 48 biases, in host memory. fast_gelu: GELU on the A&S erf (the
-// tensor-core builds), else on erff (the SIMT fp32 build). False: not that shape.
+// then the 48 biases, in host memory. False: not that shape.
 bool launch_first_conv(const ConvParams& p, int pro, int epi, const float* w_host,
-                       cudaStream_t stream, bool fast_gelu = false);
+                       cudaStream_t stream);
 
 }  // namespace dmx

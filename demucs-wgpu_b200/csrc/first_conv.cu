@@ -37,7 +37,7 @@ DMX_DEVICE void accumulate(const FirstConvW<CIN>& cw, const float* in, float* ac
     for (int j = 0; j < 24; ++j) acc[j] = fmaf(in[k], cw.w[k][24 * H + j], acc[j]);
 }
 
-template <int CIN, bool FAST>
+template <int CIN>
 __global__ void __launch_bounds__(256) first_conv_kernel(const ConvParams p,
                                                          const __grid_constant__ FirstConvW<CIN> cw) {
   constexpr int K = 8 * CIN;
@@ -76,11 +76,10 @@ __global__ void __launch_bounds__(256) first_conv_kernel(const ConvParams p,
   else
     accumulate<CIN, 1>(cw, in, acc);
   float4* orow = reinterpret_cast<float4*>(&os[pl * kRow + 24 * half]);
-  auto act = [](float v) { return FAST ? gelu_tc(v) : gelu(v); };
 #pragma unroll
   for (int c = 0; c < 6; ++c)
-    orow[c] = make_float4(act(acc[4 * c]), act(acc[4 * c + 1]), act(acc[4 * c + 2]),
-                          act(acc[4 * c + 3]));
+    orow[c] = make_float4(gelu(acc[4 * c]), gelu(acc[4 * c + 1]), gelu(acc[4 * c + 2]),
+                          gelu(acc[4 * c + 3]));
   __syncthreads();
   // the tile's positions are consecutive rows of the channels-last output
   const int rows = M - m0 < kBM ? (int)(M - m0) : kBM;
@@ -92,21 +91,17 @@ __global__ void __launch_bounds__(256) first_conv_kernel(const ConvParams p,
 }
 
 template <int CIN>
-void launch_cin(const ConvParams& p, const float* w_host, unsigned grid, cudaStream_t s, bool fast) {
+void launch_cin(const ConvParams& p, const float* w_host, unsigned grid, cudaStream_t s) {
   FirstConvW<CIN> cw;
   for (int k = 0; k < 8 * CIN; ++k)
     for (int n = 0; n < kCo; ++n) cw.w[k][n] = w_host[k * kCo + n];
   for (int n = 0; n < kCo; ++n) cw.b[n] = w_host[8 * CIN * kCo + n];
-  if (fast)
-    first_conv_kernel<CIN, true><<<grid, 256, 0, s>>>(p, cw);
-  else
-    first_conv_kernel<CIN, false><<<grid, 256, 0, s>>>(p, cw);
+  first_conv_kernel<CIN><<<grid, 256, 0, s>>>(p, cw);
 }
 
 }  // namespace
 
-bool launch_first_conv(const ConvParams& p, int pro, int epi, const float* w_host, cudaStream_t s,
-                       bool fast_gelu) {
+bool launch_first_conv(const ConvParams& p, int pro, int epi, const float* w_host, cudaStream_t s) {
   if (pro != PRO_BATCH_AFFINE || epi != EPI_GELU || (p.Cin != 2 && p.Cin != 4) || p.ntaps != 8 ||
       p.K != 8 * p.Cin || p.N != kCo || p.Npad < kCo || p.epi_add || p.round_out || p.o_lim ||
       p.o_off != 0 || p.o_xs != kCo || p.o_ys != (int64_t)p.Wq * kCo ||
@@ -115,9 +110,9 @@ bool launch_first_conv(const ConvParams& p, int pro, int epi, const float* w_hos
   const int64_t M = (int64_t)p.B * p.Hq * p.Wq;
   const unsigned grid = (unsigned)((M + kBM - 1) / kBM);
   if (p.Cin == 4)
-    launch_cin<4>(p, w_host, grid, s, fast_gelu);
+    launch_cin<4>(p, w_host, grid, s);
   else
-    launch_cin<2>(p, w_host, grid, s, fast_gelu);
+    launch_cin<2>(p, w_host, grid, s);
   return true;
 }
 

@@ -42,8 +42,7 @@ void dmx_handle::gemm(const ConvParams& p0, int pro, int epi, const char* tag,
     return;
   if (p.a_bf16 || p.out16)
     throw Error(DMX_ERR_INVALID, std::string(tag) + ": bf16 operands need the tensor-core kernel");
-  if (pk && !pk->host_w.empty() &&
-      launch_first_conv(p, pro, epi, pk->host_w.data(), stream, cfg.precision != DMX_FP32))
+  if (pk && !pk->host_w.empty() && launch_first_conv(p, pro, epi, pk->host_w.data(), stream))
     return;
   launch_conv_gemm(p, pro, epi, stream);
 }
