@@ -41,12 +41,14 @@ SEGMENT = synth.SEGMENT_SAMPLES
 SEGMENT_GFLOP = 334.9  # algorithmic FLOPs of one segment forward (2*MAC over the layer table)
 METRIC = "audio-sec separated/sec (htdemucs)"
 UNIT = "audio-s/s"
-# Measured DRAM bytes (read + write) per algorithmic byte for a kernel tag, from
-# one ncu capture of that kernel (profiles/): roofline.traffic = ratio x the
-# tag's algorithmic bytes per launch. The attention capture is the layer-0
-# spectral self-attention on a 3-chunk track (50.4 MB of DRAM traffic for
-# 66.1 MB of q, k, v, o); traffic scales with the chunks a launch processes.
-TRAFFIC_RATIO = {"xf.attention": 50.393 / 66.060}
+# Measured DRAM bytes (read + write) per algorithmic byte for a kernel tag and
+# build, from one ncu capture of that kernel (profiles/): roofline.traffic =
+# ratio x the tag's algorithmic bytes per launch. The attention captures are the
+# layer-0 spectral self-attention on a 3-chunk track: tf32, 50.4 MB of DRAM
+# traffic for 66.1 MB of q, k, v, o; bf16, 24.8 MB for 33.0 MB. Traffic scales
+# with the chunks a launch processes.
+TRAFFIC_RATIO = {("xf.attention", "TF32"): 50.393 / 66.060,
+                 ("xf.attention", "BF16"): 24.810 / 33.030}
 
 
 def workload(seconds):
@@ -97,7 +99,7 @@ def _peaks():
         return 6650.0, 1590.0, 1400.0, "fallback"
 
 
-def roofline(stages):
+def roofline(stages, precision):
     """Roofline of the dominant kernel tag (most device time in the step).
 
     ``stages``: {tag: (ms, launches, flops, bytes)} from the runtime's
@@ -120,7 +122,7 @@ def roofline(stages):
                          "dense ratio), not itself measured"}
     else:
         bound, achieved, peak, unit = "hbm", nbytes / s / 1e9, hbm, "GB/s"
-    ratio = TRAFFIC_RATIO.get(tag)
+    ratio = TRAFFIC_RATIO.get((tag, precision))
     traffic = round(ratio * nbytes / max(launches, 1)) if ratio else None
     out = {"bound": bound, "achieved": round(achieved, 3), "peak": peak, "unit": unit,
            "frac": round(achieved / peak, 5), "traffic": traffic,
@@ -543,7 +545,7 @@ def run_ours(args, rank, world, local_rank):
                     "chunks_per_forward": e2e_batch, "api": e2e_api},
             "gpu_launches": int(launches) * args.steps,
             "clocks": clocks.summary(),
-            "roofline": roofline(stages),
+            "roofline": roofline(stages, args.precision),
             "whole_forward": {"achieved": round(whole, 3), "unit": "TFLOP/s",
                               "frac_of_bf16_sustained": round(whole / bf16_sustained, 5),
                               "note": "334.9 GFLOP per segment over the whole step, rank 0's chunks"},
