@@ -9,7 +9,8 @@
 //       [--dump-trace DIR]
 //   dmx bench -m CHECKPOINT [--repeats N] [--device cuda[:N]] [--precision P]
 //   dmx profile INPUT.wav -m CHECKPOINT [--repeats N] [--device ...] [--precision P]
-//   dmx wav-copy IN.wav OUT.wav [--stereo]   decode a WAV, write it as float32
+//   dmx wav-copy IN.wav OUT.wav [--stereo] [--window N]   decode a WAV (whole, or in
+//       windows of N frames as separate reads it), write it as float32
 //
 // OUT is a directory (one <stem>.wav per source, float32) or, for a single stem
 // or --stem, a file path. WAV input: PCM 16 / 24 / 32-bit, IEEE float 32 / 64-bit and the
@@ -270,7 +271,7 @@ struct Args {
   std::vector<std::string> pos;
   std::string output, model, stem, two_stems, other_method = "add", device = "cuda",
                                                      precision = "tf32", dump_trace;
-  int shifts = 1, batch = 0, repeats = 3;
+  int shifts = 1, batch = 0, repeats = 3, window = 0;
   double overlap = 0.25, segment = 0.0;
   bool timings = false, stereo = false;
 };
@@ -298,6 +299,7 @@ Args parse(int argc, char** argv, int from) {
     else if (k == "--dump-trace") a.dump_trace = val();
     else if (k == "--timings") a.timings = true;
     else if (k == "--stereo") a.stereo = true;
+    else if (k == "--window") a.window = std::atoi(val().c_str());
     else if (!k.empty() && k[0] == '-') throw Fail("unknown option " + k);
     else a.pos.push_back(k);
   }
@@ -627,8 +629,34 @@ int cmd_profile(const Args& a) {
   return 0;
 }
 
+// wav-copy: decode and write back as float32. With --window N the input is
+// read through WavSource in windows of N frames (with --stereo: the two
+// channels separate's read callback hands to the library), the path separate
+// uses, instead of whole.
 int cmd_wav_copy(const Args& a) {
-  if (a.pos.size() != 2) throw Fail("usage: dmx wav-copy IN.wav OUT.wav [--stereo]");
+  if (a.pos.size() != 2) throw Fail("usage: dmx wav-copy IN.wav OUT.wav [--stereo] [--window N]");
+  if (a.window > 0) {
+    WavSource src(a.pos[0]);
+    const int ch = a.stereo ? 2 : src.channels;
+    if (a.stereo && src.channels > 2) throw Fail(a.pos[0] + ": more than two channels");
+    WavWriter w(a.pos[1], src.rate, ch);
+    std::vector<float> cols((size_t)a.window * ch), inter((size_t)a.window * ch);
+    for (int64_t t0 = 0; t0 < src.frames; t0 += a.window) {
+      const int64_t count = std::min<int64_t>(a.window, src.frames - t0);
+      std::vector<float*> out(ch);
+      for (int c = 0; c < ch; ++c) out[c] = cols.data() + (size_t)c * count;
+      if (a.stereo)
+        src.read_stereo(t0, count, out[0], out[1]);
+      else
+        src.read(t0, count, out.data());
+      for (int64_t t = 0; t < count; ++t)
+        for (int c = 0; c < ch; ++c) inter[(size_t)t * ch + c] = out[c][t];
+      w.write(inter.data(), count);
+    }
+    w.close();
+    std::printf("%d Hz, %d channels, %lld frames\n", src.rate, ch, (long long)src.frames);
+    return 0;
+  }
   Audio in = read_wav(a.pos[0]);
   if (a.stereo) ensure_stereo(in, a.pos[0]);
   WavWriter w(a.pos[1], in.rate, in.channels);

@@ -153,3 +153,21 @@ def test_usage_errors():
     r = subprocess.run([dmx.cli_path(), "separate", "x.wav", "-m", "m", "--stem", "drums",
                         "--two-stems", "bass", "-o", "out"], capture_output=True, text=True, timeout=60)
     assert r.returncode == 1 and "exclude" in r.stderr
+
+
+@pytest.mark.parametrize("window", [1, 7, 1000, 1 << 20])
+@pytest.mark.parametrize("tag,bits,channels", [(1, 16, 2), (1, 24, 1), (3, 64, 2), (0xFFFE, 32, 1)])
+def test_windowed_reads_match_the_whole_file(tmp_path, window, tag, bits, channels):
+    # separate reads the input through the same source in windows of a forward's chunks
+    rng = np.random.default_rng(bits + channels)
+    n = 2501
+    if tag == 1:
+        raw = rng.integers(-(1 << (bits - 1)), 1 << (bits - 1), size=n * channels)
+        payload = b"".join(int(v).to_bytes(bits // 8, "little", signed=True) for v in raw)
+    else:
+        payload = (rng.standard_normal(n * channels) * 0.3).astype("<f8" if bits == 64 else "<f4").tobytes()
+    wav = build_wav(tag, channels, 44100, bits, payload)
+    whole, _ = copy(tmp_path, wav, "--stereo")
+    windowed, _ = copy(tmp_path, wav, "--stereo", "--window", str(window))
+    assert windowed[1] == 2 and whole[1] == 2
+    np.testing.assert_array_equal(windowed[2], whole[2])
