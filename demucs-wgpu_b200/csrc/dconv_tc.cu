@@ -100,6 +100,45 @@ struct DcTc {
   static constexpr bool chunk_used(int c) { return (c % 2) * 4 < JA; }
 };
 
+// C = 192 (hidden 24), single-pass tf32 only (dconv_tc_wide_kernel): conv1's
+// three taps come from three x tiles loaded at frame offsets -d, 0, +d into
+// one accumulator of 32 columns (the hidden channels, zero-padded), so no
+// tap exchange is needed; g lives in TMEM as conv2's A operand, 32 K slots
+// (hidden channel h at slot h, the constant 1 that carries the bias at slot
+// 31). Shared memory: the x ring, conv1's weights (3 taps x 6 K blocks of
+// 32 x 32) and conv2's (384 x 32), all with 128-byte rows.
+template <>
+struct DcTc<192> {
+  static constexpr int C = 192;
+  static constexpr int HID = C / 8;
+  static constexpr int ACT = HID + 1;
+  static constexpr int NQ = ACT * (ACT + 1) / 2;
+  static constexpr int YS = (HID + 3) / 4 * 4;
+  static constexpr int KS = 32;        // conv1 N per block = conv2 K slots
+  static constexpr int BIAS = KS - 1;  // the K slot of conv2's bias
+  static constexpr int BK = 32;        // conv1 K (channels) per x tile
+  static constexpr int KB = C / BK;
+  static constexpr int NCH = 96;       // conv2 columns per MMA (48 channels)
+  static constexpr int NCHUNK = 2 * C / NCH;
+  static constexpr int NB2 = 3;        // conv2 accumulators in TMEM
+  static constexpr int A_BYTES = 128 * BK * 4;
+  static constexpr int STAGES = 5;
+  static constexpr int W1_TILE = KS * BK * 4;        // one tap, one K block
+  static constexpr int W1_BYTES = 3 * KB * W1_TILE;  // [tap][kb][32 rows][32]
+  static constexpr int W2_BYTES = 2 * C * KS * 4;    // [2C rows][32 slots]
+  static constexpr int OFF_W1 = STAGES * A_BYTES;
+  static constexpr int OFF_W2 = OFF_W1 + W1_BYTES;
+  static constexpr int OFF_CH = OFF_W2 + W2_BYTES;  // per-channel constants [C][8]
+  static constexpr int OFF_AFF = OFF_CH + C * 32;   // per-item GN2 affine [C] float4
+  static constexpr int SMEM = OFF_AFF + C * 16 + 1024;
+  // TMEM columns: conv1 of block m at 32 m, g of block m at 96 + 32 m, the
+  // conv2 accumulators at 192 + 96 j
+  static constexpr uint32_t TM_D1 = 0, TM_G = 96, TM_D2 = 192;
+  static_assert(TM_D2 + NB2 * NCH <= 512 && HID < BIAS && 2 * C % NCH == 0, "tmem");
+  // dynamic shared memory plus the kernel's static barriers within 227 KB
+  static_assert(SMEM <= 227 * 1024 - 1024, "smem");
+};
+
 // Per-layer constants, passed by value (they sit in the constant bank): the
 // moments of z as functions of g (v and M above, over the active K slots in
 // act_slot order) and GroupNorm1's per-channel terms with conv1's bias.
@@ -756,6 +795,413 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
+// DConv of a C = 192 layer on the tensor cores, single-pass tf32 (the BF16
+// build). Same work items, modes, moments and output arithmetic as
+// dconv_tc_row_kernel; what differs is the width:
+//  * conv1: per 128-frame block m, tap t and 32-channel K block kb, warp 0
+//    loads the x tile at frames ts + 128 m + (t - 1) d (TMA zero-fills
+//    frames outside the row) and warp 1 accumulates it against tap t's
+//    weights into the block's 32 TMEM columns; the three loads of a tile
+//    run back to back, so the second and third come from L2.
+//  * the epilogue warps read y straight out of TMEM (no tap exchange), write
+//    g into TMEM as conv2's A operand (with the constant 1 at slot 31), and
+//    conv2 runs in 96-column chunks (48 channels) through three TMEM
+//    accumulators, overlapping the output of the chunk before.
+template <int C>
+__global__ void __launch_bounds__(kThreads, 1)
+    dconv_tc_wide_kernel(const __grid_constant__ CUtensorMap tmX,
+                         const __grid_constant__ CUtensorMap tmW1,
+                         const __grid_constant__ CUtensorMap tmW2, const DConvArgs a,
+                         const __grid_constant__ DcConst<C> k, int mode) {
+  using S = DcTc<C>;
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  unsigned char* smem = reinterpret_cast<unsigned char*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  __shared__ __align__(8) uint64_t full[S::STAGES], empty[S::STAGES];
+  __shared__ __align__(8) uint64_t w1_full, w2_full, d1_full, d1_empty, g_ready;
+  __shared__ __align__(8) uint64_t d2_full[S::NB2], d2_empty[S::NB2];
+  __shared__ uint32_t tmem_slot;
+  __shared__ double red[2 * kEpiWarps];
+
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  if (a.err && *reinterpret_cast<volatile int*>(a.err) != 0) return;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S::STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(&w1_full, 1);
+    mbar_init(&w2_full, 1);
+    mbar_init(&d1_full, 1);
+    mbar_init(&d1_empty, kEpiThreads);
+    mbar_init(&g_ready, kEpiThreads);
+    for (int j = 0; j < S::NB2; ++j) {
+      mbar_init(&d2_full[j], 1);
+      mbar_init(&d2_empty[j], kEpiThreads);
+    }
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_u32(&tmem_slot)),
+                 "r"(512));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+  const uint32_t tmem = tmem_slot;
+  const int T = a.T;
+  const int items = a.rows * a.tiles;
+  const bool conv1 = mode == DC_ROW || mode == DC_STATS1;
+  const bool conv2 = mode == DC_ROW || mode == DC_OUT;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---------------- TMA producer ----------------
+      if (conv2) {
+        mbar_expect_tx(&w2_full, S::W2_BYTES);
+        for (int h = 0; h < 2; ++h)
+          tma_load_2d(smem + S::OFF_W2 + h * C * 128, &tmW2, &w2_full, 0, h * C);
+      }
+      if (conv1) {
+        mbar_expect_tx(&w1_full, S::W1_BYTES);
+        for (int tap = 0; tap < 3; ++tap)
+          for (int kb = 0; kb < S::KB; ++kb)
+            tma_load_2d(smem + S::OFF_W1 + (tap * S::KB + kb) * S::W1_TILE, &tmW1, &w1_full,
+                        tap * C + kb * S::BK, 0);
+        uint32_t it = 0;
+        bool ok = true;
+        for (int w = blockIdx.x; w < items && ok; w += gridDim.x) {
+          const int row = w / a.tiles, ts = (w - row * a.tiles) * kTileStride - 2;
+          for (int m = 0; m < 3 && ok; ++m)
+            for (int kb = 0; kb < S::KB && ok; ++kb)
+              for (int tap = 0; tap < 3; ++tap, ++it) {
+                const int s = it % S::STAGES;
+                if (!mbar_wait(&empty[s], ((it / S::STAGES) & 1) ^ 1, a.err, 51)) {
+                  ok = false;
+                  break;
+                }
+                mbar_expect_tx(&full[s], S::A_BYTES);
+                // frames ts + 128 m + (tap - 1) d .. +127 (zero outside the row)
+                tma_load_3d(smem + s * S::A_BYTES, &tmX, &full[s], kb * S::BK,
+                            ts + m * 128 + (tap - 1) * a.dil, row);
+              }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ---------------- MMA issuer ----------------
+      constexpr uint32_t idesc1 = idesc_tf32(128, S::KS);
+      constexpr uint32_t idesc2 = idesc_tf32(128, S::NCH);
+      bool ok = (!conv1 || mbar_wait(&w1_full, 0, a.err, 52)) &&
+                (!conv2 || mbar_wait(&w2_full, 0, a.err, 53));
+      uint32_t it = 0, u = 0;
+      // conv2 of item `pend` (-1: none) is issued once its g is in TMEM
+      int pend = -1, cur = 0;
+      bool g_in = false;
+      auto conv2_progress = [&](bool block) {
+        if (pend < 0 || !ok) return;
+        if (!g_in) {
+          if (block) {
+            if (!mbar_wait(&g_ready, pend & 1, a.err, 54)) {
+              ok = false;
+              return;
+            }
+          } else if (!mbar_test(&g_ready, pend & 1)) {
+            return;
+          }
+          g_in = true;
+          asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        }
+        while (cur < 3 * S::NCHUNK) {
+          const int j = u % S::NB2;
+          const uint32_t par = ((u / S::NB2) & 1) ^ 1;
+          if (block) {
+            if (!mbar_wait(&d2_empty[j], par, a.err, 55)) {
+              ok = false;
+              return;
+            }
+          } else if (!mbar_test(&d2_empty[j], par)) {
+            return;
+          }
+          asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+          const int m = cur / S::NCHUNK, ch = cur % S::NCHUNK;
+          const uint32_t wb = smem_u32(smem + S::OFF_W2 + ch * S::NCH * 128);
+#pragma unroll
+          for (int kk = 0; kk < S::KS / 8; ++kk)
+            umma_tf32_ta(tmem + S::TM_D2 + S::NCH * j, tmem + S::TM_G + 32 * m + 8 * kk,
+                         umma_desc_k(wb + kk * 32, 128), idesc2, kk != 0);
+          umma_commit(&d2_full[j]);
+          ++u;
+          ++cur;
+        }
+        pend = -1;
+      };
+      int ri = 0;
+      if (conv1) {
+        for (int w = blockIdx.x; w < items && ok; w += gridDim.x, ++ri) {
+          // D1 is free once the epilogue has read the previous item's conv1
+          if (!mbar_wait(&d1_empty, (ri & 1) ^ 1, a.err, 56)) {
+            ok = false;
+            break;
+          }
+          asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+          for (int m = 0; m < 3 && ok; ++m)
+            for (int kb = 0; kb < S::KB && ok; ++kb)
+              for (int tap = 0; tap < 3; ++tap, ++it) {
+                conv2_progress(false);
+                const int s = it % S::STAGES;
+                if (!ok || !mbar_wait(&full[s], (it / S::STAGES) & 1, a.err, 57)) {
+                  ok = false;
+                  break;
+                }
+                asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+                const uint32_t xa = smem_u32(smem + s * S::A_BYTES);
+                const uint32_t wa = smem_u32(smem + S::OFF_W1 + (tap * S::KB + kb) * S::W1_TILE);
+#pragma unroll
+                for (int j = 0; j < S::BK / 8; ++j)
+                  umma_tf32(tmem + S::TM_D1 + 32 * m, umma_desc_k(xa + j * 32, 128),
+                            umma_desc_k(wa + j * 32, 128), idesc1, (kb | tap | j) != 0);
+                umma_commit(&empty[s]);
+              }
+          if (!ok) break;
+          umma_commit(&d1_full);
+          conv2_progress(true);  // the rest of the previous item's conv2
+          if (conv2) {
+            pend = ri;
+            cur = 0;
+            g_in = false;
+          }
+        }
+        conv2_progress(true);
+      } else if (conv2) {
+        // DC_OUT: conv2 alone, item by item
+        for (int w = blockIdx.x; w < items && ok; w += gridDim.x, ++ri) {
+          pend = ri;
+          cur = 0;
+          g_in = false;
+          conv2_progress(true);
+        }
+      }
+    }
+  } else if (warp >= 4) {
+    // ---------------- epilogue: warps 4-15 ----------------
+    // TMEM lane quarter q = warp % 4 (frames 32q .. 32q+31 of a block); b:
+    // the block of this warp's frames for y and g, its third of the columns
+    // of each 96-column conv2 chunk for the output
+    const int e = warp - 4, q = warp % 4, b = e / 4;
+    const int r = q * 32 + lane;
+    const int p = 128 * b + r;  // this thread's frame (y, g)
+    const int et = threadIdx.x - kEpiBase;
+    const uint32_t lane_base = (uint32_t)(q * 32) << 16;
+    float4* chan = reinterpret_cast<float4*>(smem + S::OFF_CH);
+    for (int c = et; c < C; c += kEpiThreads) {
+      chan[2 * c] = make_float4(a.b2[2 * c], a.b2[2 * c + 1], a.n2w[c], a.n2w[c + C]);
+      chan[2 * c + 1] = make_float4(a.n2b[c], a.n2b[c + C], a.gamma[c], 0.f);
+    }
+    epi_bar();
+    const double ic1 = 1.0 / ((double)S::HID * T), ic2 = 1.0 / (2.0 * C * T);
+    // the row's moments from its tiles' partials, summed by one warp in a
+    // fixed order; every epilogue thread gets them
+    auto row_sum = [&](const double* part, int row, double& s, double& q2) {
+      if (warp == kEpiBase / 32) {
+        double ls = 0.0, lq = 0.0;
+        for (int t = lane; t < a.tiles; t += 32) {
+          ls += part[2 * ((int64_t)row * a.tiles + t)];
+          lq += part[2 * ((int64_t)row * a.tiles + t) + 1];
+        }
+#pragma unroll
+        for (int o = 16; o; o >>= 1) {
+          ls += __shfl_xor_sync(0xffffffffu, ls, o);
+          lq += __shfl_xor_sync(0xffffffffu, lq, o);
+        }
+        if (lane == 0) {
+          red[0] = ls;
+          red[1] = lq;
+        }
+      }
+      epi_bar();
+      s = red[0];
+      q2 = red[1];
+      epi_bar();
+    };
+    uint32_t u = 0;
+    int ri = 0;
+    bool ok = true;
+    for (int w = blockIdx.x; w < items; w += gridDim.x, ++ri) {
+      const int row = w / a.tiles, ts = (w - row * a.tiles) * kTileStride - 2;
+      // local frame i = 128 m + r is frame ts + i; owned: 2 <= i < 382, inside the row
+      auto owned = [&](int i) { return i >= 2 && i < 382 && ts + i < T; };
+      const bool mine = owned(p);
+      float yh[S::HID];  // y of frame p by hidden channel
+      double s, sq;
+      if (conv1) {
+        // ---- y = conv1 + bias, straight from block b's accumulator ----
+        if (ok && !mbar_wait(&d1_full, ri & 1, a.err, 58)) ok = false;
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        {
+          uint32_t d1[32];
+          __syncwarp();
+          tmem_ld32_nw(tmem + lane_base + S::TM_D1 + 32 * b, d1);
+          tmem_ld_wait<32>(d1);
+          // D1 is read out: the next item's conv1 may overwrite it
+          asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+          mbar_arrive(&d1_empty);
+#pragma unroll
+          for (int h = 0; h < S::HID; ++h) yh[h] = __uint_as_float(d1[h]) + k.b1[h];
+        }
+        float fs = 0.f, fq = 0.f;
+#pragma unroll
+        for (int h = 0; h < S::HID; ++h) {
+          fs += yh[h];
+          fq = fmaf(yh[h], yh[h], fq);
+        }
+        s = mine ? fs : 0.f;
+        sq = mine ? fq : 0.f;
+        if (mode == DC_STATS1) {
+          // y of the owned frames for the later launches
+          if (mine) {
+            float4* yp = reinterpret_cast<float4*>(a.y + ((int64_t)row * T + ts + p) * S::YS);
+#pragma unroll
+            for (int c = 0; c < S::YS / 4; ++c)
+              yp[c] = make_float4(yh[4 * c], yh[4 * c + 1], yh[4 * c + 2], yh[4 * c + 3]);
+          }
+          epi_sum2(s, sq, red);
+          if (threadIdx.x == kEpiBase) {
+            a.part1[2 * (int64_t)w] = s;
+            a.part1[2 * (int64_t)w + 1] = sq;
+          }
+          continue;
+        }
+        epi_sum2(s, sq, red);
+      } else {
+        // DC_OUT: y of the owned frames from the buffer
+        if (mine) {
+          const float4* yp = reinterpret_cast<const float4*>(a.y + ((int64_t)row * T + ts + p) * S::YS);
+#pragma unroll
+          for (int c = 0; c < S::YS / 4; ++c) {
+            const float4 v = yp[c];
+            yh[4 * c] = v.x;
+            yh[4 * c + 1] = v.y;
+            yh[4 * c + 2] = v.z;
+            yh[4 * c + 3] = v.w;
+          }
+        } else {
+#pragma unroll
+          for (int h = 0; h < S::HID; ++h) yh[h] = 0.f;
+        }
+        row_sum(a.part1, row, s, sq);
+      }
+      // ---- g = GELU(GN1(y)) of frame p; conv2's A operand, into TMEM ----
+      float mean, inv;
+      norm_of(s, sq, ic1, mean, inv);
+      float ga[S::ACT];  // g by conv2 input (hidden channels, then the bias input 1)
+#pragma unroll
+      for (int h = 0; h < S::HID; ++h) {
+        const float scale = inv * k.n1w[h];
+        ga[h] = mine ? gelu_tc(yh[h] * scale + (k.n1b[h] - mean * scale)) : 0.f;
+      }
+      ga[S::HID] = 1.0f;
+      if (conv2) {
+        float gs[S::KS];
+#pragma unroll
+        for (int j = 0; j < S::KS; ++j) gs[j] = j < S::HID ? ga[j] : (j == S::BIAS ? 1.0f : 0.f);
+        __syncwarp();
+        tmem_st32(tmem + lane_base + S::TM_G + 32 * b, gs);
+        tmem_st_wait();
+        asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+        mbar_arrive(&g_ready);
+      }
+
+      // ---- moments of z: the sums of v.g and g'Mg over the owned frames ----
+      if (mode == DC_OUT) {
+        row_sum(a.part2, row, s, sq);
+      } else {
+        float l = 0.f, qf = 0.f;
+        if (mine) {
+#pragma unroll
+          for (int i = 0, idx = 0; i < S::ACT; ++i) {
+            l = fmaf(k.v[i], ga[i], l);
+            float t = 0.f;
+#pragma unroll
+            for (int j = i; j < S::ACT; ++j, ++idx) t = fmaf(k.m[idx], ga[j], t);
+            qf = fmaf(ga[i], t, qf);
+          }
+        }
+        s = l;
+        sq = qf;
+        epi_sum2(s, sq, red);
+      }
+      float mean2, inv2;
+      norm_of(s, sq, ic2, mean2, inv2);
+      // GN2 with LayerScale folded in: gamma * value = z_v * a + b, gate = z_g * c + d
+      float4* aff = reinterpret_cast<float4*>(smem + S::OFF_AFF);
+      for (int c = et; c < C; c += kEpiThreads) {
+        const float4 t0 = chan[2 * c], t1 = chan[2 * c + 1];
+        const float vs = inv2 * t0.z, gs = inv2 * t0.w;
+        aff[c] = make_float4(t1.z * vs, t1.z * (t1.x - mean2 * vs), gs, t1.y - mean2 * gs);
+      }
+      epi_bar();
+
+      // ---- conv2, the output: x += gamma * GLU(GN2(z)) ----
+      for (int m = 0; m < 3; ++m)
+        for (int ch = 0; ch < S::NCHUNK; ++ch) {
+          const int j = u % S::NB2;
+          const int pm = m * 128 + r;
+          const bool own = owned(pm);
+          const int c0 = ch * (S::NCH / 2) + 16 * b;  // this thread's 16 channels
+          float* xp = a.x + ((int64_t)row * T + (own ? ts + pm : 0)) * C + c0;
+          // the residual from HBM, in flight while this chunk's conv2 completes
+          float4 res[4];
+          if (ok && own) {
+#pragma unroll
+            for (int i = 0; i < 4; ++i) res[i] = reinterpret_cast<const float4*>(xp)[i];
+          }
+          if (ok && !mbar_wait(&d2_full[j], (u / S::NB2) & 1, a.err, 59)) ok = false;
+          asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+          uint32_t zr[32];
+          __syncwarp();
+          tmem_ld32_nw(tmem + lane_base + S::TM_D2 + S::NCH * j + 32 * b, zr);
+          tmem_ld_wait<32>(zr);
+          asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+          mbar_arrive(&d2_empty[j]);
+          ++u;
+          if (ok && own) {
+            float o[16];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              o[4 * i] = res[i].x;
+              o[4 * i + 1] = res[i].y;
+              o[4 * i + 2] = res[i].z;
+              o[4 * i + 3] = res[i].w;
+            }
+#pragma unroll
+            for (int kk = 0; kk < 16; ++kk) {
+              const float4 f = aff[c0 + kk];
+              const float value = fmaf(__uint_as_float(zr[2 * kk]), f.x, f.y);
+              const float gate = fmaf(__uint_as_float(zr[2 * kk + 1]), f.z, f.w);
+              o[kk] += glu_tc(value, gate);
+              if (a.round_out) o[kk] = round_tf32(o[kk]);
+            }
+            float4* x4 = reinterpret_cast<float4*>(xp);
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+              x4[i] = make_float4(o[4 * i], o[4 * i + 1], o[4 * i + 2], o[4 * i + 3]);
+          }
+        }
+    }
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(512));
+  }
+}
+
 // DC_STATS2 as a plain kernel: one 384-thread block per tile, thread p on
 // local frame p, the same arithmetic in the same order as the persistent
 // kernel's epilogue warps (thread p there is epilogue thread p): the row's
@@ -909,10 +1355,64 @@ bool launch_c(const DConvArgs& a, cudaStream_t s) {
   return true;
 }
 
+// C = 192: single-pass only (the split variant's low parts do not fit in
+// shared memory beside the weights).
+bool launch_wide(const DConvArgs& a, cudaStream_t s) {
+  constexpr int C = 192;
+  using S = DcTc<C>;
+  CUtensorMap mx, m1, m2;
+  bool ok;
+  {
+    const cuuint64_t dims[3] = {(cuuint64_t)C, (cuuint64_t)a.T, (cuuint64_t)a.rows};
+    const cuuint64_t str[2] = {(cuuint64_t)C * 4, (cuuint64_t)a.T * C * 4};
+    const cuuint32_t box[3] = {(cuuint32_t)S::BK, 128, 1};
+    ok = make_tensor_map(&mx, a.x, 3, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B);
+  }
+  {
+    // rows = hidden channels (zero beyond HID), columns tap * C + channel
+    const cuuint64_t dims[2] = {(cuuint64_t)(3 * C), (cuuint64_t)a.w1_npad};
+    const cuuint64_t str[1] = {(cuuint64_t)(3 * C) * 4};
+    const cuuint32_t box[2] = {(cuuint32_t)S::BK, (cuuint32_t)S::KS};
+    ok = ok && make_tensor_map(&m1, a.w1_tc, 2, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B);
+  }
+  {
+    // rows = conv2 output columns, 32 K slots each; two boxes of C rows
+    const cuuint64_t dims[2] = {(cuuint64_t)S::KS, (cuuint64_t)a.w2_npad};
+    const cuuint64_t str[1] = {(cuuint64_t)S::KS * 4};
+    const cuuint32_t box[2] = {(cuuint32_t)S::KS, (cuuint32_t)C};
+    ok = ok && make_tensor_map(&m2, a.w2_tc, 2, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B);
+  }
+  if (!ok) return false;
+  DcConst<C> k;
+  const float* src = a.zq_host;
+  for (int i = 0; i < S::ACT; ++i) k.v[i] = *src++;
+  for (int i = 0; i < S::NQ; ++i) k.m[i] = *src++;
+  for (int i = 0; i < S::HID; ++i) k.b1[i] = *src++;
+  for (int i = 0; i < S::HID; ++i) k.n1w[i] = *src++;
+  for (int i = 0; i < S::HID; ++i) k.n1b[i] = *src++;
+  static PerDevice configured;
+  if (configured.first())
+    cudaFuncSetAttribute(dconv_tc_wide_kernel<C>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         S::SMEM);
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int items = a.rows * a.tiles;
+  const int grid = items < sms ? items : sms;
+  if (a.tiles == 1) {
+    dconv_tc_wide_kernel<C><<<grid, kThreads, S::SMEM, s>>>(mx, m1, m2, a, k, DC_ROW);
+  } else {
+    dconv_tc_wide_kernel<C><<<grid, kThreads, S::SMEM, s>>>(mx, m1, m2, a, k, DC_STATS1);
+    dconv_tc_stats2_kernel<C><<<items, kEpiThreads, 0, s>>>(a, k);
+    dconv_tc_wide_kernel<C><<<grid, kThreads, S::SMEM, s>>>(mx, m1, m2, a, k, DC_OUT);
+  }
+  return true;
+}
+
 }  // namespace
 
-bool dconv_tc_supported(int C, int T) {
-  return (C == 48 || C == 96) && T > 0 && tensor_map_encoder() != nullptr;
+bool dconv_tc_supported(int C, int T, bool single) {
+  return (C == 48 || C == 96 || (C == 192 && single)) && T > 0 && tensor_map_encoder() != nullptr;
 }
 
 int dconv_tc_tiles(int T) { return (T + kTileStride - 1) / kTileStride; }
@@ -925,14 +1425,15 @@ int dconv_tc_const_floats(int C) {
 }
 
 bool launch_dconv_tc(const DConvArgs& a, cudaStream_t s) {
-  if (!dconv_tc_supported(a.C, a.T) || a.dil < 1 || a.dil > 2 || !a.w1_tc || !a.w1_tc_lo ||
-      !a.w2_tc || !a.w2_tc_lo || !a.zq_host || a.w1_npad < 16 || a.w2_npad < 2 * a.C ||
-      a.tiles != dconv_tc_tiles(a.T) || (a.tiles > 1 && (!a.part1 || !a.part2 || !a.y)) ||
-      (int64_t)a.rows * a.tiles > INT32_MAX)
+  if (!dconv_tc_supported(a.C, a.T, a.single != 0) || a.dil < 1 || a.dil > 2 || !a.w1_tc ||
+      !a.w1_tc_lo || !a.w2_tc || !a.w2_tc_lo || !a.zq_host || a.w1_npad < (a.C == 192 ? 32 : 16) ||
+      a.w2_npad < 2 * a.C || a.tiles != dconv_tc_tiles(a.T) ||
+      (a.tiles > 1 && (!a.part1 || !a.part2 || !a.y)) || (int64_t)a.rows * a.tiles > INT32_MAX)
     return false;
   switch (a.C) {
     case 48: return launch_c<48>(a, s);
     case 96: return launch_c<96>(a, s);
+    case 192: return launch_wide(a, s);
     default: return false;
   }
 }

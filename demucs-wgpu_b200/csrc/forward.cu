@@ -329,8 +329,10 @@ void run_dconv(dmx_handle* h, const DConvFull& dc, float* x, int rows, int T, bo
   // TF32 builds: tensor cores (3xTF32, fp32-accurate) for the narrow layers
   // (the fused kernel: one launch per spectral row, three over the tiles of a
   // waveform row) and the widest layers (three GEMMs, where the SIMT kernels
-  // are compute-bound); the SIMT kernels are faster elsewhere
-  const bool tc = tf32 && has_tc && !dc.layer[0].zq.empty() && dconv_tc_supported(C, T);
+  // are compute-bound); the SIMT kernels are faster elsewhere. The BF16
+  // build's single-pass contractions also take C 192 onto a fused kernel.
+  const bool tc = tf32 && has_tc && !dc.layer[0].zq.empty() &&
+                  dconv_tc_supported(C, T, dconv_single_pass(h));
   if (tf32 && has_tc && !tc && C >= DMX_DCONV_GEMM_MIN_C) {
     run_dconv_gemm(h, dc, x, rows, T, round_out);
     return;

@@ -87,7 +87,9 @@ int dconv_zstats_parts(int T);
 bool launch_dconv_zstats(int C, const float* y, int ld, int rows, int T, const float* n1w,
                          const float* n1b, const double* st1, double* st2, double* part,
                          const float* zq, cudaStream_t s);
-bool dconv_tc_supported(int C, int T);
+// tensor-core DConv widths: C 48 and 96 (3xTF32 or single-pass), C 192
+// (single-pass only)
+bool dconv_tc_supported(int C, int T, bool single);
 // work items per row of the tensor-core DConv (rows of more than one need
 // part1/part2 and y: rows*T*dconv_tc_ystride(C) floats)
 int dconv_tc_tiles(int T);

@@ -428,34 +428,18 @@ void load_model(dmx_handle* h, const std::map<std::string, HostTensor>& t) {
     }
     return std::make_pair(k, taps);
   };
-  // The fused tensor-core DConv kernel (C = 48, 96) reads its hidden channels
-  // in K slots (dconv_tc_slot): conv1's output rows and conv2's input columns
-  // of the tensor-core copies move there, and the moments of conv2's output
-  // get their host-side constants v = sum_c w_c, M = sum_c w_c w_c'.
-  auto tc_dconv_slots = [&](int C, DConvLayerW& Lw) {
+  // The moments of conv2's output for the fused tensor-core DConv kernels:
+  // host-side constants v = sum_c w_c, M = sum_c w_c w_c' over conv2's inputs
+  // in act order (hidden channels, then the bias input), input i read from K
+  // slot slot(i) of the tensor-core copy (high + low parts), then conv1's bias
+  // and GroupNorm1's weight and bias.
+  auto tc_dconv_moments = [&](int C, DConvLayerW& Lw, auto slot) {
     const int hid = C / 8, act = hid + 1;
-    int src[16];  // slot -> old slot (hidden channel h sat at h, the bias at 15)
-    for (int k = 0; k < 16; ++k) src[k] = -1;
-    for (int i = 0; i < act; ++i) src[dconv_tc_slot(hid, i)] = i < hid ? i : 15;
-    const Packed& p1 = Lw.conv1;
-    for (size_t off : {p1.tc_off, p1.tc_lo_off}) {
-      std::vector<float> old(wb.host.begin() + off, wb.host.begin() + off + (size_t)16 * p1.K);
-      for (int k = 0; k < 16; ++k)
-        for (int j = 0; j < p1.K; ++j)
-          wb.host[off + (size_t)k * p1.K + j] = src[k] >= 0 && src[k] < hid ? old[(size_t)src[k] * p1.K + j] : 0.f;
-    }
     const Packed& p2 = Lw.conv2;
-    for (size_t off : {p2.tc_off, p2.tc_lo_off})
-      for (int n = 0; n < 2 * C; ++n) {
-        float* row = &wb.host[off + (size_t)n * 16];
-        float old[16];
-        std::copy(row, row + 16, old);
-        for (int k = 0; k < 16; ++k) row[k] = src[k] >= 0 ? old[src[k]] : 0.f;
-      }
     std::vector<double> w((size_t)2 * C * act);
     for (int n = 0; n < 2 * C; ++n)
       for (int i = 0; i < act; ++i) {
-        const size_t e = (size_t)n * 16 + dconv_tc_slot(hid, i);
+        const size_t e = (size_t)n * p2.K + slot(i);
         w[(size_t)n * act + i] = (double)wb.host[p2.tc_off + e] + (double)wb.host[p2.tc_lo_off + e];
       }
     Lw.zq.assign(dconv_tc_const_floats(C), 0.f);
@@ -476,6 +460,31 @@ void load_model(dmx_handle* h, const std::map<std::string, HostTensor>& t) {
       tail[hid + h] = wb.host[Lw.n1w.off + h];
       tail[2 * hid + h] = wb.host[Lw.n1b.off + h];
     }
+  };
+  // The fused tensor-core DConv kernel for C = 48, 96 reads its hidden
+  // channels in K slots (dconv_tc_slot): conv1's output rows and conv2's
+  // input columns of the tensor-core copies move there.
+  auto tc_dconv_slots = [&](int C, DConvLayerW& Lw) {
+    const int hid = C / 8, act = hid + 1;
+    int src[16];  // slot -> old slot (hidden channel h sat at h, the bias at 15)
+    for (int k = 0; k < 16; ++k) src[k] = -1;
+    for (int i = 0; i < act; ++i) src[dconv_tc_slot(hid, i)] = i < hid ? i : 15;
+    const Packed& p1 = Lw.conv1;
+    for (size_t off : {p1.tc_off, p1.tc_lo_off}) {
+      std::vector<float> old(wb.host.begin() + off, wb.host.begin() + off + (size_t)16 * p1.K);
+      for (int k = 0; k < 16; ++k)
+        for (int j = 0; j < p1.K; ++j)
+          wb.host[off + (size_t)k * p1.K + j] = src[k] >= 0 && src[k] < hid ? old[(size_t)src[k] * p1.K + j] : 0.f;
+    }
+    const Packed& p2 = Lw.conv2;
+    for (size_t off : {p2.tc_off, p2.tc_lo_off})
+      for (int n = 0; n < 2 * C; ++n) {
+        float* row = &wb.host[off + (size_t)n * 16];
+        float old[16];
+        std::copy(row, row + 16, old);
+        for (int k = 0; k < 16; ++k) row[k] = src[k] >= 0 ? old[src[k]] : 0.f;
+      }
+    tc_dconv_moments(C, Lw, [hid](int i) { return dconv_tc_slot(hid, i); });
   };
   // The SIMT DConv kernels' GroupNorm2 moments from g: w~_n = (conv2 column
   // n's weights, its bias) over all 2C columns; v = sum_n w~_n and
@@ -530,6 +539,10 @@ void load_model(dmx_handle* h, const std::map<std::string, HostTensor>& t) {
       }
       if ((C == 48 || C == 96) && Lw.conv1.has_tc && Lw.conv2.has_tc && Lw.conv2.K == 16)
         tc_dconv_slots(C, Lw);
+      // C = 192: hidden channel h at K slot h, the bias input at the last slot
+      if (C == 192 && Lw.conv1.has_tc && Lw.conv2.has_tc && Lw.conv2.K == 32 &&
+          Lw.conv1.Npad >= 32)
+        tc_dconv_moments(C, Lw, [hid = C / 8, kb = Lw.conv2.K - 1](int i) { return i < hid ? i : kb; });
       simt_dconv_moments(C, Lw);
       Lw.n2w = L.vec(at + ".4.weight", 2 * C);
       Lw.n2b = L.vec(at + ".4.bias", 2 * C);

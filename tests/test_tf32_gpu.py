@@ -56,3 +56,31 @@ def test_tensor_core_forward(layer_scale, precision):
         worst = np.abs(got.astype(np.float64) - ref).reshape(4, -1).max(axis=1)
         print("TF32X3 per-stem max-abs", worst)
         assert worst.max() <= 1e-4, worst
+
+
+def test_bf16_wide_dconv_runs_on_the_tensor_cores_and_matches_the_oracle():
+    """The BF16 build runs the C = 192 DConv layers on the fused tensor-core
+    kernel: one launch per spectral row (encoder.2, decoder.1) and the three
+    tiled launches over the waveform rows (tencoder.2, tdecoder.1, 5375 frames
+    a row). With LayerScale 1 the branch carries its full weight, so the
+    layers after it show its single-pass tf32 error undamped."""
+    import dmx
+    w = synth.random_weights(5, layer_scale=1.0, norm_jitter=0.1)
+    mix = synth.gaussian_audio(11, 1)
+    tr_o, tr_g = {}, {}
+    oracle.OracleModel(w).forward(mix, trace=tr_o)
+    h = dmx.Handle(synth.write_safetensors(w), device=0, precision=dmx.BF16, max_batch=1)
+    h.set_trace(tr_g)
+    got = h.forward(mix)
+    assert np.isfinite(got).all()
+    h.set_trace(None)
+    h.set_stage_timing(True)
+    again = h.forward(mix)
+    tags = h.stage_times()
+    assert np.array_equal(got, again)
+    assert "dconv.tc192" in tags and "dconv.tctiled192" in tags, sorted(tags)
+    assert not any(t in tags for t in ("dconv.row192", "dconv.tiled192")), sorted(tags)
+    for name in ("encoder.2", "tencoder.2", "encoder.3", "tencoder.3"):
+        s = snr_db(tr_o[name], tr_g[name])
+        print(f"{name:12s} snr {s:7.2f} dB")
+        assert s >= 50.0, (name, s)
