@@ -801,8 +801,9 @@ __global__ void __launch_bounds__(kThreads, 1)
 //  * conv1: per 128-frame block m, tap t and 32-channel K block kb, warp 0
 //    loads the x tile at frames ts + 128 m + (t - 1) d (TMA zero-fills
 //    frames outside the row) and warp 1 accumulates it against tap t's
-//    weights into the block's 32 TMEM columns; the three loads of a tile
-//    run back to back, so the second and third come from L2.
+//    weights into the block's 32 TMEM columns; a block's centre-tap tiles
+//    go first, so the outer taps' loads (the same frames shifted by d)
+//    mostly hit L2.
 //  * the epilogue warps read y straight out of TMEM (no tap exchange), write
 //    g into TMEM as conv2's A operand (with the constant 1 at slot 31), and
 //    conv2 runs in 96-column chunks (48 channels) through three TMEM
@@ -874,9 +875,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         bool ok = true;
         for (int w = blockIdx.x; w < items && ok; w += gridDim.x) {
           const int row = w / a.tiles, ts = (w - row * a.tiles) * kTileStride - 2;
+          // per block: the centre tap's tiles first, then the outer taps'
+          // (the same frames shifted by d, mostly L2 hits by then)
           for (int m = 0; m < 3 && ok; ++m)
-            for (int kb = 0; kb < S::KB && ok; ++kb)
-              for (int tap = 0; tap < 3; ++tap, ++it) {
+            for (int ti = 0; ti < 3 && ok; ++ti)
+              for (int kb = 0; kb < S::KB; ++kb, ++it) {
+                const int tap = ti == 0 ? 1 : (ti == 1 ? 0 : 2);
                 const int s = it % S::STAGES;
                 if (!mbar_wait(&empty[s], ((it / S::STAGES) & 1) ^ 1, a.err, 51)) {
                   ok = false;
@@ -949,8 +953,9 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
           for (int m = 0; m < 3 && ok; ++m)
-            for (int kb = 0; kb < S::KB && ok; ++kb)
-              for (int tap = 0; tap < 3; ++tap, ++it) {
+            for (int ti = 0; ti < 3 && ok; ++ti)
+              for (int kb = 0; kb < S::KB; ++kb, ++it) {
+                const int tap = ti == 0 ? 1 : (ti == 1 ? 0 : 2);  // the producer's order
                 conv2_progress(false);
                 const int s = it % S::STAGES;
                 if (!ok || !mbar_wait(&full[s], (it / S::STAGES) & 1, a.err, 57)) {
@@ -963,7 +968,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
                 for (int j = 0; j < S::BK / 8; ++j)
                   umma_tf32(tmem + S::TM_D1 + 32 * m, umma_desc_k(xa + j * 32, 128),
-                            umma_desc_k(wa + j * 32, 128), idesc1, (kb | tap | j) != 0);
+                            umma_desc_k(wa + j * 32, 128), idesc1, (kb | ti | j) != 0);
                 umma_commit(&empty[s]);
               }
           if (!ok) break;
@@ -1146,19 +1151,31 @@ __global__ void __launch_bounds__(kThreads, 1)
       epi_bar();
 
       // ---- conv2, the output: x += gamma * GLU(GN2(z)) ----
-      for (int m = 0; m < 3; ++m)
-        for (int ch = 0; ch < S::NCHUNK; ++ch) {
+      // chunk cc = (block, 48-channel group); the residual of the next chunk
+      // is loaded from HBM while this one's conv2 completes and is stored
+      auto load_res = [&](int cc, float4* dst) {
+        const int pm = (cc / S::NCHUNK) * 128 + r;
+        if (ok && owned(pm)) {
+          const float* xp =
+              a.x + ((int64_t)row * T + ts + pm) * C + (cc % S::NCHUNK) * (S::NCH / 2) + 16 * b;
+#pragma unroll
+          for (int i = 0; i < 4; ++i) dst[i] = reinterpret_cast<const float4*>(xp)[i];
+        }
+      };
+      float4 nxt[4];
+      load_res(0, nxt);
+#pragma unroll 1
+      for (int cc = 0; cc < 3 * S::NCHUNK; ++cc) {
+          const int m = cc / S::NCHUNK, ch = cc % S::NCHUNK;
           const int j = u % S::NB2;
           const int pm = m * 128 + r;
           const bool own = owned(pm);
           const int c0 = ch * (S::NCH / 2) + 16 * b;  // this thread's 16 channels
           float* xp = a.x + ((int64_t)row * T + (own ? ts + pm : 0)) * C + c0;
-          // the residual from HBM, in flight while this chunk's conv2 completes
           float4 res[4];
-          if (ok && own) {
 #pragma unroll
-            for (int i = 0; i < 4; ++i) res[i] = reinterpret_cast<const float4*>(xp)[i];
-          }
+          for (int i = 0; i < 4; ++i) res[i] = nxt[i];
+          if (cc + 1 < 3 * S::NCHUNK) load_res(cc + 1, nxt);
           if (ok && !mbar_wait(&d2_full[j], (u / S::NB2) & 1, a.err, 59)) ok = false;
           asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
           uint32_t zr[32];
@@ -1190,7 +1207,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int i = 0; i < 4; ++i)
               x4[i] = make_float4(o[4 * i], o[4 * i + 1], o[4 * i + 2], o[4 * i + 3]);
           }
-        }
+      }
     }
   }
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
