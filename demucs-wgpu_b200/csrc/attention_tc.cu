@@ -23,9 +23,12 @@
 // The bf16 variant (the BF16 build) runs both products on kind::f16 with
 // bf16 q, k and V^T stored so by the projection GEMMs: TMA also brings the
 // CTA's Q tile into shared memory, and the softmax warps write P, rounded to
-// bf16 (the row sum adds the rounded values), into a shared-memory buffer
-// per S buffer instead of over S; both are K-major, 128-byte swizzled A
-// operands. No load uses cluster multicast.
+// bf16, into a shared-memory buffer per S buffer instead of over S; both are
+// K-major, 128-byte swizzled A operands. The row sum comes from the MMA: 16
+// rows of ones after each V^T tile make columns 64..79 of the P V^T
+// accumulator the sums of P exactly as the tensor core adds them, so the
+// softmax warps do not add the weights themselves. No load uses cluster
+// multicast.
 #include <cudaTypedefs.h>
 
 #include "common.cuh"
@@ -45,11 +48,14 @@ constexpr int STAGES = 3;
 constexpr int KCHUNK = KT * 128;             // one 64-row x 128-byte swizzled chunk
 
 // Shared memory: the K / V^T ring (fp32: two 32-column chunks per operand;
-// bf16: one 64-column chunk), then for bf16 the Q tile and two P buffers.
+// bf16: one 64-column chunk, and after V^T 16 rows of ones, so P V^T's
+// columns 64..79 are the row sums of P as the tensor core adds them), then
+// for bf16 the Q tile and two P buffers.
 template <bool BF>
 struct AttnSmem {
   static constexpr int KV_BYTES = BF ? KCHUNK : 2 * KCHUNK;  // 64 x 64 values
-  static constexpr int STAGE_BYTES = 2 * KV_BYTES;            // K then V^T
+  static constexpr int ONES_BYTES = BF ? 16 * 128 : 0;        // 16 rows x 64 bf16 ones
+  static constexpr int STAGE_BYTES = 2 * KV_BYTES + ONES_BYTES;  // K, V^T (, ones)
   static constexpr int Q_BYTES = BF ? QT * 128 : 0;           // 128 rows x 64 bf16
   static constexpr int P_BYTES = BF ? QT * 128 : 0;           // one P buffer, 128 x 64 bf16
   static constexpr int OFF_Q = STAGES * STAGE_BYTES;
@@ -57,8 +63,11 @@ struct AttnSmem {
   static constexpr int OFF_BAR = OFF_P + 2 * P_BYTES;
   static constexpr int TOTAL = OFF_BAR + 256 + 1024 /*align*/;
 };
-// TMEM columns
-constexpr uint32_t TM_Q = 0, TM_S = 64, TM_O = 192;  // S buffers at 64 and 128
+// TMEM columns. fp32: Q at 0, S buffers at 64 and 128, O at 192. bf16: O
+// (64 columns) and the row sums (16 equal columns) at 0, S buffers at 128 and
+// 192.
+constexpr uint32_t TM_Q = 0, TM_S = 64, TM_O = 192;
+constexpr uint32_t TM_S_BF = 128, TM_O_BF = 0;
 constexpr float kRescale = 8.0f;  // log2 of the largest P tolerated before O is rescaled
 
 // 2^x by the hardware approximation (PTX ex2.approx.ftz: relative error near
@@ -98,6 +107,7 @@ __global__ void __launch_bounds__(192, 2)
                         const __grid_constant__ CUtensorMap tmQ, const AttnParams p) {
   using L = AttnSmem<BF>;
   constexpr int STAGE_BYTES = L::STAGE_BYTES, KV_BYTES = L::KV_BYTES;
+  constexpr uint32_t tmS = BF ? TM_S_BF : TM_S, tmO = BF ? TM_O_BF : TM_O;
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   unsigned char* smem = reinterpret_cast<unsigned char*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
@@ -132,6 +142,15 @@ __global__ void __launch_bounds__(192, 2)
     mbar_init(o_final, 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
+  if (BF) {
+    // the ones rows after each stage's V^T (bf16 1.0; swizzling leaves them as they are)
+    for (int i = threadIdx.x; i < STAGES * L::ONES_BYTES / 16; i += blockDim.x) {
+      const int s = i / (L::ONES_BYTES / 16), c = i % (L::ONES_BYTES / 16);
+      *reinterpret_cast<uint4*>(KVs + s * STAGE_BYTES + 2 * KV_BYTES + 16 * c) =
+          make_uint4(0x3F803F80u, 0x3F803F80u, 0x3F803F80u, 0x3F803F80u);
+    }
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  }
   if (warp == 1) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
                      smem_u32(tmem_slot)),
@@ -159,7 +178,7 @@ __global__ void __launch_bounds__(192, 2)
         const uint32_t ph = (j / STAGES) & 1;
         if (!mbar_wait(&kv_empty[s], ph ^ 1, p.err, 11)) break;
         unsigned char* st = KVs + s * STAGE_BYTES;
-        mbar_expect_tx(&kv_full[s], STAGE_BYTES);
+        mbar_expect_tx(&kv_full[s], 2 * KV_BYTES);  // K and V^T (not the ones rows)
         if (BF) {
           // 64 keys x 64 dims of k, and V^T rows (b, h, dim) over this tile's 64 keys
           tma_load_2d(st, &tmKV, &kv_full[s], p.k_col + h * HD, krow0 + j * KT);
@@ -181,6 +200,10 @@ __global__ void __launch_bounds__(192, 2)
       constexpr uint32_t ab = BF ? 1u : 2u;
       constexpr uint32_t idesc = (1u << 4) | (ab << 7) | (ab << 10) | ((64u >> 3) << 17) |
                                  ((128u >> 4) << 24);
+      // bf16 P V^T: N = 80, V^T's 64 rows and the 16 ones rows after them
+      constexpr uint32_t idesc_pv = BF ? (1u << 4) | (ab << 7) | (ab << 10) | ((80u >> 3) << 17) |
+                                             ((128u >> 4) << 24)
+                                       : idesc;
       bool ok = mbar_wait(q_full, 0, p.err, 12);
       asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
       // S_j = Q K_j^T into buffer j%2
@@ -191,7 +214,7 @@ __global__ void __launch_bounds__(192, 2)
         if (j >= 2 && !mbar_wait(&pv_done[j & 1], ((j - 2) >> 1) & 1, p.err, 17)) return false;
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
         const uint32_t k_addr = smem_u32(KVs + s * STAGE_BYTES);
-        const uint32_t d = tmem + TM_S + (uint32_t)((j & 1) * 64);
+        const uint32_t d = tmem + tmS + (uint32_t)((j & 1) * 64);
         if (BF) {
           const uint32_t q_addr = smem_u32(Qs);
 #pragma unroll
@@ -218,15 +241,15 @@ __global__ void __launch_bounds__(192, 2)
           const uint32_t p_addr = smem_u32(Ps + (j & 1) * L::P_BYTES);
 #pragma unroll
           for (int kk = 0; kk < 4; ++kk)
-            umma_bf16(tmem + TM_O, umma_desc_k(p_addr + kk * 32, 128),
-                      umma_desc_k(v_addr + kk * 32, 128), idesc, (j | kk) != 0);
+            umma_bf16(tmem + tmO, umma_desc_k(p_addr + kk * 32, 128),
+                      umma_desc_k(v_addr + kk * 32, 128), idesc_pv, (j | kk) != 0);
         } else {
-          const uint32_t pa = tmem + TM_S + (uint32_t)((j & 1) * 64);
+          const uint32_t pa = tmem + tmS + (uint32_t)((j & 1) * 64);
           // K = 64 keys in steps of 8: V^T chunk kc holds keys 32kc..32kc+31,
           // 32 bytes per step inside its 128-byte rows
 #pragma unroll
           for (int kk = 0; kk < 8; ++kk)
-            umma_tf32_ta(tmem + TM_O, pa + 8 * kk,
+            umma_tf32_ta(tmem + tmO, pa + 8 * kk,
                          umma_desc_k(v_addr + (kk / 4) * KCHUNK + (kk % 4) * 32, 128), idesc,
                          (j | kk) != 0);
         }
@@ -266,7 +289,7 @@ __global__ void __launch_bounds__(192, 2)
     for (int j = 0; j < ntiles; ++j) {
       if (ok && !mbar_wait(&s_full[j & 1], (j >> 1) & 1, p.err, 15)) ok = false;
       asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-      const uint32_t sb = tmem + lane_base + TM_S + (uint32_t)((j & 1) * 64);
+      const uint32_t sb = tmem + lane_base + tmS + (uint32_t)((j & 1) * 64);
       float sv[64];
       {
         uint32_t sr[64];
@@ -297,14 +320,16 @@ __global__ void __launch_bounds__(192, 2)
           if (ok && !mbar_wait(&pv_done[(j - 1) & 1], ((j - 1) >> 1) & 1, p.err, 18)) ok = false;
           asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
           __syncwarp();
+          // (bf16: the row-sum columns 64..79 too; 80..95 are unused)
           float ov[32];
 #pragma unroll
-          for (int c = 0; c < 64; c += 32) {
-            tmem_ld32(tmem + lane_base + TM_O + c, ov);
+          for (int c = 0; c < (BF ? 96 : 64); c += 32) {
+            tmem_ld32(tmem + lane_base + tmO + c, ov);
 #pragma unroll
             for (int i = 0; i < 32; ++i) ov[i] *= corr;
-            tmem_st32(tmem + lane_base + TM_O + c, ov);
+            tmem_st32(tmem + lane_base + tmO + c, ov);
           }
+          tmem_st_wait();
         }
       }
       // P = 2^(s sl - m) over S in TMEM, with paired f32 arithmetic. The
@@ -317,14 +342,13 @@ __global__ void __launch_bounds__(192, 2)
       for (int i = 0; i < 4; ++i) rs4[i] = make_float2(0.f, 0.f);
       if (BF) {
         // P rounded to bf16 into row r of P buffer j%2 (128-byte rows, 16-byte
-        // chunk c at chunk c ^ (r % 8)); the row sum adds the rounded values
+        // chunk c at chunk c ^ (r % 8)); the row sum is the MMA's (ones rows)
         uint32_t pk[32];
 #pragma unroll
         for (int i = 0; i < 32; ++i) {
           const float2 t = __ffma2_rn(make_float2(sv[2 * i], sv[2 * i + 1]), sl2, nm2);
           const __nv_bfloat162 pb = __floats2bfloat162_rn(ex2_approx(t.x), ex2_approx(t.y));
           pk[i] = *reinterpret_cast<const uint32_t*>(&pb);
-          rs4[i % 4] = __fadd2_rn(rs4[i % 4], __bfloat1622float2(pb));
         }
         unsigned char* prow = Ps + (j & 1) * L::P_BYTES + r * 128;
 #pragma unroll
@@ -344,8 +368,10 @@ __global__ void __launch_bounds__(192, 2)
         tmem_st32(sb + 32, sv + 32);
         tmem_st_wait();
       }
-      rs4[0] = __fadd2_rn(__fadd2_rn(rs4[0], rs4[1]), __fadd2_rn(rs4[2], rs4[3]));
-      l += rs4[0].x + rs4[0].y;
+      if (!BF) {
+        rs4[0] = __fadd2_rn(__fadd2_rn(rs4[0], rs4[1]), __fadd2_rn(rs4[2], rs4[3]));
+        l += rs4[0].x + rs4[0].y;
+      }
       asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
       asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(&p_full[j & 1]))
                    : "memory");
@@ -354,8 +380,13 @@ __global__ void __launch_bounds__(192, 2)
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     float ov[64];
     __syncwarp();
-    tmem_ld32(tmem + lane_base + TM_O, ov);
-    tmem_ld32(tmem + lane_base + TM_O + 32, ov + 32);
+    tmem_ld32(tmem + lane_base + tmO, ov);
+    tmem_ld32(tmem + lane_base + tmO + 32, ov + 32);
+    if (BF) {
+      float ls[16];
+      tmem_ld16(tmem + lane_base + tmO + 64, ls);
+      l = ls[0];
+    }
     if (ok && qvalid && p.out16) {
       // the output feeds only the bf16 out-projection: stored as bf16
       const float inv = l > 0.f ? 1.0f / l : 0.f;
