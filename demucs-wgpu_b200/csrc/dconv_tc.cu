@@ -216,10 +216,15 @@ __global__ void __launch_bounds__(kThreads, 1)
                         const __grid_constant__ CUtensorMap tmW2lo, const DConvArgs a,
                         const __grid_constant__ DcConst<C> k, int mode) {
   using S = DcTc<C>;
+  // x ring: 3xTF32 stages hold a tile and its low part; single-pass ones only
+  // the tile, so the same bytes make twice the stages
+  constexpr int NST = SPLIT ? S::STAGES : 2 * S::STAGES;
+  constexpr int SST = SPLIT ? S::STAGE : S::A_BYTES;
+  static_assert(NST * SST == S::STAGES * S::STAGE, "ring");
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   unsigned char* smem = reinterpret_cast<unsigned char*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
-  __shared__ __align__(8) uint64_t full[S::STAGES], empty[S::STAGES], conv[S::STAGES];
+  __shared__ __align__(8) uint64_t full[NST], empty[NST], conv[NST];
   __shared__ __align__(8) uint64_t w1_full, w2_full, d1_full, d1_empty, g_ready, res_full;
   __shared__ __align__(8) uint64_t d2_full[2], d2_empty[2];
   __shared__ uint32_t tmem_slot;
@@ -228,7 +233,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   if (a.err && *reinterpret_cast<volatile int*>(a.err) != 0) return;
   if (threadIdx.x == 0) {
-    for (int s = 0; s < S::STAGES; ++s) {
+    for (int s = 0; s < NST; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
       mbar_init(&conv[s], 64);
@@ -286,14 +291,14 @@ __global__ void __launch_bounds__(kThreads, 1)
           const int row = w / a.tiles, ts = (w - row * a.tiles) * kTileStride - 2;
           for (int m = 0; m < 3 && ok; ++m) {
             for (int kb = 0; kb < S::KB; ++kb, ++it) {
-              const int s = it % S::STAGES;
-              if (!mbar_wait(&empty[s], ((it / S::STAGES) & 1) ^ 1, a.err, 31)) {
+              const int s = it % NST;
+              if (!mbar_wait(&empty[s], ((it / NST) & 1) ^ 1, a.err, 31)) {
                 ok = false;
                 break;
               }
               mbar_expect_tx(&full[s], S::A_BYTES);
               // frames ts + 128 m .. +127 (zero outside the row), channels kb BK ..
-              tma_load_3d(smem + s * S::STAGE, &tmX, &full[s], kb * S::BK, ts + m * 128, row);
+              tma_load_3d(smem + s * SST, &tmX, &full[s], kb * S::BK, ts + m * 128, row);
             }
           }
         }
@@ -394,9 +399,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             const uint32_t d = tm_d1 + 64 * m;
             for (int kb = 0; kb < S::KB; ++kb, ++it) {
               conv2_progress(false);
-              const int s = it % S::STAGES;
-              const uint32_t par = (it / S::STAGES) & 1;
-              const uint32_t a_hi = smem_u32(smem + s * S::STAGE);
+              const int s = it % NST;
+              const uint32_t par = (it / NST) & 1;
+              const uint32_t a_hi = smem_u32(smem + s * SST);
               const uint32_t a_lo = a_hi + S::A_BYTES;
               const uint32_t b_hi = smem_u32(smem + S::OFF_W1 + kb * S::W1_KB);
               const uint32_t b_lo = b_hi + S::W1_BYTES;
@@ -457,14 +462,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int w = blockIdx.x; w < items; w += gridDim.x)
         for (int m = 0; m < 3; ++m)
           for (int kb = 0; kb < S::KB; ++kb, ++it) {
-            const int s = it % S::STAGES;
-            if (live && !mbar_wait(&full[s], (it / S::STAGES) & 1, a.err, 36)) live = false;
+            const int s = it % NST;
+            if (live && !mbar_wait(&full[s], (it / NST) & 1, a.err, 36)) live = false;
             if (live) {
 #pragma unroll
               for (int h = 0; h < 2; ++h) {
                 const int r = c + 64 * h;
-                const float4* x4 = reinterpret_cast<const float4*>(smem + s * S::STAGE + r * S::BK * 4);
-                float4* lo4 = reinterpret_cast<float4*>(smem + s * S::STAGE + S::A_BYTES + r * S::BK * 4);
+                const float4* x4 = reinterpret_cast<const float4*>(smem + s * SST + r * S::BK * 4);
+                float4* lo4 = reinterpret_cast<float4*>(smem + s * SST + S::A_BYTES + r * S::BK * 4);
 #pragma unroll
                 for (int qq = 0; qq < S::BK / 4; ++qq) {
                   const int q = qq ^ swz;
