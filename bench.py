@@ -533,7 +533,7 @@ def run_ours(args, rank, world, local_rank):
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 3),
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
             "dtype": {"FP32": "f32", "TF32": "tf32", "TF32X3": "tf32x3",
-                      "BF16": "bf16 (transformer linears), tf32 (convolutions, attention)"}[args.precision],
+                      "BF16": "bf16 (transformer linears and attention), tf32 (convolutions and DConv)"}[args.precision],
             "data": "synthetic",
             "config": track_config(seconds),
             "precision": args.precision,
