@@ -26,15 +26,25 @@ struct FirstConvW {
   float b[kCo];
 };
 
-// 24 channels from 24 h of one position, weights from the constant bank
+// 24 channels from 24 h of one position, weights from the constant bank;
+// channel pairs on the paired fp32 FMA (each lane rounds as fmaf does)
 template <int CIN, int H>
 DMX_DEVICE void accumulate(const FirstConvW<CIN>& cw, const float* in, float* acc) {
+  float2 a2[12];
 #pragma unroll
-  for (int j = 0; j < 24; ++j) acc[j] = cw.b[24 * H + j];
+  for (int j = 0; j < 12; ++j) a2[j] = make_float2(cw.b[24 * H + 2 * j], cw.b[24 * H + 2 * j + 1]);
 #pragma unroll
-  for (int k = 0; k < 8 * CIN; ++k)
+  for (int k = 0; k < 8 * CIN; ++k) {
+    const float2 xk = make_float2(in[k], in[k]);
 #pragma unroll
-    for (int j = 0; j < 24; ++j) acc[j] = fmaf(in[k], cw.w[k][24 * H + j], acc[j]);
+    for (int j = 0; j < 12; ++j)
+      a2[j] = __ffma2_rn(xk, make_float2(cw.w[k][24 * H + 2 * j], cw.w[k][24 * H + 2 * j + 1]), a2[j]);
+  }
+#pragma unroll
+  for (int j = 0; j < 12; ++j) {
+    acc[2 * j] = a2[j].x;
+    acc[2 * j + 1] = a2[j].y;
+  }
 }
 
 template <int CIN>
