@@ -63,6 +63,22 @@ DMX_DEVICE float round_tf32(float x) {
   return __uint_as_float(b & 0xFFFFE000u);
 }
 
+// Eight floats from / to a 32-byte-aligned global address in one access
+// (sm_100's 256-bit loads and stores): half the requests of two float4s, for
+// the per-thread row segments of the tensor-core epilogues.
+DMX_DEVICE void ld_global8(const float* p, float* v) {
+  asm volatile("ld.global.v8.f32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
+               : "=f"(v[0]), "=f"(v[1]), "=f"(v[2]), "=f"(v[3]), "=f"(v[4]), "=f"(v[5]),
+                 "=f"(v[6]), "=f"(v[7])
+               : "l"(p)
+               : "memory");
+}
+DMX_DEVICE void st_global8(float* p, const float* v) {
+  asm volatile("st.global.v8.f32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"l"(p), "f"(v[0]),
+               "f"(v[1]), "f"(v[2]), "f"(v[3]), "f"(v[4]), "f"(v[5]), "f"(v[6]), "f"(v[7])
+               : "memory");
+}
+
 DMX_DEVICE double warp_sum(double v) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);

@@ -734,12 +734,14 @@ __global__ void __launch_bounds__(kThreads, 1)
           const bool own = owned(pm);
           const int c0 = ch * (S::NCH / 2) + 16 * b;  // this thread's 16 channels
           float* xp = a.x + ((int64_t)row * T + (own ? ts + pm : 0)) * C + c0;
-          float4 res[4];
+          // the residual, then the output, of this thread's 16 channels (64
+          // bytes at a 32-byte-aligned address: frames are 192 or 384 bytes)
+          float o[16];
           if (!S::ALL) {
             // the residual from HBM, in flight while this chunk's conv2 completes
             if (ok && own) {
-#pragma unroll
-              for (int i = 0; i < 4; ++i) res[i] = reinterpret_cast<const float4*>(xp)[i];
+              ld_global8(xp, o);
+              ld_global8(xp + 8, o + 8);
             }
             if (ok && !mbar_wait(&d2_full[j], (u >> 1) & 1, a.err, 39)) ok = false;
             asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
@@ -751,8 +753,13 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (S::ALL) {
             const unsigned char* rb = smem + S::OFF_RES + (3 * m + b) * S::RES_BOX + r * 64;
 #pragma unroll
-            for (int i = 0; i < 4; ++i)
-              res[i] = *reinterpret_cast<const float4*>(rb + ((i ^ ((r >> 1) & 3)) << 4));
+            for (int i = 0; i < 4; ++i) {
+              const float4 t = *reinterpret_cast<const float4*>(rb + ((i ^ ((r >> 1) & 3)) << 4));
+              o[4 * i] = t.x;
+              o[4 * i + 1] = t.y;
+              o[4 * i + 2] = t.z;
+              o[4 * i + 3] = t.w;
+            }
           }
           tmem_ld_wait<32>(zr);
           if (!S::ALL) {
@@ -761,14 +768,6 @@ __global__ void __launch_bounds__(kThreads, 1)
             ++u;
           }
           if (ok && own) {
-            float o[16];
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-              o[4 * i] = res[i].x;
-              o[4 * i + 1] = res[i].y;
-              o[4 * i + 2] = res[i].z;
-              o[4 * i + 3] = res[i].w;
-            }
 #pragma unroll
             for (int kk = 0; kk < 16; ++kk) {
               const float4 f = aff[c0 + kk];
@@ -778,10 +777,8 @@ __global__ void __launch_bounds__(kThreads, 1)
               o[kk] += glu_tc(value, gate);
               if (a.round_out) o[kk] = round_tf32(o[kk]);
             }
-            float4* x4 = reinterpret_cast<float4*>(xp);
-#pragma unroll
-            for (int i = 0; i < 4; ++i)
-              x4[i] = make_float4(o[4 * i], o[4 * i + 1], o[4 * i + 2], o[4 * i + 3]);
+            st_global8(xp, o);
+            st_global8(xp + 8, o + 8);
           }
         }
       if (S::ALL) {
@@ -1158,16 +1155,17 @@ __global__ void __launch_bounds__(kThreads, 1)
       // ---- conv2, the output: x += gamma * GLU(GN2(z)) ----
       // chunk cc = (block, 48-channel group); the residual of the next chunk
       // is loaded from HBM while this one's conv2 completes and is stored
-      auto load_res = [&](int cc, float4* dst) {
+      // (16 channels = 64 bytes at a 64-byte-aligned offset: two 32-byte accesses)
+      auto load_res = [&](int cc, float* dst) {
         const int pm = (cc / S::NCHUNK) * 128 + r;
         if (ok && owned(pm)) {
           const float* xp =
               a.x + ((int64_t)row * T + ts + pm) * C + (cc % S::NCHUNK) * (S::NCH / 2) + 16 * b;
-#pragma unroll
-          for (int i = 0; i < 4; ++i) dst[i] = reinterpret_cast<const float4*>(xp)[i];
+          ld_global8(xp, dst);
+          ld_global8(xp + 8, dst + 8);
         }
       };
-      float4 nxt[4];
+      float nxt[16];
       load_res(0, nxt);
 #pragma unroll 1
       for (int cc = 0; cc < 3 * S::NCHUNK; ++cc) {
@@ -1177,9 +1175,9 @@ __global__ void __launch_bounds__(kThreads, 1)
           const bool own = owned(pm);
           const int c0 = ch * (S::NCH / 2) + 16 * b;  // this thread's 16 channels
           float* xp = a.x + ((int64_t)row * T + (own ? ts + pm : 0)) * C + c0;
-          float4 res[4];
+          float o[16];
 #pragma unroll
-          for (int i = 0; i < 4; ++i) res[i] = nxt[i];
+          for (int i = 0; i < 16; ++i) o[i] = nxt[i];
           if (cc + 1 < 3 * S::NCHUNK) load_res(cc + 1, nxt);
           if (ok && !mbar_wait(&d2_full[j], (u / S::NB2) & 1, a.err, 59)) ok = false;
           asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
@@ -1191,14 +1189,6 @@ __global__ void __launch_bounds__(kThreads, 1)
           mbar_arrive(&d2_empty[j]);
           ++u;
           if (ok && own) {
-            float o[16];
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-              o[4 * i] = res[i].x;
-              o[4 * i + 1] = res[i].y;
-              o[4 * i + 2] = res[i].z;
-              o[4 * i + 3] = res[i].w;
-            }
 #pragma unroll
             for (int kk = 0; kk < 16; ++kk) {
               const float4 f = aff[c0 + kk];
@@ -1207,10 +1197,8 @@ __global__ void __launch_bounds__(kThreads, 1)
               o[kk] += glu_tc(value, gate);
               if (a.round_out) o[kk] = round_tf32(o[kk]);
             }
-            float4* x4 = reinterpret_cast<float4*>(xp);
-#pragma unroll
-            for (int i = 0; i < 4; ++i)
-              x4[i] = make_float4(o[4 * i], o[4 * i + 1], o[4 * i + 2], o[4 * i + 3]);
+            st_global8(xp, o);
+            st_global8(xp + 8, o + 8);
           }
       }
     }

@@ -478,7 +478,10 @@ __global__ void __launch_bounds__(kThreads, 1)
               }
             } else {
               float* o = p.out + orow + nb;
-              if (vec) {
+              if (vec && (reinterpret_cast<uintptr_t>(o) & 31) == 0) {
+#pragma unroll
+                for (int j = 0; j < 32; j += 8) st_global8(o + j, v + j);
+              } else if (vec) {
 #pragma unroll
                 for (int j = 0; j < 32; j += 4)
                   *reinterpret_cast<float4*>(o + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
@@ -594,7 +597,22 @@ __global__ void __launch_bounds__(kThreads, 1)
             const float* rr = p.epi_res + orow + nb;
             const bool vec = full && ((orow + nb) & 3) == 0 &&
                              ((reinterpret_cast<uintptr_t>(p.epi_gamma + nb) & 15) == 0);
-            if (vec) {
+            if (vec && ((reinterpret_cast<uintptr_t>(o) | reinterpret_cast<uintptr_t>(rr)) & 31) == 0) {
+              // 32-byte accesses: the row's residual first, then the outputs
+              float r32[32];
+#pragma unroll
+              for (int j = 0; j < 32; j += 8) ld_global8(rr + j, r32 + j);
+#pragma unroll
+              for (int j = 0; j < 32; j += 4) {
+                const float4 g4 = *reinterpret_cast<const float4*>(p.epi_gamma + nb + j);
+                v[j] = fmaf(g4.x, v[j], r32[j]);
+                v[j + 1] = fmaf(g4.y, v[j + 1], r32[j + 1]);
+                v[j + 2] = fmaf(g4.z, v[j + 2], r32[j + 2]);
+                v[j + 3] = fmaf(g4.w, v[j + 3], r32[j + 3]);
+              }
+#pragma unroll
+              for (int j = 0; j < 32; j += 8) st_global8(o + j, v + j);
+            } else if (vec) {
 #pragma unroll
               for (int j = 0; j < 32; j += 4) {
                 const float4 r4 = *reinterpret_cast<const float4*>(rr + j);
