@@ -391,13 +391,28 @@ __global__ void __launch_bounds__(192, 2)
       // the output feeds only the bf16 out-projection: stored as bf16
       const float inv = l > 0.f ? 1.0f / l : 0.f;
       uint16_t* o = p.out16 + (int64_t)(b * p.nq + q0 + r) * p.ldo + h * HD;
+      if ((reinterpret_cast<uintptr_t>(o) & 31) == 0) {
+        // the row's 64 values in 32-byte stores
 #pragma unroll
-      for (int i = 0; i < HD; i += 8) {
-        __nv_bfloat162 w[4];
+        for (int i = 0; i < HD; i += 16) {
+          uint32_t w[8];
 #pragma unroll
-        for (int e = 0; e < 4; ++e)
-          w[e] = __float22bfloat162_rn(make_float2(ov[i + 2 * e] * inv, ov[i + 2 * e + 1] * inv));
-        *reinterpret_cast<uint4*>(o + i) = *reinterpret_cast<const uint4*>(w);
+          for (int e = 0; e < 8; ++e) {
+            const __nv_bfloat162 t =
+                __float22bfloat162_rn(make_float2(ov[i + 2 * e] * inv, ov[i + 2 * e + 1] * inv));
+            w[e] = *reinterpret_cast<const uint32_t*>(&t);
+          }
+          st_global8(reinterpret_cast<uint32_t*>(o + i), w);
+        }
+      } else {
+#pragma unroll
+        for (int i = 0; i < HD; i += 8) {
+          __nv_bfloat162 w[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e)
+            w[e] = __float22bfloat162_rn(make_float2(ov[i + 2 * e] * inv, ov[i + 2 * e + 1] * inv));
+          *reinterpret_cast<uint4*>(o + i) = *reinterpret_cast<const uint4*>(w);
+        }
       }
     } else if (ok && qvalid) {
       const float inv = l > 0.f ? 1.0f / l : 0.f;

@@ -409,7 +409,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                   for (int j = 0; j < 16; ++j) v[16 * hf + j] = round_tf32(v[16 * hf + j]);
                 }
                 float* o = p.out + at;
-                if (v4) {
+                if (v4 && (reinterpret_cast<uintptr_t>(o) & 31) == 0) {
+                  st_global8(o, v + 16 * hf);
+                  st_global8(o + 8, v + 16 * hf + 8);
+                } else if (v4) {
 #pragma unroll
                   for (int j = 0; j < 16; j += 4)
                     *reinterpret_cast<float4*>(o + j) =
@@ -430,7 +433,13 @@ __global__ void __launch_bounds__(kThreads, 1)
             const bool vec = full && ((orow + nb) & 3) == 0;
             if (p.epi_add) {
               const float* ad = p.epi_add + orow + nb;
-              if (vec) {
+              if (vec && (reinterpret_cast<uintptr_t>(ad) & 31) == 0) {
+                float a32[32];
+#pragma unroll
+                for (int j = 0; j < 32; j += 8) ld_global8(ad + j, a32 + j);
+#pragma unroll
+                for (int j = 0; j < 32; ++j) v[j] += a32[j];
+              } else if (vec) {
 #pragma unroll
                 for (int j = 0; j < 32; j += 4) {
                   const float4 t4 = *reinterpret_cast<const float4*>(ad + j);
@@ -466,7 +475,13 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (p.out16) {
               // bf16 output (the A operand of a bf16 GEMM): 32 values in 64 bytes
               uint16_t* o16 = p.out16 + orow + nb;
-              if (full && ((orow + nb) & 7) == 0) {
+              if (full && (reinterpret_cast<uintptr_t>(o16) & 31) == 0) {
+                uint32_t w16[16];
+#pragma unroll
+                for (int j = 0; j < 16; ++j) w16[j] = pack_bf16(v[2 * j], v[2 * j + 1]);
+                st_global8(reinterpret_cast<uint32_t*>(o16), w16);
+                st_global8(reinterpret_cast<uint32_t*>(o16) + 8, w16 + 8);
+              } else if (full && ((orow + nb) & 7) == 0) {
 #pragma unroll
                 for (int j = 0; j < 32; j += 8)
                   *reinterpret_cast<uint4*>(o16 + j) =
@@ -515,7 +530,10 @@ __global__ void __launch_bounds__(kThreads, 1)
               }
             }
             float* o = p.out + orow + c0o;
-            if (vec) {
+            if (vec && (reinterpret_cast<uintptr_t>(o) & 31) == 0) {
+              st_global8(o, g);
+              st_global8(o + 8, g + 8);
+            } else if (vec) {
 #pragma unroll
               for (int j = 0; j < 16; j += 4)
                 *reinterpret_cast<float4*>(o + j) = make_float4(g[j], g[j + 1], g[j + 2], g[j + 3]);
@@ -530,8 +548,12 @@ __global__ void __launch_bounds__(kThreads, 1)
             float* o = p.out + orow + c0o;
             const float* rr = p.epi_res + orow + c0o;
             const bool vec = full && ((orow + c0o) & 3) == 0;
+            const bool v8 = vec && ((reinterpret_cast<uintptr_t>(o) | reinterpret_cast<uintptr_t>(rr)) & 31) == 0;
             float res[16];
-            if (vec) {
+            if (v8) {
+              ld_global8(rr, res);
+              ld_global8(rr + 8, res + 8);
+            } else if (vec) {
 #pragma unroll
               for (int j = 0; j < 16; j += 4) {
                 const float4 r4 = *reinterpret_cast<const float4*>(rr + j);
@@ -583,7 +605,10 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
               for (int j = 0; j < 16; ++j) res[j] = round_tf32(res[j]);
             }
-            if (vec) {
+            if (v8) {
+              st_global8(o, res);
+              st_global8(o + 8, res + 8);
+            } else if (vec) {
 #pragma unroll
               for (int j = 0; j < 16; j += 4)
                 *reinterpret_cast<float4*>(o + j) = make_float4(res[j], res[j + 1], res[j + 2], res[j + 3]);
